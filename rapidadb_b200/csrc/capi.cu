@@ -1,0 +1,77 @@
+// C-ABI plumbing: thread-local error messages, the per-device status word
+// that bounded device waits report into, and small shared helpers.
+#include <stdarg.h>
+#include <stdio.h>
+
+#include <mutex>
+
+#include "common.cuh"
+
+namespace rdb {
+
+static thread_local char g_err[1024] = "";
+
+int set_error(int code, const char* fmt, ...) {
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(g_err, sizeof(g_err), fmt, ap);
+    va_end(ap);
+    return code;
+}
+
+int num_sms() {
+    static int cached[64] = {0};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev >= 0 && dev < 64 && cached[dev]) return cached[dev];
+    int v = 0;
+    cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev);
+    if (v <= 0) v = 148;
+    if (dev >= 0 && dev < 64) cached[dev] = v;
+    return v;
+}
+
+size_t elem_size(int dtype) {
+    switch (dtype) {
+        case RDB_F32: return 4;
+        case RDB_F16: return 2;
+        case RDB_BF16: return 2;
+        default: return 0;
+    }
+}
+
+// One zero-initialised status word per device, allocated on first use.
+unsigned* device_status_word() {
+    static std::mutex mu;
+    static unsigned* words[64] = {nullptr};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
+    std::lock_guard<std::mutex> lock(mu);
+    if (!words[dev]) {
+        unsigned* p = nullptr;
+        if (cudaMalloc(&p, sizeof(unsigned)) != cudaSuccess) return nullptr;
+        if (cudaMemset(p, 0, sizeof(unsigned)) != cudaSuccess) return nullptr;
+        words[dev] = p;
+    }
+    return words[dev];
+}
+
+}  // namespace rdb
+
+extern "C" {
+
+const char* rdb_last_error(void) { return rdb::g_err; }
+
+int rdb_version(void) { return 100; }
+
+int rdb_device_status(unsigned* out_host, int clear) {
+    RDB_CHECK_ARG(out_host != nullptr, "out_host is NULL");
+    unsigned* w = rdb::device_status_word();
+    if (!w) return rdb::set_error(RDB_ERR_CUDA, "cannot allocate the device status word");
+    RDB_CUDA_TRY(cudaDeviceSynchronize());
+    RDB_CUDA_TRY(cudaMemcpy(out_host, w, sizeof(unsigned), cudaMemcpyDeviceToHost));
+    if (clear) RDB_CUDA_TRY(cudaMemset(w, 0, sizeof(unsigned)));
+    return RDB_OK;
+}
+
+}  // extern "C"

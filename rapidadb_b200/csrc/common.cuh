@@ -1,0 +1,170 @@
+// Shared helpers for the RapidaDB B200 kernels: status reporting, metric
+// score algebra, orderable sort keys and bounded spin-waits.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+#include <string.h>
+
+#include "rapidadb_b200.h"
+
+namespace rdb {
+
+// ---------------------------------------------------------------- errors --
+
+// Records a message for rdb_last_error() (thread-local) and returns `code`.
+int set_error(int code, const char* fmt, ...);
+
+#define RDB_CHECK_ARG(cond, ...)                                   \
+    do {                                                           \
+        if (!(cond)) return ::rdb::set_error(RDB_ERR_INVALID, __VA_ARGS__); \
+    } while (0)
+
+#define RDB_CUDA_TRY(expr)                                                        \
+    do {                                                                          \
+        cudaError_t e_ = (expr);                                                  \
+        if (e_ != cudaSuccess)                                                    \
+            return ::rdb::set_error(RDB_ERR_CUDA, "%s: %s (%s:%d)", #expr,        \
+                                    cudaGetErrorString(e_), __FILE__, __LINE__);  \
+    } while (0)
+
+#define RDB_LAUNCH_CHECK()                                                        \
+    do {                                                                          \
+        cudaError_t e_ = cudaGetLastError();                                      \
+        if (e_ != cudaSuccess)                                                    \
+            return ::rdb::set_error(RDB_ERR_CUDA, "kernel launch: %s (%s:%d)",    \
+                                    cudaGetErrorString(e_), __FILE__, __LINE__);  \
+    } while (0)
+
+#define RDB_TRY(expr)              \
+    do {                           \
+        int s_ = (expr);           \
+        if (s_ != RDB_OK) return s_; \
+    } while (0)
+
+int num_sms();
+size_t elem_size(int dtype);
+
+// Device status word: kernels that give up on a bounded wait OR in a code here
+// instead of hanging; the host reads it with read_device_status().
+enum DeviceStatus : unsigned {
+    DEV_OK = 0,
+    DEV_TIMEOUT_PRODUCER = 1u << 0,
+    DEV_TIMEOUT_MMA = 1u << 1,
+    DEV_TIMEOUT_EPILOGUE = 1u << 2,
+    DEV_OVERFLOW = 1u << 3,
+};
+unsigned* device_status_word();  // per-device, zero-initialised
+
+// ------------------------------------------------------- score algebra --
+//
+// Every metric's final score is a function of the raw dot product <q, x> and
+// two per-vector scalars (the reference formulas, csrc/kernels/distance.cu):
+//   L2      : qv + xv - 2 dot          qv = |q|^2,  xv = |x|^2
+//   DOT     : dot
+//   COSINE  : d >  128: dot / (qv xv + 1e-8)      qv = sqrt|q|^2,  xv = sqrt|x|^2
+//             d <= 128: dot / (qv xv)             qv = sqrt(|q|^2 + 1e-8), ...
+// "xv" is the per-row value the index stores beside each row.
+
+__host__ __device__ inline bool metric_largest(int metric) { return metric != RDB_METRIC_L2; }
+
+__host__ __device__ inline float vec_value(int metric, int cos_small, float sq) {
+    if (metric == RDB_METRIC_L2) return sq;
+    if (metric == RDB_METRIC_COSINE) return cos_small ? sqrtf(sq + 1e-8f) : sqrtf(sq);
+    return 0.f;
+}
+
+__device__ __forceinline__ float final_score(int metric, int cos_small, float dot, float qv,
+                                             float xv) {
+    if (metric == RDB_METRIC_L2) return fmaxf(qv + xv - 2.f * dot, 0.f);
+    if (metric == RDB_METRIC_COSINE) return cos_small ? dot / (qv * xv) : dot / (qv * xv + 1e-8f);
+    return dot;
+}
+
+// Filter coefficients: a row passes when dot >= A * xv + B.  Derived from a
+// threshold `thr` in final-score units, with a relative slack of 2^-16 so
+// that rounding can never reject a row whose final score reaches thr.
+struct FilterCoef {
+    float A, B;
+};
+
+__device__ __forceinline__ FilterCoef filter_coef(int metric, int cos_small, float thr, float qv) {
+    FilterCoef f;
+    const float eps = 1.52587890625e-05f;  // 2^-16
+    if (metric == RDB_METRIC_L2) {
+        // qv + xv - 2 dot <= thr  <=>  dot >= 0.5 xv + 0.5 (qv - thr)
+        f.A = 0.5f;
+        f.B = 0.5f * (qv - thr);
+    } else if (metric == RDB_METRIC_COSINE) {
+        f.A = thr * qv;
+        f.B = cos_small ? 0.f : thr * 1e-8f;
+    } else {
+        f.A = 0.f;
+        f.B = thr;
+    }
+    f.A -= fabsf(f.A) * eps;  // xv >= 0, so lowering A lowers the bound
+    f.B -= fabsf(f.B) * eps + 1e-30f;
+    if (!(thr == thr) || isinf(thr)) {  // "accept all"
+        f.A = 0.f;
+        f.B = -INFINITY;
+    }
+    return f;
+}
+
+// ------------------------------------------------------------- bit casts --
+
+__host__ __device__ inline uint32_t f2u(float f) {
+#ifdef __CUDA_ARCH__
+    return __float_as_uint(f);
+#else
+    uint32_t u;
+    memcpy(&u, &f, 4);
+    return u;
+#endif
+}
+
+__host__ __device__ inline float u2f(uint32_t u) {
+#ifdef __CUDA_ARCH__
+    return __uint_as_float(u);
+#else
+    float f;
+    memcpy(&f, &u, 4);
+    return f;
+#endif
+}
+
+// ------------------------------------------------------------- sort keys --
+// 32-bit key, ascending = better.  Ties are broken by the row index in the
+// low half of a 64-bit key, so every key is unique.
+
+__host__ __device__ inline uint32_t float_asc_key(float f) {
+    uint32_t u = f2u(f);
+    return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+
+__host__ __device__ inline float asc_key_float(uint32_t k) {
+    uint32_t u = (k & 0x80000000u) ? (k & 0x7fffffffu) : ~k;
+    return u2f(u);
+}
+
+__host__ __device__ inline uint32_t score_key(float s, bool largest) {
+    uint32_t k = float_asc_key(s);
+    return largest ? ~k : k;
+}
+
+__host__ __device__ inline float key_score(uint32_t k, bool largest) {
+    return asc_key_float(largest ? ~k : k);
+}
+
+// --------------------------------------------------------- spin waits --
+
+__device__ __forceinline__ uint64_t globaltimer_ns() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+// Upper bound on any single pipeline wait: a healthy wait lasts microseconds.
+constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s
+
+}  // namespace rdb

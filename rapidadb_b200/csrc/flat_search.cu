@@ -1,0 +1,347 @@
+// Exact flat search (the replacement of FlatIndex::search,
+// csrc/index/flat_index.cpp:49-86) and dense top-k (topk_thrust,
+// csrc/kernels/topk.cu:14-28).
+//
+// Flat search never materialises the [nq, n] score matrix:
+//   1. sample pass   - scan a strided sample of S rows with no threshold; the
+//                      selection kernel returns each query's k-th best sample
+//                      score thr[q].  The k sample winners are real rows, so
+//                      the true k-th best score over all n rows is at least as
+//                      good as thr[q]: rows scoring worse can never be in the
+//                      answer.
+//   2. main pass     - the fused scan (tcgen05 for fp16/bf16, CUDA cores for
+//                      fp32) scores every row and appends only rows reaching
+//                      thr[q] (about n k / S per query) to per-(split, query)
+//                      candidate lists.
+//   3. select        - per query: exact top-k of its candidates, sorted, ties to
+//                      the lower row, rows -> user ids; L2 winners are
+//                      re-scored as sum (q - x)^2.
+// A candidate list that overflows its capacity is reported (RDB_ERR_OVERFLOW)
+// and the caller repeats the search with RDB_SEARCH_EXHAUSTIVE (no sampled
+// threshold, capacity = rows per split, so nothing can overflow).
+#include <math.h>
+
+#include <algorithm>
+
+#include "scan.cuh"
+#include "select.cuh"
+
+namespace rdb {
+namespace {
+
+inline size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+
+struct PassPlan {
+    int64_t rows;  // logical rows scanned
+    int64_t row_step;
+    int nsplit;
+    int64_t rps;   // rows per split
+    int64_t cap;   // candidates per (split, query)
+};
+
+struct FlatPlan {
+    bool tc;
+    int qtile, rtile;
+    int64_t nq;  // queries in one chunk
+    bool sample;
+    PassPlan s, m;
+    size_t ws_bytes;
+    size_t off_qv, off_thr, off_cand, off_counts, off_flag;
+};
+
+PassPlan plan_pass(int64_t rows, int64_t row_step, int64_t nq, int qtile, int rtile, int sms,
+                   bool tc) {
+    PassPlan p;
+    p.rows = rows;
+    p.row_step = row_step;
+    int64_t nqb = (nq + qtile - 1) / qtile;
+    int64_t ntiles = (rows + rtile - 1) / rtile;
+    int64_t target = tc ? sms : 2LL * sms;
+    int64_t nsplit = std::max<int64_t>(1, target / std::max<int64_t>(nqb, 1));
+    nsplit = std::min<int64_t>(nsplit, std::max<int64_t>(ntiles, 1));
+    nsplit = std::min<int64_t>(nsplit, 1024);
+    int64_t tiles_per = (ntiles + nsplit - 1) / nsplit;
+    p.rps = std::max<int64_t>(tiles_per, 1) * rtile;
+    p.nsplit = (int)std::max<int64_t>(1, (rows + p.rps - 1) / p.rps);
+    p.cap = p.rps;
+    return p;
+}
+
+FlatPlan make_plan(int metric, int dtype, int64_t nq, int64_t n, int d, int k, int flags,
+                   bool tc_ok) {
+    (void)metric;
+    (void)d;
+    FlatPlan P = {};
+    P.tc = tc_ok && (dtype == RDB_F16 || dtype == RDB_BF16);
+    P.qtile = P.tc ? kTcQueries : kSimtQueries;
+    P.rtile = P.tc ? kTcRows : kSimtRows;
+    P.nq = nq;
+    const int sms = num_sms();
+
+    // sample size: ~1.5 sqrt(n k) rows (balances sample cost against the
+    // candidate volume n k / S), a power of two in [1024, 32768], >= 8 k
+    double sd = 1.5 * sqrt((double)n * (double)k);
+    int64_t S = 1024;
+    while (S < sd && S < 32768) S <<= 1;
+    while (S < 8LL * k) S <<= 1;
+    P.sample = !(flags & RDB_SEARCH_EXHAUSTIVE) && n >= 4 * S;
+    if (P.sample) {
+        int64_t step = n / S;
+        P.s = plan_pass(S, step, nq, P.qtile, P.rtile, sms, P.tc);
+    }
+    P.m = plan_pass(n, 1, nq, P.qtile, P.rtile, sms, P.tc);
+    if (P.sample) {
+        // expected candidates per split: rps * k / S; keep 8x headroom
+        int64_t expect = (int64_t)ceil((double)P.m.rps * (double)k / (double)S);
+        P.m.cap = std::min<int64_t>(P.m.rps, std::max<int64_t>(1024, 8 * expect + 256));
+    }
+    size_t cand_main = (size_t)P.m.nsplit * nq * P.m.cap * sizeof(uint2);
+    size_t cand_samp = P.sample ? (size_t)P.s.nsplit * nq * P.s.cap * sizeof(uint2) : 0;
+    size_t cnt_main = (size_t)P.m.nsplit * nq * sizeof(int);
+    size_t cnt_samp = P.sample ? (size_t)P.s.nsplit * nq * sizeof(int) : 0;
+    size_t off = 0;
+    P.off_qv = off;
+    off = align_up(off + nq * sizeof(float), 256);
+    P.off_thr = off;
+    off = align_up(off + nq * sizeof(float), 256);
+    P.off_cand = off;
+    off = align_up(off + std::max(cand_main, cand_samp), 256);
+    P.off_counts = off;
+    off = align_up(off + std::max(cnt_main, cnt_samp), 256);
+    P.off_flag = off;
+    off = align_up(off + 16, 256);
+    P.ws_bytes = off;
+    return P;
+}
+
+bool tc_layout_ok(int dtype, const void* q, int64_t ldq, const void* x, int64_t ldx, int d) {
+    if (dtype != RDB_F16 && dtype != RDB_BF16) return false;
+    if ((reinterpret_cast<uintptr_t>(q) & 15) || (reinterpret_cast<uintptr_t>(x) & 15)) return false;
+    if ((ldq * 2) % 16 || (ldx * 2) % 16) return false;
+    return d >= 8;
+}
+
+int run_chunk(const FlatPlan& P, int metric, int dtype, const void* q, int64_t nq, int64_t ldq,
+              const void* x, int64_t n, int64_t ldx, const float* xv, int d, int k,
+              const int64_t* ids, int64_t id_offset, float* out_d, int64_t* out_i,
+              unsigned char* ws, cudaStream_t s) {
+    float* qv = reinterpret_cast<float*>(ws + P.off_qv);
+    float* thr = reinterpret_cast<float*>(ws + P.off_thr);
+    uint2* cand = reinterpret_cast<uint2*>(ws + P.off_cand);
+    int* counts = reinterpret_cast<int*>(ws + P.off_counts);
+    unsigned* flag = reinterpret_cast<unsigned*>(ws + P.off_flag);
+    const int cos_small = d <= 128 ? 1 : 0;
+    const bool largest = metric_largest(metric);
+
+    // per-query metric values (queries are strided: norms of each row)
+    if (ldq == d) {
+        RDB_TRY(rdb_row_sqnorms(dtype, q, nq, d, qv, s));
+    } else {
+        // strided queries: compute row by row via a contiguous view per row
+        for (int64_t i = 0; i < nq; ++i)
+            RDB_TRY(rdb_row_sqnorms(dtype, static_cast<const char*>(q) + i * ldq * elem_size(dtype),
+                                    1, d, qv + i, s));
+    }
+    RDB_TRY(rdb_vec_values(metric, d, qv, nq, qv, s));
+
+    ScanArgs a = {};
+    a.metric = metric;
+    a.cos_small = cos_small;
+    a.dtype = dtype;
+    a.q = q;
+    a.nq = nq;
+    a.ldq = ldq;
+    a.x = x;
+    a.ldx = ldx;
+    a.d = d;
+    a.qv = qv;
+    a.xv = xv;
+    a.cand = cand;
+    a.counts = counts;
+
+    SelectArgs sa = {};
+    sa.input = SEL_CANDIDATES;
+    sa.nq = nq;
+    sa.k = k;
+    sa.largest = largest ? 1 : 0;
+    sa.cand = cand;
+    sa.counts = counts;
+    sa.metric = metric;
+    sa.cos_small = cos_small;
+    sa.qv = qv;
+    sa.xv = xv;
+    sa.dtype = dtype;
+    sa.qdata = q;
+    sa.ldq = ldq;
+    sa.xdata = x;
+    sa.ldx = ldx;
+    sa.d = d;
+
+    auto scan = [&](const ScanArgs& sc) {
+        return P.tc ? launch_scan_tc(sc, SCAN_FILTER, s) : launch_scan_simt(sc, SCAN_FILTER, s);
+    };
+
+    if (P.sample) {
+        ScanArgs sc = a;
+        sc.n = P.s.rows;
+        sc.row_step = P.s.row_step;
+        sc.thr = nullptr;
+        sc.nsplit = P.s.nsplit;
+        sc.rows_per_split = P.s.rps;
+        sc.cap = P.s.cap;
+        RDB_TRY(scan(sc));
+        SelectArgs ss = sa;
+        ss.output = SEL_OUT_THRESHOLD;
+        ss.cap = P.s.cap;
+        ss.nsplit = P.s.nsplit;
+        ss.row_step = P.s.row_step;
+        ss.out_thr = thr;
+        ss.overflow = nullptr;
+        RDB_TRY(launch_select(ss, s));
+    }
+    RDB_CUDA_TRY(cudaMemsetAsync(flag, 0, sizeof(unsigned), s));
+    {
+        ScanArgs sc = a;
+        sc.n = n;
+        sc.row_step = 1;
+        sc.thr = P.sample ? thr : nullptr;
+        sc.nsplit = P.m.nsplit;
+        sc.rows_per_split = P.m.rps;
+        sc.cap = P.m.cap;
+        RDB_TRY(scan(sc));
+        SelectArgs ss = sa;
+        ss.output = SEL_OUT_TOPK;
+        ss.cap = P.m.cap;
+        ss.nsplit = P.m.nsplit;
+        ss.row_step = 1;
+        ss.out_v = out_d;
+        ss.out_i = out_i;
+        ss.ids = ids;
+        ss.id_offset = id_offset;
+        ss.overflow = flag;
+        ss.rescore_margin = metric == RDB_METRIC_L2 ? 16 : 0;
+        RDB_TRY(launch_select(ss, s));
+    }
+    return RDB_OK;
+}
+
+}  // namespace
+}  // namespace rdb
+
+using namespace rdb;
+
+extern "C" {
+
+size_t rdb_flat_search_workspace(int metric, int dtype, int64_t nq, int64_t n, int d, int k,
+                                 int flags) {
+    if (nq <= 0 || n <= 0 || d <= 0 || k <= 0) return 256;
+    return make_plan(metric, dtype, nq, n, d, k, flags, true).ws_bytes;
+}
+
+int rdb_flat_search(int metric, int dtype, const void* q, int64_t nq, int64_t ldq,
+                    const void* x, int64_t n, int64_t ldx, const float* xv, int d, int k,
+                    const int64_t* ids, int64_t id_offset, int flags, float* out_d,
+                    int64_t* out_i, void* ws, size_t ws_bytes, void* stream) {
+    RDB_CHECK_ARG(metric >= 0 && metric <= 2, "unknown metric %d", metric);
+    RDB_CHECK_ARG(elem_size(dtype) != 0, "unknown dtype %d", dtype);
+    RDB_CHECK_ARG(nq >= 0 && d >= 1, "bad shape");
+    RDB_CHECK_ARG(n >= 1, "index is empty");
+    RDB_CHECK_ARG(k >= 1 && k <= n, "k must be in [1, %lld]", (long long)n);
+    RDB_CHECK_ARG(k <= kMaxK, "k must be <= %d", kMaxK);
+    RDB_CHECK_ARG(n < (1LL << 32), "at most 2^32 - 1 rows per device");
+    RDB_CHECK_ARG(ldq >= d && ldx >= d, "row strides must be >= d");
+    if (nq == 0) return RDB_OK;
+    RDB_CHECK_ARG(q && x && out_d && out_i && ws, "NULL pointer");
+    RDB_CHECK_ARG(metric != RDB_METRIC_COSINE || xv, "cosine needs per-row values");
+    RDB_CHECK_ARG(metric != RDB_METRIC_L2 || xv, "L2 needs per-row values");
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    bool tc_ok = tc_layout_ok(dtype, q, ldq, x, ldx, d);
+
+    // largest query chunk whose plan fits the workspace
+    FlatPlan P = make_plan(metric, dtype, nq, n, d, k, flags, tc_ok);
+    int64_t chunk = nq;
+    while (P.ws_bytes > ws_bytes && chunk > P.qtile) {
+        chunk = std::max<int64_t>(P.qtile, (chunk / 2 + P.qtile - 1) / P.qtile * P.qtile);
+        P = make_plan(metric, dtype, chunk, n, d, k, flags, tc_ok);
+    }
+    if (P.ws_bytes > ws_bytes)
+        return set_error(RDB_ERR_WORKSPACE, "workspace too small: %zu bytes, need %zu", ws_bytes,
+                         P.ws_bytes);
+    unsigned char* w = static_cast<unsigned char*>(ws);
+    unsigned* flag = reinterpret_cast<unsigned*>(w + P.off_flag);
+    unsigned any_overflow = 0;
+    const size_t es = elem_size(dtype);
+    for (int64_t c0 = 0; c0 < nq; c0 += chunk) {
+        int64_t cn = std::min(chunk, nq - c0);
+        FlatPlan Pc = cn == chunk ? P : make_plan(metric, dtype, cn, n, d, k, flags, tc_ok);
+        RDB_TRY(run_chunk(Pc, metric, dtype, static_cast<const char*>(q) + c0 * ldq * es, cn, ldq,
+                          x, n, ldx, xv, d, k, ids, id_offset, out_d + c0 * k, out_i + c0 * k, w,
+                          s));
+        unsigned h = 0;
+        RDB_CUDA_TRY(cudaMemcpyAsync(&h, w + Pc.off_flag, sizeof(unsigned), cudaMemcpyDeviceToHost, s));
+        RDB_CUDA_TRY(cudaStreamSynchronize(s));
+        any_overflow |= h;
+    }
+    (void)flag;
+    unsigned* st = device_status_word();
+    if (st) {
+        unsigned hs = 0;
+        RDB_CUDA_TRY(cudaMemcpyAsync(&hs, st, sizeof(unsigned), cudaMemcpyDeviceToHost, s));
+        RDB_CUDA_TRY(cudaStreamSynchronize(s));
+        if (hs) return set_error(RDB_ERR_TIMEOUT, "a search kernel gave up on a device wait (status 0x%x)", hs);
+    }
+    if (any_overflow)
+        return set_error(RDB_ERR_OVERFLOW, "candidate list overflow; repeat with RDB_SEARCH_EXHAUSTIVE");
+    return RDB_OK;
+}
+
+size_t rdb_topk_workspace(int64_t B, int64_t N, int k) {
+    (void)B;
+    (void)N;
+    (void)k;
+    return 0;
+}
+
+int rdb_topk(const float* dist, int64_t B, int64_t N, int k, int largest, float* out_v,
+             int64_t* out_i, void* ws, size_t ws_bytes, void* stream) {
+    (void)ws;
+    (void)ws_bytes;
+    RDB_CHECK_ARG(B >= 0 && N >= 1, "bad shape");
+    RDB_CHECK_ARG(k >= 1 && k <= N, "k must be in [1, num_vectors]");
+    RDB_CHECK_ARG(k <= kMaxK, "k must be <= %d", kMaxK);
+    RDB_CHECK_ARG(N < (1LL << 31), "rows longer than 2^31 - 1");
+    if (B == 0) return RDB_OK;
+    SelectArgs a = {};
+    a.input = SEL_DENSE;
+    a.output = SEL_OUT_TOPK;
+    a.nq = B;
+    a.k = k;
+    a.largest = largest ? 1 : 0;
+    a.dense = dist;
+    a.dense_n = N;
+    a.out_v = out_v;
+    a.out_i = out_i;
+    return launch_select(a, static_cast<cudaStream_t>(stream));
+}
+
+int rdb_topk_merge(int largest, const float* in_v, const int64_t* in_i, int G, int64_t nq,
+                   int kin, int k, float* out_v, int64_t* out_i, void* stream) {
+    RDB_CHECK_ARG(G >= 1 && kin >= 1 && k >= 1, "bad shape");
+    RDB_CHECK_ARG(k <= (int64_t)G * kin, "k must be <= G * kin");
+    if (nq == 0) return RDB_OK;
+    SelectArgs a = {};
+    a.input = SEL_MERGE;
+    a.output = SEL_OUT_TOPK;
+    a.nq = nq;
+    a.k = k;
+    a.largest = largest ? 1 : 0;
+    a.merge_v = in_v;
+    a.merge_i = in_i;
+    a.G = G;
+    a.kin = kin;
+    a.out_v = out_v;
+    a.out_i = out_i;
+    return launch_select(a, static_cast<cudaStream_t>(stream));
+}
+
+}  // extern "C"

@@ -1,0 +1,64 @@
+// Shared description of a "scan": score a block of queries against a range of
+// stored rows and either keep the rows that pass a per-query threshold
+// (candidate lists for the selection kernel), write the dense score matrix,
+// or keep the best row per query (argmin, for k-means / list assignment).
+#pragma once
+
+#include "common.cuh"
+
+namespace rdb {
+
+enum ScanMode : int {
+    SCAN_FILTER = 0,  // append (dot, row) pairs whose score reaches thr[q]
+    SCAN_DENSE = 1,   // write final scores to dense_out[q, row]
+    SCAN_ARGMIN = 2,  // best row per (split, query) by squared L2
+};
+
+struct ScanArgs {
+    int metric;
+    int cos_small;
+    int dtype;
+
+    const void* q;  // [nq, d] (row stride ldq elements)
+    int64_t nq;
+    int64_t ldq;
+
+    const void* x;     // stored rows; logical row j is physical row j * row_step
+    int64_t n;         // logical rows
+    int64_t ldx;
+    int64_t row_step;
+    int d;
+
+    const float* qv;   // [nq] per-query metric value
+    const float* xv;   // per physical row metric value
+    const float* thr;  // [nq] thresholds in final-score units (NULL: accept all)
+
+    // SCAN_FILTER: candidate lists [nsplit][nq][cap] + counts [nsplit][nq]
+    uint2* cand;
+    int* counts;
+    int64_t cap;
+
+    int nsplit;
+    int64_t rows_per_split;  // multiple of the kernel's row tile
+
+    // SCAN_DENSE
+    float* dense_out;
+    int64_t ld_out;
+
+    // SCAN_ARGMIN: [nsplit][nq] best (score key, row) pairs
+    unsigned long long* best;
+};
+
+// CUDA-core scan (any dtype).  Grid = (nsplit, ceil(nq / 32)).
+int launch_scan_simt(const ScanArgs& a, int mode, cudaStream_t stream);
+
+// tcgen05 scan for fp16 / bf16 (sm_100a).  Grid = (nsplit, ceil(nq / 128)).
+int launch_scan_tc(const ScanArgs& a, int mode, cudaStream_t stream);
+
+// Row tiles of the two kernels (rows_per_split must be a multiple).
+constexpr int kSimtRows = 128;
+constexpr int kSimtQueries = 32;
+constexpr int kTcRows = 256;
+constexpr int kTcQueries = 128;
+
+}  // namespace rdb

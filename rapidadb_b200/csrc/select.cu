@@ -1,0 +1,356 @@
+// Per-query top-k selection: one CTA per query.
+//
+// Every element gets a unique 64-bit key  (score key << 32) | index  that
+// sorts ascending best-first (csrc/kernels/topk.cu:25 semantics: sorted,
+// largest for cosine / dot, smallest for L2; ties go to the lower index).  An
+// MSD radix select finds the k-th smallest key in a few passes over the
+// elements (shared-memory cached when they fit), the k winners are gathered
+// and bitonic-sorted in shared memory.  For L2 over stored vectors the winners
+// (plus a margin) are re-scored exactly as sum (q - x)^2 before the final
+// sort, which is the reference formula (csrc/kernels/distance.cu:414-438).
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+
+#include "select.cuh"
+
+namespace rdb {
+namespace {
+
+constexpr int NT = 256;
+constexpr int NWARP = NT / 32;
+constexpr int kCacheKeys = 4096;  // keys cached in shared memory when T fits
+constexpr int kMaxSeg = 1024;
+
+struct SelShared {
+    int seg_off[kMaxSeg + 1];
+    int hist[256];
+    unsigned long long red_min[NWARP];
+    unsigned long long red_max[NWARP];
+    unsigned long long prefix;
+    int top;
+    int remaining;
+    int done;
+    int nsel;
+    int total;
+};
+
+__device__ __forceinline__ float load_as_float(int dtype, const void* p, int64_t i) {
+    if (dtype == RDB_F32) return static_cast<const float*>(p)[i];
+    if (dtype == RDB_BF16) return __bfloat162float(static_cast<const __nv_bfloat16*>(p)[i]);
+    return __half2float(static_cast<const __half*>(p)[i]);
+}
+
+__device__ __forceinline__ bool hi_eq(unsigned long long a, unsigned long long b, int top) {
+    return top >= 64 ? true : ((a >> top) == (b >> top));
+}
+
+// Key of element e (0 <= e < total) of query q.
+__device__ __forceinline__ unsigned long long elem_key(const SelectArgs& a, const SelShared& S,
+                                                       int64_t q, int e, float qv) {
+    // segment by binary search over the prefix offsets
+    int nseg = a.input == SEL_DENSE ? 1 : (a.input == SEL_MERGE ? a.G : a.nsplit);
+    int lo = 0, hi = nseg - 1;
+    while (lo < hi) {
+        int mid = (lo + hi + 1) >> 1;
+        if (S.seg_off[mid] <= e) lo = mid; else hi = mid - 1;
+    }
+    int t = e - S.seg_off[lo];
+    bool largest = a.largest != 0;
+    if (a.input == SEL_CANDIDATES) {
+        uint2 c = a.cand[((int64_t)lo * a.nq + q) * a.cap + t];
+        float dot = __uint_as_float(c.x);
+        float xv = a.xv ? a.xv[(int64_t)c.y * a.row_step] : 0.f;
+        float s = final_score(a.metric, a.cos_small, dot, qv, xv);
+        return ((unsigned long long)score_key(s, largest) << 32) | c.y;
+    } else if (a.input == SEL_DENSE) {
+        float s = a.dense[q * a.dense_n + t];
+        return ((unsigned long long)score_key(s, largest) << 32) | (uint32_t)t;
+    } else {
+        float s = a.merge_v[((int64_t)lo * a.nq + q) * a.kin + t];
+        return ((unsigned long long)score_key(s, largest) << 32) | (uint32_t)(lo * a.kin + t);
+    }
+}
+
+__device__ void bitonic_sort(unsigned long long* keys, int n /* power of two */) {
+    for (int size = 2; size <= n; size <<= 1) {
+        for (int stride = size >> 1; stride > 0; stride >>= 1) {
+            for (int i = threadIdx.x; i < (n >> 1); i += NT) {
+                int lo = 2 * i - (i & (stride - 1));
+                int hi = lo + stride;
+                bool up = ((lo & size) == 0);
+                unsigned long long x = keys[lo], y = keys[hi];
+                if ((x > y) == up) {
+                    keys[lo] = y;
+                    keys[hi] = x;
+                }
+            }
+            __syncthreads();
+        }
+    }
+}
+
+__device__ __forceinline__ int next_pow2(int v) {
+    int p = 1;
+    while (p < v) p <<= 1;
+    return p;
+}
+
+__global__ void __launch_bounds__(NT) select_kernel(SelectArgs a) {
+    extern __shared__ __align__(16) unsigned char dsm[];
+    __shared__ SelShared S;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const bool largest = a.largest != 0;
+    const int out_k_req = a.k + a.rescore_margin;
+    const int sel_cap = next_pow2(out_k_req > 0 ? out_k_req : 1);
+    unsigned long long* sel = reinterpret_cast<unsigned long long*>(dsm);
+    unsigned long long* cache = sel + sel_cap;
+
+    for (int64_t q = blockIdx.x; q < a.nq; q += gridDim.x) {
+        // ---- segment offsets -------------------------------------------
+        if (warp == 0) {
+            int nseg = a.input == SEL_DENSE ? 1 : (a.input == SEL_MERGE ? a.G : a.nsplit);
+            int per = (nseg + 31) / 32;
+            int b0 = lane * per, b1 = min(b0 + per, nseg);
+            int local = 0;
+            bool ovf = false;
+            for (int s = b0; s < b1; ++s) {
+                int len;
+                if (a.input == SEL_CANDIDATES) {
+                    int c = a.counts[(int64_t)s * a.nq + q];
+                    ovf |= (int64_t)c > a.cap;
+                    len = (int)min((int64_t)c, a.cap);
+                } else if (a.input == SEL_DENSE) {
+                    len = (int)a.dense_n;
+                } else {
+                    len = a.kin;
+                }
+                S.seg_off[s] = local;  // provisional (local prefix)
+                local += len;
+            }
+            if (ovf && a.overflow) atomicOr(a.overflow, 1u);
+            int incl = local;
+            for (int o = 1; o < 32; o <<= 1) {
+                int v = __shfl_up_sync(0xffffffffu, incl, o);
+                if (lane >= o) incl += v;
+            }
+            int excl = incl - local;
+            for (int s = b0; s < b1; ++s) S.seg_off[s] += excl;
+            if (lane == 31) {
+                S.seg_off[nseg] = incl;
+                S.total = incl;
+            }
+        }
+        __syncthreads();
+        const int T = S.total;
+        const float qv = (a.input == SEL_CANDIDATES && a.qv) ? a.qv[q] : 0.f;
+        const int want = min(out_k_req, T);  // elements to select
+        const bool cached = T <= kCacheKeys;
+
+        // ---- pass 0: keys (cached) and min / max ---------------------------
+        unsigned long long kmin = ~0ull, kmax = 0ull;
+        for (int e = threadIdx.x; e < T; e += NT) {
+            unsigned long long key = elem_key(a, S, q, e, qv);
+            if (cached) cache[e] = key;
+            kmin = min(kmin, key);
+            kmax = max(kmax, key);
+        }
+        for (int o = 16; o > 0; o >>= 1) {
+            kmin = min(kmin, __shfl_xor_sync(0xffffffffu, kmin, o));
+            kmax = max(kmax, __shfl_xor_sync(0xffffffffu, kmax, o));
+        }
+        if (lane == 0) {
+            S.red_min[warp] = kmin;
+            S.red_max[warp] = kmax;
+        }
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            unsigned long long mn = ~0ull, mx = 0ull;
+            for (int w = 0; w < NWARP; ++w) {
+                mn = min(mn, S.red_min[w]);
+                mx = max(mx, S.red_max[w]);
+            }
+            S.prefix = mn;
+            S.remaining = want;
+            S.nsel = 0;
+            // all elements selected, or nothing to select: finish immediately
+            if (want >= T || want == 0) {
+                S.done = 1;
+                S.top = 0;
+                S.prefix = mx;  // every key <= max
+            } else {
+                unsigned long long diff = mn ^ mx;
+                S.top = diff ? 64 - __clzll(diff) : 0;  // bits >= top are common
+                S.done = diff ? 0 : 1;
+            }
+        }
+        __syncthreads();
+
+        // ---- MSD radix select --------------------------------------------
+        while (!S.done) {
+            const int top = S.top;
+            const int shift = top > 8 ? top - 8 : 0;
+            const unsigned width_mask = (1u << (top - shift)) - 1u;
+            const unsigned long long prefix = S.prefix;
+            for (int i = threadIdx.x; i < 256; i += NT) S.hist[i] = 0;
+            __syncthreads();
+            const int Tr = (T + 31) & ~31;
+            for (int e = threadIdx.x; e < Tr; e += NT) {
+                int bin = -1;
+                if (e < T) {
+                    unsigned long long key = cached ? cache[e] : elem_key(a, S, q, e, qv);
+                    if (hi_eq(key, prefix, top)) bin = (int)((key >> shift) & width_mask);
+                }
+                unsigned peers = __match_any_sync(0xffffffffu, bin);
+                if (bin >= 0 && lane == __ffs(peers) - 1) atomicAdd(&S.hist[bin], __popc(peers));
+            }
+            __syncthreads();
+            if (warp == 0) {
+                // bucket b holding the remaining-th smallest key
+                int c[8];
+                int local = 0;
+                for (int j = 0; j < 8; ++j) {
+                    c[j] = S.hist[lane * 8 + j];
+                    local += c[j];
+                }
+                int incl = local;
+                for (int o = 1; o < 32; o <<= 1) {
+                    int v = __shfl_up_sync(0xffffffffu, incl, o);
+                    if (lane >= o) incl += v;
+                }
+                int excl = incl - local;
+                int rem = S.remaining;
+                bool mine = excl < rem && rem <= incl;
+                unsigned owner = __ballot_sync(0xffffffffu, mine);
+                if (mine) {
+                    int cum = excl, b = 0;
+                    for (int j = 0; j < 8; ++j) {
+                        if (cum + c[j] >= rem) {
+                            b = lane * 8 + j;
+                            break;
+                        }
+                        cum += c[j];
+                    }
+                    int nrem = rem - cum;
+                    int cnt_b = S.hist[b];
+                    unsigned long long mask = (unsigned long long)width_mask << shift;
+                    S.prefix = (prefix & ~mask) | ((unsigned long long)b << shift);
+                    S.remaining = nrem;
+                    S.top = shift;
+                    S.done = (cnt_b == nrem || shift == 0) ? 1 : 0;
+                }
+                (void)owner;
+            }
+            __syncthreads();
+        }
+
+        // ---- gather the winners: (key >> top) <= (prefix >> top) ------------
+        {
+            const int top = S.top;
+            const unsigned long long pref = top >= 64 ? 0ull : (S.prefix >> top);
+            for (int e = threadIdx.x; e < T; e += NT) {
+                unsigned long long key = cached ? cache[e] : elem_key(a, S, q, e, qv);
+                bool take = top >= 64 ? true : ((key >> top) <= pref);
+                if (take) {
+                    int slot = atomicAdd(&S.nsel, 1);
+                    if (slot < sel_cap) sel[slot] = key;
+                }
+            }
+        }
+        __syncthreads();
+        int nsel = min(S.nsel, sel_cap);
+
+        // ---- exact L2 re-scoring of the winners --------------------------
+        if (a.rescore_margin > 0 && a.input == SEL_CANDIDATES && a.metric == RDB_METRIC_L2) {
+            for (int i = warp; i < nsel; i += NWARP) {
+                unsigned long long key = sel[i];
+                uint32_t row = (uint32_t)key;
+                int64_t prow = (int64_t)row * a.row_step;
+                float acc = 0.f;
+                for (int t = lane; t < a.d; t += 32) {
+                    float df = load_as_float(a.dtype, a.qdata, q * a.ldq + t) -
+                               load_as_float(a.dtype, a.xdata, prow * a.ldx + t);
+                    acc = fmaf(df, df, acc);
+                }
+                for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+                if (lane == 0) sel[i] = ((unsigned long long)score_key(acc, false) << 32) | row;
+            }
+            __syncthreads();
+        }
+
+        // ---- sort + write -------------------------------------------------
+        if (a.output == SEL_OUT_THRESHOLD) {
+            // the k-th best score (winners hold exactly min(k, T) keys)
+            unsigned long long m = 0ull;
+            for (int i = threadIdx.x; i < nsel; i += NT) m = max(m, sel[i]);
+            for (int o = 16; o > 0; o >>= 1) m = max(m, __shfl_xor_sync(0xffffffffu, m, o));
+            if (lane == 0) S.red_max[warp] = m;
+            __syncthreads();
+            if (threadIdx.x == 0) {
+                unsigned long long mm = 0ull;
+                for (int w = 0; w < NWARP; ++w) mm = max(mm, S.red_max[w]);
+                float thr = (nsel >= a.k && nsel > 0) ? key_score((uint32_t)(mm >> 32), largest)
+                                                      : (largest ? -INFINITY : INFINITY);
+                a.out_thr[q] = thr;
+            }
+        } else {
+            int P = next_pow2(nsel > 0 ? nsel : 1);
+            for (int i = nsel + threadIdx.x; i < P; i += NT) sel[i] = ~0ull;
+            __syncthreads();
+            bitonic_sort(sel, P);
+            for (int i = threadIdx.x; i < a.k; i += NT) {
+                float v;
+                int64_t id;
+                if (i < nsel) {
+                    unsigned long long key = sel[i];
+                    v = key_score((uint32_t)(key >> 32), largest);
+                    uint32_t idx = (uint32_t)key;
+                    if (a.input == SEL_CANDIDATES) {
+                        int64_t prow = (int64_t)idx * a.row_step;
+                        id = a.ids ? a.ids[prow] : prow + a.id_offset;
+                    } else if (a.input == SEL_DENSE) {
+                        id = idx;
+                    } else {
+                        int g = idx / a.kin, t = idx % a.kin;
+                        id = a.merge_i[((int64_t)g * a.nq + q) * a.kin + t];
+                    }
+                } else {
+                    v = largest ? -INFINITY : INFINITY;
+                    id = -1;
+                }
+                a.out_v[q * a.k + i] = v;
+                a.out_i[q * a.k + i] = id;
+            }
+        }
+        __syncthreads();
+    }
+}
+
+}  // namespace
+
+int launch_select(const SelectArgs& a, cudaStream_t stream) {
+    if (a.nq <= 0) return RDB_OK;
+    int out_k = a.k + a.rescore_margin;
+    RDB_CHECK_ARG(a.k >= 1 && out_k <= kMaxK + 64, "k must be in [1, %d], got %d", kMaxK, a.k);
+    if (a.input == SEL_CANDIDATES)
+        RDB_CHECK_ARG(a.nsplit >= 1 && a.nsplit <= kMaxSeg, "nsplit %d out of range", a.nsplit);
+    if (a.input == SEL_MERGE)
+        RDB_CHECK_ARG(a.G >= 1 && a.G <= kMaxSeg, "G %d out of range", a.G);
+    int P = 1;
+    while (P < out_k) P <<= 1;
+    size_t smem = sizeof(unsigned long long) * ((size_t)P + kCacheKeys);
+    static bool attr_set[64] = {false};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 64 && !attr_set[dev]) {
+        size_t maxdyn = sizeof(unsigned long long) * (8192 + 64 + kCacheKeys);
+        RDB_CUDA_TRY(cudaFuncSetAttribute(select_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                          (int)maxdyn));
+        attr_set[dev] = true;
+    }
+    int64_t grid = a.nq < 65535 * 4 ? a.nq : 65535 * 4;
+    select_kernel<<<(unsigned)grid, NT, smem, stream>>>(a);
+    RDB_LAUNCH_CHECK();
+    return RDB_OK;
+}
+
+}  // namespace rdb

@@ -1,0 +1,70 @@
+// Per-query top-k selection over candidate lists (internal interface).
+#pragma once
+
+#include "common.cuh"
+
+namespace rdb {
+
+enum SelectInput : int {
+    SEL_CANDIDATES = 0,  // segmented (raw dot bits, row) pairs from a scan kernel
+    SEL_DENSE = 1,       // one row of a dense [B, N] fp32 score matrix
+    SEL_MERGE = 2,       // G sorted lists of (score, int64 id)
+};
+
+enum SelectOutput : int {
+    SEL_OUT_TOPK = 0,       // sorted best-k scores + ids
+    SEL_OUT_THRESHOLD = 1,  // only the k-th best score
+};
+
+struct SelectArgs {
+    int input;
+    int output;
+    int64_t nq;  // number of queries (rows)
+    int k;       // results per query
+    int largest;
+
+    // SEL_CANDIDATES
+    const uint2* cand;   // [nsplit][nq][cap]
+    const int* counts;   // [nsplit][nq] (may exceed cap: overflow)
+    int64_t cap;
+    int nsplit;
+    int metric;
+    int cos_small;
+    const float* qv;     // [nq]
+    const float* xv;     // per physical row
+    int64_t row_step;    // candidate row r is physical row r * row_step
+
+    // SEL_DENSE
+    const float* dense;  // [nq][dense_n]
+    int64_t dense_n;
+
+    // SEL_MERGE
+    const float* merge_v;  // [G][nq][kin]
+    const int64_t* merge_i;
+    int G;
+    int kin;
+
+    // outputs
+    float* out_v;         // [nq][k]
+    int64_t* out_i;       // [nq][k]
+    float* out_thr;       // [nq]
+    const int64_t* ids;   // physical row -> user id (NULL: row + id_offset)
+    int64_t id_offset;
+    unsigned* overflow;   // set to 1 when any count exceeded cap
+
+    // exact L2 rescoring of the selected rows (SEL_CANDIDATES, metric L2)
+    int rescore_margin;  // extra rows selected before rescoring (0 = off)
+    int dtype;
+    const void* qdata;
+    int64_t ldq;
+    const void* xdata;
+    int64_t ldx;
+    int d;
+};
+
+// Largest k supported by the in-shared-memory final sort.
+constexpr int kMaxK = 4096;
+
+int launch_select(const SelectArgs& a, cudaStream_t stream);
+
+}  // namespace rdb
