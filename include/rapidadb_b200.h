@@ -111,6 +111,14 @@ int rdb_flat_search(int metric, int dtype, const void* q, int64_t nq, int64_t ld
 int rdb_topk_merge(int largest, const float* in_v, const int64_t* in_i, int G, int64_t nq,
                    int kin, int k, float* out_v, int64_t* out_i, void* stream);
 
+/* Profiling hook (no reference counterpart; the reference times whole calls,
+ * benchmarks/src/bench_compare.py:56-59): when enabled, CUDA events are
+ * recorded on the launching stream around every main-pass scan launch of
+ * rdb_flat_search; rdb_timing_read synchronises them and returns the summed
+ * device time and the number of timed launches. */
+int rdb_timing_enable(int enable);
+int rdb_timing_read(double* total_ms, int* launches, int reset);
+
 #ifdef __cplusplus
 }
 #endif

@@ -1,0 +1,94 @@
+// Python module rapidadb_b200._C: the names of the reference's rapidadb._C
+// (csrc/bindings/torch_extension.cpp:16-90) plus the IVF / PQ / k-means
+// additions.  Thin: argument conversion only; logic lives in host/*.cpp.
+#include <torch/extension.h>
+
+#include "host.h"
+
+namespace py = pybind11;
+using namespace rdbh;
+
+static at::Tensor opt_tensor(const py::object& o) {
+    if (o.is_none()) return at::Tensor();
+    return o.cast<at::Tensor>();
+}
+
+PYBIND11_MODULE(_C, m) {
+    m.doc() = "RapidaDB B200: sm_100a search kernels behind the RapidaDB API";
+
+    py::enum_<Metric>(m, "Metric")
+        .value("COSINE", Metric::COSINE)
+        .value("L2", Metric::L2)
+        .value("DOT_PRODUCT", Metric::DOT_PRODUCT);
+
+    py::enum_<Precision>(m, "Precision")
+        .value("FP32", Precision::FP32)
+        .value("FP16", Precision::FP16)
+        .value("BF16", Precision::BF16)
+        .value("INT8", Precision::INT8);
+
+    // ---- raw distance ops (torch_extension.cpp:34-44)
+    m.def("cosine_similarity", [](const at::Tensor& q, const at::Tensor& x) { return distance(Metric::COSINE, q, x); },
+          "Cosine similarity matrix [Q, N]", py::arg("queries"), py::arg("database"));
+    m.def("l2_distance", [](const at::Tensor& q, const at::Tensor& x) { return distance(Metric::L2, q, x); },
+          "Squared L2 distance matrix [Q, N]", py::arg("queries"), py::arg("database"));
+    m.def("dot_product", [](const at::Tensor& q, const at::Tensor& x) { return distance(Metric::DOT_PRODUCT, q, x); },
+          "Dot product matrix [Q, N]", py::arg("queries"), py::arg("database"));
+
+    // ---- top-k (torch_extension.cpp:47-63)
+    m.def("topk", [](const at::Tensor& d, int64_t k, bool largest) { return topk(d, k, largest); },
+          "Sorted top-k per row", py::arg("distances"), py::arg("k"), py::arg("largest") = true);
+    m.def("topk_thrust", [](const at::Tensor& d, int64_t k, bool largest) { return topk(d, k, largest); },
+          "Sorted top-k per row (same kernel as topk)", py::arg("distances"), py::arg("k"),
+          py::arg("largest") = true);
+    m.def(
+        "topk_warp_heap",
+        [](const at::Tensor& d, int64_t k, bool largest) {
+            // the reference's warp-heap entry keeps its k <= 128 contract (topk_warp.cu:86)
+            TORCH_CHECK(k > 0 && k <= 128, "warp heap supports k in [1, 128]");
+            return topk(d, k, largest);
+        },
+        "Sorted top-k per row, k <= 128", py::arg("distances"), py::arg("k"), py::arg("largest") = true);
+    m.def("topk_merge", &topk_merge, "Merge [G, Q, k_in] sorted lists into [Q, k]", py::arg("values"),
+          py::arg("ids"), py::arg("k"), py::arg("largest"));
+
+    // ---- FlatIndex (torch_extension.cpp:66-89)
+    py::class_<FlatIndex>(m, "FlatIndex")
+        .def(py::init<int, Metric, Precision>(), py::arg("dim"), py::arg("metric") = Metric::COSINE,
+             py::arg("precision") = Precision::FP32)
+        .def(
+            "add", [](FlatIndex& self, const at::Tensor& v, const py::object& ids) { self.add(v, opt_tensor(ids)); },
+            py::arg("vectors"), py::arg("ids") = py::none())
+        .def(
+            "search", [](const FlatIndex& self, const at::Tensor& q, int64_t k) { return self.search(q, k); },
+            py::arg("queries"), py::arg("k"))
+        .def("reset", &FlatIndex::reset)
+        .def("size", &FlatIndex::size)
+        .def("dim", &FlatIndex::dim)
+        .def("capacity", &FlatIndex::capacity)
+        .def("vectors", &FlatIndex::vectors)
+        .def("ids", &FlatIndex::ids)
+        .def("__len__", &FlatIndex::size)
+        .def("__repr__", [](const FlatIndex& self) {
+            return "FlatIndex(dim=" + std::to_string(self.dim()) + ", size=" + std::to_string(self.size()) + ")";
+        });
+
+    m.def(
+        "search_rows",
+        [](Metric metric, const at::Tensor& rows, int dim, const at::Tensor& xv, const at::Tensor& q, int64_t k,
+           const py::object& ids, int64_t id_offset) {
+            return FlatIndex::search_rows(metric, rows, dim, xv, q, k, opt_tensor(ids), id_offset);
+        },
+        "Fused top-k search over caller-owned padded rows", py::arg("metric"), py::arg("rows"), py::arg("dim"),
+        py::arg("row_values"), py::arg("queries"), py::arg("k"), py::arg("ids") = py::none(),
+        py::arg("id_offset") = 0);
+    m.def("padded_ld", [](int dim, at::ScalarType t) { return padded_ld(dim, t); });
+    m.def("prepare_rows", &prepare_rows, py::arg("src"), py::arg("dtype"), py::arg("ld"));
+    m.def("row_values", &row_values, py::arg("metric"), py::arg("rows"), py::arg("dim"));
+    m.def("abi_version", []() { return rdb_version(); });
+    m.def("device_status", [](bool clear) {
+        unsigned v = 0;
+        check_status(rdb_device_status(&v, clear ? 1 : 0), "device status");
+        return v;
+    }, py::arg("clear") = true);
+}

@@ -186,6 +186,7 @@ __global__ void __launch_bounds__(NT) select_kernel(SelectArgs a) {
         __syncthreads();
 
         // ---- MSD radix select --------------------------------------------
+        int rounds = 0;
         while (!S.done) {
             const int top = S.top;
             const int shift = top > 8 ? top - 8 : 0;
@@ -238,8 +239,10 @@ __global__ void __launch_bounds__(NT) select_kernel(SelectArgs a) {
                     S.top = shift;
                     S.done = (cnt_b == nrem || shift == 0) ? 1 : 0;
                 }
-                (void)owner;
+                if (owner == 0 && lane == 0) S.done = 1;  // no bucket (cannot happen): stop
             }
+            __syncthreads();
+            if (++rounds >= 9 && threadIdx.x == 0) S.done = 1;  // 64-bit keys need <= 8 rounds
             __syncthreads();
         }
 

@@ -8,6 +8,8 @@
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 
+#include <algorithm>
+
 #include "scan.cuh"
 
 namespace rdb {
@@ -279,7 +281,7 @@ int rdb_distance(int metric, int dtype, const void* q, int64_t nq, const void* x
     // grid.x is limited to 2^31-1 splits; chunk the rows for the 65535-query limit only
     for (int64_t qc = 0; qc < nq; qc += 65535LL * kSimtQueries) {
         ScanArgs c = a;
-        c.nq = min(nq - qc, 65535LL * kSimtQueries);
+        c.nq = std::min<int64_t>(nq - qc, 65535LL * kSimtQueries);
         c.q = static_cast<const char*>(q) + qc * d * elem_size(dtype);
         c.dense_out = out + qc * nx;
         c.nsplit = (int)nsplit;

@@ -1,0 +1,149 @@
+"""High-level Python API, the drop-in for python/rapidadb/index.py.
+
+``RapidaDB(dim, metric).add(vectors).search(queries, k)`` with torch tensors
+in and out, as in the reference (index.py:24-140).  Differences:
+
+* IVF and IVF-PQ index types are implemented (the reference raises
+  NotImplementedError, index.py:64-69); they need ``train()`` (or
+  ``set_quantizer``) before ``add``.
+* Inputs keep their float dtype up to the index, which stores rows in
+  ``config.precision`` (FP32 by default, as the reference's fp32 cast);
+  FP16 / BF16 storage searches on the tcgen05 tensor cores.
+"""
+from __future__ import annotations
+
+from typing import Optional, Tuple
+
+import torch
+
+from rapidadb_b200._lib import C
+from rapidadb_b200.config import IndexConfig, IndexType, Metric, Precision
+
+
+def _metric_to_cpp(metric: Metric):
+    """Python Metric -> extension Metric (index.py:12-21)."""
+    _C = C()
+    return {
+        Metric.COSINE: _C.Metric.COSINE,
+        Metric.L2: _C.Metric.L2,
+        Metric.DOT_PRODUCT: _C.Metric.DOT_PRODUCT,
+    }[metric]
+
+
+def _precision_to_cpp(p: Precision):
+    _C = C()
+    return {
+        Precision.FP32: _C.Precision.FP32,
+        Precision.FP16: _C.Precision.FP16,
+        Precision.BF16: _C.Precision.BF16,
+        Precision.INT8: _C.Precision.INT8,
+    }[p]
+
+
+def _as_float_cuda(t: torch.Tensor) -> torch.Tensor:
+    if not t.is_cuda:
+        t = t.cuda()
+    if t.dtype not in (torch.float32, torch.float16, torch.bfloat16):
+        t = t.float()
+    return t.contiguous()
+
+
+class RapidaDB:
+    """GPU vector database (index.py:24-53).
+
+    Example::
+
+        db = RapidaDB(dim=768, metric='cosine')
+        db.add(embeddings)                      # [n, 768] tensor
+        distances, indices = db.search(queries, k=10)
+
+    Args:
+        dim:     Dimensionality of vectors.
+        metric:  'cosine', 'l2' or 'dot_product'.
+        config:  Full IndexConfig (overrides dim / metric if given).
+    """
+
+    def __init__(self, dim: int = 768, metric: str = "cosine",
+                 config: Optional[IndexConfig] = None):
+        if config is not None:
+            self._config = config
+        else:
+            self._config = IndexConfig(dim=dim, metric=Metric(metric))
+        self._index = self._build_index()
+
+    def _build_index(self):
+        _C = C()
+        cfg = self._config
+        if cfg.index_type == IndexType.FLAT:
+            return _C.FlatIndex(cfg.dim, _metric_to_cpp(cfg.metric), _precision_to_cpp(cfg.precision))
+        if cfg.index_type == IndexType.IVF and hasattr(_C, "IVFFlatIndex"):
+            return _C.IVFFlatIndex(cfg.dim, _metric_to_cpp(cfg.metric), cfg.nlist, cfg.nprobe,
+                                   _precision_to_cpp(cfg.precision))
+        if cfg.index_type == IndexType.IVF_PQ and hasattr(_C, "IVFPQIndex"):
+            return _C.IVFPQIndex(cfg.dim, _metric_to_cpp(cfg.metric), cfg.nlist, cfg.nprobe,
+                                 cfg.pq_m, cfg.pq_k)
+        raise NotImplementedError(
+            f"Index type '{cfg.index_type.value}' not available in this build")
+
+    # -------------------------------------------------------------- training
+    def train(self, vectors: torch.Tensor) -> None:
+        """Train the IVF coarse quantizer (and PQ codebooks) on `vectors`."""
+        if not hasattr(self._index, "train"):
+            return
+        cfg = self._config
+        self._index.train(_as_float_cuda(vectors), cfg.kmeans_iters, cfg.seed, cfg.train_sample)
+
+    @property
+    def is_trained(self) -> bool:
+        return bool(getattr(self._index, "is_trained", lambda: True)())
+
+    # ------------------------------------------------------------------- data
+    def add(self, vectors: torch.Tensor, ids: Optional[torch.Tensor] = None) -> None:
+        """Add [n, dim] vectors (moved to CUDA if needed) with optional int64 ids
+        (index.py:71-92)."""
+        vectors = _as_float_cuda(vectors)
+        if ids is not None:
+            if not ids.is_cuda:
+                ids = ids.cuda()
+            ids = ids.contiguous().long()
+            self._index.add(vectors, ids)
+        else:
+            self._index.add(vectors)
+
+    def search(self, queries: torch.Tensor, k: int = 10) -> Tuple[torch.Tensor, torch.Tensor]:
+        """k nearest neighbours of each query -> (distances [B, k] fp32,
+        indices [B, k] int64), best first (index.py:94-112)."""
+        queries = _as_float_cuda(queries)
+        return self._index.search(queries, k)
+
+    def reset(self) -> None:
+        """Remove all vectors (index.py:114-116)."""
+        self._index.reset()
+
+    @property
+    def size(self) -> int:
+        return self._index.size()
+
+    @property
+    def dim(self) -> int:
+        return self._config.dim
+
+    @property
+    def metric(self) -> str:
+        return self._config.metric.value
+
+    @property
+    def config(self) -> IndexConfig:
+        return self._config
+
+    @property
+    def index(self):
+        """The underlying extension index object."""
+        return self._index
+
+    def __len__(self) -> int:
+        return self.size
+
+    def __repr__(self) -> str:
+        return (f"RapidaDB(dim={self.dim}, metric='{self.metric}', "
+                f"index='{self._config.index_type.value}', size={self.size})")

@@ -1,0 +1,74 @@
+"""Row-sharded search over one process per GPU (torch.distributed).
+
+The reference is single-GPU (its README.md:14 only claims multi-GPU).  Here
+the database is split by rows across the ranks of a process group: every rank
+holds a contiguous slice with global ids, answers the same query batch with its
+local fused search, the per-rank [Q, k] candidate lists are exchanged with ONE
+all-gather (NCCL over NVLink on GPUs, gloo on CPU in tests), and a final merge
+kernel keeps the best k per query.  k-means centroid sums are reduced with an
+all-reduce (see rapidadb_b200.kmeans).
+
+``local_search`` and ``merge`` are injectable so the exchange logic can be
+exercised on CPU ranks with the oracle standing in for the GPU parts.
+"""
+from __future__ import annotations
+
+from typing import Callable, Optional, Tuple
+
+import torch
+import torch.distributed as dist
+
+
+def shard_range(n: int, rank: int, world: int) -> Tuple[int, int]:
+    """Contiguous rows [lo, hi) of rank `rank` when n rows are split evenly
+    (the first n % world ranks get one extra row)."""
+    base, extra = divmod(n, world)
+    lo = rank * base + min(rank, extra)
+    hi = lo + base + (1 if rank < extra else 0)
+    return lo, hi
+
+
+def gather_candidates(local_d: torch.Tensor, local_i: torch.Tensor,
+                      group: Optional[dist.ProcessGroup] = None) -> Tuple[torch.Tensor, torch.Tensor]:
+    """All-gather [Q, k] scores and ids from every rank into [G, Q, k]."""
+    world = dist.get_world_size(group)
+    Q, k = local_d.shape
+    out_d = torch.empty((world, Q, k), dtype=local_d.dtype, device=local_d.device)
+    out_i = torch.empty((world, Q, k), dtype=local_i.dtype, device=local_i.device)
+    dist.all_gather_into_tensor(out_d, local_d.contiguous(), group=group)
+    dist.all_gather_into_tensor(out_i, local_i.contiguous(), group=group)
+    return out_d, out_i
+
+
+def gpu_merge(vals: torch.Tensor, ids: torch.Tensor, k: int, largest: bool):
+    from rapidadb_b200._lib import C
+
+    return C().topk_merge(vals, ids, k, largest)
+
+
+class ShardedSearch:
+    """Search one query batch against a row-sharded index.
+
+    Args:
+        index:        this rank's index object (anything with .search(q, k)
+                      returning (scores [Q, k], global ids [Q, k])), or a
+                      callable (q, k) -> (scores, ids).
+        largest:      True for cosine / dot (descending), False for L2.
+        group:        process group (default: the world).
+        merge:        (vals [G,Q,k], ids [G,Q,k], k, largest) -> (vals, ids);
+                      defaults to the GPU merge kernel.
+    """
+
+    def __init__(self, index, largest: bool, group: Optional[dist.ProcessGroup] = None,
+                 merge: Optional[Callable] = None):
+        self.search_fn = index if callable(index) and not hasattr(index, "search") else index.search
+        self.largest = largest
+        self.group = group
+        self.merge = merge or gpu_merge
+
+    def search(self, queries: torch.Tensor, k: int) -> Tuple[torch.Tensor, torch.Tensor]:
+        local_d, local_i = self.search_fn(queries, k)
+        if not dist.is_initialized() or dist.get_world_size(self.group) == 1:
+            return local_d, local_i
+        vals, ids = gather_candidates(local_d, local_i, self.group)
+        return self.merge(vals, ids, k, self.largest)

@@ -1,0 +1,81 @@
+"""CPU-only checks of the native boundary: the C-ABI library loads and exports
+every function include/rapidadb_b200.h declares, the extension imports, and
+argument errors are raised without touching a GPU."""
+import ctypes
+import os
+import re
+
+import pytest
+import torch
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+HEADER = os.path.join(ROOT, "include", "rapidadb_b200.h")
+LIB = os.path.join(ROOT, "rapidadb_b200", "librdb_kernels.so")
+
+
+def declared_functions():
+    src = open(HEADER).read()
+    src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
+    return sorted(set(re.findall(r"\b(rdb_[a-z0-9_]+)\s*\(", src)))
+
+
+def test_header_declares_entry_points():
+    names = declared_functions()
+    for n in ("rdb_flat_search", "rdb_distance", "rdb_topk", "rdb_topk_merge", "rdb_last_error"):
+        assert n in names
+
+
+def test_library_exports_every_declared_symbol():
+    lib = ctypes.CDLL(LIB)
+    missing = [n for n in declared_functions() if not hasattr(lib, n)]
+    assert not missing, f"not exported: {missing}"
+
+
+def test_abi_calls_without_gpu():
+    """Pure host-side entry points work on a CPU-only machine."""
+    lib = ctypes.CDLL(LIB)
+    lib.rdb_version.restype = ctypes.c_int
+    assert lib.rdb_version() >= 100
+    lib.rdb_last_error.restype = ctypes.c_char_p
+    lib.rdb_flat_search_workspace.restype = ctypes.c_size_t
+    lib.rdb_flat_search_workspace.argtypes = [ctypes.c_int, ctypes.c_int, ctypes.c_int64, ctypes.c_int64,
+                                              ctypes.c_int, ctypes.c_int, ctypes.c_int]
+    ws = lib.rdb_flat_search_workspace(0, 2, 1024, 1_000_000, 768, 100, 0)
+    assert 0 < ws < (1 << 31)
+    # exhaustive workspace bounds every candidate list by its split
+    ws_ex = lib.rdb_flat_search_workspace(0, 2, 1024, 1_000_000, 768, 100, 1)
+    assert ws_ex >= 1024 * 1_000_000 * 8
+
+
+def test_argument_errors_reported():
+    lib = ctypes.CDLL(LIB)
+    lib.rdb_last_error.restype = ctypes.c_char_p
+    # k > n is rejected before any device work
+    f = lib.rdb_flat_search
+    f.restype = ctypes.c_int
+    rc = f(1, 2, None, ctypes.c_int64(1), ctypes.c_int64(8), None, ctypes.c_int64(5), ctypes.c_int64(8),
+           None, 8, 6, None, ctypes.c_int64(0), 0, None, None, None, ctypes.c_size_t(0), None)
+    assert rc == 1
+    assert b"k must be in [1, 5]" in lib.rdb_last_error()
+
+
+def test_extension_imports_and_rejects_cpu_tensors():
+    import rapidadb._C as _C
+
+    with pytest.raises(RuntimeError, match="CUDA"):
+        _C.l2_distance(torch.randn(2, 8), torch.randn(3, 8))
+    idx = _C.FlatIndex(8, _C.Metric.L2)
+    with pytest.raises(RuntimeError, match="must be on CUDA"):
+        idx.add(torch.randn(3, 8))
+    assert repr(idx) == "FlatIndex(dim=8, size=0)"
+
+
+def test_dropin_surface():
+    import rapidadb
+    from rapidadb import IndexConfig, Metric, RapidaDB
+
+    db = RapidaDB(dim=32, metric="l2")
+    assert db.dim == 32 and db.metric == "l2" and len(db) == 0
+    assert "index='flat'" in repr(db)
+    assert IndexConfig().nlist == 4096 and Metric("dot_product") == Metric.DOT_PRODUCT
+    assert rapidadb.RapidaDB is RapidaDB
