@@ -70,19 +70,22 @@ struct FlatPlan {
     int qtile, rtile;
     int64_t nq;  // queries in one chunk
     bool sample;
+    int group;        // tensor-core sample pass: rows per group maximum
+    int64_t ngroups;  // sample rows / group
     PassPlan s, m;
     size_t ws_bytes;
     size_t off_qv, off_thr, off_cand, off_counts, off_flag;
 };
 
-PassPlan plan_pass(int64_t rows, int64_t row_step, int64_t nq, int qtile, int rtile, int sms,
-                   bool tc) {
+// target: (split x query-block) units to launch, about one per SM for the
+// tensor-core scan (a CTA pair per two SMs when queries come in 256s), two per
+// SM for the CUDA-core scan
+PassPlan plan_pass(int64_t rows, int64_t row_step, int64_t nq, int qtile, int rtile, int64_t target) {
     PassPlan p;
     p.rows = rows;
     p.row_step = row_step;
     int64_t nqb = (nq + qtile - 1) / qtile;
     int64_t ntiles = (rows + rtile - 1) / rtile;
-    int64_t target = tc ? sms : 2LL * sms;
     int64_t nsplit = std::max<int64_t>(1, target / std::max<int64_t>(nqb, 1));
     nsplit = std::min<int64_t>(nsplit, std::max<int64_t>(ntiles, 1));
     nsplit = std::min<int64_t>(nsplit, 1024);
@@ -99,10 +102,12 @@ FlatPlan make_plan(int metric, int dtype, int64_t nq, int64_t n, int d, int k, i
     (void)d;
     FlatPlan P = {};
     P.tc = tc_ok && (dtype == RDB_F16 || dtype == RDB_BF16);
-    P.qtile = P.tc ? kTcQueries : kSimtQueries;
+    const bool pair = P.tc && tc_use_pair(nq);
+    P.qtile = P.tc ? (pair ? 2 * kTcQueries : kTcQueries) : kSimtQueries;
     P.rtile = P.tc ? kTcRows : kSimtRows;
     P.nq = nq;
     const int sms = num_sms();
+    const int64_t target = P.tc ? (pair ? sms / 2 : sms) : 2LL * sms;
 
     // sample size: ~1.5 sqrt(n k) rows (balances sample cost against the
     // candidate volume n k / S), a power of two in [1024, 32768], >= 8 k
@@ -113,16 +118,25 @@ FlatPlan make_plan(int metric, int dtype, int64_t nq, int64_t n, int d, int k, i
     P.sample = !(flags & RDB_SEARCH_EXHAUSTIVE) && n >= 4 * S;
     if (P.sample) {
         int64_t step = n / S;
-        P.s = plan_pass(S, step, nq, P.qtile, P.rtile, sms, P.tc);
+        P.s = plan_pass(S, step, nq, P.qtile, P.rtile, target);
+        // tensor-core sample pass keeps the best score of each group of
+        // `group` sample rows; the k-th best of those group maxima is still a
+        // lower bound on the k-th best score (k distinct rows reach it), and
+        // with >= 4 k groups it is nearly as tight as the k-th best row
+        P.group = 1;
+        while (P.group < 16 && S / (2 * P.group) >= 4LL * k) P.group <<= 1;
+        P.ngroups = S / P.group;
     }
-    P.m = plan_pass(n, 1, nq, P.qtile, P.rtile, sms, P.tc);
+    P.m = plan_pass(n, 1, nq, P.qtile, P.rtile, target);
     if (P.sample) {
         // expected candidates per split: rps * k / S; keep 8x headroom
         int64_t expect = (int64_t)ceil((double)P.m.rps * (double)k / (double)S);
         P.m.cap = std::min<int64_t>(P.m.rps, std::max<int64_t>(1024, 8 * expect + 256));
     }
     size_t cand_main = (size_t)P.m.nsplit * nq * P.m.cap * sizeof(uint2);
-    size_t cand_samp = P.sample ? (size_t)P.s.nsplit * nq * P.s.cap * sizeof(uint2) : 0;
+    size_t cand_samp = !P.sample ? 0
+                       : P.tc ? (size_t)nq * P.ngroups * sizeof(float)
+                              : (size_t)P.s.nsplit * nq * P.s.cap * sizeof(uint2);
     size_t cnt_main = (size_t)P.m.nsplit * nq * sizeof(int);
     size_t cnt_samp = P.sample ? (size_t)P.s.nsplit * nq * sizeof(int) : 0;
     size_t off = 0;
@@ -207,7 +221,29 @@ int run_chunk(const FlatPlan& P, int metric, int dtype, const void* q, int64_t n
         return P.tc ? launch_scan_tc(sc, SCAN_FILTER, s) : launch_scan_simt(sc, SCAN_FILTER, s);
     };
 
-    if (P.sample) {
+    if (P.sample && P.tc) {
+        // group maxima over the strided sample, then the k-th best of them
+        ScanArgs sc = a;
+        sc.n = P.s.rows;
+        sc.row_step = P.s.row_step;
+        sc.thr = nullptr;
+        sc.nsplit = P.s.nsplit;
+        sc.rows_per_split = P.s.rps;
+        sc.group_out = reinterpret_cast<float*>(cand);
+        sc.group = P.group;
+        sc.ngroups = P.ngroups;
+        RDB_TRY(launch_scan_tc(sc, SCAN_GROUPMAX, s));
+        SelectArgs ss = {};
+        ss.input = SEL_DENSE;
+        ss.output = SEL_OUT_THRESHOLD;
+        ss.nq = nq;
+        ss.k = k;
+        ss.largest = largest ? 1 : 0;
+        ss.dense = reinterpret_cast<const float*>(cand);
+        ss.dense_n = P.ngroups;
+        ss.out_thr = thr;
+        RDB_TRY(launch_select(ss, s));
+    } else if (P.sample) {
         ScanArgs sc = a;
         sc.n = P.s.rows;
         sc.row_step = P.s.row_step;

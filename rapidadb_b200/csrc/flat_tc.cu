@@ -1,13 +1,15 @@
 // tcgen05 fused scan for fp16 / bf16 rows (sm_100a).
 //
-// One CTA = 128 queries (UMMA M) x a contiguous split of rows, walked in tiles
-// of 256 rows (UMMA N).  Warp roles:
+// One CTA = 128 queries x a contiguous split of rows, walked in tiles of 256
+// rows (UMMA N = 256); with more than 128 queries two CTAs pair up (UMMA
+// M = 256, see TcCfg).  Warp roles:
 //   warp 0      TMA producer: per K block of 64 (one 128-byte swizzle atom)
-//               loads the 128 x 64 query tile and the 256 x 64 row tile into a
-//               4-stage shared-memory ring (SWIZZLE_128B, K-major).
+//               loads the query tile and the row tile into a shared-memory
+//               ring (SWIZZLE_128B, K-major).
 //   warp 1      allocates 512 TMEM columns (two 128 x 256 fp32 accumulators);
-//               one lane issues tcgen05.mma kind::f16 (K = 16 per instruction)
-//               and commits stage releases / accumulator-ready barriers.
+//               one lane (of the leader CTA) issues tcgen05.mma kind::f16
+//               (K = 16 per instruction) and commits stage releases /
+//               accumulator-ready barriers.
 //   warps 2..5  epilogue: each thread owns one query row (one TMEM lane),
 //               reads 32 accumulator columns per tcgen05.ld and keeps only the
 //               rows whose dot product passes the query's threshold
@@ -31,15 +33,14 @@ constexpr int BM = kTcQueries;  // 128
 constexpr int BN = kTcRows;     // 256
 constexpr int BK = 64;
 constexpr int UK = 16;
-constexpr int STAGES = 4;
-constexpr int A_BYTES = BM * BK * 2;
-constexpr int B_BYTES = BN * BK * 2;
-constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
 constexpr int NUM_ACC = 2;
 constexpr int TMEM_COLS = 512;
 constexpr int NUM_THREADS = 192;
 constexpr int BAR_BYTES = 256;
-constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 + BAR_BYTES;
+constexpr int EPI_THREADS = 128;
+constexpr int kStageStride = 36;  // floats per staged chunk row (32 + pad, 16-byte aligned)
+constexpr int XV_BYTES = 2 * BN * 4;
+constexpr int STAGE_ROWS_BYTES = EPI_THREADS * kStageStride * 4;
 
 static_assert(NUM_ACC * BN <= TMEM_COLS, "accumulators exceed TMEM allocation");
 
@@ -91,6 +92,26 @@ __device__ __noinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile 
         if (*abort_flag) return false;
         if (globaltimer_ns() - t0 > kWaitLimitNs) return false;
     }
+}
+
+// Named barrier among the four epilogue warps (id 1; id 0 is __syncthreads).
+__device__ __forceinline__ void epi_bar_sync() {
+    asm volatile("bar.sync 1, %0;" ::"n"(EPI_THREADS) : "memory");
+}
+
+// Same barrier with an AND-reduction: every epilogue thread learns whether all
+// of them succeeded, so they leave the tile loop together.
+__device__ __forceinline__ bool epi_bar_and(bool ok) {
+    uint32_t r;
+    asm volatile(
+        "{\n\t.reg .pred pin, pout;\n\t"
+        "setp.ne.u32 pin, %1, 0;\n\t"
+        "bar.red.and.pred pout, 1, %2, pin;\n\t"
+        "selp.u32 %0, 1, 0, pout;\n\t}"
+        : "=r"(r)
+        : "r"(ok ? 1u : 0u), "n"(EPI_THREADS)
+        : "memory");
+    return r != 0;
 }
 
 __device__ __forceinline__ void tma_load_2d(const CUtensorMap* map, uint64_t* bar, void* dst, int x,
@@ -178,44 +199,158 @@ __device__ __forceinline__ uint64_t make_sdesc(uint32_t saddr) {
 }
 
 // Instruction descriptor, kind::f16: D fp32, A/B fp16 (0) or bf16 (1),
-// both K-major, N = BN, M = BM.
-__host__ __device__ constexpr uint32_t make_idesc(bool bf16) {
+// both K-major, N = BN, M = 128 (one CTA) or 256 (CTA pair).
+__host__ __device__ constexpr uint32_t make_idesc(bool bf16, int m) {
     return (1u << 4) | ((bf16 ? 1u : 0u) << 7) | ((bf16 ? 1u : 0u) << 10) |
-           (static_cast<uint32_t>(BN >> 3) << 17) | (static_cast<uint32_t>(BM >> 4) << 24);
+           (static_cast<uint32_t>(BN >> 3) << 17) | (static_cast<uint32_t>(m >> 4) << 24);
 }
 
 // ------------------------------------------------------------------ kernel --
+//
+// Two launch shapes share one body:
+//   single CTA  (PAIR = false): UMMA M = 128, the CTA loads its 128 queries and
+//               all 256 rows of each tile; 4 stages of 48 KB.
+//   CTA pair    (PAIR = true, cluster of 2, tcgen05 cta_group::2): UMMA
+//               M = 256 across the pair.  CTA r loads its own 128 queries and
+//               rows [128 r, 128 r + 128) of each 256-row tile, so a pair reads
+//               every row tile once for 256 queries (a third less L2 traffic
+//               per SM than the single-CTA shape); 6 stages of 32 KB.  Only
+//               the leader (rank 0) issues MMAs; both CTAs' TMA loads complete
+//               on the leader's stage barrier; stage / accumulator releases
+//               are committed to both CTAs; both epilogues arrive on the
+//               leader's accumulator-empty barrier.  No TMA load uses
+//               multicast.
 
-template <int MODE>
-__global__ void __launch_bounds__(NUM_THREADS, 1)
-    tc_scan_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_constant__ CUtensorMap tmap_x,
-                   const ScanArgs a, const uint32_t idesc, unsigned* status) {
-    extern __shared__ uint8_t smem_raw[];
+template <bool PAIR>
+struct TcCfg {
+    static constexpr int B_ROWS = PAIR ? BN / 2 : BN;  // rows of B loaded per CTA
+    static constexpr int A_B = BM * BK * 2;
+    static constexpr int B_B = B_ROWS * BK * 2;
+    static constexpr int STAGE_B = A_B + B_B;
+    static constexpr int NSTAGE = PAIR ? 6 : 4;
+    static constexpr int UMMA_M = PAIR ? 2 * BM : BM;
+    static constexpr int SMEM = NSTAGE * STAGE_B + 1024 + BAR_BYTES + XV_BYTES + STAGE_ROWS_BYTES;
+};
+static_assert(TcCfg<false>::SMEM <= 232448 && TcCfg<true>::SMEM <= 232448, "shared memory over 227 KB");
+
+__device__ __forceinline__ uint32_t cluster_rank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+
+__device__ __forceinline__ void cluster_sync_all() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+// shared::cluster address of the same shared-memory offset in CTA `rank`
+__device__ __forceinline__ uint32_t map_to_rank(const void* p, uint32_t rank) {
+    uint32_t r;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_u32(p)), "r"(rank));
+    return r;
+}
+
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
+    asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
+
+// 2-CTA tensor load: data lands in this CTA's shared memory, the transaction
+// bytes complete on the barrier at `bar_cluster` (the leader's stage barrier).
+__device__ __forceinline__ void tma_load_2d_pair(const CUtensorMap* map, uint32_t bar_cluster, void* dst,
+                                                 int x, int y) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%3, %4}], [%2];" ::"r"(smem_u32(dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(bar_cluster), "r"(x), "r"(y)
+        : "memory");
+}
+
+template <bool PAIR>
+__device__ __forceinline__ void tmem_alloc_t(uint32_t* dst, uint32_t ncols) {
+    if (PAIR)
+        asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(dst)),
+                     "r"(ncols)
+                     : "memory");
+    else
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(dst)),
+                     "r"(ncols)
+                     : "memory");
+}
+
+template <bool PAIR>
+__device__ __forceinline__ void tmem_relinquish_t() {
+    if (PAIR)
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+    else
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+
+template <bool PAIR>
+__device__ __forceinline__ void tmem_dealloc_t(uint32_t taddr, uint32_t ncols) {
+    if (PAIR)
+        asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+    else
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+
+__device__ __forceinline__ void umma_f16_pair(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                              uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
+// Commit of the pair's MMAs: arrives on the barrier at the same offset in both CTAs.
+__device__ __forceinline__ void umma_commit_pair_both(uint64_t* bar) {
+    asm volatile(
+        "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(
+            smem_u32(bar)),
+        "h"(static_cast<uint16_t>(3))
+        : "memory");
+}
+
+__device__ __forceinline__ void umma_commit_pair_self(uint64_t* bar) {
+    asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+                 : "memory");
+}
+
+template <int MODE, bool PAIR>
+__device__ __forceinline__ void tc_scan_body(uint8_t* smem_raw, const CUtensorMap& tmap_q, const CUtensorMap& tmap_x,
+                                             const ScanArgs& a, const uint32_t idesc, unsigned* status) {
+    using Cfg = TcCfg<PAIR>;
+    constexpr int NST = Cfg::NSTAGE;
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES);
-    uint64_t* empty = full + STAGES;
-    uint64_t* tfull = empty + STAGES;
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + NST * Cfg::STAGE_B);
+    uint64_t* empty = full + NST;
+    uint64_t* tfull = empty + NST;
     uint64_t* tempty = tfull + NUM_ACC;
     uint64_t* mma_done = tempty + NUM_ACC;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done + 1);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+    float* xv_s = reinterpret_cast<float*>(smem + NST * Cfg::STAGE_B + BAR_BYTES);
+    float* stage_rows = xv_s + 2 * BN;
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int split = blockIdx.x;
-    const int64_t q0 = static_cast<int64_t>(blockIdx.y) * BM;
+    const uint32_t rank = PAIR ? cluster_rank() : 0u;
+    const bool leader = rank == 0;
+    const int split = PAIR ? static_cast<int>(blockIdx.x >> 1) : static_cast<int>(blockIdx.x);
+    const int64_t q0 = (PAIR ? (2 * static_cast<int64_t>(blockIdx.y) + rank) : static_cast<int64_t>(blockIdx.y)) * BM;
     const int64_t r_begin = static_cast<int64_t>(split) * a.rows_per_split;
     const int64_t r_end = min(a.n, r_begin + a.rows_per_split);
     const int ntiles = r_end > r_begin ? static_cast<int>((r_end - r_begin + BN - 1) / BN) : 0;
     const int nk = (a.d + BK - 1) / BK;
 
     if (threadIdx.x == 0) {
-        for (int s = 0; s < STAGES; ++s) {
+        for (int s = 0; s < NST; ++s) {
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], 1);
         }
         for (int c = 0; c < NUM_ACC; ++c) {
             mbar_init(&tfull[c], 1);
-            mbar_init(&tempty[c], 4);
+            mbar_init(&tempty[c], PAIR ? 8 : 4);
         }
         mbar_init(mma_done, 1);
         *abort_flag = 0;
@@ -224,13 +359,21 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         tma_prefetch_desc(&tmap_x);
     }
     if (warp == 1) {
-        tmem_alloc(tmem_slot, TMEM_COLS);
-        tmem_relinquish();
+        tmem_alloc_t<PAIR>(tmem_slot, TMEM_COLS);
+        tmem_relinquish_t<PAIR>();
     }
     tc_fence_before();
-    __syncthreads();
+    if (PAIR)
+        cluster_sync_all();  // both CTAs' barriers initialised before any remote use
+    else
+        __syncthreads();
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
+    // the leader's barriers as shared::cluster addresses (own barriers without a pair)
+    uint32_t full_lead0 = PAIR ? map_to_rank(&full[0], 0) : smem_u32(&full[0]);
+    uint32_t tempty_lead[NUM_ACC];
+#pragma unroll
+    for (int c = 0; c < NUM_ACC; ++c) tempty_lead[c] = PAIR ? map_to_rank(&tempty[c], 0) : smem_u32(&tempty[c]);
 
     if (warp == 0) {
         if (lane == 0) {
@@ -240,19 +383,27 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             uint32_t issued_mask = 0, issued_phase = 0;
             bool ok = true;
             for (int t = 0; t < ntiles && ok; ++t) {
-                const int row0 = static_cast<int>(r_begin + static_cast<int64_t>(t) * BN);
+                const int row0 = static_cast<int>(r_begin + static_cast<int64_t>(t) * BN) +
+                                 static_cast<int>(rank) * Cfg::B_ROWS;
                 for (int kb = 0; kb < nk; ++kb) {
                     if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag)) {
                         ok = false;
                         break;
                     }
-                    mbar_arrive_expect_tx(&full[stage], STAGE_BYTES);
-                    uint8_t* sa = smem + stage * STAGE_BYTES;
-                    tma_load_2d(&tmap_q, &full[stage], sa, kb * BK, static_cast<int>(q0));
-                    tma_load_2d(&tmap_x, &full[stage], sa + A_BYTES, kb * BK, row0);
+                    uint8_t* sa = smem + stage * Cfg::STAGE_B;
+                    if (PAIR) {
+                        if (leader) mbar_arrive_expect_tx(&full[stage], 2 * Cfg::STAGE_B);
+                        const uint32_t bar = full_lead0 + static_cast<uint32_t>(stage * sizeof(uint64_t));
+                        tma_load_2d_pair(&tmap_q, bar, sa, kb * BK, static_cast<int>(q0));
+                        tma_load_2d_pair(&tmap_x, bar, sa + Cfg::A_B, kb * BK, row0);
+                    } else {
+                        mbar_arrive_expect_tx(&full[stage], Cfg::STAGE_B);
+                        tma_load_2d(&tmap_q, &full[stage], sa, kb * BK, static_cast<int>(q0));
+                        tma_load_2d(&tmap_x, &full[stage], sa + Cfg::A_B, kb * BK, row0);
+                    }
                     issued_mask |= 1u << stage;
                     issued_phase = (issued_phase & ~(1u << stage)) | (phase << stage);
-                    if (++stage == STAGES) {
+                    if (++stage == NST) {
                         stage = 0;
                         phase ^= 1;
                     }
@@ -261,18 +412,20 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             if (!ok) {
                 *abort_flag = 1;
                 if (status) atomicOr(status, DEV_TIMEOUT_PRODUCER);
-                // let this thread's loads land before the CTA's shared memory is released
-                for (int s = 0; s < STAGES; ++s)
-                    if (issued_mask & (1u << s)) {
-                        const uint64_t t0 = globaltimer_ns();
-                        while (!mbar_try_wait(&full[s], (issued_phase >> s) & 1) &&
-                               globaltimer_ns() - t0 < kWaitLimitNs) {
+                // let the loads tracked by this CTA's barriers land before its
+                // shared memory is released
+                if (!PAIR || leader)
+                    for (int s = 0; s < NST; ++s)
+                        if (issued_mask & (1u << s)) {
+                            const uint64_t t0 = globaltimer_ns();
+                            while (!mbar_try_wait(&full[s], (issued_phase >> s) & 1) &&
+                                   globaltimer_ns() - t0 < kWaitLimitNs) {
+                            }
                         }
-                    }
             }
         }
     } else if (warp == 1) {
-        if (lane == 0) {
+        if (lane == 0 && leader) {
             // ---------------------------------------------- MMA issuer
             int stage = 0;
             uint32_t phase = 0;
@@ -292,21 +445,32 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                         break;
                     }
                     tc_fence_after();
-                    const uint32_t a_addr = smem_u32(smem + stage * STAGE_BYTES);
+                    const uint32_t a_addr = smem_u32(smem + stage * Cfg::STAGE_B);
                     const uint64_t adesc = make_sdesc(a_addr);
-                    const uint64_t bdesc = make_sdesc(a_addr + A_BYTES);
+                    const uint64_t bdesc = make_sdesc(a_addr + Cfg::A_B);
 #pragma unroll
-                    for (int k = 0; k < BK / UK; ++k)
-                        umma_f16(d_tmem, adesc + 2 * k, bdesc + 2 * k, idesc,
-                                 (kb > 0 || k > 0) ? 1u : 0u);
+                    for (int k = 0; k < BK / UK; ++k) {
+                        if (PAIR)
+                            umma_f16_pair(d_tmem, adesc + 2 * k, bdesc + 2 * k, idesc, (kb > 0 || k > 0) ? 1u : 0u);
+                        else
+                            umma_f16(d_tmem, adesc + 2 * k, bdesc + 2 * k, idesc, (kb > 0 || k > 0) ? 1u : 0u);
+                    }
                     any = true;
-                    umma_commit(&empty[stage]);
-                    if (++stage == STAGES) {
+                    if (PAIR)
+                        umma_commit_pair_both(&empty[stage]);
+                    else
+                        umma_commit(&empty[stage]);
+                    if (++stage == NST) {
                         stage = 0;
                         phase ^= 1;
                     }
                 }
-                if (ok) umma_commit(&tfull[acc]);
+                if (ok) {
+                    if (PAIR)
+                        umma_commit_pair_both(&tfull[acc]);
+                    else
+                        umma_commit(&tfull[acc]);
+                }
             }
             if (!ok) {
                 *abort_flag = 1;
@@ -314,7 +478,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             }
             if (any) {
                 // wait for every MMA this thread issued before TMEM is freed
-                umma_commit(mma_done);
+                if (PAIR)
+                    umma_commit_pair_self(mma_done);
+                else
+                    umma_commit(mma_done);
                 const uint64_t t0 = globaltimer_ns();
                 while (!mbar_try_wait(mma_done, 0) && globaltimer_ns() - t0 < kWaitLimitNs) {
                 }
@@ -322,7 +489,14 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         }
     } else {
         // -------------------------------------------------- epilogue
-        const int quad = warp & 3;  // TMEM lanes this warp may read
+        // Thread = one query row = one TMEM lane.  Per tile the 256 per-row
+        // values xv[] sit in shared memory (loaded one tile ahead by these
+        // 128 threads); per 32-column chunk the pass test is branch-free
+        // (one FFMA + FSETP + predicated OR per column), and only lanes with a
+        // hit stage their chunk in shared memory to append it.
+        const int ew = warp - 2;          // 0..3
+        const int quad = warp & 3;        // TMEM lanes this warp may read
+        const int etid = ew * 32 + lane;  // 0..127
         const int qrow = quad * 32 + lane;
         const int64_t q = q0 + qrow;
         const bool qvalid = q < a.nq;
@@ -332,24 +506,41 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             const float thr = (qvalid && a.thr) ? a.thr[q] : __int_as_float(0x7fc00000);
             fc = filter_coef(a.metric, a.cos_small, thr, qv);
         }
+        const float nA = -fc.A;
         uint2* cbase = (MODE == SCAN_FILTER && qvalid)
                            ? a.cand + (static_cast<int64_t>(split) * a.nq + q) * a.cap
                            : nullptr;
+        float* stg = stage_rows + (ew * 32 + lane) * kStageStride;
         int64_t cnt = 0;
         float best = -INFINITY;
         uint32_t best_r = 0;
         const float* __restrict__ xvp = a.xv;
         const int64_t step = a.row_step;
+        // per-row values of tile t -> xv_s[t & 1]; each thread covers 2 rows
+        auto load_xv = [&](int t, float2& out) {
+            const int64_t r = r_begin + static_cast<int64_t>(t) * BN + 2 * etid;
+            out.x = (xvp && r < r_end) ? __ldg(xvp + r * step) : 0.f;
+            out.y = (xvp && r + 1 < r_end) ? __ldg(xvp + (r + 1) * step) : 0.f;
+        };
+        float2 xv_next = make_float2(0.f, 0.f);
+        if (ntiles > 0) {
+            load_xv(0, xv_next);
+            reinterpret_cast<float2*>(xv_s)[etid] = xv_next;
+        }
+        epi_bar_sync();
         for (int t = 0; t < ntiles; ++t) {
             const int acc = t & 1;
             const uint32_t acc_phase = (t >> 1) & 1;
-            if (!mbar_wait(&tfull[acc], acc_phase, abort_flag)) {
+            if (t + 1 < ntiles) load_xv(t + 1, xv_next);
+            // all four epilogue warps leave together if any wait gave up
+            if (!epi_bar_and(mbar_wait(&tfull[acc], acc_phase, abort_flag))) {
                 *abort_flag = 1;
                 if (status) atomicOr(status, DEV_TIMEOUT_EPILOGUE);
                 break;
             }
             tc_fence_after();
             const int64_t row0 = r_begin + static_cast<int64_t>(t) * BN;
+            const float* xs_tile = xv_s + acc * BN;
 #pragma unroll 1
             for (int c = 0; c < BN / 32; ++c) {
                 float v[32];
@@ -357,54 +548,124 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                               static_cast<uint32_t>(acc * BN + c * 32),
                           v);
                 const int64_t col0 = row0 + c * 32;
-                const int nvalid = static_cast<int>(min(static_cast<int64_t>(32), r_end - col0));
-                float xv[32];
-                if (step == 1 && nvalid == 32 && xvp) {
-                    const float4* p4 = reinterpret_cast<const float4*>(xvp + col0);
-#pragma unroll
-                    for (int j = 0; j < 8; ++j) {
-                        float4 f = __ldg(p4 + j);
-                        xv[4 * j] = f.x;
-                        xv[4 * j + 1] = f.y;
-                        xv[4 * j + 2] = f.z;
-                        xv[4 * j + 3] = f.w;
-                    }
-                } else {
-#pragma unroll
-                    for (int j = 0; j < 32; ++j)
-                        xv[j] = (j < nvalid && xvp) ? __ldg(xvp + (col0 + j) * step) : 0.f;
-                }
+                const int64_t nv64 = r_end - col0;
+                const uint32_t valid = nv64 >= 32 ? 0xffffffffu : (nv64 > 0 ? ((1u << nv64) - 1u) : 0u);
+                const float4* xs4 = reinterpret_cast<const float4*>(xs_tile + c * 32);
                 if (MODE == SCAN_FILTER) {
-                    if (qvalid) {
+                    uint32_t m = 0;
 #pragma unroll
-                        for (int j = 0; j < 32; ++j) {
-                            if (j < nvalid && v[j] >= fmaf(fc.A, xv[j], fc.B)) {
-                                if (cnt < a.cap)
-                                    cbase[cnt] = make_uint2(__float_as_uint(v[j]),
-                                                            static_cast<uint32_t>(col0 + j));
-                                ++cnt;
-                            }
+                    for (int j4 = 0; j4 < 8; ++j4) {
+                        const float4 x4 = xs4[j4];
+                        const float xx[4] = {x4.x, x4.y, x4.z, x4.w};
+#pragma unroll
+                        for (int u = 0; u < 4; ++u) {
+                            const int j = 4 * j4 + u;
+                            if (fmaf(nA, xx[u], v[j]) >= fc.B) m |= 1u << j;
                         }
+                    }
+                    m &= valid;
+                    if (!qvalid) m = 0;
+                    if (m) {
+                        float4* st4 = reinterpret_cast<float4*>(stg);
+#pragma unroll
+                        for (int j4 = 0; j4 < 8; ++j4)
+                            st4[j4] = make_float4(v[4 * j4], v[4 * j4 + 1], v[4 * j4 + 2], v[4 * j4 + 3]);
+                        do {
+                            const int j = __ffs(m) - 1;
+                            m &= m - 1;
+                            if (cnt < a.cap) {
+                                const float sc = final_score(a.metric, a.cos_small, stg[j], qv, xs_tile[c * 32 + j]);
+                                cbase[cnt] = make_uint2(__float_as_uint(sc), static_cast<uint32_t>(col0 + j));
+                            }
+                            ++cnt;
+                        } while (m);
                     }
                 } else if (MODE == SCAN_ARGMIN) {
 #pragma unroll
-                    for (int j = 0; j < 32; ++j) {
-                        const float tt = fmaf(-0.5f, xv[j], v[j]);
-                        if (j < nvalid && tt > best) {
-                            best = tt;
-                            best_r = static_cast<uint32_t>(col0 + j);
+                    for (int j4 = 0; j4 < 8; ++j4) {
+                        const float4 x4 = xs4[j4];
+                        const float xx[4] = {x4.x, x4.y, x4.z, x4.w};
+#pragma unroll
+                        for (int u = 0; u < 4; ++u) {
+                            const int j = 4 * j4 + u;
+                            const float tt = fmaf(-0.5f, xx[u], v[j]);
+                            if (((valid >> j) & 1u) && tt > best) {
+                                best = tt;
+                                best_r = static_cast<uint32_t>(col0 + j);
+                            }
+                        }
+                    }
+                } else if (MODE == SCAN_GROUPMAX) {
+                    // approximate final scores (fast reciprocal: a few ulps; the
+                    // threshold's 2^-16 slack absorbs it), larger = better; L2 is
+                    // ranked in the order-reversed space dot - xv / 2
+#pragma unroll
+                    for (int j4 = 0; j4 < 8; ++j4) {
+                        const float4 x4 = xs4[j4];
+                        const float xx[4] = {x4.x, x4.y, x4.z, x4.w};
+#pragma unroll
+                        for (int u = 0; u < 4; ++u) {
+                            const int j = 4 * j4 + u;
+                            float sc;
+                            if (a.metric == RDB_METRIC_L2) {
+                                sc = fmaf(-0.5f, xx[u], v[j]);
+                            } else if (a.metric == RDB_METRIC_COSINE) {
+                                const float den = a.cos_small ? qv * xx[u] : fmaf(qv, xx[u], 1e-8f);
+                                sc = __fdividef(v[j], den);
+                            } else {
+                                sc = v[j];
+                            }
+                            v[j] = ((valid >> j) & 1u) ? sc : -INFINITY;
+                        }
+                    }
+                    const int g = a.group;
+                    if (qvalid) {
+                        float* gout = a.group_out + q * a.ngroups + col0 / g;
+                        if (g == 16) {
+#pragma unroll
+                            for (int h = 0; h < 2; ++h) {
+                                float m0 = v[16 * h];
+#pragma unroll
+                                for (int j = 1; j < 16; ++j) m0 = fmaxf(m0, v[16 * h + j]);
+                                if ((valid >> (16 * h)) & 1u)
+                                    gout[h] = a.metric == RDB_METRIC_L2 ? fmaxf(qv - 2.f * m0, 0.f) : m0;
+                            }
+                        } else {
+                            float gb = -INFINITY;
+#pragma unroll
+                            for (int j = 0; j < 32; ++j) {
+                                gb = fmaxf(gb, v[j]);
+                                if (((j + 1) & (g - 1)) == 0) {
+                                    if ((valid >> j) & 1u)
+                                        gout[j / g] = a.metric == RDB_METRIC_L2 ? fmaxf(qv - 2.f * gb, 0.f) : gb;
+                                    gb = -INFINITY;
+                                }
+                            }
                         }
                     }
                 } else {  // SCAN_DENSE
-                    if (qvalid)
-                        for (int j = 0; j < nvalid; ++j)
-                            a.dense_out[q * a.ld_out + col0 + j] =
-                                final_score(a.metric, a.cos_small, v[j], qv, xv[j]);
+                    if (qvalid) {
+                        float* orow = a.dense_out + q * a.ld_out + col0;
+#pragma unroll
+                        for (int j4 = 0; j4 < 8; ++j4) {
+                            const float4 x4 = xs4[j4];
+                            const float xx[4] = {x4.x, x4.y, x4.z, x4.w};
+#pragma unroll
+                            for (int u = 0; u < 4; ++u) {
+                                const int j = 4 * j4 + u;
+                                if ((valid >> j) & 1u) orow[j] = final_score(a.metric, a.cos_small, v[j], qv, xx[u]);
+                            }
+                        }
+                    }
                 }
             }
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(&tempty[acc]);
+            if (lane == 0) mbar_arrive_cluster(tempty_lead[acc]);
+            // publish the next tile's row values (its buffer was last read in
+            // tile t - 1, which every epilogue thread has finished)
+            if (t + 1 < ntiles) reinterpret_cast<float2*>(xv_s + ((t + 1) & 1) * BN)[etid] = xv_next;
+            epi_bar_sync();
         }
         if (qvalid) {
             if (MODE == SCAN_FILTER)
@@ -421,10 +682,27 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     }
     tc_fence_before();
     __syncthreads();
+    if (PAIR) cluster_sync_all();  // neither CTA leaves while its partner may still signal it
     if (warp == 1) {
         tc_fence_after();
-        tmem_dealloc(tmem_base, TMEM_COLS);
+        tmem_dealloc_t<PAIR>(tmem_base, TMEM_COLS);
     }
+}
+
+template <int MODE>
+__global__ void __launch_bounds__(NUM_THREADS, 1)
+    tc_scan_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_constant__ CUtensorMap tmap_x,
+                   const ScanArgs a, const uint32_t idesc, unsigned* status) {
+    extern __shared__ uint8_t smem_raw[];
+    tc_scan_body<MODE, false>(smem_raw, tmap_q, tmap_x, a, idesc, status);
+}
+
+template <int MODE>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
+    tc_scan_pair_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_constant__ CUtensorMap tmap_x,
+                        const ScanArgs a, const uint32_t idesc, unsigned* status) {
+    extern __shared__ uint8_t smem_raw[];
+    tc_scan_body<MODE, true>(smem_raw, tmap_q, tmap_x, a, idesc, status);
 }
 
 // --------------------------------------------------------------- host side --
@@ -458,23 +736,48 @@ int make_map(CUtensorMap* m, int dtype, const void* base, int64_t rows, int d, i
     return RDB_OK;
 }
 
-template <int MODE>
+template <int MODE, bool PAIR>
 int launch_mode(const CUtensorMap& mq, const CUtensorMap& mx, const ScanArgs& a, uint32_t idesc,
                 dim3 grid, cudaStream_t s) {
     static bool attr[64] = {false};
     int dev = 0;
     cudaGetDevice(&dev);
+    constexpr int smem = TcCfg<PAIR>::SMEM;
     if (dev < 64 && !attr[dev]) {
-        RDB_CUDA_TRY(cudaFuncSetAttribute(tc_scan_kernel<MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                          SMEM_BYTES));
+        if (PAIR)
+            RDB_CUDA_TRY(cudaFuncSetAttribute(tc_scan_pair_kernel<MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                              smem));
+        else
+            RDB_CUDA_TRY(cudaFuncSetAttribute(tc_scan_kernel<MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
         attr[dev] = true;
     }
-    tc_scan_kernel<MODE><<<grid, NUM_THREADS, SMEM_BYTES, s>>>(mq, mx, a, idesc, device_status_word());
+    if (PAIR)
+        tc_scan_pair_kernel<MODE><<<grid, NUM_THREADS, smem, s>>>(mq, mx, a, idesc, device_status_word());
+    else
+        tc_scan_kernel<MODE><<<grid, NUM_THREADS, smem, s>>>(mq, mx, a, idesc, device_status_word());
     RDB_LAUNCH_CHECK();
     return RDB_OK;
 }
 
+template <bool PAIR>
+int launch_shape(const ScanArgs& a, int mode, cudaStream_t s) {
+    const int qunit = PAIR ? 2 * BM : BM;
+    const int64_t gy = (a.nq + qunit - 1) / qunit;
+    RDB_CHECK_ARG(gy <= 65535, "too many queries for one launch");
+    CUtensorMap mq, mx;
+    RDB_TRY(make_map(&mq, a.dtype, a.q, a.nq, a.d, a.ldq * 2, BM));
+    RDB_TRY(make_map(&mx, a.dtype, a.x, a.n, a.d, a.ldx * 2 * a.row_step, TcCfg<PAIR>::B_ROWS));
+    const uint32_t idesc = make_idesc(a.dtype == RDB_BF16, TcCfg<PAIR>::UMMA_M);
+    dim3 grid(PAIR ? 2 * a.nsplit : a.nsplit, static_cast<unsigned>(gy));
+    if (mode == SCAN_FILTER) return launch_mode<SCAN_FILTER, PAIR>(mq, mx, a, idesc, grid, s);
+    if (mode == SCAN_ARGMIN) return launch_mode<SCAN_ARGMIN, PAIR>(mq, mx, a, idesc, grid, s);
+    if (mode == SCAN_GROUPMAX) return launch_mode<SCAN_GROUPMAX, PAIR>(mq, mx, a, idesc, grid, s);
+    return launch_mode<SCAN_DENSE, PAIR>(mq, mx, a, idesc, grid, s);
+}
+
 }  // namespace
+
+bool tc_use_pair(int64_t nq) { return nq > kTcQueries; }
 
 int launch_scan_tc(const ScanArgs& a, int mode, cudaStream_t s) {
     if (a.nq <= 0 || a.n <= 0) return RDB_OK;
@@ -485,16 +788,10 @@ int launch_scan_tc(const ScanArgs& a, int mode, cudaStream_t s) {
                   "row strides must be multiples of 16 bytes");
     RDB_CHECK_ARG((reinterpret_cast<uintptr_t>(a.q) & 15) == 0 && (reinterpret_cast<uintptr_t>(a.x) & 15) == 0,
                   "base pointers must be 16-byte aligned");
-    int64_t gy = (a.nq + BM - 1) / BM;
-    RDB_CHECK_ARG(gy <= 65535, "too many queries for one launch");
-    CUtensorMap mq, mx;
-    RDB_TRY(make_map(&mq, a.dtype, a.q, a.nq, a.d, a.ldq * 2, BM));
-    RDB_TRY(make_map(&mx, a.dtype, a.x, a.n, a.d, a.ldx * 2 * a.row_step, BN));
-    const uint32_t idesc = make_idesc(a.dtype == RDB_BF16);
-    dim3 grid(a.nsplit, static_cast<unsigned>(gy));
-    if (mode == SCAN_FILTER) return launch_mode<SCAN_FILTER>(mq, mx, a, idesc, grid, s);
-    if (mode == SCAN_ARGMIN) return launch_mode<SCAN_ARGMIN>(mq, mx, a, idesc, grid, s);
-    return launch_mode<SCAN_DENSE>(mq, mx, a, idesc, grid, s);
+    if (mode == SCAN_GROUPMAX)
+        RDB_CHECK_ARG(a.group >= 1 && a.group <= 32 && (a.group & (a.group - 1)) == 0 && a.n % a.group == 0,
+                      "group must be a power of two <= 32 dividing n");
+    return tc_use_pair(a.nq) ? launch_shape<true>(a, mode, s) : launch_shape<false>(a, mode, s);
 }
 
 }  // namespace rdb

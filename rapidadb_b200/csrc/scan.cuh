@@ -9,9 +9,10 @@
 namespace rdb {
 
 enum ScanMode : int {
-    SCAN_FILTER = 0,  // append (dot, row) pairs whose score reaches thr[q]
+    SCAN_FILTER = 0,  // append (final score, row) pairs whose score reaches thr[q]
     SCAN_DENSE = 1,   // write final scores to dense_out[q, row]
     SCAN_ARGMIN = 2,  // best row per (split, query) by squared L2
+    SCAN_GROUPMAX = 3,  // best score of every `group` consecutive logical rows
 };
 
 struct ScanArgs {
@@ -47,13 +48,22 @@ struct ScanArgs {
 
     // SCAN_ARGMIN: [nsplit][nq] best (score key, row) pairs
     unsigned long long* best;
+
+    // SCAN_GROUPMAX: group_out[q][row / group] = best final score (approximate
+    // to a few ulps) over logical rows [g * group, (g + 1) * group); group is a
+    // power of two <= 32 and n a multiple of it.
+    float* group_out;
+    int group;
+    int64_t ngroups;
 };
 
 // CUDA-core scan (any dtype).  Grid = (nsplit, ceil(nq / 32)).
 int launch_scan_simt(const ScanArgs& a, int mode, cudaStream_t stream);
 
-// tcgen05 scan for fp16 / bf16 (sm_100a).  Grid = (nsplit, ceil(nq / 128)).
+// tcgen05 scan for fp16 / bf16 (sm_100a).  Grid = (nsplit, ceil(nq / 128)), or
+// with more than 128 queries CTA pairs: (2 nsplit, ceil(nq / 256)).
 int launch_scan_tc(const ScanArgs& a, int mode, cudaStream_t stream);
+bool tc_use_pair(int64_t nq);
 
 // Row tiles of the two kernels (rows_per_split must be a multiple).
 constexpr int kSimtRows = 128;

@@ -18,7 +18,7 @@ namespace {
 
 constexpr int NT = 256;
 constexpr int NWARP = NT / 32;
-constexpr int kCacheKeys = 4096;  // keys cached in shared memory when T fits
+constexpr int kCacheKeys = 8192;  // keys cached in shared memory when T fits
 constexpr int kMaxSeg = 1024;
 
 struct SelShared {
@@ -44,32 +44,33 @@ __device__ __forceinline__ bool hi_eq(unsigned long long a, unsigned long long b
     return top >= 64 ? true : ((a >> top) == (b >> top));
 }
 
-// Key of element e (0 <= e < total) of query q.
-__device__ __forceinline__ unsigned long long elem_key(const SelectArgs& a, const SelShared& S,
-                                                       int64_t q, int e, float qv) {
-    // segment by binary search over the prefix offsets
-    int nseg = a.input == SEL_DENSE ? 1 : (a.input == SEL_MERGE ? a.G : a.nsplit);
-    int lo = 0, hi = nseg - 1;
-    while (lo < hi) {
-        int mid = (lo + hi + 1) >> 1;
-        if (S.seg_off[mid] <= e) lo = mid; else hi = mid - 1;
-    }
-    int t = e - S.seg_off[lo];
-    bool largest = a.largest != 0;
+// Key of element t of segment seg of query q.
+__device__ __forceinline__ unsigned long long seg_key(const SelectArgs& a, int64_t q, int seg, int t,
+                                                      float qv) {
+    const bool largest = a.largest != 0;
     if (a.input == SEL_CANDIDATES) {
-        uint2 c = a.cand[((int64_t)lo * a.nq + q) * a.cap + t];
-        float dot = __uint_as_float(c.x);
-        float xv = a.xv ? a.xv[(int64_t)c.y * a.row_step] : 0.f;
-        float s = final_score(a.metric, a.cos_small, dot, qv, xv);
-        return ((unsigned long long)score_key(s, largest) << 32) | c.y;
+        // candidates carry their final score (computed by the scan epilogue)
+        uint2 c = a.cand[((int64_t)seg * a.nq + q) * a.cap + t];
+        return ((unsigned long long)score_key(__uint_as_float(c.x), largest) << 32) | c.y;
     } else if (a.input == SEL_DENSE) {
         float s = a.dense[q * a.dense_n + t];
         return ((unsigned long long)score_key(s, largest) << 32) | (uint32_t)t;
     } else {
-        float s = a.merge_v[((int64_t)lo * a.nq + q) * a.kin + t];
-        return ((unsigned long long)score_key(s, largest) << 32) | (uint32_t)(lo * a.kin + t);
+        float s = a.merge_v[((int64_t)seg * a.nq + q) * a.kin + t];
+        return ((unsigned long long)score_key(s, largest) << 32) | (uint32_t)(seg * a.kin + t);
     }
 }
+
+// Walks elements e = threadIdx.x, +NT, ... of query q; the segment of e is
+// tracked with a monotone cursor (each thread's e only grows).
+struct ElemCursor {
+    int seg = 0;
+    __device__ __forceinline__ unsigned long long key(const SelectArgs& a, const SelShared& S,
+                                                      int64_t q, int e, float qv) {
+        while (e >= S.seg_off[seg + 1]) ++seg;
+        return seg_key(a, q, seg, e - S.seg_off[seg], qv);
+    }
+};
 
 __device__ void bitonic_sort(unsigned long long* keys, int n /* power of two */) {
     for (int size = 2; size <= n; size <<= 1) {
@@ -148,8 +149,9 @@ __global__ void __launch_bounds__(NT) select_kernel(SelectArgs a) {
 
         // ---- pass 0: keys (cached) and min / max ---------------------------
         unsigned long long kmin = ~0ull, kmax = 0ull;
+        ElemCursor cur0;
         for (int e = threadIdx.x; e < T; e += NT) {
-            unsigned long long key = elem_key(a, S, q, e, qv);
+            unsigned long long key = cur0.key(a, S, q, e, qv);
             if (cached) cache[e] = key;
             kmin = min(kmin, key);
             kmax = max(kmax, key);
@@ -195,10 +197,11 @@ __global__ void __launch_bounds__(NT) select_kernel(SelectArgs a) {
             for (int i = threadIdx.x; i < 256; i += NT) S.hist[i] = 0;
             __syncthreads();
             const int Tr = (T + 31) & ~31;
+            ElemCursor cur;
             for (int e = threadIdx.x; e < Tr; e += NT) {
                 int bin = -1;
                 if (e < T) {
-                    unsigned long long key = cached ? cache[e] : elem_key(a, S, q, e, qv);
+                    unsigned long long key = cached ? cache[e] : cur.key(a, S, q, e, qv);
                     if (hi_eq(key, prefix, top)) bin = (int)((key >> shift) & width_mask);
                 }
                 unsigned peers = __match_any_sync(0xffffffffu, bin);
@@ -250,8 +253,9 @@ __global__ void __launch_bounds__(NT) select_kernel(SelectArgs a) {
         {
             const int top = S.top;
             const unsigned long long pref = top >= 64 ? 0ull : (S.prefix >> top);
+            ElemCursor cur;
             for (int e = threadIdx.x; e < T; e += NT) {
-                unsigned long long key = cached ? cache[e] : elem_key(a, S, q, e, qv);
+                unsigned long long key = cached ? cache[e] : cur.key(a, S, q, e, qv);
                 bool take = top >= 64 ? true : ((key >> top) <= pref);
                 if (take) {
                     int slot = atomicAdd(&S.nsel, 1);

@@ -6,7 +6,7 @@
 namespace rdb {
 
 enum SelectInput : int {
-    SEL_CANDIDATES = 0,  // segmented (raw dot bits, row) pairs from a scan kernel
+    SEL_CANDIDATES = 0,  // segmented (final score bits, row) pairs from a scan kernel
     SEL_DENSE = 1,       // one row of a dense [B, N] fp32 score matrix
     SEL_MERGE = 2,       // G sorted lists of (score, int64 id)
 };

@@ -170,8 +170,8 @@ __global__ void __launch_bounds__(NT) simt_scan_kernel(ScanArgs a) {
                     if (v >= fmaf(sA[qi], xv, sB[qi])) {
                         int slot = atomicAdd(&scnt[qi], 1);
                         if (slot < a.cap)
-                            a.cand[((int64_t)split * a.nq + q) * a.cap + slot] =
-                                make_uint2(__float_as_uint(v), (uint32_t)r);
+                            a.cand[((int64_t)split * a.nq + q) * a.cap + slot] = make_uint2(
+                                __float_as_uint(final_score(a.metric, a.cos_small, v, sQv[qi], xv)), (uint32_t)r);
                     }
                 } else {  // SCAN_ARGMIN (squared L2)
                     float xv = a.xv[r * a.row_step];
