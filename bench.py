@@ -286,10 +286,11 @@ def run_ours(args, wl):
     tv, ti = torch.topk(s, k, dim=1)
     ti = ti + lo
     if world > 1:
-        gv = torch.empty((world, nrec, k), device=dev, dtype=tv.dtype)
-        gi = torch.empty((world, nrec, k), device=dev, dtype=ti.dtype)
+        gv = torch.empty((world * nrec, k), device=dev, dtype=tv.dtype)
+        gi = torch.empty((world * nrec, k), device=dev, dtype=ti.dtype)
         dist.all_gather_into_tensor(gv, tv.contiguous())
         dist.all_gather_into_tensor(gi, ti.contiguous())
+        gv, gi = gv.view(world, nrec, k), gi.view(world, nrec, k)
         order = torch.topk(gv.permute(1, 0, 2).reshape(nrec, -1), k, dim=1).indices
         ti = torch.gather(gi.permute(1, 0, 2).reshape(nrec, -1), 1, order)
     del s, xs

@@ -111,6 +111,82 @@ int rdb_flat_search(int metric, int dtype, const void* q, int64_t nq, int64_t ld
 int rdb_topk_merge(int largest, const float* in_v, const int64_t* in_i, int G, int64_t nq,
                    int kin, int k, float* out_v, int64_t* out_i, void* stream);
 
+/* ---- k-means --------------------------------------------------------- */
+
+/* Lloyd assign step: label[i] = argmin_c |x_i - c|^2 (ties to the lower
+ * centroid) and its squared distance.  Replaces assign_clusters_kernel
+ * (csrc/kernels/kmeans.cu:11-45; the reference writes sqrt of the minimum and
+ * has no launcher).  fp16 / bf16 points and centroids run as a tcgen05 GEMM
+ * with the argmin fused into the epilogue (|c|^2 - 2 x.c), fp32 on CUDA cores.
+ * x [n, d] (stride ldx), centroids [K, d] (stride ldc, same dtype),
+ * c_sqnorms [K] = |c|^2 of the centroids as stored. */
+size_t rdb_kmeans_assign_workspace(int dtype, int64_t n, int K, int d);
+int rdb_kmeans_assign(int dtype, const void* x, int64_t n, int64_t ldx, int d, const void* centroids, int K,
+                      int64_t ldc, const float* c_sqnorms, int32_t* labels, float* sqdist, void* ws,
+                      size_t ws_bytes, void* stream);
+
+/* Lloyd update step, atomic-free: per-centroid sums [K, d] (fp32) and counts
+ * [K] of the points with each label, summed in ascending point order.
+ * Replaces update_centroids_kernel (csrc/kernels/kmeans.cu:48-94, float
+ * atomics).  Multi-GPU callers all-reduce sums and counts, then finalize. */
+size_t rdb_kmeans_update_workspace(int64_t n, int K);
+int rdb_kmeans_update(int dtype, const void* x, int64_t n, int64_t ldx, int d, const int32_t* labels, int K,
+                      float* sums, int64_t* counts, void* ws, size_t ws_bytes, void* stream);
+
+/* centroid = sums / count; a centroid with count 0 keeps its value (the
+ * reference leaves it unwritten, csrc/kernels/kmeans.cu:88-93). */
+int rdb_kmeans_finalize(const float* sums, const int64_t* counts, int K, int d, float* centroids, void* stream);
+
+/* Exact list assignment for IVF indices: argmin over centroids of the
+ * sequential sum of (x - c)^2 with one fused multiply-add per element, the
+ * reference assign arithmetic (csrc/kernels/kmeans.cu:31-35) bit for bit;
+ * fp32 only. */
+size_t rdb_assign_exact_workspace(int64_t n, int K, int d);
+int rdb_assign_exact(const float* x, int64_t n, int64_t ldx, int d, const float* centroids, int K, int64_t ldc,
+                     int32_t* labels, float* sqdist, void* ws, size_t ws_bytes, void* stream);
+
+/* Stable counting sort by label (no reference counterpart; the building block
+ * of the atomic-free k-means update and of the IVF list layouts):
+ * perm[seg_start[c] .. seg_start[c + 1]) = the ids i with labels[i] == c in
+ * ascending order, counts[c] the segment sizes (counts may be NULL).
+ * Labels must lie in [0, K), K <= 16384. */
+size_t rdb_label_sort_workspace(int64_t n, int K);
+int rdb_label_sort(const int32_t* labels, int64_t n, int K, int64_t* seg_start, int64_t* perm, int64_t* counts,
+                   void* ws, size_t ws_bytes, void* stream);
+
+/* ---- IVF-Flat / IVF-PQ (no reference implementation: the reference only
+ * names them, python/rapidadb/config.py:14-18, :50-56; index.py:64-69) ---- */
+
+/* List-major scan of an IVF index whose rows are stored list by list
+ * (list l = rows list_off[l] .. list_off[l + 1] - 1).  probe [nq, nprobe]
+ * holds each query's lists (from a coarse rdb_flat_search over the
+ * centroids).  For every (query, probe slot) the best k rows of that list,
+ * scored with the flat formula of `metric` (L2 summed directly), go to
+ * out_v / out_i [nprobe, nq, k] (ids[row], or -1 padding when a list has
+ * fewer than k rows); rdb_topk_merge then keeps the best k per query.
+ * q and rows share `dtype`; xv [n] per-row values (cosine only); k <= 32. */
+size_t rdb_ivf_scan_workspace(int64_t nq, int nprobe, int nlist);
+int rdb_ivf_flat_scan(int metric, int dtype, const void* q, int64_t nq, int64_t ldq, int d, const int64_t* probe,
+                      int nprobe, const void* rows, int64_t ldx, const float* xv, const int64_t* list_off, int nlist,
+                      const int64_t* ids, int k, float* out_v, int64_t* out_i, void* ws, size_t ws_bytes,
+                      void* stream);
+
+/* Residual product-quantisation codes: for row i in list labels[i], residual
+ * r = x_i - centroid; code m = argmin over the ksub codewords of subspace m
+ * (codebooks [M, ksub, d / M]) of the sequential fused-FMA squared distance,
+ * ties to the lower codeword.  codes [n, M] uint8.  fp32 inputs. */
+int rdb_pq_encode(const float* x, int64_t n, int64_t ldx, int d, const int32_t* labels, const float* centroids,
+                  const float* codebooks, int M, int ksub, uint8_t* codes, void* stream);
+
+/* List-major IVF-PQ asymmetric-distance scan (squared L2): per (query,
+ * probed list) a table LUT[m][j] = |(q - centroid)_m - codeword_mj|^2 is built
+ * in shared memory and each stored code scores sum_m LUT[m][code_m]; output
+ * layout as rdb_ivf_flat_scan.  Codes stored list by list; k <= 32. */
+int rdb_ivfpq_scan(const float* q, int64_t nq, int64_t ldq, int d, const int64_t* probe, int nprobe,
+                   const float* centroids, int nlist, const float* codebooks, int M, int ksub, const uint8_t* codes,
+                   const int64_t* list_off, const int64_t* ids, int k, float* out_v, int64_t* out_i, void* ws,
+                   size_t ws_bytes, void* stream);
+
 /* Profiling hook (no reference counterpart; the reference times whole calls,
  * benchmarks/src/bench_compare.py:56-59): when enabled, CUDA events are
  * recorded on the launching stream around every main-pass scan launch of

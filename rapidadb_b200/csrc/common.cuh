@@ -20,12 +20,16 @@ int set_error(int code, const char* fmt, ...);
         if (!(cond)) return ::rdb::set_error(RDB_ERR_INVALID, __VA_ARGS__); \
     } while (0)
 
+// On failure the runtime's (non-sticky) last-error state is cleared, so a
+// later launch check does not report this failure a second time.
 #define RDB_CUDA_TRY(expr)                                                        \
     do {                                                                          \
         cudaError_t e_ = (expr);                                                  \
-        if (e_ != cudaSuccess)                                                    \
+        if (e_ != cudaSuccess) {                                                  \
+            (void)cudaGetLastError();                                             \
             return ::rdb::set_error(RDB_ERR_CUDA, "%s: %s (%s:%d)", #expr,        \
                                     cudaGetErrorString(e_), __FILE__, __LINE__);  \
+        }                                                                         \
     } while (0)
 
 #define RDB_LAUNCH_CHECK()                                                        \

@@ -4,6 +4,7 @@
 #include <torch/extension.h>
 
 #include "host.h"
+#include "ivf.h"
 
 namespace py = pybind11;
 using namespace rdbh;
@@ -82,6 +83,75 @@ PYBIND11_MODULE(_C, m) {
         "Fused top-k search over caller-owned padded rows", py::arg("metric"), py::arg("rows"), py::arg("dim"),
         py::arg("row_values"), py::arg("queries"), py::arg("k"), py::arg("ids") = py::none(),
         py::arg("id_offset") = 0);
+    // ---- k-means primitives (rapidadb_b200.kmeans drives the Lloyd loop)
+    m.def("kmeans_assign", &kmeans_assign, "labels, squared distances", py::arg("points"), py::arg("centroids"),
+          py::arg("exact") = false);
+    m.def("kmeans_update", &kmeans_update, "per-centroid sums and counts", py::arg("points"), py::arg("labels"),
+          py::arg("k"));
+    m.def("kmeans_finalize", &kmeans_finalize, "sums / counts (empty clusters keep their centroid)",
+          py::arg("sums"), py::arg("counts"), py::arg("centroids"));
+    m.def("label_sort", &label_sort, "stable counting sort by label", py::arg("labels"), py::arg("k"));
+    m.def("pq_encode", &pq_encode, "residual PQ codes", py::arg("points"), py::arg("labels"),
+          py::arg("centroids"), py::arg("codebooks"));
+
+    // ---- IVF indices
+    py::class_<IVFFlatIndex>(m, "IVFFlatIndex")
+        .def(py::init<int, Metric, int, int, Precision>(), py::arg("dim"), py::arg("metric") = Metric::L2,
+             py::arg("nlist") = 4096, py::arg("nprobe") = 64, py::arg("precision") = Precision::FP32)
+        .def("set_quantizer", &IVFFlatIndex::set_quantizer, py::arg("centroids"))
+        .def(
+            "add", [](IVFFlatIndex& s, const at::Tensor& v, const py::object& ids) { s.add(v, opt_tensor(ids)); },
+            py::arg("vectors"), py::arg("ids") = py::none())
+        .def("search", &IVFFlatIndex::search, py::arg("queries"), py::arg("k"))
+        .def("reset", &IVFFlatIndex::reset)
+        .def("size", &IVFFlatIndex::size)
+        .def("dim", &IVFFlatIndex::dim)
+        .def("nlist", &IVFFlatIndex::nlist)
+        .def("nprobe", &IVFFlatIndex::nprobe)
+        .def("set_nprobe", &IVFFlatIndex::set_nprobe)
+        .def("is_trained", &IVFFlatIndex::is_trained)
+        .def("centroids", &IVFFlatIndex::centroids)
+        .def("list_offsets", &IVFFlatIndex::list_offsets)
+        .def("list_sizes", &IVFFlatIndex::list_sizes)
+        .def("stored_ids", &IVFFlatIndex::stored_ids)
+        .def("stored_labels", &IVFFlatIndex::stored_labels)
+        .def("stored_vectors", &IVFFlatIndex::stored_vectors)
+        .def("__len__", &IVFFlatIndex::size)
+        .def("__repr__", [](const IVFFlatIndex& s) {
+            return "IVFFlatIndex(dim=" + std::to_string(s.dim()) + ", nlist=" + std::to_string(s.nlist()) +
+                   ", size=" + std::to_string(s.size()) + ")";
+        });
+
+    py::class_<IVFPQIndex>(m, "IVFPQIndex")
+        .def(py::init<int, Metric, int, int, int, int>(), py::arg("dim"), py::arg("metric") = Metric::L2,
+             py::arg("nlist") = 4096, py::arg("nprobe") = 64, py::arg("m") = 16, py::arg("ksub") = 256)
+        .def("set_quantizer", &IVFPQIndex::set_quantizer, py::arg("centroids"), py::arg("codebooks"))
+        .def(
+            "add", [](IVFPQIndex& s, const at::Tensor& v, const py::object& ids) { s.add(v, opt_tensor(ids)); },
+            py::arg("vectors"), py::arg("ids") = py::none())
+        .def("search", &IVFPQIndex::search, py::arg("queries"), py::arg("k"))
+        .def("reset", &IVFPQIndex::reset)
+        .def("size", &IVFPQIndex::size)
+        .def("dim", &IVFPQIndex::dim)
+        .def("nlist", &IVFPQIndex::nlist)
+        .def("nprobe", &IVFPQIndex::nprobe)
+        .def("set_nprobe", &IVFPQIndex::set_nprobe)
+        .def("pq_m", &IVFPQIndex::pq_m)
+        .def("pq_k", &IVFPQIndex::pq_k)
+        .def("is_trained", &IVFPQIndex::is_trained)
+        .def("centroids", &IVFPQIndex::centroids)
+        .def("codebooks", &IVFPQIndex::codebooks)
+        .def("list_offsets", &IVFPQIndex::list_offsets)
+        .def("list_sizes", &IVFPQIndex::list_sizes)
+        .def("stored_ids", &IVFPQIndex::stored_ids)
+        .def("stored_labels", &IVFPQIndex::stored_labels)
+        .def("stored_codes", &IVFPQIndex::stored_codes)
+        .def("__len__", &IVFPQIndex::size)
+        .def("__repr__", [](const IVFPQIndex& s) {
+            return "IVFPQIndex(dim=" + std::to_string(s.dim()) + ", nlist=" + std::to_string(s.nlist()) +
+                   ", m=" + std::to_string(s.pq_m()) + ", size=" + std::to_string(s.size()) + ")";
+        });
+
     m.def("padded_ld", [](int dim, at::ScalarType t) { return padded_ld(dim, t); });
     m.def("prepare_rows", &prepare_rows, py::arg("src"), py::arg("dtype"), py::arg("ld"));
     m.def("row_values", &row_values, py::arg("metric"), py::arg("rows"), py::arg("dim"));

@@ -1,0 +1,326 @@
+// Host-side k-means primitives and the IVF-Flat / IVF-PQ indices.
+//
+// The reference declares IVF / IVF-PQ only as configuration
+// (python/rapidadb/config.py:14-18, :50-56; index.py:64-69 raises) and its
+// k-means has kernels without launchers (csrc/kernels/kmeans.cu,
+// csrc/include/rapidadb/clustering/kmeans.h:18-24).  Semantics here follow
+// the CPU oracle: coarse L2 probe of the nprobe nearest lists, exact scoring
+// of the probed rows (IVF-Flat) or residual-PQ asymmetric distances (IVF-PQ),
+// rows assigned to lists with the reference's sequential-FMA L2 arithmetic.
+//
+// Layout: rows (or codes) are kept list by list -- list l owns stored rows
+// list_off[l] .. list_off[l + 1] - 1 -- rebuilt on add() with the stable
+// label sort (rows already stored keep their order, new rows follow).
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+
+#include <algorithm>
+
+#include "host.h"
+#include "ivf.h"
+
+namespace rdbh {
+
+static at::Tensor ws_bytes(const at::Tensor& like, size_t n) {
+    return at::empty({static_cast<int64_t>(std::max<size_t>(n, 256))}, like.options().dtype(at::kByte));
+}
+
+static at::Tensor contig_f32(const at::Tensor& t) { return t.to(at::kFloat).contiguous(); }
+
+// ------------------------------------------------------------------ k-means
+
+std::tuple<at::Tensor, at::Tensor> kmeans_assign(const at::Tensor& x, const at::Tensor& centroids, bool exact) {
+    TORCH_CHECK(x.is_cuda() && centroids.is_cuda(), "points and centroids must be CUDA tensors");
+    TORCH_CHECK(x.dim() == 2 && centroids.dim() == 2 && x.size(1) == centroids.size(1), "dimension mismatch");
+    c10::cuda::CUDAGuard guard(x.device());
+    const int d = static_cast<int>(x.size(1));
+    const int64_t n = x.size(0);
+    const int K = static_cast<int>(centroids.size(0));
+    at::Tensor labels = at::empty({n}, x.options().dtype(at::kInt));
+    at::Tensor sqd = at::empty({n}, x.options().dtype(at::kFloat));
+    if (n == 0) return {labels, sqd};
+    if (exact) {
+        at::Tensor xf = contig_f32(x), cf = contig_f32(centroids);
+        size_t wsb = rdb_assign_exact_workspace(n, K, d);
+        at::Tensor ws = ws_bytes(x, wsb);
+        check_status(rdb_assign_exact(xf.data_ptr<float>(), n, d, d, cf.data_ptr<float>(), K, d,
+                                      labels.data_ptr<int32_t>(), sqd.data_ptr<float>(), ws.data_ptr(), ws.numel(),
+                                      stream_ptr()),
+                     "exact assign");
+        return {labels, sqd};
+    }
+    const at::ScalarType dt = is_half(x.scalar_type()) ? x.scalar_type() : at::kFloat;
+    const int64_t ld = padded_ld(d, dt);
+    at::Tensor xp = prepare_rows(x, dt, ld);
+    at::Tensor cp = prepare_rows(centroids, dt, ld);
+    at::Tensor csq = at::empty({K}, x.options().dtype(at::kFloat));
+    check_status(rdb_row_sqnorms(dtype_code(dt), cp.data_ptr(), K, static_cast<int>(ld), csq.data_ptr<float>(),
+                                 stream_ptr()),
+                 "centroid norms");
+    size_t wsb = rdb_kmeans_assign_workspace(dtype_code(dt), n, K, d);
+    at::Tensor ws = ws_bytes(x, wsb);
+    check_status(rdb_kmeans_assign(dtype_code(dt), xp.data_ptr(), n, ld, d, cp.data_ptr(), K, ld,
+                                   csq.data_ptr<float>(), labels.data_ptr<int32_t>(), sqd.data_ptr<float>(),
+                                   ws.data_ptr(), ws.numel(), stream_ptr()),
+                 "kmeans assign");
+    return {labels, sqd};
+}
+
+std::tuple<at::Tensor, at::Tensor> kmeans_update(const at::Tensor& x, const at::Tensor& labels, int64_t K) {
+    TORCH_CHECK(x.is_cuda() && labels.is_cuda(), "points and labels must be CUDA tensors");
+    TORCH_CHECK(x.dim() == 2 && labels.dim() == 1 && labels.size(0) == x.size(0), "labels must be [n]");
+    c10::cuda::CUDAGuard guard(x.device());
+    const int d = static_cast<int>(x.size(1));
+    const int64_t n = x.size(0);
+    const at::ScalarType dt = is_half(x.scalar_type()) ? x.scalar_type() : at::kFloat;
+    at::Tensor xc = x.to(dt).contiguous();
+    at::Tensor lab = labels.to(at::kInt).contiguous();
+    at::Tensor sums = at::empty({K, d}, x.options().dtype(at::kFloat));
+    at::Tensor counts = at::empty({K}, x.options().dtype(at::kLong));
+    at::Tensor ws = ws_bytes(x, rdb_kmeans_update_workspace(n, static_cast<int>(K)));
+    check_status(rdb_kmeans_update(dtype_code(dt), xc.data_ptr(), n, d, d, lab.data_ptr<int32_t>(),
+                                   static_cast<int>(K), sums.data_ptr<float>(), counts.data_ptr<int64_t>(),
+                                   ws.data_ptr(), ws.numel(), stream_ptr()),
+                 "kmeans update");
+    return {sums, counts};
+}
+
+at::Tensor kmeans_finalize(const at::Tensor& sums, const at::Tensor& counts, const at::Tensor& centroids) {
+    c10::cuda::CUDAGuard guard(sums.device());
+    at::Tensor s = contig_f32(sums);
+    at::Tensor c = counts.to(at::kLong).contiguous();
+    at::Tensor out = contig_f32(centroids).clone();
+    check_status(rdb_kmeans_finalize(s.data_ptr<float>(), c.data_ptr<int64_t>(), static_cast<int>(s.size(0)),
+                                     static_cast<int>(s.size(1)), out.data_ptr<float>(), stream_ptr()),
+                 "kmeans finalize");
+    return out;
+}
+
+std::tuple<at::Tensor, at::Tensor, at::Tensor> label_sort(const at::Tensor& labels, int64_t K) {
+    TORCH_CHECK(labels.is_cuda() && labels.dim() == 1, "labels must be a 1-D CUDA tensor");
+    c10::cuda::CUDAGuard guard(labels.device());
+    at::Tensor lab = labels.to(at::kInt).contiguous();
+    const int64_t n = lab.size(0);
+    at::Tensor seg = at::empty({K + 1}, lab.options().dtype(at::kLong));
+    at::Tensor perm = at::empty({n}, lab.options().dtype(at::kLong));
+    at::Tensor counts = at::empty({K}, lab.options().dtype(at::kLong));
+    at::Tensor ws = ws_bytes(lab, rdb_label_sort_workspace(n, static_cast<int>(K)));
+    check_status(rdb_label_sort(lab.data_ptr<int32_t>(), n, static_cast<int>(K), seg.data_ptr<int64_t>(),
+                                perm.data_ptr<int64_t>(), counts.data_ptr<int64_t>(), ws.data_ptr(), ws.numel(),
+                                stream_ptr()),
+                 "label sort");
+    return {seg, perm, counts};
+}
+
+at::Tensor pq_encode(const at::Tensor& x, const at::Tensor& labels, const at::Tensor& centroids,
+                     const at::Tensor& codebooks) {
+    TORCH_CHECK(codebooks.dim() == 3, "codebooks must be [M, ksub, d / M]");
+    c10::cuda::CUDAGuard guard(x.device());
+    at::Tensor xf = contig_f32(x), cf = contig_f32(centroids), cb = contig_f32(codebooks);
+    at::Tensor lab = labels.to(at::kInt).contiguous();
+    const int64_t n = xf.size(0);
+    const int d = static_cast<int>(xf.size(1)), M = static_cast<int>(cb.size(0)), ksub = static_cast<int>(cb.size(1));
+    TORCH_CHECK(cb.size(2) * M == d, "codebooks must be [M, ksub, d / M]");
+    at::Tensor codes = at::empty({n, M}, xf.options().dtype(at::kByte));
+    check_status(rdb_pq_encode(xf.data_ptr<float>(), n, d, d, lab.data_ptr<int32_t>(), cf.data_ptr<float>(),
+                               cb.data_ptr<float>(), M, ksub, codes.data_ptr<uint8_t>(), stream_ptr()),
+                 "pq encode");
+    return codes;
+}
+
+// ------------------------------------------------------------- IVF common
+
+IVFBase::IVFBase(int dim, Metric metric, int nlist, int nprobe) : dim_(dim), metric_(metric), nlist_(nlist) {
+    TORCH_CHECK(dim > 0, "dim must be positive");
+    TORCH_CHECK(nlist >= 1 && nlist <= 16384, "nlist must be in [1, 16384]");
+    set_nprobe(nprobe);
+}
+
+void IVFBase::set_nprobe(int nprobe) {
+    TORCH_CHECK(nprobe >= 1, "nprobe must be >= 1");
+    nprobe_ = nprobe;
+}
+
+void IVFBase::set_centroids(const at::Tensor& centroids) {
+    TORCH_CHECK(centroids.is_cuda(), "centroids must be a CUDA tensor");
+    TORCH_CHECK(centroids.dim() == 2 && centroids.size(0) == nlist_ && centroids.size(1) == dim_,
+                "centroids must be [nlist, dim] = [" + std::to_string(nlist_) + ", " + std::to_string(dim_) + "]");
+    c10::cuda::CUDAGuard guard(centroids.device());
+    centroids_ = contig_f32(centroids).clone();
+    cent_ld_ = padded_ld(dim_, at::kFloat);
+    cent_rows_ = prepare_rows(centroids_, at::kFloat, cent_ld_).clone();
+    cent_xv_ = row_values(Metric::L2, cent_rows_, dim_);
+}
+
+at::Tensor IVFBase::probe(const at::Tensor& queries) const {
+    // nprobe nearest lists by squared L2 (ties to the lower list id)
+    const int np = std::min(nprobe_, nlist_);
+    at::Tensor q32 = prepare_rows(queries.to(at::kFloat), at::kFloat, cent_ld_);
+    auto res = FlatIndex::search_rows(Metric::L2, cent_rows_, dim_, cent_xv_, q32, np, at::Tensor(), 0);
+    return std::get<1>(res);
+}
+
+void IVFBase::check_query(const at::Tensor& queries, int64_t k) const {
+    TORCH_CHECK(queries.is_cuda(), "queries must be on CUDA");
+    TORCH_CHECK(queries.dim() == 2 && queries.size(1) == dim_,
+                "queries must be [batch, " + std::to_string(dim_) + "]");
+    TORCH_CHECK(is_trained(), "index is not trained (call train() or set_quantizer())");
+    TORCH_CHECK(n_ > 0, "index is empty");
+    TORCH_CHECK(k > 0 && k <= n_, "k must be in [1, " + std::to_string(n_) + "]");
+    TORCH_CHECK(k <= 32, "IVF search supports k in [1, 32]");
+}
+
+// Rebuild list-major order after appending rows with list labels `lab_all`:
+// returns the permutation (stored order -> source order) and list offsets.
+std::tuple<at::Tensor, at::Tensor> IVFBase::relist(const at::Tensor& lab_all) {
+    auto sorted = label_sort(lab_all, nlist_);
+    return {std::get<1>(sorted), std::get<0>(sorted)};
+}
+
+void IVFBase::reset() {
+    n_ = 0;
+    labels_ = at::Tensor();
+    ids_ = at::Tensor();
+    list_off_ = at::Tensor();
+}
+
+at::Tensor IVFBase::new_ids(const at::Tensor& vectors, const at::Tensor& ids) const {
+    const int64_t m = vectors.size(0);
+    if (ids.defined() && ids.numel() > 0) {
+        TORCH_CHECK(ids.size(0) == m, "ids length must match vectors");
+        return ids.to(at::kLong).to(vectors.device()).contiguous();
+    }
+    return at::arange(n_, n_ + m, vectors.options().dtype(at::kLong));
+}
+
+at::Tensor IVFBase::list_sizes() const {
+    if (!list_off_.defined()) return at::Tensor();
+    return list_off_.narrow(0, 1, nlist_) - list_off_.narrow(0, 0, nlist_);
+}
+
+// --------------------------------------------------------------- IVF-Flat
+
+IVFFlatIndex::IVFFlatIndex(int dim, Metric metric, int nlist, int nprobe, Precision precision)
+    : IVFBase(dim, metric, nlist, nprobe), precision_(precision) {
+    ld_ = padded_ld(dim, storage_type(precision));
+}
+
+void IVFFlatIndex::add(const at::Tensor& vectors, const at::Tensor& ids) {
+    TORCH_CHECK(vectors.is_cuda(), "vectors must be on CUDA");
+    TORCH_CHECK(vectors.dim() == 2 && vectors.size(1) == dim_, "vectors must be [n, " + std::to_string(dim_) + "]");
+    TORCH_CHECK(is_trained(), "index is not trained (call train() or set_quantizer())");
+    c10::cuda::CUDAGuard guard(vectors.device());
+    const int64_t m = vectors.size(0);
+    if (m == 0) return;
+    at::Tensor nid = new_ids(vectors, ids);
+    // exact list assignment (reference assign arithmetic on fp32 values)
+    at::Tensor lab = std::get<0>(kmeans_assign(vectors.to(at::kFloat), centroids_, true));
+    at::Tensor rows_new = prepare_rows(vectors, storage_type(precision_), ld_);
+    if (!rows_new.is_same(vectors)) rows_new = rows_new.contiguous();
+    at::Tensor xv_new = row_values(metric_, rows_new, dim_);
+    at::Tensor lab_all = n_ ? at::cat({labels_, lab}) : lab;
+    at::Tensor rows_all = n_ ? at::cat({rows_, rows_new}) : rows_new;
+    at::Tensor xv_all = n_ ? at::cat({xv_, xv_new}) : xv_new;
+    at::Tensor ids_all = n_ ? at::cat({ids_, nid}) : nid;
+    auto pl = relist(lab_all);
+    at::Tensor perm = std::get<0>(pl);
+    rows_ = rows_all.index_select(0, perm);
+    xv_ = xv_all.index_select(0, perm);
+    ids_ = ids_all.index_select(0, perm);
+    labels_ = lab_all.index_select(0, perm);
+    list_off_ = std::get<1>(pl);
+    n_ += m;
+}
+
+Result IVFFlatIndex::search(const at::Tensor& queries, int64_t k) const {
+    check_query(queries, k);
+    c10::cuda::CUDAGuard guard(rows_.device());
+    at::Tensor qd = queries.to(rows_.device());
+    at::Tensor probe_lists = probe(qd);
+    const int np = static_cast<int>(probe_lists.size(1));
+    at::Tensor q = prepare_rows(qd, rows_.scalar_type(), ld_);
+    const int64_t nq = q.size(0);
+    at::Tensor cv = at::empty({np, nq, k}, q.options().dtype(at::kFloat));
+    at::Tensor ci = at::empty({np, nq, k}, q.options().dtype(at::kLong));
+    at::Tensor ws = ws_bytes(q, rdb_ivf_scan_workspace(nq, np, nlist_));
+    check_status(rdb_ivf_flat_scan(static_cast<int>(metric_), dtype_code(rows_.scalar_type()), q.data_ptr(), nq, ld_,
+                                   dim_, probe_lists.data_ptr<int64_t>(), np, rows_.data_ptr(), ld_,
+                                   xv_.data_ptr<float>(), list_off_.data_ptr<int64_t>(), nlist_,
+                                   ids_.data_ptr<int64_t>(), static_cast<int>(k), cv.data_ptr<float>(),
+                                   ci.data_ptr<int64_t>(), ws.data_ptr(), ws.numel(), stream_ptr()),
+                 "ivf scan");
+    return topk_merge(cv, ci, k, metric_ != Metric::L2);
+}
+
+void IVFFlatIndex::reset() {
+    IVFBase::reset();
+    rows_ = at::Tensor();
+    xv_ = at::Tensor();
+}
+
+// ----------------------------------------------------------------- IVF-PQ
+
+IVFPQIndex::IVFPQIndex(int dim, Metric metric, int nlist, int nprobe, int m, int ksub)
+    : IVFBase(dim, metric, nlist, nprobe), M_(m), ksub_(ksub) {
+    TORCH_CHECK(metric == Metric::L2, "IVF-PQ supports the l2 metric");
+    TORCH_CHECK(m >= 1 && dim % m == 0, "pq_m must divide dim");
+    TORCH_CHECK(dim / m <= 32, "dim / pq_m must be <= 32");
+    TORCH_CHECK(ksub >= 1 && ksub <= 256, "pq_k must be in [1, 256] (8-bit codes)");
+}
+
+void IVFPQIndex::set_quantizer(const at::Tensor& centroids, const at::Tensor& codebooks) {
+    set_centroids(centroids);
+    TORCH_CHECK(codebooks.is_cuda() && codebooks.dim() == 3 && codebooks.size(0) == M_ && codebooks.size(1) == ksub_ &&
+                    codebooks.size(2) * M_ == dim_,
+                "codebooks must be [pq_m, pq_k, dim / pq_m]");
+    codebooks_ = contig_f32(codebooks).clone();
+}
+
+void IVFPQIndex::add(const at::Tensor& vectors, const at::Tensor& ids) {
+    TORCH_CHECK(vectors.is_cuda(), "vectors must be on CUDA");
+    TORCH_CHECK(vectors.dim() == 2 && vectors.size(1) == dim_, "vectors must be [n, " + std::to_string(dim_) + "]");
+    TORCH_CHECK(is_trained() && codebooks_.defined(), "index is not trained (call train() or set_quantizer())");
+    c10::cuda::CUDAGuard guard(vectors.device());
+    const int64_t m = vectors.size(0);
+    if (m == 0) return;
+    at::Tensor nid = new_ids(vectors, ids);
+    at::Tensor xf = contig_f32(vectors);
+    at::Tensor lab = std::get<0>(kmeans_assign(xf, centroids_, true));
+    at::Tensor codes_new = pq_encode(xf, lab, centroids_, codebooks_);
+    at::Tensor lab_all = n_ ? at::cat({labels_, lab}) : lab;
+    at::Tensor codes_all = n_ ? at::cat({codes_, codes_new}) : codes_new;
+    at::Tensor ids_all = n_ ? at::cat({ids_, nid}) : nid;
+    auto pl = relist(lab_all);
+    at::Tensor perm = std::get<0>(pl);
+    codes_ = codes_all.index_select(0, perm);
+    ids_ = ids_all.index_select(0, perm);
+    labels_ = lab_all.index_select(0, perm);
+    list_off_ = std::get<1>(pl);
+    n_ += m;
+}
+
+Result IVFPQIndex::search(const at::Tensor& queries, int64_t k) const {
+    check_query(queries, k);
+    c10::cuda::CUDAGuard guard(codes_.device());
+    at::Tensor q = contig_f32(queries.to(codes_.device()));
+    at::Tensor probe_lists = probe(q);
+    const int np = static_cast<int>(probe_lists.size(1));
+    const int64_t nq = q.size(0);
+    at::Tensor cv = at::empty({np, nq, k}, q.options());
+    at::Tensor ci = at::empty({np, nq, k}, q.options().dtype(at::kLong));
+    at::Tensor ws = ws_bytes(q, rdb_ivf_scan_workspace(nq, np, nlist_));
+    check_status(rdb_ivfpq_scan(q.data_ptr<float>(), nq, dim_, dim_, probe_lists.data_ptr<int64_t>(), np,
+                                centroids_.data_ptr<float>(), nlist_, codebooks_.data_ptr<float>(), M_, ksub_,
+                                codes_.data_ptr<uint8_t>(), list_off_.data_ptr<int64_t>(), ids_.data_ptr<int64_t>(),
+                                static_cast<int>(k), cv.data_ptr<float>(), ci.data_ptr<int64_t>(), ws.data_ptr(),
+                                ws.numel(), stream_ptr()),
+                 "ivf-pq scan");
+    return topk_merge(cv, ci, k, false);
+}
+
+void IVFPQIndex::reset() {
+    IVFBase::reset();
+    codes_ = at::Tensor();
+}
+
+}  // namespace rdbh

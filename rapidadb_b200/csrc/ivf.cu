@@ -1,0 +1,515 @@
+// IVF-Flat and IVF-PQ list scans, PQ encoding.
+//
+// The reference has no IVF or PQ code (its config fields nlist / nprobe /
+// pq_m / pq_k, python/rapidadb/config.py:50-56, are unused); the semantics
+// follow the CPU oracle (oracle/cpu_oracle.c: orc_ivf_flat_search,
+// orc_pq_encode, orc_ivfpq_search).
+//
+// Both scans are LIST-MAJOR: the [Q, nprobe] probe table is inverted with the
+// stable label sort (entries grouped by list), and one CTA scores a list's
+// rows (IVF-Flat) or codes (IVF-PQ) for every query that probes it, so a list
+// crosses HBM once per CTA instead of once per probing query.  Each
+// (query, probed list) pair yields its best k (k <= 32, kept sorted in the
+// registers of one warp: lane i holds the i-th best), written to
+// out[probe slot][query][k]; the merge kernel (rdb_topk_merge) then keeps the
+// best k of the nprobe lists.
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+
+#include <algorithm>
+
+#include "scan.cuh"
+#include "sort.cuh"
+
+namespace rdb {
+namespace {
+
+constexpr unsigned FULL = 0xffffffffu;
+constexpr int kMaxIvfK = 32;
+
+inline size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+
+template <typename T>
+__device__ __forceinline__ float to_f(T v);
+template <>
+__device__ __forceinline__ float to_f<float>(float v) { return v; }
+template <>
+__device__ __forceinline__ float to_f<__half>(__half v) { return __half2float(v); }
+template <>
+__device__ __forceinline__ float to_f<__nv_bfloat16>(__nv_bfloat16 v) { return __bfloat162float(v); }
+
+// a ranks before b; ties to the lower row
+__device__ __forceinline__ bool ranks_before(float a, int64_t ia, float b, int64_t ib, bool largest) {
+    if (a != b) return largest ? (a > b) : (a < b);
+    return ia < ib;
+}
+
+// Sorted best-k of one query held by one warp: lane i < k keeps the i-th best.
+struct WarpTopK {
+    float v;
+    int64_t id;
+    __device__ __forceinline__ void init(bool largest) {
+        v = largest ? -INFINITY : INFINITY;
+        id = INT64_MAX;
+    }
+    // every lane offers (s, sid) when `valid`; the warp inserts those that
+    // beat the current k-th, lowest lane first
+    __device__ __forceinline__ void offer(float s, int64_t sid, bool valid, int k, bool largest, int lane) {
+        float kv = __shfl_sync(FULL, v, k - 1);
+        int64_t kid = __shfl_sync(FULL, id, k - 1);
+        unsigned m = __ballot_sync(FULL, valid && ranks_before(s, sid, kv, kid, largest));
+        while (m) {
+            const int src = __ffs(m) - 1;
+            m &= m - 1;
+            const float cs = __shfl_sync(FULL, s, src);
+            const int64_t cid = __shfl_sync(FULL, sid, src);
+            kv = __shfl_sync(FULL, v, k - 1);
+            kid = __shfl_sync(FULL, id, k - 1);
+            if (!ranks_before(cs, cid, kv, kid, largest)) continue;
+            const unsigned bm = __ballot_sync(FULL, lane < k && ranks_before(v, id, cs, cid, largest));
+            const int pos = __popc(bm);
+            const float pv = __shfl_up_sync(FULL, v, 1);
+            const int64_t pid = __shfl_up_sync(FULL, id, 1);
+            if (lane == pos) {
+                v = cs;
+                id = cid;
+            } else if (lane > pos && lane < k) {
+                v = pv;
+                id = pid;
+            }
+        }
+    }
+};
+
+__global__ void probe_to_labels_kernel(const int64_t* __restrict__ probe, int64_t n, int nlist,
+                                       int32_t* __restrict__ labels) {
+    int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= n) return;
+    int64_t l = probe[i];
+    labels[i] = (l >= 0 && l < nlist) ? (int32_t)l : 0;
+}
+
+// ------------------------------------------------------------- IVF-Flat scan
+
+constexpr int FQ = 32;   // queries per chunk
+constexpr int FR = 128;  // rows per tile
+constexpr int FK = 32;   // K chunk
+constexpr int FNT = 256;
+
+template <typename T>
+__global__ void __launch_bounds__(FNT) ivf_flat_scan_kernel(
+    int metric, int cos_small, const T* __restrict__ q, int64_t Q, int64_t ldq, int d, const float* __restrict__ qv,
+    int nprobe, const int64_t* __restrict__ eperm, const int64_t* __restrict__ eseg, const T* __restrict__ rows,
+    int64_t ldx, const float* __restrict__ xv, const int64_t* __restrict__ list_off, int nlist,
+    const int64_t* __restrict__ ids, int k, float* __restrict__ out_v, int64_t* __restrict__ out_i) {
+    __shared__ float Qs[FK][FQ];
+    __shared__ float Xs[FK][FR + 4];
+    __shared__ float S[FQ][FR + 1];
+    __shared__ int64_t s_q[FQ];
+    __shared__ int s_p[FQ];
+    __shared__ float s_qv[FQ];
+    const bool largest = metric != RDB_METRIC_L2;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, tq = tid >> 5, tr = tid & 31;
+
+    for (int l = blockIdx.x; l < nlist; l += gridDim.x) {
+        const int64_t e0 = eseg[l], e1 = eseg[l + 1];
+        const int64_t r0 = list_off[l], r1 = list_off[l + 1];
+        for (int64_t ec = e0; ec < e1; ec += FQ) {
+            const int nqc = (int)min((int64_t)FQ, e1 - ec);
+            __syncthreads();
+            if (tid < FQ) {
+                if (tid < nqc) {
+                    const int64_t e = eperm[ec + tid];
+                    s_q[tid] = e / nprobe;
+                    s_p[tid] = (int)(e % nprobe);
+                    s_qv[tid] = qv ? qv[e / nprobe] : 0.f;
+                } else {
+                    s_q[tid] = -1;
+                    s_p[tid] = 0;
+                    s_qv[tid] = 0.f;
+                }
+            }
+            WarpTopK st[4];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) st[j].init(largest);
+            __syncthreads();
+            for (int64_t t0 = r0; t0 < r1; t0 += FR) {
+                float acc[4][4];
+#pragma unroll
+                for (int i = 0; i < 4; ++i)
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) acc[i][j] = 0.f;
+                for (int k0 = 0; k0 < d; k0 += FK) {
+                    __syncthreads();
+                    {
+                        const int qi = tid >> 3, kk = (tid & 7) * 4;
+                        const int64_t qq = s_q[qi];
+#pragma unroll
+                        for (int i = 0; i < 4; ++i) {
+                            const int kx = k0 + kk + i;
+                            Qs[kk + i][qi] = (qq >= 0 && kx < d) ? to_f<T>(q[qq * ldq + kx]) : 0.f;
+                        }
+                    }
+                    {
+                        const int ri = tid >> 1, kk = (tid & 1) * 16;
+                        const int64_t r = t0 + ri;
+                        const bool rv = r < r1;
+#pragma unroll
+                        for (int i = 0; i < 16; ++i) {
+                            const int kx = k0 + kk + i;
+                            Xs[kk + i][ri] = (rv && kx < d) ? to_f<T>(rows[r * ldx + kx]) : 0.f;
+                        }
+                    }
+                    __syncthreads();
+#pragma unroll 8
+                    for (int kk = 0; kk < FK; ++kk) {
+                        const float4 av = *reinterpret_cast<const float4*>(&Qs[kk][tq * 4]);
+                        const float a_[4] = {av.x, av.y, av.z, av.w};
+                        float b_[4];
+#pragma unroll
+                        for (int j = 0; j < 4; ++j) b_[j] = Xs[kk][tr + 32 * j];
+#pragma unroll
+                        for (int i = 0; i < 4; ++i)
+#pragma unroll
+                            for (int j = 0; j < 4; ++j) {
+                                if (metric == RDB_METRIC_L2) {
+                                    const float df = a_[i] - b_[j];
+                                    acc[i][j] = fmaf(df, df, acc[i][j]);
+                                } else {
+                                    acc[i][j] = fmaf(a_[i], b_[j], acc[i][j]);
+                                }
+                            }
+                    }
+                }
+                // final scores of the tile -> S
+#pragma unroll
+                for (int i = 0; i < 4; ++i)
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) {
+                        const int qi = tq * 4 + i, ri = tr + 32 * j;
+                        const int64_t r = t0 + ri;
+                        float sc = acc[i][j];
+                        if (metric == RDB_METRIC_COSINE && r < r1) sc = final_score(metric, cos_small, sc, s_qv[qi], xv[r]);
+                        S[qi][ri] = sc;
+                    }
+                __syncthreads();
+                // warp w keeps queries 4w .. 4w + 3
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    const int qi = warp * 4 + j;
+#pragma unroll
+                    for (int b = 0; b < FR / 32; ++b) {
+                        const int64_t r = t0 + 32 * b + lane;
+                        st[j].offer(S[qi][32 * b + lane], r, r < r1, k, largest, lane);
+                    }
+                }
+            }
+            // write the (query, probe slot) lists
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const int qi = warp * 4 + j;
+                const int64_t qq = s_q[qi];
+                if (qq >= 0 && lane < k) {
+                    const int64_t o = ((int64_t)s_p[qi] * Q + qq) * k + lane;
+                    const bool has = st[j].id != INT64_MAX;
+                    out_v[o] = st[j].v;
+                    out_i[o] = has ? (ids ? ids[st[j].id] : st[j].id) : -1;
+                }
+            }
+        }
+    }
+}
+
+// ------------------------------------------------------------- PQ encode
+
+// One thread per (row, subspace): argmin over codewords of the sequential
+// fused-FMA squared distance to the residual sub-vector (ties: lower codeword).
+__global__ void pq_encode_kernel(const float* __restrict__ x, int64_t n, int64_t ldx, int d,
+                                 const int32_t* __restrict__ labels, const float* __restrict__ centroids,
+                                 const float* __restrict__ codebooks, int M, int ksub, uint8_t* __restrict__ codes) {
+    extern __shared__ float cb[];  // [M][ksub][dsub]
+    const int dsub = d / M;
+    for (int i = threadIdx.x; i < M * ksub * dsub; i += blockDim.x) cb[i] = codebooks[i];
+    __syncthreads();
+    const int64_t pairs = n * M;
+    for (int64_t pi = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; pi < pairs; pi += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t row = pi / M;
+        const int m = (int)(pi % M);
+        const float* xr = x + row * ldx + m * dsub;
+        const float* cr = centroids + (int64_t)labels[row] * d + m * dsub;
+        float r[32];
+#pragma unroll 4
+        for (int u = 0; u < dsub; ++u) r[u] = xr[u] - cr[u];
+        const float* cbm = cb + (int64_t)m * ksub * dsub;
+        float best = INFINITY;
+        int bj = 0;
+        for (int j = 0; j < ksub; ++j) {
+            const float* p = cbm + j * dsub;
+            float s = 0.f;
+            for (int u = 0; u < dsub; ++u) {
+                const float t = r[u] - p[u];
+                s = fmaf(t, t, s);
+            }
+            if (s < best) {
+                best = s;
+                bj = j;
+            }
+        }
+        codes[row * M + m] = (uint8_t)bj;
+    }
+}
+
+// ------------------------------------------------------------- IVF-PQ scan
+
+constexpr int PNT = 512;
+constexpr int PNW = PNT / 32;
+
+__global__ void __launch_bounds__(PNT) ivfpq_scan_kernel(
+    const float* __restrict__ q, int64_t Q, int64_t ldq, int d, int nprobe, const int64_t* __restrict__ eperm,
+    const int64_t* __restrict__ eseg, const float* __restrict__ centroids, const float* __restrict__ codebooks, int M,
+    int ksub, const uint8_t* __restrict__ codes, const int64_t* __restrict__ list_off, int nlist,
+    const int64_t* __restrict__ ids, int k, float* __restrict__ out_v, int64_t* __restrict__ out_i) {
+    extern __shared__ float psm[];
+    const int dsub = d / M;
+    float* cb = psm;                                  // M * ksub * dsub
+    float* lut = cb + (size_t)M * ksub * dsub;        // M * ksub
+    float* res = lut + (size_t)M * ksub;              // d
+    float* mv = res + ((d + 3) & ~3);                 // PNW * kMaxIvfK
+    int64_t* mi = reinterpret_cast<int64_t*>(
+        (reinterpret_cast<uintptr_t>(mv + PNW * kMaxIvfK) + 7) & ~uintptr_t(7));  // PNW * kMaxIvfK
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    for (int i = tid; i < M * ksub * dsub; i += PNT) cb[i] = codebooks[i];
+    __syncthreads();
+    const bool m16 = (M % 16) == 0;
+
+    for (int l = blockIdx.x; l < nlist; l += gridDim.x) {
+        const int64_t e0 = eseg[l], e1 = eseg[l + 1];
+        const int64_t r0 = list_off[l], r1 = list_off[l + 1];
+        const float* cl = centroids + (int64_t)l * d;
+        for (int64_t e = e0; e < e1; ++e) {
+            const int64_t ent = eperm[e];
+            const int64_t qq = ent / nprobe;
+            const int p = (int)(ent % nprobe);
+            __syncthreads();
+            for (int t = tid; t < d; t += PNT) res[t] = q[qq * ldq + t] - cl[t];
+            __syncthreads();
+            // LUT[m][j] = |res_m - codeword_mj|^2
+            for (int i = tid; i < M * ksub; i += PNT) {
+                const int m = i / ksub, j = i % ksub;
+                const float* pv = cb + ((size_t)m * ksub + j) * dsub;
+                const float* rv = res + m * dsub;
+                float s = 0.f;
+                for (int u = 0; u < dsub; ++u) {
+                    const float t = rv[u] - pv[u];
+                    s = fmaf(t, t, s);
+                }
+                lut[i] = s;
+            }
+            __syncthreads();
+            WarpTopK st;
+            st.init(false);
+            // rows of the list, 32 per warp step (one 128-bit code load per row when M % 16 == 0)
+            for (int64_t base = r0 + (int64_t)warp * 32; base < r1; base += (int64_t)PNT) {
+                const int64_t row = base + lane;
+                float dist = INFINITY;
+                const bool valid = row < r1;
+                if (valid) {
+                    const uint8_t* cr = codes + row * M;
+                    dist = 0.f;
+                    if (m16) {
+                        for (int m0 = 0; m0 < M; m0 += 16) {
+                            const uint4 w4 = *reinterpret_cast<const uint4*>(cr + m0);
+                            const uint32_t w[4] = {w4.x, w4.y, w4.z, w4.w};
+#pragma unroll
+                            for (int b = 0; b < 16; ++b) {
+                                const uint32_t c = (w[b >> 2] >> (8 * (b & 3))) & 0xffu;
+                                dist += lut[(m0 + b) * ksub + c];
+                            }
+                        }
+                    } else {
+                        for (int m = 0; m < M; ++m) dist += lut[m * ksub + cr[m]];
+                    }
+                }
+                st.offer(dist, row, valid, k, false, lane);
+            }
+            // merge the warps' lists
+            if (lane < k) {
+                mv[warp * kMaxIvfK + lane] = st.v;
+                mi[warp * kMaxIvfK + lane] = st.id;
+            }
+            __syncthreads();
+            if (warp == 0) {
+                WarpTopK fin;
+                fin.init(false);
+                // warp-uniform trip count: every lane offers in every round
+                for (int base = 0; base < PNW * k; base += 32) {
+                    const int i = base + lane;
+                    const bool valid = i < PNW * k;
+                    const int w = valid ? i / k : 0, j = valid ? i % k : 0;
+                    fin.offer(mv[w * kMaxIvfK + j], mi[w * kMaxIvfK + j], valid, k, false, lane);
+                }
+                if (lane < k) {
+                    const int64_t o = ((int64_t)p * Q + qq) * k + lane;
+                    const bool has = fin.id != INT64_MAX;
+                    out_v[o] = fin.v;
+                    out_i[o] = has ? (ids ? ids[fin.id] : fin.id) : -1;
+                }
+            }
+        }
+    }
+}
+
+struct IvfWs {
+    size_t off_lab, off_perm, off_seg, off_qv, off_sort, bytes;
+};
+
+IvfWs ivf_ws(int64_t Q, int nprobe, int nlist) {
+    IvfWs w;
+    const int64_t ne = Q * nprobe;
+    size_t off = 0;
+    w.off_lab = off;
+    off = align_up(off + sizeof(int32_t) * std::max<int64_t>(ne, 1), 256);
+    w.off_perm = off;
+    off = align_up(off + sizeof(int64_t) * std::max<int64_t>(ne, 1), 256);
+    w.off_seg = off;
+    off = align_up(off + sizeof(int64_t) * (nlist + 1), 256);
+    w.off_qv = off;
+    off = align_up(off + sizeof(float) * std::max<int64_t>(Q, 1), 256);
+    w.off_sort = off;
+    off = align_up(off + label_sort_workspace(ne, nlist), 256);
+    w.bytes = off;
+    return w;
+}
+
+// group the Q x nprobe probe entries by list
+int invert_probes(const int64_t* probe, int64_t Q, int nprobe, int nlist, const IvfWs& w, char* base,
+                  cudaStream_t s) {
+    const int64_t ne = Q * nprobe;
+    int32_t* lab = reinterpret_cast<int32_t*>(base + w.off_lab);
+    probe_to_labels_kernel<<<(unsigned)((ne + 255) / 256), 256, 0, s>>>(probe, ne, nlist, lab);
+    RDB_LAUNCH_CHECK();
+    return label_sort(lab, ne, nlist, reinterpret_cast<int64_t*>(base + w.off_seg),
+                      reinterpret_cast<int64_t*>(base + w.off_perm), nullptr, base + w.off_sort,
+                      label_sort_workspace(ne, nlist), s);
+}
+
+size_t pq_smem(int d, int M, int ksub) {
+    return sizeof(float) * ((size_t)ksub * d + (size_t)M * ksub + ((d + 3) & ~3) + PNW * kMaxIvfK) +
+           sizeof(int64_t) * (PNW * kMaxIvfK + 1);
+}
+
+}  // namespace
+}  // namespace rdb
+
+using namespace rdb;
+
+extern "C" {
+
+size_t rdb_ivf_scan_workspace(int64_t nq, int nprobe, int nlist) { return ivf_ws(nq, nprobe, nlist).bytes; }
+
+int rdb_ivf_flat_scan(int metric, int dtype, const void* q, int64_t nq, int64_t ldq, int d, const int64_t* probe,
+                      int nprobe, const void* rows, int64_t ldx, const float* xv, const int64_t* list_off, int nlist,
+                      const int64_t* ids, int k, float* out_v, int64_t* out_i, void* ws, size_t ws_bytes,
+                      void* stream) {
+    RDB_CHECK_ARG(metric >= 0 && metric <= 2, "unknown metric %d", metric);
+    RDB_CHECK_ARG(elem_size(dtype) != 0, "unknown dtype %d", dtype);
+    RDB_CHECK_ARG(nq >= 0 && d >= 1 && nprobe >= 1 && nlist >= 1 && nlist <= kMaxLabels, "bad shape");
+    RDB_CHECK_ARG(k >= 1 && k <= kMaxIvfK, "IVF search supports k in [1, %d]", kMaxIvfK);
+    if (nq == 0) return RDB_OK;
+    RDB_CHECK_ARG(q && probe && list_off && out_v && out_i && ws, "NULL pointer");
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    IvfWs w = ivf_ws(nq, nprobe, nlist);
+    if (ws_bytes < w.bytes) return set_error(RDB_ERR_WORKSPACE, "workspace too small: %zu < %zu", ws_bytes, w.bytes);
+    char* base = static_cast<char*>(ws);
+    RDB_TRY(invert_probes(probe, nq, nprobe, nlist, w, base, s));
+    float* qv = reinterpret_cast<float*>(base + w.off_qv);
+    const int cos_small = d <= 128 ? 1 : 0;
+    if (metric == RDB_METRIC_COSINE) {
+        RDB_CHECK_ARG(xv, "cosine needs per-row values");
+        if (ldq == d) {
+            RDB_TRY(rdb_row_sqnorms(dtype, q, nq, d, qv, s));
+        } else {
+            RDB_TRY(rdb_row_sqnorms(dtype, q, nq, (int)ldq, qv, s));
+        }
+        RDB_TRY(rdb_vec_values(metric, d, qv, nq, qv, s));
+    }
+    const unsigned grid = (unsigned)std::min<int64_t>(nlist, 65535LL * 16);
+    const int64_t* eperm = reinterpret_cast<const int64_t*>(base + w.off_perm);
+    const int64_t* eseg = reinterpret_cast<const int64_t*>(base + w.off_seg);
+    switch (dtype) {
+        case RDB_F32:
+            ivf_flat_scan_kernel<float><<<grid, FNT, 0, s>>>(metric, cos_small, (const float*)q, nq, ldq, d, qv, nprobe,
+                                                             eperm, eseg, (const float*)rows, ldx, xv, list_off, nlist,
+                                                             ids, k, out_v, out_i);
+            break;
+        case RDB_F16:
+            ivf_flat_scan_kernel<__half><<<grid, FNT, 0, s>>>(metric, cos_small, (const __half*)q, nq, ldq, d, qv,
+                                                              nprobe, eperm, eseg, (const __half*)rows, ldx, xv,
+                                                              list_off, nlist, ids, k, out_v, out_i);
+            break;
+        default:
+            ivf_flat_scan_kernel<__nv_bfloat16><<<grid, FNT, 0, s>>>(
+                metric, cos_small, (const __nv_bfloat16*)q, nq, ldq, d, qv, nprobe, eperm, eseg,
+                (const __nv_bfloat16*)rows, ldx, xv, list_off, nlist, ids, k, out_v, out_i);
+    }
+    RDB_LAUNCH_CHECK();
+    return RDB_OK;
+}
+
+int rdb_pq_encode(const float* x, int64_t n, int64_t ldx, int d, const int32_t* labels, const float* centroids,
+                  const float* codebooks, int M, int ksub, uint8_t* codes, void* stream) {
+    RDB_CHECK_ARG(n >= 0 && d >= 1 && M >= 1 && d % M == 0, "d must be a multiple of M");
+    RDB_CHECK_ARG(d / M <= 32, "sub-vector dimension d / M must be <= 32");
+    RDB_CHECK_ARG(ksub >= 1 && ksub <= 256, "ksub must be in [1, 256] (8-bit codes)");
+    if (n == 0) return RDB_OK;
+    RDB_CHECK_ARG(x && labels && centroids && codebooks && codes, "NULL pointer");
+    const size_t smem = sizeof(float) * (size_t)ksub * d;
+    RDB_CHECK_ARG(smem <= 200 * 1024, "codebooks too large for shared memory (ksub * d <= 51200)");
+    static bool attr[64] = {false};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 64 && !attr[dev]) {
+        RDB_CUDA_TRY(cudaFuncSetAttribute(pq_encode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
+        attr[dev] = true;
+    }
+    const int64_t pairs = n * M;
+    const unsigned grid = (unsigned)std::min<int64_t>((pairs + 255) / 256, 4LL * num_sms());
+    pq_encode_kernel<<<grid, 256, smem, static_cast<cudaStream_t>(stream)>>>(x, n, ldx, d, labels, centroids,
+                                                                           codebooks, M, ksub, codes);
+    RDB_LAUNCH_CHECK();
+    return RDB_OK;
+}
+
+int rdb_ivfpq_scan(const float* q, int64_t nq, int64_t ldq, int d, const int64_t* probe, int nprobe,
+                   const float* centroids, int nlist, const float* codebooks, int M, int ksub, const uint8_t* codes,
+                   const int64_t* list_off, const int64_t* ids, int k, float* out_v, int64_t* out_i, void* ws,
+                   size_t ws_bytes, void* stream) {
+    RDB_CHECK_ARG(nq >= 0 && d >= 1 && M >= 1 && d % M == 0, "d must be a multiple of M");
+    RDB_CHECK_ARG(ksub >= 1 && ksub <= 256, "ksub must be in [1, 256]");
+    RDB_CHECK_ARG(nprobe >= 1 && nlist >= 1 && nlist <= kMaxLabels, "bad shape");
+    RDB_CHECK_ARG(k >= 1 && k <= kMaxIvfK, "IVF-PQ search supports k in [1, %d]", kMaxIvfK);
+    if (nq == 0) return RDB_OK;
+    RDB_CHECK_ARG(q && probe && centroids && codebooks && codes && list_off && out_v && out_i && ws, "NULL pointer");
+    const size_t smem = pq_smem(d, M, ksub);
+    RDB_CHECK_ARG(smem <= 220 * 1024, "codebooks + tables too large for shared memory");
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    IvfWs w = ivf_ws(nq, nprobe, nlist);
+    if (ws_bytes < w.bytes) return set_error(RDB_ERR_WORKSPACE, "workspace too small: %zu < %zu", ws_bytes, w.bytes);
+    char* base = static_cast<char*>(ws);
+    RDB_TRY(invert_probes(probe, nq, nprobe, nlist, w, base, s));
+    static bool attr[64] = {false};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 64 && !attr[dev]) {
+        RDB_CUDA_TRY(cudaFuncSetAttribute(ivfpq_scan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 220 * 1024));
+        attr[dev] = true;
+    }
+    const unsigned grid = (unsigned)std::min<int64_t>(nlist, (int64_t)num_sms());
+    ivfpq_scan_kernel<<<grid, PNT, smem, s>>>(q, nq, ldq, d, nprobe, reinterpret_cast<const int64_t*>(base + w.off_perm),
+                                            reinterpret_cast<const int64_t*>(base + w.off_seg), centroids, codebooks, M,
+                                            ksub, codes, list_off, nlist, ids, k, out_v, out_i);
+    RDB_LAUNCH_CHECK();
+    return RDB_OK;
+}
+
+}  // extern "C"

@@ -13,6 +13,7 @@ enum ScanMode : int {
     SCAN_DENSE = 1,   // write final scores to dense_out[q, row]
     SCAN_ARGMIN = 2,  // best row per (split, query) by squared L2
     SCAN_GROUPMAX = 3,  // best score of every `group` consecutive logical rows
+    SCAN_ARGMIN_EXACT = 4,  // CUDA cores: argmin of sum (q - x)^2, one FMA per element in order
 };
 
 struct ScanArgs {

@@ -173,9 +173,8 @@ __global__ void __launch_bounds__(NT) simt_scan_kernel(ScanArgs a) {
                             a.cand[((int64_t)split * a.nq + q) * a.cap + slot] = make_uint2(
                                 __float_as_uint(final_score(a.metric, a.cos_small, v, sQv[qi], xv)), (uint32_t)r);
                     }
-                } else {  // SCAN_ARGMIN (squared L2)
-                    float xv = a.xv[r * a.row_step];
-                    float dist = fmaxf(sQv[qi] + xv - 2.f * v, 0.f);
+                } else {  // SCAN_ARGMIN (squared L2; exact: summed directly)
+                    float dist = DIRECT_L2 ? v : fmaxf(sQv[qi] + a.xv[r * a.row_step] - 2.f * v, 0.f);
                     unsigned long long key =
                         ((unsigned long long)float_asc_key(dist) << 32) | (uint32_t)r;
                     atomicMin(&sbest[qi], key);
@@ -196,6 +195,8 @@ int launch_typed(const ScanArgs& a, int mode, cudaStream_t s, dim3 grid) {
         simt_scan_kernel<T, SCAN_FILTER, false><<<grid, NT, 0, s>>>(a);
     else if (mode == SCAN_ARGMIN)
         simt_scan_kernel<T, SCAN_ARGMIN, false><<<grid, NT, 0, s>>>(a);
+    else if (mode == SCAN_ARGMIN_EXACT)
+        simt_scan_kernel<T, SCAN_ARGMIN, true><<<grid, NT, 0, s>>>(a);
     else if (a.metric == RDB_METRIC_L2)
         simt_scan_kernel<T, SCAN_DENSE, true><<<grid, NT, 0, s>>>(a);
     else

@@ -86,12 +86,38 @@ class RapidaDB:
             f"Index type '{cfg.index_type.value}' not available in this build")
 
     # -------------------------------------------------------------- training
-    def train(self, vectors: torch.Tensor) -> None:
-        """Train the IVF coarse quantizer (and PQ codebooks) on `vectors`."""
-        if not hasattr(self._index, "train"):
-            return
+    def train(self, vectors: torch.Tensor, group=None) -> None:
+        """Train the IVF coarse quantizer (k-means, ``config.nlist`` lists,
+        ``config.kmeans_iters`` Lloyd iterations) and, for IVF-PQ, the
+        per-subspace codebooks on the residuals.  ``config.train_sample`` > 0
+        trains on that many seeded rows.  No-op for Flat."""
         cfg = self._config
-        self._index.train(_as_float_cuda(vectors), cfg.kmeans_iters, cfg.seed, cfg.train_sample)
+        if cfg.index_type == IndexType.FLAT:
+            return
+        from rapidadb_b200.kmeans import kmeans, train_pq
+        from rapidadb_b200.utils import sample_rows
+
+        x = _as_float_cuda(vectors)
+        if 0 < cfg.train_sample < x.shape[0]:
+            idx = torch.tensor(sorted(sample_rows(x.shape[0], cfg.train_sample, cfg.seed)),
+                               dtype=torch.long, device=x.device)
+            x = x.index_select(0, idx)
+        coarse = kmeans(x, cfg.nlist, cfg.kmeans_iters, 0.0, cfg.seed, group=group).centroids
+        if cfg.index_type == IndexType.IVF:
+            self._index.set_quantizer(coarse)
+            return
+        labels, _ = C().kmeans_assign(x.float(), coarse, True)
+        residuals = x.float() - coarse.index_select(0, labels.long())
+        books = train_pq(residuals, cfg.pq_m, cfg.pq_k, cfg.kmeans_iters, cfg.seed, group=group)
+        self._index.set_quantizer(coarse, books)
+
+    def set_quantizer(self, centroids: torch.Tensor, codebooks: Optional[torch.Tensor] = None) -> None:
+        """Install trained IVF centroids [nlist, dim] (and IVF-PQ codebooks
+        [pq_m, pq_k, dim / pq_m]) directly."""
+        if codebooks is None:
+            self._index.set_quantizer(centroids.cuda().float())
+        else:
+            self._index.set_quantizer(centroids.cuda().float(), codebooks.cuda().float())
 
     @property
     def is_trained(self) -> bool:

@@ -33,11 +33,12 @@ def gather_candidates(local_d: torch.Tensor, local_i: torch.Tensor,
     """All-gather [Q, k] scores and ids from every rank into [G, Q, k]."""
     world = dist.get_world_size(group)
     Q, k = local_d.shape
-    out_d = torch.empty((world, Q, k), dtype=local_d.dtype, device=local_d.device)
-    out_i = torch.empty((world, Q, k), dtype=local_i.dtype, device=local_i.device)
+    # gathered along dim 0 as [G * Q, k] (the layout every backend accepts)
+    out_d = torch.empty((world * Q, k), dtype=local_d.dtype, device=local_d.device)
+    out_i = torch.empty((world * Q, k), dtype=local_i.dtype, device=local_i.device)
     dist.all_gather_into_tensor(out_d, local_d.contiguous(), group=group)
     dist.all_gather_into_tensor(out_i, local_i.contiguous(), group=group)
-    return out_d, out_i
+    return out_d.view(world, Q, k), out_i.view(world, Q, k)
 
 
 def gpu_merge(vals: torch.Tensor, ids: torch.Tensor, k: int, largest: bool):
