@@ -171,6 +171,24 @@ int rdb_ivf_flat_scan(int metric, int dtype, const void* q, int64_t nq, int64_t 
                       const int64_t* ids, int k, float* out_v, int64_t* out_i, void* ws, size_t ws_bytes,
                       void* stream);
 
+/* rdb_ivf_flat_scan for callers that may not allocate GPU memory (no
+ * counterpart in the reference): the same list-major scan and the same
+ * results, with its scratch taken from an 8 MiB array compiled into the
+ * library (rdb_noalloc_scratch_bytes) instead of a caller workspace, for
+ * hosts that pool all device memory themselves, serving threads that must
+ * not block in an allocator, or plug-ins whose host runtime forbids guest
+ * allocations.  Returns RDB_ERR_UNSUPPORTED when rdb_ivf_scan_workspace(nq,
+ * nprobe, nlist) exceeds the array.  Every GPU that loads the library holds
+ * the array until exit; all calls on a device share it, so calls that
+ * overlap on the GPU race -- serialise them.  The first call on each device
+ * looks the array up with cudaGetSymbolAddress: make it before any stream
+ * capture.  The call allocates nothing. */
+size_t rdb_noalloc_scratch_bytes(void);
+int rdb_ivf_flat_scan_noalloc(int metric, int dtype, const void* q, int64_t nq, int64_t ldq, int d,
+                              const int64_t* probe, int nprobe, const void* rows, int64_t ldx, const float* xv,
+                              const int64_t* list_off, int nlist, const int64_t* ids, int k, float* out_v,
+                              int64_t* out_i, void* stream);
+
 /* Residual product-quantisation codes: for row i in list labels[i], residual
  * r = x_i - centroid; code m = argmin over the ksub codewords of subspace m
  * (codebooks [M, ksub, d / M]) of the sequential fused-FMA squared distance,

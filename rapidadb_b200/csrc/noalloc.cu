@@ -1,0 +1,81 @@
+// IVF-Flat list scan for callers that cannot allocate GPU memory.
+//
+// Some hosts embed this library where device allocation is off limits while
+// they run: a caller that has already carved all device memory into its own
+// pool, a real-time serving thread that must never block in the allocator, or
+// a plug-in whose host runtime owns the CUDA context and forbids allocations
+// from guest code.  rdb_ivf_flat_scan needs a scratch workspace from its
+// caller; rdb_ivf_flat_scan_noalloc runs the same scan with its scratch taken
+// from a fixed array compiled into this library, so the call itself allocates
+// nothing.
+//
+// Costs and rules:
+//   - every GPU that loads the library holds kNoAllocScratchBytes (8 MiB) of
+//     device memory for this array until the process exits;
+//   - all calls on a device share the one array: calls that overlap on the
+//     GPU (on different streams, or from different host threads) race and
+//     corrupt each other's results -- serialise them;
+//   - the first call on each device looks up the array's device address with
+//     cudaGetSymbolAddress (with that device current); make that first call
+//     before any stream capture begins;
+//   - the array keeps the previous call's contents, but nothing in it needs to
+//     start at zero: every scratch byte the scan reads is written earlier in
+//     the same call.
+#include <mutex>
+
+#include "common.cuh"
+
+namespace rdb {
+namespace {
+
+constexpr size_t kNoAllocScratchBytes = size_t(8) << 20;
+
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
+
+void* g_scratch_addr[64] = {nullptr};
+std::mutex g_scratch_mu;
+
+// Device address of the scratch array on the current device (looked up once
+// per device).
+int scratch_address(void** out) {
+    int dev = 0;
+    RDB_CUDA_TRY(cudaGetDevice(&dev));
+    RDB_CHECK_ARG(dev >= 0 && dev < 64, "device ordinal %d out of range", dev);
+    std::lock_guard<std::mutex> lock(g_scratch_mu);
+    if (!g_scratch_addr[dev]) {
+        void* p = nullptr;
+        RDB_CUDA_TRY(cudaGetSymbolAddress(&p, g_noalloc_scratch));
+        g_scratch_addr[dev] = p;
+    }
+    *out = g_scratch_addr[dev];
+    return RDB_OK;
+}
+
+}  // namespace
+}  // namespace rdb
+
+using namespace rdb;
+
+extern "C" {
+
+size_t rdb_noalloc_scratch_bytes(void) { return kNoAllocScratchBytes; }
+
+int rdb_ivf_flat_scan_noalloc(int metric, int dtype, const void* q, int64_t nq, int64_t ldq, int d,
+                              const int64_t* probe, int nprobe, const void* rows, int64_t ldx, const float* xv,
+                              const int64_t* list_off, int nlist, const int64_t* ids, int k, float* out_v,
+                              int64_t* out_i, void* stream) {
+    RDB_CHECK_ARG(nq >= 0 && nprobe >= 1 && nlist >= 1, "bad shape");
+    const size_t need = rdb_ivf_scan_workspace(nq, nprobe, nlist);
+    if (need > kNoAllocScratchBytes)
+        return set_error(RDB_ERR_UNSUPPORTED,
+                         "rdb_ivf_flat_scan_noalloc: nq=%lld x nprobe=%d over nlist=%d needs %zu bytes of scratch, "
+                         "more than the %zu-byte static array; use rdb_ivf_flat_scan with a workspace or split the "
+                         "queries",
+                         (long long)nq, nprobe, nlist, need, kNoAllocScratchBytes);
+    void* scratch = nullptr;
+    RDB_TRY(scratch_address(&scratch));
+    return rdb_ivf_flat_scan(metric, dtype, q, nq, ldq, d, probe, nprobe, rows, ldx, xv, list_off, nlist, ids, k,
+                             out_v, out_i, scratch, kNoAllocScratchBytes, stream);
+}
+
+}  // extern "C"
