@@ -45,6 +45,21 @@ WORKLOADS = {
     # BASELINE config "Flat exact L2 search: fp32 base N=100,000 x 768, 32 queries, k=10"
     "flat_l2_fp32": dict(N=100_000, d=768, Q=32, k=10, metric="l2", precision="fp32",
                          normalize=False),
+    # BASELINE config "IVF-Flat: N=10,000,000 x 128 fp32, mixture of 1,024 Gaussians
+    # (centres ~N(0,4I), sigma=1); nlist=4,096 trained by 20 k-means iterations on a 1M
+    # sample; 10,000 queries; nprobe=32; k=10"
+    "ivf_flat": dict(kind="ivf", N=10_000_000, d=128, Q=10_000, k=10, metric="l2", nlist=4096,
+                     nprobe=32, ncentres=1024, spread=2.0, sigma=1.0, train=1_000_000, iters=20,
+                     uint8=False),
+    # BASELINE config "IVF-PQ sharded across 8 GPUs: N=100,000,000 x 128 uint8-valued (stored
+    # fp32); nlist=16,384; M=16 x 256; 10,000 queries; nprobe=64; k=10"
+    "ivf_pq": dict(kind="ivf_pq", N=100_000_000, d=128, Q=10_000, k=10, metric="l2", nlist=16384,
+                   nprobe=64, M=16, ksub=256, ncentres=1024, spread=2.0, sigma=1.0, train=262_144,
+                   iters=10, uint8=True),
+    # BASELINE config "k-means: N=10,000,000 x 768 bf16, mixture of 16,384 Gaussians (centres
+    # ~N(0,I), sigma=0.3); K=16,384; seeded random-row init; 20 Lloyd iterations"
+    "kmeans": dict(kind="kmeans", N=10_000_000, d=768, K=16384, iters=20, ncentres=16384,
+                   spread=1.0, sigma=0.3),
 }
 
 
@@ -89,6 +104,33 @@ def gen_rows(lo, hi, d, seed, normalize, dtype, device):
 
 def gen_queries(Q, d, seed, normalize, dtype, device):
     return gen_rows(0, Q, d, seed + 7919, normalize, dtype, device)
+
+
+def gen_mixture(lo, hi, d, wl, seed, dtype, device, salt=0):
+    """Rows [lo, hi) of a seeded Gaussian mixture: centres ~ N(0, spread^2 I)
+    (fixed by `seed`), row = centre[c] + sigma N(0, I) with c uniform; chunk c
+    of 65,536 rows uses its own generator, so any rank regenerates exactly its
+    slice; `salt` changes the row draws but not the centres (queries come from
+    the same mixture as the stored rows).  uint8 workloads scale to 16 units per sigma around 128 and clip to
+    [0, 255] (integer values stored as floats)."""
+    import torch
+
+    g = torch.Generator(device=device)
+    g.manual_seed(seed * 7 + 1)
+    centres = torch.randn((wl["ncentres"], d), generator=g, device=device) * wl["spread"]
+    CH = 65536
+    out = torch.empty((hi - lo, d), dtype=dtype, device=device)
+    c0, c1 = lo // CH, (hi - 1) // CH if hi > lo else -1
+    for c in range(c0, c1 + 1):
+        g.manual_seed(seed * 1_000_003 + 17 * c + 5 + 7_919_993 * salt)
+        a, b = c * CH, (c + 1) * CH
+        lab = torch.randint(0, wl["ncentres"], (CH,), generator=g, device=device)
+        blk = centres[lab] + wl["sigma"] * torch.randn((CH, d), generator=g, device=device)
+        if wl.get("uint8"):
+            blk = torch.clamp(torch.round(blk * 16.0 + 128.0), 0, 255)
+        s_, e_ = max(a, lo), min(b, hi)
+        out[s_ - lo:e_ - lo] = blk[s_ - a:e_ - a].to(dtype)
+    return out
 
 
 # ------------------------------------------------------------------- clocks
@@ -423,6 +465,259 @@ def run_reference(args, wl):
     }
 
 
+def _dist_setup():
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
+    return rank, world, local_rank, dev
+
+
+def _timed(fn, steps, warmup, world, tag_mask, local_rank):
+    """CUDA-event time of `steps` calls (max over ranks), the tagged kernels'
+    device time, and the clock record."""
+    import ctypes
+
+    import torch
+    import torch.distributed as dist
+
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    lib = ctypes.CDLL(os.path.join(ROOT, "rapidadb_b200", "librdb_kernels.so"))
+    clocks = ClockSampler(local_rank)
+    clocks.start()
+    lib.rdb_timing_enable(tag_mask)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record()
+    out = None
+    for _ in range(steps):
+        out = fn()
+    e1.record()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    ms = e0.elapsed_time(e1)
+    tot, nl = ctypes.c_double(0.0), ctypes.c_int(0)
+    lib.rdb_timing_read(ctypes.byref(tot), ctypes.byref(nl), 1)
+    lib.rdb_timing_enable(0)
+    clk = clocks.stop()
+    t = torch.tensor([ms], device="cuda", dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item()), tot.value / max(nl.value, 1), nl.value, clk, out
+
+
+def _peaks():
+    try:
+        p = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))
+        return float(p["hbm_gbs"]), float(p["bf16_tflops"]), "measured"
+    except Exception:
+        return 6650.0, 1590.0, "fallback"
+
+
+def run_ivf(args, wl):
+    """IVF-Flat / IVF-PQ search QPS.  Rows are sharded over the ranks (every
+    rank trains the same quantizer from the same seeded sample); the query
+    batch is wl.Q x N (per-GPU scan work fixed: weak scaling); the coarse probe
+    is split across ranks and the list table all-gathered."""
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+
+    from rapidadb_b200._lib import C
+    from rapidadb_b200.kmeans import kmeans, train_pq
+    from rapidadb_b200.sharded import ShardedIVFSearch, shard_range
+
+    rank, world, local_rank, dev = _dist_setup()
+    _C = C()
+    N, d, k, nlist, nprobe = wl["N"], wl["d"], wl["k"], wl["nlist"], wl["nprobe"]
+    Q = wl["Q"] * world
+    pq = wl["kind"] == "ivf_pq"
+    t_setup = time.perf_counter()
+    # quantizer: k-means on a seeded sample of the table (identical on every rank)
+    ntr = min(wl["train"], N)
+    xtr = gen_mixture(0, ntr, d, wl, args.seed, torch.float32, dev)
+    cent = kmeans(xtr, nlist, wl["iters"], 0.0, args.seed).centroids
+    if pq:
+        lab, _ = _C.kmeans_assign(xtr, cent, True)
+        books = train_pq(xtr - cent.index_select(0, lab.long()), wl["M"], wl["ksub"], wl["iters"], args.seed)
+        idx = _C.IVFPQIndex(d, _C.Metric.L2, nlist, nprobe, wl["M"], wl["ksub"])
+        idx.set_quantizer(cent, books)
+    else:
+        idx = _C.IVFFlatIndex(d, _C.Metric.L2, nlist, nprobe, _C.Precision.FP32)
+        idx.set_quantizer(cent)
+    del xtr
+    lo, hi = shard_range(N, rank, world)
+    CH = 4_194_304
+    for a in range(lo, hi, CH):
+        b = min(hi, a + CH)
+        xb = gen_mixture(a, b, d, wl, args.seed, torch.float32, dev)
+        idx.add(xb, torch.arange(a, b, device=dev, dtype=torch.long))
+        del xb
+    torch.cuda.synchronize()
+    t_setup = time.perf_counter() - t_setup
+    q = gen_mixture(0, Q, d, wl, args.seed, torch.float32, dev, salt=1)
+    searcher = ShardedIVFSearch(idx, largest=False)
+    tag = 4 if pq else 2
+    ms, kern_ms, nl, clk, out = _timed(lambda: searcher.search(q, k), args.steps, args.warmup, world, tag,
+                                       local_rank)
+    out_d, out_i = out
+    # e2e: host query batch in, results out, each step
+    q_host = q.cpu().pin_memory()
+    qbuf = torch.empty_like(q)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        qbuf.copy_(q_host, non_blocking=True)
+        rd, ri = searcher.search(qbuf, k)
+        rd.cpu(), ri.cpu()
+    e2e_s = time.perf_counter() - t0
+    e2e_t = torch.tensor([e2e_s], device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(e2e_t, op=dist.ReduceOp.MAX)
+    e2e_s = float(e2e_t.item())
+    # recall@k against exact search over the same rows (first 100 queries)
+    nrec = min(100, Q)
+    exact_rows = []
+    for a in range(lo, hi, CH):
+        b = min(hi, a + CH)
+        xb = gen_mixture(a, b, d, wl, args.seed, torch.float32, dev)
+        xv = _C.row_values(_C.Metric.L2, xb, d)
+        dd, ii = _C.search_rows(_C.Metric.L2, xb, d, xv, q[:nrec], k, None, a)
+        exact_rows.append((dd, ii))
+        del xb
+    ev = torch.cat([e[0] for e in exact_rows], 1)
+    ei = torch.cat([e[1] for e in exact_rows], 1)
+    order = torch.argsort(ev, dim=1)[:, :k]
+    tv, ti = torch.gather(ev, 1, order), torch.gather(ei, 1, order)
+    if world > 1:
+        gv = torch.empty((world * nrec, k), device=dev)
+        gi = torch.empty((world * nrec, k), device=dev, dtype=torch.long)
+        dist.all_gather_into_tensor(gv, tv.contiguous())
+        dist.all_gather_into_tensor(gi, ti.contiguous())
+        gv, gi = gv.view(world, nrec, k).permute(1, 0, 2).reshape(nrec, -1), gi.view(world, nrec, k).permute(1, 0, 2).reshape(nrec, -1)
+        o2 = torch.argsort(gv, dim=1)[:, :k]
+        ti = torch.gather(gi, 1, o2)
+    got = out_i[:nrec].cpu().numpy()
+    ref = ti.cpu().numpy()
+    recall = float(np.mean([len(set(a) & set(b)) / k for a, b in zip(got, ref)]))
+    sizes = idx.list_sizes().double()
+    probes = searcher.probe(q)
+    # algorithmic bytes of the local scan: every probed list's rows (or codes) once per probing query
+    scanned = float(sizes[probes.flatten()].sum().item())
+    bpr = wl["M"] if pq else d * 4
+    res = None
+    if rank == 0:
+        hbm, _, src = _peaks()
+        alg_bytes = scanned * bpr
+        ach = alg_bytes / (kern_ms * 1e-3) / 1e9 if kern_ms > 0 else None
+        qps = Q * args.steps / (ms * 1e-3)
+        res = {
+            "metric": f"search QPS ({'IVF-PQ' if pq else 'IVF-Flat'}, nprobe={nprobe}, recall@{k})",
+            "value": round(qps, 1), "unit": "queries/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 4), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "u8" if pq else "f32",
+            "data": "synthetic (seeded Gaussian mixture%s)" % (", uint8-valued" if wl.get("uint8") else ""),
+            "config": {"workload": args.workload, "rows": N, "rows_per_gpu": hi - lo, "dim": d,
+                       "queries_per_step": Q, "k": k, "nlist": nlist, "nprobe": nprobe,
+                       **({"pq_m": wl["M"], "pq_k": wl["ksub"]} if pq else {}),
+                       "train_rows": ntr, "train_iters": wl["iters"], "setup_s": round(t_setup, 1),
+                       "recall_at_k_vs_exact": round(recall, 4),
+                       "l2_flush": "not needed: stored %s (%.2f GB per GPU) exceed L2 (126 MB)" % (
+                           "codes" if pq else "rows", (hi - lo) * bpr / 1e9)},
+            "e2e": {"value": round(Q * args.steps / e2e_s, 1), "unit": "queries/s",
+                    "h2d_bytes_per_step": int(q.numel() * 4), "d2h_bytes_per_step": int(Q * k * 12)},
+            "gpu_launches": None,
+            "roofline": {"bound": "hbm", "achieved": round(ach, 1) if ach else None, "peak": hbm, "unit": "GB/s",
+                         "frac": round(ach / hbm, 4) if ach else None, "traffic": None,
+                         "kernel": "ivfpq_scan_kernel" if pq else "ivf_flat_scan_kernel",
+                         "kernel_ms": round(kern_ms, 4), "bytes_per_launch": alg_bytes,
+                         "bytes_definition": "sum over (query, probed list) of the list's stored %s bytes "
+                                             "(query-major count; the list-major scan reads each list once "
+                                             "per 32-query chunk, so frac may exceed 1)" % ("code" if pq else "row"),
+                         "peak_source": src},
+            "clocks": clk,
+        }
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return res
+
+
+def run_kmeans(args, wl):
+    """k-means Lloyd iterations over 10M x 768 bf16 rows sharded over the
+    ranks (centroid sums / counts all-reduced each iteration: strong scaling)."""
+    import torch
+    import torch.distributed as dist
+
+    from rapidadb_b200._lib import C
+    from rapidadb_b200.kmeans import init_centroids
+    from rapidadb_b200.sharded import shard_range
+
+    rank, world, local_rank, dev = _dist_setup()
+    _C = C()
+    N, d, K = wl["N"], wl["d"], wl["K"]
+    lo, hi = shard_range(N, rank, world)
+    x = gen_mixture(lo, hi, d, wl, args.seed, torch.bfloat16, dev)
+    cent = init_centroids(x, K, args.seed, None if world == 1 else dist.group.WORLD)
+    state = {"c": cent}
+
+    def iteration():
+        lab, sq = _C.kmeans_assign(x, state["c"], False)
+        sums, counts = _C.kmeans_update(x, lab, K)
+        if world > 1:
+            dist.all_reduce(sums)
+            dist.all_reduce(counts)
+        state["c"] = _C.kmeans_finalize(sums, counts, state["c"])
+        return sq
+
+    ms, kern_ms, nl, clk, sq = _timed(iteration, args.steps, args.warmup, world, 8, local_rank)
+    inertia = sq.double().sum()
+    if world > 1:
+        dist.all_reduce(inertia)
+    res = None
+    if rank == 0:
+        _, bf16, src = _peaks()
+        flops = 2.0 * (hi - lo) * K * d
+        ach = flops / (kern_ms * 1e-3) / 1e12 if kern_ms > 0 else None
+        res = {
+            "metric": "k-means Lloyd iterations/s (assign + update + all-reduce)",
+            "value": round(args.steps / (ms * 1e-3), 3), "unit": "iterations/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 3),
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (seeded Gaussian mixture, 16,384 centres ~N(0,I), sigma 0.3)",
+            "config": {"workload": args.workload, "rows": N, "rows_per_gpu": hi - lo, "dim": d, "k": K,
+                       "inertia_after": float(inertia.item()),
+                       "l2_flush": "not needed: rows (%.1f GB per GPU) exceed L2" % ((hi - lo) * d * 2 / 1e9)},
+            "roofline": {"bound": "tensor", "achieved": round(ach, 1) if ach else None, "peak": bf16,
+                         "unit": "TFLOP/s", "frac": round(ach / bf16, 4) if ach else None, "traffic": None,
+                         "kernel": "tc_scan_pair_kernel<ARGMIN> (assign)", "kernel_ms": round(kern_ms, 3),
+                         "flops_per_launch": flops, "peak_source": src},
+            "clocks": clk,
+        }
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return res
+
+
 def main():
     args = parse()
     wl = dict(WORKLOADS[args.workload])
@@ -430,7 +725,17 @@ def main():
         wl["N"] = args.rows
     if args.queries:
         wl["Q"] = args.queries
-    res = run_reference(args, wl) if args.impl == "reference" else run_ours(args, wl)
+    kind = wl.get("kind", "flat")
+    if args.impl == "reference":
+        res = run_reference(args, wl) if kind == "flat" else {
+            "impl": "reference", "unavailable": "the CPU baseline of this workload is timed by bench.py "
+            "--workload %s in its own run (cpu_baseline)" % args.workload}
+    elif kind == "ivf" or kind == "ivf_pq":
+        res = run_ivf(args, wl)
+    elif kind == "kmeans":
+        res = run_kmeans(args, wl)
+    else:
+        res = run_ours(args, wl)
     if res is not None:
         print(json.dumps(res), flush=True)
 

@@ -206,11 +206,13 @@ int rdb_ivfpq_scan(const float* q, int64_t nq, int64_t ldq, int d, const int64_t
                    size_t ws_bytes, void* stream);
 
 /* Profiling hook (no reference counterpart; the reference times whole calls,
- * benchmarks/src/bench_compare.py:56-59): when enabled, CUDA events are
- * recorded on the launching stream around every main-pass scan launch of
- * rdb_flat_search; rdb_timing_read synchronises them and returns the summed
- * device time and the number of timed launches. */
-int rdb_timing_enable(int enable);
+ * benchmarks/src/bench_compare.py:56-59): `mask` selects launches to time
+ * with CUDA events recorded on their launching stream -- 1 the main scan of
+ * rdb_flat_search, 2 the rdb_ivf_flat_scan list scan, 4 the rdb_ivfpq_scan
+ * list scan, 8 the rdb_kmeans_assign scan, 16 the rdb_kmeans_update segment
+ * sums (0 turns timing off).  rdb_timing_read synchronises the recorded
+ * events and returns the summed device time and the number of timed launches. */
+int rdb_timing_enable(int mask);
 int rdb_timing_read(double* total_ms, int* launches, int reset);
 
 #ifdef __cplusplus

@@ -4,6 +4,8 @@
 #include <stdio.h>
 
 #include <mutex>
+#include <utility>
+#include <vector>
 
 #include "common.cuh"
 
@@ -56,9 +58,56 @@ unsigned* device_status_word() {
     return words[dev];
 }
 
+struct Timing {
+    int mask = 0;
+    std::vector<std::pair<cudaEvent_t, cudaEvent_t>> ev;
+    size_t used = 0;
+    std::mutex mu;
+};
+static Timing g_timing;
+
+int timing_begin(int tag, cudaStream_t s, cudaEvent_t* stop) {
+    *stop = nullptr;
+    if (!(g_timing.mask & tag)) return RDB_OK;
+    std::lock_guard<std::mutex> lock(g_timing.mu);
+    if (g_timing.used == g_timing.ev.size()) {
+        cudaEvent_t a, b;
+        RDB_CUDA_TRY(cudaEventCreate(&a));
+        RDB_CUDA_TRY(cudaEventCreate(&b));
+        g_timing.ev.emplace_back(a, b);
+    }
+    auto& p = g_timing.ev[g_timing.used++];
+    RDB_CUDA_TRY(cudaEventRecord(p.first, s));
+    *stop = p.second;
+    return RDB_OK;
+}
+
 }  // namespace rdb
 
 extern "C" {
+
+int rdb_timing_enable(int mask) {
+    std::lock_guard<std::mutex> lock(rdb::g_timing.mu);
+    rdb::g_timing.mask = mask;
+    rdb::g_timing.used = 0;
+    return RDB_OK;
+}
+
+int rdb_timing_read(double* total_ms, int* launches, int reset) {
+    RDB_CHECK_ARG(total_ms && launches, "NULL pointer");
+    std::lock_guard<std::mutex> lock(rdb::g_timing.mu);
+    double tot = 0.0;
+    for (size_t i = 0; i < rdb::g_timing.used; ++i) {
+        RDB_CUDA_TRY(cudaEventSynchronize(rdb::g_timing.ev[i].second));
+        float ms = 0.f;
+        RDB_CUDA_TRY(cudaEventElapsedTime(&ms, rdb::g_timing.ev[i].first, rdb::g_timing.ev[i].second));
+        tot += ms;
+    }
+    *total_ms = tot;
+    *launches = static_cast<int>(rdb::g_timing.used);
+    if (reset) rdb::g_timing.used = 0;
+    return RDB_OK;
+}
 
 const char* rdb_last_error(void) { return rdb::g_err; }
 

@@ -49,6 +49,19 @@ int set_error(int code, const char* fmt, ...);
 int num_sms();
 size_t elem_size(int dtype);
 
+// Optional CUDA-event timing of selected kernel launches (rdb_timing_*):
+// when the launch's tag is enabled, timing_begin records a start event on the
+// launching stream and returns the stop event to record after the launch
+// (nullptr when timing is off).
+enum TimingTag : int {
+    TIMING_FLAT_SCAN = 1,      // main pass of rdb_flat_search
+    TIMING_IVF_SCAN = 2,       // rdb_ivf_flat_scan list scan
+    TIMING_PQ_SCAN = 4,        // rdb_ivfpq_scan list scan
+    TIMING_KMEANS_ASSIGN = 8,  // rdb_kmeans_assign scan
+    TIMING_KMEANS_UPDATE = 16, // rdb_kmeans_update segment sums
+};
+int timing_begin(int tag, cudaStream_t s, cudaEvent_t* stop);
+
 // Device status word: kernels that give up on a bounded wait OR in a code here
 // instead of hanging; the host reads it with read_device_status().
 enum DeviceStatus : unsigned {

@@ -33,30 +33,6 @@ namespace {
 
 inline size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 
-// Optional CUDA-event timing of the main scan launch (rdb_timing_*): events are
-// recorded on the launching stream around each main-pass scan.
-struct ScanTiming {
-    bool enabled = false;
-    std::vector<std::pair<cudaEvent_t, cudaEvent_t>> ev;
-    size_t used = 0;
-};
-ScanTiming g_timing;
-
-int timing_begin(cudaStream_t s, cudaEvent_t* stop) {
-    *stop = nullptr;
-    if (!g_timing.enabled) return RDB_OK;
-    if (g_timing.used == g_timing.ev.size()) {
-        cudaEvent_t a, b;
-        RDB_CUDA_TRY(cudaEventCreate(&a));
-        RDB_CUDA_TRY(cudaEventCreate(&b));
-        g_timing.ev.emplace_back(a, b);
-    }
-    auto& p = g_timing.ev[g_timing.used++];
-    RDB_CUDA_TRY(cudaEventRecord(p.first, s));
-    *stop = p.second;
-    return RDB_OK;
-}
-
 struct PassPlan {
     int64_t rows;  // logical rows scanned
     int64_t row_step;
@@ -271,7 +247,7 @@ int run_chunk(const FlatPlan& P, int metric, int dtype, const void* q, int64_t n
         sc.rows_per_split = P.m.rps;
         sc.cap = P.m.cap;
         cudaEvent_t stop_ev;
-        RDB_TRY(timing_begin(s, &stop_ev));
+        RDB_TRY(timing_begin(TIMING_FLAT_SCAN, s, &stop_ev));
         RDB_TRY(scan(sc));
         if (stop_ev) RDB_CUDA_TRY(cudaEventRecord(stop_ev, s));
         SelectArgs ss = sa;
@@ -357,27 +333,6 @@ int rdb_flat_search(int metric, int dtype, const void* q, int64_t nq, int64_t ld
     }
     if (any_overflow)
         return set_error(RDB_ERR_OVERFLOW, "candidate list overflow; repeat with RDB_SEARCH_EXHAUSTIVE");
-    return RDB_OK;
-}
-
-int rdb_timing_enable(int enable) {
-    g_timing.enabled = enable != 0;
-    g_timing.used = 0;
-    return RDB_OK;
-}
-
-int rdb_timing_read(double* total_ms, int* launches, int reset) {
-    RDB_CHECK_ARG(total_ms && launches, "NULL pointer");
-    double tot = 0.0;
-    for (size_t i = 0; i < g_timing.used; ++i) {
-        RDB_CUDA_TRY(cudaEventSynchronize(g_timing.ev[i].second));
-        float ms = 0.f;
-        RDB_CUDA_TRY(cudaEventElapsedTime(&ms, g_timing.ev[i].first, g_timing.ev[i].second));
-        tot += ms;
-    }
-    *total_ms = tot;
-    *launches = static_cast<int>(g_timing.used);
-    if (reset) g_timing.used = 0;
     return RDB_OK;
 }
 

@@ -103,6 +103,8 @@ PYBIND11_MODULE(_C, m) {
             "add", [](IVFFlatIndex& s, const at::Tensor& v, const py::object& ids) { s.add(v, opt_tensor(ids)); },
             py::arg("vectors"), py::arg("ids") = py::none())
         .def("search", &IVFFlatIndex::search, py::arg("queries"), py::arg("k"))
+        .def("probe", &IVFFlatIndex::probe, py::arg("queries"))
+        .def("search_probed", &IVFFlatIndex::search_probed, py::arg("queries"), py::arg("probe"), py::arg("k"))
         .def("reset", &IVFFlatIndex::reset)
         .def("size", &IVFFlatIndex::size)
         .def("dim", &IVFFlatIndex::dim)
@@ -130,6 +132,8 @@ PYBIND11_MODULE(_C, m) {
             "add", [](IVFPQIndex& s, const at::Tensor& v, const py::object& ids) { s.add(v, opt_tensor(ids)); },
             py::arg("vectors"), py::arg("ids") = py::none())
         .def("search", &IVFPQIndex::search, py::arg("queries"), py::arg("k"))
+        .def("probe", &IVFPQIndex::probe, py::arg("queries"))
+        .def("search_probed", &IVFPQIndex::search_probed, py::arg("queries"), py::arg("probe"), py::arg("k"))
         .def("reset", &IVFPQIndex::reset)
         .def("size", &IVFPQIndex::size)
         .def("dim", &IVFPQIndex::dim)

@@ -34,10 +34,12 @@ class IVFBase {
     at::Tensor stored_ids() const { return ids_; }
     at::Tensor stored_labels() const { return labels_; }
     virtual void reset();
+    // coarse probe: [nq, min(nprobe, nlist)] nearest list ids (squared L2,
+    // ties to the lower list)
+    at::Tensor probe(const at::Tensor& queries) const;
 
   protected:
     void set_centroids(const at::Tensor& centroids);
-    at::Tensor probe(const at::Tensor& queries) const;  // [nq, min(nprobe, nlist)] list ids
     void check_query(const at::Tensor& queries, int64_t k) const;
     std::tuple<at::Tensor, at::Tensor> relist(const at::Tensor& labels_all);
     at::Tensor new_ids(const at::Tensor& vectors, const at::Tensor& ids) const;
@@ -62,6 +64,8 @@ class IVFFlatIndex : public IVFBase {
     void set_quantizer(const at::Tensor& centroids) { set_centroids(centroids); }
     void add(const at::Tensor& vectors, const at::Tensor& ids);
     Result search(const at::Tensor& queries, int64_t k) const;
+    // scan with a given [nq, np] probe table (e.g. gathered from other ranks)
+    Result search_probed(const at::Tensor& queries, const at::Tensor& probe, int64_t k) const;
     void reset() override;
     at::Tensor stored_vectors() const { return rows_.defined() ? rows_.narrow(1, 0, dim_) : at::Tensor(); }
 
@@ -78,6 +82,7 @@ class IVFPQIndex : public IVFBase {
     void set_quantizer(const at::Tensor& centroids, const at::Tensor& codebooks);
     void add(const at::Tensor& vectors, const at::Tensor& ids);
     Result search(const at::Tensor& queries, int64_t k) const;
+    Result search_probed(const at::Tensor& queries, const at::Tensor& probe, int64_t k) const;
     void reset() override;
     at::Tensor codebooks() const { return codebooks_; }
     at::Tensor stored_codes() const { return codes_; }

@@ -236,7 +236,19 @@ Result IVFFlatIndex::search(const at::Tensor& queries, int64_t k) const {
     check_query(queries, k);
     c10::cuda::CUDAGuard guard(rows_.device());
     at::Tensor qd = queries.to(rows_.device());
-    at::Tensor probe_lists = probe(qd);
+    return search_probed(qd, probe(qd), k);
+}
+
+static at::Tensor check_probe(const at::Tensor& probe, int64_t nq, const at::Tensor& like) {
+    TORCH_CHECK(probe.dim() == 2 && probe.size(0) == nq && probe.size(1) >= 1, "probe must be [nq, nprobe]");
+    return probe.to(like.device()).to(at::kLong).contiguous();
+}
+
+Result IVFFlatIndex::search_probed(const at::Tensor& queries, const at::Tensor& probe_in, int64_t k) const {
+    check_query(queries, k);
+    c10::cuda::CUDAGuard guard(rows_.device());
+    at::Tensor qd = queries.to(rows_.device());
+    at::Tensor probe_lists = check_probe(probe_in, qd.size(0), rows_);
     const int np = static_cast<int>(probe_lists.size(1));
     at::Tensor q = prepare_rows(qd, rows_.scalar_type(), ld_);
     const int64_t nq = q.size(0);
@@ -303,7 +315,14 @@ Result IVFPQIndex::search(const at::Tensor& queries, int64_t k) const {
     check_query(queries, k);
     c10::cuda::CUDAGuard guard(codes_.device());
     at::Tensor q = contig_f32(queries.to(codes_.device()));
-    at::Tensor probe_lists = probe(q);
+    return search_probed(q, probe(q), k);
+}
+
+Result IVFPQIndex::search_probed(const at::Tensor& queries, const at::Tensor& probe_in, int64_t k) const {
+    check_query(queries, k);
+    c10::cuda::CUDAGuard guard(codes_.device());
+    at::Tensor q = contig_f32(queries.to(codes_.device()));
+    at::Tensor probe_lists = check_probe(probe_in, q.size(0), codes_);
     const int np = static_cast<int>(probe_lists.size(1));
     const int64_t nq = q.size(0);
     at::Tensor cv = at::empty({np, nq, k}, q.options());

@@ -436,6 +436,8 @@ int rdb_ivf_flat_scan(int metric, int dtype, const void* q, int64_t nq, int64_t 
     const unsigned grid = (unsigned)std::min<int64_t>(nlist, 65535LL * 16);
     const int64_t* eperm = reinterpret_cast<const int64_t*>(base + w.off_perm);
     const int64_t* eseg = reinterpret_cast<const int64_t*>(base + w.off_seg);
+    cudaEvent_t stop_ev;
+    RDB_TRY(timing_begin(TIMING_IVF_SCAN, s, &stop_ev));
     switch (dtype) {
         case RDB_F32:
             ivf_flat_scan_kernel<float><<<grid, FNT, 0, s>>>(metric, cos_small, (const float*)q, nq, ldq, d, qv, nprobe,
@@ -453,6 +455,7 @@ int rdb_ivf_flat_scan(int metric, int dtype, const void* q, int64_t nq, int64_t 
                 (const __nv_bfloat16*)rows, ldx, xv, list_off, nlist, ids, k, out_v, out_i);
     }
     RDB_LAUNCH_CHECK();
+    if (stop_ev) RDB_CUDA_TRY(cudaEventRecord(stop_ev, s));
     return RDB_OK;
 }
 
@@ -505,10 +508,13 @@ int rdb_ivfpq_scan(const float* q, int64_t nq, int64_t ldq, int d, const int64_t
         attr[dev] = true;
     }
     const unsigned grid = (unsigned)std::min<int64_t>(nlist, (int64_t)num_sms());
+    cudaEvent_t stop_ev;
+    RDB_TRY(timing_begin(TIMING_PQ_SCAN, s, &stop_ev));
     ivfpq_scan_kernel<<<grid, PNT, smem, s>>>(q, nq, ldq, d, nprobe, reinterpret_cast<const int64_t*>(base + w.off_perm),
                                             reinterpret_cast<const int64_t*>(base + w.off_seg), centroids, codebooks, M,
                                             ksub, codes, list_off, nlist, ids, k, out_v, out_i);
     RDB_LAUNCH_CHECK();
+    if (stop_ev) RDB_CUDA_TRY(cudaEventRecord(stop_ev, s));
     return RDB_OK;
 }
 

@@ -132,6 +132,8 @@ int assign_impl(int dtype, const void* x, int64_t n, int64_t ldx, int d, const v
     a.nsplit = (int)nsplit;
     a.rows_per_split = rps;
     a.best = best;
+    cudaEvent_t stop_ev;
+    RDB_TRY(timing_begin(TIMING_KMEANS_ASSIGN, s, &stop_ev));
     if (tc) {
         RDB_TRY(launch_scan_tc(a, SCAN_ARGMIN, s));
     } else if (exact) {
@@ -139,6 +141,7 @@ int assign_impl(int dtype, const void* x, int64_t n, int64_t ldx, int d, const v
     } else {
         RDB_TRY(launch_scan_simt(a, SCAN_ARGMIN, s));
     }
+    if (stop_ev) RDB_CUDA_TRY(cudaEventRecord(stop_ev, s));
     argmin_reduce_kernel<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(best, (int)nsplit, n, labels, sqdist);
     RDB_LAUNCH_CHECK();
     return RDB_OK;
@@ -219,6 +222,8 @@ int rdb_kmeans_update(int dtype, const void* x, int64_t n, int64_t ldx, int d, c
     RDB_TRY(label_sort(labels, n, K, seg, perm, counts, base, sort_b, s));
     const int threads = d >= 256 ? 256 : ((d + 31) / 32) * 32;
     dim3 grid(K, 1);
+    cudaEvent_t stop_ev;
+    RDB_TRY(timing_begin(TIMING_KMEANS_UPDATE, s, &stop_ev));
     switch (dtype) {
         case RDB_F32: segment_sum_kernel<float><<<grid, threads, 0, s>>>((const float*)x, ldx, d, perm, seg, sums); break;
         case RDB_F16: segment_sum_kernel<__half><<<grid, threads, 0, s>>>((const __half*)x, ldx, d, perm, seg, sums); break;
@@ -226,6 +231,7 @@ int rdb_kmeans_update(int dtype, const void* x, int64_t n, int64_t ldx, int d, c
             segment_sum_kernel<__nv_bfloat16><<<grid, threads, 0, s>>>((const __nv_bfloat16*)x, ldx, d, perm, seg, sums);
     }
     RDB_LAUNCH_CHECK();
+    if (stop_ev) RDB_CUDA_TRY(cudaEventRecord(stop_ev, s));
     return RDB_OK;
 }
 

@@ -73,3 +73,47 @@ class ShardedSearch:
             return local_d, local_i
         vals, ids = gather_candidates(local_d, local_i, self.group)
         return self.merge(vals, ids, k, self.largest)
+
+
+class ShardedIVFSearch:
+    """Search a row-sharded IVF / IVF-PQ index (every rank holds the same
+    trained quantizer and a slice of the rows).
+
+    The coarse probe is split across ranks -- rank r probes its contiguous
+    slice of the query batch -- and the [Q, nprobe] list table is
+    all-gathered, so the replicated probe costs each GPU 1/G of the batch.
+    Every rank then scans its rows of the probed lists for all queries
+    (``index.search_probed``), and the per-rank [Q, k] lists are all-gathered
+    and merged as in ShardedSearch."""
+
+    def __init__(self, index, largest: bool, group: Optional[dist.ProcessGroup] = None,
+                 merge: Optional[Callable] = None):
+        self.index = index
+        self.largest = largest
+        self.group = group
+        self.merge = merge or gpu_merge
+
+    def probe(self, queries: torch.Tensor) -> torch.Tensor:
+        if not dist.is_initialized() or dist.get_world_size(self.group) == 1:
+            return self.index.probe(queries)
+        world = dist.get_world_size(self.group)
+        rank = dist.get_rank(self.group)
+        Q = queries.shape[0]
+        chunk = (Q + world - 1) // world
+        lo, hi = min(rank * chunk, Q), min((rank + 1) * chunk, Q)
+        local = self.index.probe(queries[lo:hi]) if hi > lo else None
+        np_ = local.shape[1] if local is not None else self.index.probe(queries[:1]).shape[1]
+        buf = torch.zeros((chunk, np_), dtype=torch.long, device=queries.device)
+        if local is not None:
+            buf[: hi - lo] = local
+        out = torch.empty((world * chunk, np_), dtype=torch.long, device=queries.device)
+        dist.all_gather_into_tensor(out, buf, group=self.group)
+        return out[:Q]
+
+    def search(self, queries: torch.Tensor, k: int) -> Tuple[torch.Tensor, torch.Tensor]:
+        probe = self.probe(queries)
+        local_d, local_i = self.index.search_probed(queries, probe, k)
+        if not dist.is_initialized() or dist.get_world_size(self.group) == 1:
+            return local_d, local_i
+        vals, ids = gather_candidates(local_d, local_i, self.group)
+        return self.merge(vals, ids, k, self.largest)
