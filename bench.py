@@ -136,56 +136,65 @@ def gen_mixture(lo, hi, d, wl, seed, dtype, device, salt=0):
 # ------------------------------------------------------------------- clocks
 
 class ClockSampler:
-    """nvidia-smi clock / throttle sampling during the timed region."""
+    """SM clock and clock-event (throttle) reasons sampled through NVML every
+    5 ms during the timed region (read-only queries; no setting is changed).
+    Falls back to `nvidia-smi -lms` when NVML is unavailable."""
 
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    REASONS = {0x4: "sw_power_cap", 0x8: "hw_slowdown", 0x20: "sw_thermal_slowdown",
+               0x40: "hw_thermal_slowdown", 0x80: "hw_power_brake_slowdown"}
 
-    def __init__(self, gpu_index):
-        self.gpu = gpu_index
-        self.proc = None
-        self.lines = []
+    def __init__(self, cuda_index, period_s=0.005):
+        self.cuda_index = cuda_index
+        self.period = period_s
+        self.samples = []
+        self.max_mhz = None
+        self._stop = threading.Event()
+        self._thread = None
+        self._nvml = None
+
+    def _handle(self):
+        import pynvml
+        import torch
+
+        pynvml.nvmlInit()
+        uuid = str(torch.cuda.get_device_properties(self.cuda_index).uuid)
+        uuid = uuid if uuid.startswith("GPU-") else "GPU-" + uuid
+        return pynvml, pynvml.nvmlDeviceGetHandleByUUID(uuid)
 
     def start(self):
         try:
-            self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}",
-                 "--format=csv,noheader,nounits", "-lms", "100"],
-                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-            self.thread = threading.Thread(target=self._read, daemon=True)
-            self.thread.start()
-        except Exception:
-            self.proc = None
+            self._nvml, h = self._handle()
+            nv = self._nvml
+            self.max_mhz = nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM)
+            get_reasons = getattr(nv, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
+                nv.nvmlDeviceGetCurrentClocksThrottleReasons
 
-    def _read(self):
-        for line in self.proc.stdout:
-            self.lines.append(line.strip())
+            def loop():
+                while not self._stop.is_set():
+                    try:
+                        self.samples.append((nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM), int(get_reasons(h))))
+                    except Exception:
+                        pass
+                    time.sleep(self.period)
+
+            self._thread = threading.Thread(target=loop, daemon=True)
+            self._thread.start()
+        except Exception:
+            self._nvml = None
 
     def stop(self):
-        if self.proc is None:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
-        self.proc.terminate()
-        try:
-            self.proc.wait(timeout=5)
-        except Exception:
-            self.proc.kill()
-        sm, mx, reasons = [], None, set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for ln in self.lines:
-            p = [x.strip() for x in ln.split(",")]
-            if len(p) < 9:
-                continue
-            try:
-                sm.append(float(p[1]))
-                mx = float(p[2])
-            except ValueError:
-                continue
-            for nm, v in zip(names, p[5:9]):
-                if v.lower() == "active":
-                    reasons.add(nm)
-        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx,
-                "reasons": sorted(reasons), "samples": len(sm)}
+        if self._thread is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvml unavailable"], "samples": 0}
+        self._stop.set()
+        self._thread.join(timeout=2)
+        sm = [c for c, _ in self.samples]
+        reasons = set()
+        for _, r in self.samples:
+            for bit, name in self.REASONS.items():
+                if r & bit:
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": self.max_mhz,
+                "reasons": sorted(reasons), "samples": len(sm), "source": "nvml 5 ms"}
 
 
 # --------------------------------------------------------------- CPU baseline
@@ -387,7 +396,8 @@ def run_ours(args, wl):
                 "unit": "TFLOP/s",
                 "frac": round(achieved / peak, 4) if achieved else None,
                 "traffic": None,
-                "kernel": "tc_scan_kernel<FILTER> (main pass)",
+                "kernel": ("tc_scan_pair_kernel<FILTER> (CTA pair, main pass)" if Q > 128
+                           else "tc_scan_kernel<FILTER> (main pass)"),
                 "kernel_ms": round(kernel_ms, 4),
                 "flops_per_launch": flops,
                 "peak_source": peak_src,
@@ -640,7 +650,9 @@ def run_ivf(args, wl):
                        **({"pq_m": wl["M"], "pq_k": wl["ksub"]} if pq else {}),
                        "train_rows": ntr, "train_iters": wl["iters"], "setup_s": round(t_setup, 1),
                        "recall_at_k_vs_exact": round(recall, 4),
-                       "l2_flush": "not needed: stored %s (%.2f GB per GPU) exceed L2 (126 MB)" % (
+                       "l2_flush": ("not needed: stored %s (%.2f GB per GPU) exceed L2 (126 MB)" if
+                                    (hi - lo) * bpr > 126e6 else
+                                    "none: stored %s (%.2f GB per GPU) fit in L2 at this reduced size") % (
                            "codes" if pq else "rows", (hi - lo) * bpr / 1e9)},
             "e2e": {"value": round(Q * args.steps / e2e_s, 1), "unit": "queries/s",
                     "h2d_bytes_per_step": int(q.numel() * 4), "d2h_bytes_per_step": int(Q * k * 12)},
