@@ -85,11 +85,16 @@ FlatPlan make_plan(int metric, int dtype, int64_t nq, int64_t n, int d, int k, i
     const int sms = num_sms();
     const int64_t target = P.tc ? (pair ? sms / 2 : sms) : 2LL * sms;
 
-    // sample size: ~1.5 sqrt(n k) rows (balances sample cost against the
-    // candidate volume n k / S), a power of two in [1024, 32768], >= 8 k
-    double sd = 1.5 * sqrt((double)n * (double)k);
+    // sample size S, a power of two >= 8 k: the sample pass costs S / n of the
+    // main scan, the candidates (about n k / S per query) cost the main scan's
+    // epilogue and the select.  The tensor-core sample pass keeps group maxima
+    // and its candidates are costly relative to its cheap per-row MMA work:
+    // ~6 sqrt(n k) rows in [1024, 131072]; the CUDA-core sample pass emits
+    // every sampled score as a candidate: ~1.5 sqrt(n k) in [1024, 32768].
+    const double sd = (P.tc ? 6.0 : 1.5) * sqrt((double)n * (double)k);
+    const int64_t smax = P.tc ? 131072 : 32768;
     int64_t S = 1024;
-    while (S < sd && S < 32768) S <<= 1;
+    while (S < sd && S < smax) S <<= 1;
     while (S < 8LL * k) S <<= 1;
     P.sample = !(flags & RDB_SEARCH_EXHAUSTIVE) && n >= 4 * S;
     if (P.sample) {
@@ -98,9 +103,10 @@ FlatPlan make_plan(int metric, int dtype, int64_t nq, int64_t n, int d, int k, i
         // tensor-core sample pass keeps the best score of each group of
         // `group` sample rows; the k-th best of those group maxima is still a
         // lower bound on the k-th best score (k distinct rows reach it), and
-        // with >= 4 k groups it is nearly as tight as the k-th best row
+        // with >= 10 k groups it is nearly as tight as the k-th best row
+        // (pass rate 1 - (1 - k / G)^(1 / group) against k / S)
         P.group = 1;
-        while (P.group < 16 && S / (2 * P.group) >= 4LL * k) P.group <<= 1;
+        while (P.group < 128 && S / (2 * P.group) >= 10LL * k) P.group <<= 1;
         P.ngroups = S / P.group;
     }
     P.m = plan_pass(n, 1, nq, P.qtile, P.rtile, target);

@@ -10,12 +10,13 @@
 //               one lane (of the leader CTA) issues tcgen05.mma kind::f16
 //               (K = 16 per instruction) and commits stage releases /
 //               accumulator-ready barriers.
-//   warps 2..5  epilogue: each thread owns one query row (one TMEM lane),
+//   warps 2..9  epilogue, two warps per TMEM lane quadrant: each thread owns
+//               one query row (one TMEM lane) and half of the tile's columns,
 //               reads 32 accumulator columns per tcgen05.ld and keeps only the
 //               rows whose dot product passes the query's threshold
 //               (dot >= A * xv[row] + B, see filter_coef), appending
-//               (dot, row) to the query's private candidate list.  Nothing
-//               else of the [queries, rows] score tile leaves the SM.
+//               (score, row) to the query's candidate list.  Nothing else of
+//               the [queries, rows] score tile leaves the SM.
 // While the epilogue drains one accumulator the MMA fills the other.
 //
 // Every mbarrier wait is bounded (kWaitLimitNs): a role that gives up sets the
@@ -35,12 +36,13 @@ constexpr int BK = 64;
 constexpr int UK = 16;
 constexpr int NUM_ACC = 2;
 constexpr int TMEM_COLS = 512;
-constexpr int NUM_THREADS = 192;
+constexpr int EPI_WARPS = 8;  // two per TMEM lane quadrant
+constexpr int EPI_THREADS = EPI_WARPS * 32;
+constexpr int NUM_THREADS = 64 + EPI_THREADS;
 constexpr int BAR_BYTES = 256;
-constexpr int EPI_THREADS = 128;
-constexpr int kStageStride = 36;  // floats per staged chunk row (32 + pad, 16-byte aligned)
 constexpr int XV_BYTES = 2 * BN * 4;
-constexpr int STAGE_ROWS_BYTES = EPI_THREADS * kStageStride * 4;
+constexpr int EPI_SHARED_BYTES = 2 * BM * 4;  // per-query candidate counters / arg-best hand-over
+static_assert(EPI_THREADS == BN, "one epilogue thread per row of a tile (row values)");
 
 static_assert(NUM_ACC * BN <= TMEM_COLS, "accumulators exceed TMEM allocation");
 
@@ -62,10 +64,6 @@ __device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t by
     asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)),
                  "r"(bytes)
                  : "memory");
-}
-
-__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
-    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
 
 __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
@@ -94,7 +92,7 @@ __device__ __noinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile 
     }
 }
 
-// Named barrier among the four epilogue warps (id 1; id 0 is __syncthreads).
+// Named barrier among the epilogue warps (id 1; id 0 is __syncthreads).
 __device__ __forceinline__ void epi_bar_sync() {
     asm volatile("bar.sync 1, %0;" ::"n"(EPI_THREADS) : "memory");
 }
@@ -127,21 +125,6 @@ __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }
 
-__device__ __forceinline__ void tmem_alloc(uint32_t* dst, uint32_t ncols) {
-    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(dst)),
-                 "r"(ncols)
-                 : "memory");
-}
-
-__device__ __forceinline__ void tmem_relinquish() {
-    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
-}
-
-__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols)
-                 : "memory");
-}
-
 __device__ __forceinline__ void tc_fence_before() {
     asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
 }
@@ -167,8 +150,9 @@ __device__ __forceinline__ void umma_commit(uint64_t* bar) {
         : "memory");
 }
 
-__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
-    uint32_t r[32];
+// Asynchronous form: the registers are valid only after tmem_ld_wait(r),
+// which names them as in/out operands so no use can move above the wait.
+__device__ __forceinline__ void tmem_ld32_async(uint32_t taddr, uint32_t (&r)[32]) {
     asm volatile(
         "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
         "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
@@ -180,9 +164,32 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
           "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]),
           "=r"(r[31])
         : "r"(taddr));
-    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ void tmem_ld_wait(uint32_t (&r)[32]) {
+    asm volatile("tcgen05.wait::ld.sync.aligned;"
+                 : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]),
+                   "+r"(r[7]), "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]),
+                   "+r"(r[14]), "+r"(r[15]), "+r"(r[16]), "+r"(r[17]), "+r"(r[18]), "+r"(r[19]), "+r"(r[20]),
+                   "+r"(r[21]), "+r"(r[22]), "+r"(r[23]), "+r"(r[24]), "+r"(r[25]), "+r"(r[26]), "+r"(r[27]),
+                   "+r"(r[28]), "+r"(r[29]), "+r"(r[30]), "+r"(r[31])
+                 :
+                 : "memory");
+}
+
+// v[j] for a run-time j without spilling v to local memory: a 5-level select
+// network on the bits of j (31 selects).
+__device__ __forceinline__ float pick32(const float (&v)[32], int j) {
+    float t16[16], t8[8], t4[4], t2[2];
 #pragma unroll
-    for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+    for (int i = 0; i < 16; ++i) t16[i] = (j & 16) ? v[i + 16] : v[i];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) t8[i] = (j & 8) ? t16[i + 8] : t16[i];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) t4[i] = (j & 4) ? t8[i + 4] : t8[i];
+#pragma unroll
+    for (int i = 0; i < 2; ++i) t2[i] = (j & 2) ? t4[i + 2] : t4[i];
+    return (j & 1) ? t2[1] : t2[0];
 }
 
 // Shared-memory matrix descriptor: K-major, SWIZZLE_128B, 8-row core groups
@@ -229,7 +236,7 @@ struct TcCfg {
     static constexpr int STAGE_B = A_B + B_B;
     static constexpr int NSTAGE = PAIR ? 6 : 4;
     static constexpr int UMMA_M = PAIR ? 2 * BM : BM;
-    static constexpr int SMEM = NSTAGE * STAGE_B + 1024 + BAR_BYTES + XV_BYTES + STAGE_ROWS_BYTES;
+    static constexpr int SMEM = NSTAGE * STAGE_B + 1024 + BAR_BYTES + XV_BYTES + EPI_SHARED_BYTES;
 };
 static_assert(TcCfg<false>::SMEM <= 232448 && TcCfg<true>::SMEM <= 232448, "shared memory over 227 KB");
 
@@ -331,7 +338,8 @@ __device__ __forceinline__ void tc_scan_body(uint8_t* smem_raw, const CUtensorMa
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done + 1);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
     float* xv_s = reinterpret_cast<float*>(smem + NST * Cfg::STAGE_B + BAR_BYTES);
-    float* stage_rows = xv_s + 2 * BN;
+    uint32_t* cnt_s = reinterpret_cast<uint32_t*>(xv_s + 2 * BN);  // [BM]
+    float* best_s = reinterpret_cast<float*>(cnt_s + BM);            // [BM]
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const uint32_t rank = PAIR ? cluster_rank() : 0u;
@@ -350,7 +358,7 @@ __device__ __forceinline__ void tc_scan_body(uint8_t* smem_raw, const CUtensorMa
         }
         for (int c = 0; c < NUM_ACC; ++c) {
             mbar_init(&tfull[c], 1);
-            mbar_init(&tempty[c], PAIR ? 8 : 4);
+            mbar_init(&tempty[c], PAIR ? 2 * EPI_WARPS : EPI_WARPS);
         }
         mbar_init(mma_done, 1);
         *abort_flag = 0;
@@ -489,14 +497,18 @@ __device__ __forceinline__ void tc_scan_body(uint8_t* smem_raw, const CUtensorMa
         }
     } else {
         // -------------------------------------------------- epilogue
-        // Thread = one query row = one TMEM lane.  Per tile the 256 per-row
-        // values xv[] sit in shared memory (loaded one tile ahead by these
-        // 128 threads); per 32-column chunk the pass test is branch-free
-        // (one FFMA + FSETP + predicated OR per column), and only lanes with a
-        // hit stage their chunk in shared memory to append it.
-        const int ew = warp - 2;          // 0..3
+        // Eight warps, two per TMEM lane quadrant: thread = one query row =
+        // one TMEM lane; warp half h drains columns [128 h, 128 h + 128) of
+        // each 256-row tile.  Per tile the 256 per-row values xv[] sit in
+        // shared memory (loaded one tile ahead, one row per thread); per
+        // 32-column chunk the pass test is branch-free (FFMA + FSETP + OR per
+        // column, four independent OR chains), and a lane with hits reserves
+        // slots in its query's list with one shared-memory atomic and picks
+        // each hit out of its registers with a select network.
+        const int ew = warp - 2;          // 0..7
         const int quad = warp & 3;        // TMEM lanes this warp may read
-        const int etid = ew * 32 + lane;  // 0..127
+        const int half = ew >> 2;         // which 128 columns of each tile
+        const int etid = ew * 32 + lane;  // 0..255
         const int qrow = quad * 32 + lane;
         const int64_t q = q0 + qrow;
         const bool qvalid = q < a.nq;
@@ -510,29 +522,25 @@ __device__ __forceinline__ void tc_scan_body(uint8_t* smem_raw, const CUtensorMa
         uint2* cbase = (MODE == SCAN_FILTER && qvalid)
                            ? a.cand + (static_cast<int64_t>(split) * a.nq + q) * a.cap
                            : nullptr;
-        float* stg = stage_rows + (ew * 32 + lane) * kStageStride;
-        int64_t cnt = 0;
+        const uint32_t cap = static_cast<uint32_t>(min(a.cap, static_cast<int64_t>(0xffffffffu)));
+        if (MODE == SCAN_FILTER && half == 0) cnt_s[qrow] = 0u;
         float best = -INFINITY;
         uint32_t best_r = 0;
+        float gb = -INFINITY;  // running group maximum (groups of 64 / 128 rows)
         const float* __restrict__ xvp = a.xv;
         const int64_t step = a.row_step;
-        // per-row values of tile t -> xv_s[t & 1]; each thread covers 2 rows
-        auto load_xv = [&](int t, float2& out) {
-            const int64_t r = r_begin + static_cast<int64_t>(t) * BN + 2 * etid;
-            out.x = (xvp && r < r_end) ? __ldg(xvp + r * step) : 0.f;
-            out.y = (xvp && r + 1 < r_end) ? __ldg(xvp + (r + 1) * step) : 0.f;
+        auto load_xv = [&](int t) -> float {
+            const int64_t r = r_begin + static_cast<int64_t>(t) * BN + etid;
+            return (xvp && r < r_end) ? __ldg(xvp + r * step) : 0.f;
         };
-        float2 xv_next = make_float2(0.f, 0.f);
-        if (ntiles > 0) {
-            load_xv(0, xv_next);
-            reinterpret_cast<float2*>(xv_s)[etid] = xv_next;
-        }
+        float xv_next = 0.f;
+        if (ntiles > 0) xv_s[etid] = load_xv(0);
         epi_bar_sync();
         for (int t = 0; t < ntiles; ++t) {
             const int acc = t & 1;
             const uint32_t acc_phase = (t >> 1) & 1;
-            if (t + 1 < ntiles) load_xv(t + 1, xv_next);
-            // all four epilogue warps leave together if any wait gave up
+            if (t + 1 < ntiles) xv_next = load_xv(t + 1);
+            // all eight epilogue warps leave together if any wait gave up
             if (!epi_bar_and(mbar_wait(&tfull[acc], acc_phase, abort_flag))) {
                 *abort_flag = 1;
                 if (status) atomicOr(status, DEV_TIMEOUT_EPILOGUE);
@@ -541,43 +549,41 @@ __device__ __forceinline__ void tc_scan_body(uint8_t* smem_raw, const CUtensorMa
             tc_fence_after();
             const int64_t row0 = r_begin + static_cast<int64_t>(t) * BN;
             const float* xs_tile = xv_s + acc * BN;
-#pragma unroll 1
-            for (int c = 0; c < BN / 32; ++c) {
+            // 32-column chunk c (0..7 within the tile) of this tile: the
+            // accumulator values are in r
+            auto process_chunk = [&](const uint32_t (&r)[32], const int c) {
                 float v[32];
-                tmem_ld32(tmem_base + (static_cast<uint32_t>(quad * 32) << 16) +
-                              static_cast<uint32_t>(acc * BN + c * 32),
-                          v);
+#pragma unroll
+                for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
                 const int64_t col0 = row0 + c * 32;
                 const int64_t nv64 = r_end - col0;
                 const uint32_t valid = nv64 >= 32 ? 0xffffffffu : (nv64 > 0 ? ((1u << nv64) - 1u) : 0u);
                 const float4* xs4 = reinterpret_cast<const float4*>(xs_tile + c * 32);
                 if (MODE == SCAN_FILTER) {
-                    uint32_t m = 0;
+                    uint32_t m0 = 0, m1 = 0, m2 = 0, m3 = 0;
 #pragma unroll
                     for (int j4 = 0; j4 < 8; ++j4) {
                         const float4 x4 = xs4[j4];
-                        const float xx[4] = {x4.x, x4.y, x4.z, x4.w};
-#pragma unroll
-                        for (int u = 0; u < 4; ++u) {
-                            const int j = 4 * j4 + u;
-                            if (fmaf(nA, xx[u], v[j]) >= fc.B) m |= 1u << j;
-                        }
+                        const int j = 4 * j4;
+                        m0 |= fmaf(nA, x4.x, v[j]) >= fc.B ? 1u << j : 0u;
+                        m1 |= fmaf(nA, x4.y, v[j + 1]) >= fc.B ? 2u << j : 0u;
+                        m2 |= fmaf(nA, x4.z, v[j + 2]) >= fc.B ? 4u << j : 0u;
+                        m3 |= fmaf(nA, x4.w, v[j + 3]) >= fc.B ? 8u << j : 0u;
                     }
+                    uint32_t m = (m0 | m1) | (m2 | m3);
                     m &= valid;
                     if (!qvalid) m = 0;
                     if (m) {
-                        float4* st4 = reinterpret_cast<float4*>(stg);
-#pragma unroll
-                        for (int j4 = 0; j4 < 8; ++j4)
-                            st4[j4] = make_float4(v[4 * j4], v[4 * j4 + 1], v[4 * j4 + 2], v[4 * j4 + 3]);
+                        uint32_t slot = atomicAdd(&cnt_s[qrow], static_cast<uint32_t>(__popc(m)));
                         do {
                             const int j = __ffs(m) - 1;
                             m &= m - 1;
-                            if (cnt < a.cap) {
-                                const float sc = final_score(a.metric, a.cos_small, stg[j], qv, xs_tile[c * 32 + j]);
-                                cbase[cnt] = make_uint2(__float_as_uint(sc), static_cast<uint32_t>(col0 + j));
+                            if (slot < cap) {
+                                const float sc = final_score(a.metric, a.cos_small, pick32(v, j), qv,
+                                                             xs_tile[c * 32 + j]);
+                                cbase[slot] = make_uint2(__float_as_uint(sc), static_cast<uint32_t>(col0 + j));
                             }
-                            ++cnt;
+                            ++slot;
                         } while (m);
                     }
                 } else if (MODE == SCAN_ARGMIN) {
@@ -619,26 +625,38 @@ __device__ __forceinline__ void tc_scan_body(uint8_t* smem_raw, const CUtensorMa
                         }
                     }
                     const int g = a.group;
+                    auto emit = [&](float* p, float mx) {
+                        *p = a.metric == RDB_METRIC_L2 ? fmaxf(qv - 2.f * mx, 0.f) : mx;
+                    };
                     if (qvalid) {
-                        float* gout = a.group_out + q * a.ngroups + col0 / g;
-                        if (g == 16) {
+                        float* gout = a.group_out + q * a.ngroups;
+                        if (g > 32) {
+                            // groups of 64 / 128 span two / four chunks of this warp
+                            float m0 = v[0];
+#pragma unroll
+                            for (int j = 1; j < 32; ++j) m0 = fmaxf(m0, v[j]);
+                            gb = fmaxf(gb, m0);
+                            if (((c + 1) * 32) % g == 0) {
+                                const int64_t gs = (col0 + 32) - g;  // first row of the group
+                                if (gs < r_end) emit(gout + gs / g, gb);
+                                gb = -INFINITY;
+                            }
+                        } else if (g == 16) {
 #pragma unroll
                             for (int h = 0; h < 2; ++h) {
                                 float m0 = v[16 * h];
 #pragma unroll
                                 for (int j = 1; j < 16; ++j) m0 = fmaxf(m0, v[16 * h + j]);
-                                if ((valid >> (16 * h)) & 1u)
-                                    gout[h] = a.metric == RDB_METRIC_L2 ? fmaxf(qv - 2.f * m0, 0.f) : m0;
+                                if ((valid >> (16 * h)) & 1u) emit(gout + col0 / 16 + h, m0);
                             }
                         } else {
-                            float gb = -INFINITY;
+                            float gm = -INFINITY;
 #pragma unroll
                             for (int j = 0; j < 32; ++j) {
-                                gb = fmaxf(gb, v[j]);
+                                gm = fmaxf(gm, v[j]);
                                 if (((j + 1) & (g - 1)) == 0) {
-                                    if ((valid >> j) & 1u)
-                                        gout[j / g] = a.metric == RDB_METRIC_L2 ? fmaxf(qv - 2.f * gb, 0.f) : gb;
-                                    gb = -INFINITY;
+                                    if ((valid >> (j + 1 - g)) & 1u) emit(gout + (col0 + j) / g, gm);
+                                    gm = -INFINITY;
                                 }
                             }
                         }
@@ -658,20 +676,50 @@ __device__ __forceinline__ void tc_scan_body(uint8_t* smem_raw, const CUtensorMa
                         }
                     }
                 }
+            };
+            // TMEM loads double-buffered: chunk c + 1 is in flight while chunk c
+            // is processed
+            constexpr int NCH = BN / 2 / 32;  // chunks per warp half
+            const int c0 = half * NCH;
+            const uint32_t tbase = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) +
+                                   static_cast<uint32_t>(acc * BN + c0 * 32);
+            uint32_t ra[32], rb[32];
+            tmem_ld32_async(tbase, ra);
+            tmem_ld_wait(ra);
+#pragma unroll 1
+            for (int c = 0; c < NCH; c += 2) {
+                tmem_ld32_async(tbase + static_cast<uint32_t>((c + 1) * 32), rb);
+                process_chunk(ra, c0 + c);
+                tmem_ld_wait(rb);
+                if (c + 2 < NCH) tmem_ld32_async(tbase + static_cast<uint32_t>((c + 2) * 32), ra);
+                process_chunk(rb, c0 + c + 1);
+                if (c + 2 < NCH) tmem_ld_wait(ra);
             }
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive_cluster(tempty_lead[acc]);
             // publish the next tile's row values (its buffer was last read in
             // tile t - 1, which every epilogue thread has finished)
-            if (t + 1 < ntiles) reinterpret_cast<float2*>(xv_s + ((t + 1) & 1) * BN)[etid] = xv_next;
+            if (t + 1 < ntiles) xv_s[((t + 1) & 1) * BN + etid] = xv_next;
             epi_bar_sync();
         }
-        if (qvalid) {
+        // the second warp of each quadrant hands its arg-best to the first
+        if (MODE == SCAN_ARGMIN && half == 1) {
+            best_s[qrow] = best;
+            cnt_s[qrow] = best_r;
+        }
+        epi_bar_sync();
+        if (qvalid && half == 0) {
             if (MODE == SCAN_FILTER)
-                a.counts[static_cast<int64_t>(split) * a.nq + q] =
-                    static_cast<int>(min(cnt, static_cast<int64_t>(0x7fffffff)));
+                a.counts[static_cast<int64_t>(split) * a.nq + q] = static_cast<int>(min(cnt_s[qrow], 0x7fffffffu));
             if (MODE == SCAN_ARGMIN) {
+                // larger wins, the lower row on ties (each half kept its first)
+                const float b1 = best_s[qrow];
+                const uint32_t r1 = cnt_s[qrow];
+                if (b1 > best || (b1 == best && r1 < best_r)) {
+                    best = b1;
+                    best_r = r1;
+                }
                 const float dist = fmaxf(qv - 2.f * best, 0.f);
                 a.best[static_cast<int64_t>(split) * a.nq + q] =
                     (ntiles > 0 && best > -INFINITY)
@@ -789,8 +837,8 @@ int launch_scan_tc(const ScanArgs& a, int mode, cudaStream_t s) {
     RDB_CHECK_ARG((reinterpret_cast<uintptr_t>(a.q) & 15) == 0 && (reinterpret_cast<uintptr_t>(a.x) & 15) == 0,
                   "base pointers must be 16-byte aligned");
     if (mode == SCAN_GROUPMAX)
-        RDB_CHECK_ARG(a.group >= 1 && a.group <= 32 && (a.group & (a.group - 1)) == 0 && a.n % a.group == 0,
-                      "group must be a power of two <= 32 dividing n");
+        RDB_CHECK_ARG(a.group >= 1 && a.group <= BN / 2 && (a.group & (a.group - 1)) == 0 && a.n % a.group == 0,
+                      "group must be a power of two <= %d dividing n", BN / 2);
     return tc_use_pair(a.nq) ? launch_shape<true>(a, mode, s) : launch_shape<false>(a, mode, s);
 }
 

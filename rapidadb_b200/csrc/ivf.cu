@@ -274,11 +274,15 @@ __global__ void __launch_bounds__(PNT) ivfpq_scan_kernel(
     float* cb = psm;                                  // M * ksub * dsub
     float* lut = cb + (size_t)M * ksub * dsub;        // M * ksub
     float* res = lut + (size_t)M * ksub;              // d
-    float* mv = res + ((d + 3) & ~3);                 // PNW * kMaxIvfK
-    int64_t* mi = reinterpret_cast<int64_t*>(
-        (reinterpret_cast<uintptr_t>(mv + PNW * kMaxIvfK) + 7) & ~uintptr_t(7));  // PNW * kMaxIvfK
+    unsigned long long* mkey = reinterpret_cast<unsigned long long*>(
+        (reinterpret_cast<uintptr_t>(res + ((d + 3) & ~3)) + 7) & ~uintptr_t(7));  // PNW * kMaxIvfK
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    for (int i = tid; i < M * ksub * dsub; i += PNT) cb[i] = codebooks[i];
+    // codebooks transposed to [m][u][j]: the LUT build reads them with
+    // consecutive codewords j in consecutive threads (no bank conflicts)
+    for (int i = tid; i < M * ksub * dsub; i += PNT) {
+        const int m = i / (ksub * dsub), r = i % (ksub * dsub), j = r / dsub, u = r % dsub;
+        cb[((size_t)m * dsub + u) * ksub + j] = codebooks[i];
+    }
     __syncthreads();
     const bool m16 = (M % 16) == 0;
 
@@ -296,11 +300,11 @@ __global__ void __launch_bounds__(PNT) ivfpq_scan_kernel(
             // LUT[m][j] = |res_m - codeword_mj|^2
             for (int i = tid; i < M * ksub; i += PNT) {
                 const int m = i / ksub, j = i % ksub;
-                const float* pv = cb + ((size_t)m * ksub + j) * dsub;
+                const float* pv = cb + (size_t)m * dsub * ksub + j;
                 const float* rv = res + m * dsub;
                 float s = 0.f;
                 for (int u = 0; u < dsub; ++u) {
-                    const float t = rv[u] - pv[u];
+                    const float t = rv[u] - pv[(size_t)u * ksub];
                     s = fmaf(t, t, s);
                 }
                 lut[i] = s;
@@ -332,28 +336,34 @@ __global__ void __launch_bounds__(PNT) ivfpq_scan_kernel(
                 }
                 st.offer(dist, row, valid, k, false, lane);
             }
-            // merge the warps' lists
-            if (lane < k) {
-                mv[warp * kMaxIvfK + lane] = st.v;
-                mi[warp * kMaxIvfK + lane] = st.id;
+            // merge the warps' sorted lists: block bitonic sort of the
+            // PNW x k (score key, row) keys, best k written out
+            if (lane < kMaxIvfK) {
+                const bool has = lane < k && st.id != INT64_MAX;
+                mkey[warp * kMaxIvfK + lane] =
+                    has ? (((unsigned long long)float_asc_key(st.v) << 32) | (uint32_t)st.id) : ~0ull;
             }
             __syncthreads();
-            if (warp == 0) {
-                WarpTopK fin;
-                fin.init(false);
-                // warp-uniform trip count: every lane offers in every round
-                for (int base = 0; base < PNW * k; base += 32) {
-                    const int i = base + lane;
-                    const bool valid = i < PNW * k;
-                    const int w = valid ? i / k : 0, j = valid ? i % k : 0;
-                    fin.offer(mv[w * kMaxIvfK + j], mi[w * kMaxIvfK + j], valid, k, false, lane);
+            for (int size = 2; size <= PNW * kMaxIvfK; size <<= 1)
+                for (int stride = size >> 1; stride > 0; stride >>= 1) {
+                    const int t = tid, o = tid ^ stride;
+                    if (o > t) {
+                        const bool up = (t & size) == 0;
+                        const unsigned long long a = mkey[t], b = mkey[o];
+                        if ((a > b) == up) {
+                            mkey[t] = b;
+                            mkey[o] = a;
+                        }
+                    }
+                    __syncthreads();
                 }
-                if (lane < k) {
-                    const int64_t o = ((int64_t)p * Q + qq) * k + lane;
-                    const bool has = fin.id != INT64_MAX;
-                    out_v[o] = fin.v;
-                    out_i[o] = has ? (ids ? ids[fin.id] : fin.id) : -1;
-                }
+            if (tid < k) {
+                const unsigned long long key = mkey[tid];
+                const int64_t o = ((int64_t)p * Q + qq) * k + tid;
+                const bool has = key != ~0ull;
+                out_v[o] = has ? asc_key_float((uint32_t)(key >> 32)) : INFINITY;
+                const int64_t row = (int64_t)(uint32_t)key;
+                out_i[o] = has ? (ids ? ids[row] : row) : -1;
             }
         }
     }
@@ -394,8 +404,8 @@ int invert_probes(const int64_t* probe, int64_t Q, int nprobe, int nlist, const 
 }
 
 size_t pq_smem(int d, int M, int ksub) {
-    return sizeof(float) * ((size_t)ksub * d + (size_t)M * ksub + ((d + 3) & ~3) + PNW * kMaxIvfK) +
-           sizeof(int64_t) * (PNW * kMaxIvfK + 1);
+    return sizeof(float) * ((size_t)ksub * d + (size_t)M * ksub + ((d + 3) & ~3)) +
+           sizeof(unsigned long long) * (PNW * kMaxIvfK + 1);
 }
 
 }  // namespace

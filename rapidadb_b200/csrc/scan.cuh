@@ -52,7 +52,7 @@ struct ScanArgs {
 
     // SCAN_GROUPMAX: group_out[q][row / group] = best final score (approximate
     // to a few ulps) over logical rows [g * group, (g + 1) * group); group is a
-    // power of two <= 32 and n a multiple of it.
+    // power of two <= 128 and n a multiple of it.
     float* group_out;
     int group;
     int64_t ngroups;

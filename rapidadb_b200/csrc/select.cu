@@ -20,10 +20,13 @@ constexpr int NT = 256;
 constexpr int NWARP = NT / 32;
 constexpr int kCacheKeys = 8192;  // keys cached in shared memory when T fits
 constexpr int kMaxSeg = 1024;
+constexpr int kDigit = 11;  // radix digit width
+constexpr int kBins = 1 << kDigit;
 
 struct SelShared {
     int seg_off[kMaxSeg + 1];
-    int hist[256];
+    int hist[kBins];
+    int wsum[NWARP];
     unsigned long long red_min[NWARP];
     unsigned long long red_max[NWARP];
     unsigned long long prefix;
@@ -187,65 +190,62 @@ __global__ void __launch_bounds__(NT) select_kernel(SelectArgs a) {
         }
         __syncthreads();
 
-        // ---- MSD radix select --------------------------------------------
+        // ---- MSD radix select: 11-bit digits from the highest bit that differs
         int rounds = 0;
         while (!S.done) {
             const int top = S.top;
-            const int shift = top > 8 ? top - 8 : 0;
+            const int shift = top > kDigit ? top - kDigit : 0;
             const unsigned width_mask = (1u << (top - shift)) - 1u;
             const unsigned long long prefix = S.prefix;
-            for (int i = threadIdx.x; i < 256; i += NT) S.hist[i] = 0;
+            const int rem = S.remaining;  // read before the owner below rewrites it
+            for (int i = threadIdx.x; i < kBins; i += NT) S.hist[i] = 0;
             __syncthreads();
-            const int Tr = (T + 31) & ~31;
             ElemCursor cur;
-            for (int e = threadIdx.x; e < Tr; e += NT) {
-                int bin = -1;
-                if (e < T) {
-                    unsigned long long key = cached ? cache[e] : cur.key(a, S, q, e, qv);
-                    if (hi_eq(key, prefix, top)) bin = (int)((key >> shift) & width_mask);
-                }
-                unsigned peers = __match_any_sync(0xffffffffu, bin);
-                if (bin >= 0 && lane == __ffs(peers) - 1) atomicAdd(&S.hist[bin], __popc(peers));
+            for (int e = threadIdx.x; e < T; e += NT) {
+                const unsigned long long key = cached ? cache[e] : cur.key(a, S, q, e, qv);
+                if (hi_eq(key, prefix, top)) atomicAdd(&S.hist[(key >> shift) & width_mask], 1);
             }
             __syncthreads();
-            if (warp == 0) {
-                // bucket b holding the remaining-th smallest key
-                int c[8];
-                int local = 0;
-                for (int j = 0; j < 8; ++j) {
-                    c[j] = S.hist[lane * 8 + j];
-                    local += c[j];
-                }
-                int incl = local;
-                for (int o = 1; o < 32; o <<= 1) {
-                    int v = __shfl_up_sync(0xffffffffu, incl, o);
-                    if (lane >= o) incl += v;
-                }
-                int excl = incl - local;
-                int rem = S.remaining;
-                bool mine = excl < rem && rem <= incl;
-                unsigned owner = __ballot_sync(0xffffffffu, mine);
-                if (mine) {
-                    int cum = excl, b = 0;
-                    for (int j = 0; j < 8; ++j) {
-                        if (cum + c[j] >= rem) {
-                            b = lane * 8 + j;
-                            break;
-                        }
-                        cum += c[j];
+            // block-wide scan of the bins: thread t owns bins [8t, 8t + 8)
+            constexpr int PER = kBins / NT;
+            int c[PER];
+            int local = 0;
+#pragma unroll
+            for (int j = 0; j < PER; ++j) {
+                c[j] = S.hist[threadIdx.x * PER + j];
+                local += c[j];
+            }
+            int incl = local;
+            for (int o = 1; o < 32; o <<= 1) {
+                const int v = __shfl_up_sync(0xffffffffu, incl, o);
+                if (lane >= o) incl += v;
+            }
+            if (lane == 31) S.wsum[warp] = incl;
+            __syncthreads();
+            int before = 0;
+            for (int w = 0; w < warp; ++w) before += S.wsum[w];
+            incl += before;
+            const int excl = incl - local;
+            if (excl < rem && rem <= incl) {
+                int cum = excl, b = 0;
+#pragma unroll
+                for (int j = 0; j < PER; ++j) {
+                    if (cum + c[j] >= rem) {
+                        b = threadIdx.x * PER + j;
+                        break;
                     }
-                    int nrem = rem - cum;
-                    int cnt_b = S.hist[b];
-                    unsigned long long mask = (unsigned long long)width_mask << shift;
-                    S.prefix = (prefix & ~mask) | ((unsigned long long)b << shift);
-                    S.remaining = nrem;
-                    S.top = shift;
-                    S.done = (cnt_b == nrem || shift == 0) ? 1 : 0;
+                    cum += c[j];
                 }
-                if (owner == 0 && lane == 0) S.done = 1;  // no bucket (cannot happen): stop
+                const int nrem = rem - cum;
+                const int cnt_b = S.hist[b];
+                const unsigned long long mask = (unsigned long long)width_mask << shift;
+                S.prefix = (prefix & ~mask) | ((unsigned long long)b << shift);
+                S.remaining = nrem;
+                S.top = shift;
+                S.done = (cnt_b == nrem || shift == 0) ? 1 : 0;
             }
             __syncthreads();
-            if (++rounds >= 9 && threadIdx.x == 0) S.done = 1;  // 64-bit keys need <= 8 rounds
+            if (++rounds >= 8 && threadIdx.x == 0) S.done = 1;  // 64-bit keys need <= 6 rounds
             __syncthreads();
         }
 
