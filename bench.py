@@ -270,6 +270,7 @@ def run_ours(args, wl):
     import ctypes
 
     lib = ctypes.CDLL(os.path.join(ROOT, "rapidadb_b200", "librdb_kernels.so"))
+    lib.rdb_launch_count.restype = ctypes.c_ulonglong
     lib.rdb_timing_enable(1)
     torch.cuda.synchronize()
     if world > 1:
@@ -277,10 +278,12 @@ def run_ours(args, wl):
     torch.cuda.synchronize()
     e0 = torch.cuda.Event(enable_timing=True)
     e1 = torch.cuda.Event(enable_timing=True)
+    n_launch0 = lib.rdb_launch_count()
     e0.record()
     for _ in range(args.steps):
         out_d, out_i = step(q)
     e1.record()
+    n_launches = int(lib.rdb_launch_count() - n_launch0)
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
@@ -360,9 +363,6 @@ def run_ours(args, wl):
         n_local = hi - lo
         flops = 2.0 * Q * n_local * d
         achieved = flops / (kernel_ms * 1e-3) / 1e12 if kernel_ms > 0 else None
-        launches_per_step = 6 if wl["precision"] != "fp32" or N >= 4096 else 4
-        if world > 1:
-            launches_per_step += 1
         qps = Q * args.steps / (ms * 1e-3)
         result = {
             "metric": "search QPS (exact flat search, recall@%d)" % k,
@@ -388,7 +388,7 @@ def run_ours(args, wl):
             },
             "e2e": {"value": round(Q * args.steps / e2e_s, 1), "unit": "queries/s",
                     "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h)},
-            "gpu_launches": launches_per_step * args.steps,
+            "gpu_launches": n_launches,
             "roofline": {
                 "bound": "tensor",
                 "achieved": round(achieved, 1) if achieved else None,
@@ -493,7 +493,8 @@ def _dist_setup():
 
 def _timed(fn, steps, warmup, world, tag_mask, local_rank):
     """CUDA-event time of `steps` calls (max over ranks), the tagged kernels'
-    device time, and the clock record."""
+    device time, and the clock record; `_timed.launches` = this library's
+    kernel launches inside the timed region."""
     import ctypes
 
     import torch
@@ -505,6 +506,7 @@ def _timed(fn, steps, warmup, world, tag_mask, local_rank):
     if world > 1:
         dist.barrier()
     lib = ctypes.CDLL(os.path.join(ROOT, "rapidadb_b200", "librdb_kernels.so"))
+    lib.rdb_launch_count.restype = ctypes.c_ulonglong
     clocks = ClockSampler(local_rank)
     clocks.start()
     lib.rdb_timing_enable(tag_mask)
@@ -513,11 +515,13 @@ def _timed(fn, steps, warmup, world, tag_mask, local_rank):
         dist.barrier()
     e0 = torch.cuda.Event(enable_timing=True)
     e1 = torch.cuda.Event(enable_timing=True)
+    n_launch0 = lib.rdb_launch_count()
     e0.record()
     out = None
     for _ in range(steps):
         out = fn()
     e1.record()
+    _timed.launches = int(lib.rdb_launch_count() - n_launch0)
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
@@ -656,14 +660,20 @@ def run_ivf(args, wl):
                            "codes" if pq else "rows", (hi - lo) * bpr / 1e9)},
             "e2e": {"value": round(Q * args.steps / e2e_s, 1), "unit": "queries/s",
                     "h2d_bytes_per_step": int(q.numel() * 4), "d2h_bytes_per_step": int(Q * k * 12)},
-            "gpu_launches": None,
+            "gpu_launches": _timed.launches,
             "roofline": {"bound": "hbm", "achieved": round(ach, 1) if ach else None, "peak": hbm, "unit": "GB/s",
                          "frac": round(ach / hbm, 4) if ach else None, "traffic": None,
-                         "kernel": "ivfpq_scan_kernel" if pq else "ivf_flat_scan_kernel",
+                         "kernel": ("ivfpq_search_kernel<%d> (query-major)" % wl["M"] if idx.query_major()
+                                    else "ivfpq_scan_kernel") if pq else "ivf_flat_scan_kernel",
                          "kernel_ms": round(kern_ms, 4), "bytes_per_launch": alg_bytes,
-                         "bytes_definition": "sum over (query, probed list) of the list's stored %s bytes "
-                                             "(query-major count; the list-major scan reads each list once "
-                                             "per 32-query chunk, so frac may exceed 1)" % ("code" if pq else "row"),
+                         "bytes_definition": (
+                             "sum over (query, probed list) of the list's stored code bytes (query-major "
+                             "count; the kernel also reads a 4-byte per-row term, not counted; lists shared by "
+                             "queries running at the same time are served from L2, so frac may exceed 1)"
+                             if pq else
+                             "sum over (query, probed list) of the list's stored row bytes (query-major count; "
+                             "the list-major scan reads each list once per 32-query chunk, so frac may exceed "
+                             "1)"),
                          "peak_source": src},
             "clocks": clk,
         }
@@ -722,6 +732,7 @@ def run_kmeans(args, wl):
                          "unit": "TFLOP/s", "frac": round(ach / bf16, 4) if ach else None, "traffic": None,
                          "kernel": "tc_scan_pair_kernel<ARGMIN> (assign)", "kernel_ms": round(kern_ms, 3),
                          "flops_per_launch": flops, "peak_source": src},
+            "gpu_launches": _timed.launches,
             "clocks": clk,
         }
     if world > 1:

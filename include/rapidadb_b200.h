@@ -205,15 +205,48 @@ int rdb_ivfpq_scan(const float* q, int64_t nq, int64_t ldq, int d, const int64_t
                    const int64_t* list_off, const int64_t* ids, int k, float* out_v, int64_t* out_i, void* ws,
                    size_t ws_bytes, void* stream);
 
+/* Query-major IVF-PQ search (squared L2; replaces rdb_ivfpq_scan + the merge
+ * when rdb_pq_fast_layout(M) is 1, i.e. M in {4, 8, 16, 32, 64, 96}).
+ * The residual ADC distance is regrouped as
+ *   |q - c_l|^2 + row_terms[row] + sum_m QT[m][code_m],  QT[m][j] = -2 <q_m, cb[m][j]>,
+ * so one lookup table per query serves all of its probed lists.
+ *   rdb_pq_row_terms     row_terms[i] = sum_m |cb[m][c_m]|^2 + 2 <(c_{labels[i]})_m, cb[m][c_m]>
+ *                        for unrotated codes [n, M] (once per added row);
+ *   rdb_pq_rotate_codes  in place: within each group of G = min(M, 32) code
+ *                        bytes, row i (list order) is rotated by i mod G
+ *                        (stored byte s = code[(i + s) mod G]); inverse != 0
+ *                        undoes it.  rdb_ivfpq_search reads rotated codes;
+ *   rdb_ivfpq_search     probe [nq, nprobe] list ids; codes / row_terms /
+ *                        ids in list order (list_off [nlist + 1]); writes the
+ *                        best k (k <= 32) per query, ascending, ties to the
+ *                        lower stored row, to out_v / out_i [nq, k] (ids[row],
+ *                        or -1 padding).  nprobe <= 4096, nlist <= 16384,
+ *                        fewer than 2^32 stored rows.
+ * No reference counterpart (the reference declares IVF-PQ parameters only,
+ * python/rapidadb/config.py:50-56). */
+int rdb_pq_fast_layout(int M);
+int rdb_pq_row_terms(const uint8_t* codes, int64_t n, int M, const int32_t* labels, const float* centroids, int d,
+                     const float* codebooks, int ksub, float* out_terms, void* stream);
+int rdb_pq_rotate_codes(uint8_t* codes, int64_t n, int M, int inverse, void* stream);
+size_t rdb_ivfpq_search_workspace(int64_t nq, int nlist);
+int rdb_ivfpq_search(const float* q, int64_t nq, int64_t ldq, int d, const int64_t* probe, int nprobe,
+                     const float* centroids, int nlist, const float* codebooks, int M, int ksub, const uint8_t* codes,
+                     const float* row_terms, const int64_t* list_off, const int64_t* ids, int k, float* out_v,
+                     int64_t* out_i, void* ws, size_t ws_bytes, void* stream);
+
 /* Profiling hook (no reference counterpart; the reference times whole calls,
  * benchmarks/src/bench_compare.py:56-59): `mask` selects launches to time
  * with CUDA events recorded on their launching stream -- 1 the main scan of
  * rdb_flat_search, 2 the rdb_ivf_flat_scan list scan, 4 the rdb_ivfpq_scan
- * list scan, 8 the rdb_kmeans_assign scan, 16 the rdb_kmeans_update segment
- * sums (0 turns timing off).  rdb_timing_read synchronises the recorded
+ * list scan or the rdb_ivfpq_search kernel, 8 the rdb_kmeans_assign scan, 16
+ * the rdb_kmeans_update segment sums (0 turns timing off).  rdb_timing_read synchronises the recorded
  * events and returns the summed device time and the number of timed launches. */
 int rdb_timing_enable(int mask);
 int rdb_timing_read(double* total_ms, int* launches, int reset);
+
+/* Kernels this library has launched so far in the process, all devices and
+ * threads (no reference counterpart): read it before and after a region. */
+unsigned long long rdb_launch_count(void);
 
 #ifdef __cplusplus
 }

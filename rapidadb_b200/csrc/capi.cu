@@ -3,6 +3,7 @@
 #include <stdarg.h>
 #include <stdio.h>
 
+#include <atomic>
 #include <mutex>
 #include <utility>
 #include <vector>
@@ -20,6 +21,10 @@ int set_error(int code, const char* fmt, ...) {
     va_end(ap);
     return code;
 }
+
+static std::atomic<unsigned long long> g_launches{0};
+
+void note_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
 
 int num_sms() {
     static int cached[64] = {0};
@@ -110,6 +115,8 @@ int rdb_timing_read(double* total_ms, int* launches, int reset) {
 }
 
 const char* rdb_last_error(void) { return rdb::g_err; }
+
+unsigned long long rdb_launch_count(void) { return rdb::g_launches.load(std::memory_order_relaxed); }
 
 int rdb_version(void) { return 100; }
 

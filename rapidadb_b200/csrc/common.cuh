@@ -14,6 +14,7 @@ namespace rdb {
 
 // Records a message for rdb_last_error() (thread-local) and returns `code`.
 int set_error(int code, const char* fmt, ...);
+void note_launch();
 
 #define RDB_CHECK_ARG(cond, ...)                                   \
     do {                                                           \
@@ -32,12 +33,15 @@ int set_error(int code, const char* fmt, ...);
         }                                                                         \
     } while (0)
 
+// After every kernel launch of the library (exactly one per launch site):
+// reports a launch error, else counts the launch (rdb_launch_count).
 #define RDB_LAUNCH_CHECK()                                                        \
     do {                                                                          \
         cudaError_t e_ = cudaGetLastError();                                      \
         if (e_ != cudaSuccess)                                                    \
             return ::rdb::set_error(RDB_ERR_CUDA, "kernel launch: %s (%s:%d)",    \
                                     cudaGetErrorString(e_), __FILE__, __LINE__);  \
+        ::rdb::note_launch();                                                     \
     } while (0)
 
 #define RDB_TRY(expr)              \

@@ -345,7 +345,11 @@ __device__ __forceinline__ void tc_scan_body(uint8_t* smem_raw, const CUtensorMa
     const uint32_t rank = PAIR ? cluster_rank() : 0u;
     const bool leader = rank == 0;
     const int split = PAIR ? static_cast<int>(blockIdx.x >> 1) : static_cast<int>(blockIdx.x);
-    const int64_t q0 = (PAIR ? (2 * static_cast<int64_t>(blockIdx.y) + rank) : static_cast<int64_t>(blockIdx.y)) * BM;
+    // query blocks run along y, continuing in z past the 65535 limit of y; both
+    // CTAs of a pair share y and z, so they leave together
+    const int64_t qblk = static_cast<int64_t>(blockIdx.z) * gridDim.y + blockIdx.y;
+    if ((PAIR ? 2 * qblk : qblk) * BM >= a.nq) return;
+    const int64_t q0 = (PAIR ? (2 * qblk + rank) : qblk) * BM;
     const int64_t r_begin = static_cast<int64_t>(split) * a.rows_per_split;
     const int64_t r_end = min(a.n, r_begin + a.rows_per_split);
     const int ntiles = r_end > r_begin ? static_cast<int>((r_end - r_begin + BN - 1) / BN) : 0;
@@ -810,13 +814,14 @@ int launch_mode(const CUtensorMap& mq, const CUtensorMap& mx, const ScanArgs& a,
 template <bool PAIR>
 int launch_shape(const ScanArgs& a, int mode, cudaStream_t s) {
     const int qunit = PAIR ? 2 * BM : BM;
-    const int64_t gy = (a.nq + qunit - 1) / qunit;
-    RDB_CHECK_ARG(gy <= 65535, "too many queries for one launch");
+    const int64_t gq = (a.nq + qunit - 1) / qunit;
+    const int64_t gy = std::min<int64_t>(gq, 65535), gz = (gq + gy - 1) / gy;
+    RDB_CHECK_ARG(gz <= 65535, "too many queries for one launch");
     CUtensorMap mq, mx;
     RDB_TRY(make_map(&mq, a.dtype, a.q, a.nq, a.d, a.ldq * 2, BM));
     RDB_TRY(make_map(&mx, a.dtype, a.x, a.n, a.d, a.ldx * 2 * a.row_step, TcCfg<PAIR>::B_ROWS));
     const uint32_t idesc = make_idesc(a.dtype == RDB_BF16, TcCfg<PAIR>::UMMA_M);
-    dim3 grid(PAIR ? 2 * a.nsplit : a.nsplit, static_cast<unsigned>(gy));
+    dim3 grid(PAIR ? 2 * a.nsplit : a.nsplit, static_cast<unsigned>(gy), static_cast<unsigned>(gz));
     if (mode == SCAN_FILTER) return launch_mode<SCAN_FILTER, PAIR>(mq, mx, a, idesc, grid, s);
     if (mode == SCAN_ARGMIN) return launch_mode<SCAN_ARGMIN, PAIR>(mq, mx, a, idesc, grid, s);
     if (mode == SCAN_GROUPMAX) return launch_mode<SCAN_GROUPMAX, PAIR>(mq, mx, a, idesc, grid, s);

@@ -91,6 +91,8 @@ PYBIND11_MODULE(_C, m) {
     m.def("kmeans_finalize", &kmeans_finalize, "sums / counts (empty clusters keep their centroid)",
           py::arg("sums"), py::arg("counts"), py::arg("centroids"));
     m.def("label_sort", &label_sort, "stable counting sort by label", py::arg("labels"), py::arg("k"));
+    m.def("pq_row_terms", &pq_row_terms, "per-row constant of the IVF-PQ distance", py::arg("codes"),
+          py::arg("labels"), py::arg("centroids"), py::arg("codebooks"));
     m.def("pq_encode", &pq_encode, "residual PQ codes", py::arg("points"), py::arg("labels"),
           py::arg("centroids"), py::arg("codebooks"));
 
@@ -150,6 +152,8 @@ PYBIND11_MODULE(_C, m) {
         .def("stored_ids", &IVFPQIndex::stored_ids)
         .def("stored_labels", &IVFPQIndex::stored_labels)
         .def("stored_codes", &IVFPQIndex::stored_codes)
+        .def("stored_row_terms", &IVFPQIndex::stored_row_terms)
+        .def("query_major", &IVFPQIndex::query_major)
         .def("__len__", &IVFPQIndex::size)
         .def("__repr__", [](const IVFPQIndex& s) {
             return "IVFPQIndex(dim=" + std::to_string(s.dim()) + ", nlist=" + std::to_string(s.nlist()) +

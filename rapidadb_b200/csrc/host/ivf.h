@@ -15,6 +15,8 @@ std::tuple<at::Tensor, at::Tensor> kmeans_update(const at::Tensor& x, const at::
 at::Tensor kmeans_finalize(const at::Tensor& sums, const at::Tensor& counts, const at::Tensor& centroids);
 // (seg_start [K + 1], perm [n], counts [K]) of a stable sort by label
 std::tuple<at::Tensor, at::Tensor, at::Tensor> label_sort(const at::Tensor& labels, int64_t K);
+at::Tensor pq_row_terms(const at::Tensor& codes, const at::Tensor& labels, const at::Tensor& centroids,
+                        const at::Tensor& codebooks);
 at::Tensor pq_encode(const at::Tensor& x, const at::Tensor& labels, const at::Tensor& centroids,
                      const at::Tensor& codebooks);
 
@@ -85,14 +87,20 @@ class IVFPQIndex : public IVFBase {
     Result search_probed(const at::Tensor& queries, const at::Tensor& probe, int64_t k) const;
     void reset() override;
     at::Tensor codebooks() const { return codebooks_; }
-    at::Tensor stored_codes() const { return codes_; }
+    // codes [n, M] in list order, as encoded (the stored copy may be rotated)
+    at::Tensor stored_codes() const;
+    at::Tensor stored_row_terms() const { return row_terms_; }
     int pq_m() const { return M_; }
     int pq_k() const { return ksub_; }
+    // true when search runs the query-major kernel (rotated code layout)
+    bool query_major() const { return fast_; }
 
   private:
     int M_, ksub_;
+    bool fast_;
     at::Tensor codebooks_;  // [M, ksub, dim / M] fp32
-    at::Tensor codes_;      // [n, M] uint8, list-major
+    at::Tensor codes_;      // [n, M] uint8, list-major (rotated when fast_)
+    at::Tensor row_terms_;  // [n] fp32, list-major (fast_ only)
 };
 
 }  // namespace rdbh

@@ -128,6 +128,25 @@ at::Tensor pq_encode(const at::Tensor& x, const at::Tensor& labels, const at::Te
     return codes;
 }
 
+at::Tensor pq_row_terms(const at::Tensor& codes, const at::Tensor& labels, const at::Tensor& centroids,
+                        const at::Tensor& codebooks) {
+    TORCH_CHECK(codebooks.dim() == 3 && codes.dim() == 2 && codes.size(1) == codebooks.size(0),
+                "codes must be [n, M] for codebooks [M, ksub, d / M]");
+    c10::cuda::CUDAGuard guard(codes.device());
+    at::Tensor cf = contig_f32(centroids), cb = contig_f32(codebooks);
+    at::Tensor cd = codes.to(at::kByte).contiguous();
+    at::Tensor lab = labels.to(at::kInt).contiguous();
+    const int64_t n = cd.size(0);
+    const int M = static_cast<int>(cb.size(0)), ksub = static_cast<int>(cb.size(1));
+    const int d = static_cast<int>(cb.size(2)) * M;
+    TORCH_CHECK(cf.dim() == 2 && cf.size(1) == d, "centroids must be [nlist, d]");
+    at::Tensor out = at::empty({n}, cf.options());
+    check_status(rdb_pq_row_terms(cd.data_ptr<uint8_t>(), n, M, lab.data_ptr<int32_t>(), cf.data_ptr<float>(), d,
+                                  cb.data_ptr<float>(), ksub, out.data_ptr<float>(), stream_ptr()),
+                 "pq row terms");
+    return out;
+}
+
 // ------------------------------------------------------------- IVF common
 
 IVFBase::IVFBase(int dim, Metric metric, int nlist, int nprobe) : dim_(dim), metric_(metric), nlist_(nlist) {
@@ -273,7 +292,7 @@ void IVFFlatIndex::reset() {
 // ----------------------------------------------------------------- IVF-PQ
 
 IVFPQIndex::IVFPQIndex(int dim, Metric metric, int nlist, int nprobe, int m, int ksub)
-    : IVFBase(dim, metric, nlist, nprobe), M_(m), ksub_(ksub) {
+    : IVFBase(dim, metric, nlist, nprobe), M_(m), ksub_(ksub), fast_(rdb_pq_fast_layout(m) != 0) {
     TORCH_CHECK(metric == Metric::L2, "IVF-PQ supports the l2 metric");
     TORCH_CHECK(m >= 1 && dim % m == 0, "pq_m must divide dim");
     TORCH_CHECK(dim / m <= 32, "dim / pq_m must be <= 32");
@@ -298,9 +317,10 @@ void IVFPQIndex::add(const at::Tensor& vectors, const at::Tensor& ids) {
     at::Tensor nid = new_ids(vectors, ids);
     at::Tensor xf = contig_f32(vectors);
     at::Tensor lab = std::get<0>(kmeans_assign(xf, centroids_, true));
+    TORCH_CHECK(n_ + m < (int64_t(1) << 32), "at most 2^32 - 1 rows per device");
     at::Tensor codes_new = pq_encode(xf, lab, centroids_, codebooks_);
     at::Tensor lab_all = n_ ? at::cat({labels_, lab}) : lab;
-    at::Tensor codes_all = n_ ? at::cat({codes_, codes_new}) : codes_new;
+    at::Tensor codes_all = n_ ? at::cat({stored_codes(), codes_new}) : codes_new;
     at::Tensor ids_all = n_ ? at::cat({ids_, nid}) : nid;
     auto pl = relist(lab_all);
     at::Tensor perm = std::get<0>(pl);
@@ -308,7 +328,22 @@ void IVFPQIndex::add(const at::Tensor& vectors, const at::Tensor& ids) {
     ids_ = ids_all.index_select(0, perm);
     labels_ = lab_all.index_select(0, perm);
     list_off_ = std::get<1>(pl);
+    if (fast_) {
+        at::Tensor terms_new = pq_row_terms(codes_new, lab, centroids_, codebooks_);
+        at::Tensor terms_all = n_ ? at::cat({row_terms_, terms_new}) : terms_new;
+        row_terms_ = terms_all.index_select(0, perm);
+        check_status(rdb_pq_rotate_codes(codes_.data_ptr<uint8_t>(), codes_.size(0), M_, 0, stream_ptr()),
+                     "pq code layout");
+    }
     n_ += m;
+}
+
+at::Tensor IVFPQIndex::stored_codes() const {
+    if (!fast_ || !codes_.defined() || codes_.size(0) == 0) return codes_;
+    c10::cuda::CUDAGuard guard(codes_.device());
+    at::Tensor c = codes_.clone();
+    check_status(rdb_pq_rotate_codes(c.data_ptr<uint8_t>(), c.size(0), M_, 1, stream_ptr()), "pq code layout");
+    return c;
 }
 
 Result IVFPQIndex::search(const at::Tensor& queries, int64_t k) const {
@@ -325,6 +360,19 @@ Result IVFPQIndex::search_probed(const at::Tensor& queries, const at::Tensor& pr
     at::Tensor probe_lists = check_probe(probe_in, q.size(0), codes_);
     const int np = static_cast<int>(probe_lists.size(1));
     const int64_t nq = q.size(0);
+    if (fast_) {
+        at::Tensor dv = at::empty({nq, k}, q.options());
+        at::Tensor di = at::empty({nq, k}, q.options().dtype(at::kLong));
+        at::Tensor ws = ws_bytes(q, rdb_ivfpq_search_workspace(nq, nlist_));
+        check_status(rdb_ivfpq_search(q.data_ptr<float>(), nq, dim_, dim_, probe_lists.data_ptr<int64_t>(), np,
+                                      centroids_.data_ptr<float>(), nlist_, codebooks_.data_ptr<float>(), M_, ksub_,
+                                      codes_.data_ptr<uint8_t>(), row_terms_.data_ptr<float>(),
+                                      list_off_.data_ptr<int64_t>(), ids_.data_ptr<int64_t>(), static_cast<int>(k),
+                                      dv.data_ptr<float>(), di.data_ptr<int64_t>(), ws.data_ptr(), ws.numel(),
+                                      stream_ptr()),
+                     "ivf-pq search");
+        return {dv, di};
+    }
     at::Tensor cv = at::empty({np, nq, k}, q.options());
     at::Tensor ci = at::empty({np, nq, k}, q.options().dtype(at::kLong));
     at::Tensor ws = ws_bytes(q, rdb_ivf_scan_workspace(nq, np, nlist_));
@@ -340,6 +388,7 @@ Result IVFPQIndex::search_probed(const at::Tensor& queries, const at::Tensor& pr
 void IVFPQIndex::reset() {
     IVFBase::reset();
     codes_ = at::Tensor();
+    row_terms_ = at::Tensor();
 }
 
 }  // namespace rdbh

@@ -66,7 +66,9 @@ __global__ void __launch_bounds__(NT) simt_scan_kernel(ScanArgs a) {
     const T* __restrict__ qp = static_cast<const T*>(a.q);
     const T* __restrict__ xp = static_cast<const T*>(a.x);
     const int split = blockIdx.x;
-    const int64_t q0 = (int64_t)blockIdx.y * BQ;
+    // query blocks run along y, continuing in z past the 65535 limit of y
+    const int64_t q0 = ((int64_t)blockIdx.z * gridDim.y + blockIdx.y) * BQ;
+    if (q0 >= a.nq) return;
     const int64_t r_begin = (int64_t)split * a.rows_per_split;
     const int64_t r_end = min(a.n, r_begin + a.rows_per_split);
     const int tid = threadIdx.x, tq = tid >> 5, tr = tid & 31;
@@ -211,9 +213,10 @@ int launch_scan_simt(const ScanArgs& a, int mode, cudaStream_t s) {
     if (a.nq <= 0 || a.n <= 0) return RDB_OK;
     RDB_CHECK_ARG(a.rows_per_split % kSimtRows == 0, "rows_per_split must be a multiple of %d",
                   kSimtRows);
-    int64_t gy = (a.nq + BQ - 1) / BQ;
-    RDB_CHECK_ARG(gy <= 65535, "too many queries for one launch (%lld)", (long long)a.nq);
-    dim3 grid(a.nsplit, (unsigned)gy);
+    const int64_t gq = (a.nq + BQ - 1) / BQ;
+    const int64_t gy = std::min<int64_t>(gq, 65535), gz = (gq + gy - 1) / gy;
+    RDB_CHECK_ARG(gz <= 65535, "too many queries for one launch (%lld)", (long long)a.nq);
+    dim3 grid(a.nsplit, (unsigned)gy, (unsigned)gz);
     switch (a.dtype) {
         case RDB_F32: return launch_typed<float>(a, mode, s, grid);
         case RDB_F16: return launch_typed<__half>(a, mode, s, grid);

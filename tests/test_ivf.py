@@ -71,26 +71,37 @@ def test_ivf_flat_bf16_storage(device):
     assert recall(i.cpu().numpy(), ri) >= 0.99
 
 
-def test_ivfpq_codes_and_search_match_oracle(device):
+@pytest.mark.parametrize("M,nlist,nprobe,query_major", [(8, 32, 6, True), (16, 64, 40, True), (2, 32, 6, False)])
+def test_ivfpq_codes_and_search_match_oracle(device, M, nlist, nprobe, query_major):
+    """M = 8 / 16 run the query-major kernel (rotated code layout, per-row
+    terms), M = 2 the list-major scan + merge; both against the oracle's ADC."""
     import rapidadb._C as _C
     from rapidadb_b200.kmeans import kmeans, train_pq
 
     x, g = mixture(2, 30000, 32, 50)
     q = (x[g.integers(0, len(x), 100)] + 0.3 * g.standard_normal((100, 32))).astype(np.float32)
     xt = torch.from_numpy(x).cuda()
-    cent = kmeans(xt, 32, 8, 0.0, seed=3).centroids
+    cent = kmeans(xt, nlist, 8, 0.0, seed=3).centroids
     lab, _ = _C.kmeans_assign(xt, cent, True)
-    books = train_pq(xt - cent.index_select(0, lab.long()), 8, 64, 6, seed=4)
-    idx = _C.IVFPQIndex(32, _C.Metric.L2, 32, 6, 8, 64)
+    books = train_pq(xt - cent.index_select(0, lab.long()), M, 64, 6, seed=4)
+    idx = _C.IVFPQIndex(32, _C.Metric.L2, nlist, nprobe, M, 64)
+    assert idx.query_major() == query_major
     idx.set_quantizer(cent, books)
     idx.add(xt[:12345])
     idx.add(xt[12345:])
     off, row_ids, xs = layout(idx, x)
-    lab_or, _, _ = oracle.kmeans_assign(x, cent.cpu().numpy())
-    codes_or = oracle.pq_encode(x, lab_or, cent.cpu().numpy(), books.cpu().numpy())
+    cn, bn = cent.cpu().numpy(), books.cpu().numpy()
+    lab_or, _, _ = oracle.kmeans_assign(x, cn)
+    codes_or = oracle.pq_encode(x, lab_or, cn, bn)
     np.testing.assert_array_equal(idx.stored_codes().cpu().numpy(), codes_or[row_ids])
+    if query_major:
+        # T[row] = sum_m |cb[m][c_m]|^2 + 2 <(c_l)_m, cb[m][c_m]>
+        c = codes_or[row_ids].astype(np.int64)
+        rec = bn[np.arange(M)[None, :], c].reshape(len(c), -1).astype(np.float64)
+        t = (rec * rec).sum(1) + 2.0 * (rec * cn[lab_or[row_ids]].astype(np.float64)).sum(1)
+        np.testing.assert_allclose(idx.stored_row_terms().cpu().numpy(), t, rtol=1e-5, atol=1e-3)
     d, i = idx.search(torch.from_numpy(q).cuda(), 10)
-    rd, ri = oracle.ivfpq_search(q, cent.cpu().numpy(), off, codes_or[row_ids], row_ids, books.cpu().numpy(), 6, 10)
+    rd, ri = oracle.ivfpq_search(q, cn, off, codes_or[row_ids], row_ids, bn, nprobe, 10)
     assert recall(i.cpu().numpy(), ri) >= 0.999
     np.testing.assert_allclose(d.cpu().numpy(), rd, rtol=1e-4, atol=1e-3)
 

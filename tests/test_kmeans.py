@@ -54,6 +54,17 @@ def test_exact_assign_bitwise_oracle(device, d):
     np.testing.assert_array_equal(sq.cpu().numpy(), rsq)
 
 
+def test_exact_assign_past_65535_query_blocks(device):
+    """2.2M points = 68,750 blocks of 32 queries: the grid continues in z."""
+    g = np.random.default_rng(11)
+    x = g.standard_normal((2_200_000, 8), dtype=np.float32)
+    c = g.standard_normal((5, 8), dtype=np.float32)
+    lab, sq = _C().kmeans_assign(torch.from_numpy(x).cuda(), torch.from_numpy(c).cuda(), True)
+    rl, _, rsq = oracle.kmeans_assign(x, c)
+    np.testing.assert_array_equal(lab.cpu().numpy(), rl)
+    np.testing.assert_array_equal(sq.cpu().numpy(), rsq)
+
+
 @pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16, torch.float16])
 def test_fast_assign_near_ties_only(device, dtype):
     """GEMM assignment may differ from the exact one only where the two
