@@ -5,14 +5,16 @@
 // follow the CPU oracle (oracle/cpu_oracle.c: orc_ivf_flat_search,
 // orc_pq_encode, orc_ivfpq_search).
 //
-// Both scans are LIST-MAJOR: the [Q, nprobe] probe table is inverted with the
-// stable label sort (entries grouped by list), and one CTA scores a list's
-// rows (IVF-Flat) or codes (IVF-PQ) for every query that probes it, so a list
-// crosses HBM once per CTA instead of once per probing query.  Each
+// Both scans here are LIST-MAJOR: the [Q, nprobe] probe table is inverted
+// with the stable label sort (entries grouped by list), and a CTA scores a
+// list's rows (IVF-Flat) or codes (IVF-PQ) for a chunk of the queries that
+// probe it, so a list crosses HBM once per chunk instead of once per probing
+// query (IVF-Flat deals a popular list's chunks to several CTAs).  Each
 // (query, probed list) pair yields its best k (k <= 32, kept sorted in the
 // registers of one warp: lane i holds the i-th best), written to
 // out[probe slot][query][k]; the merge kernel (rdb_topk_merge) then keeps the
-// best k of the nprobe lists.
+// best k of the nprobe lists.  The IVF-PQ scan here serves code widths that
+// the query-major search (ivfpq.cu) does not.
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 
@@ -114,7 +116,9 @@ __global__ void __launch_bounds__(FNT) ivf_flat_scan_kernel(
     for (int l = blockIdx.x; l < nlist; l += gridDim.x) {
         const int64_t e0 = eseg[l], e1 = eseg[l + 1];
         const int64_t r0 = list_off[l], r1 = list_off[l + 1];
-        for (int64_t ec = e0; ec < e1; ec += FQ) {
+        // chunks of FQ probing queries, dealt round-robin to the gridDim.y
+        // CTAs of this list (a popular list is shared by several SMs)
+        for (int64_t ec = e0 + (int64_t)blockIdx.y * FQ; ec < e1; ec += (int64_t)gridDim.y * FQ) {
             const int nqc = (int)min((int64_t)FQ, e1 - ec);
             __syncthreads();
             if (tid < FQ) {
@@ -443,7 +447,9 @@ int rdb_ivf_flat_scan(int metric, int dtype, const void* q, int64_t nq, int64_t 
         }
         RDB_TRY(rdb_vec_values(metric, d, qv, nq, qv, s));
     }
-    const unsigned grid = (unsigned)std::min<int64_t>(nlist, 65535LL * 16);
+    // x: lists; y: CTAs sharing a list's query chunks, ~4x the mean chunk count
+    const int64_t mean_chunks = (nq * nprobe + (int64_t)nlist * FQ - 1) / ((int64_t)nlist * FQ);
+    const dim3 grid((unsigned)nlist, (unsigned)std::min<int64_t>(64, std::max<int64_t>(1, 4 * mean_chunks)));
     const int64_t* eperm = reinterpret_cast<const int64_t*>(base + w.off_perm);
     const int64_t* eseg = reinterpret_cast<const int64_t*>(base + w.off_seg);
     cudaEvent_t stop_ev;
