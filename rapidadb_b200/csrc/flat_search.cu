@@ -95,6 +95,7 @@ FlatPlan make_plan(int metric, int dtype, int64_t nq, int64_t n, int d, int k, i
     const int64_t smax = P.tc ? 131072 : 32768;
     int64_t S = 1024;
     while (S < sd && S < smax) S <<= 1;
+    while (S > 1024 && 4 * S > n) S >>= 1;  // at most a quarter of the rows
     while (S < 8LL * k) S <<= 1;
     P.sample = !(flags & RDB_SEARCH_EXHAUSTIVE) && n >= 4 * S;
     if (P.sample) {

@@ -1,4 +1,5 @@
-// Per-query top-k selection: one CTA per query.
+// Per-query top-k selection: one CTA per query, or one warp per query for
+// small outputs over few elements (select_warp_kernel).
 //
 // Every element gets a unique 64-bit key  (score key << 32) | index  that
 // sorts ascending best-first (csrc/kernels/topk.cu:25 semantics: sorted,
@@ -10,6 +11,8 @@
 // sort, which is the reference formula (csrc/kernels/distance.cu:414-438).
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
+
+#include <algorithm>
 
 #include "select.cuh"
 
@@ -332,6 +335,322 @@ __global__ void __launch_bounds__(NT) select_kernel(SelectArgs a) {
     }
 }
 
+// ---------------------------------------------------------------------------
+// Warp-per-query selection for small outputs (k + margin <= 128) over at most
+// kWarpSeg segments: eight queries per CTA, no block barriers, same keys and
+// results as select_kernel.  The want-th smallest score key s* is found by an
+// MSD radix select over the 32-bit score keys (8-bit digits, per-warp
+// shared-memory histogram); when more elements tie at s* than are needed, a
+// second radix select over their indices keeps the lowest.  Up to 1024
+// elements per query are held in registers; more are streamed from global
+// memory / L2 on every pass.  Winners are gathered in shared memory and
+// each goes to the output position given by its rank.
+
+constexpr int kWarpSeg = 64;
+constexpr int kWarpOut = 128;
+
+constexpr int kWarpCache = 1024;  // elements per query kept on chip
+
+struct WarpSel {
+    int seg_off[kWarpSeg + 1];
+    int hist[256];
+    int nsel;
+    unsigned long long sel[kWarpOut];
+    unsigned long long cache[kWarpCache];  // candidate / merge keys when T <= kWarpCache
+};
+
+// One histogram pass + bucket search.  Elements are offered through `each`
+// (calls fn(key64) for every element of the query).  Among elements with
+// pred(key), digit ((field(key) >> shift) & 255) is counted; returns the bucket
+// holding the remaining-th smallest field value and updates remaining / the
+// count of that bucket.
+template <class Each, class Pred, class Field>
+__device__ __forceinline__ uint32_t warp_radix_pass(WarpSel& W, int lane, Each&& each, Pred&& pred, Field&& field,
+                                                    int shift, uint32_t match_mask, uint32_t match_val,
+                                                    int& remaining, int& cnt_b) {
+    const unsigned FULLM = 0xffffffffu;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) W.hist[lane * 8 + i] = 0;
+    __syncwarp();
+    each([&](unsigned long long key) {
+        const uint32_t f = field(key);
+        if (pred(key) && (f & match_mask) == match_val) atomicAdd(&W.hist[(f >> shift) & 255u], 1);
+    });
+    __syncwarp();
+    int c[8], local = 0;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        c[i] = W.hist[lane * 8 + i];
+        local += c[i];
+    }
+    int incl = local;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const int v = __shfl_up_sync(FULLM, incl, o);
+        if (lane >= o) incl += v;
+    }
+    const int excl = incl - local;
+    const unsigned own = __ballot_sync(FULLM, excl < remaining && remaining <= incl);
+    const int src = own ? __ffs(own) - 1 : 31;
+    int b = 255, before = 0, cb = 0;
+    if (lane == src && own) {
+        before = excl;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            if (before + c[i] >= remaining) {
+                b = lane * 8 + i;
+                cb = c[i];
+                break;
+            }
+            before += c[i];
+        }
+    }
+    b = __shfl_sync(FULLM, b, src);
+    before = __shfl_sync(FULLM, before, src);
+    cb = __shfl_sync(FULLM, cb, src);
+    remaining -= before;
+    cnt_b = cb;
+    __syncwarp();
+    return static_cast<uint32_t>(b);
+}
+
+// want-th smallest 32-bit field among elements with pred (want >= 1 and at
+// most the number of such elements); fmin / fmax bound the field values.
+// Returns the value; remaining = how many elements equal to it are needed,
+// cnt_eq = how many there are.
+template <class Each, class Pred, class Field>
+__device__ __forceinline__ uint32_t warp_select32(WarpSel& W, int lane, Each&& each, Pred&& pred, Field&& field,
+                                                  uint32_t fmin, uint32_t fmax, int want, int& remaining,
+                                                  int& cnt_eq) {
+    uint32_t val = fmin;
+    remaining = want;
+    cnt_eq = 0;
+    const uint32_t diff = fmin ^ fmax;
+    int top = diff ? 32 - __clz(diff) : 0;  // bits >= top are common to all
+    if (top == 0) {
+        // a single value: count it
+        int n = 0;
+        each([&](unsigned long long key) { n += pred(key) ? 1 : 0; });
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) n += __shfl_xor_sync(0xffffffffu, n, o);
+        cnt_eq = n;
+        return val;
+    }
+    while (top > 0) {
+        const int shift = top > 8 ? top - 8 : 0;
+        const uint32_t match_mask = top >= 32 ? 0u : (0xffffffffu << top);
+        int cb = 0;
+        const uint32_t b = warp_radix_pass(W, lane, each, pred, field, shift, match_mask, val & match_mask, remaining,
+                                           cb);
+        const uint32_t dmask = (top - shift >= 32 ? 0xffffffffu : ((1u << (top - shift)) - 1u)) << shift;
+        val = (val & ~dmask) | (b << shift);
+        top = shift;
+        cnt_eq = cb;
+    }
+    return val;
+}
+
+__global__ void __launch_bounds__(NT, 2) select_warp_kernel(SelectArgs a) {
+    extern __shared__ __align__(16) unsigned char wsm[];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    WarpSel& W = reinterpret_cast<WarpSel*>(wsm)[warp];
+    const unsigned FULLM = 0xffffffffu;
+    const bool largest = a.largest != 0;
+    const int out_k_req = a.k + a.rescore_margin;
+    const int nseg = a.input == SEL_DENSE ? 1 : (a.input == SEL_MERGE ? a.G : a.nsplit);
+
+    for (int64_t q = (int64_t)blockIdx.x * NWARP + warp; q < a.nq; q += (int64_t)gridDim.x * NWARP) {
+        // ---- segment offsets (two segments per lane at most)
+        int len[2] = {0, 0};
+        bool ovf = false;
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            const int sgi = lane + 32 * h;
+            if (sgi < nseg) {
+                if (a.input == SEL_CANDIDATES) {
+                    const int c = a.counts[(int64_t)sgi * a.nq + q];
+                    ovf |= (int64_t)c > a.cap;
+                    len[h] = (int)min((int64_t)c, a.cap);
+                } else if (a.input == SEL_DENSE) {
+                    len[h] = (int)a.dense_n;
+                } else {
+                    len[h] = a.kin;
+                }
+            }
+        }
+        if (__any_sync(FULLM, ovf) && lane == 0 && a.overflow) atomicOr(a.overflow, 1u);
+        int base = 0;
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            int incl = len[h];
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const int v = __shfl_up_sync(FULLM, incl, o);
+                if (lane >= o) incl += v;
+            }
+            if (lane + 32 * h < kWarpSeg) W.seg_off[lane + 32 * h] = base + incl - len[h];
+            base += __shfl_sync(FULLM, incl, 31);
+        }
+        if (lane == 0) {
+            W.seg_off[min(nseg, kWarpSeg)] = base;
+            W.nsel = 0;
+        }
+        __syncwarp();
+        const int T = base;
+        const float qv = (a.input == SEL_CANDIDATES && a.qv) ? a.qv[q] : 0.f;
+        const int want = min(out_k_req, T);
+
+        // element keys: a dense row of <= kWarpCache scores in registers
+        // (element lane + 32 i: score key kh[i]), other inputs of
+        // <= kWarpCache elements copied once into W.cache, larger ones
+        // re-read from global memory / L2 on every pass
+        const int mode = T > kWarpCache ? 0 : (a.input == SEL_DENSE ? 1 : 2);
+        uint32_t kh[kWarpCache / 32];
+        if (mode == 1) {
+#pragma unroll
+            for (int i = 0; i < kWarpCache / 32; ++i) {
+                const int e = lane + 32 * i;
+                kh[i] = e < T ? score_key(a.dense[q * a.dense_n + e], largest) : 0xffffffffu;
+            }
+        } else if (mode == 2) {
+            for (int sgi = 0; sgi < nseg; ++sgi) {
+                const int o = W.seg_off[sgi], n = W.seg_off[sgi + 1] - o;
+                for (int t = lane; t < n; t += 32) W.cache[o + t] = seg_key(a, q, sgi, t, qv);
+            }
+            __syncwarp();
+        }
+        auto each = [&](auto&& fn) {
+            if (mode == 1) {
+#pragma unroll
+                for (int i = 0; i < kWarpCache / 32; ++i) {
+                    const int e = lane + 32 * i;
+                    if (e < T) fn((static_cast<unsigned long long>(kh[i]) << 32) | static_cast<uint32_t>(e));
+                }
+            } else if (mode == 2) {
+                for (int e = lane; e < T; e += 32) fn(W.cache[e]);
+            } else {
+                int sgc = 0;
+                for (int e = lane; e < T; e += 32) {
+                    while (e >= W.seg_off[sgc + 1]) ++sgc;
+                    fn(seg_key(a, q, sgc, e - W.seg_off[sgc], qv));
+                }
+            }
+        };
+        auto& each_score = each;
+        auto hi32 = [](unsigned long long key) { return static_cast<uint32_t>(key >> 32); };
+        auto lo32 = [](unsigned long long key) { return static_cast<uint32_t>(key); };
+        auto all = [](unsigned long long) { return true; };
+
+        // ---- s* = want-th smallest score key, then the index bound r* among ties
+        uint32_t s_star = 0xffffffffu, r_star = 0xffffffffu;
+        bool any = want > 0;
+        if (any && want < T) {
+            uint32_t mn = 0xffffffffu, mx = 0u;
+            each_score([&](unsigned long long key) {
+                mn = min(mn, hi32(key));
+                mx = max(mx, hi32(key));
+            });
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) {
+                mn = min(mn, __shfl_xor_sync(FULLM, mn, o));
+                mx = max(mx, __shfl_xor_sync(FULLM, mx, o));
+            }
+            int rem = 0, cnt_eq = 0;
+            s_star = warp_select32(W, lane, each_score, all, hi32, mn, mx, want, rem, cnt_eq);
+            if (a.output == SEL_OUT_TOPK && cnt_eq > rem) {
+                // more ties at s* than needed: keep the rem lowest indices
+                auto tie = [&](unsigned long long key) { return hi32(key) == s_star; };
+                uint32_t rmn = 0xffffffffu, rmx = 0u;
+                each([&](unsigned long long key) {
+                    if (tie(key)) {
+                        rmn = min(rmn, lo32(key));
+                        rmx = max(rmx, lo32(key));
+                    }
+                });
+#pragma unroll
+                for (int o = 16; o > 0; o >>= 1) {
+                    rmn = min(rmn, __shfl_xor_sync(FULLM, rmn, o));
+                    rmx = max(rmx, __shfl_xor_sync(FULLM, rmx, o));
+                }
+                int rem2 = 0, cnt2 = 0;
+                r_star = warp_select32(W, lane, each, tie, lo32, rmn, rmx, rem, rem2, cnt2);
+            }
+        }
+
+        if (a.output == SEL_OUT_THRESHOLD) {
+            // the k-th best score: s*, or the largest key when every element wins
+            uint32_t mx = 0u;
+            if (any && want >= T) {
+                each_score([&](unsigned long long key) { mx = max(mx, hi32(key)); });
+#pragma unroll
+                for (int o = 16; o > 0; o >>= 1) mx = max(mx, __shfl_xor_sync(FULLM, mx, o));
+            } else {
+                mx = s_star;
+            }
+            if (lane == 0)
+                a.out_thr[q] = (want >= a.k && want > 0) ? key_score(mx, largest) : (largest ? -INFINITY : INFINITY);
+            __syncwarp();
+            continue;
+        }
+
+        // ---- gather the winners: score < s*, or score == s* and index <= r*
+        each([&](unsigned long long key) {
+            const uint32_t h = hi32(key);
+            if (h < s_star || (h == s_star && lo32(key) <= r_star)) {
+                const int slot = atomicAdd(&W.nsel, 1);
+                if (slot < kWarpOut) W.sel[slot] = key;
+            }
+        });
+        __syncwarp();
+        const int nsel = min(W.nsel, kWarpOut);
+        // ---- exact L2 re-scoring of the winners (one winner per warp step)
+        if (a.rescore_margin > 0 && a.input == SEL_CANDIDATES && a.metric == RDB_METRIC_L2) {
+            for (int i = 0; i < nsel; ++i) {
+                const unsigned long long key = W.sel[i];
+                const uint32_t row = (uint32_t)key;
+                const int64_t prow = (int64_t)row * a.row_step;
+                float acc = 0.f;
+                for (int t = lane; t < a.d; t += 32) {
+                    const float df = load_as_float(a.dtype, a.qdata, q * a.ldq + t) -
+                                     load_as_float(a.dtype, a.xdata, prow * a.ldx + t);
+                    acc = fmaf(df, df, acc);
+                }
+#pragma unroll
+                for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(FULLM, acc, o);
+                if (lane == 0) W.sel[i] = ((unsigned long long)score_key(acc, false) << 32) | row;
+                __syncwarp();
+            }
+        }
+        // ---- winner i goes to position rank(i) = #winners with a smaller key
+        for (int i = lane; i < nsel; i += 32) {
+            const unsigned long long key = W.sel[i];
+            int rank = 0;
+            for (int j = 0; j < nsel; ++j) rank += W.sel[j] < key ? 1 : 0;
+            if (rank < a.k) {
+                const float v = key_score((uint32_t)(key >> 32), largest);
+                const uint32_t idx = (uint32_t)key;
+                int64_t id;
+                if (a.input == SEL_CANDIDATES) {
+                    const int64_t prow = (int64_t)idx * a.row_step;
+                    id = a.ids ? a.ids[prow] : prow + a.id_offset;
+                } else if (a.input == SEL_DENSE) {
+                    id = idx;
+                } else {
+                    const int g = idx / a.kin, t = idx % a.kin;
+                    id = a.merge_i[((int64_t)g * a.nq + q) * a.kin + t];
+                }
+                a.out_v[q * a.k + rank] = v;
+                a.out_i[q * a.k + rank] = id;
+            }
+        }
+        for (int i = nsel + lane; i < a.k; i += 32) {
+            a.out_v[q * a.k + i] = largest ? -INFINITY : INFINITY;
+            a.out_i[q * a.k + i] = -1;
+        }
+        __syncwarp();
+    }
+}
+
 }  // namespace
 
 int launch_select(const SelectArgs& a, cudaStream_t stream) {
@@ -353,6 +672,24 @@ int launch_select(const SelectArgs& a, cudaStream_t stream) {
         RDB_CUDA_TRY(cudaFuncSetAttribute(select_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                           (int)maxdyn));
         attr_set[dev] = true;
+    }
+    const int nseg = a.input == SEL_DENSE ? 1 : (a.input == SEL_MERGE ? a.G : a.nsplit);
+    // small outputs over few elements per query: one warp per query
+    const int64_t max_elems = a.input == SEL_DENSE ? a.dense_n
+                              : a.input == SEL_MERGE ? (int64_t)a.G * a.kin
+                                                     : a.cap * a.nsplit;
+    if (out_k <= kWarpOut && nseg <= kWarpSeg && max_elems <= 32768) {
+        const int64_t blocks = (a.nq + NWARP - 1) / NWARP;
+        static bool wattr[64] = {false};
+        if (dev < 64 && !wattr[dev]) {
+            RDB_CUDA_TRY(cudaFuncSetAttribute(select_warp_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                              (int)(sizeof(WarpSel) * NWARP)));
+            wattr[dev] = true;
+        }
+        select_warp_kernel<<<(unsigned)std::min<int64_t>(blocks, 65535LL * 16), NT, sizeof(WarpSel) * NWARP,
+                             stream>>>(a);
+        RDB_LAUNCH_CHECK();
+        return RDB_OK;
     }
     int64_t grid = a.nq < 65535 * 4 ? a.nq : 65535 * 4;
     select_kernel<<<(unsigned)grid, NT, smem, stream>>>(a);
