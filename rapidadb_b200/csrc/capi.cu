@@ -63,6 +63,21 @@ unsigned* device_status_word() {
     return words[dev];
 }
 
+// Four pinned host words per host thread (allocated on first use, kept until
+// exit) for asynchronous device-to-host reads of flags.
+unsigned* host_words() {
+    static thread_local unsigned* words = nullptr;
+    if (!words) {
+        void* p = nullptr;
+        if (cudaMallocHost(&p, 4 * sizeof(unsigned)) != cudaSuccess) {
+            cudaGetLastError();
+            return nullptr;
+        }
+        words = static_cast<unsigned*>(p);
+    }
+    return words;
+}
+
 struct Timing {
     int mask = 0;
     std::vector<std::pair<cudaEvent_t, cudaEvent_t>> ev;

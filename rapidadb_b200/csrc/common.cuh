@@ -15,6 +15,7 @@ namespace rdb {
 // Records a message for rdb_last_error() (thread-local) and returns `code`.
 int set_error(int code, const char* fmt, ...);
 void note_launch();
+unsigned* host_words();
 
 #define RDB_CHECK_ARG(cond, ...)                                   \
     do {                                                           \

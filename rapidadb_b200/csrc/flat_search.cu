@@ -123,6 +123,8 @@ FlatPlan make_plan(int metric, int dtype, int64_t nq, int64_t n, int d, int k, i
     size_t cnt_main = (size_t)P.m.nsplit * nq * sizeof(int);
     size_t cnt_samp = P.sample ? (size_t)P.s.nsplit * nq * sizeof(int) : 0;
     size_t off = 0;
+    P.off_flag = off;  // first in every plan: one overflow word for all query chunks
+    off = align_up(off + 16, 256);
     P.off_qv = off;
     off = align_up(off + nq * sizeof(float), 256);
     P.off_thr = off;
@@ -131,8 +133,6 @@ FlatPlan make_plan(int metric, int dtype, int64_t nq, int64_t n, int d, int k, i
     off = align_up(off + std::max(cand_main, cand_samp), 256);
     P.off_counts = off;
     off = align_up(off + std::max(cnt_main, cnt_samp), 256);
-    P.off_flag = off;
-    off = align_up(off + 16, 256);
     P.ws_bytes = off;
     return P;
 }
@@ -244,7 +244,6 @@ int run_chunk(const FlatPlan& P, int metric, int dtype, const void* q, int64_t n
         ss.overflow = nullptr;
         RDB_TRY(launch_select(ss, s));
     }
-    RDB_CUDA_TRY(cudaMemsetAsync(flag, 0, sizeof(unsigned), s));
     {
         ScanArgs sc = a;
         sc.n = n;
@@ -268,6 +267,9 @@ int run_chunk(const FlatPlan& P, int metric, int dtype, const void* q, int64_t n
         ss.id_offset = id_offset;
         ss.overflow = flag;
         ss.rescore_margin = metric == RDB_METRIC_L2 ? 16 : 0;
+        // candidates per query: ~1.1 n k / S under a sampled threshold
+        // (group maxima loosen it slightly), every row without one
+        ss.expect = P.sample ? (int64_t)(1.1 * (double)n * (double)k / (double)(P.s.rows)) + 1 : n;
         RDB_TRY(launch_select(ss, s));
     }
     return RDB_OK;
@@ -316,8 +318,11 @@ int rdb_flat_search(int metric, int dtype, const void* q, int64_t nq, int64_t ld
         return set_error(RDB_ERR_WORKSPACE, "workspace too small: %zu bytes, need %zu", ws_bytes,
                          P.ws_bytes);
     unsigned char* w = static_cast<unsigned char*>(ws);
-    unsigned* flag = reinterpret_cast<unsigned*>(w + P.off_flag);
-    unsigned any_overflow = 0;
+    // the overflow word sits at offset 0 of every chunk's plan: cleared once,
+    // or-ed by every chunk's select, read back with the device status word
+    // after the last chunk (one host synchronisation per call)
+    unsigned* flag = reinterpret_cast<unsigned*>(w);
+    RDB_CUDA_TRY(cudaMemsetAsync(flag, 0, sizeof(unsigned), s));
     const size_t es = elem_size(dtype);
     for (int64_t c0 = 0; c0 < nq; c0 += chunk) {
         int64_t cn = std::min(chunk, nq - c0);
@@ -325,19 +330,16 @@ int rdb_flat_search(int metric, int dtype, const void* q, int64_t nq, int64_t ld
         RDB_TRY(run_chunk(Pc, metric, dtype, static_cast<const char*>(q) + c0 * ldq * es, cn, ldq,
                           x, n, ldx, xv, d, k, ids, id_offset, out_d + c0 * k, out_i + c0 * k, w,
                           s));
-        unsigned h = 0;
-        RDB_CUDA_TRY(cudaMemcpyAsync(&h, w + Pc.off_flag, sizeof(unsigned), cudaMemcpyDeviceToHost, s));
-        RDB_CUDA_TRY(cudaStreamSynchronize(s));
-        any_overflow |= h;
     }
-    (void)flag;
+    unsigned* host = host_words();
+    if (!host) return set_error(RDB_ERR_CUDA, "cannot allocate pinned host words");
+    host[0] = host[1] = 0;
+    RDB_CUDA_TRY(cudaMemcpyAsync(&host[0], flag, sizeof(unsigned), cudaMemcpyDeviceToHost, s));
     unsigned* st = device_status_word();
-    if (st) {
-        unsigned hs = 0;
-        RDB_CUDA_TRY(cudaMemcpyAsync(&hs, st, sizeof(unsigned), cudaMemcpyDeviceToHost, s));
-        RDB_CUDA_TRY(cudaStreamSynchronize(s));
-        if (hs) return set_error(RDB_ERR_TIMEOUT, "a search kernel gave up on a device wait (status 0x%x)", hs);
-    }
+    if (st) RDB_CUDA_TRY(cudaMemcpyAsync(&host[1], st, sizeof(unsigned), cudaMemcpyDeviceToHost, s));
+    RDB_CUDA_TRY(cudaStreamSynchronize(s));
+    const unsigned any_overflow = host[0], hs = host[1];
+    if (hs) return set_error(RDB_ERR_TIMEOUT, "a search kernel gave up on a device wait (status 0x%x)", hs);
     if (any_overflow)
         return set_error(RDB_ERR_OVERFLOW, "candidate list overflow; repeat with RDB_SEARCH_EXHAUSTIVE");
     return RDB_OK;

@@ -257,8 +257,11 @@ __device__ __forceinline__ uint32_t map_to_rank(const void* p, uint32_t rank) {
     return r;
 }
 
-__device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
-    asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+// Relaxed arrive: it only has to follow this warp's completed TMEM loads
+// (tcgen05.wait::ld), not its candidate stores to global memory, so it does
+// not wait for those to drain as a release would.
+__device__ __forceinline__ void mbar_arrive_cluster_relaxed(uint32_t cluster_addr) {
+    asm volatile("mbarrier.arrive.relaxed.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
 }
 
 // 2-CTA tensor load: data lands in this CTA's shared memory, the transaction
@@ -701,7 +704,7 @@ __device__ __forceinline__ void tc_scan_body(uint8_t* smem_raw, const CUtensorMa
             }
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive_cluster(tempty_lead[acc]);
+            if (lane == 0) mbar_arrive_cluster_relaxed(tempty_lead[acc]);
             // publish the next tile's row values (its buffer was last read in
             // tile t - 1, which every epilogue thread has finished)
             if (t + 1 < ntiles) xv_s[((t + 1) & 1) * BN + etid] = xv_next;

@@ -678,7 +678,10 @@ int launch_select(const SelectArgs& a, cudaStream_t stream) {
     const int64_t max_elems = a.input == SEL_DENSE ? a.dense_n
                               : a.input == SEL_MERGE ? (int64_t)a.G * a.kin
                                                      : a.cap * a.nsplit;
-    if (out_k <= kWarpOut && nseg <= kWarpSeg && max_elems <= 32768) {
+    // a warp re-reads elements beyond its on-chip cache on every pass: larger
+    // expected inputs go to the CTA kernel
+    const bool small = a.expect > 0 ? a.expect <= kWarpCache : max_elems <= 32768;
+    if (out_k <= kWarpOut && nseg <= kWarpSeg && small) {
         const int64_t blocks = (a.nq + NWARP - 1) / NWARP;
         static bool wattr[64] = {false};
         if (dev < 64 && !wattr[dev]) {

@@ -51,6 +51,7 @@ struct SelectArgs {
     const int64_t* ids;   // physical row -> user id (NULL: row + id_offset)
     int64_t id_offset;
     unsigned* overflow;   // set to 1 when any count exceeded cap
+    int64_t expect;       // expected elements per query (0: unknown); picks the kernel
 
     // exact L2 rescoring of the selected rows (SEL_CANDIDATES, metric L2)
     int rescore_margin;  // extra rows selected before rescoring (0 = off)
