@@ -65,6 +65,22 @@ PassPlan plan_pass(int64_t rows, int64_t row_step, int64_t nq, int qtile, int rt
     int64_t nsplit = std::max<int64_t>(1, target / std::max<int64_t>(nqb, 1));
     nsplit = std::min<int64_t>(nsplit, std::max<int64_t>(ntiles, 1));
     nsplit = std::min<int64_t>(nsplit, 1024);
+    // (query block, split) units run in waves of `target`; a CTA's time is
+    // about (its tiles + 1) per wave.  When the one-wave split leaves many
+    // SMs idle (nqb not dividing target), more splits over several waves can
+    // balance better: take the split count with the least modelled time if
+    // it gains more than 3 %
+    {
+        auto cost = [&](int64_t ns) {
+            const int64_t waves = (nqb * ns + target - 1) / target;
+            return (double)waves * (double)((ntiles + ns - 1) / ns + 1);
+        };
+        int64_t best = nsplit;
+        double best_t = cost(nsplit);
+        for (int64_t ns = 1; ns <= std::min<int64_t>(std::max<int64_t>(ntiles, 1), 64); ++ns)
+            if (cost(ns) < best_t * 0.97 && cost(ns) < cost(best)) best = ns;
+        nsplit = best;
+    }
     int64_t tiles_per = (ntiles + nsplit - 1) / nsplit;
     p.rps = std::max<int64_t>(tiles_per, 1) * rtile;
     p.nsplit = (int)std::max<int64_t>(1, (rows + p.rps - 1) / p.rps);
