@@ -395,7 +395,13 @@ def run_ours(args, wl):
                 "peak": peak,
                 "unit": "TFLOP/s",
                 "frac": round(achieved / peak, 4) if achieved else None,
-                "traffic": None,
+                # DRAM bytes of one main-scan launch: ncu capture of the
+                # 262,144-row launch (profiles/tc_scan_flat_262kx768_full.md:
+                # 408.7 MB read + 9.4 MB written = 1,595 B per row) scaled by
+                # the rows of this launch; bf16 tensor-core path only
+                "traffic": (round(1595.0 * n_local) if wl["precision"] != "fp32" else None),
+                "traffic_source": ("ncu dram__bytes_read.sum + dram__bytes_write.sum of a 262,144-row "
+                                   "launch, scaled by rows" if wl["precision"] != "fp32" else None),
                 "kernel": ("tc_scan_pair_kernel<FILTER> (CTA pair, main pass)" if Q > 128
                            else "tc_scan_kernel<FILTER> (main pass)"),
                 "kernel_ms": round(kernel_ms, 4),
