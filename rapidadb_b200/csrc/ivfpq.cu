@@ -41,6 +41,7 @@ constexpr int SNT = 512;
 constexpr int SNW = SNT / 32;
 constexpr int kMaxPqK = 32;
 constexpr int kMaxPqProbe = 4096;
+constexpr int RPL = 4;  // rows per lane in a scan chunk (chunks of 128 rows)
 constexpr int kMaxPqSmem = 227 * 1024;
 
 inline size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
@@ -170,7 +171,8 @@ __global__ void __launch_bounds__(SNT, (M <= 32 ? 2 : 1)) ivfpq_search_kernel(
             }
             r0s[p] = r0;
             r1s[p] = r1;
-            pfx[p + 1] = r1 > r0 ? static_cast<int>((r1 - (r0 & ~31u) + 31u) >> 5) : 0;  // 32-row chunks
+            // chunks of 32 * RPL rows from the 32-aligned row at or below r0
+            pfx[p + 1] = r1 > r0 ? static_cast<int>((r1 - (r0 & ~31u) + (32u * RPL - 1)) / (32u * RPL)) : 0;
         }
         __syncthreads();
         if (warp == 0) {
@@ -247,66 +249,65 @@ __global__ void __launch_bounds__(SNT, (M <= 32 ? 2 : 1)) ivfpq_search_kernel(
         }
         __syncthreads();
 
-        // ---- scan: warps take 32-row chunks of the probed lists in turn (the
-        // 16 warps of a CTA read 16 consecutive chunks together); the codes
-        // and row term of a warp's next chunk are loaded before its current
-        // chunk is scored (two chunks in flight per warp)
+        // ---- scan: warps take chunks of 32 * RPL rows of the probed lists in
+        // turn (the 16 warps of a CTA read 16 consecutive chunks together);
+        // lane L scores rows L, L + 32, ... of its chunk (all rotated alike)
         WarpKeys tk;
         tk.init();
         float kth_d = INFINITY;  // distance of the warp's current k-th best
         const int total = pfx[nprobe];
         int p = 0;
-        auto locate = [&](int c, int& pc, uint32_t& row, uint32_t& rr) {
-            while (pfx[pc + 1] <= c) ++pc;
-            const uint32_t r0 = r0s[pc];
-            row = (r0 & ~31u) + 32u * static_cast<uint32_t>(c - pfx[pc]) + static_cast<uint32_t>(lane);
-            // rows outside the list read the list's first row (always valid)
-            // and are masked from the top-k
-            rr = (row >= r0 && row < r1s[pc]) ? row : r0;
-        };
-        uint32_t row = 0, rr = 0;
-        uint32_t cw[M / 4];
-        float term = 0.f;
-        if (warp < total) {
-            locate(warp, p, row, rr);
-            load_codes<M>(codes + static_cast<size_t>(rr) * M, cw);
-            term = __ldg(row_terms + rr);
-        }
         for (int c = warp; c < total; c += SNW) {
-            int pn = p;
-            uint32_t rown = 0, rrn = 0;
-            uint32_t cwn[M / 4];
-            float termn = 0.f;
-            if (c + SNW < total) {
-                locate(c + SNW, pn, rown, rrn);
-                load_codes<M>(codes + static_cast<size_t>(rrn) * M, cwn);
-                termn = __ldg(row_terms + rrn);
+            while (pfx[p + 1] <= c) ++p;
+            const uint32_t r0 = r0s[p], r1 = r1s[p];
+            const uint32_t base = (r0 & ~31u) + 32u * RPL * static_cast<uint32_t>(c - pfx[p]) + lane;
+            uint32_t cw[RPL][M / 4];
+            float term[RPL];
+            bool valid[RPL];
+#pragma unroll
+            for (int h = 0; h < RPL; ++h) {
+                const uint32_t row = base + 32u * h;
+                valid[h] = row >= r0 && row < r1;
+                // rows outside the list read the list's first row (always
+                // valid) and are masked from the top-k
+                const uint32_t rr = valid[h] ? row : r0;
+                load_codes<M>(codes + static_cast<size_t>(rr) * M, cw[h]);
+                term[h] = __ldg(row_terms + rr);
             }
-            uint32_t acc = 0;  // two's-complement sum of the fixed-point entries
+            uint32_t acc[RPL];
+#pragma unroll
+            for (int h = 0; h < RPL; ++h) acc[h] = 0;  // two's-complement sums of fixed-point entries
 #pragma unroll
             for (int g = 0; g < L::NG; ++g) {
 #pragma unroll
                 for (int s = 0; s < L::G; ++s) {
                     const int b = g * L::G + s;
-                    // byte 0: this lane's word offset, byte 1: the code (= code * 256 bytes)
-                    const uint32_t a = __byte_perm(cw[b >> 2], lane_off, 0x5504u | ((b & 3) << 4));
-                    acc += *reinterpret_cast<const uint32_t*>(pq_shared + a + 4 * (g * kGroupWords + L::NC * s));
+#pragma unroll
+                    for (int h = 0; h < RPL; ++h) {
+                        // byte 0: this lane's word offset, byte 1: the code (= code * 256 bytes)
+                        const uint32_t a = __byte_perm(cw[h][b >> 2], lane_off, 0x5504u | ((b & 3) << 4));
+                        acc[h] += *reinterpret_cast<const uint32_t*>(pq_shared + a + 4 * (g * kGroupWords + L::NC * s));
+                    }
                 }
             }
-            const bool valid = rr == row;
-            const float dist = fmaf(static_cast<float>(static_cast<int>(acc)), inv_scale, t1[p] + term);
-            if (__any_sync(FULL, valid && dist <= kth_d)) {
-                const unsigned long long key =
-                    valid ? (static_cast<unsigned long long>(float_asc_key(dist)) << 32) | row : ~0ull;
-                tk.offer(key, valid, k, lane);
+            const float tl = t1[p];
+            float dist[RPL];
+            bool hit = false;
+#pragma unroll
+            for (int h = 0; h < RPL; ++h) {
+                dist[h] = fmaf(static_cast<float>(static_cast<int>(acc[h])), inv_scale, tl + term[h]);
+                hit |= valid[h] && dist[h] <= kth_d;
+            }
+            if (__any_sync(FULL, hit)) {
+#pragma unroll
+                for (int h = 0; h < RPL; ++h) {
+                    const unsigned long long key =
+                        valid[h] ? (static_cast<unsigned long long>(float_asc_key(dist[h])) << 32) | (base + 32u * h)
+                                 : ~0ull;
+                    tk.offer(key, valid[h], k, lane);
+                }
                 kth_d = tk.kth == ~0ull ? INFINITY : asc_key_float(static_cast<uint32_t>(tk.kth >> 32));
             }
-            p = pn;
-            row = rown;
-            rr = rrn;
-            term = termn;
-#pragma unroll
-            for (int i = 0; i < M / 4; ++i) cw[i] = cwn[i];
         }
         if (lane < k) mk[warp * kMaxPqK + lane] = tk.key;
         __syncthreads();
