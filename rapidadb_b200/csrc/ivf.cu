@@ -92,26 +92,62 @@ __global__ void probe_to_labels_kernel(const int64_t* __restrict__ probe, int64_
 }
 
 // ------------------------------------------------------------- IVF-Flat scan
+//
+// CTA = one list x a chunk of FQ = 32 probing queries, rows walked in tiles
+// of FR = 256 over K chunks of FK = 32 staged in shared memory (the next
+// chunk loaded into registers while the current one is consumed).  Warp w
+// computes queries 8 (w mod 4) .. + 7 against rows 128 (w / 4) + lane + 32 j
+// (j < 4): query operands are shared-memory broadcasts, each lane loads 4 row
+// values per k for 32 multiply-adds.  The tile's scores go through shared
+// memory to the per-query warp top-k lists (warp w keeps queries 4 w .. + 3).
 
 constexpr int FQ = 32;   // queries per chunk
-constexpr int FR = 128;  // rows per tile
+constexpr int FR = 256;  // rows per tile
 constexpr int FK = 32;   // K chunk
 constexpr int FNT = 256;
+constexpr int FXS = FR + 1;  // row stride of the transposed row tile
 
 template <typename T>
-__global__ void __launch_bounds__(FNT) ivf_flat_scan_kernel(
+__device__ __forceinline__ float4 load4f(const T* p, bool vec, int nvalid) {
+    if (vec && nvalid >= 4) {
+        if constexpr (sizeof(T) == 4) {
+            return __ldg(reinterpret_cast<const float4*>(p));
+        } else {
+            const uint2 u = __ldg(reinterpret_cast<const uint2*>(p));
+            const T* e = reinterpret_cast<const T*>(&u);
+            return make_float4(to_f<T>(e[0]), to_f<T>(e[1]), to_f<T>(e[2]), to_f<T>(e[3]));
+        }
+    }
+    float v[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) v[i] = i < nvalid ? to_f<T>(p[i]) : 0.f;
+    return make_float4(v[0], v[1], v[2], v[3]);
+}
+
+struct IvfFlatSmem {
+    float Qs[FK][FQ];
+    float Xs[FK][FXS];
+    float S[FQ][FXS];
+    int64_t s_q[FQ];
+    int s_p[FQ];
+    float s_qv[FQ];
+};
+
+template <typename T>
+__global__ void __launch_bounds__(FNT, 2) ivf_flat_scan_kernel(
     int metric, int cos_small, const T* __restrict__ q, int64_t Q, int64_t ldq, int d, const float* __restrict__ qv,
     int nprobe, const int64_t* __restrict__ eperm, const int64_t* __restrict__ eseg, const T* __restrict__ rows,
     int64_t ldx, const float* __restrict__ xv, const int64_t* __restrict__ list_off, int nlist,
     const int64_t* __restrict__ ids, int k, float* __restrict__ out_v, int64_t* __restrict__ out_i) {
-    __shared__ float Qs[FK][FQ];
-    __shared__ float Xs[FK][FR + 4];
-    __shared__ float S[FQ][FR + 1];
-    __shared__ int64_t s_q[FQ];
-    __shared__ int s_p[FQ];
-    __shared__ float s_qv[FQ];
+    extern __shared__ __align__(16) unsigned char ivf_smem[];
+    IvfFlatSmem& sh = *reinterpret_cast<IvfFlatSmem*>(ivf_smem);
     const bool largest = metric != RDB_METRIC_L2;
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, tq = tid >> 5, tr = tid & 31;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int qg = (warp & 3) * 8;     // this warp's first query
+    const int rb = (warp >> 2) * 128;  // this warp's first tile row
+    const int sq = tid >> 3, sk = (tid & 7) * 4;  // staging: query / row t / 8 (+ 32 i), k 4 (t mod 8)
+    const bool vec_q = (reinterpret_cast<uintptr_t>(q) % 16 == 0) && (ldq % 4 == 0);
+    const bool vec_x = (reinterpret_cast<uintptr_t>(rows) % 16 == 0) && (ldx % 4 == 0);
 
     for (int l = blockIdx.x; l < nlist; l += gridDim.x) {
         const int64_t e0 = eseg[l], e1 = eseg[l + 1];
@@ -124,78 +160,90 @@ __global__ void __launch_bounds__(FNT) ivf_flat_scan_kernel(
             if (tid < FQ) {
                 if (tid < nqc) {
                     const int64_t e = eperm[ec + tid];
-                    s_q[tid] = e / nprobe;
-                    s_p[tid] = (int)(e % nprobe);
-                    s_qv[tid] = qv ? qv[e / nprobe] : 0.f;
+                    sh.s_q[tid] = e / nprobe;
+                    sh.s_p[tid] = (int)(e % nprobe);
+                    sh.s_qv[tid] = qv ? qv[e / nprobe] : 0.f;
                 } else {
-                    s_q[tid] = -1;
-                    s_p[tid] = 0;
-                    s_qv[tid] = 0.f;
+                    sh.s_q[tid] = -1;
+                    sh.s_p[tid] = 0;
+                    sh.s_qv[tid] = 0.f;
                 }
             }
             WarpTopK st[4];
 #pragma unroll
             for (int j = 0; j < 4; ++j) st[j].init(largest);
             __syncthreads();
+            const int64_t my_q = sh.s_q[sq];
             for (int64_t t0 = r0; t0 < r1; t0 += FR) {
-                float acc[4][4];
+                float acc[8][4];
 #pragma unroll
-                for (int i = 0; i < 4; ++i)
+                for (int i = 0; i < 8; ++i)
 #pragma unroll
                     for (int j = 0; j < 4; ++j) acc[i][j] = 0.f;
+                float4 pq, px[8];
+                auto fetch = [&](int k0) {
+                    const int kx = k0 + sk;
+                    const int nv = min(4, d - kx);
+                    pq = (my_q >= 0 && nv > 0) ? load4f<T>(q + my_q * ldq + kx, vec_q, nv)
+                                               : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+                    for (int i = 0; i < 8; ++i) {
+                        const int64_t r = t0 + sq + 32 * i;
+                        px[i] = (r < r1 && nv > 0) ? load4f<T>(rows + r * ldx + kx, vec_x, nv)
+                                                   : make_float4(0.f, 0.f, 0.f, 0.f);
+                    }
+                };
+                fetch(0);
                 for (int k0 = 0; k0 < d; k0 += FK) {
-                    __syncthreads();
-                    {
-                        const int qi = tid >> 3, kk = (tid & 7) * 4;
-                        const int64_t qq = s_q[qi];
+                    __syncthreads();  // the previous chunk (and tile's scores) are consumed
+                    sh.Qs[sk + 0][sq] = pq.x;
+                    sh.Qs[sk + 1][sq] = pq.y;
+                    sh.Qs[sk + 2][sq] = pq.z;
+                    sh.Qs[sk + 3][sq] = pq.w;
 #pragma unroll
-                        for (int i = 0; i < 4; ++i) {
-                            const int kx = k0 + kk + i;
-                            Qs[kk + i][qi] = (qq >= 0 && kx < d) ? to_f<T>(q[qq * ldq + kx]) : 0.f;
-                        }
-                    }
-                    {
-                        const int ri = tid >> 1, kk = (tid & 1) * 16;
-                        const int64_t r = t0 + ri;
-                        const bool rv = r < r1;
-#pragma unroll
-                        for (int i = 0; i < 16; ++i) {
-                            const int kx = k0 + kk + i;
-                            Xs[kk + i][ri] = (rv && kx < d) ? to_f<T>(rows[r * ldx + kx]) : 0.f;
-                        }
+                    for (int i = 0; i < 8; ++i) {
+                        sh.Xs[sk + 0][sq + 32 * i] = px[i].x;
+                        sh.Xs[sk + 1][sq + 32 * i] = px[i].y;
+                        sh.Xs[sk + 2][sq + 32 * i] = px[i].z;
+                        sh.Xs[sk + 3][sq + 32 * i] = px[i].w;
                     }
                     __syncthreads();
-#pragma unroll 8
+                    if (k0 + FK < d) fetch(k0 + FK);
+#pragma unroll 4
                     for (int kk = 0; kk < FK; ++kk) {
-                        const float4 av = *reinterpret_cast<const float4*>(&Qs[kk][tq * 4]);
-                        const float a_[4] = {av.x, av.y, av.z, av.w};
-                        float b_[4];
+                        const float4 a0 = *reinterpret_cast<const float4*>(&sh.Qs[kk][qg]);
+                        const float4 a1 = *reinterpret_cast<const float4*>(&sh.Qs[kk][qg + 4]);
+                        const float av[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+                        float bv[4];
 #pragma unroll
-                        for (int j = 0; j < 4; ++j) b_[j] = Xs[kk][tr + 32 * j];
+                        for (int j = 0; j < 4; ++j) bv[j] = sh.Xs[kk][rb + lane + 32 * j];
 #pragma unroll
-                        for (int i = 0; i < 4; ++i)
+                        for (int i = 0; i < 8; ++i)
 #pragma unroll
                             for (int j = 0; j < 4; ++j) {
                                 if (metric == RDB_METRIC_L2) {
-                                    const float df = a_[i] - b_[j];
+                                    const float df = av[i] - bv[j];
                                     acc[i][j] = fmaf(df, df, acc[i][j]);
                                 } else {
-                                    acc[i][j] = fmaf(a_[i], b_[j], acc[i][j]);
+                                    acc[i][j] = fmaf(av[i], bv[j], acc[i][j]);
                                 }
                             }
                     }
                 }
                 // final scores of the tile -> S
 #pragma unroll
-                for (int i = 0; i < 4; ++i)
+                for (int j = 0; j < 4; ++j) {
+                    const int ri = rb + lane + 32 * j;
+                    const int64_t r = t0 + ri;
+                    const float xr = (metric == RDB_METRIC_COSINE && r < r1) ? xv[r] : 0.f;
 #pragma unroll
-                    for (int j = 0; j < 4; ++j) {
-                        const int qi = tq * 4 + i, ri = tr + 32 * j;
-                        const int64_t r = t0 + ri;
+                    for (int i = 0; i < 8; ++i) {
+                        const int qi = qg + i;
                         float sc = acc[i][j];
-                        if (metric == RDB_METRIC_COSINE && r < r1) sc = final_score(metric, cos_small, sc, s_qv[qi], xv[r]);
-                        S[qi][ri] = sc;
+                        if (metric == RDB_METRIC_COSINE && r < r1) sc = final_score(metric, cos_small, sc, sh.s_qv[qi], xr);
+                        sh.S[qi][ri] = sc;
                     }
+                }
                 __syncthreads();
                 // warp w keeps queries 4w .. 4w + 3
 #pragma unroll
@@ -204,7 +252,7 @@ __global__ void __launch_bounds__(FNT) ivf_flat_scan_kernel(
 #pragma unroll
                     for (int b = 0; b < FR / 32; ++b) {
                         const int64_t r = t0 + 32 * b + lane;
-                        st[j].offer(S[qi][32 * b + lane], r, r < r1, k, largest, lane);
+                        st[j].offer(sh.S[qi][32 * b + lane], r, r < r1, k, largest, lane);
                     }
                 }
             }
@@ -212,9 +260,9 @@ __global__ void __launch_bounds__(FNT) ivf_flat_scan_kernel(
 #pragma unroll
             for (int j = 0; j < 4; ++j) {
                 const int qi = warp * 4 + j;
-                const int64_t qq = s_q[qi];
+                const int64_t qq = sh.s_q[qi];
                 if (qq >= 0 && lane < k) {
-                    const int64_t o = ((int64_t)s_p[qi] * Q + qq) * k + lane;
+                    const int64_t o = ((int64_t)sh.s_p[qi] * Q + qq) * k + lane;
                     const bool has = st[j].id != INT64_MAX;
                     out_v[o] = st[j].v;
                     out_i[o] = has ? (ids ? ids[st[j].id] : st[j].id) : -1;
@@ -452,21 +500,34 @@ int rdb_ivf_flat_scan(int metric, int dtype, const void* q, int64_t nq, int64_t 
     const dim3 grid((unsigned)nlist, (unsigned)std::min<int64_t>(64, std::max<int64_t>(1, 4 * mean_chunks)));
     const int64_t* eperm = reinterpret_cast<const int64_t*>(base + w.off_perm);
     const int64_t* eseg = reinterpret_cast<const int64_t*>(base + w.off_seg);
+    {
+        static bool attr[64] = {false};
+        int dev = 0;
+        cudaGetDevice(&dev);
+        if (dev < 64 && !attr[dev]) {
+            const int bytes = (int)sizeof(IvfFlatSmem);
+            RDB_CUDA_TRY(cudaFuncSetAttribute(ivf_flat_scan_kernel<float>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes));
+            RDB_CUDA_TRY(cudaFuncSetAttribute(ivf_flat_scan_kernel<__half>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes));
+            RDB_CUDA_TRY(cudaFuncSetAttribute(ivf_flat_scan_kernel<__nv_bfloat16>,
+                                              cudaFuncAttributeMaxDynamicSharedMemorySize, bytes));
+            attr[dev] = true;
+        }
+    }
     cudaEvent_t stop_ev;
     RDB_TRY(timing_begin(TIMING_IVF_SCAN, s, &stop_ev));
     switch (dtype) {
         case RDB_F32:
-            ivf_flat_scan_kernel<float><<<grid, FNT, 0, s>>>(metric, cos_small, (const float*)q, nq, ldq, d, qv, nprobe,
+            ivf_flat_scan_kernel<float><<<grid, FNT, sizeof(IvfFlatSmem), s>>>(metric, cos_small, (const float*)q, nq, ldq, d, qv, nprobe,
                                                              eperm, eseg, (const float*)rows, ldx, xv, list_off, nlist,
                                                              ids, k, out_v, out_i);
             break;
         case RDB_F16:
-            ivf_flat_scan_kernel<__half><<<grid, FNT, 0, s>>>(metric, cos_small, (const __half*)q, nq, ldq, d, qv,
+            ivf_flat_scan_kernel<__half><<<grid, FNT, sizeof(IvfFlatSmem), s>>>(metric, cos_small, (const __half*)q, nq, ldq, d, qv,
                                                               nprobe, eperm, eseg, (const __half*)rows, ldx, xv,
                                                               list_off, nlist, ids, k, out_v, out_i);
             break;
         default:
-            ivf_flat_scan_kernel<__nv_bfloat16><<<grid, FNT, 0, s>>>(
+            ivf_flat_scan_kernel<__nv_bfloat16><<<grid, FNT, sizeof(IvfFlatSmem), s>>>(
                 metric, cos_small, (const __nv_bfloat16*)q, nq, ldq, d, qv, nprobe, eperm, eseg,
                 (const __nv_bfloat16*)rows, ldx, xv, list_off, nlist, ids, k, out_v, out_i);
     }

@@ -67,7 +67,7 @@ int launch_scan_tc(const ScanArgs& a, int mode, cudaStream_t stream);
 bool tc_use_pair(int64_t nq);
 
 // Row tiles of the two kernels (rows_per_split must be a multiple).
-constexpr int kSimtRows = 128;
+constexpr int kSimtRows = 256;
 constexpr int kSimtQueries = 32;
 constexpr int kTcRows = 256;
 constexpr int kTcQueries = 128;

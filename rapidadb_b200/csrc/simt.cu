@@ -2,7 +2,7 @@
 // (the raw ops of csrc/kernels/distance.cu), and the fused fp32 scan used by
 // flat search for fp32 storage.
 //
-// The scan tiles 32 queries x 128 rows per CTA (256 threads, 4 x 4 outputs per
+// The scan tiles 32 queries x 256 rows per CTA (256 threads, 8 x 4 outputs per
 // thread) over K chunks of 32 staged through shared memory; each CTA walks a
 // contiguous split of rows so its per-query candidate counters stay private.
 #include <cuda_bf16.h>
@@ -49,16 +49,44 @@ __global__ void vec_values_kernel(int metric, int cos_small, const float* sq, in
 }
 
 // --------------------------------------------------------------- scan --
+//
+// CTA tile: 32 queries x 256 rows, 256 threads, K chunks of 32 staged in
+// shared memory (the next chunk is loaded into registers while the current
+// one is consumed).  Warp w owns queries 8 (w mod 4) .. + 7 and rows
+// 128 (w / 4) + lane + 32 j (j < 4): its query operands are shared-memory
+// broadcasts (two 16-byte loads per k) and each lane loads 4 row values per
+// k for 32 multiply-adds.
 
 constexpr int BQ = kSimtQueries;  // 32
-constexpr int BN = kSimtRows;     // 128
+constexpr int BN = kSimtRows;     // 256
 constexpr int BK = 32;
 constexpr int NT = 256;
+constexpr int XS = BN + 1;  // Xs row stride (conflict-free transposing stores)
+static_assert(BQ == 32 && BN == 256, "thread mapping assumes 32 x 256 tiles");
+
+// four consecutive elements (k .. k + 3 < kmax) as floats; vector loads when
+// the caller knows the address is aligned
+template <typename T>
+__device__ __forceinline__ float4 load4(const T* p, bool vec, int nvalid) {
+    if (vec && nvalid >= 4) {
+        if constexpr (sizeof(T) == 4) {
+            return __ldg(reinterpret_cast<const float4*>(p));
+        } else {
+            const uint2 u = __ldg(reinterpret_cast<const uint2*>(p));
+            const T* e = reinterpret_cast<const T*>(&u);
+            return make_float4(to_f<T>(e[0]), to_f<T>(e[1]), to_f<T>(e[2]), to_f<T>(e[3]));
+        }
+    }
+    float v[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) v[i] = i < nvalid ? to_f<T>(p[i]) : 0.f;
+    return make_float4(v[0], v[1], v[2], v[3]);
+}
 
 template <typename T, int MODE, bool DIRECT_L2>
-__global__ void __launch_bounds__(NT) simt_scan_kernel(ScanArgs a) {
-    __shared__ float Qs[BK][BQ];
-    __shared__ float Xs[BK][BN + 4];
+__global__ void __launch_bounds__(NT, 2) simt_scan_kernel(ScanArgs a) {
+    __shared__ __align__(16) float Qs[BK][BQ];
+    __shared__ float Xs[BK][XS];
     __shared__ float sA[BQ], sB[BQ], sQv[BQ];
     __shared__ int scnt[BQ];
     __shared__ unsigned long long sbest[BQ];
@@ -71,7 +99,12 @@ __global__ void __launch_bounds__(NT) simt_scan_kernel(ScanArgs a) {
     if (q0 >= a.nq) return;
     const int64_t r_begin = (int64_t)split * a.rows_per_split;
     const int64_t r_end = min(a.n, r_begin + a.rows_per_split);
-    const int tid = threadIdx.x, tq = tid >> 5, tr = tid & 31;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int qg = (warp & 3) * 8;     // first query of this warp
+    const int rb = (warp >> 2) * 128;  // first row (in the tile) of this warp
+    const int64_t xstride = a.ldx * a.row_step;
+    const bool vec_q = (reinterpret_cast<uintptr_t>(qp) % 16 == 0) && (a.ldq % 4 == 0);
+    const bool vec_x = (reinterpret_cast<uintptr_t>(xp) % 16 == 0) && (xstride % 4 == 0);
 
     if (tid < BQ) {
         int64_t q = q0 + tid;
@@ -84,104 +117,134 @@ __global__ void __launch_bounds__(NT) simt_scan_kernel(ScanArgs a) {
         scnt[tid] = 0;
         sbest[tid] = ~0ull;
     }
-
-    for (int64_t r0 = r_begin; r0 < r_end; r0 += BN) {
-        float acc[4][4];
-        float qsq[4], xsq[4];
+    // ARGMIN: best (distance key, row) of each of this thread's 8 queries
+    unsigned long long best[8];
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
+    for (int i = 0; i < 8; ++i) best[i] = ~0ull;
+
+    // staging map: queries -> thread (query t / 8, k 4 (t mod 8) .. + 3);
+    // rows -> thread (rows t / 8 + 32 i, same k)
+    const int sq = tid >> 3, sk = (tid & 7) * 4;
+    for (int64_t r0 = r_begin; r0 < r_end; r0 += BN) {
+        float acc[8][4];
+        float qsq[8], xsq[4];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
             qsq[i] = 0.f;
-            xsq[i] = 0.f;
 #pragma unroll
             for (int j = 0; j < 4; ++j) acc[i][j] = 0.f;
         }
+#pragma unroll
+        for (int j = 0; j < 4; ++j) xsq[j] = 0.f;
+
+        float4 pq, px[8];
+        auto fetch = [&](int k0) {
+            const int k = k0 + sk;
+            const int nv = min(4, a.d - k);
+            const int64_t q = q0 + sq;
+            pq = (q < a.nq && nv > 0) ? load4<T>(qp + q * a.ldq + k, vec_q, nv) : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                const int64_t r = r0 + sq + 32 * i;
+                px[i] = (r < r_end && nv > 0) ? load4<T>(xp + r * xstride + k, vec_x, nv)
+                                             : make_float4(0.f, 0.f, 0.f, 0.f);
+            }
+        };
+        fetch(0);
         for (int k0 = 0; k0 < a.d; k0 += BK) {
-            __syncthreads();
-            {  // queries: thread -> (query tid / 8, 4 consecutive k)
-                int qi = tid >> 3, kk = (tid & 7) * 4;
-                int64_t q = q0 + qi;
+            __syncthreads();  // the previous chunk is consumed
+            Qs[sk + 0][sq] = pq.x;
+            Qs[sk + 1][sq] = pq.y;
+            Qs[sk + 2][sq] = pq.z;
+            Qs[sk + 3][sq] = pq.w;
 #pragma unroll
-                for (int i = 0; i < 4; ++i) {
-                    int k = k0 + kk + i;
-                    Qs[kk + i][qi] = (q < a.nq && k < a.d) ? to_f<T>(qp[q * a.ldq + k]) : 0.f;
-                }
-            }
-            {  // rows: thread -> (row tid / 2, 16 consecutive k)
-                int ri = tid >> 1, kk = (tid & 1) * 16;
-                int64_t r = r0 + ri;
-                bool rv = r < r_end;
-                const T* src = xp + r * a.row_step * a.ldx + k0 + kk;
-#pragma unroll
-                for (int i = 0; i < 16; ++i) {
-                    int k = k0 + kk + i;
-                    Xs[kk + i][ri] = (rv && k < a.d) ? to_f<T>(src[i]) : 0.f;
-                }
+            for (int i = 0; i < 8; ++i) {
+                Xs[sk + 0][sq + 32 * i] = px[i].x;
+                Xs[sk + 1][sq + 32 * i] = px[i].y;
+                Xs[sk + 2][sq + 32 * i] = px[i].z;
+                Xs[sk + 3][sq + 32 * i] = px[i].w;
             }
             __syncthreads();
-#pragma unroll 8
+            if (k0 + BK < a.d) fetch(k0 + BK);
+#pragma unroll 4
             for (int kk = 0; kk < BK; ++kk) {
-                float4 av = *reinterpret_cast<const float4*>(&Qs[kk][tq * 4]);
-                float av_[4] = {av.x, av.y, av.z, av.w};
+                const float4 a0 = *reinterpret_cast<const float4*>(&Qs[kk][qg]);
+                const float4 a1 = *reinterpret_cast<const float4*>(&Qs[kk][qg + 4]);
+                const float av[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
                 float bv[4];
 #pragma unroll
-                for (int j = 0; j < 4; ++j) bv[j] = Xs[kk][tr + 32 * j];
+                for (int j = 0; j < 4; ++j) bv[j] = Xs[kk][rb + lane + 32 * j];
 #pragma unroll
-                for (int i = 0; i < 4; ++i)
+                for (int i = 0; i < 8; ++i)
 #pragma unroll
                     for (int j = 0; j < 4; ++j) {
                         if (DIRECT_L2) {
-                            float df = av_[i] - bv[j];
+                            const float df = av[i] - bv[j];
                             acc[i][j] = fmaf(df, df, acc[i][j]);
                         } else {
-                            acc[i][j] = fmaf(av_[i], bv[j], acc[i][j]);
+                            acc[i][j] = fmaf(av[i], bv[j], acc[i][j]);
                         }
                     }
                 if (MODE == SCAN_DENSE && !DIRECT_L2 && a.metric == RDB_METRIC_COSINE) {
 #pragma unroll
-                    for (int i = 0; i < 4; ++i) qsq[i] = fmaf(av_[i], av_[i], qsq[i]);
+                    for (int i = 0; i < 8; ++i) qsq[i] = fmaf(av[i], av[i], qsq[i]);
 #pragma unroll
                     for (int j = 0; j < 4; ++j) xsq[j] = fmaf(bv[j], bv[j], xsq[j]);
                 }
             }
         }
         // ---- epilogue ----
+        float xvr[4];
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-            int qi = tq * 4 + i;
-            int64_t q = q0 + qi;
+        for (int j = 0; j < 4; ++j) {
+            const int64_t r = r0 + rb + lane + 32 * j;
+            xvr[j] = (r < r_end && a.xv && MODE != SCAN_DENSE) ? a.xv[r * a.row_step] : 0.f;
+        }
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const int qi = qg + i;
+            const int64_t q = q0 + qi;
             if (q >= a.nq) continue;
 #pragma unroll
             for (int j = 0; j < 4; ++j) {
-                int64_t r = r0 + tr + 32 * j;
+                const int64_t r = r0 + rb + lane + 32 * j;
                 if (r >= r_end) continue;
-                float v = acc[i][j];
+                const float v = acc[i][j];
                 if (MODE == SCAN_DENSE) {
                     float s;
                     if (DIRECT_L2) {
                         s = v;
                     } else if (a.metric == RDB_METRIC_COSINE) {
-                        float qn = vec_value(RDB_METRIC_COSINE, a.cos_small, qsq[i]);
-                        float xn = vec_value(RDB_METRIC_COSINE, a.cos_small, xsq[j]);
+                        const float qn = vec_value(RDB_METRIC_COSINE, a.cos_small, qsq[i]);
+                        const float xn = vec_value(RDB_METRIC_COSINE, a.cos_small, xsq[j]);
                         s = final_score(RDB_METRIC_COSINE, a.cos_small, v, qn, xn);
                     } else {
                         s = v;
                     }
                     a.dense_out[q * a.ld_out + r] = s;
                 } else if (MODE == SCAN_FILTER) {
-                    float xv = a.xv ? a.xv[r * a.row_step] : 0.f;
-                    if (v >= fmaf(sA[qi], xv, sB[qi])) {
-                        int slot = atomicAdd(&scnt[qi], 1);
+                    if (v >= fmaf(sA[qi], xvr[j], sB[qi])) {
+                        const int slot = atomicAdd(&scnt[qi], 1);
                         if (slot < a.cap)
                             a.cand[((int64_t)split * a.nq + q) * a.cap + slot] = make_uint2(
-                                __float_as_uint(final_score(a.metric, a.cos_small, v, sQv[qi], xv)), (uint32_t)r);
+                                __float_as_uint(final_score(a.metric, a.cos_small, v, sQv[qi], xvr[j])), (uint32_t)r);
                     }
                 } else {  // SCAN_ARGMIN (squared L2; exact: summed directly)
-                    float dist = DIRECT_L2 ? v : fmaxf(sQv[qi] + a.xv[r * a.row_step] - 2.f * v, 0.f);
-                    unsigned long long key =
-                        ((unsigned long long)float_asc_key(dist) << 32) | (uint32_t)r;
-                    atomicMin(&sbest[qi], key);
+                    const float dist = DIRECT_L2 ? v : fmaxf(sQv[qi] + xvr[j] - 2.f * v, 0.f);
+                    const unsigned long long key = ((unsigned long long)float_asc_key(dist) << 32) | (uint32_t)r;
+                    best[i] = min(best[i], key);
                 }
             }
+        }
+    }
+    if (MODE == SCAN_ARGMIN) {
+        // the 32 lanes of a warp share its 8 queries
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            unsigned long long b = best[i];
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) b = min(b, __shfl_xor_sync(0xffffffffu, b, o));
+            if (lane == 0) atomicMin(&sbest[qg + i], b);
         }
     }
     __syncthreads();
