@@ -120,6 +120,7 @@ PYBIND11_MODULE(_C, m) {
         .def("stored_ids", &IVFFlatIndex::stored_ids)
         .def("stored_labels", &IVFFlatIndex::stored_labels)
         .def("stored_vectors", &IVFFlatIndex::stored_vectors)
+        .def("restore", &IVFFlatIndex::restore, py::arg("vectors"), py::arg("labels"), py::arg("ids"))
         .def("__len__", &IVFFlatIndex::size)
         .def("__repr__", [](const IVFFlatIndex& s) {
             return "IVFFlatIndex(dim=" + std::to_string(s.dim()) + ", nlist=" + std::to_string(s.nlist()) +
@@ -153,6 +154,7 @@ PYBIND11_MODULE(_C, m) {
         .def("stored_labels", &IVFPQIndex::stored_labels)
         .def("stored_codes", &IVFPQIndex::stored_codes)
         .def("stored_row_terms", &IVFPQIndex::stored_row_terms)
+        .def("restore", &IVFPQIndex::restore, py::arg("codes"), py::arg("labels"), py::arg("ids"))
         .def("query_major", &IVFPQIndex::query_major)
         .def("__len__", &IVFPQIndex::size)
         .def("__repr__", [](const IVFPQIndex& s) {

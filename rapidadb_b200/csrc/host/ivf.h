@@ -41,6 +41,8 @@ class IVFBase {
     at::Tensor probe(const at::Tensor& queries) const;
 
   protected:
+    // reinstalls stored-order labels (non-decreasing) and ids; rebuilds list_off
+    void restore_lists(const at::Tensor& labels, const at::Tensor& ids);
     void set_centroids(const at::Tensor& centroids);
     void check_query(const at::Tensor& queries, int64_t k) const;
     std::tuple<at::Tensor, at::Tensor> relist(const at::Tensor& labels_all);
@@ -70,6 +72,9 @@ class IVFFlatIndex : public IVFBase {
     Result search_probed(const at::Tensor& queries, const at::Tensor& probe, int64_t k) const;
     void reset() override;
     at::Tensor stored_vectors() const { return rows_.defined() ? rows_.narrow(1, 0, dim_) : at::Tensor(); }
+    // reinstalls a saved index: vectors [n, dim], list labels [n] (non-
+    // decreasing) and ids [n], all in stored order (see stored_*())
+    void restore(const at::Tensor& vectors, const at::Tensor& labels, const at::Tensor& ids);
 
   private:
     Precision precision_;
@@ -94,6 +99,9 @@ class IVFPQIndex : public IVFBase {
     int pq_k() const { return ksub_; }
     // true when search runs the query-major kernel (rotated code layout)
     bool query_major() const { return fast_; }
+    // reinstalls a saved index: codes [n, M] as stored_codes(), list labels
+    // [n] (non-decreasing) and ids [n] in stored order
+    void restore(const at::Tensor& codes, const at::Tensor& labels, const at::Tensor& ids);
 
   private:
     int M_, ksub_;

@@ -196,6 +196,24 @@ std::tuple<at::Tensor, at::Tensor> IVFBase::relist(const at::Tensor& lab_all) {
     return {std::get<1>(sorted), std::get<0>(sorted)};
 }
 
+void IVFBase::restore_lists(const at::Tensor& labels, const at::Tensor& ids) {
+    TORCH_CHECK(labels.dim() == 1 && ids.dim() == 1 && labels.size(0) == ids.size(0),
+                "labels and ids must be [n]");
+    const int64_t n = labels.size(0);
+    at::Tensor lab = labels.to(centroids_.device()).to(at::kInt).contiguous();
+    if (n > 0) {
+        TORCH_CHECK(lab.min().item<int>() >= 0 && lab.max().item<int>() < nlist_, "labels out of range");
+        if (n > 1)
+            TORCH_CHECK((lab.narrow(0, 1, n - 1) >= lab.narrow(0, 0, n - 1)).all().item<bool>(),
+                        "labels must be in stored (non-decreasing) order");
+    }
+    at::Tensor counts = at::bincount(lab.to(at::kLong), {}, nlist_);
+    list_off_ = at::cat({at::zeros({1}, counts.options()), counts.cumsum(0)}).to(at::kLong).contiguous();
+    labels_ = lab;
+    ids_ = ids.to(centroids_.device()).to(at::kLong).contiguous();
+    n_ = n;
+}
+
 void IVFBase::reset() {
     n_ = 0;
     labels_ = at::Tensor();
@@ -249,6 +267,19 @@ void IVFFlatIndex::add(const at::Tensor& vectors, const at::Tensor& ids) {
     labels_ = lab_all.index_select(0, perm);
     list_off_ = std::get<1>(pl);
     n_ += m;
+}
+
+void IVFFlatIndex::restore(const at::Tensor& vectors, const at::Tensor& labels, const at::Tensor& ids) {
+    TORCH_CHECK(is_trained(), "index is not trained (call set_quantizer() first)");
+    TORCH_CHECK(vectors.dim() == 2 && vectors.size(1) == dim_, "vectors must be [n, " + std::to_string(dim_) + "]");
+    TORCH_CHECK(vectors.size(0) == labels.size(0), "vectors and labels must have the same length");
+    c10::cuda::CUDAGuard guard(centroids_.device());
+    reset();
+    if (vectors.size(0) == 0) return;
+    at::Tensor v = vectors.to(centroids_.device());
+    rows_ = prepare_rows(v, storage_type(precision_), ld_).contiguous();
+    xv_ = row_values(metric_, rows_, dim_);
+    restore_lists(labels, ids);
 }
 
 Result IVFFlatIndex::search(const at::Tensor& queries, int64_t k) const {
@@ -336,6 +367,23 @@ void IVFPQIndex::add(const at::Tensor& vectors, const at::Tensor& ids) {
                      "pq code layout");
     }
     n_ += m;
+}
+
+void IVFPQIndex::restore(const at::Tensor& codes, const at::Tensor& labels, const at::Tensor& ids) {
+    TORCH_CHECK(is_trained() && codebooks_.defined(), "index is not trained (call set_quantizer() first)");
+    TORCH_CHECK(codes.dim() == 2 && codes.size(1) == M_ && codes.size(0) == labels.size(0),
+                "codes must be [n, pq_m] with one label per row");
+    c10::cuda::CUDAGuard guard(centroids_.device());
+    reset();
+    if (codes.size(0) == 0) return;
+    TORCH_CHECK(codes.size(0) < (int64_t(1) << 32), "at most 2^32 - 1 rows per device");
+    restore_lists(labels, ids);
+    codes_ = codes.to(centroids_.device()).to(at::kByte).contiguous().clone();
+    if (fast_) {
+        row_terms_ = pq_row_terms(codes_, labels_, centroids_, codebooks_);
+        check_status(rdb_pq_rotate_codes(codes_.data_ptr<uint8_t>(), codes_.size(0), M_, 0, stream_ptr()),
+                     "pq code layout");
+    }
 }
 
 at::Tensor IVFPQIndex::stored_codes() const {

@@ -9,9 +9,15 @@ in and out, as in the reference (index.py:24-140).  Differences:
 * Inputs keep their float dtype up to the index, which stores rows in
   ``config.precision`` (FP32 by default, as the reference's fp32 cast);
   FP16 / BF16 storage searches on the tcgen05 tensor cores.
+* ``save(path)`` / ``RapidaDB.load(path)`` persist an index (the reference
+  has no persistence): one ``torch.save`` file holding the configuration and
+  the stored arrays in stored order -- rows or PQ codes, list labels, ids,
+  centroids, codebooks -- so a loaded index answers exactly like the saved
+  one without retraining or re-encoding.
 """
 from __future__ import annotations
 
+import dataclasses
 from typing import Optional, Tuple
 
 import torch
@@ -169,6 +175,74 @@ class RapidaDB:
 
     def __len__(self) -> int:
         return self.size
+
+    # ------------------------------------------------------------ persistence
+    FORMAT = "rapidadb_b200.index"
+    FORMAT_VERSION = 1
+
+    def state_dict(self) -> dict:
+        """Configuration and stored arrays (host tensors) of this index."""
+        cfg = {f.name: (getattr(self._config, f.name).value
+                        if hasattr(getattr(self._config, f.name), "value") else getattr(self._config, f.name))
+               for f in dataclasses.fields(self._config)}
+        st = {"format": self.FORMAT, "version": self.FORMAT_VERSION, "config": cfg, "size": self.size}
+        ix = self._index
+        it = self._config.index_type
+        if it == IndexType.FLAT:
+            if self.size:
+                st["vectors"] = ix.vectors().cpu()
+                st["ids"] = ix.ids().cpu()
+        else:
+            if ix.is_trained():
+                st["centroids"] = ix.centroids().cpu()
+                if it == IndexType.IVF_PQ:
+                    st["codebooks"] = ix.codebooks().cpu()
+            if self.size:
+                st["labels"] = ix.stored_labels().cpu()
+                st["ids"] = ix.stored_ids().cpu()
+                if it == IndexType.IVF:
+                    st["vectors"] = ix.stored_vectors().cpu()
+                else:
+                    st["codes"] = ix.stored_codes().cpu()
+        return st
+
+    def save(self, path) -> None:
+        """Write the index to `path` (one torch.save file)."""
+        torch.save(self.state_dict(), path)
+
+    @classmethod
+    def from_state_dict(cls, st: dict, device=None) -> "RapidaDB":
+        if st.get("format") != cls.FORMAT or st.get("version") != cls.FORMAT_VERSION:
+            raise ValueError("not a rapidadb_b200 index file (format %r, version %r)"
+                             % (st.get("format"), st.get("version")))
+        c = dict(st["config"])
+        c["metric"] = Metric(c["metric"])
+        c["index_type"] = IndexType(c["index_type"])
+        c["precision"] = Precision(c["precision"])
+        db = cls(config=IndexConfig(**c))
+        dev = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
+        ix = db._index
+        it = db._config.index_type
+        with torch.cuda.device(dev):
+            if it == IndexType.FLAT:
+                if st.get("size", 0):
+                    ix.add(st["vectors"].to(dev), st["ids"].to(dev))
+            else:
+                if "centroids" in st:
+                    if it == IndexType.IVF_PQ:
+                        ix.set_quantizer(st["centroids"].to(dev), st["codebooks"].to(dev))
+                    else:
+                        ix.set_quantizer(st["centroids"].to(dev))
+                if st.get("size", 0):
+                    data = st["vectors"] if it == IndexType.IVF else st["codes"]
+                    ix.restore(data.to(dev), st["labels"].to(dev), st["ids"].to(dev))
+        return db
+
+    @classmethod
+    def load(cls, path, device=None) -> "RapidaDB":
+        """Read an index written by save() onto `device` (default: the
+        current CUDA device)."""
+        return cls.from_state_dict(torch.load(path, map_location="cpu", weights_only=True), device)
 
     def __repr__(self) -> str:
         return (f"RapidaDB(dim={self.dim}, metric='{self.metric}', "

@@ -1,6 +1,7 @@
-"""Row-sharded search and k-means over NCCL, one process per GPU (needs >= 2
-GPUs; skipped otherwise).  Each rank holds a contiguous slice of the rows; the
-sharded answer must equal the single-GPU answer on the full table."""
+"""Row-sharded search (Flat, IVF-Flat, IVF-PQ) and k-means over NCCL, one
+process per GPU (needs >= 2 GPUs; skipped otherwise).  Each rank holds a
+contiguous slice of the rows; the sharded answer must equal the single-GPU
+answer on the full table."""
 import os
 import socket
 
@@ -27,6 +28,11 @@ def _data():
     x = (centres[g.integers(0, 40, 30000)] + g.standard_normal((30000, 64))).astype(np.float32)
     q = (centres[g.integers(0, 40, 300)] + g.standard_normal((300, 64))).astype(np.float32)
     return x, q
+
+
+def _books(dev):
+    g = np.random.default_rng(9)
+    return torch.from_numpy(g.standard_normal((16, 64, 4)).astype(np.float32)).to(dev)
 
 
 def _worker(rank, port, out_q):
@@ -63,6 +69,12 @@ def _worker(rank, port, out_q):
         ivf.add(xt, torch.arange(lo, hi, device=dev))
         d, i = ShardedIVFSearch(ivf, largest=False).search(qt, 10)
         res["ivf"] = (d.cpu().numpy(), i.cpu().numpy())
+        # IVF-PQ (query-major search) with the same quantizer, shared codebooks
+        pq = _C.IVFPQIndex(64, _C.Metric.L2, 32, 6, 16, 64)
+        pq.set_quantizer(km.centroids, _books(dev))
+        pq.add(xt, torch.arange(lo, hi, device=dev))
+        d, i = ShardedIVFSearch(pq, largest=False).search(qt, 10)
+        res["ivfpq"] = (d.cpu().numpy(), i.cpu().numpy())
         out_q.put((rank, res))
         dist.barrier()
     finally:
@@ -99,8 +111,13 @@ def test_sharded_equals_single_gpu():
     ivf.set_quantizer(km.centroids)
     ivf.add(xt)
     di, ii = ivf.search(qt, 10)
+    pq = _C.IVFPQIndex(64, _C.Metric.L2, 32, 6, 16, 64)
+    pq.set_quantizer(km.centroids, _books(xt.device))
+    pq.add(xt)
+    dp, ip = pq.search(qt, 10)
     for r in range(WORLD):
         assert_topk_match(d.cpu().numpy(), i.cpu().numpy(), *out[r]["flat"], rtol=1e-4, atol=1e-5)
         np.testing.assert_allclose(out[r]["kmeans"][0], km.centroids.cpu().numpy(), rtol=1e-5, atol=1e-5)
         assert abs(out[r]["kmeans"][1] - km.inertia) <= 1e-5 * km.inertia
         assert_topk_match(di.cpu().numpy(), ii.cpu().numpy(), *out[r]["ivf"], rtol=1e-5, atol=1e-4)
+        assert_topk_match(dp.cpu().numpy(), ip.cpu().numpy(), *out[r]["ivfpq"], rtol=1e-5, atol=1e-3)
