@@ -105,6 +105,38 @@ int rdb_flat_search(int metric, int dtype, const void* q, int64_t nq, int64_t ld
                     const int64_t* ids, int64_t id_offset, int flags, float* out_d,
                     int64_t* out_i, void* ws, size_t ws_bytes, void* stream);
 
+/* Row-sharded flat search with one threshold for all shards (no reference
+ * counterpart: the reference is single-GPU).  Each shard computes the group
+ * maxima of a strided sample of its rows, the maxima of every shard are
+ * gathered (one all-gather), the k-th best of them is a lower bound on the
+ * global k-th best score (k distinct rows reach it), and each shard keeps
+ * only rows reaching it:
+ *   rdb_flat_sample_maxima  out [nq, sample_rows / group]: best final score
+ *                           of each group of `group` (power of two <= 128)
+ *                           consecutive sampled rows; the sample is rows
+ *                           0, s, 2 s, ... (s = n / sample_rows) of x.
+ *                           fp16 / bf16 rows on the tensor cores only
+ *                           (RDB_ERR_UNSUPPORTED otherwise); the scores are
+ *                           exact up to a few ulps.  ws: rdb_flat_sample_workspace.
+ *   rdb_select_threshold    out_thr[q] = k-th best of scores[q, 0..G) (L2
+ *                           smallest, cosine / dot largest; +-inf if G < k).
+ *   rdb_flat_search_thr     rdb_flat_search with caller thresholds thr [nq]
+ *                           (final-score units; must not be better than the
+ *                           true k-th best) and `expect` candidates per query
+ *                           expected over the n rows (sizes the candidate
+ *                           lists); RDB_ERR_OVERFLOW as rdb_flat_search. */
+size_t rdb_flat_sample_workspace(int64_t nq);
+int rdb_flat_sample_maxima(int metric, int dtype, const void* q, int64_t nq, int64_t ldq, const void* x, int64_t n,
+                           int64_t ldx, const float* xv, int d, int64_t sample_rows, int group, float* out, void* ws,
+                           size_t ws_bytes, void* stream);
+int rdb_select_threshold(int largest, const float* scores, int64_t nq, int64_t G, int k, float* out_thr,
+                         void* stream);
+size_t rdb_flat_search_thr_workspace(int metric, int dtype, int64_t nq, int64_t n, int d, int k, int64_t expect);
+int rdb_flat_search_thr(int metric, int dtype, const void* q, int64_t nq, int64_t ldq, const void* x, int64_t n,
+                        int64_t ldx, const float* xv, int d, int k, const int64_t* ids, int64_t id_offset,
+                        const float* thr, int64_t expect, float* out_d, int64_t* out_i, void* ws, size_t ws_bytes,
+                        void* stream);
+
 /* Merge G per-shard sorted lists [G, nq, kin] (scores + int64 ids) into the
  * best k per query, ties to the lower id: the final step after the NCCL
  * all-gather of row-sharded search (the reference is single-GPU). */

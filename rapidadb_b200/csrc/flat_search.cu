@@ -46,6 +46,8 @@ struct FlatPlan {
     int qtile, rtile;
     int64_t nq;  // queries in one chunk
     bool sample;
+    bool given;       // thresholds supplied by the caller
+    int64_t expect;   // candidates per query expected under given thresholds
     int group;        // tensor-core sample pass: rows per group maximum
     int64_t ngroups;  // sample rows / group
     PassPlan s, m;
@@ -88,8 +90,10 @@ PassPlan plan_pass(int64_t rows, int64_t row_step, int64_t nq, int qtile, int rt
     return p;
 }
 
+// expect_given > 0: the caller supplies the thresholds (no sample pass) and
+// expects about that many candidates per query over the n rows
 FlatPlan make_plan(int metric, int dtype, int64_t nq, int64_t n, int d, int k, int flags,
-                   bool tc_ok) {
+                   bool tc_ok, int64_t expect_given = 0) {
     (void)metric;
     (void)d;
     FlatPlan P = {};
@@ -113,7 +117,8 @@ FlatPlan make_plan(int metric, int dtype, int64_t nq, int64_t n, int d, int k, i
     while (S < sd && S < smax) S <<= 1;
     while (S > 1024 && 4 * S > n) S >>= 1;  // at most a quarter of the rows
     while (S < 8LL * k) S <<= 1;
-    P.sample = !(flags & RDB_SEARCH_EXHAUSTIVE) && n >= 4 * S;
+    P.sample = !(flags & RDB_SEARCH_EXHAUSTIVE) && n >= 4 * S && expect_given <= 0;
+    P.given = expect_given > 0 && !(flags & RDB_SEARCH_EXHAUSTIVE);
     if (P.sample) {
         int64_t step = n / S;
         P.s = plan_pass(S, step, nq, P.qtile, P.rtile, target);
@@ -127,6 +132,11 @@ FlatPlan make_plan(int metric, int dtype, int64_t nq, int64_t n, int d, int k, i
         P.ngroups = S / P.group;
     }
     P.m = plan_pass(n, 1, nq, P.qtile, P.rtile, target);
+    if (P.given) {
+        const int64_t expect = (int64_t)ceil((double)P.m.rps * (double)expect_given / (double)n);
+        P.m.cap = std::min<int64_t>(P.m.rps, std::max<int64_t>(1024, 8 * expect + 256));
+        P.expect = expect_given;
+    }
     if (P.sample) {
         // expected candidates per split: rps * k / S; keep 8x headroom
         int64_t expect = (int64_t)ceil((double)P.m.rps * (double)k / (double)S);
@@ -163,7 +173,7 @@ bool tc_layout_ok(int dtype, const void* q, int64_t ldq, const void* x, int64_t 
 int run_chunk(const FlatPlan& P, int metric, int dtype, const void* q, int64_t nq, int64_t ldq,
               const void* x, int64_t n, int64_t ldx, const float* xv, int d, int k,
               const int64_t* ids, int64_t id_offset, float* out_d, int64_t* out_i,
-              unsigned char* ws, cudaStream_t s) {
+              unsigned char* ws, cudaStream_t s, const float* thr_given) {
     float* qv = reinterpret_cast<float*>(ws + P.off_qv);
     float* thr = reinterpret_cast<float*>(ws + P.off_thr);
     uint2* cand = reinterpret_cast<uint2*>(ws + P.off_cand);
@@ -264,7 +274,7 @@ int run_chunk(const FlatPlan& P, int metric, int dtype, const void* q, int64_t n
         ScanArgs sc = a;
         sc.n = n;
         sc.row_step = 1;
-        sc.thr = P.sample ? thr : nullptr;
+        sc.thr = P.given ? thr_given : (P.sample ? thr : nullptr);
         sc.nsplit = P.m.nsplit;
         sc.rows_per_split = P.m.rps;
         sc.cap = P.m.cap;
@@ -285,7 +295,7 @@ int run_chunk(const FlatPlan& P, int metric, int dtype, const void* q, int64_t n
         ss.rescore_margin = metric == RDB_METRIC_L2 ? 16 : 0;
         // candidates per query: ~1.1 n k / S under a sampled threshold
         // (group maxima loosen it slightly), every row without one
-        ss.expect = P.sample ? (int64_t)(1.1 * (double)n * (double)k / (double)(P.s.rows)) + 1 : n;
+        ss.expect = P.given ? P.expect : P.sample ? (int64_t)(1.1 * (double)n * (double)k / (double)(P.s.rows)) + 1 : n;
         RDB_TRY(launch_select(ss, s));
     }
     return RDB_OK;
@@ -304,10 +314,15 @@ size_t rdb_flat_search_workspace(int metric, int dtype, int64_t nq, int64_t n, i
     return make_plan(metric, dtype, nq, n, d, k, flags, true).ws_bytes;
 }
 
-int rdb_flat_search(int metric, int dtype, const void* q, int64_t nq, int64_t ldq,
-                    const void* x, int64_t n, int64_t ldx, const float* xv, int d, int k,
-                    const int64_t* ids, int64_t id_offset, int flags, float* out_d,
-                    int64_t* out_i, void* ws, size_t ws_bytes, void* stream) {
+}  // extern "C"
+
+namespace rdb {
+namespace {
+
+int flat_search_impl(int metric, int dtype, const void* q, int64_t nq, int64_t ldq, const void* x, int64_t n,
+                     int64_t ldx, const float* xv, int d, int k, const int64_t* ids, int64_t id_offset, int flags,
+                     const float* thr_given, int64_t expect_given, float* out_d, int64_t* out_i, void* ws,
+                     size_t ws_bytes, void* stream) {
     RDB_CHECK_ARG(metric >= 0 && metric <= 2, "unknown metric %d", metric);
     RDB_CHECK_ARG(elem_size(dtype) != 0, "unknown dtype %d", dtype);
     RDB_CHECK_ARG(nq >= 0 && d >= 1, "bad shape");
@@ -322,13 +337,14 @@ int rdb_flat_search(int metric, int dtype, const void* q, int64_t nq, int64_t ld
     RDB_CHECK_ARG(metric != RDB_METRIC_L2 || xv, "L2 needs per-row values");
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     bool tc_ok = tc_layout_ok(dtype, q, ldq, x, ldx, d);
+    const int64_t eg = thr_given ? std::max<int64_t>(expect_given, 1) : 0;
 
     // largest query chunk whose plan fits the workspace
-    FlatPlan P = make_plan(metric, dtype, nq, n, d, k, flags, tc_ok);
+    FlatPlan P = make_plan(metric, dtype, nq, n, d, k, flags, tc_ok, eg);
     int64_t chunk = nq;
     while (P.ws_bytes > ws_bytes && chunk > P.qtile) {
         chunk = std::max<int64_t>(P.qtile, (chunk / 2 + P.qtile - 1) / P.qtile * P.qtile);
-        P = make_plan(metric, dtype, chunk, n, d, k, flags, tc_ok);
+        P = make_plan(metric, dtype, chunk, n, d, k, flags, tc_ok, eg);
     }
     if (P.ws_bytes > ws_bytes)
         return set_error(RDB_ERR_WORKSPACE, "workspace too small: %zu bytes, need %zu", ws_bytes,
@@ -342,10 +358,10 @@ int rdb_flat_search(int metric, int dtype, const void* q, int64_t nq, int64_t ld
     const size_t es = elem_size(dtype);
     for (int64_t c0 = 0; c0 < nq; c0 += chunk) {
         int64_t cn = std::min(chunk, nq - c0);
-        FlatPlan Pc = cn == chunk ? P : make_plan(metric, dtype, cn, n, d, k, flags, tc_ok);
+        FlatPlan Pc = cn == chunk ? P : make_plan(metric, dtype, cn, n, d, k, flags, tc_ok, eg);
         RDB_TRY(run_chunk(Pc, metric, dtype, static_cast<const char*>(q) + c0 * ldq * es, cn, ldq,
                           x, n, ldx, xv, d, k, ids, id_offset, out_d + c0 * k, out_i + c0 * k, w,
-                          s));
+                          s, thr_given ? thr_given + c0 : nullptr));
     }
     unsigned* host = host_words();
     if (!host) return set_error(RDB_ERR_CUDA, "cannot allocate pinned host words");
@@ -359,6 +375,101 @@ int rdb_flat_search(int metric, int dtype, const void* q, int64_t nq, int64_t ld
     if (any_overflow)
         return set_error(RDB_ERR_OVERFLOW, "candidate list overflow; repeat with RDB_SEARCH_EXHAUSTIVE");
     return RDB_OK;
+}
+
+}  // namespace
+}  // namespace rdb
+
+extern "C" {
+
+int rdb_flat_search(int metric, int dtype, const void* q, int64_t nq, int64_t ldq,
+                    const void* x, int64_t n, int64_t ldx, const float* xv, int d, int k,
+                    const int64_t* ids, int64_t id_offset, int flags, float* out_d,
+                    int64_t* out_i, void* ws, size_t ws_bytes, void* stream) {
+    return flat_search_impl(metric, dtype, q, nq, ldq, x, n, ldx, xv, d, k, ids, id_offset, flags, nullptr, 0,
+                            out_d, out_i, ws, ws_bytes, stream);
+}
+
+size_t rdb_flat_search_thr_workspace(int metric, int dtype, int64_t nq, int64_t n, int d, int k, int64_t expect) {
+    if (nq <= 0 || n <= 0 || d <= 0 || k <= 0) return 256;
+    return make_plan(metric, dtype, nq, n, d, k, 0, true, std::max<int64_t>(expect, 1)).ws_bytes;
+}
+
+int rdb_flat_search_thr(int metric, int dtype, const void* q, int64_t nq, int64_t ldq, const void* x, int64_t n,
+                        int64_t ldx, const float* xv, int d, int k, const int64_t* ids, int64_t id_offset,
+                        const float* thr, int64_t expect, float* out_d, int64_t* out_i, void* ws, size_t ws_bytes,
+                        void* stream) {
+    RDB_CHECK_ARG(thr != nullptr, "thr is NULL");
+    return flat_search_impl(metric, dtype, q, nq, ldq, x, n, ldx, xv, d, k, ids, id_offset, 0, thr, expect, out_d,
+                            out_i, ws, ws_bytes, stream);
+}
+
+size_t rdb_flat_sample_workspace(int64_t nq) { return align_up(sizeof(float) * std::max<int64_t>(nq, 1), 256); }
+
+int rdb_flat_sample_maxima(int metric, int dtype, const void* q, int64_t nq, int64_t ldq, const void* x, int64_t n,
+                           int64_t ldx, const float* xv, int d, int64_t sample_rows, int group, float* out, void* ws,
+                           size_t ws_bytes, void* stream) {
+    RDB_CHECK_ARG(metric >= 0 && metric <= 2, "unknown metric %d", metric);
+    RDB_CHECK_ARG(nq >= 0 && n >= 1 && d >= 1, "bad shape");
+    RDB_CHECK_ARG(group >= 1 && group <= 128 && (group & (group - 1)) == 0, "group must be a power of two <= 128");
+    RDB_CHECK_ARG(sample_rows >= group && sample_rows % group == 0 && sample_rows <= n,
+                  "sample_rows must be a multiple of group in [group, n]");
+    RDB_CHECK_ARG(metric == RDB_METRIC_DOT || xv, "cosine / L2 need per-row values");
+    if (nq == 0) return RDB_OK;
+    RDB_CHECK_ARG(q && x && out && ws, "NULL pointer");
+    RDB_CHECK_ARG(ws_bytes >= rdb_flat_sample_workspace(nq), "workspace too small");
+    if (!tc_layout_ok(dtype, q, ldq, x, ldx, d))
+        return set_error(RDB_ERR_UNSUPPORTED, "sample maxima need fp16 / bf16 rows with 16-byte aligned strides");
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    float* qv = static_cast<float*>(ws);
+    if (ldq == d) {
+        RDB_TRY(rdb_row_sqnorms(dtype, q, nq, d, qv, s));
+    } else {
+        for (int64_t i = 0; i < nq; ++i)
+            RDB_TRY(rdb_row_sqnorms(dtype, static_cast<const char*>(q) + i * ldq * elem_size(dtype), 1, d, qv + i, s));
+    }
+    RDB_TRY(rdb_vec_values(metric, d, qv, nq, qv, s));
+    const bool pair = tc_use_pair(nq);
+    const int qtile = pair ? 2 * kTcQueries : kTcQueries;
+    const int64_t target = pair ? num_sms() / 2 : num_sms();
+    const PassPlan pp = plan_pass(sample_rows, n / sample_rows, nq, qtile, kTcRows, target);
+    ScanArgs a = {};
+    a.metric = metric;
+    a.cos_small = d <= 128 ? 1 : 0;
+    a.dtype = dtype;
+    a.q = q;
+    a.nq = nq;
+    a.ldq = ldq;
+    a.x = x;
+    a.ldx = ldx;
+    a.d = d;
+    a.qv = qv;
+    a.xv = xv;
+    a.n = sample_rows;
+    a.row_step = n / sample_rows;
+    a.nsplit = pp.nsplit;
+    a.rows_per_split = pp.rps;
+    a.group_out = out;
+    a.group = group;
+    a.ngroups = sample_rows / group;
+    return launch_scan_tc(a, SCAN_GROUPMAX, s);
+}
+
+int rdb_select_threshold(int largest, const float* scores, int64_t nq, int64_t G, int k, float* out_thr,
+                         void* stream) {
+    RDB_CHECK_ARG(nq >= 0 && G >= 1 && k >= 1 && k <= kMaxK, "bad shape");
+    if (nq == 0) return RDB_OK;
+    RDB_CHECK_ARG(scores && out_thr, "NULL pointer");
+    SelectArgs ss = {};
+    ss.input = SEL_DENSE;
+    ss.output = SEL_OUT_THRESHOLD;
+    ss.nq = nq;
+    ss.k = k;
+    ss.largest = largest ? 1 : 0;
+    ss.dense = scores;
+    ss.dense_n = G;
+    ss.out_thr = out_thr;
+    return launch_select(ss, static_cast<cudaStream_t>(stream));
 }
 
 size_t rdb_topk_workspace(int64_t B, int64_t N, int k) {

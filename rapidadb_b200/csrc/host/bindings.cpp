@@ -68,6 +68,11 @@ PYBIND11_MODULE(_C, m) {
         .def("dim", &FlatIndex::dim)
         .def("capacity", &FlatIndex::capacity)
         .def("vectors", &FlatIndex::vectors)
+        .def("sample_maxima", &FlatIndex::sample_maxima, py::arg("queries"), py::arg("sample_rows"),
+             py::arg("group"))
+        .def("search_threshold", &FlatIndex::search_threshold, py::arg("queries"), py::arg("k"), py::arg("thr"),
+             py::arg("expect"))
+        .def("tensor_core", &FlatIndex::tensor_core)
         .def("ids", &FlatIndex::ids)
         .def("__len__", &FlatIndex::size)
         .def("__repr__", [](const FlatIndex& self) {
@@ -91,6 +96,8 @@ PYBIND11_MODULE(_C, m) {
     m.def("kmeans_finalize", &kmeans_finalize, "sums / counts (empty clusters keep their centroid)",
           py::arg("sums"), py::arg("counts"), py::arg("centroids"));
     m.def("label_sort", &label_sort, "stable counting sort by label", py::arg("labels"), py::arg("k"));
+    m.def("select_threshold", &select_threshold, "k-th best score of each row", py::arg("scores"), py::arg("k"),
+          py::arg("largest"));
     m.def("pq_row_terms", &pq_row_terms, "per-row constant of the IVF-PQ distance", py::arg("codes"),
           py::arg("labels"), py::arg("centroids"), py::arg("codebooks"));
     m.def("pq_encode", &pq_encode, "residual PQ codes", py::arg("points"), py::arg("labels"),

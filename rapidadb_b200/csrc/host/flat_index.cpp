@@ -135,6 +135,17 @@ Result topk_merge(const at::Tensor& vals, const at::Tensor& ids, int64_t k, bool
     return {ov, oi};
 }
 
+at::Tensor select_threshold(const at::Tensor& scores, int64_t k, bool largest) {
+    TORCH_CHECK(scores.is_cuda() && scores.dim() == 2, "scores must be a [nq, G] CUDA tensor");
+    c10::cuda::CUDAGuard guard(scores.device());
+    at::Tensor sc = scores.to(at::kFloat).contiguous();
+    at::Tensor out = at::empty({sc.size(0)}, sc.options());
+    check_status(rdb_select_threshold(largest ? 1 : 0, sc.data_ptr<float>(), sc.size(0), sc.size(1),
+                                      static_cast<int>(k), out.data_ptr<float>(), stream_ptr()),
+                 "select threshold");
+    return out;
+}
+
 // ---------------------------------------------------------------- FlatIndex
 
 FlatIndex::FlatIndex(int dim, Metric metric, Precision precision)
@@ -244,6 +255,52 @@ Result FlatIndex::search(const at::Tensor& queries, int64_t k) const {
     at::Tensor q = prepare_rows(queries.to(storage_.device()), storage_.scalar_type(), ld_);
     return search_impl(metric_, storage_.narrow(0, 0, n_), dim_, xv_.narrow(0, 0, n_), q, k,
                        ids_.narrow(0, 0, n_), 0);
+}
+
+at::Tensor FlatIndex::sample_maxima(const at::Tensor& queries, int64_t sample_rows, int64_t group) const {
+    TORCH_CHECK(queries.is_cuda(), "queries must be on CUDA");
+    TORCH_CHECK(queries.dim() == 2 && queries.size(1) == dim_,
+                "queries must be [batch, " + std::to_string(dim_) + "]");
+    TORCH_CHECK(n_ > 0, "index is empty");
+    TORCH_CHECK(sample_rows >= group && sample_rows <= n_ && group >= 1, "bad sample size");
+    c10::cuda::CUDAGuard guard(storage_.device());
+    at::Tensor q = prepare_rows(queries.to(storage_.device()), storage_.scalar_type(), ld_);
+    const int64_t nq = q.size(0);
+    at::Tensor out = at::empty({nq, sample_rows / group}, q.options().dtype(at::kFloat));
+    at::Tensor ws = at::empty({static_cast<int64_t>(rdb_flat_sample_workspace(nq))}, q.options().dtype(at::kByte));
+    check_status(rdb_flat_sample_maxima(static_cast<int>(metric_), dtype_code(storage_.scalar_type()), q.data_ptr(),
+                                        nq, ld_, storage_.data_ptr(), n_, ld_, xv_.data_ptr<float>(), dim_,
+                                        sample_rows, static_cast<int>(group), out.data_ptr<float>(), ws.data_ptr(),
+                                        ws.numel(), stream_ptr()),
+                 "sample maxima");
+    return out;
+}
+
+Result FlatIndex::search_threshold(const at::Tensor& queries, int64_t k, const at::Tensor& thr_in,
+                                   int64_t expect) const {
+    TORCH_CHECK(queries.is_cuda(), "queries must be on CUDA");
+    TORCH_CHECK(queries.dim() == 2 && queries.size(1) == dim_,
+                "queries must be [batch, " + std::to_string(dim_) + "]");
+    TORCH_CHECK(n_ > 0, "index is empty");
+    TORCH_CHECK(k > 0 && k <= n_, "k must be in [1, " + std::to_string(n_) + "]");
+    TORCH_CHECK(thr_in.dim() == 1 && thr_in.size(0) == queries.size(0), "thr must be [batch]");
+    c10::cuda::CUDAGuard guard(storage_.device());
+    at::Tensor q = prepare_rows(queries.to(storage_.device()), storage_.scalar_type(), ld_);
+    at::Tensor thr = thr_in.to(storage_.device()).to(at::kFloat).contiguous();
+    const int64_t nq = q.size(0);
+    const int m = static_cast<int>(metric_), dt = dtype_code(storage_.scalar_type());
+    at::Tensor out_d = at::empty({nq, k}, q.options().dtype(at::kFloat));
+    at::Tensor out_i = at::empty({nq, k}, q.options().dtype(at::kLong));
+    if (nq == 0) return {out_d, out_i};
+    size_t wsb = rdb_flat_search_thr_workspace(m, dt, nq, n_, dim_, static_cast<int>(k), expect);
+    at::Tensor ws = at::empty({static_cast<int64_t>(wsb)}, q.options().dtype(at::kByte));
+    int st = rdb_flat_search_thr(m, dt, q.data_ptr(), nq, ld_, storage_.data_ptr(), n_, ld_, xv_.data_ptr<float>(),
+                                 dim_, static_cast<int>(k), ids_.data_ptr<int64_t>(), 0, thr.data_ptr<float>(), expect,
+                                 out_d.data_ptr<float>(), out_i.data_ptr<int64_t>(), ws.data_ptr(), wsb,
+                                 stream_ptr());
+    if (st == RDB_ERR_OVERFLOW) return search(queries, k);  // the plain search retries exhaustively if needed
+    check_status(st, "flat search");
+    return {out_d, out_i};
 }
 
 void FlatIndex::reset() {

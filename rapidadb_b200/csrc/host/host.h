@@ -35,6 +35,8 @@ at::Tensor distance(Metric metric, const at::Tensor& queries, const at::Tensor& 
 Result topk(const at::Tensor& distances, int64_t k, bool largest);
 // merge of per-shard [G, Q, kin] lists into [Q, k]
 Result topk_merge(const at::Tensor& vals, const at::Tensor& ids, int64_t k, bool largest);
+// k-th best of each row of scores [nq, G] (L2 smallest, else largest)
+at::Tensor select_threshold(const at::Tensor& scores, int64_t k, bool largest);
 
 // -------------------------------------------------------------- FlatIndex --
 // csrc/include/rapidadb/index/flat_index.h:12-53, csrc/index/flat_index.cpp
@@ -52,6 +54,14 @@ class FlatIndex {
     at::Tensor vectors() const;
     at::Tensor ids() const;
     int64_t capacity() const { return storage_.defined() ? storage_.size(0) : 0; }
+
+    // Row-sharded search with a shared threshold (rdb_flat_sample_maxima /
+    // rdb_flat_search_thr): group maxima [nq, sample_rows / group] of a
+    // strided sample of the stored rows, and a search keeping only rows that
+    // reach thr [nq] (expect: candidates per query expected over the rows).
+    at::Tensor sample_maxima(const at::Tensor& queries, int64_t sample_rows, int64_t group) const;
+    Result search_threshold(const at::Tensor& queries, int64_t k, const at::Tensor& thr, int64_t expect) const;
+    bool tensor_core() const { return precision_ == Precision::FP16 || precision_ == Precision::BF16; }
 
     // Search against externally owned rows (same layout rules): used by the
     // IVF coarse probe and by tests.

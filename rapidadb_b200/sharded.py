@@ -13,6 +13,7 @@ exercised on CPU ranks with the oracle standing in for the GPU parts.
 """
 from __future__ import annotations
 
+import math
 from typing import Callable, Optional, Tuple
 
 import torch
@@ -47,6 +48,30 @@ def gpu_merge(vals: torch.Tensor, ids: torch.Tensor, k: int, largest: bool):
     return C().topk_merge(vals, ids, k, largest)
 
 
+def shared_sample_plan(sizes, k: int) -> Optional[Tuple[int, int, int]]:
+    """Sample plan of the shared-threshold protocol for shard sizes `sizes`:
+    (rows sampled per rank, rows per group maximum, total sampled rows), or
+    None when the shards are too small for a useful sample.  The total sample
+    S follows the single-GPU rule (a power of two near 6 sqrt(n k), at most
+    n / 4 rows, groups of up to 128 rows while >= 10 k groups remain), spread
+    evenly over the ranks."""
+    world, n = len(sizes), int(sum(sizes))
+    S, sd = 1024, 6.0 * math.sqrt(n * k)
+    while S < sd and S < 131072:
+        S <<= 1
+    while S > 1024 and 4 * S > n:
+        S >>= 1
+    while S < 8 * k:
+        S <<= 1
+    g = 1
+    while g < 128 and S // (2 * g) >= 10 * k:
+        g <<= 1
+    per = (S // world) // g * g
+    if per < g or 4 * per > min(sizes) or world * (per // g) < 4 * k:
+        return None
+    return per, g, world * per
+
+
 class ShardedSearch:
     """Search one query batch against a row-sharded index.
 
@@ -61,16 +86,50 @@ class ShardedSearch:
     """
 
     def __init__(self, index, largest: bool, group: Optional[dist.ProcessGroup] = None,
-                 merge: Optional[Callable] = None):
+                 merge: Optional[Callable] = None, shared_threshold: bool = True):
         self.search_fn = index if callable(index) and not hasattr(index, "search") else index.search
         self.largest = largest
         self.group = group
         self.merge = merge or gpu_merge
+        # the extension FlatIndex (directly or inside a RapidaDB facade) with
+        # fp16 / bf16 rows can share one sampled threshold across the shards
+        flat = getattr(index, "index", index)
+        self.flat = flat if shared_threshold and hasattr(flat, "sample_maxima") and flat.tensor_core() else None
+
+    def _shared_threshold_search(self, queries: torch.Tensor, k: int):
+        """Shared-threshold protocol: every rank computes group maxima of a
+        strided sample of its rows (1 / world of the single-GPU sample), the
+        maxima are all-gathered, the k-th best of them -- a lower bound on the
+        global k-th best score -- filters every shard.  Two small collectives
+        (shard sizes, maxima); None (before any data collective) when the
+        shards are too small."""
+        world = dist.get_world_size(self.group)
+        dev = queries.device
+        n_local = torch.tensor([self.flat.size()], dtype=torch.long, device=dev)
+        sizes = torch.empty(world, dtype=torch.long, device=dev)
+        dist.all_gather_into_tensor(sizes, n_local, group=self.group)
+        plan = shared_sample_plan(sizes.tolist(), k)
+        if plan is None:
+            return None
+        per, g, total = plan
+        maxima = self.flat.sample_maxima(queries, per, g)  # [Q, per / g]
+        Q, gl = maxima.shape
+        allm = torch.empty((world * Q, gl), dtype=maxima.dtype, device=dev)
+        dist.all_gather_into_tensor(allm, maxima.contiguous(), group=self.group)
+        allm = allm.view(world, Q, gl).permute(1, 0, 2).reshape(Q, world * gl)
+        from rapidadb_b200._lib import C
+
+        thr = C().select_threshold(allm, k, self.largest)
+        expect = int(math.ceil(1.1 * self.flat.size() * k / total)) + 1
+        return self.flat.search_threshold(queries, k, thr, expect)
 
     def search(self, queries: torch.Tensor, k: int) -> Tuple[torch.Tensor, torch.Tensor]:
-        local_d, local_i = self.search_fn(queries, k)
         if not dist.is_initialized() or dist.get_world_size(self.group) == 1:
-            return local_d, local_i
+            return self.search_fn(queries, k)
+        out = None
+        if self.flat is not None:
+            out = self._shared_threshold_search(queries, k)
+        local_d, local_i = out if out is not None else self.search_fn(queries, k)
         vals, ids = gather_candidates(local_d, local_i, self.group)
         return self.merge(vals, ids, k, self.largest)
 
