@@ -31,15 +31,21 @@ def shard_range(n: int, rank: int, world: int) -> Tuple[int, int]:
 
 def gather_candidates(local_d: torch.Tensor, local_i: torch.Tensor,
                       group: Optional[dist.ProcessGroup] = None) -> Tuple[torch.Tensor, torch.Tensor]:
-    """All-gather [Q, k] scores and ids from every rank into [G, Q, k]."""
+    """All-gather [Q, k] fp32 scores and int64 ids from every rank into
+    [G, Q, k] with one collective: each entry travels as three 32-bit words
+    (score bits, id low, id high)."""
     world = dist.get_world_size(group)
     Q, k = local_d.shape
-    # gathered along dim 0 as [G * Q, k] (the layout every backend accepts)
-    out_d = torch.empty((world * Q, k), dtype=local_d.dtype, device=local_d.device)
-    out_i = torch.empty((world * Q, k), dtype=local_i.dtype, device=local_i.device)
-    dist.all_gather_into_tensor(out_d, local_d.contiguous(), group=group)
-    dist.all_gather_into_tensor(out_i, local_i.contiguous(), group=group)
-    return out_d.view(world, Q, k), out_i.view(world, Q, k)
+    packed = torch.empty((Q, k, 3), dtype=torch.int32, device=local_d.device)
+    packed[:, :, 0] = local_d.float().contiguous().view(torch.int32)
+    packed[:, :, 1:] = local_i.long().contiguous().view(torch.int32).view(Q, k, 2)
+    # gathered along dim 0 (the layout every backend accepts)
+    out = torch.empty((world * Q, k, 3), dtype=torch.int32, device=local_d.device)
+    dist.all_gather_into_tensor(out, packed, group=group)
+    out = out.view(world, Q, k, 3)
+    vals = out[..., 0].contiguous().view(torch.float32)
+    ids = out[..., 1:].contiguous().view(torch.int64).view(world, Q, k)
+    return vals, ids
 
 
 def gpu_merge(vals: torch.Tensor, ids: torch.Tensor, k: int, largest: bool):
@@ -95,20 +101,32 @@ class ShardedSearch:
         # fp16 / bf16 rows can share one sampled threshold across the shards
         flat = getattr(index, "index", index)
         self.flat = flat if shared_threshold and hasattr(flat, "sample_maxima") and flat.tensor_core() else None
+        self._sizes = None
+
+    def refresh_sizes(self) -> None:
+        """Forget the cached shard sizes (call on every rank after adds or
+        resets); the next search gathers them again."""
+        self._sizes = None
 
     def _shared_threshold_search(self, queries: torch.Tensor, k: int):
         """Shared-threshold protocol: every rank computes group maxima of a
         strided sample of its rows (1 / world of the single-GPU sample), the
         maxima are all-gathered, the k-th best of them -- a lower bound on the
-        global k-th best score -- filters every shard.  Two small collectives
-        (shard sizes, maxima); None (before any data collective) when the
-        shards are too small."""
+        global k-th best score -- filters every shard.  One collective per
+        search (the maxima) besides the result gather; the shard sizes are
+        gathered on the first search.  None (before any data collective) when
+        the shards are too small."""
         world = dist.get_world_size(self.group)
         dev = queries.device
-        n_local = torch.tensor([self.flat.size()], dtype=torch.long, device=dev)
-        sizes = torch.empty(world, dtype=torch.long, device=dev)
-        dist.all_gather_into_tensor(sizes, n_local, group=self.group)
-        plan = shared_sample_plan(sizes.tolist(), k)
+        if self._sizes is None:
+            # shard sizes, gathered once (refresh_sizes() after the index changes)
+            n_local = torch.tensor([self.flat.size()], dtype=torch.long, device=dev)
+            sizes = torch.empty(world, dtype=torch.long, device=dev)
+            dist.all_gather_into_tensor(sizes, n_local, group=self.group)
+            self._sizes = sizes.tolist()
+        if self._sizes[dist.get_rank(self.group)] != self.flat.size():
+            raise RuntimeError("shard size changed since the sizes were gathered: call refresh_sizes() on every rank")
+        plan = shared_sample_plan(self._sizes, k)
         if plan is None:
             return None
         per, g, total = plan
