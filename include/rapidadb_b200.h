@@ -142,6 +142,11 @@ int rdb_flat_search_thr(int metric, int dtype, const void* q, int64_t nq, int64_
  * all-gather of row-sharded search (the reference is single-GPU). */
 int rdb_topk_merge(int largest, const float* in_v, const int64_t* in_i, int G, int64_t nq,
                    int kin, int k, float* out_v, int64_t* out_i, void* stream);
+/* Same with list g at in_v + g * gstride_v and in_i + g * gstride_i (0: nq *
+ * kin), e.g. the per-rank blocks of an all-gather buffer, read in place. */
+int rdb_topk_merge_strided(int largest, const float* in_v, int64_t gstride_v, const int64_t* in_i,
+                           int64_t gstride_i, int G, int64_t nq, int kin, int k, float* out_v, int64_t* out_i,
+                           void* stream);
 
 /* ---- k-means --------------------------------------------------------- */
 

@@ -503,8 +503,16 @@ int rdb_topk(const float* dist, int64_t B, int64_t N, int k, int largest, float*
 
 int rdb_topk_merge(int largest, const float* in_v, const int64_t* in_i, int G, int64_t nq,
                    int kin, int k, float* out_v, int64_t* out_i, void* stream) {
+    return rdb_topk_merge_strided(largest, in_v, 0, in_i, 0, G, nq, kin, k, out_v, out_i, stream);
+}
+
+int rdb_topk_merge_strided(int largest, const float* in_v, int64_t gstride_v, const int64_t* in_i,
+                           int64_t gstride_i, int G, int64_t nq, int kin, int k, float* out_v, int64_t* out_i,
+                           void* stream) {
     RDB_CHECK_ARG(G >= 1 && kin >= 1 && k >= 1, "bad shape");
     RDB_CHECK_ARG(k <= (int64_t)G * kin, "k must be <= G * kin");
+    RDB_CHECK_ARG(gstride_v == 0 || gstride_v >= nq * kin, "list stride of the scores below nq * kin");
+    RDB_CHECK_ARG(gstride_i == 0 || gstride_i >= nq * kin, "list stride of the ids below nq * kin");
     if (nq == 0) return RDB_OK;
     SelectArgs a = {};
     a.input = SEL_MERGE;
@@ -514,6 +522,8 @@ int rdb_topk_merge(int largest, const float* in_v, const int64_t* in_i, int G, i
     a.largest = largest ? 1 : 0;
     a.merge_v = in_v;
     a.merge_i = in_i;
+    a.gstride_v = gstride_v;
+    a.gstride_i = gstride_i;
     a.G = G;
     a.kin = kin;
     a.out_v = out_v;

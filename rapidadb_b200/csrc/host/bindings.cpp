@@ -30,18 +30,18 @@ PYBIND11_MODULE(_C, m) {
 
     // ---- raw distance ops (torch_extension.cpp:34-44)
     m.def("cosine_similarity", [](const at::Tensor& q, const at::Tensor& x) { return distance(Metric::COSINE, q, x); },
-          "Cosine similarity matrix [Q, N]", py::arg("queries"), py::arg("database"));
+          "Cosine similarity matrix [Q, N]", py::arg("queries"), py::arg("database"), py::call_guard<py::gil_scoped_release>());
     m.def("l2_distance", [](const at::Tensor& q, const at::Tensor& x) { return distance(Metric::L2, q, x); },
-          "Squared L2 distance matrix [Q, N]", py::arg("queries"), py::arg("database"));
+          "Squared L2 distance matrix [Q, N]", py::arg("queries"), py::arg("database"), py::call_guard<py::gil_scoped_release>());
     m.def("dot_product", [](const at::Tensor& q, const at::Tensor& x) { return distance(Metric::DOT_PRODUCT, q, x); },
-          "Dot product matrix [Q, N]", py::arg("queries"), py::arg("database"));
+          "Dot product matrix [Q, N]", py::arg("queries"), py::arg("database"), py::call_guard<py::gil_scoped_release>());
 
     // ---- top-k (torch_extension.cpp:47-63)
     m.def("topk", [](const at::Tensor& d, int64_t k, bool largest) { return topk(d, k, largest); },
-          "Sorted top-k per row", py::arg("distances"), py::arg("k"), py::arg("largest") = true);
+          "Sorted top-k per row", py::arg("distances"), py::arg("k"), py::arg("largest") = true, py::call_guard<py::gil_scoped_release>());
     m.def("topk_thrust", [](const at::Tensor& d, int64_t k, bool largest) { return topk(d, k, largest); },
           "Sorted top-k per row (same kernel as topk)", py::arg("distances"), py::arg("k"),
-          py::arg("largest") = true);
+          py::arg("largest") = true, py::call_guard<py::gil_scoped_release>());
     m.def(
         "topk_warp_heap",
         [](const at::Tensor& d, int64_t k, bool largest) {
@@ -51,18 +51,22 @@ PYBIND11_MODULE(_C, m) {
         },
         "Sorted top-k per row, k <= 128", py::arg("distances"), py::arg("k"), py::arg("largest") = true);
     m.def("topk_merge", &topk_merge, "Merge [G, Q, k_in] sorted lists into [Q, k]", py::arg("values"),
-          py::arg("ids"), py::arg("k"), py::arg("largest"));
+          py::arg("ids"), py::arg("k"), py::arg("largest"), py::call_guard<py::gil_scoped_release>());
 
     // ---- FlatIndex (torch_extension.cpp:66-89)
     py::class_<FlatIndex>(m, "FlatIndex")
         .def(py::init<int, Metric, Precision>(), py::arg("dim"), py::arg("metric") = Metric::COSINE,
              py::arg("precision") = Precision::FP32)
         .def(
-            "add", [](FlatIndex& self, const at::Tensor& v, const py::object& ids) { self.add(v, opt_tensor(ids)); },
+            "add", [](FlatIndex& self, const at::Tensor& v, const py::object& ids) {
+                at::Tensor t = opt_tensor(ids);
+                py::gil_scoped_release release;
+                self.add(v, t);
+            },
             py::arg("vectors"), py::arg("ids") = py::none())
         .def(
             "search", [](const FlatIndex& self, const at::Tensor& q, int64_t k) { return self.search(q, k); },
-            py::arg("queries"), py::arg("k"))
+            py::arg("queries"), py::arg("k"), py::call_guard<py::gil_scoped_release>())
         .def("reset", &FlatIndex::reset)
         .def("size", &FlatIndex::size)
         .def("dim", &FlatIndex::dim)
@@ -90,18 +94,18 @@ PYBIND11_MODULE(_C, m) {
         py::arg("id_offset") = 0);
     // ---- k-means primitives (rapidadb_b200.kmeans drives the Lloyd loop)
     m.def("kmeans_assign", &kmeans_assign, "labels, squared distances", py::arg("points"), py::arg("centroids"),
-          py::arg("exact") = false);
+          py::arg("exact") = false, py::call_guard<py::gil_scoped_release>());
     m.def("kmeans_update", &kmeans_update, "per-centroid sums and counts", py::arg("points"), py::arg("labels"),
-          py::arg("k"));
+          py::arg("k"), py::call_guard<py::gil_scoped_release>());
     m.def("kmeans_finalize", &kmeans_finalize, "sums / counts (empty clusters keep their centroid)",
-          py::arg("sums"), py::arg("counts"), py::arg("centroids"));
-    m.def("label_sort", &label_sort, "stable counting sort by label", py::arg("labels"), py::arg("k"));
+          py::arg("sums"), py::arg("counts"), py::arg("centroids"), py::call_guard<py::gil_scoped_release>());
+    m.def("label_sort", &label_sort, "stable counting sort by label", py::arg("labels"), py::arg("k"), py::call_guard<py::gil_scoped_release>());
     m.def("select_threshold", &select_threshold, "k-th best score of each row", py::arg("scores"), py::arg("k"),
-          py::arg("largest"));
+          py::arg("largest"), py::call_guard<py::gil_scoped_release>());
     m.def("pq_row_terms", &pq_row_terms, "per-row constant of the IVF-PQ distance", py::arg("codes"),
-          py::arg("labels"), py::arg("centroids"), py::arg("codebooks"));
+          py::arg("labels"), py::arg("centroids"), py::arg("codebooks"), py::call_guard<py::gil_scoped_release>());
     m.def("pq_encode", &pq_encode, "residual PQ codes", py::arg("points"), py::arg("labels"),
-          py::arg("centroids"), py::arg("codebooks"));
+          py::arg("centroids"), py::arg("codebooks"), py::call_guard<py::gil_scoped_release>());
 
     // ---- IVF indices
     py::class_<IVFFlatIndex>(m, "IVFFlatIndex")
@@ -109,11 +113,15 @@ PYBIND11_MODULE(_C, m) {
              py::arg("nlist") = 4096, py::arg("nprobe") = 64, py::arg("precision") = Precision::FP32)
         .def("set_quantizer", &IVFFlatIndex::set_quantizer, py::arg("centroids"))
         .def(
-            "add", [](IVFFlatIndex& s, const at::Tensor& v, const py::object& ids) { s.add(v, opt_tensor(ids)); },
+            "add", [](IVFFlatIndex& s, const at::Tensor& v, const py::object& ids) {
+                at::Tensor t = opt_tensor(ids);
+                py::gil_scoped_release release;
+                s.add(v, t);
+            },
             py::arg("vectors"), py::arg("ids") = py::none())
-        .def("search", &IVFFlatIndex::search, py::arg("queries"), py::arg("k"))
-        .def("probe", &IVFFlatIndex::probe, py::arg("queries"))
-        .def("search_probed", &IVFFlatIndex::search_probed, py::arg("queries"), py::arg("probe"), py::arg("k"))
+        .def("search", &IVFFlatIndex::search, py::arg("queries"), py::arg("k"), py::call_guard<py::gil_scoped_release>())
+        .def("probe", &IVFFlatIndex::probe, py::arg("queries"), py::call_guard<py::gil_scoped_release>())
+        .def("search_probed", &IVFFlatIndex::search_probed, py::arg("queries"), py::arg("probe"), py::arg("k"), py::call_guard<py::gil_scoped_release>())
         .def("reset", &IVFFlatIndex::reset)
         .def("size", &IVFFlatIndex::size)
         .def("dim", &IVFFlatIndex::dim)
@@ -127,7 +135,7 @@ PYBIND11_MODULE(_C, m) {
         .def("stored_ids", &IVFFlatIndex::stored_ids)
         .def("stored_labels", &IVFFlatIndex::stored_labels)
         .def("stored_vectors", &IVFFlatIndex::stored_vectors)
-        .def("restore", &IVFFlatIndex::restore, py::arg("vectors"), py::arg("labels"), py::arg("ids"))
+        .def("restore", &IVFFlatIndex::restore, py::arg("vectors"), py::arg("labels"), py::arg("ids"), py::call_guard<py::gil_scoped_release>())
         .def("__len__", &IVFFlatIndex::size)
         .def("__repr__", [](const IVFFlatIndex& s) {
             return "IVFFlatIndex(dim=" + std::to_string(s.dim()) + ", nlist=" + std::to_string(s.nlist()) +
@@ -139,11 +147,15 @@ PYBIND11_MODULE(_C, m) {
              py::arg("nlist") = 4096, py::arg("nprobe") = 64, py::arg("m") = 16, py::arg("ksub") = 256)
         .def("set_quantizer", &IVFPQIndex::set_quantizer, py::arg("centroids"), py::arg("codebooks"))
         .def(
-            "add", [](IVFPQIndex& s, const at::Tensor& v, const py::object& ids) { s.add(v, opt_tensor(ids)); },
+            "add", [](IVFPQIndex& s, const at::Tensor& v, const py::object& ids) {
+                at::Tensor t = opt_tensor(ids);
+                py::gil_scoped_release release;
+                s.add(v, t);
+            },
             py::arg("vectors"), py::arg("ids") = py::none())
-        .def("search", &IVFPQIndex::search, py::arg("queries"), py::arg("k"))
-        .def("probe", &IVFPQIndex::probe, py::arg("queries"))
-        .def("search_probed", &IVFPQIndex::search_probed, py::arg("queries"), py::arg("probe"), py::arg("k"))
+        .def("search", &IVFPQIndex::search, py::arg("queries"), py::arg("k"), py::call_guard<py::gil_scoped_release>())
+        .def("probe", &IVFPQIndex::probe, py::arg("queries"), py::call_guard<py::gil_scoped_release>())
+        .def("search_probed", &IVFPQIndex::search_probed, py::arg("queries"), py::arg("probe"), py::arg("k"), py::call_guard<py::gil_scoped_release>())
         .def("reset", &IVFPQIndex::reset)
         .def("size", &IVFPQIndex::size)
         .def("dim", &IVFPQIndex::dim)
@@ -161,7 +173,7 @@ PYBIND11_MODULE(_C, m) {
         .def("stored_labels", &IVFPQIndex::stored_labels)
         .def("stored_codes", &IVFPQIndex::stored_codes)
         .def("stored_row_terms", &IVFPQIndex::stored_row_terms)
-        .def("restore", &IVFPQIndex::restore, py::arg("codes"), py::arg("labels"), py::arg("ids"))
+        .def("restore", &IVFPQIndex::restore, py::arg("codes"), py::arg("labels"), py::arg("ids"), py::call_guard<py::gil_scoped_release>())
         .def("query_major", &IVFPQIndex::query_major)
         .def("__len__", &IVFPQIndex::size)
         .def("__repr__", [](const IVFPQIndex& s) {

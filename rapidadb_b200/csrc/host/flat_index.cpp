@@ -121,16 +121,22 @@ Result topk_merge(const at::Tensor& vals, const at::Tensor& ids, int64_t k, bool
     TORCH_CHECK(vals.is_cuda() && ids.is_cuda(), "merge inputs must be CUDA tensors");
     TORCH_CHECK(vals.dim() == 3 && ids.sizes() == vals.sizes(), "merge inputs must be [G, Q, k]");
     c10::cuda::CUDAGuard guard(vals.device());
-    at::Tensor v = vals.to(at::kFloat).contiguous();
-    at::Tensor i = ids.to(at::kLong).contiguous();
+    // each list [Q, k] must be dense; the lists themselves may be strided
+    // (per-rank blocks of a gather buffer are read in place)
+    auto dense_lists = [](const at::Tensor& t) {
+        return t.stride(2) == 1 && t.stride(1) == t.size(2) && t.stride(0) >= t.size(1) * t.size(2);
+    };
+    at::Tensor v = vals.scalar_type() == at::kFloat && dense_lists(vals) ? vals : vals.to(at::kFloat).contiguous();
+    at::Tensor i = ids.scalar_type() == at::kLong && dense_lists(ids) ? ids : ids.to(at::kLong).contiguous();
     const int64_t G = v.size(0), Q = v.size(1), kin = v.size(2);
     TORCH_CHECK(k >= 1 && k <= G * kin, "k must be in [1, G * k_in]");
-    at::Tensor ov = at::empty({Q, k}, v.options());
-    at::Tensor oi = at::empty({Q, k}, i.options());
+    at::Tensor ov = at::empty({Q, k}, v.options().memory_format(at::MemoryFormat::Contiguous));
+    at::Tensor oi = at::empty({Q, k}, i.options().memory_format(at::MemoryFormat::Contiguous));
     if (Q == 0) return {ov, oi};
-    check_status(rdb_topk_merge(largest ? 1 : 0, v.data_ptr<float>(), i.data_ptr<int64_t>(), static_cast<int>(G),
-                                Q, static_cast<int>(kin), static_cast<int>(k), ov.data_ptr<float>(),
-                                oi.data_ptr<int64_t>(), stream_ptr()),
+    check_status(rdb_topk_merge_strided(largest ? 1 : 0, v.data_ptr<float>(), v.stride(0), i.data_ptr<int64_t>(),
+                                        i.stride(0), static_cast<int>(G), Q, static_cast<int>(kin),
+                                        static_cast<int>(k), ov.data_ptr<float>(), oi.data_ptr<int64_t>(),
+                                        stream_ptr()),
                  "topk merge");
     return {ov, oi};
 }

@@ -62,7 +62,8 @@ __device__ __forceinline__ unsigned long long seg_key(const SelectArgs& a, int64
         float s = a.dense[q * a.dense_n + t];
         return ((unsigned long long)score_key(s, largest) << 32) | (uint32_t)t;
     } else {
-        float s = a.merge_v[((int64_t)seg * a.nq + q) * a.kin + t];
+        const int64_t gs = a.gstride_v ? a.gstride_v : a.nq * a.kin;
+        float s = a.merge_v[(int64_t)seg * gs + q * a.kin + t];
         return ((unsigned long long)score_key(s, largest) << 32) | (uint32_t)(seg * a.kin + t);
     }
 }
@@ -321,7 +322,7 @@ __global__ void __launch_bounds__(NT) select_kernel(SelectArgs a) {
                         id = idx;
                     } else {
                         int g = idx / a.kin, t = idx % a.kin;
-                        id = a.merge_i[((int64_t)g * a.nq + q) * a.kin + t];
+                        id = a.merge_i[(int64_t)g * (a.gstride_i ? a.gstride_i : a.nq * a.kin) + q * a.kin + t];
                     }
                 } else {
                     v = largest ? -INFINITY : INFINITY;
@@ -637,7 +638,7 @@ __global__ void __launch_bounds__(NT, 2) select_warp_kernel(SelectArgs a) {
                     id = idx;
                 } else {
                     const int g = idx / a.kin, t = idx % a.kin;
-                    id = a.merge_i[((int64_t)g * a.nq + q) * a.kin + t];
+                    id = a.merge_i[(int64_t)g * (a.gstride_i ? a.gstride_i : a.nq * a.kin) + q * a.kin + t];
                 }
                 a.out_v[q * a.k + rank] = v;
                 a.out_i[q * a.k + rank] = id;

@@ -39,8 +39,10 @@ struct SelectArgs {
     int64_t dense_n;
 
     // SEL_MERGE
-    const float* merge_v;  // [G][nq][kin]
-    const int64_t* merge_i;
+    const float* merge_v;  // [G][nq][kin]; list g starts at merge_v + g * gstride_v
+    const int64_t* merge_i;  // same shape; list g starts at merge_i + g * gstride_i
+    int64_t gstride_v;       // 0: nq * kin
+    int64_t gstride_i;       // 0: nq * kin
     int G;
     int kin;
 

@@ -31,20 +31,22 @@ def shard_range(n: int, rank: int, world: int) -> Tuple[int, int]:
 
 def gather_candidates(local_d: torch.Tensor, local_i: torch.Tensor,
                       group: Optional[dist.ProcessGroup] = None) -> Tuple[torch.Tensor, torch.Tensor]:
-    """All-gather [Q, k] fp32 scores and int64 ids from every rank into
-    [G, Q, k] with one collective: each entry travels as three 32-bit words
-    (score bits, id low, id high)."""
+    """All-gather [Q, k] fp32 scores and int64 ids from every rank with one
+    collective.  Rank r's block of the gather buffer is [Q k scores | Q k ids]
+    (32-bit words, the id block 8-byte aligned); the returned [G, Q, k] score
+    and id tensors are views of the blocks (no copies), which the merge reads
+    in place."""
     world = dist.get_world_size(group)
     Q, k = local_d.shape
-    packed = torch.empty((Q, k, 3), dtype=torch.int32, device=local_d.device)
-    packed[:, :, 0] = local_d.float().contiguous().view(torch.int32)
-    packed[:, :, 1:] = local_i.long().contiguous().view(torch.int32).view(Q, k, 2)
-    # gathered along dim 0 (the layout every backend accepts)
-    out = torch.empty((world * Q, k, 3), dtype=torch.int32, device=local_d.device)
-    dist.all_gather_into_tensor(out, packed, group=group)
-    out = out.view(world, Q, k, 3)
-    vals = out[..., 0].contiguous().view(torch.float32)
-    ids = out[..., 1:].contiguous().view(torch.int64).view(world, Q, k)
+    nv = Q * k + (Q * k) % 2  # score words, padded so the ids stay 8-byte aligned
+    words = nv + 2 * Q * k
+    send = torch.empty(words, dtype=torch.int32, device=local_d.device)
+    send[:Q * k].view(torch.float32).copy_(local_d.reshape(-1))
+    send[nv:].view(torch.int64).copy_(local_i.reshape(-1))
+    out = torch.empty((world, words), dtype=torch.int32, device=local_d.device)
+    dist.all_gather_into_tensor(out.view(-1), send, group=group)
+    vals = out[:, :Q * k].view(torch.float32).view(world, Q, k)
+    ids = out[:, nv:].view(torch.int64).view(world, Q, k)
     return vals, ids
 
 

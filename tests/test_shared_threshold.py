@@ -44,3 +44,29 @@ def test_shared_threshold_equals_single(device, metric, k, world):
     ids = torch.stack([o[1] for o in outs])
     md, mi = _C.topk_merge(vals, ids, k, largest)
     assert_topk_match(rd.cpu().numpy(), ri.cpu().numpy(), md.cpu().numpy(), mi.cpu().numpy(), rtol=1e-5, atol=1e-5)
+
+
+@pytest.mark.parametrize("largest", [True, False])
+def test_merge_reads_gather_blocks_in_place(device, largest):
+    """The merge reads per-rank lists straight out of a gather buffer laid out
+    like sharded.gather_candidates (scores block, then 8-byte aligned ids)."""
+    import oracle
+    import rapidadb._C as _C
+
+    g = np.random.default_rng(3)
+    G, Q, k = 5, 77, 13  # odd Q * k: the id block needs the alignment pad
+    v = np.sort(g.standard_normal((G, Q, k)).astype(np.float32), axis=2)
+    if largest:
+        v = v[:, :, ::-1].copy()
+    ids = g.permutation(G * Q * k).astype(np.int64).reshape(G, Q, k)
+    nv = Q * k + (Q * k) % 2
+    buf = torch.zeros((G, nv + 2 * Q * k), dtype=torch.int32, device="cuda")
+    buf[:, :Q * k].view(torch.float32).copy_(torch.from_numpy(v.reshape(G, -1)))
+    buf[:, nv:].view(torch.int64).copy_(torch.from_numpy(ids.reshape(G, -1)))
+    vals = buf[:, :Q * k].view(torch.float32).view(G, Q, k)
+    idv = buf[:, nv:].view(torch.int64).view(G, Q, k)
+    assert not vals.is_contiguous()
+    md, mi = _C.topk_merge(vals, idv, k, largest)
+    rd, ri = oracle.topk_merge(v, ids, k, largest)
+    np.testing.assert_array_equal(md.cpu().numpy(), rd)
+    np.testing.assert_array_equal(mi.cpu().numpy(), ri)
