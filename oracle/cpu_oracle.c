@@ -1,10 +1,11 @@
 /*
  * CPU oracle for the RapidaDB search hot path.
  *
- * TEST INFRASTRUCTURE ONLY.  This file is the checker: it is loaded by the
- * tests, by __graft_entry__.smoke() and by bench.py's CPU-baseline leg, never
- * by the product path (rapidadb_b200/), which fails loudly when its CUDA
- * library is missing instead of falling back to anything here.
+ * TEST INFRASTRUCTURE ONLY.  The parity tests compare against this file: it
+ * is loaded by the tests, by __graft_entry__.smoke() and by bench.py's
+ * CPU-baseline leg, never by the product path (rapidadb_b200/), which fails
+ * loudly when its CUDA library is missing instead of falling back to anything
+ * here.
  *
  * Every function restates the reference's algorithm in plain C (+ OpenMP) and
  * cites the reference file:line it follows (paths are relative to the

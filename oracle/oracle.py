@@ -1,7 +1,7 @@
 """ctypes front end of ``liborc.so``, the C restatement in ``cpu_oracle.c``.
 
-TEST INFRASTRUCTURE ONLY: the checker for parity tests and the timed CPU
-baseline.  Arrays are numpy; every function returns fresh arrays.
+TEST INFRASTRUCTURE ONLY: what the parity tests compare against, and the
+timed CPU baseline.  Arrays are numpy; every function returns fresh arrays.
 """
 from __future__ import annotations
 

@@ -89,7 +89,7 @@ class RapidaDB:
             return _C.IVFPQIndex(cfg.dim, _metric_to_cpp(cfg.metric), cfg.nlist, cfg.nprobe,
                                  cfg.pq_m, cfg.pq_k)
         raise NotImplementedError(
-            f"Index type '{cfg.index_type.value}' not available in this build")
+            f"Index type '{cfg.index_type.value}' is not implemented")
 
     # -------------------------------------------------------------- training
     def train(self, vectors: torch.Tensor, group=None) -> None:

@@ -5,7 +5,7 @@ CUDA device.  Writes ``ref_golden.npz`` (reference outputs only; inputs are
 regenerated from the seeds in cases.py) to the directory given as argv[1]
 (default: this directory).
 
-    python tests/golden/make_golden.py gpurun_out/golden
+    python tests/golden/make_golden.py /tmp/golden
 """
 from __future__ import annotations
 
