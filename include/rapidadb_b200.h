@@ -201,7 +201,10 @@ int rdb_label_sort(const int32_t* labels, int64_t n, int K, int64_t* seg_start, 
  * scored with the flat formula of `metric` (L2 summed directly), go to
  * out_v / out_i [nprobe, nq, k] (ids[row], or -1 padding when a list has
  * fewer than k rows); rdb_topk_merge then keeps the best k per query.
- * q and rows share `dtype`; xv [n] per-row values (cosine only); k <= 32. */
+ * q and rows share `dtype`; xv [n] per-row values (rdb_row_sqnorms then
+ * rdb_vec_values: required for cosine; for L2 with k <= 24, |x|^2 lets the
+ * scan rank by |q|^2 + |x|^2 - 2 q.x and rescore k + 8 rows per list
+ * directly; NULL keeps the direct L2 scan); k <= 32. */
 size_t rdb_ivf_scan_workspace(int64_t nq, int nprobe, int nlist);
 int rdb_ivf_flat_scan(int metric, int dtype, const void* q, int64_t nq, int64_t ldq, int d, const int64_t* probe,
                       int nprobe, const void* rows, int64_t ldx, const float* xv, const int64_t* list_off, int nlist,

@@ -100,12 +100,21 @@ __global__ void probe_to_labels_kernel(const int64_t* __restrict__ probe, int64_
 // (j < 4): query operands are shared-memory broadcasts, each lane loads 4 row
 // values per k for 32 multiply-adds.  The tile's scores go through shared
 // memory to the per-query warp top-k lists (warp w keeps queries 4 w .. + 3).
+//
+// L2 with k <= kL2ExpandMaxK uses the expansion |q|^2 + |x|^2 - 2 q.x (one
+// multiply-add per element instead of a subtract and a multiply-add) and
+// keeps k + kL2Margin rows per (query, list); once the list is scanned, each
+// kept row is rescored with the direct sum of (q - x)^2 in dimension order
+// and the best k of those are written, so the reported distances are the
+// direct ones.  Larger k accumulates (q - x)^2 directly.
 
 constexpr int FQ = 32;   // queries per chunk
 constexpr int FR = 256;  // rows per tile
 constexpr int FK = 32;   // K chunk
 constexpr int FNT = 256;
 constexpr int FXS = FR + 1;  // row stride of the transposed row tile
+constexpr int kL2Margin = 8;
+constexpr int kL2ExpandMaxK = kMaxIvfK - kL2Margin;
 
 template <typename T>
 __device__ __forceinline__ float4 load4f(const T* p, bool vec, int nvalid) {
@@ -133,7 +142,8 @@ struct IvfFlatSmem {
     float s_qv[FQ];
 };
 
-template <typename T>
+// EXPAND: accumulate q.x (every metric but direct L2); false: accumulate (q - x)^2
+template <typename T, bool EXPAND>
 __global__ void __launch_bounds__(FNT, 2) ivf_flat_scan_kernel(
     int metric, int cos_small, const T* __restrict__ q, int64_t Q, int64_t ldq, int d, const float* __restrict__ qv,
     int nprobe, const int64_t* __restrict__ eperm, const int64_t* __restrict__ eseg, const T* __restrict__ rows,
@@ -142,6 +152,8 @@ __global__ void __launch_bounds__(FNT, 2) ivf_flat_scan_kernel(
     extern __shared__ __align__(16) unsigned char ivf_smem[];
     IvfFlatSmem& sh = *reinterpret_cast<IvfFlatSmem*>(ivf_smem);
     const bool largest = metric != RDB_METRIC_L2;
+    const bool rescore = EXPAND && metric == RDB_METRIC_L2;
+    const int kk = rescore ? min(kMaxIvfK, k + kL2Margin) : k;  // rows kept per (query, list)
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int qg = (warp & 3) * 8;     // this warp's first query
     const int rb = (warp >> 2) * 128;  // this warp's first tile row
@@ -221,11 +233,11 @@ __global__ void __launch_bounds__(FNT, 2) ivf_flat_scan_kernel(
                         for (int i = 0; i < 8; ++i)
 #pragma unroll
                             for (int j = 0; j < 4; ++j) {
-                                if (metric == RDB_METRIC_L2) {
+                                if constexpr (EXPAND) {
+                                    acc[i][j] = fmaf(av[i], bv[j], acc[i][j]);
+                                } else {
                                     const float df = av[i] - bv[j];
                                     acc[i][j] = fmaf(df, df, acc[i][j]);
-                                } else {
-                                    acc[i][j] = fmaf(av[i], bv[j], acc[i][j]);
                                 }
                             }
                     }
@@ -235,12 +247,14 @@ __global__ void __launch_bounds__(FNT, 2) ivf_flat_scan_kernel(
                 for (int j = 0; j < 4; ++j) {
                     const int ri = rb + lane + 32 * j;
                     const int64_t r = t0 + ri;
-                    const float xr = (metric == RDB_METRIC_COSINE && r < r1) ? xv[r] : 0.f;
+                    const bool need_xv = metric == RDB_METRIC_COSINE || rescore;
+                    const float xr = (need_xv && r < r1) ? xv[r] : 0.f;
 #pragma unroll
                     for (int i = 0; i < 8; ++i) {
                         const int qi = qg + i;
                         float sc = acc[i][j];
                         if (metric == RDB_METRIC_COSINE && r < r1) sc = final_score(metric, cos_small, sc, sh.s_qv[qi], xr);
+                        if (rescore) sc = sh.s_qv[qi] + xr - 2.f * sc;  // ranking only: rescored below
                         sh.S[qi][ri] = sc;
                     }
                 }
@@ -252,8 +266,46 @@ __global__ void __launch_bounds__(FNT, 2) ivf_flat_scan_kernel(
 #pragma unroll
                     for (int b = 0; b < FR / 32; ++b) {
                         const int64_t r = t0 + 32 * b + lane;
-                        st[j].offer(sh.S[qi][32 * b + lane], r, r < r1, k, largest, lane);
+                        st[j].offer(sh.S[qi][32 * b + lane], r, r < r1, kk, largest, lane);
                     }
+                }
+            }
+            if (rescore) {
+                // direct (q - x)^2 of the kept rows, then their best k
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    const int64_t qq = sh.s_q[warp * 4 + j];
+                    const bool has = qq >= 0 && lane < kk && st[j].id != INT64_MAX;
+                    float dist = INFINITY;
+                    if (has) {
+                        const T* qp = q + qq * ldq;
+                        const T* xp = rows + st[j].id * ldx;
+                        float a = 0.f;
+                        int c = 0;
+                        if (vec_q && vec_x) {
+                            for (; c + 4 <= d; c += 4) {
+                                const float4 u = load4f<T>(qp + c, true, 4);
+                                const float4 v = load4f<T>(xp + c, true, 4);
+                                float df = u.x - v.x;
+                                a = fmaf(df, df, a);
+                                df = u.y - v.y;
+                                a = fmaf(df, df, a);
+                                df = u.z - v.z;
+                                a = fmaf(df, df, a);
+                                df = u.w - v.w;
+                                a = fmaf(df, df, a);
+                            }
+                        }
+                        for (; c < d; ++c) {
+                            const float df = to_f<T>(qp[c]) - to_f<T>(xp[c]);
+                            a = fmaf(df, df, a);
+                        }
+                        dist = a;
+                    }
+                    WarpTopK fin;
+                    fin.init(false);
+                    fin.offer(dist, st[j].id, has, k, false, lane);
+                    st[j] = fin;
                 }
             }
             // write the (query, probe slot) lists
@@ -455,6 +507,24 @@ int invert_probes(const int64_t* probe, int64_t Q, int nprobe, int nlist, const 
                       label_sort_workspace(ne, nlist), s);
 }
 
+template <typename T>
+int ivf_flat_smem_attr(int bytes) {
+    RDB_CUDA_TRY(cudaFuncSetAttribute(ivf_flat_scan_kernel<T, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes));
+    RDB_CUDA_TRY(cudaFuncSetAttribute(ivf_flat_scan_kernel<T, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes));
+    return RDB_OK;
+}
+
+template <typename T>
+void launch_ivf_flat(bool expand, dim3 grid, cudaStream_t s, int metric, int cos_small, const void* q, int64_t nq,
+                     int64_t ldq, int d, const float* qv, int nprobe, const int64_t* eperm, const int64_t* eseg,
+                     const void* rows, int64_t ldx, const float* xv, const int64_t* list_off, int nlist,
+                     const int64_t* ids, int k, float* out_v, int64_t* out_i) {
+    auto kern = expand ? ivf_flat_scan_kernel<T, true> : ivf_flat_scan_kernel<T, false>;
+    kern<<<grid, FNT, sizeof(IvfFlatSmem), s>>>(metric, cos_small, static_cast<const T*>(q), nq, ldq, d, qv, nprobe,
+                                                eperm, eseg, static_cast<const T*>(rows), ldx, xv, list_off, nlist,
+                                                ids, k, out_v, out_i);
+}
+
 size_t pq_smem(int d, int M, int ksub) {
     return sizeof(float) * ((size_t)ksub * d + (size_t)M * ksub + ((d + 3) & ~3)) +
            sizeof(unsigned long long) * (PNW * kMaxIvfK + 1);
@@ -486,14 +556,16 @@ int rdb_ivf_flat_scan(int metric, int dtype, const void* q, int64_t nq, int64_t 
     RDB_TRY(invert_probes(probe, nq, nprobe, nlist, w, base, s));
     float* qv = reinterpret_cast<float*>(base + w.off_qv);
     const int cos_small = d <= 128 ? 1 : 0;
-    if (metric == RDB_METRIC_COSINE) {
+    // L2 with k <= kL2ExpandMaxK ranks by |q|^2 + |x|^2 - 2 q.x, then rescores
+    const bool expand = metric != RDB_METRIC_L2 || (k <= kL2ExpandMaxK && xv != nullptr);
+    if (metric == RDB_METRIC_COSINE || (metric == RDB_METRIC_L2 && expand)) {
         RDB_CHECK_ARG(xv, "cosine needs per-row values");
         if (ldq == d) {
             RDB_TRY(rdb_row_sqnorms(dtype, q, nq, d, qv, s));
         } else {
             RDB_TRY(rdb_row_sqnorms(dtype, q, nq, (int)ldq, qv, s));
         }
-        RDB_TRY(rdb_vec_values(metric, d, qv, nq, qv, s));
+        if (metric == RDB_METRIC_COSINE) RDB_TRY(rdb_vec_values(metric, d, qv, nq, qv, s));
     }
     // x: lists; y: CTAs sharing a list's query chunks, ~4x the mean chunk count
     const int64_t mean_chunks = (nq * nprobe + (int64_t)nlist * FQ - 1) / ((int64_t)nlist * FQ);
@@ -506,10 +578,9 @@ int rdb_ivf_flat_scan(int metric, int dtype, const void* q, int64_t nq, int64_t 
         cudaGetDevice(&dev);
         if (dev < 64 && !attr[dev]) {
             const int bytes = (int)sizeof(IvfFlatSmem);
-            RDB_CUDA_TRY(cudaFuncSetAttribute(ivf_flat_scan_kernel<float>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes));
-            RDB_CUDA_TRY(cudaFuncSetAttribute(ivf_flat_scan_kernel<__half>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes));
-            RDB_CUDA_TRY(cudaFuncSetAttribute(ivf_flat_scan_kernel<__nv_bfloat16>,
-                                              cudaFuncAttributeMaxDynamicSharedMemorySize, bytes));
+            RDB_TRY(ivf_flat_smem_attr<float>(bytes));
+            RDB_TRY(ivf_flat_smem_attr<__half>(bytes));
+            RDB_TRY(ivf_flat_smem_attr<__nv_bfloat16>(bytes));
             attr[dev] = true;
         }
     }
@@ -517,19 +588,16 @@ int rdb_ivf_flat_scan(int metric, int dtype, const void* q, int64_t nq, int64_t 
     RDB_TRY(timing_begin(TIMING_IVF_SCAN, s, &stop_ev));
     switch (dtype) {
         case RDB_F32:
-            ivf_flat_scan_kernel<float><<<grid, FNT, sizeof(IvfFlatSmem), s>>>(metric, cos_small, (const float*)q, nq, ldq, d, qv, nprobe,
-                                                             eperm, eseg, (const float*)rows, ldx, xv, list_off, nlist,
-                                                             ids, k, out_v, out_i);
+            launch_ivf_flat<float>(expand, grid, s, metric, cos_small, q, nq, ldq, d, qv, nprobe, eperm, eseg, rows,
+                                   ldx, xv, list_off, nlist, ids, k, out_v, out_i);
             break;
         case RDB_F16:
-            ivf_flat_scan_kernel<__half><<<grid, FNT, sizeof(IvfFlatSmem), s>>>(metric, cos_small, (const __half*)q, nq, ldq, d, qv,
-                                                              nprobe, eperm, eseg, (const __half*)rows, ldx, xv,
-                                                              list_off, nlist, ids, k, out_v, out_i);
+            launch_ivf_flat<__half>(expand, grid, s, metric, cos_small, q, nq, ldq, d, qv, nprobe, eperm, eseg, rows,
+                                    ldx, xv, list_off, nlist, ids, k, out_v, out_i);
             break;
         default:
-            ivf_flat_scan_kernel<__nv_bfloat16><<<grid, FNT, sizeof(IvfFlatSmem), s>>>(
-                metric, cos_small, (const __nv_bfloat16*)q, nq, ldq, d, qv, nprobe, eperm, eseg,
-                (const __nv_bfloat16*)rows, ldx, xv, list_off, nlist, ids, k, out_v, out_i);
+            launch_ivf_flat<__nv_bfloat16>(expand, grid, s, metric, cos_small, q, nq, ldq, d, qv, nprobe, eperm, eseg,
+                                           rows, ldx, xv, list_off, nlist, ids, k, out_v, out_i);
     }
     RDB_LAUNCH_CHECK();
     if (stop_ev) RDB_CUDA_TRY(cudaEventRecord(stop_ev, s));

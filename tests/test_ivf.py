@@ -51,6 +51,30 @@ def test_ivf_flat_matches_oracle(device, metric):
     np.testing.assert_allclose(d.cpu().numpy(), rd, rtol=1e-4, atol=1e-4)
 
 
+@pytest.mark.parametrize("k,shift", [(24, 0.0), (25, 0.0), (32, 0.0), (10, 20.0)])
+def test_ivf_flat_l2_expansion_and_direct(device, k, shift):
+    """L2 with k <= 24 ranks by |q|^2 + |x|^2 - 2 q.x and rescores k + 8 rows
+    per list directly; k > 24 sums (q - x)^2 directly.  Both report the
+    direct distances, also when every vector carries a large common offset
+    (|x|^2 far above the neighbour distances)."""
+    import rapidadb._C as _C
+    from rapidadb_b200.kmeans import kmeans
+
+    x, g = mixture(5, 12000, 48, 30)
+    x += shift
+    q = (x[g.integers(0, len(x), 50)] + 0.5 * g.standard_normal((50, 48))).astype(np.float32)
+    xt = torch.from_numpy(x).cuda()
+    cent = kmeans(xt, 32, 8, 0.0, seed=2).centroids
+    idx = _C.IVFFlatIndex(48, _C.Metric.L2, 32, 6)
+    idx.set_quantizer(cent)
+    idx.add(xt)
+    off, row_ids, xs = layout(idx, x)
+    d, i = idx.search(torch.from_numpy(q).cuda(), k)
+    rd, ri = oracle.ivf_flat_search("l2", q, cent.cpu().numpy(), off, xs, row_ids, 6, k)
+    assert recall(i.cpu().numpy(), ri) >= 0.999
+    np.testing.assert_allclose(d.cpu().numpy(), rd, rtol=1e-5, atol=1e-5)
+
+
 def test_ivf_flat_bf16_storage(device):
     import rapidadb._C as _C
     from rapidadb_b200.kmeans import kmeans
