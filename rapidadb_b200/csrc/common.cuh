@@ -75,6 +75,7 @@ enum DeviceStatus : unsigned {
     DEV_TIMEOUT_MMA = 1u << 1,
     DEV_TIMEOUT_EPILOGUE = 1u << 2,
     DEV_OVERFLOW = 1u << 3,
+    DEV_TIMEOUT_SIMT = 1u << 4,  // TMA-fed CUDA-core scan
 };
 unsigned* device_status_word();  // per-device, zero-initialised
 

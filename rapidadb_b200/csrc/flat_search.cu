@@ -103,7 +103,9 @@ FlatPlan make_plan(int metric, int dtype, int64_t nq, int64_t n, int d, int k, i
     P.rtile = P.tc ? kTcRows : kSimtRows;
     P.nq = nq;
     const int sms = num_sms();
-    const int64_t target = P.tc ? (pair ? sms / 2 : sms) : 2LL * sms;
+    // CTAs that run at once: TMA-fed fp32 scans hold one per SM (their ring
+    // fills the shared memory), the register-staged CUDA-core scan two
+    const int64_t target = P.tc ? (pair ? sms / 2 : sms) : dtype == RDB_F32 ? sms : 2LL * sms;
 
     // sample size S, a power of two >= 8 k: the sample pass costs S / n of the
     // main scan, the candidates (about n k / S per query) cost the main scan's
@@ -111,7 +113,11 @@ FlatPlan make_plan(int metric, int dtype, int64_t nq, int64_t n, int d, int k, i
     // and its candidates are costly relative to its cheap per-row MMA work:
     // ~6 sqrt(n k) rows in [1024, 131072]; the CUDA-core sample pass emits
     // every sampled score as a candidate: ~1.5 sqrt(n k) in [1024, 32768].
-    const double sd = (P.tc ? 6.0 : 1.5) * sqrt((double)n * (double)k);
+    double sd = (P.tc ? 6.0 : 1.5) * sqrt((double)n * (double)k);
+    // one CUDA-core query block: the sample pass runs one CTA per 256-row
+    // tile, each as long as any other, so up to 32 tiles cost no more than
+    // one and tighten the threshold (fewer candidates for the main pass)
+    if (!P.tc && nq <= kSimtQueries) sd = std::max(sd, 8192.0);
     const int64_t smax = P.tc ? 131072 : 32768;
     int64_t S = 1024;
     while (S < sd && S < smax) S <<= 1;

@@ -682,7 +682,10 @@ int launch_select(const SelectArgs& a, cudaStream_t stream) {
     // a warp re-reads elements beyond its on-chip cache on every pass: larger
     // expected inputs go to the CTA kernel
     const bool small = a.expect > 0 ? a.expect <= kWarpCache : max_elems <= 32768;
-    if (out_k <= kWarpOut && nseg <= kWarpSeg && small) {
+    // fewer queries than SMs: a CTA per query spreads them over the GPU (the
+    // warp kernel would occupy nq / 8 SMs)
+    const bool many = a.nq >= num_sms();
+    if (out_k <= kWarpOut && nseg <= kWarpSeg && small && many) {
         const int64_t blocks = (a.nq + NWARP - 1) / NWARP;
         static bool wattr[64] = {false};
         if (dev < 64 && !wattr[dev]) {

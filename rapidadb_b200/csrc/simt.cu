@@ -5,12 +5,16 @@
 // The scan tiles 32 queries x 256 rows per CTA (256 threads, 8 x 4 outputs per
 // thread) over K chunks of 32 staged through shared memory; each CTA walks a
 // contiguous split of rows so its per-query candidate counters stay private.
+// fp32 operands with TMA-compatible layouts go through simt_tma_scan_kernel
+// (a 4-stage TMA ring, one CTA per SM); other dtypes / layouts and the dense
+// distance matrix through simt_scan_kernel (register-staged chunks).
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 
 #include <algorithm>
 
 #include "scan.cuh"
+#include "tma.cuh"
 
 namespace rdb {
 namespace {
@@ -81,6 +85,48 @@ __device__ __forceinline__ float4 load4(const T* p, bool vec, int nvalid) {
 #pragma unroll
     for (int i = 0; i < 4; ++i) v[i] = i < nvalid ? to_f<T>(p[i]) : 0.f;
     return make_float4(v[0], v[1], v[2], v[3]);
+}
+
+// SCAN_FILTER / SCAN_ARGMIN handling of one tile score: v = dot product (or
+// the directly summed squared distance) of query q = q0 + qi and logical row r
+template <int MODE, bool DIRECT_L2>
+__device__ __forceinline__ void emit_score(const ScanArgs& a, float v, int qi, int64_t q, int64_t r, float xr,
+                                           int split, const float* sA, const float* sB, const float* sQv, int* scnt,
+                                           unsigned long long& best) {
+    if (MODE == SCAN_FILTER) {
+        if (v >= fmaf(sA[qi], xr, sB[qi])) {
+            const int slot = atomicAdd(&scnt[qi], 1);
+            if (slot < a.cap)
+                a.cand[((int64_t)split * a.nq + q) * a.cap + slot] =
+                    make_uint2(__float_as_uint(final_score(a.metric, a.cos_small, v, sQv[qi], xr)), (uint32_t)r);
+        }
+    } else {  // SCAN_ARGMIN (squared L2; exact: summed directly)
+        const float dist = DIRECT_L2 ? v : fmaxf(sQv[qi] + xr - 2.f * v, 0.f);
+        const unsigned long long key = ((unsigned long long)float_asc_key(dist) << 32) | (uint32_t)r;
+        best = min(best, key);
+    }
+}
+
+// end of a CTA's split: per-query candidate counts / arg-best to global memory
+template <int MODE>
+__device__ __forceinline__ void finish_split(const ScanArgs& a, int64_t q0, int split, int qg, int lane, int tid,
+                                             const int* scnt, unsigned long long* sbest,
+                                             const unsigned long long (&best)[8]) {
+    if (MODE == SCAN_ARGMIN) {
+        // the 32 lanes of a warp share its 8 queries
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            unsigned long long b = best[i];
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) b = min(b, __shfl_xor_sync(0xffffffffu, b, o));
+            if (lane == 0) atomicMin(&sbest[qg + i], b);
+        }
+    }
+    __syncthreads();
+    if (tid < BQ && q0 + tid < a.nq) {
+        if (MODE == SCAN_FILTER) a.counts[(int64_t)split * a.nq + q0 + tid] = scnt[tid];
+        if (MODE == SCAN_ARGMIN) a.best[(int64_t)split * a.nq + q0 + tid] = sbest[tid];
+    }
 }
 
 template <typename T, int MODE, bool DIRECT_L2>
@@ -222,36 +268,204 @@ __global__ void __launch_bounds__(NT, 2) simt_scan_kernel(ScanArgs a) {
                         s = v;
                     }
                     a.dense_out[q * a.ld_out + r] = s;
-                } else if (MODE == SCAN_FILTER) {
-                    if (v >= fmaf(sA[qi], xvr[j], sB[qi])) {
-                        const int slot = atomicAdd(&scnt[qi], 1);
-                        if (slot < a.cap)
-                            a.cand[((int64_t)split * a.nq + q) * a.cap + slot] = make_uint2(
-                                __float_as_uint(final_score(a.metric, a.cos_small, v, sQv[qi], xvr[j])), (uint32_t)r);
-                    }
-                } else {  // SCAN_ARGMIN (squared L2; exact: summed directly)
-                    const float dist = DIRECT_L2 ? v : fmaxf(sQv[qi] + xvr[j] - 2.f * v, 0.f);
-                    const unsigned long long key = ((unsigned long long)float_asc_key(dist) << 32) | (uint32_t)r;
-                    best[i] = min(best[i], key);
+                } else {
+                    emit_score<MODE, DIRECT_L2>(a, v, qi, q, r, xvr[j], split, sA, sB, sQv, scnt, best[i]);
                 }
             }
         }
     }
-    if (MODE == SCAN_ARGMIN) {
-        // the 32 lanes of a warp share its 8 queries
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-            unsigned long long b = best[i];
-#pragma unroll
-            for (int o = 16; o > 0; o >>= 1) b = min(b, __shfl_xor_sync(0xffffffffu, b, o));
-            if (lane == 0) atomicMin(&sbest[qg + i], b);
-        }
+    finish_split<MODE>(a, q0, split, qg, lane, tid, scnt, sbest, best);
+}
+
+// ------------------------------------------------- TMA-fed fp32 scan --
+//
+// simt_scan_kernel's tile and thread mapping (32 queries x 256 rows, 8 x 4
+// outputs per thread) for fp32 rows, with the operands delivered by TMA: a
+// ring of kTmaStages stages, each holding one K chunk of 32 floats (one
+// 128-byte line per row, 128-byte swizzle) of the query tile and of the row
+// tile, so that several chunks are in flight per CTA and the DRAM latency
+// hides behind the multiply-adds of earlier chunks.  One CTA per SM walks
+// its split of rows tile by tile, the ring running on across tiles; thread 0
+// refills a stage after the CTA barrier that ends its use.  Swizzled reads:
+// 16-byte group g of line L sits at group g ^ (L mod 8), so the lanes of a
+// warp (rows L = lane + 32 j) read 8 distinct groups per 128 bytes and the
+// query reads are broadcasts.  Summation order per (query, row) is
+// k = 0, 1, ..., d - 1 as in simt_scan_kernel (bit-identical results);
+// columns past d and rows past n read as zero.
+
+constexpr int kTmaStages = 4;
+constexpr int kTmaXBytes = BN * BK * 4;  // 32 KB
+constexpr int kTmaQBytes = BQ * BK * 4;  // 4 KB
+constexpr int kTmaStageBytes = kTmaXBytes + kTmaQBytes;
+constexpr int kTmaSmemBytes = kTmaStages * kTmaStageBytes + 1024 /* alignment */ + 64 /* barriers */;
+static_assert(BK * 4 == 128, "one 128-byte swizzle line per row and chunk");
+
+template <int MODE, bool DIRECT_L2>
+__global__ void __launch_bounds__(NT, 1)
+    simt_tma_scan_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_constant__ CUtensorMap tmap_x,
+                         const ScanArgs a, unsigned* status) {
+    extern __shared__ unsigned char tma_smem_raw[];
+    __shared__ float sA[BQ], sB[BQ], sQv[BQ];
+    __shared__ int scnt[BQ];
+    __shared__ unsigned long long sbest[BQ];
+
+    // 1024-byte aligned ring (the swizzle atom); an offset from the shared
+    // array itself keeps the accesses in the shared window (LDS, not generic)
+    unsigned char* smem = tma_smem_raw + ((1024u - (tma::smem_addr(tma_smem_raw) & 1023u)) & 1023u);
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + kTmaStages * kTmaStageBytes);
+
+    const int split = blockIdx.x;
+    const int64_t q0 = ((int64_t)blockIdx.z * gridDim.y + blockIdx.y) * BQ;
+    if (q0 >= a.nq) return;
+    const int64_t r_begin = (int64_t)split * a.rows_per_split;
+    const int64_t r_end = min(a.n, r_begin + a.rows_per_split);
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int qg = (warp & 3) * 8;
+    const int rb = (warp >> 2) * 128;
+    const int nchunk = (a.d + BK - 1) / BK;
+    const int ntile = (int)((r_end - r_begin + BN - 1) / BN);
+    const int nitems = ntile * nchunk;  // (tile, chunk) pairs in ring order
+
+    auto issue = [&](int it) {
+        const int st = it % kTmaStages;
+        const int t = it / nchunk, c = it - t * nchunk;
+        unsigned char* dst = smem + st * kTmaStageBytes;
+        tma::bar_expect_tx(&full[st], kTmaStageBytes);
+        tma::load_2d(&tmap_x, &full[st], dst, c * BK, (int)(r_begin + (int64_t)t * BN));
+        tma::load_2d(&tmap_q, &full[st], dst + kTmaXBytes, c * BK, (int)q0);
+    };
+    if (tid == 0) {
+        tma::prefetch_map(&tmap_x);
+        tma::prefetch_map(&tmap_q);
+        for (int st = 0; st < kTmaStages; ++st) tma::bar_init(&full[st], 1);
+        tma::fence_init();
+    }
+    if (tid < BQ) {
+        const int64_t q = q0 + tid;
+        const float qv = (q < a.nq && a.qv) ? a.qv[q] : 0.f;
+        const float thr = (a.thr && q < a.nq) ? a.thr[q] : __int_as_float(0x7fc00000);
+        const FilterCoef f = filter_coef(a.metric, a.cos_small, thr, qv);
+        sA[tid] = f.A;
+        sB[tid] = f.B;
+        sQv[tid] = qv;
+        scnt[tid] = 0;
+        sbest[tid] = ~0ull;
     }
     __syncthreads();
-    if (tid < BQ && q0 + tid < a.nq) {
-        if (MODE == SCAN_FILTER) a.counts[(int64_t)split * a.nq + q0 + tid] = scnt[tid];
-        if (MODE == SCAN_ARGMIN) a.best[(int64_t)split * a.nq + q0 + tid] = sbest[tid];
+    if (tid == 0)
+        for (int it = 0; it < min(kTmaStages, nitems); ++it) issue(it);
+
+    unsigned long long best[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) best[i] = ~0ull;
+    const int sw = lane & 7;  // (row line) mod 8 of every row this lane reads
+    int it = 0;
+    for (int t = 0; t < ntile; ++t) {
+        const int64_t r0 = r_begin + (int64_t)t * BN;
+        float acc[8][4];
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+#pragma unroll
+            for (int j = 0; j < 4; ++j) acc[i][j] = 0.f;
+        for (int c = 0; c < nchunk; ++c, ++it) {
+            const int st = it % kTmaStages;
+            const bool ok = tma::bar_wait(&full[st], (uint32_t)((it / kTmaStages) & 1));
+            const float* Xs = reinterpret_cast<const float*>(smem + st * kTmaStageBytes);
+            const float* Qs = reinterpret_cast<const float*>(smem + st * kTmaStageBytes + kTmaXBytes);
+            if (ok) {
+#pragma unroll 2
+                for (int g = 0; g < BK / 4; ++g) {
+                    float4 xb[4];
+#pragma unroll
+                    for (int j = 0; j < 4; ++j)
+                        xb[j] = *reinterpret_cast<const float4*>(Xs + (rb + lane + 32 * j) * BK + ((g ^ sw) << 2));
+#pragma unroll
+                    for (int i = 0; i < 8; ++i) {
+                        const float4 qa = *reinterpret_cast<const float4*>(Qs + (qg + i) * BK + ((g ^ i) << 2));
+#pragma unroll
+                        for (int j = 0; j < 4; ++j) {
+                            if (DIRECT_L2) {
+                                float df = qa.x - xb[j].x;
+                                acc[i][j] = fmaf(df, df, acc[i][j]);
+                                df = qa.y - xb[j].y;
+                                acc[i][j] = fmaf(df, df, acc[i][j]);
+                                df = qa.z - xb[j].z;
+                                acc[i][j] = fmaf(df, df, acc[i][j]);
+                                df = qa.w - xb[j].w;
+                                acc[i][j] = fmaf(df, df, acc[i][j]);
+                            } else {
+                                acc[i][j] = fmaf(qa.x, xb[j].x, acc[i][j]);
+                                acc[i][j] = fmaf(qa.y, xb[j].y, acc[i][j]);
+                                acc[i][j] = fmaf(qa.z, xb[j].z, acc[i][j]);
+                                acc[i][j] = fmaf(qa.w, xb[j].w, acc[i][j]);
+                            }
+                        }
+                    }
+                }
+            }
+            // every thread is done with stage st (and agrees whether a wait gave up)
+            if (__syncthreads_or(!ok)) {
+                if (tid == 0) {
+                    if (status) atomicOr(status, DEV_TIMEOUT_SIMT);
+                    // bounded wait for the copies still in flight, then leave
+                    for (int j = it; j < min(it + kTmaStages, nitems); ++j)
+                        tma::bar_wait(&full[j % kTmaStages], (uint32_t)((j / kTmaStages) & 1));
+                }
+                __syncthreads();
+                return;
+            }
+            if (tid == 0 && it + kTmaStages < nitems) issue(it + kTmaStages);
+        }
+        float xvr[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const int64_t r = r0 + rb + lane + 32 * j;
+            xvr[j] = (r < r_end && a.xv) ? a.xv[r * a.row_step] : 0.f;
+        }
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const int qi = qg + i;
+            const int64_t q = q0 + qi;
+            if (q >= a.nq) continue;
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const int64_t r = r0 + rb + lane + 32 * j;
+                if (r >= r_end) continue;
+                emit_score<MODE, DIRECT_L2>(a, acc[i][j], qi, q, r, xvr[j], split, sA, sB, sQv, scnt, best[i]);
+            }
+        }
     }
+    finish_split<MODE>(a, q0, split, qg, lane, tid, scnt, sbest, best);
+}
+
+// fp32 rows and queries whose layout suits the TMA maps (16-byte aligned
+// bases and strides, coordinates within int32)
+bool tma_scan_ok(const ScanArgs& a, int mode) {
+    if (a.dtype != RDB_F32) return false;
+    if (mode != SCAN_FILTER && mode != SCAN_ARGMIN && mode != SCAN_ARGMIN_EXACT) return false;
+    if ((reinterpret_cast<uintptr_t>(a.q) & 15) || (reinterpret_cast<uintptr_t>(a.x) & 15)) return false;
+    if (a.ldq % 4 || (a.ldx * a.row_step) % 4) return false;
+    if (a.nq >= (1LL << 31) - BQ || a.n >= (1LL << 31) - 2 * BN) return false;
+    if (a.ldx * a.row_step * 4 >= (1LL << 40) || a.ldq * 4 >= (1LL << 40)) return false;
+    return tma::encode_tiled() != nullptr;
+}
+
+template <int MODE, bool DIRECT_L2>
+int launch_tma_typed(const ScanArgs& a, dim3 grid, cudaStream_t s) {
+    static bool attr[64] = {false};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 64 && !attr[dev]) {
+        RDB_CUDA_TRY(cudaFuncSetAttribute(simt_tma_scan_kernel<MODE, DIRECT_L2>,
+                                          cudaFuncAttributeMaxDynamicSharedMemorySize, kTmaSmemBytes));
+        attr[dev] = true;
+    }
+    CUtensorMap mq, mx;
+    RDB_TRY(tma::map_f32_2d(&mq, a.q, a.nq, a.d, a.ldq * 4, BK, BQ));
+    RDB_TRY(tma::map_f32_2d(&mx, a.x, a.n, a.d, a.ldx * a.row_step * 4, BK, BN));
+    simt_tma_scan_kernel<MODE, DIRECT_L2><<<grid, NT, kTmaSmemBytes, s>>>(mq, mx, a, device_status_word());
+    RDB_LAUNCH_CHECK();
+    return RDB_OK;
 }
 
 template <typename T>
@@ -280,6 +494,11 @@ int launch_scan_simt(const ScanArgs& a, int mode, cudaStream_t s) {
     const int64_t gy = std::min<int64_t>(gq, 65535), gz = (gq + gy - 1) / gy;
     RDB_CHECK_ARG(gz <= 65535, "too many queries for one launch (%lld)", (long long)a.nq);
     dim3 grid(a.nsplit, (unsigned)gy, (unsigned)gz);
+    if (tma_scan_ok(a, mode)) {
+        if (mode == SCAN_FILTER) return launch_tma_typed<SCAN_FILTER, false>(a, grid, s);
+        if (mode == SCAN_ARGMIN) return launch_tma_typed<SCAN_ARGMIN, false>(a, grid, s);
+        return launch_tma_typed<SCAN_ARGMIN, true>(a, grid, s);
+    }
     switch (a.dtype) {
         case RDB_F32: return launch_typed<float>(a, mode, s, grid);
         case RDB_F16: return launch_typed<__half>(a, mode, s, grid);

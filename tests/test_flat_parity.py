@@ -32,6 +32,7 @@ SHAPES = [  # (N, Q, d, k)
     (300, 5, 8, 300),
     (4097, 1, 200, 1),
     (20000, 33, 768, 100),
+    (20000, 300, 64, 10),  # at least one query per SM: the warp-per-query selects
 ]
 
 
