@@ -621,6 +621,10 @@ def run_ivf(args, wl):
     # e2e: host query batch in, results out, each step
     q_host = q.cpu().pin_memory()
     qbuf = torch.empty_like(q)
+    for _ in range(max(1, args.warmup // 2)):
+        qbuf.copy_(q_host, non_blocking=True)
+        rd, ri = searcher.search(qbuf, k)
+        rd.cpu(), ri.cpu()
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()

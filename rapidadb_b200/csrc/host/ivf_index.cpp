@@ -237,6 +237,8 @@ at::Tensor IVFBase::list_sizes() const {
 
 // --------------------------------------------------------------- IVF-Flat
 
+constexpr int64_t kIvfExpandRowsPerList = 768;
+
 IVFFlatIndex::IVFFlatIndex(int dim, Metric metric, int nlist, int nprobe, Precision precision)
     : IVFBase(dim, metric, nlist, nprobe), precision_(precision) {
     ld_ = padded_ld(dim, storage_type(precision));
@@ -305,9 +307,14 @@ Result IVFFlatIndex::search_probed(const at::Tensor& queries, const at::Tensor& 
     at::Tensor cv = at::empty({np, nq, k}, q.options().dtype(at::kFloat));
     at::Tensor ci = at::empty({np, nq, k}, q.options().dtype(at::kLong));
     at::Tensor ws = ws_bytes(q, rdb_ivf_scan_workspace(nq, np, nlist_));
+    // L2 ranked by |q|^2 + |x|^2 - 2 q.x (one FMA per element, k + 8 rows per
+    // (query, list) rescored directly) pays off once lists hold about 768
+    // rows on average; shorter lists are scanned with (q - x)^2 directly
+    // (no row values passed)
+    const bool expand = metric_ != Metric::L2 || n_ >= kIvfExpandRowsPerList * static_cast<int64_t>(nlist_);
     check_status(rdb_ivf_flat_scan(static_cast<int>(metric_), dtype_code(rows_.scalar_type()), q.data_ptr(), nq, ld_,
                                    dim_, probe_lists.data_ptr<int64_t>(), np, rows_.data_ptr(), ld_,
-                                   xv_.data_ptr<float>(), list_off_.data_ptr<int64_t>(), nlist_,
+                                   expand ? xv_.data_ptr<float>() : nullptr, list_off_.data_ptr<int64_t>(), nlist_,
                                    ids_.data_ptr<int64_t>(), static_cast<int>(k), cv.data_ptr<float>(),
                                    ci.data_ptr<int64_t>(), ws.data_ptr(), ws.numel(), stream_ptr()),
                  "ivf scan");

@@ -283,6 +283,7 @@ __global__ void __launch_bounds__(FNT, 2) ivf_flat_scan_kernel(
                         float a = 0.f;
                         int c = 0;
                         if (vec_q && vec_x) {
+#pragma unroll 8
                             for (; c + 4 <= d; c += 4) {
                                 const float4 u = load4f<T>(qp + c, true, 4);
                                 const float4 v = load4f<T>(xp + c, true, 4);

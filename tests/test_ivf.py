@@ -53,14 +53,15 @@ def test_ivf_flat_matches_oracle(device, metric):
 
 @pytest.mark.parametrize("k,shift", [(24, 0.0), (25, 0.0), (32, 0.0), (10, 20.0)])
 def test_ivf_flat_l2_expansion_and_direct(device, k, shift):
-    """L2 with k <= 24 ranks by |q|^2 + |x|^2 - 2 q.x and rescores k + 8 rows
-    per list directly; k > 24 sums (q - x)^2 directly.  Both report the
-    direct distances, also when every vector carries a large common offset
-    (|x|^2 far above the neighbour distances)."""
+    """L2 with k <= 24 over lists of >= 768 rows on average ranks by
+    |q|^2 + |x|^2 - 2 q.x and rescores k + 8 rows per list directly; k > 24
+    (and short lists, test_ivf_flat_matches_oracle) sum (q - x)^2 directly.
+    Both report the direct distances, also when every vector carries a large
+    common offset (|x|^2 far above the neighbour distances)."""
     import rapidadb._C as _C
     from rapidadb_b200.kmeans import kmeans
 
-    x, g = mixture(5, 12000, 48, 30)
+    x, g = mixture(5, 40000, 48, 30)  # 1,250 rows per list
     x += shift
     q = (x[g.integers(0, len(x), 50)] + 0.5 * g.standard_normal((50, 48))).astype(np.float32)
     xt = torch.from_numpy(x).cuda()
