@@ -54,8 +54,9 @@ const char* rdb_last_error(void);
 /* ABI version (major * 100 + minor). */
 int rdb_version(void);
 /* Reads (and with clear != 0 resets) the current device's status word, where
- * kernels record bounded waits that ran out (bit 0 producer, 1 MMA issuer,
- * 2 epilogue).  Synchronises the device. */
+ * kernels record bounded waits that ran out (tensor-core scan: bit 0 producer,
+ * 1 MMA issuer, 2 epilogue; bit 4 the TMA-fed CUDA-core scan).  Synchronises
+ * the device. */
 int rdb_device_status(unsigned* out_host, int clear);
 
 /* Dense [nq, nx] score matrix with the reference formulas.
@@ -194,8 +195,11 @@ int rdb_label_sort(const int32_t* labels, int64_t n, int K, int64_t* seg_start, 
 /* ---- IVF-Flat / IVF-PQ (no reference implementation: the reference only
  * names them, python/rapidadb/config.py:14-18, :50-56; index.py:64-69) ---- */
 
-/* List-major scan of an IVF index whose rows are stored list by list
- * (list l = rows list_off[l] .. list_off[l + 1] - 1).  probe [nq, nprobe]
+/* List-major scan of an IVF index whose rows are stored list by list:
+ * list l is rows list_off[l] .. list_end[l] - 1, inside its capacity
+ * list_off[l] .. list_off[l + 1] - 1 (list_end NULL: the whole capacity, no
+ * free slots; free slots let rows be appended without moving the others, see
+ * rdb_pq_scatter_codes).  probe [nq, nprobe]
  * holds each query's lists (from a coarse rdb_flat_search over the
  * centroids).  For every (query, probe slot) the best k rows of that list,
  * scored with the flat formula of `metric` (L2 summed directly), go to
@@ -207,9 +211,9 @@ int rdb_label_sort(const int32_t* labels, int64_t n, int K, int64_t* seg_start, 
  * directly; NULL keeps the direct L2 scan); k <= 32. */
 size_t rdb_ivf_scan_workspace(int64_t nq, int nprobe, int nlist);
 int rdb_ivf_flat_scan(int metric, int dtype, const void* q, int64_t nq, int64_t ldq, int d, const int64_t* probe,
-                      int nprobe, const void* rows, int64_t ldx, const float* xv, const int64_t* list_off, int nlist,
-                      const int64_t* ids, int k, float* out_v, int64_t* out_i, void* ws, size_t ws_bytes,
-                      void* stream);
+                      int nprobe, const void* rows, int64_t ldx, const float* xv, const int64_t* list_off,
+                      const int64_t* list_end, int nlist, const int64_t* ids, int k, float* out_v, int64_t* out_i,
+                      void* ws, size_t ws_bytes, void* stream);
 
 /* rdb_ivf_flat_scan for callers that may not allocate GPU memory (no
  * counterpart in the reference): the same list-major scan and the same
@@ -226,8 +230,8 @@ int rdb_ivf_flat_scan(int metric, int dtype, const void* q, int64_t nq, int64_t 
 size_t rdb_noalloc_scratch_bytes(void);
 int rdb_ivf_flat_scan_noalloc(int metric, int dtype, const void* q, int64_t nq, int64_t ldq, int d,
                               const int64_t* probe, int nprobe, const void* rows, int64_t ldx, const float* xv,
-                              const int64_t* list_off, int nlist, const int64_t* ids, int k, float* out_v,
-                              int64_t* out_i, void* stream);
+                              const int64_t* list_off, const int64_t* list_end, int nlist, const int64_t* ids, int k,
+                              float* out_v, int64_t* out_i, void* stream);
 
 /* Residual product-quantisation codes: for row i in list labels[i], residual
  * r = x_i - centroid; code m = argmin over the ksub codewords of subspace m
@@ -242,8 +246,8 @@ int rdb_pq_encode(const float* x, int64_t n, int64_t ldx, int d, const int32_t* 
  * layout as rdb_ivf_flat_scan.  Codes stored list by list; k <= 32. */
 int rdb_ivfpq_scan(const float* q, int64_t nq, int64_t ldq, int d, const int64_t* probe, int nprobe,
                    const float* centroids, int nlist, const float* codebooks, int M, int ksub, const uint8_t* codes,
-                   const int64_t* list_off, const int64_t* ids, int k, float* out_v, int64_t* out_i, void* ws,
-                   size_t ws_bytes, void* stream);
+                   const int64_t* list_off, const int64_t* list_end, const int64_t* ids, int k, float* out_v,
+                   int64_t* out_i, void* ws, size_t ws_bytes, void* stream);
 
 /* Query-major IVF-PQ search (squared L2; replaces rdb_ivfpq_scan + the merge
  * when rdb_pq_fast_layout(M) is 1, i.e. M in {4, 8, 16, 32, 64, 96}).
@@ -268,11 +272,17 @@ int rdb_pq_fast_layout(int M);
 int rdb_pq_row_terms(const uint8_t* codes, int64_t n, int M, const int32_t* labels, const float* centroids, int d,
                      const float* codebooks, int ksub, float* out_terms, void* stream);
 int rdb_pq_rotate_codes(uint8_t* codes, int64_t n, int M, int inverse, void* stream);
+/* Appends into free list slots (no reference counterpart): dst row dest[i] =
+ * src row i for i < n (rows of M code bytes, dest distinct), stored as
+ * rdb_pq_rotate_codes lays out row dest[i] when `rotated` != 0 (M as
+ * rdb_pq_fast_layout).  src holds unrotated codes. */
+int rdb_pq_scatter_codes(const uint8_t* src, int64_t n, int M, const int64_t* dest, uint8_t* dst, int rotated,
+                         void* stream);
 size_t rdb_ivfpq_search_workspace(int64_t nq, int nlist);
 int rdb_ivfpq_search(const float* q, int64_t nq, int64_t ldq, int d, const int64_t* probe, int nprobe,
                      const float* centroids, int nlist, const float* codebooks, int M, int ksub, const uint8_t* codes,
-                     const float* row_terms, const int64_t* list_off, const int64_t* ids, int k, float* out_v,
-                     int64_t* out_i, void* ws, size_t ws_bytes, void* stream);
+                     const float* row_terms, const int64_t* list_off, const int64_t* list_end, const int64_t* ids,
+                     int k, float* out_v, int64_t* out_i, void* ws, size_t ws_bytes, void* stream);
 
 /* Profiling hook (no reference counterpart; the reference times whole calls,
  * benchmarks/src/bench_compare.py:56-59): `mask` selects launches to time

@@ -133,7 +133,7 @@ const char* rdb_last_error(void) { return rdb::g_err; }
 
 unsigned long long rdb_launch_count(void) { return rdb::g_launches.load(std::memory_order_relaxed); }
 
-int rdb_version(void) { return 100; }
+int rdb_version(void) { return 200; }  // 2.00: IVF scans take list_end
 
 int rdb_device_status(unsigned* out_host, int clear) {
     RDB_CHECK_ARG(out_host != nullptr, "out_host is NULL");

@@ -132,6 +132,7 @@ PYBIND11_MODULE(_C, m) {
         .def("centroids", &IVFFlatIndex::centroids)
         .def("list_offsets", &IVFFlatIndex::list_offsets)
         .def("list_sizes", &IVFFlatIndex::list_sizes)
+        .def("capacity", &IVFFlatIndex::capacity)
         .def("stored_ids", &IVFFlatIndex::stored_ids)
         .def("stored_labels", &IVFFlatIndex::stored_labels)
         .def("stored_vectors", &IVFFlatIndex::stored_vectors)
@@ -169,6 +170,7 @@ PYBIND11_MODULE(_C, m) {
         .def("codebooks", &IVFPQIndex::codebooks)
         .def("list_offsets", &IVFPQIndex::list_offsets)
         .def("list_sizes", &IVFPQIndex::list_sizes)
+        .def("capacity", &IVFPQIndex::capacity)
         .def("stored_ids", &IVFPQIndex::stored_ids)
         .def("stored_labels", &IVFPQIndex::stored_labels)
         .def("stored_codes", &IVFPQIndex::stored_codes)

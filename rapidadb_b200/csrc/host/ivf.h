@@ -31,21 +31,39 @@ class IVFBase {
     int64_t size() const { return n_; }
     bool is_trained() const { return centroids_.defined(); }
     at::Tensor centroids() const { return centroids_; }
-    at::Tensor list_offsets() const { return list_off_; }
+    // the stored rows, list by list without the free slots: offsets
+    // [nlist + 1], per-list sizes, ids and list labels in that order
+    at::Tensor list_offsets() const;
     at::Tensor list_sizes() const;
-    at::Tensor stored_ids() const { return ids_; }
-    at::Tensor stored_labels() const { return labels_; }
+    at::Tensor stored_ids() const { return live_select(ids_); }
+    at::Tensor stored_labels() const { return live_select(labels_); }
+    // stored row slots, free ones included (each list keeps spare slots so
+    // that adds append in place)
+    int64_t capacity() const { return cap_; }
     virtual void reset();
     // coarse probe: [nq, min(nprobe, nlist)] nearest list ids (squared L2,
     // ties to the lower list)
     at::Tensor probe(const at::Tensor& queries) const;
 
   protected:
-    // reinstalls stored-order labels (non-decreasing) and ids; rebuilds list_off
+    // reinstalls stored-order labels (non-decreasing) and ids; rebuilds the
+    // list ranges without free slots
     void restore_lists(const at::Tensor& labels, const at::Tensor& ids);
+    // physical slot of each stored row, list by list ([n] int64)
+    at::Tensor live_slots() const;
+    at::Tensor live_select(const at::Tensor& t) const;
+    // m new rows with list labels `lab` [m]: when every list has room, `dest`
+    // gets the free slots after each list's rows (new rows in their given
+    // order), list_end_ advances and true is returned; otherwise nothing
+    // changes and false is returned.
+    bool append_slots(const at::Tensor& lab, at::Tensor& dest);
+    // new layout for the stored rows (in list order) followed by m new rows
+    // with labels `lab`, every list with spare slots: `dest` gets the slot of
+    // each of those rows; list_off_ / list_end_ / cap_ / n_ describe the new
+    // layout (the caller moves its payloads there).
+    void new_layout(const at::Tensor& lab, at::Tensor& dest);
     void set_centroids(const at::Tensor& centroids);
     void check_query(const at::Tensor& queries, int64_t k) const;
-    std::tuple<at::Tensor, at::Tensor> relist(const at::Tensor& labels_all);
     at::Tensor new_ids(const at::Tensor& vectors, const at::Tensor& ids) const;
 
     int dim_;
@@ -57,9 +75,11 @@ class IVFBase {
     at::Tensor cent_rows_;  // padded copy for the coarse probe
     int64_t cent_ld_ = 0;
     at::Tensor cent_xv_;    // |c|^2
-    at::Tensor labels_;     // [n] list of each stored row (stored order)
-    at::Tensor ids_;        // [n] user ids (stored order)
-    at::Tensor list_off_;   // [nlist + 1]
+    at::Tensor labels_;     // [cap] list of each slot (-1: free)
+    at::Tensor ids_;        // [cap] user id of each slot (-1: free)
+    at::Tensor list_off_;   // [nlist + 1] slot ranges: list l owns list_off_[l] .. list_off_[l + 1] - 1
+    at::Tensor list_end_;   // [nlist] its rows fill list_off_[l] .. list_end_[l] - 1
+    int64_t cap_ = 0;       // slots
 };
 
 class IVFFlatIndex : public IVFBase {
@@ -71,7 +91,7 @@ class IVFFlatIndex : public IVFBase {
     // scan with a given [nq, np] probe table (e.g. gathered from other ranks)
     Result search_probed(const at::Tensor& queries, const at::Tensor& probe, int64_t k) const;
     void reset() override;
-    at::Tensor stored_vectors() const { return rows_.defined() ? rows_.narrow(1, 0, dim_) : at::Tensor(); }
+    at::Tensor stored_vectors() const { return rows_.defined() ? live_select(rows_).narrow(1, 0, dim_) : at::Tensor(); }
     // reinstalls a saved index: vectors [n, dim], list labels [n] (non-
     // decreasing) and ids [n], all in stored order (see stored_*())
     void restore(const at::Tensor& vectors, const at::Tensor& labels, const at::Tensor& ids);
@@ -79,8 +99,8 @@ class IVFFlatIndex : public IVFBase {
   private:
     Precision precision_;
     int64_t ld_;
-    at::Tensor rows_;  // [n, ld] list-major, storage dtype
-    at::Tensor xv_;    // [n]
+    at::Tensor rows_;  // [cap, ld] slots list by list, storage dtype (free slots zero)
+    at::Tensor xv_;    // [cap]
 };
 
 class IVFPQIndex : public IVFBase {
@@ -94,7 +114,7 @@ class IVFPQIndex : public IVFBase {
     at::Tensor codebooks() const { return codebooks_; }
     // codes [n, M] in list order, as encoded (the stored copy may be rotated)
     at::Tensor stored_codes() const;
-    at::Tensor stored_row_terms() const { return row_terms_; }
+    at::Tensor stored_row_terms() const { return fast_ ? live_select(row_terms_) : row_terms_; }
     int pq_m() const { return M_; }
     int pq_k() const { return ksub_; }
     // true when search runs the query-major kernel (rotated code layout)
@@ -107,8 +127,8 @@ class IVFPQIndex : public IVFBase {
     int M_, ksub_;
     bool fast_;
     at::Tensor codebooks_;  // [M, ksub, dim / M] fp32
-    at::Tensor codes_;      // [n, M] uint8, list-major (rotated when fast_)
-    at::Tensor row_terms_;  // [n] fp32, list-major (fast_ only)
+    at::Tensor codes_;      // [cap, M] uint8 slots list by list (rotated by slot when fast_)
+    at::Tensor row_terms_;  // [cap] fp32 (fast_ only)
 };
 
 }  // namespace rdbh

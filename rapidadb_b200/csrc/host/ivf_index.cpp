@@ -189,11 +189,62 @@ void IVFBase::check_query(const at::Tensor& queries, int64_t k) const {
     TORCH_CHECK(k <= 32, "IVF search supports k in [1, 32]");
 }
 
-// Rebuild list-major order after appending rows with list labels `lab_all`:
-// returns the permutation (stored order -> source order) and list offsets.
-std::tuple<at::Tensor, at::Tensor> IVFBase::relist(const at::Tensor& lab_all) {
+// Spare slots a list gets when the layout is rebuilt: a quarter of its rows
+// plus a few, so that a stream of adds moves every row O(1) times amortised.
+static at::Tensor list_capacity(const at::Tensor& sizes) { return sizes + at::floor_divide(sizes, 4) + 8; }
+
+at::Tensor IVFBase::live_slots() const {
+    if (n_ == 0 || !list_off_.defined()) return at::empty({0}, ids_.defined() ? ids_.options() : at::TensorOptions(at::kLong));
+    at::Tensor starts = list_off_.narrow(0, 0, nlist_);
+    at::Tensor sizes = list_end_ - starts;
+    at::Tensor packed = sizes.cumsum(0) - sizes;  // first position of each list without free slots
+    at::Tensor shift = at::repeat_interleave(starts - packed, sizes, 0, n_);
+    return at::arange(n_, starts.options()) + shift;
+}
+
+at::Tensor IVFBase::live_select(const at::Tensor& t) const {
+    if (!t.defined()) return t;
+    if (cap_ == n_) return t.narrow(0, 0, n_);  // no free slots
+    return t.index_select(0, live_slots());
+}
+
+at::Tensor IVFBase::list_offsets() const {
+    if (!list_off_.defined()) return at::Tensor();
+    at::Tensor sizes = list_sizes();
+    return at::cat({at::zeros({1}, sizes.options()), sizes.cumsum(0)});
+}
+
+bool IVFBase::append_slots(const at::Tensor& lab, at::Tensor& dest) {
+    if (n_ == 0 || !list_end_.defined()) return false;
+    const int64_t m = lab.size(0);
+    at::Tensor lab_l = lab.to(at::kLong);
+    at::Tensor add = at::bincount(lab_l, {}, nlist_);
+    at::Tensor room = list_off_.narrow(0, 1, nlist_) - list_end_;
+    if (!(add <= room).all().item<bool>()) return false;
+    auto sorted = label_sort(lab, nlist_);
+    at::Tensor seg = std::get<0>(sorted), perm = std::get<1>(sorted);
+    at::Tensor ls = lab_l.index_select(0, perm);
+    at::Tensor slot = list_end_.index_select(0, ls) + at::arange(m, ls.options()) - seg.index_select(0, ls);
+    dest = at::empty_like(slot).index_copy_(0, perm, slot);
+    list_end_ = list_end_ + add;
+    n_ += m;
+    return true;
+}
+
+void IVFBase::new_layout(const at::Tensor& lab, at::Tensor& dest) {
+    const int64_t m = lab.size(0);
+    at::Tensor lab_all = n_ ? at::cat({stored_labels().to(at::kInt), lab.to(at::kInt)}) : lab.to(at::kInt);
     auto sorted = label_sort(lab_all, nlist_);
-    return {std::get<1>(sorted), std::get<0>(sorted)};
+    at::Tensor seg = std::get<0>(sorted), perm = std::get<1>(sorted), counts = std::get<2>(sorted);
+    at::Tensor capl = list_capacity(counts);
+    at::Tensor off = at::cat({at::zeros({1}, capl.options()), capl.cumsum(0)});
+    at::Tensor ls = lab_all.to(at::kLong).index_select(0, perm);
+    at::Tensor slot = off.index_select(0, ls) + at::arange(ls.size(0), ls.options()) - seg.index_select(0, ls);
+    dest = at::empty_like(slot).index_copy_(0, perm, slot);
+    list_off_ = off.contiguous();
+    list_end_ = (off.narrow(0, 0, nlist_) + counts).contiguous();
+    cap_ = off[nlist_].item<int64_t>();
+    n_ += m;
 }
 
 void IVFBase::restore_lists(const at::Tensor& labels, const at::Tensor& ids) {
@@ -209,16 +260,20 @@ void IVFBase::restore_lists(const at::Tensor& labels, const at::Tensor& ids) {
     }
     at::Tensor counts = at::bincount(lab.to(at::kLong), {}, nlist_);
     list_off_ = at::cat({at::zeros({1}, counts.options()), counts.cumsum(0)}).to(at::kLong).contiguous();
+    list_end_ = list_off_.narrow(0, 1, nlist_).clone();
     labels_ = lab;
     ids_ = ids.to(centroids_.device()).to(at::kLong).contiguous();
     n_ = n;
+    cap_ = n;
 }
 
 void IVFBase::reset() {
     n_ = 0;
+    cap_ = 0;
     labels_ = at::Tensor();
     ids_ = at::Tensor();
     list_off_ = at::Tensor();
+    list_end_ = at::Tensor();
 }
 
 at::Tensor IVFBase::new_ids(const at::Tensor& vectors, const at::Tensor& ids) const {
@@ -232,7 +287,19 @@ at::Tensor IVFBase::new_ids(const at::Tensor& vectors, const at::Tensor& ids) co
 
 at::Tensor IVFBase::list_sizes() const {
     if (!list_off_.defined()) return at::Tensor();
-    return list_off_.narrow(0, 1, nlist_) - list_off_.narrow(0, 0, nlist_);
+    return list_end_ - list_off_.narrow(0, 0, nlist_);
+}
+
+// payload of the n_ rows for a new layout: the stored rows in list order,
+// then `added`, moved to the slots `dest` of a [cap_, ...] buffer filled
+// with `fill`
+static at::Tensor relayout(const at::Tensor& stored, const at::Tensor& added, const at::Tensor& dest, int64_t cap,
+                           double fill) {
+    at::Tensor src = stored.defined() && stored.size(0) ? at::cat({stored, added}) : added;
+    std::vector<int64_t> shape = src.sizes().vec();
+    shape[0] = cap;
+    at::Tensor out = at::full(shape, fill, src.options());
+    return out.index_copy_(0, dest, src);
 }
 
 // --------------------------------------------------------------- IVF-Flat
@@ -257,18 +324,27 @@ void IVFFlatIndex::add(const at::Tensor& vectors, const at::Tensor& ids) {
     at::Tensor rows_new = prepare_rows(vectors, storage_type(precision_), ld_);
     if (!rows_new.is_same(vectors)) rows_new = rows_new.contiguous();
     at::Tensor xv_new = row_values(metric_, rows_new, dim_);
-    at::Tensor lab_all = n_ ? at::cat({labels_, lab}) : lab;
-    at::Tensor rows_all = n_ ? at::cat({rows_, rows_new}) : rows_new;
-    at::Tensor xv_all = n_ ? at::cat({xv_, xv_new}) : xv_new;
-    at::Tensor ids_all = n_ ? at::cat({ids_, nid}) : nid;
-    auto pl = relist(lab_all);
-    at::Tensor perm = std::get<0>(pl);
-    rows_ = rows_all.index_select(0, perm);
-    xv_ = xv_all.index_select(0, perm);
-    ids_ = ids_all.index_select(0, perm);
-    labels_ = lab_all.index_select(0, perm);
-    list_off_ = std::get<1>(pl);
-    n_ += m;
+    TORCH_CHECK(n_ + m < (int64_t(1) << 32), "at most 2^32 - 1 rows per device");
+    at::Tensor dest;
+    if (append_slots(lab, dest)) {
+        // every list had room: rows go to free slots, nothing else moves
+        rows_.index_copy_(0, dest, rows_new);
+        xv_.index_copy_(0, dest, xv_new);
+        ids_.index_copy_(0, dest, nid);
+        labels_.index_copy_(0, dest, lab.to(at::kInt));
+        return;
+    }
+    // stored payloads in list order, read before the layout changes
+    const bool had = n_ > 0;
+    at::Tensor old_rows = had ? live_select(rows_) : at::Tensor();
+    at::Tensor old_xv = had ? live_select(xv_) : at::Tensor();
+    at::Tensor old_ids = had ? stored_ids() : at::Tensor();
+    at::Tensor old_lab = had ? stored_labels() : at::Tensor();
+    new_layout(lab, dest);
+    rows_ = relayout(old_rows, rows_new, dest, cap_, 0.0);
+    xv_ = relayout(old_xv, xv_new, dest, cap_, 0.0);
+    ids_ = relayout(old_ids, nid, dest, cap_, -1.0);
+    labels_ = relayout(old_lab, lab.to(at::kInt), dest, cap_, -1.0);
 }
 
 void IVFFlatIndex::restore(const at::Tensor& vectors, const at::Tensor& labels, const at::Tensor& ids) {
@@ -314,7 +390,8 @@ Result IVFFlatIndex::search_probed(const at::Tensor& queries, const at::Tensor& 
     const bool expand = metric_ != Metric::L2 || n_ >= kIvfExpandRowsPerList * static_cast<int64_t>(nlist_);
     check_status(rdb_ivf_flat_scan(static_cast<int>(metric_), dtype_code(rows_.scalar_type()), q.data_ptr(), nq, ld_,
                                    dim_, probe_lists.data_ptr<int64_t>(), np, rows_.data_ptr(), ld_,
-                                   expand ? xv_.data_ptr<float>() : nullptr, list_off_.data_ptr<int64_t>(), nlist_,
+                                   expand ? xv_.data_ptr<float>() : nullptr, list_off_.data_ptr<int64_t>(),
+                                   list_end_.data_ptr<int64_t>(), nlist_,
                                    ids_.data_ptr<int64_t>(), static_cast<int>(k), cv.data_ptr<float>(),
                                    ci.data_ptr<int64_t>(), ws.data_ptr(), ws.numel(), stream_ptr()),
                  "ivf scan");
@@ -357,23 +434,32 @@ void IVFPQIndex::add(const at::Tensor& vectors, const at::Tensor& ids) {
     at::Tensor lab = std::get<0>(kmeans_assign(xf, centroids_, true));
     TORCH_CHECK(n_ + m < (int64_t(1) << 32), "at most 2^32 - 1 rows per device");
     at::Tensor codes_new = pq_encode(xf, lab, centroids_, codebooks_);
-    at::Tensor lab_all = n_ ? at::cat({labels_, lab}) : lab;
-    at::Tensor codes_all = n_ ? at::cat({stored_codes(), codes_new}) : codes_new;
-    at::Tensor ids_all = n_ ? at::cat({ids_, nid}) : nid;
-    auto pl = relist(lab_all);
-    at::Tensor perm = std::get<0>(pl);
-    codes_ = codes_all.index_select(0, perm);
-    ids_ = ids_all.index_select(0, perm);
-    labels_ = lab_all.index_select(0, perm);
-    list_off_ = std::get<1>(pl);
-    if (fast_) {
-        at::Tensor terms_new = pq_row_terms(codes_new, lab, centroids_, codebooks_);
-        at::Tensor terms_all = n_ ? at::cat({row_terms_, terms_new}) : terms_new;
-        row_terms_ = terms_all.index_select(0, perm);
-        check_status(rdb_pq_rotate_codes(codes_.data_ptr<uint8_t>(), codes_.size(0), M_, 0, stream_ptr()),
-                     "pq code layout");
+    at::Tensor terms_new = fast_ ? pq_row_terms(codes_new, lab, centroids_, codebooks_) : at::Tensor();
+    at::Tensor dest;
+    if (append_slots(lab, dest)) {
+        // every list had room: codes go to free slots (laid out for their slot)
+        check_status(rdb_pq_scatter_codes(codes_new.data_ptr<uint8_t>(), m, M_, dest.data_ptr<int64_t>(),
+                                          codes_.data_ptr<uint8_t>(), fast_ ? 1 : 0, stream_ptr()),
+                     "pq code append");
+        if (fast_) row_terms_.index_copy_(0, dest, terms_new);
+        ids_.index_copy_(0, dest, nid);
+        labels_.index_copy_(0, dest, lab.to(at::kInt));
+        return;
     }
-    n_ += m;
+    const bool had = n_ > 0;
+    at::Tensor old_codes = had ? stored_codes() : at::Tensor();
+    at::Tensor old_terms = had && fast_ ? stored_row_terms() : at::Tensor();
+    at::Tensor old_ids = had ? stored_ids() : at::Tensor();
+    at::Tensor old_lab = had ? stored_labels() : at::Tensor();
+    new_layout(lab, dest);
+    at::Tensor src = had ? at::cat({old_codes, codes_new}) : codes_new;
+    codes_ = at::zeros({cap_, M_}, src.options());
+    check_status(rdb_pq_scatter_codes(src.data_ptr<uint8_t>(), src.size(0), M_, dest.data_ptr<int64_t>(),
+                                      codes_.data_ptr<uint8_t>(), fast_ ? 1 : 0, stream_ptr()),
+                 "pq code layout");
+    if (fast_) row_terms_ = relayout(old_terms, terms_new, dest, cap_, 0.0);
+    ids_ = relayout(old_ids, nid, dest, cap_, -1.0);
+    labels_ = relayout(old_lab, lab.to(at::kInt), dest, cap_, -1.0);
 }
 
 void IVFPQIndex::restore(const at::Tensor& codes, const at::Tensor& labels, const at::Tensor& ids) {
@@ -394,11 +480,12 @@ void IVFPQIndex::restore(const at::Tensor& codes, const at::Tensor& labels, cons
 }
 
 at::Tensor IVFPQIndex::stored_codes() const {
-    if (!fast_ || !codes_.defined() || codes_.size(0) == 0) return codes_;
+    if (!codes_.defined() || codes_.size(0) == 0) return codes_;
+    if (!fast_) return live_select(codes_);
     c10::cuda::CUDAGuard guard(codes_.device());
     at::Tensor c = codes_.clone();
     check_status(rdb_pq_rotate_codes(c.data_ptr<uint8_t>(), c.size(0), M_, 1, stream_ptr()), "pq code layout");
-    return c;
+    return live_select(c);
 }
 
 Result IVFPQIndex::search(const at::Tensor& queries, int64_t k) const {
@@ -422,7 +509,8 @@ Result IVFPQIndex::search_probed(const at::Tensor& queries, const at::Tensor& pr
         check_status(rdb_ivfpq_search(q.data_ptr<float>(), nq, dim_, dim_, probe_lists.data_ptr<int64_t>(), np,
                                       centroids_.data_ptr<float>(), nlist_, codebooks_.data_ptr<float>(), M_, ksub_,
                                       codes_.data_ptr<uint8_t>(), row_terms_.data_ptr<float>(),
-                                      list_off_.data_ptr<int64_t>(), ids_.data_ptr<int64_t>(), static_cast<int>(k),
+                                      list_off_.data_ptr<int64_t>(), list_end_.data_ptr<int64_t>(),
+                                      ids_.data_ptr<int64_t>(), static_cast<int>(k),
                                       dv.data_ptr<float>(), di.data_ptr<int64_t>(), ws.data_ptr(), ws.numel(),
                                       stream_ptr()),
                      "ivf-pq search");
@@ -433,7 +521,8 @@ Result IVFPQIndex::search_probed(const at::Tensor& queries, const at::Tensor& pr
     at::Tensor ws = ws_bytes(q, rdb_ivf_scan_workspace(nq, np, nlist_));
     check_status(rdb_ivfpq_scan(q.data_ptr<float>(), nq, dim_, dim_, probe_lists.data_ptr<int64_t>(), np,
                                 centroids_.data_ptr<float>(), nlist_, codebooks_.data_ptr<float>(), M_, ksub_,
-                                codes_.data_ptr<uint8_t>(), list_off_.data_ptr<int64_t>(), ids_.data_ptr<int64_t>(),
+                                codes_.data_ptr<uint8_t>(), list_off_.data_ptr<int64_t>(),
+                                list_end_.data_ptr<int64_t>(), ids_.data_ptr<int64_t>(),
                                 static_cast<int>(k), cv.data_ptr<float>(), ci.data_ptr<int64_t>(), ws.data_ptr(),
                                 ws.numel(), stream_ptr()),
                  "ivf-pq scan");

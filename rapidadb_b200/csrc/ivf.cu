@@ -147,7 +147,8 @@ template <typename T, bool EXPAND>
 __global__ void __launch_bounds__(FNT, 2) ivf_flat_scan_kernel(
     int metric, int cos_small, const T* __restrict__ q, int64_t Q, int64_t ldq, int d, const float* __restrict__ qv,
     int nprobe, const int64_t* __restrict__ eperm, const int64_t* __restrict__ eseg, const T* __restrict__ rows,
-    int64_t ldx, const float* __restrict__ xv, const int64_t* __restrict__ list_off, int nlist,
+    int64_t ldx, const float* __restrict__ xv, const int64_t* __restrict__ list_off,
+    const int64_t* __restrict__ list_end, int nlist,
     const int64_t* __restrict__ ids, int k, float* __restrict__ out_v, int64_t* __restrict__ out_i) {
     extern __shared__ __align__(16) unsigned char ivf_smem[];
     IvfFlatSmem& sh = *reinterpret_cast<IvfFlatSmem*>(ivf_smem);
@@ -163,7 +164,7 @@ __global__ void __launch_bounds__(FNT, 2) ivf_flat_scan_kernel(
 
     for (int l = blockIdx.x; l < nlist; l += gridDim.x) {
         const int64_t e0 = eseg[l], e1 = eseg[l + 1];
-        const int64_t r0 = list_off[l], r1 = list_off[l + 1];
+        const int64_t r0 = list_off[l], r1 = list_end ? list_end[l] : list_off[l + 1];
         // chunks of FQ probing queries, dealt round-robin to the gridDim.y
         // CTAs of this list (a popular list is shared by several SMs)
         for (int64_t ec = e0 + (int64_t)blockIdx.y * FQ; ec < e1; ec += (int64_t)gridDim.y * FQ) {
@@ -372,7 +373,8 @@ constexpr int PNW = PNT / 32;
 __global__ void __launch_bounds__(PNT) ivfpq_scan_kernel(
     const float* __restrict__ q, int64_t Q, int64_t ldq, int d, int nprobe, const int64_t* __restrict__ eperm,
     const int64_t* __restrict__ eseg, const float* __restrict__ centroids, const float* __restrict__ codebooks, int M,
-    int ksub, const uint8_t* __restrict__ codes, const int64_t* __restrict__ list_off, int nlist,
+    int ksub, const uint8_t* __restrict__ codes, const int64_t* __restrict__ list_off,
+    const int64_t* __restrict__ list_end, int nlist,
     const int64_t* __restrict__ ids, int k, float* __restrict__ out_v, int64_t* __restrict__ out_i) {
     extern __shared__ float psm[];
     const int dsub = d / M;
@@ -393,7 +395,7 @@ __global__ void __launch_bounds__(PNT) ivfpq_scan_kernel(
 
     for (int l = blockIdx.x; l < nlist; l += gridDim.x) {
         const int64_t e0 = eseg[l], e1 = eseg[l + 1];
-        const int64_t r0 = list_off[l], r1 = list_off[l + 1];
+        const int64_t r0 = list_off[l], r1 = list_end ? list_end[l] : list_off[l + 1];
         const float* cl = centroids + (int64_t)l * d;
         for (int64_t e = e0; e < e1; ++e) {
             const int64_t ent = eperm[e];
@@ -518,11 +520,11 @@ int ivf_flat_smem_attr(int bytes) {
 template <typename T>
 void launch_ivf_flat(bool expand, dim3 grid, cudaStream_t s, int metric, int cos_small, const void* q, int64_t nq,
                      int64_t ldq, int d, const float* qv, int nprobe, const int64_t* eperm, const int64_t* eseg,
-                     const void* rows, int64_t ldx, const float* xv, const int64_t* list_off, int nlist,
+                     const void* rows, int64_t ldx, const float* xv, const int64_t* list_off, const int64_t* list_end, int nlist,
                      const int64_t* ids, int k, float* out_v, int64_t* out_i) {
     auto kern = expand ? ivf_flat_scan_kernel<T, true> : ivf_flat_scan_kernel<T, false>;
     kern<<<grid, FNT, sizeof(IvfFlatSmem), s>>>(metric, cos_small, static_cast<const T*>(q), nq, ldq, d, qv, nprobe,
-                                                eperm, eseg, static_cast<const T*>(rows), ldx, xv, list_off, nlist,
+                                                eperm, eseg, static_cast<const T*>(rows), ldx, xv, list_off, list_end, nlist,
                                                 ids, k, out_v, out_i);
 }
 
@@ -541,7 +543,7 @@ extern "C" {
 size_t rdb_ivf_scan_workspace(int64_t nq, int nprobe, int nlist) { return ivf_ws(nq, nprobe, nlist).bytes; }
 
 int rdb_ivf_flat_scan(int metric, int dtype, const void* q, int64_t nq, int64_t ldq, int d, const int64_t* probe,
-                      int nprobe, const void* rows, int64_t ldx, const float* xv, const int64_t* list_off, int nlist,
+                      int nprobe, const void* rows, int64_t ldx, const float* xv, const int64_t* list_off, const int64_t* list_end, int nlist,
                       const int64_t* ids, int k, float* out_v, int64_t* out_i, void* ws, size_t ws_bytes,
                       void* stream) {
     RDB_CHECK_ARG(metric >= 0 && metric <= 2, "unknown metric %d", metric);
@@ -590,15 +592,15 @@ int rdb_ivf_flat_scan(int metric, int dtype, const void* q, int64_t nq, int64_t 
     switch (dtype) {
         case RDB_F32:
             launch_ivf_flat<float>(expand, grid, s, metric, cos_small, q, nq, ldq, d, qv, nprobe, eperm, eseg, rows,
-                                   ldx, xv, list_off, nlist, ids, k, out_v, out_i);
+                                   ldx, xv, list_off, list_end, nlist, ids, k, out_v, out_i);
             break;
         case RDB_F16:
             launch_ivf_flat<__half>(expand, grid, s, metric, cos_small, q, nq, ldq, d, qv, nprobe, eperm, eseg, rows,
-                                    ldx, xv, list_off, nlist, ids, k, out_v, out_i);
+                                    ldx, xv, list_off, list_end, nlist, ids, k, out_v, out_i);
             break;
         default:
             launch_ivf_flat<__nv_bfloat16>(expand, grid, s, metric, cos_small, q, nq, ldq, d, qv, nprobe, eperm, eseg,
-                                           rows, ldx, xv, list_off, nlist, ids, k, out_v, out_i);
+                                           rows, ldx, xv, list_off, list_end, nlist, ids, k, out_v, out_i);
     }
     RDB_LAUNCH_CHECK();
     if (stop_ev) RDB_CUDA_TRY(cudaEventRecord(stop_ev, s));
@@ -631,7 +633,7 @@ int rdb_pq_encode(const float* x, int64_t n, int64_t ldx, int d, const int32_t* 
 
 int rdb_ivfpq_scan(const float* q, int64_t nq, int64_t ldq, int d, const int64_t* probe, int nprobe,
                    const float* centroids, int nlist, const float* codebooks, int M, int ksub, const uint8_t* codes,
-                   const int64_t* list_off, const int64_t* ids, int k, float* out_v, int64_t* out_i, void* ws,
+                   const int64_t* list_off, const int64_t* list_end, const int64_t* ids, int k, float* out_v, int64_t* out_i, void* ws,
                    size_t ws_bytes, void* stream) {
     RDB_CHECK_ARG(nq >= 0 && d >= 1 && M >= 1 && d % M == 0, "d must be a multiple of M");
     RDB_CHECK_ARG(ksub >= 1 && ksub <= 256, "ksub must be in [1, 256]");
@@ -658,7 +660,7 @@ int rdb_ivfpq_scan(const float* q, int64_t nq, int64_t ldq, int d, const int64_t
     RDB_TRY(timing_begin(TIMING_PQ_SCAN, s, &stop_ev));
     ivfpq_scan_kernel<<<grid, PNT, smem, s>>>(q, nq, ldq, d, nprobe, reinterpret_cast<const int64_t*>(base + w.off_perm),
                                             reinterpret_cast<const int64_t*>(base + w.off_seg), centroids, codebooks, M,
-                                            ksub, codes, list_off, nlist, ids, k, out_v, out_i);
+                                            ksub, codes, list_off, list_end, nlist, ids, k, out_v, out_i);
     RDB_LAUNCH_CHECK();
     if (stop_ev) RDB_CUDA_TRY(cudaEventRecord(stop_ev, s));
     return RDB_OK;

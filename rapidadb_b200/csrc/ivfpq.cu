@@ -140,6 +140,7 @@ __global__ void __launch_bounds__(SNT, (M <= 32 ? 2 : 1)) ivfpq_search_kernel(
     const float* __restrict__ q, int64_t Q, int64_t ldq, int d, const int64_t* __restrict__ probe, int nprobe,
     const float* __restrict__ centroids, int nlist, const float* __restrict__ codebooks, int ksub,
     const uint8_t* __restrict__ codes, const float* __restrict__ row_terms, const int64_t* __restrict__ list_off,
+    const int64_t* __restrict__ list_end,
     const int64_t* __restrict__ ids, const int64_t* __restrict__ order, int k, PqSmem sm, float* __restrict__ out_v,
     int64_t* __restrict__ out_i) {
     using L = PqLayout<M>;
@@ -167,7 +168,7 @@ __global__ void __launch_bounds__(SNT, (M <= 32 ? 2 : 1)) ivfpq_search_kernel(
             uint32_t r0 = 0, r1 = 0;
             if (l >= 0 && l < nlist) {
                 r0 = static_cast<uint32_t>(list_off[l]);
-                r1 = static_cast<uint32_t>(list_off[l + 1]);
+                r1 = static_cast<uint32_t>(list_end ? list_end[l] : list_off[l + 1]);
             }
             r0s[p] = r0;
             r1s[p] = r1;
@@ -367,6 +368,24 @@ __global__ void pq_rotate_kernel(uint8_t* __restrict__ codes, int64_t n, int M, 
     }
 }
 
+// dst row dest[i] = src row i, rotated by dest[i] mod G when G > 0 (the
+// stored layout of pq_rotate_kernel for that row)
+__global__ void pq_scatter_kernel(const uint8_t* __restrict__ src, int64_t n, int M, const int64_t* __restrict__ dest,
+                                  uint8_t* __restrict__ dst, int G) {
+    const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (i >= n) return;
+    const int64_t o = dest[i];
+    const uint8_t* r = src + i * M;
+    uint8_t* w = dst + o * M;
+    if (G <= 0) {
+        for (int s = 0; s < M; ++s) w[s] = r[s];
+        return;
+    }
+    const int sh = static_cast<int>(o % G);
+    for (int g = 0; g < M / G; ++g)
+        for (int s = 0; s < G; ++s) w[g * G + s] = r[g * G + (s + sh) % G];
+}
+
 __global__ void first_probe_kernel(const int64_t* __restrict__ probe, int64_t nq, int nprobe, int nlist,
                                    int32_t* __restrict__ labels) {
     const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
@@ -399,7 +418,7 @@ PqSearchWs pq_search_ws(int64_t nq, int nlist) {
 template <int M>
 int launch_search(const float* q, int64_t nq, int64_t ldq, int d, const int64_t* probe, int nprobe,
                   const float* centroids, int nlist, const float* codebooks, int ksub, const uint8_t* codes,
-                  const float* row_terms, const int64_t* list_off, const int64_t* ids, const int64_t* order, int k,
+                  const float* row_terms, const int64_t* list_off, const int64_t* list_end, const int64_t* ids, const int64_t* order, int k,
                   float* out_v, int64_t* out_i, cudaStream_t s) {
     const PqSmem sm = pq_smem(M, d, nprobe);
     static bool attr[64] = {false};
@@ -418,7 +437,7 @@ int launch_search(const float* q, int64_t nq, int64_t ldq, int d, const int64_t*
     cudaEvent_t stop_ev;
     RDB_TRY(timing_begin(TIMING_PQ_SCAN, s, &stop_ev));
     ivfpq_search_kernel<M><<<static_cast<unsigned>(grid), SNT, sm.bytes, s>>>(
-        q, nq, ldq, d, probe, nprobe, centroids, nlist, codebooks, ksub, codes, row_terms, list_off, ids, order, k,
+        q, nq, ldq, d, probe, nprobe, centroids, nlist, codebooks, ksub, codes, row_terms, list_off, list_end, ids, order, k,
         sm, out_v, out_i);
     RDB_LAUNCH_CHECK();
     if (stop_ev) RDB_CUDA_TRY(cudaEventRecord(stop_ev, s));
@@ -458,6 +477,19 @@ int rdb_pq_rotate_codes(uint8_t* codes, int64_t n, int M, int inverse, void* str
     return RDB_OK;
 }
 
+int rdb_pq_scatter_codes(const uint8_t* src, int64_t n, int M, const int64_t* dest, uint8_t* dst, int rotated,
+                         void* stream) {
+    RDB_CHECK_ARG(M >= 1 && n >= 0, "bad shape");
+    RDB_CHECK_ARG(!rotated || fast_m(M), "no rotated code layout for pq_m = %d", M);
+    if (n == 0) return RDB_OK;
+    RDB_CHECK_ARG(src && dest && dst, "NULL pointer");
+    const int G = rotated ? (M < 32 ? M : 32) : 0;
+    pq_scatter_kernel<<<static_cast<unsigned>((n + 255) / 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+        src, n, M, dest, dst, G);
+    RDB_LAUNCH_CHECK();
+    return RDB_OK;
+}
+
 size_t rdb_ivfpq_search_workspace(int64_t nq, int nlist) {
     if (nq <= 0 || nlist <= 0) return 256;
     return pq_search_ws(nq, nlist).bytes;
@@ -465,7 +497,7 @@ size_t rdb_ivfpq_search_workspace(int64_t nq, int nlist) {
 
 int rdb_ivfpq_search(const float* q, int64_t nq, int64_t ldq, int d, const int64_t* probe, int nprobe,
                      const float* centroids, int nlist, const float* codebooks, int M, int ksub,
-                     const uint8_t* codes, const float* row_terms, const int64_t* list_off, const int64_t* ids,
+                     const uint8_t* codes, const float* row_terms, const int64_t* list_off, const int64_t* list_end, const int64_t* ids,
                      int k, float* out_v, int64_t* out_i, void* ws, size_t ws_bytes, void* stream) {
     RDB_CHECK_ARG(fast_m(M), "rdb_ivfpq_search needs pq_m in {4, 8, 16, 32, 64, 96}, got %d", M);
     RDB_CHECK_ARG(d >= M && d % M == 0 && ldq >= d, "bad shape");
@@ -491,22 +523,22 @@ int rdb_ivfpq_search(const float* q, int64_t nq, int64_t ldq, int d, const int64
     switch (M) {
         case 4:
             return launch_search<4>(q, nq, ldq, d, probe, nprobe, centroids, nlist, codebooks, ksub, codes, row_terms,
-                                    list_off, ids, order, k, out_v, out_i, s);
+                                    list_off, list_end, ids, order, k, out_v, out_i, s);
         case 8:
             return launch_search<8>(q, nq, ldq, d, probe, nprobe, centroids, nlist, codebooks, ksub, codes, row_terms,
-                                    list_off, ids, order, k, out_v, out_i, s);
+                                    list_off, list_end, ids, order, k, out_v, out_i, s);
         case 16:
             return launch_search<16>(q, nq, ldq, d, probe, nprobe, centroids, nlist, codebooks, ksub, codes,
-                                     row_terms, list_off, ids, order, k, out_v, out_i, s);
+                                     row_terms, list_off, list_end, ids, order, k, out_v, out_i, s);
         case 32:
             return launch_search<32>(q, nq, ldq, d, probe, nprobe, centroids, nlist, codebooks, ksub, codes,
-                                     row_terms, list_off, ids, order, k, out_v, out_i, s);
+                                     row_terms, list_off, list_end, ids, order, k, out_v, out_i, s);
         case 64:
             return launch_search<64>(q, nq, ldq, d, probe, nprobe, centroids, nlist, codebooks, ksub, codes,
-                                     row_terms, list_off, ids, order, k, out_v, out_i, s);
+                                     row_terms, list_off, list_end, ids, order, k, out_v, out_i, s);
         default:
             return launch_search<96>(q, nq, ldq, d, probe, nprobe, centroids, nlist, codebooks, ksub, codes,
-                                     row_terms, list_off, ids, order, k, out_v, out_i, s);
+                                     row_terms, list_off, list_end, ids, order, k, out_v, out_i, s);
     }
 }
 

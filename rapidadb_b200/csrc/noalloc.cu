@@ -62,7 +62,8 @@ size_t rdb_noalloc_scratch_bytes(void) { return kNoAllocScratchBytes; }
 
 int rdb_ivf_flat_scan_noalloc(int metric, int dtype, const void* q, int64_t nq, int64_t ldq, int d,
                               const int64_t* probe, int nprobe, const void* rows, int64_t ldx, const float* xv,
-                              const int64_t* list_off, int nlist, const int64_t* ids, int k, float* out_v,
+                              const int64_t* list_off, const int64_t* list_end, int nlist, const int64_t* ids,
+                              int k, float* out_v,
                               int64_t* out_i, void* stream) {
     RDB_CHECK_ARG(nq >= 0 && nprobe >= 1 && nlist >= 1, "bad shape");
     const size_t need = rdb_ivf_scan_workspace(nq, nprobe, nlist);
@@ -74,7 +75,7 @@ int rdb_ivf_flat_scan_noalloc(int metric, int dtype, const void* q, int64_t nq, 
                          (long long)nq, nprobe, nlist, need, kNoAllocScratchBytes);
     void* scratch = nullptr;
     RDB_TRY(scratch_address(&scratch));
-    return rdb_ivf_flat_scan(metric, dtype, q, nq, ldq, d, probe, nprobe, rows, ldx, xv, list_off, nlist, ids, k,
+    return rdb_ivf_flat_scan(metric, dtype, q, nq, ldq, d, probe, nprobe, rows, ldx, xv, list_off, list_end, nlist, ids, k,
                              out_v, out_i, scratch, kNoAllocScratchBytes, stream);
 }
 

@@ -131,6 +131,66 @@ def test_ivfpq_codes_and_search_match_oracle(device, M, nlist, nprobe, query_maj
     np.testing.assert_allclose(d.cpu().numpy(), rd, rtol=1e-4, atol=1e-3)
 
 
+@pytest.mark.parametrize("kind", ["flat_l2", "flat_cosine", "pq_m16", "pq_m2"])
+def test_ivf_streaming_add_matches_bulk_add(device, kind):
+    """Adds in many small and large batches -- appends into the free slots of
+    every list when they have room, a new layout with spare slots when one
+    runs out -- store exactly what one bulk add stores (lists, row order, ids,
+    vectors / codes / row terms) and search identically (scores and ids
+    equal, tolerance 0)."""
+    import rapidadb._C as _C
+    from rapidadb_b200.kmeans import kmeans, train_pq
+
+    d, nlist = 32, 32
+    x, g = mixture(7, 12000, d, 24)
+    q = (x[g.integers(0, len(x), 60)] + 0.3 * g.standard_normal((60, d))).astype(np.float32)
+    xt = torch.from_numpy(x).cuda()
+    ids = torch.arange(len(x), device=device) * 3 + 11
+    cent = kmeans(xt, nlist, 6, 0.0, seed=3).centroids
+    books = None
+    if kind.startswith("pq"):
+        lab, _ = _C.kmeans_assign(xt, cent, True)
+        books = train_pq(xt - cent.index_select(0, lab.long()), int(kind[4:]), 64, 4, seed=4)
+
+    def make():
+        if kind.startswith("flat"):
+            met = _C.Metric.L2 if kind == "flat_l2" else _C.Metric.COSINE
+            ix = _C.IVFFlatIndex(d, met, nlist, 5)
+            ix.set_quantizer(cent)
+        else:
+            ix = _C.IVFPQIndex(d, _C.Metric.L2, nlist, 5, int(kind[4:]), 64)
+            ix.set_quantizer(cent, books)
+        return ix
+
+    bulk = make()
+    bulk.add(xt, ids)
+    stream = make()
+    appends, lo = 0, 0
+    for m in [1, 7, 300, 45, 2500, 2, 1200, 3000, 1, 4944]:
+        cap0, n0 = stream.capacity(), stream.size()
+        stream.add(xt[lo:lo + m], ids[lo:lo + m])
+        lo += m
+        assert stream.size() == n0 + m and stream.capacity() >= stream.size()
+        appends += int(n0 > 0 and stream.capacity() == cap0)
+    assert lo == len(x)
+    assert appends >= 2  # some batches went into free slots without moving rows
+    assert torch.equal(stream.list_offsets(), bulk.list_offsets())
+    assert torch.equal(stream.list_sizes(), bulk.list_sizes())
+    assert torch.equal(stream.stored_ids(), bulk.stored_ids())
+    assert torch.equal(stream.stored_labels(), bulk.stored_labels())
+    if kind.startswith("flat"):
+        assert torch.equal(stream.stored_vectors(), bulk.stored_vectors())
+    else:
+        assert torch.equal(stream.stored_codes(), bulk.stored_codes())
+        if stream.query_major():
+            assert torch.equal(stream.stored_row_terms(), bulk.stored_row_terms())
+    qt = torch.from_numpy(q).cuda()
+    ds, is_ = stream.search(qt, 10)
+    db, ib = bulk.search(qt, 10)
+    assert torch.equal(is_, ib)
+    assert torch.equal(ds, db)
+
+
 def test_ivf_errors(device):
     import rapidadb._C as _C
 

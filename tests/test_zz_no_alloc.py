@@ -31,10 +31,10 @@ def _lib():
     lib.rdb_noalloc_scratch_bytes.restype = ctypes.c_size_t
     lib.rdb_last_error.restype = ctypes.c_char_p
     lib.rdb_ivf_flat_scan.argtypes = [ctypes.c_int, ctypes.c_int, _vp, _i64, _i64, ctypes.c_int, _vp, ctypes.c_int,
-                                      _vp, _i64, _vp, _vp, ctypes.c_int, _vp, ctypes.c_int, _vp, _vp, _vp,
+                                      _vp, _i64, _vp, _vp, _vp, ctypes.c_int, _vp, ctypes.c_int, _vp, _vp, _vp,
                                       ctypes.c_size_t, _vp]
     lib.rdb_ivf_flat_scan_noalloc.argtypes = [ctypes.c_int, ctypes.c_int, _vp, _i64, _i64, ctypes.c_int, _vp,
-                                              ctypes.c_int, _vp, _i64, _vp, _vp, ctypes.c_int, _vp, ctypes.c_int,
+                                              ctypes.c_int, _vp, _i64, _vp, _vp, _vp, ctypes.c_int, _vp, ctypes.c_int,
                                               _vp, _vp, _vp]
     return lib
 
@@ -61,7 +61,7 @@ def _scan(lib, noalloc, q, probe, rows, list_off, ids, k, metric=1):
     xv = (rows * rows).sum(1).sqrt().contiguous()
     stream = _vp(torch.cuda.current_stream().cuda_stream)
     args = [metric, 0, q.data_ptr(), nq, d, d, probe.data_ptr(), nprobe, rows.data_ptr(), d, xv.data_ptr(),
-            list_off.data_ptr(), nlist, ids.data_ptr(), k, out_v.data_ptr(), out_i.data_ptr()]
+            list_off.data_ptr(), None, nlist, ids.data_ptr(), k, out_v.data_ptr(), out_i.data_ptr()]
     if noalloc:
         rc = lib.rdb_ivf_flat_scan_noalloc(*args, stream)
     else:
@@ -92,7 +92,7 @@ def test_noalloc_rejects_oversized_requests(device):
     assert lib.rdb_ivf_scan_workspace(nq, nprobe, nlist) > cap
     z = torch.zeros(1, device="cuda")
     rc = lib.rdb_ivf_flat_scan_noalloc(1, 0, z.data_ptr(), nq, 8, 8, z.data_ptr(), nprobe, z.data_ptr(), 8,
-                                       z.data_ptr(), z.data_ptr(), nlist, None, 10, z.data_ptr(), z.data_ptr(),
+                                       z.data_ptr(), z.data_ptr(), None, nlist, None, 10, z.data_ptr(), z.data_ptr(),
                                        _vp(torch.cuda.current_stream().cuda_stream))
     assert rc == 4  # RDB_ERR_UNSUPPORTED, raised before any device work
     assert b"static array" in lib.rdb_last_error()
