@@ -56,6 +56,10 @@ WORKLOADS = {
     "ivf_pq": dict(kind="ivf_pq", N=100_000_000, d=128, Q=10_000, k=10, metric="l2", nlist=16384,
                    nprobe=64, M=16, ksub=256, ncentres=1024, spread=2.0, sigma=1.0, train=262_144,
                    iters=10, uint8=True),
+    # streaming add into the IVF-Flat config's index: batches of 10,000 rows
+    # appended to the 10,000,000 stored rows
+    "ivf_add": dict(kind="ivf_add", N=10_000_000, d=128, batch=10_000, nlist=4096, nprobe=32,
+                    ncentres=1024, spread=2.0, sigma=1.0, train=1_000_000, iters=20, uint8=False),
     # BASELINE config "k-means: N=10,000,000 x 768 bf16, mixture of 16,384 Gaussians (centres
     # ~N(0,I), sigma=0.3); K=16,384; seeded random-row init; 20 Lloyd iterations"
     "kmeans": dict(kind="kmeans", N=10_000_000, d=768, K=16384, iters=20, ncentres=16384,
@@ -714,6 +718,99 @@ def run_ivf(args, wl):
     return res
 
 
+def run_ivf_add(args, wl):
+    """Streaming add: rows/s of batches added to an IVF-Flat index that
+    already holds wl.N rows (the ivf_flat workload's table; each rank its own
+    shard, so per-GPU work is fixed).  A batch that fits every list's spare
+    slots is written in place; the line reports how many did."""
+    import torch
+    import torch.distributed as dist
+
+    from rapidadb_b200._lib import C
+    from rapidadb_b200.kmeans import kmeans
+    from rapidadb_b200.sharded import shard_range
+
+    rank, world, local_rank, dev = _dist_setup()
+    _C = C()
+    N, d, B, nlist = wl["N"], wl["d"], wl["batch"], wl["nlist"]
+    ntr = min(wl["train"], N)
+    xtr = gen_mixture(0, ntr, d, wl, args.seed, torch.float32, dev)
+    cent = kmeans(xtr, nlist, wl["iters"], 0.0, args.seed).centroids
+    del xtr
+    idx = _C.IVFFlatIndex(d, _C.Metric.L2, nlist, wl["nprobe"], _C.Precision.FP32)
+    idx.set_quantizer(cent)
+    lo, hi = shard_range(N, rank, world)
+    CH = 4_194_304
+    for a in range(lo, hi, CH):
+        b = min(hi, a + CH)
+        idx.add(gen_mixture(a, b, d, wl, args.seed, torch.float32, dev), torch.arange(a, b, device=dev))
+    # new rows (ids past the table), generated before the timed region
+    nb = args.warmup + 2 * args.steps
+    base = N + rank * nb * B
+    new = gen_mixture(base, base + nb * B, d, wl, args.seed, torch.float32, dev, salt=2)
+    new_ids = torch.arange(base, base + nb * B, device=dev)
+    state = {"i": 0, "in_place": 0}
+
+    def add_batch():
+        i = state["i"]
+        cap0 = idx.capacity()
+        idx.add(new[i * B:(i + 1) * B], new_ids[i * B:(i + 1) * B])
+        state["in_place"] += int(idx.capacity() == cap0)
+        state["i"] = i + 1
+
+    n0 = idx.size()
+    ms, kern_ms, nl, clk, _ = _timed(add_batch, args.steps, args.warmup, world, 8, local_rank)
+    # e2e: each batch copied in from pinned host memory, then added
+    host = new[state["i"] * B:].cpu().pin_memory()
+    buf = torch.empty((B, d), device=dev)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    t0 = time.perf_counter()
+    for j in range(args.steps):
+        buf.copy_(host[j * B:(j + 1) * B], non_blocking=True)
+        idx.add(buf, new_ids[(state["i"] + j) * B:(state["i"] + j + 1) * B])
+    torch.cuda.synchronize()
+    e2e_s = time.perf_counter() - t0
+    e2e_t = torch.tensor([e2e_s], device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(e2e_t, op=dist.ReduceOp.MAX)
+    e2e_s = float(e2e_t.item())
+    assert idx.size() == n0 + nb * B
+    res = None
+    if rank == 0:
+        # exact list assignment of each batch: 2 B nlist d FLOP on the CUDA
+        # cores (the reference's sequential fp32 arithmetic)
+        flops = 2.0 * B * nlist * d
+        peak = 148 * 128 * 2 * 1.965e9 / 1e12
+        ach = flops / (kern_ms * 1e-3) / 1e12 if kern_ms > 0 else None
+        res = {
+            "metric": "IVF-Flat streaming add (rows/s)",
+            "value": round(world * B * args.steps / (ms * 1e-3), 1), "unit": "rows/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 4),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic (seeded Gaussian mixture)",
+            "config": {"workload": args.workload, "rows_before": N, "rows_per_gpu": hi - lo, "dim": d,
+                       "batch_rows": B, "nlist": nlist, "capacity_after": idx.capacity(),
+                       "batches_in_place": "%d of %d" % (state["in_place"], args.warmup + args.steps),
+                       "l2_flush": "not needed: stored rows (%.2f GB per GPU) exceed L2" % ((hi - lo) * d * 4 / 1e9)},
+            "e2e": {"value": round(world * B * args.steps / e2e_s, 1), "unit": "rows/s",
+                    "h2d_bytes_per_step": B * d * 4, "d2h_bytes_per_step": 0},
+            "gpu_launches": _timed.launches,
+            "roofline": {"bound": "fma", "achieved": round(ach, 2) if ach else None, "peak": round(peak, 1),
+                         "unit": "TFLOP/s", "frac": round(ach / peak, 4) if ach else None, "traffic": None,
+                         "kernel": "simt_tma_scan_kernel<ARGMIN, exact> (list assignment)",
+                         "kernel_ms": round(kern_ms, 4), "flops_per_launch": flops,
+                         "peak_source": "nominal CUDA-core fp32 (148 SMs x 128 lanes x 2 x 1.965 GHz); "
+                                        "no measured CUDA-core peak"},
+            "clocks": clk,
+        }
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return res
+
+
 def run_kmeans(args, wl):
     """k-means Lloyd iterations over 10M x 768 bf16 rows sharded over the
     ranks (centroid sums / counts all-reduced each iteration: strong scaling)."""
@@ -788,6 +885,8 @@ def main():
         res = run_ivf(args, wl)
     elif kind == "kmeans":
         res = run_kmeans(args, wl)
+    elif kind == "ivf_add":
+        res = run_ivf_add(args, wl)
     else:
         res = run_ours(args, wl)
     if res is not None:
