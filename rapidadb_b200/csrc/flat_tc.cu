@@ -332,9 +332,7 @@ __device__ __forceinline__ void tc_scan_body(uint8_t* smem_raw, const CUtensorMa
                                              const ScanArgs& a, const uint32_t idesc, unsigned* status) {
     using Cfg = TcCfg<PAIR>;
     constexpr int NST = Cfg::NSTAGE;
-    // 1024-byte aligned (the swizzle atom); an offset from the shared array
-    // itself keeps the epilogue's accesses in the shared window (not generic)
-    uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + NST * Cfg::STAGE_B);
     uint64_t* empty = full + NST;
     uint64_t* tfull = empty + NST;
