@@ -243,7 +243,8 @@ int rdb_pq_encode(const float* x, int64_t n, int64_t ldx, int d, const int32_t* 
 /* List-major IVF-PQ asymmetric-distance scan (squared L2): per (query,
  * probed list) a table LUT[m][j] = |(q - centroid)_m - codeword_mj|^2 is built
  * in shared memory and each stored code scores sum_m LUT[m][code_m]; output
- * layout as rdb_ivf_flat_scan.  Codes stored list by list; k <= 32. */
+ * layout as rdb_ivf_flat_scan.  Codes stored list by list in the slot ranges
+ * of rdb_ivf_flat_scan (list_off / list_end); k <= 32. */
 int rdb_ivfpq_scan(const float* q, int64_t nq, int64_t ldq, int d, const int64_t* probe, int nprobe,
                    const float* centroids, int nlist, const float* codebooks, int M, int ksub, const uint8_t* codes,
                    const int64_t* list_off, const int64_t* list_end, const int64_t* ids, int k, float* out_v,
@@ -261,7 +262,8 @@ int rdb_ivfpq_scan(const float* q, int64_t nq, int64_t ldq, int d, const int64_t
  *                        (stored byte s = code[(i + s) mod G]); inverse != 0
  *                        undoes it.  rdb_ivfpq_search reads rotated codes;
  *   rdb_ivfpq_search     probe [nq, nprobe] list ids; codes / row_terms /
- *                        ids in list order (list_off [nlist + 1]); writes the
+ *                        ids in list order (slot ranges list_off [nlist + 1]
+ *                        / list_end [nlist] as rdb_ivf_flat_scan); writes the
  *                        best k (k <= 32) per query, ascending, ties to the
  *                        lower stored row, to out_v / out_i [nq, k] (ids[row],
  *                        or -1 padding).  nprobe <= 4096, nlist <= 16384,

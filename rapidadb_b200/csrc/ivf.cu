@@ -520,11 +520,13 @@ int ivf_flat_smem_attr(int bytes) {
 template <typename T>
 void launch_ivf_flat(bool expand, dim3 grid, cudaStream_t s, int metric, int cos_small, const void* q, int64_t nq,
                      int64_t ldq, int d, const float* qv, int nprobe, const int64_t* eperm, const int64_t* eseg,
-                     const void* rows, int64_t ldx, const float* xv, const int64_t* list_off, const int64_t* list_end, int nlist,
+                     const void* rows, int64_t ldx, const float* xv, const int64_t* list_off,
+                     const int64_t* list_end, int nlist,
                      const int64_t* ids, int k, float* out_v, int64_t* out_i) {
     auto kern = expand ? ivf_flat_scan_kernel<T, true> : ivf_flat_scan_kernel<T, false>;
     kern<<<grid, FNT, sizeof(IvfFlatSmem), s>>>(metric, cos_small, static_cast<const T*>(q), nq, ldq, d, qv, nprobe,
-                                                eperm, eseg, static_cast<const T*>(rows), ldx, xv, list_off, list_end, nlist,
+                                                eperm, eseg, static_cast<const T*>(rows), ldx, xv, list_off,
+                                                list_end, nlist,
                                                 ids, k, out_v, out_i);
 }
 
@@ -543,7 +545,8 @@ extern "C" {
 size_t rdb_ivf_scan_workspace(int64_t nq, int nprobe, int nlist) { return ivf_ws(nq, nprobe, nlist).bytes; }
 
 int rdb_ivf_flat_scan(int metric, int dtype, const void* q, int64_t nq, int64_t ldq, int d, const int64_t* probe,
-                      int nprobe, const void* rows, int64_t ldx, const float* xv, const int64_t* list_off, const int64_t* list_end, int nlist,
+                      int nprobe, const void* rows, int64_t ldx, const float* xv, const int64_t* list_off,
+                      const int64_t* list_end, int nlist,
                       const int64_t* ids, int k, float* out_v, int64_t* out_i, void* ws, size_t ws_bytes,
                       void* stream) {
     RDB_CHECK_ARG(metric >= 0 && metric <= 2, "unknown metric %d", metric);
@@ -633,7 +636,8 @@ int rdb_pq_encode(const float* x, int64_t n, int64_t ldx, int d, const int32_t* 
 
 int rdb_ivfpq_scan(const float* q, int64_t nq, int64_t ldq, int d, const int64_t* probe, int nprobe,
                    const float* centroids, int nlist, const float* codebooks, int M, int ksub, const uint8_t* codes,
-                   const int64_t* list_off, const int64_t* list_end, const int64_t* ids, int k, float* out_v, int64_t* out_i, void* ws,
+                   const int64_t* list_off, const int64_t* list_end, const int64_t* ids, int k, float* out_v,
+                   int64_t* out_i, void* ws,
                    size_t ws_bytes, void* stream) {
     RDB_CHECK_ARG(nq >= 0 && d >= 1 && M >= 1 && d % M == 0, "d must be a multiple of M");
     RDB_CHECK_ARG(ksub >= 1 && ksub <= 256, "ksub must be in [1, 256]");

@@ -418,7 +418,8 @@ PqSearchWs pq_search_ws(int64_t nq, int nlist) {
 template <int M>
 int launch_search(const float* q, int64_t nq, int64_t ldq, int d, const int64_t* probe, int nprobe,
                   const float* centroids, int nlist, const float* codebooks, int ksub, const uint8_t* codes,
-                  const float* row_terms, const int64_t* list_off, const int64_t* list_end, const int64_t* ids, const int64_t* order, int k,
+                  const float* row_terms, const int64_t* list_off, const int64_t* list_end, const int64_t* ids,
+                  const int64_t* order, int k,
                   float* out_v, int64_t* out_i, cudaStream_t s) {
     const PqSmem sm = pq_smem(M, d, nprobe);
     static bool attr[64] = {false};
@@ -437,7 +438,8 @@ int launch_search(const float* q, int64_t nq, int64_t ldq, int d, const int64_t*
     cudaEvent_t stop_ev;
     RDB_TRY(timing_begin(TIMING_PQ_SCAN, s, &stop_ev));
     ivfpq_search_kernel<M><<<static_cast<unsigned>(grid), SNT, sm.bytes, s>>>(
-        q, nq, ldq, d, probe, nprobe, centroids, nlist, codebooks, ksub, codes, row_terms, list_off, list_end, ids, order, k,
+        q, nq, ldq, d, probe, nprobe, centroids, nlist, codebooks, ksub, codes, row_terms, list_off, list_end, ids, order,
+        k,
         sm, out_v, out_i);
     RDB_LAUNCH_CHECK();
     if (stop_ev) RDB_CUDA_TRY(cudaEventRecord(stop_ev, s));
@@ -497,7 +499,8 @@ size_t rdb_ivfpq_search_workspace(int64_t nq, int nlist) {
 
 int rdb_ivfpq_search(const float* q, int64_t nq, int64_t ldq, int d, const int64_t* probe, int nprobe,
                      const float* centroids, int nlist, const float* codebooks, int M, int ksub,
-                     const uint8_t* codes, const float* row_terms, const int64_t* list_off, const int64_t* list_end, const int64_t* ids,
+                     const uint8_t* codes, const float* row_terms, const int64_t* list_off, const int64_t* list_end,
+                     const int64_t* ids,
                      int k, float* out_v, int64_t* out_i, void* ws, size_t ws_bytes, void* stream) {
     RDB_CHECK_ARG(fast_m(M), "rdb_ivfpq_search needs pq_m in {4, 8, 16, 32, 64, 96}, got %d", M);
     RDB_CHECK_ARG(d >= M && d % M == 0 && ldq >= d, "bad shape");

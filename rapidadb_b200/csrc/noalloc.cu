@@ -75,7 +75,8 @@ int rdb_ivf_flat_scan_noalloc(int metric, int dtype, const void* q, int64_t nq, 
                          (long long)nq, nprobe, nlist, need, kNoAllocScratchBytes);
     void* scratch = nullptr;
     RDB_TRY(scratch_address(&scratch));
-    return rdb_ivf_flat_scan(metric, dtype, q, nq, ldq, d, probe, nprobe, rows, ldx, xv, list_off, list_end, nlist, ids, k,
+    return rdb_ivf_flat_scan(metric, dtype, q, nq, ldq, d, probe, nprobe, rows, ldx, xv, list_off, list_end, nlist, ids,
+                             k,
                              out_v, out_i, scratch, kNoAllocScratchBytes, stream);
 }
 
