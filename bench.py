@@ -80,6 +80,9 @@ def parse():
     ap.add_argument("--seed", type=int, default=42)
     ap.add_argument("--rows", type=int, default=0, help="override the workload's stored rows")
     ap.add_argument("--queries", type=int, default=0, help="override the per-GPU query batch")
+    ap.add_argument("--results", default="owner", choices=["owner", "replicated"],
+                    help="flat search on N > 1 GPUs: each rank returns the answers of its query slice "
+                         "(owner) or of the whole batch (replicated)")
     return ap.parse_args()
 
 
@@ -258,7 +261,8 @@ def run_ours(args, wl):
     db = RapidaDB(config=cfg)
     db.add(x, torch.arange(lo, hi, device=dev, dtype=torch.long))
     largest = wl["metric"] != "l2"
-    searcher = ShardedSearch(db, largest)
+    searcher = ShardedSearch(db, largest, results=args.results if world > 1 else "replicated")
+    own_lo, own_hi = searcher.owned_range(Q)
 
     def step(qdev):
         return searcher.search(qdev, k)
@@ -352,7 +356,7 @@ def run_ours(args, wl):
         e2e_mode = "pipelined: AsyncBatchSearcher, 2 worker streams, one batch per step"
 
     # ---- recall against exact fp32 search over the same stored values
-    nrec = min(64, Q)
+    nrec = min(64, own_hi - own_lo)  # rank 0 owns the first queries in every results mode
     qs = q[:nrec].float()
     xs = x.float()
     if wl["metric"] == "cosine":
@@ -406,6 +410,11 @@ def run_ours(args, wl):
                 "rows": N, "dim": d, "queries_per_step": Q, "k": k, "metric": wl["metric"],
                 "precision": wl["precision"], "rows_per_gpu": n_local,
                 "parallelism": f"row-shard x{world}" if world > 1 else "single GPU",
+                **({"results": ("owner: rank r merges and returns the answers of its 1/%d slice of the "
+                                "query batch (all-to-all of the per-rank lists)" % world)
+                    if args.results == "owner" else "replicated: every rank merges the whole batch "
+                                                    "(all-gather of the per-rank lists)"}
+                   if world > 1 else {}),
                 "l2_flush": "not needed: stored rows (%.2f GB) exceed L2 (126 MB)" % (
                     n_local * d * (2 if wl["precision"] != "fp32" else 4) / 1e9),
                 "recall_at_k_vs_fp32_exact": round(recall, 5),

@@ -50,6 +50,24 @@ def gather_candidates(local_d: torch.Tensor, local_i: torch.Tensor,
     return vals, ids
 
 
+def exchange_owned(local_d: torch.Tensor, local_i: torch.Tensor,
+                   group: Optional[dist.ProcessGroup] = None) -> Tuple[torch.Tensor, torch.Tensor]:
+    """Owner exchange of [Q, k] lists: query slice r (shard_range(Q, r,
+    world), contiguous rows) of every rank goes to rank r, which receives
+    [G, Q_r, k] scores and ids -- 1 / G of an all-gather's bytes, no packing
+    copies (one all-to-all for the scores, one for the ids)."""
+    world = dist.get_world_size(group)
+    rank = dist.get_rank(group)
+    Q, k = local_d.shape
+    sizes = [(b - a) * k for a, b in (shard_range(Q, r, world) for r in range(world))]
+    n_r = sizes[rank] // k if k else 0
+    vals = torch.empty(world * sizes[rank], dtype=local_d.dtype, device=local_d.device)
+    ids = torch.empty(world * sizes[rank], dtype=local_i.dtype, device=local_i.device)
+    dist.all_to_all_single(vals, local_d.contiguous().view(-1), [sizes[rank]] * world, sizes, group=group)
+    dist.all_to_all_single(ids, local_i.contiguous().view(-1), [sizes[rank]] * world, sizes, group=group)
+    return vals.view(world, n_r, k), ids.view(world, n_r, k)
+
+
 def gpu_merge(vals: torch.Tensor, ids: torch.Tensor, k: int, largest: bool):
     from rapidadb_b200._lib import C
 
@@ -91,19 +109,35 @@ class ShardedSearch:
         group:        process group (default: the world).
         merge:        (vals [G,Q,k], ids [G,Q,k], k, largest) -> (vals, ids);
                       defaults to the GPU merge kernel.
+        results:      "replicated" -- every rank returns the [Q, k] answer of
+                      the whole batch (one all-gather of the per-rank lists);
+                      "owner" -- rank r returns the answer of its query slice
+                      owned_range(Q) only (an all-to-all carrying 1 / G of
+                      the bytes, and a merge of 1 / G of the queries), the
+                      shared threshold likewise selected per slice.
     """
 
     def __init__(self, index, largest: bool, group: Optional[dist.ProcessGroup] = None,
-                 merge: Optional[Callable] = None, shared_threshold: bool = True):
+                 merge: Optional[Callable] = None, shared_threshold: bool = True, results: str = "replicated"):
+        if results not in ("replicated", "owner"):
+            raise ValueError(f"results must be 'replicated' or 'owner', got {results!r}")
         self.search_fn = index if callable(index) and not hasattr(index, "search") else index.search
         self.largest = largest
         self.group = group
         self.merge = merge or gpu_merge
+        self.results = results
         # the extension FlatIndex (directly or inside a RapidaDB facade) with
         # fp16 / bf16 rows can share one sampled threshold across the shards
         flat = getattr(index, "index", index)
         self.flat = flat if shared_threshold and hasattr(flat, "sample_maxima") and flat.tensor_core() else None
         self._sizes = None
+
+    def owned_range(self, Q: int) -> Tuple[int, int]:
+        """Queries [lo, hi) of a Q-query batch whose answers this rank
+        returns ([0, Q) unless results="owner" on more than one rank)."""
+        if self.results != "owner" or not dist.is_initialized() or dist.get_world_size(self.group) == 1:
+            return 0, Q
+        return shard_range(Q, dist.get_rank(self.group), dist.get_world_size(self.group))
 
     def refresh_sizes(self) -> None:
         """Forget the cached shard sizes (call on every rank after adds or
@@ -112,12 +146,14 @@ class ShardedSearch:
 
     def _shared_threshold_search(self, queries: torch.Tensor, k: int):
         """Shared-threshold protocol: every rank computes group maxima of a
-        strided sample of its rows (1 / world of the single-GPU sample), the
-        maxima are all-gathered, the k-th best of them -- a lower bound on the
-        global k-th best score -- filters every shard.  One collective per
-        search (the maxima) besides the result gather; the shard sizes are
-        gathered on the first search.  None (before any data collective) when
-        the shards are too small."""
+        strided sample of its rows (1 / world of the single-GPU sample); the
+        k-th best of all ranks' maxima of a query -- a lower bound on its
+        global k-th best score -- filters every shard.  results="replicated"
+        all-gathers the maxima and every rank selects every query's threshold;
+        results="owner" sends each rank the maxima of its query slice
+        (all-to-all), selects those thresholds there and all-gathers them.
+        The shard sizes are gathered on the first search.  None (before any
+        data collective) when the shards are too small."""
         world = dist.get_world_size(self.group)
         dev = queries.device
         if self._sizes is None:
@@ -134,12 +170,34 @@ class ShardedSearch:
         per, g, total = plan
         maxima = self.flat.sample_maxima(queries, per, g)  # [Q, per / g]
         Q, gl = maxima.shape
-        allm = torch.empty((world * Q, gl), dtype=maxima.dtype, device=dev)
-        dist.all_gather_into_tensor(allm, maxima.contiguous(), group=self.group)
-        allm = allm.view(world, Q, gl).permute(1, 0, 2).reshape(Q, world * gl)
         from rapidadb_b200._lib import C
 
-        thr = C().select_threshold(allm, k, self.largest)
+        if self.results == "owner":
+            # each rank selects the thresholds of its query slice from every
+            # rank's maxima, then the thresholds are all-gathered
+            lo, hi = self.owned_range(Q)
+            sizes = [(b - a) * gl for a, b in (shard_range(Q, r, world) for r in range(world))]
+            recv = torch.empty(world * (hi - lo) * gl, dtype=maxima.dtype, device=dev)
+            dist.all_to_all_single(recv, maxima.contiguous().view(-1), [(hi - lo) * gl] * world, sizes,
+                                   group=self.group)
+            mine = recv.view(world, hi - lo, gl).permute(1, 0, 2).reshape(hi - lo, world * gl)
+            cap = -(-Q // world)  # slices differ by at most one query: pad to the largest
+            thr_mine = torch.zeros(cap, dtype=maxima.dtype, device=dev)
+            if hi > lo:
+                thr_mine[: hi - lo] = C().select_threshold(mine, k, self.largest)
+            allt = torch.empty(world * cap, dtype=maxima.dtype, device=dev)
+            dist.all_gather_into_tensor(allt, thr_mine, group=self.group)
+            if Q % world == 0:
+                thr = allt
+            else:
+                allt = allt.view(world, cap)
+                thr = torch.cat([allt[r, : b - a] for r, (a, b) in enumerate(shard_range(Q, r, world)
+                                                                              for r in range(world))])
+        else:
+            allm = torch.empty((world * Q, gl), dtype=maxima.dtype, device=dev)
+            dist.all_gather_into_tensor(allm, maxima.contiguous(), group=self.group)
+            allm = allm.view(world, Q, gl).permute(1, 0, 2).reshape(Q, world * gl)
+            thr = C().select_threshold(allm, k, self.largest)
         expect = int(math.ceil(1.1 * self.flat.size() * k / total)) + 1
         return self.flat.search_threshold(queries, k, thr, expect)
 
@@ -150,7 +208,10 @@ class ShardedSearch:
         if self.flat is not None:
             out = self._shared_threshold_search(queries, k)
         local_d, local_i = out if out is not None else self.search_fn(queries, k)
-        vals, ids = gather_candidates(local_d, local_i, self.group)
+        if self.results == "owner":
+            vals, ids = exchange_owned(local_d, local_i, self.group)
+        else:
+            vals, ids = gather_candidates(local_d, local_i, self.group)
         return self.merge(vals, ids, k, self.largest)
 
 

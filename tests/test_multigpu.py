@@ -60,6 +60,10 @@ def _worker(rank, port, out_q):
         flat.add(xt, torch.arange(lo, hi, device=dev))
         d, i = ShardedSearch(flat, largest=True).search(qt, 20)
         res["flat"] = (d.cpu().numpy(), i.cpu().numpy())
+        # the same with each rank answering only its query slice
+        so = ShardedSearch(flat, largest=True, results="owner")
+        d, i = so.search(qt, 20)
+        res["flat_owner"] = (so.owned_range(len(q)), d.cpu().numpy(), i.cpu().numpy())
         # k-means over the shards (sums / counts all-reduced)
         km = kmeans(xt, 32, max_iters=5, tol=0.0, seed=3, group=dist.group.WORLD, exact_assign=True)
         res["kmeans"] = (km.centroids.cpu().numpy(), km.inertia)
@@ -89,6 +93,7 @@ def test_sharded_equals_single_gpu():
     import rapidadb._C as _C
     from parity import assert_topk_match
     from rapidadb_b200.kmeans import kmeans
+    from rapidadb_b200.sharded import shard_range
 
     ctx = mp.get_context("spawn")
     q_ = ctx.Queue()
@@ -115,8 +120,15 @@ def test_sharded_equals_single_gpu():
     pq.set_quantizer(km.centroids, _books(xt.device))
     pq.add(xt)
     dp, ip = pq.search(qt, 10)
+    covered = 0
     for r in range(WORLD):
         assert_topk_match(d.cpu().numpy(), i.cpu().numpy(), *out[r]["flat"], rtol=1e-4, atol=1e-5)
+        (a, b), do, io = out[r]["flat_owner"]
+        assert (a, b) == shard_range(len(q), r, WORLD)
+        assert_topk_match(d[a:b].cpu().numpy(), i[a:b].cpu().numpy(), do, io, rtol=1e-4, atol=1e-5)
+        covered += b - a
+    assert covered == len(q)
+    for r in range(WORLD):
         np.testing.assert_allclose(out[r]["kmeans"][0], km.centroids.cpu().numpy(), rtol=1e-5, atol=1e-5)
         assert abs(out[r]["kmeans"][1] - km.inertia) <= 1e-5 * km.inertia
         assert_topk_match(di.cpu().numpy(), ii.cpu().numpy(), *out[r]["ivf"], rtol=1e-5, atol=1e-4)

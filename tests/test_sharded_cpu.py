@@ -103,6 +103,35 @@ def test_sharded_flat_search_equals_single_process():
         np.testing.assert_allclose(out[r][0], rd, rtol=1e-6)
 
 
+def _owner_search(rank, world):
+    x, q = _data()
+    lo, hi = shard_range(len(x), rank, world)
+
+    def local(qt, k):
+        d, i = oracle.flat_search("l2", qt.numpy(), x[lo:hi], k, ids=np.arange(lo, hi, dtype=np.int64))
+        return torch.from_numpy(d), torch.from_numpy(i)
+
+    s = ShardedSearch(local, largest=False, merge=_oracle_merge, results="owner")
+    d, i = s.search(torch.from_numpy(q), 10)
+    return s.owned_range(len(q)), d.numpy(), i.numpy()
+
+
+@pytest.mark.parametrize("world", [2, 3])
+def test_owner_results_cover_the_batch_once(world):
+    """results="owner": rank r returns the merged answers of its query slice
+    (17 queries: uneven slices); together they equal the single-process
+    answer, each query once."""
+    out = _run(_owner_search, world)
+    x, q = _data()
+    rd, ri = oracle.flat_search("l2", q, x, 10)
+    ranges = [out[r][0] for r in range(world)]
+    assert ranges == [shard_range(len(q), r, world) for r in range(world)]
+    for r in range(world):
+        a, b = ranges[r]
+        np.testing.assert_array_equal(out[r][2], ri[a:b])
+        np.testing.assert_allclose(out[r][1], rd[a:b], rtol=1e-6)
+
+
 def _sharded_kmeans(rank, world):
     from rapidadb_b200.kmeans import kmeans
 
