@@ -39,29 +39,29 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
 WORKLOADS = {
-    # BASELINE config "Flat cosine search ... 1,000,000 x 768 bf16 ... 1,024 queries, k=100"
+    # flat cosine search: 1,000,000 x 768 bf16 rows, 1,024 queries, k = 100 (the headline workload)
     "flat_cosine_bf16": dict(N=1_000_000, d=768, Q=1024, k=100, metric="cosine", precision="bf16",
                              normalize=True),
-    # BASELINE config "Flat exact L2 search: fp32 base N=100,000 x 768, 32 queries, k=10"
+    # flat exact L2 search: 100,000 x 768 fp32 rows, 32 queries, k = 10 (the reference's CPU-runnable case)
     "flat_l2_fp32": dict(N=100_000, d=768, Q=32, k=10, metric="l2", precision="fp32",
                          normalize=False),
-    # BASELINE config "IVF-Flat: N=10,000,000 x 128 fp32, mixture of 1,024 Gaussians
+    # IVF-Flat: 10,000,000 x 128 fp32 rows from a mixture of 1,024 Gaussians
     # (centres ~N(0,4I), sigma=1); nlist=4,096 trained by 20 k-means iterations on a 1M
-    # sample; 10,000 queries; nprobe=32; k=10"
+    # sample; 10,000 queries; nprobe=32; k=10
     "ivf_flat": dict(kind="ivf", N=10_000_000, d=128, Q=10_000, k=10, metric="l2", nlist=4096,
                      nprobe=32, ncentres=1024, spread=2.0, sigma=1.0, train=1_000_000, iters=20,
                      uint8=False),
-    # BASELINE config "IVF-PQ sharded across 8 GPUs: N=100,000,000 x 128 uint8-valued (stored
-    # fp32); nlist=16,384; M=16 x 256; 10,000 queries; nprobe=64; k=10"
+    # IVF-PQ (sharded across up to 8 GPUs): 100,000,000 x 128 uint8-valued rows (stored
+    # fp32); nlist=16,384; M=16 x 256; 10,000 queries; nprobe=64; k=10
     "ivf_pq": dict(kind="ivf_pq", N=100_000_000, d=128, Q=10_000, k=10, metric="l2", nlist=16384,
                    nprobe=64, M=16, ksub=256, ncentres=1024, spread=2.0, sigma=1.0, train=262_144,
                    iters=10, uint8=True),
-    # streaming add into the IVF-Flat config's index: batches of 10,000 rows
+    # streaming add into the IVF-Flat workload's index: batches of 10,000 rows
     # appended to the 10,000,000 stored rows
     "ivf_add": dict(kind="ivf_add", N=10_000_000, d=128, batch=10_000, nlist=4096, nprobe=32,
                     ncentres=1024, spread=2.0, sigma=1.0, train=1_000_000, iters=20, uint8=False),
-    # BASELINE config "k-means: N=10,000,000 x 768 bf16, mixture of 16,384 Gaussians (centres
-    # ~N(0,I), sigma=0.3); K=16,384; seeded random-row init; 20 Lloyd iterations"
+    # k-means: 10,000,000 x 768 bf16 points from a mixture of 16,384 Gaussians (centres
+    # ~N(0,I), sigma=0.3); K=16,384; seeded random-row init; 20 Lloyd iterations
     "kmeans": dict(kind="kmeans", N=10_000_000, d=768, K=16384, iters=20, ncentres=16384,
                    spread=1.0, sigma=0.3),
 }
