@@ -266,15 +266,41 @@ int run_chunk(const FlatPlan& P, int metric, int dtype, const void* q, int64_t n
         sc.nsplit = P.s.nsplit;
         sc.rows_per_split = P.s.rps;
         sc.cap = P.s.cap;
-        RDB_TRY(scan(sc));
-        SelectArgs ss = sa;
-        ss.output = SEL_OUT_THRESHOLD;
-        ss.cap = P.s.cap;
-        ss.nsplit = P.s.nsplit;
-        ss.row_step = P.s.row_step;
-        ss.out_thr = thr;
-        ss.overflow = nullptr;
-        RDB_TRY(launch_select(ss, s));
+        const int64_t nchunk = (d + 31) / 32;
+        const int64_t ctas = (int64_t)P.s.nsplit * ((nq + kSimtQueries - 1) / kSimtQueries);
+        if (2 * ctas <= num_sms() && nchunk > 1 && simt_tma_ok(sc, SCAN_PARTIAL)) {
+            // fewer sample tiles than half the SMs: split the K chunks of each
+            // tile over several CTAs (partial dot products summed into a dense
+            // [nq, S] block that fits in the candidate area), then final
+            // scores and the k-th best of each row.  The sums are exact to a
+            // few ulps, inside the filter's slack.
+            sc.ksplit = (int)std::min<int64_t>(nchunk, num_sms() / ctas);
+            sc.dense_out = reinterpret_cast<float*>(cand);
+            sc.ld_out = P.s.rows;
+            RDB_CUDA_TRY(cudaMemsetAsync(sc.dense_out, 0, sizeof(float) * (size_t)nq * P.s.rows, s));
+            RDB_TRY(launch_scan_simt(sc, SCAN_PARTIAL, s));
+            RDB_TRY(launch_partial_finalize(sc, s));
+            SelectArgs ss = {};
+            ss.input = SEL_DENSE;
+            ss.output = SEL_OUT_THRESHOLD;
+            ss.nq = nq;
+            ss.k = k;
+            ss.largest = largest ? 1 : 0;
+            ss.dense = sc.dense_out;
+            ss.dense_n = P.s.rows;
+            ss.out_thr = thr;
+            RDB_TRY(launch_select(ss, s));
+        } else {
+            RDB_TRY(scan(sc));
+            SelectArgs ss = sa;
+            ss.output = SEL_OUT_THRESHOLD;
+            ss.cap = P.s.cap;
+            ss.nsplit = P.s.nsplit;
+            ss.row_step = P.s.row_step;
+            ss.out_thr = thr;
+            ss.overflow = nullptr;
+            RDB_TRY(launch_select(ss, s));
+        }
     }
     {
         ScanArgs sc = a;

@@ -14,6 +14,7 @@ enum ScanMode : int {
     SCAN_ARGMIN = 2,  // best row per (split, query) by squared L2
     SCAN_GROUPMAX = 3,  // best score of every `group` consecutive logical rows
     SCAN_ARGMIN_EXACT = 4,  // CUDA cores: argmin of sum (q - x)^2, one FMA per element in order
+    SCAN_PARTIAL = 5,  // fp32 TMA scan: dense_out[q, row] += dot over the K share of blockIdx.x % ksplit
 };
 
 struct ScanArgs {
@@ -43,7 +44,10 @@ struct ScanArgs {
     int nsplit;
     int64_t rows_per_split;  // multiple of the kernel's row tile
 
-    // SCAN_DENSE
+    // SCAN_PARTIAL: grid.x = nsplit * ksplit, dense_out zeroed by the caller
+    int ksplit;
+
+    // SCAN_DENSE (and SCAN_PARTIAL)
     float* dense_out;
     int64_t ld_out;
 
@@ -60,6 +64,12 @@ struct ScanArgs {
 
 // CUDA-core scan (any dtype).  Grid = (nsplit, ceil(nq / 32)).
 int launch_scan_simt(const ScanArgs& a, int mode, cudaStream_t stream);
+// true when launch_scan_simt runs `mode` on the TMA-fed fp32 kernel (the only
+// one with SCAN_PARTIAL)
+bool simt_tma_ok(const ScanArgs& a, int mode);
+// dense_out[q, row] = final score of the dot product it holds (qv, xv per
+// query / logical row), in place
+int launch_partial_finalize(const ScanArgs& a, cudaStream_t stream);
 
 // tcgen05 scan for fp16 / bf16 (sm_100a).  Grid = (nsplit, ceil(nq / 128)), or
 // with more than 128 queries CTA pairs: (2 nsplit, ceil(nq / 256)).

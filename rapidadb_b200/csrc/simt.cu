@@ -314,7 +314,9 @@ __global__ void __launch_bounds__(NT, 1)
     unsigned char* smem = tma_smem_raw + ((1024u - (tma::smem_addr(tma_smem_raw) & 1023u)) & 1023u);
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + kTmaStages * kTmaStageBytes);
 
-    const int split = blockIdx.x;
+    // SCAN_PARTIAL: CTA x covers split x / ksplit over its share of the K chunks
+    const int ks = MODE == SCAN_PARTIAL ? max(1, a.ksplit) : 1;
+    const int split = blockIdx.x / ks;
     const int64_t q0 = ((int64_t)blockIdx.z * gridDim.y + blockIdx.y) * BQ;
     if (q0 >= a.nq) return;
     const int64_t r_begin = (int64_t)split * a.rows_per_split;
@@ -322,7 +324,11 @@ __global__ void __launch_bounds__(NT, 1)
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int qg = (warp & 3) * 8;
     const int rb = (warp >> 2) * 128;
-    const int nchunk = (a.d + BK - 1) / BK;
+    const int nchunk_all = (a.d + BK - 1) / BK;
+    const int kpart = blockIdx.x - split * ks;
+    const int c_first = (int)((int64_t)kpart * nchunk_all / ks);
+    const int nchunk = (int)((int64_t)(kpart + 1) * nchunk_all / ks) - c_first;
+    if (nchunk <= 0) return;
     const int ntile = (int)((r_end - r_begin + BN - 1) / BN);
     const int nitems = ntile * nchunk;  // (tile, chunk) pairs in ring order
 
@@ -331,8 +337,8 @@ __global__ void __launch_bounds__(NT, 1)
         const int t = it / nchunk, c = it - t * nchunk;
         unsigned char* dst = smem + st * kTmaStageBytes;
         tma::bar_expect_tx(&full[st], kTmaStageBytes);
-        tma::load_2d(&tmap_x, &full[st], dst, c * BK, (int)(r_begin + (int64_t)t * BN));
-        tma::load_2d(&tmap_q, &full[st], dst + kTmaXBytes, c * BK, (int)q0);
+        tma::load_2d(&tmap_x, &full[st], dst, (c_first + c) * BK, (int)(r_begin + (int64_t)t * BN));
+        tma::load_2d(&tmap_q, &full[st], dst + kTmaXBytes, (c_first + c) * BK, (int)q0);
     };
     if (tid == 0) {
         tma::prefetch_map(&tmap_x);
@@ -416,6 +422,19 @@ __global__ void __launch_bounds__(NT, 1)
             }
             if (tid == 0 && it + kTmaStages < nitems) issue(it + kTmaStages);
         }
+        if (MODE == SCAN_PARTIAL) {
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                const int64_t q = q0 + qg + i;
+                if (q >= a.nq) continue;
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    const int64_t r = r0 + rb + lane + 32 * j;
+                    if (r < r_end) atomicAdd(&a.dense_out[q * a.ld_out + r], acc[i][j]);
+                }
+            }
+            continue;
+        }
         float xvr[4];
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
@@ -438,11 +457,21 @@ __global__ void __launch_bounds__(NT, 1)
     finish_split<MODE>(a, q0, split, qg, lane, tid, scnt, sbest, best);
 }
 
+__global__ void partial_finalize_kernel(int metric, int cos_small, float* __restrict__ dense, int64_t nq, int64_t n,
+                                        int64_t ld, const float* __restrict__ qv, const float* __restrict__ xv,
+                                        int64_t row_step) {
+    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= nq * n) return;
+    const int64_t q = i / n, r = i - q * n;
+    float* p = dense + q * ld + r;
+    if (metric != RDB_METRIC_DOT) *p = final_score(metric, cos_small, *p, qv[q], xv[r * row_step]);
+}
+
 // fp32 rows and queries whose layout suits the TMA maps (16-byte aligned
 // bases and strides, coordinates within int32)
 bool tma_scan_ok(const ScanArgs& a, int mode) {
     if (a.dtype != RDB_F32) return false;
-    if (mode != SCAN_FILTER && mode != SCAN_ARGMIN && mode != SCAN_ARGMIN_EXACT) return false;
+    if (mode != SCAN_FILTER && mode != SCAN_ARGMIN && mode != SCAN_ARGMIN_EXACT && mode != SCAN_PARTIAL) return false;
     if ((reinterpret_cast<uintptr_t>(a.q) & 15) || (reinterpret_cast<uintptr_t>(a.x) & 15)) return false;
     if (a.ldq % 4 || (a.ldx * a.row_step) % 4) return false;
     if (a.nq >= (1LL << 31) - BQ || a.n >= (1LL << 31) - 2 * BN) return false;
@@ -486,6 +515,17 @@ int launch_typed(const ScanArgs& a, int mode, cudaStream_t s, dim3 grid) {
 
 }  // namespace
 
+bool simt_tma_ok(const ScanArgs& a, int mode) { return tma_scan_ok(a, mode); }
+
+int launch_partial_finalize(const ScanArgs& a, cudaStream_t s) {
+    const int64_t total = a.nq * a.n;
+    if (total == 0) return RDB_OK;
+    partial_finalize_kernel<<<(unsigned)((total + 255) / 256), 256, 0, s>>>(a.metric, a.cos_small, a.dense_out, a.nq,
+                                                                          a.n, a.ld_out, a.qv, a.xv, a.row_step);
+    RDB_LAUNCH_CHECK();
+    return RDB_OK;
+}
+
 int launch_scan_simt(const ScanArgs& a, int mode, cudaStream_t s) {
     if (a.nq <= 0 || a.n <= 0) return RDB_OK;
     RDB_CHECK_ARG(a.rows_per_split % kSimtRows == 0, "rows_per_split must be a multiple of %d",
@@ -497,8 +537,15 @@ int launch_scan_simt(const ScanArgs& a, int mode, cudaStream_t s) {
     if (tma_scan_ok(a, mode)) {
         if (mode == SCAN_FILTER) return launch_tma_typed<SCAN_FILTER, false>(a, grid, s);
         if (mode == SCAN_ARGMIN) return launch_tma_typed<SCAN_ARGMIN, false>(a, grid, s);
+        if (mode == SCAN_PARTIAL) {
+            RDB_CHECK_ARG(a.dense_out && a.ksplit >= 1 && a.ksplit <= (a.d + BK - 1) / BK, "bad partial scan");
+            RDB_CHECK_ARG((int64_t)a.nsplit * a.ksplit <= 0x7fffffffLL, "too many CTAs");
+            dim3 g2(a.nsplit * a.ksplit, grid.y, grid.z);
+            return launch_tma_typed<SCAN_PARTIAL, false>(a, g2, s);
+        }
         return launch_tma_typed<SCAN_ARGMIN, true>(a, grid, s);
     }
+    RDB_CHECK_ARG(mode != SCAN_PARTIAL, "SCAN_PARTIAL needs fp32 operands in a TMA layout");
     switch (a.dtype) {
         case RDB_F32: return launch_typed<float>(a, mode, s, grid);
         case RDB_F16: return launch_typed<__half>(a, mode, s, grid);

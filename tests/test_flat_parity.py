@@ -33,6 +33,8 @@ SHAPES = [  # (N, Q, d, k)
     (4097, 1, 200, 1),
     (20000, 33, 768, 100),
     (20000, 300, 64, 10),  # at least one query per SM: the warp-per-query selects
+    (40000, 7, 64, 10),    # one query block: the fp32 sample pass split over K (2 chunks)
+    (36000, 20, 300, 30),  # the same over 10 K chunks, the last one partial
 ]
 
 
