@@ -224,14 +224,24 @@ class ShardedIVFSearch:
     all-gathered, so the replicated probe costs each GPU 1/G of the batch.
     Every rank then scans its rows of the probed lists for all queries
     (``index.search_probed``), and the per-rank [Q, k] lists are all-gathered
-    and merged as in ShardedSearch."""
+    and merged as in ShardedSearch (results="owner": each rank merges and
+    returns only its query slice, owned_range(Q), after an all-to-all)."""
 
     def __init__(self, index, largest: bool, group: Optional[dist.ProcessGroup] = None,
-                 merge: Optional[Callable] = None):
+                 merge: Optional[Callable] = None, results: str = "replicated"):
+        if results not in ("replicated", "owner"):
+            raise ValueError(f"results must be 'replicated' or 'owner', got {results!r}")
         self.index = index
         self.largest = largest
         self.group = group
         self.merge = merge or gpu_merge
+        self.results = results
+
+    def owned_range(self, Q: int) -> Tuple[int, int]:
+        """Queries [lo, hi) of a Q-query batch whose answers this rank returns."""
+        if self.results != "owner" or not dist.is_initialized() or dist.get_world_size(self.group) == 1:
+            return 0, Q
+        return shard_range(Q, dist.get_rank(self.group), dist.get_world_size(self.group))
 
     def probe(self, queries: torch.Tensor) -> torch.Tensor:
         if not dist.is_initialized() or dist.get_world_size(self.group) == 1:
@@ -255,5 +265,8 @@ class ShardedIVFSearch:
         local_d, local_i = self.index.search_probed(queries, probe, k)
         if not dist.is_initialized() or dist.get_world_size(self.group) == 1:
             return local_d, local_i
-        vals, ids = gather_candidates(local_d, local_i, self.group)
+        if self.results == "owner":
+            vals, ids = exchange_owned(local_d, local_i, self.group)
+        else:
+            vals, ids = gather_candidates(local_d, local_i, self.group)
         return self.merge(vals, ids, k, self.largest)

@@ -132,6 +132,82 @@ def test_owner_results_cover_the_batch_once(world):
         np.testing.assert_allclose(out[r][1], rd[a:b], rtol=1e-6)
 
 
+class _OracleIVFShard:
+    """One rank's slice of an IVF-Flat index on the CPU oracle: the coarse
+    probe is the oracle's exact L2 search over the centroids, the list scan
+    an exact search over the slice's rows whose list is probed."""
+
+    def __init__(self, x, labels, lo, hi, cent, nprobe):
+        self.x, self.labels, self.lo, self.hi = x, labels, lo, hi
+        self.cent, self.nprobe = cent, nprobe
+
+    def probe(self, qt):
+        _, i = oracle.flat_search("l2", qt.numpy(), self.cent, self.nprobe)
+        return torch.from_numpy(i)
+
+    def search_probed(self, qt, probe, k):
+        q = qt.numpy()
+        out_d = np.full((len(q), k), np.inf, np.float32)
+        out_i = np.full((len(q), k), -1, np.int64)
+        lab = self.labels[self.lo:self.hi]
+        for j in range(len(q)):
+            rows = np.nonzero(np.isin(lab, probe[j].numpy()))[0]
+            if len(rows) == 0:
+                continue
+            kk = min(k, len(rows))
+            d, i = oracle.flat_search("l2", q[j:j + 1], self.x[self.lo + rows], kk,
+                                      ids=(self.lo + rows).astype(np.int64))
+            out_d[j, :kk], out_i[j, :kk] = d[0], i[0]
+        return torch.from_numpy(out_d), torch.from_numpy(out_i)
+
+
+def _ivf_setup():
+    x, q = _data()
+    cent = x[:20].copy()
+    labels = oracle.kmeans_assign(x, cent)[0]
+    return x, q, cent, labels
+
+
+def _sharded_ivf(rank, world, results):
+    from rapidadb_b200.sharded import ShardedIVFSearch
+
+    x, q, cent, labels = _ivf_setup()
+    lo, hi = shard_range(len(x), rank, world)
+    s = ShardedIVFSearch(_OracleIVFShard(x, labels, lo, hi, cent, 4), largest=False, merge=_oracle_merge,
+                         results=results)
+    d, i = s.search(torch.from_numpy(q), 10)
+    return s.owned_range(len(q)), d.numpy(), i.numpy()
+
+
+def _sharded_ivf_replicated(rank, world):
+    return _sharded_ivf(rank, world, "replicated")
+
+
+def _sharded_ivf_owner(rank, world):
+    return _sharded_ivf(rank, world, "owner")
+
+
+@pytest.mark.parametrize("mode", ["replicated", "owner"])
+def test_sharded_ivf_equals_single_process(mode):
+    """Coarse probe split across two ranks and all-gathered, each rank
+    scanning its rows of the probed lists, lists exchanged and merged: the
+    same answer as the single-process oracle IVF-Flat search (each query once
+    in owner mode)."""
+    out = _run(_sharded_ivf_replicated if mode == "replicated" else _sharded_ivf_owner)
+    x, q, cent, labels = _ivf_setup()
+    order = np.argsort(labels, kind="stable")
+    off = np.concatenate([[0], np.cumsum(np.bincount(labels, minlength=len(cent)))]).astype(np.int64)
+    rd, ri = oracle.ivf_flat_search("l2", q, cent, off, x[order], order.astype(np.int64), 4, 10)
+    covered = 0
+    for r in (0, 1):
+        (a, b), d, i = out[r]
+        assert (a, b) == ((0, len(q)) if mode == "replicated" else shard_range(len(q), r, 2))
+        np.testing.assert_array_equal(i, ri[a:b])
+        np.testing.assert_allclose(d, rd[a:b], rtol=1e-5)
+        covered += b - a
+    assert covered == (2 if mode == "replicated" else 1) * len(q)
+
+
 def _sharded_kmeans(rank, world):
     from rapidadb_b200.kmeans import kmeans
 
