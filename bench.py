@@ -80,7 +80,7 @@ def parse():
     ap.add_argument("--seed", type=int, default=42)
     ap.add_argument("--rows", type=int, default=0, help="override the workload's stored rows")
     ap.add_argument("--queries", type=int, default=0, help="override the per-GPU query batch")
-    ap.add_argument("--results", default="replicated", choices=["owner", "replicated"],
+    ap.add_argument("--results", default="owner", choices=["owner", "replicated"],
                     help="flat search on N > 1 GPUs: each rank returns the answers of its query slice "
                          "(owner) or of the whole batch (replicated)")
     return ap.parse_args()
