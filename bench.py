@@ -6,7 +6,9 @@ rows x 768 dims in bf16 (i.i.d. N(0,1) rows, L2-normalised, then rounded),
 queries of the same distribution, k = 100.  With N GPUs (torchrun, one
 process per GPU) the 1,000,000 rows are split by rows across the ranks and the
 query batch is 1,024 x N (per-GPU work fixed: "scaling": "weak"); each step is
-local fused search -> NCCL all-gather of the [Q, k] lists -> merge kernel.
+local fused search -> NCCL all-to-all of the [Q, k] lists by query slice ->
+merge kernel on the rank owning the slice (``--results replicated``: an
+all-gather and a merge of the whole batch on every rank).
 
 * ``value``  - queries/s with queries already resident in HBM, timed with CUDA
                events between barriers, max over ranks.  The stored rows
