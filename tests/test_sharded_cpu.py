@@ -253,6 +253,30 @@ def test_rank_failure_is_reported_not_hung():
     assert any(p.exitcode != 0 for p in ps)
 
 
+def test_shared_sample_plan_bounds():
+    """The shared-threshold sample: a power-of-two group size <= 128 dividing
+    each rank's share, at most a quarter of the smallest shard sampled, and at
+    least 4 k group maxima in all; None when the shards are too small."""
+    from rapidadb_b200.sharded import shared_sample_plan
+
+    assert shared_sample_plan([125_000] * 8, 100) == (8192, 64, 65536)  # 1M rows, k = 100 on 8 ranks
+    for sizes, k in [([500_000, 500_001], 100), ([20_000, 15_000, 15_001], 10), ([1_000_000] * 4, 1)]:
+        per, g, total = shared_sample_plan(sizes, k)
+        assert g & (g - 1) == 0 and g <= 128 and per % g == 0
+        assert total == len(sizes) * per and 4 * per <= min(sizes)
+        assert len(sizes) * (per // g) >= 4 * k
+    assert shared_sample_plan([100, 100], 10) is None
+
+
+def test_results_mode_is_checked():
+    from rapidadb_b200.sharded import ShardedIVFSearch
+
+    with pytest.raises(ValueError, match="results"):
+        ShardedSearch(lambda q, k: (q, q), largest=False, results="everyone")
+    with pytest.raises(ValueError, match="results"):
+        ShardedIVFSearch(object(), largest=False, results="")
+
+
 def test_shard_range_partitions():
     for n in (0, 1, 7, 1000, 1001):
         for w in (1, 2, 3, 8):
