@@ -32,7 +32,6 @@ import argparse
 import json
 import os
 import statistics
-import subprocess
 import sys
 import threading
 import time
@@ -147,7 +146,7 @@ def gen_mixture(lo, hi, d, wl, seed, dtype, device, salt=0):
 class ClockSampler:
     """SM clock and clock-event (throttle) reasons sampled through NVML every
     5 ms during the timed region (read-only queries; no setting is changed).
-    Falls back to `nvidia-smi -lms` when NVML is unavailable."""
+    Without NVML the record says so ("nvml unavailable") and holds no samples."""
 
     REASONS = {0x4: "sw_power_cap", 0x8: "hw_slowdown", 0x20: "sw_thermal_slowdown",
                0x40: "hw_thermal_slowdown", 0x80: "hw_power_brake_slowdown"}

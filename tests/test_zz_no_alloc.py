@@ -12,7 +12,6 @@ named to be collected last and must pass alone or after the other tests.
 import ctypes
 import os
 
-import numpy as np
 import pytest
 import torch
 
