@@ -79,3 +79,22 @@ def test_dropin_surface():
     assert "index='flat'" in repr(db)
     assert IndexConfig().nlist == 4096 and Metric("dot_product") == Metric.DOT_PRODUCT
     assert rapidadb.RapidaDB is RapidaDB
+
+
+def test_reference_module_paths():
+    """Every module of the reference's python/rapidadb package imports under
+    its own name and resolves to this implementation."""
+    import rapidadb
+    from rapidadb.async_search import AsyncBatchSearcher
+    from rapidadb.config import IndexConfig, IndexType, Metric, Precision
+    from rapidadb.index import RapidaDB
+    from rapidadb.pinned_buffer import PinnedBuffer
+    from rapidadb.utils import compute_recall, cuda_timer, generate_random_vectors
+
+    from rapidadb_b200.pipeline import AsyncBatchSearcher as A, PinnedBuffer as P
+
+    assert RapidaDB is rapidadb.RapidaDB and IndexConfig is rapidadb.IndexConfig
+    assert AsyncBatchSearcher is A and PinnedBuffer is P
+    assert IndexType("ivf_pq") == IndexType.IVF_PQ and Precision("bf16") == Precision.BF16
+    assert Metric("cosine") == Metric.COSINE
+    assert callable(compute_recall) and callable(cuda_timer) and callable(generate_random_vectors)
