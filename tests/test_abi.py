@@ -98,3 +98,25 @@ def test_reference_module_paths():
     assert IndexType("ivf_pq") == IndexType.IVF_PQ and Precision("bf16") == Precision.BF16
     assert Metric("cosine") == Metric.COSINE
     assert callable(compute_recall) and callable(cuda_timer) and callable(generate_random_vectors)
+
+
+def test_ivf_argument_errors_reported():
+    """IVF entry points reject bad shapes before any device work."""
+    lib = ctypes.CDLL(LIB)
+    lib.rdb_last_error.restype = ctypes.c_char_p
+    i64, vp = ctypes.c_int64, ctypes.c_void_p
+    # rotated code layout only for the query-major code widths
+    lib.rdb_pq_scatter_codes.argtypes = [vp, i64, ctypes.c_int, vp, vp, ctypes.c_int, vp]
+    assert lib.rdb_pq_scatter_codes(None, 10, 7, None, None, 1, None) == 1
+    assert b"pq_m = 7" in lib.rdb_last_error()
+    assert lib.rdb_pq_scatter_codes(None, 0, 7, None, None, 0, None) == 0  # nothing to place
+    # IVF scans: k above 32, unknown metric
+    lib.rdb_ivf_flat_scan.argtypes = [ctypes.c_int, ctypes.c_int, vp, i64, i64, ctypes.c_int, vp, ctypes.c_int,
+                                      vp, i64, vp, vp, vp, ctypes.c_int, vp, ctypes.c_int, vp, vp, vp,
+                                      ctypes.c_size_t, vp]
+    rc = lib.rdb_ivf_flat_scan(1, 0, None, 4, 8, 8, None, 2, None, 8, None, None, None, 16, None, 33,
+                               None, None, None, 0, None)
+    assert rc == 1 and b"k in [1, 32]" in lib.rdb_last_error()
+    rc = lib.rdb_ivf_flat_scan(7, 0, None, 4, 8, 8, None, 2, None, 8, None, None, None, 16, None, 10,
+                               None, None, None, 0, None)
+    assert rc == 1 and b"unknown metric" in lib.rdb_last_error()
