@@ -33,7 +33,7 @@ extern "C" {
 #define RDB_ERR_CUDA 2        /* CUDA runtime / launch error                  */
 #define RDB_ERR_TIMEOUT 3     /* a kernel gave up on a bounded device wait    */
 #define RDB_ERR_UNSUPPORTED 4 /* valid request outside the supported range    */
-#define RDB_ERR_OVERFLOW 5    /* candidate buffer overflowed; retry exhaustive */
+#define RDB_ERR_OVERFLOW 5    /* reserved: overflows are repaired on the device */
 #define RDB_ERR_WORKSPACE 6   /* ws_bytes smaller than *_workspace() asked    */
 
 /* ---- metrics: order of rapidadb::Metric, csrc/include/rapidadb/core/types.h:17-21 */
@@ -48,6 +48,7 @@ extern "C" {
 
 /* ---- flat-search flags -------------------------------------------------- */
 #define RDB_SEARCH_EXHAUSTIVE 1 /* no sampled threshold: every row is a candidate */
+#define RDB_SEARCH_SYNC 2       /* wait for the call; RDB_ERR_TIMEOUT if a kernel gave up on a wait */
 
 /* Message of the last failed call on this thread ("" if none). */
 const char* rdb_last_error(void);
@@ -55,9 +56,23 @@ const char* rdb_last_error(void);
 int rdb_version(void);
 /* Reads (and with clear != 0 resets) the current device's status word, where
  * kernels record bounded waits that ran out (tensor-core scan: bit 0 producer,
- * 1 MMA issuer, 2 epilogue; bit 4 the TMA-fed CUDA-core scan).  Synchronises
- * the device. */
+ * 1 MMA issuer, 2 epilogue; bit 4 the TMA-fed CUDA-core scan; bit 5
+ * rdb_probe_bounded_wait).  Synchronises the device. */
 int rdb_device_status(unsigned* out_host, int clear);
+/* The status word as last forwarded by a completed rdb_flat_search on the
+ * current device, read from mapped host memory without synchronising (0: no
+ * kernel has reported a timeout).  Asynchronous error reporting in the manner
+ * of CUDA's own: a search returns before its kernels finish, and a timeout
+ * shows up here (and in rdb_device_status) once they have.  Cleared by
+ * rdb_device_status(.., 1).  No reference counterpart (the reference checks
+ * launch errors only, csrc/include/rapidadb/core/cuda_utils.h:12-30). */
+int rdb_pending_status(unsigned* out_host);
+/* Test hook of the bounded device waits (no reference counterpart): one
+ * thread waits on an mbarrier that nothing arrives at, through the same wait
+ * routine as the tensor-core scan's roles, for limit_ns (1 us .. 1 s); no TMA
+ * load or MMA is in flight.  The wait runs out, sets bit 5 of the status
+ * word, and the call (which synchronises `stream`) returns RDB_ERR_TIMEOUT. */
+int rdb_probe_bounded_wait(unsigned long long limit_ns, void* stream);
 
 /* Dense [nq, nx] score matrix with the reference formulas.
  * Replaces cosine_similarity_cuda / l2_distance_cuda / dot_product_cuda,
@@ -95,12 +110,20 @@ int rdb_topk(const float* dist, int64_t B, int64_t N, int k, int largest, float*
  *   ids [n] user ids or NULL for (row + id_offset).
  *   out_d [nq, k] scores (L2 ascending, cosine / dot descending), out_i ids.
  * fp16 / bf16 run on the tcgen05 tensor cores; fp32 on CUDA cores.
- * Synchronises `stream` once to read its overflow flag; returns
- * RDB_ERR_OVERFLOW if a query's candidates overflowed, in which case the
- * caller repeats the call with flags = RDB_SEARCH_EXHAUSTIVE (whose
- * workspace is sized by the same flag). */
+ * Returns without waiting for the device.  A query whose candidate list
+ * overflows its sampled-threshold capacity is rescanned exactly on the
+ * device within the same call (the answer never depends on the threshold).
+ * flags: RDB_SEARCH_EXHAUSTIVE (no sampled threshold; its own workspace
+ * size), RDB_SEARCH_SYNC (wait; report a device-wait timeout). */
 size_t rdb_flat_search_workspace(int metric, int dtype, int64_t nq, int64_t n, int d, int k,
                                  int flags);
+/* The plan rdb_flat_search follows for these sizes (16-byte aligned layouts;
+ * no reference counterpart, for tests and tuning): out[0] sampled rows (0: no
+ * sample pass), out[1] rows per group maximum of the tensor-core sample pass,
+ * out[2] row splits of the main pass, out[3] candidate capacity per (split,
+ * query), out[4] rows per split, out[5] 1 when the tensor cores run the scan,
+ * out[6] queries per chunk. */
+int rdb_flat_search_plan(int metric, int dtype, int64_t nq, int64_t n, int d, int k, int flags, int64_t* out);
 int rdb_flat_search(int metric, int dtype, const void* q, int64_t nq, int64_t ldq,
                     const void* x, int64_t n, int64_t ldx, const float* xv, int d, int k,
                     const int64_t* ids, int64_t id_offset, int flags, float* out_d,
@@ -125,7 +148,8 @@ int rdb_flat_search(int metric, int dtype, const void* q, int64_t nq, int64_t ld
  *                           (final-score units; must not be better than the
  *                           true k-th best) and `expect` candidates per query
  *                           expected over the n rows (sizes the candidate
- *                           lists); RDB_ERR_OVERFLOW as rdb_flat_search. */
+ *                           lists); overflowed queries are repaired as in
+ *                           rdb_flat_search. */
 size_t rdb_flat_sample_workspace(int64_t nq);
 int rdb_flat_sample_maxima(int metric, int dtype, const void* q, int64_t nq, int64_t ldq, const void* x, int64_t n,
                            int64_t ldx, const float* xv, int d, int64_t sample_rows, int group, float* out, void* ws,
@@ -148,6 +172,13 @@ int rdb_topk_merge(int largest, const float* in_v, const int64_t* in_i, int G, i
 int rdb_topk_merge_strided(int largest, const float* in_v, int64_t gstride_v, const int64_t* in_i,
                            int64_t gstride_i, int G, int64_t nq, int kin, int k, float* out_v, int64_t* out_i,
                            void* stream);
+/* Same with row strides: element (g, q, t) of the scores at in_v[g *
+ * gstride_v + q * ldv + t], of the ids at in_i[g * gstride_i + q * ldi + t]
+ * (ldv / ldi 0: kin), e.g. scores and ids interleaved by row in one packed
+ * exchange buffer. */
+int rdb_topk_merge_ld(int largest, const float* in_v, int64_t gstride_v, int64_t ldv, const int64_t* in_i,
+                      int64_t gstride_i, int64_t ldi, int G, int64_t nq, int kin, int k, float* out_v, int64_t* out_i,
+                      void* stream);
 
 /* ---- k-means --------------------------------------------------------- */
 
@@ -222,12 +253,16 @@ int rdb_ivf_flat_scan(int metric, int dtype, const void* q, int64_t nq, int64_t 
  * hosts that pool all device memory themselves, serving threads that must
  * not block in an allocator, or plug-ins whose host runtime forbids guest
  * allocations.  Returns RDB_ERR_UNSUPPORTED when rdb_ivf_scan_workspace(nq,
- * nprobe, nlist) exceeds the array.  Every GPU that loads the library holds
- * the array until exit; all calls on a device share it, so calls that
- * overlap on the GPU race -- serialise them.  The first call on each device
- * looks the array up with cudaGetSymbolAddress: make it before any stream
- * capture.  The call allocates nothing. */
+ * nprobe, nlist) exceeds the array.  Set-up: call rdb_noalloc_init() once per
+ * device (and per context the host makes current), with that device
+ * current, before the first scan and before any stream capture; it loads the
+ * library's device module, which is when the 8 MiB is allocated (CUDA loads
+ * modules lazily by default).  After it, a scan allocates nothing; without
+ * it the first scan in a context does the lookup and allocates.  The array
+ * stays allocated until the context ends; all calls on a device share it, so
+ * calls that overlap on the GPU race -- serialise them. */
 size_t rdb_noalloc_scratch_bytes(void);
+int rdb_noalloc_init(void);
 int rdb_ivf_flat_scan_noalloc(int metric, int dtype, const void* q, int64_t nq, int64_t ldq, int d,
                               const int64_t* probe, int nprobe, const void* rows, int64_t ldx, const float* xv,
                               const int64_t* list_off, const int64_t* list_end, int nlist, const int64_t* ids, int k,
@@ -291,10 +326,15 @@ int rdb_ivfpq_search(const float* q, int64_t nq, int64_t ldq, int d, const int64
  * with CUDA events recorded on their launching stream -- 1 the main scan of
  * rdb_flat_search, 2 the rdb_ivf_flat_scan list scan, 4 the rdb_ivfpq_scan
  * list scan or the rdb_ivfpq_search kernel, 8 the rdb_kmeans_assign scan, 16
- * the rdb_kmeans_update segment sums (0 turns timing off).  rdb_timing_read synchronises the recorded
- * events and returns the summed device time and the number of timed launches. */
+ * the rdb_kmeans_update segment sums, and the phases of rdb_flat_search: 32
+ * per-query values, 64 sample pass + threshold select, 128 candidate
+ * select, 256 overflow repair (0 turns timing off).  rdb_timing_read
+ * synchronises the recorded events and returns the summed device time and
+ * the number of timed launches; rdb_timing_read_tags does the same for the
+ * launches whose tag is in `mask`, without resetting. */
 int rdb_timing_enable(int mask);
 int rdb_timing_read(double* total_ms, int* launches, int reset);
+int rdb_timing_read_tags(int mask, double* total_ms, int* launches);
 
 /* Kernels this library has launched so far in the process, all devices and
  * threads (no reference counterpart): read it before and after a region. */

@@ -16,7 +16,7 @@
 #          oracle/ref_kmeans_launch.cu, which only launches the two kernels.
 # csrc/clustering/kmeans.cpp is excluded: its line 20 is not C++.
 set -euo pipefail
-REF_SRC=${REF_SRC:-/root/reference}
+REF_SRC=${REF_SRC:?set REF_SRC to the reference source tree (oracle/Makefile sets it)}
 HERE="$(cd "$(dirname "${BASH_SOURCE[0]}")" && pwd)"
 OUT="$HERE/_ref"
 B="$OUT/build"

@@ -69,7 +69,10 @@ def _p(a: np.ndarray, ptype):
 
 
 def max_threads() -> int:
-    return int(lib().orc_max_threads())
+    """Host threads this process may run on (its CPU affinity).  Not
+    omp_get_max_threads(), which follows OMP_NUM_THREADS (torchrun sets it to
+    1); every call here passes this count explicitly."""
+    return len(os.sched_getaffinity(0))
 
 
 def distance(metric: str, q: np.ndarray, x: np.ndarray, acc64: bool = True,

@@ -64,6 +64,10 @@ enum TimingTag : int {
     TIMING_PQ_SCAN = 4,        // rdb_ivfpq_scan list scan
     TIMING_KMEANS_ASSIGN = 8,  // rdb_kmeans_assign scan
     TIMING_KMEANS_UPDATE = 16, // rdb_kmeans_update segment sums
+    TIMING_FLAT_PREP = 32,     // rdb_flat_search per-query values
+    TIMING_FLAT_SAMPLE = 64,   // rdb_flat_search sample pass + threshold select
+    TIMING_FLAT_SELECT = 128,  // rdb_flat_search candidate select
+    TIMING_FLAT_REPAIR = 256,  // rdb_flat_search overflow repair (scan + select; idle launches when none)
 };
 int timing_begin(int tag, cudaStream_t s, cudaEvent_t* stop);
 
@@ -76,8 +80,19 @@ enum DeviceStatus : unsigned {
     DEV_TIMEOUT_EPILOGUE = 1u << 2,
     DEV_OVERFLOW = 1u << 3,
     DEV_TIMEOUT_SIMT = 1u << 4,  // TMA-fed CUDA-core scan
+    DEV_TIMEOUT_PROBE = 1u << 5,  // rdb_probe_bounded_wait
 };
 unsigned* device_status_word();  // per-device, zero-initialised
+// Per-device word in mapped pinned host memory (device address) that the
+// flat-search repair kernel copies a nonzero status word into, so the host
+// can see it without synchronising; status_mirror_host() is its host address.
+unsigned* status_mirror_device();
+volatile unsigned* status_mirror_host();
+// Test probe of the bounded mbarrier wait (flat_tc.cu).
+int launch_wait_probe(uint64_t limit_ns, unsigned* out_waited_out, cudaStream_t s);
+// Load kernels into the current context ahead of use (simt.cu, ivf.cu).
+int norms_preload();
+int ivf_flat_scan_preload();
 
 // ------------------------------------------------------- score algebra --
 //

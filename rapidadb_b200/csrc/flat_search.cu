@@ -16,15 +16,20 @@
 //   3. select        - per query: exact top-k of its candidates, sorted, ties to
 //                      the lower row, rows -> user ids; L2 winners are
 //                      re-scored as sum (q - x)^2.
-// A candidate list that overflows its capacity is reported (RDB_ERR_OVERFLOW)
-// and the caller repeats the search with RDB_SEARCH_EXHAUSTIVE (no sampled
-// threshold, capacity = rows per split, so nothing can overflow).
+//   4. repair        - a query whose candidate list overflowed its capacity
+//                      (adversarial data, e.g. many identical rows) is marked
+//                      by the select; the repair kernel rescans its splits
+//                      exactly and a second select answers it (repair.cu).
+//                      Both launches return at once when nothing overflowed.
+// Everything stays on the stream: the call returns without waiting for the
+// device (RDB_SEARCH_SYNC waits and reports a bounded-wait timeout).
 #include <math.h>
 
 #include <algorithm>
 #include <utility>
 #include <vector>
 
+#include "repair.cuh"
 #include "scan.cuh"
 #include "select.cuh"
 
@@ -52,7 +57,7 @@ struct FlatPlan {
     int64_t ngroups;  // sample rows / group
     PassPlan s, m;
     size_t ws_bytes;
-    size_t off_qv, off_thr, off_cand, off_counts, off_flag;
+    size_t off_qv, off_thr, off_cand, off_counts, off_flag, off_mark;
 };
 
 // target: (split x query-block) units to launch, about one per SM for the
@@ -138,15 +143,17 @@ FlatPlan make_plan(int metric, int dtype, int64_t nq, int64_t n, int d, int k, i
         P.ngroups = S / P.group;
     }
     P.m = plan_pass(n, 1, nq, P.qtile, P.rtile, target);
+    // capacities stay >= min(k, rows per split), so an overflowed list can be
+    // replaced by its split's exact top-k (repair.cu)
     if (P.given) {
         const int64_t expect = (int64_t)ceil((double)P.m.rps * (double)expect_given / (double)n);
-        P.m.cap = std::min<int64_t>(P.m.rps, std::max<int64_t>(1024, 8 * expect + 256));
+        P.m.cap = std::min<int64_t>(P.m.rps, std::max<int64_t>({1024, 8 * expect + 256, (int64_t)k}));
         P.expect = expect_given;
     }
     if (P.sample) {
         // expected candidates per split: rps * k / S; keep 8x headroom
         int64_t expect = (int64_t)ceil((double)P.m.rps * (double)k / (double)S);
-        P.m.cap = std::min<int64_t>(P.m.rps, std::max<int64_t>(1024, 8 * expect + 256));
+        P.m.cap = std::min<int64_t>(P.m.rps, std::max<int64_t>({1024, 8 * expect + 256, (int64_t)k}));
     }
     size_t cand_main = (size_t)P.m.nsplit * nq * P.m.cap * sizeof(uint2);
     size_t cand_samp = !P.sample ? 0
@@ -161,6 +168,8 @@ FlatPlan make_plan(int metric, int dtype, int64_t nq, int64_t n, int d, int k, i
     off = align_up(off + nq * sizeof(float), 256);
     P.off_thr = off;
     off = align_up(off + nq * sizeof(float), 256);
+    P.off_mark = off;
+    off = align_up(off + nq * sizeof(unsigned), 256);
     P.off_cand = off;
     off = align_up(off + std::max(cand_main, cand_samp), 256);
     P.off_counts = off;
@@ -185,19 +194,15 @@ int run_chunk(const FlatPlan& P, int metric, int dtype, const void* q, int64_t n
     uint2* cand = reinterpret_cast<uint2*>(ws + P.off_cand);
     int* counts = reinterpret_cast<int*>(ws + P.off_counts);
     unsigned* flag = reinterpret_cast<unsigned*>(ws + P.off_flag);
+    unsigned* mark = reinterpret_cast<unsigned*>(ws + P.off_mark);
     const int cos_small = d <= 128 ? 1 : 0;
     const bool largest = metric_largest(metric);
+    cudaEvent_t ev;
 
-    // per-query metric values (queries are strided: norms of each row)
-    if (ldq == d) {
-        RDB_TRY(rdb_row_sqnorms(dtype, q, nq, d, qv, s));
-    } else {
-        // strided queries: compute row by row via a contiguous view per row
-        for (int64_t i = 0; i < nq; ++i)
-            RDB_TRY(rdb_row_sqnorms(dtype, static_cast<const char*>(q) + i * ldq * elem_size(dtype),
-                                    1, d, qv + i, s));
-    }
-    RDB_TRY(rdb_vec_values(metric, d, qv, nq, qv, s));
+    // per-query metric values (any query stride); clears the overflow word
+    RDB_TRY(timing_begin(TIMING_FLAT_PREP, s, &ev));
+    RDB_TRY(launch_query_prep(metric, dtype, q, nq, ldq, d, qv, flag, s));
+    if (ev) RDB_CUDA_TRY(cudaEventRecord(ev, s));
 
     ScanArgs a = {};
     a.metric = metric;
@@ -236,6 +241,7 @@ int run_chunk(const FlatPlan& P, int metric, int dtype, const void* q, int64_t n
         return P.tc ? launch_scan_tc(sc, SCAN_FILTER, s) : launch_scan_simt(sc, SCAN_FILTER, s);
     };
 
+    RDB_TRY(timing_begin(TIMING_FLAT_SAMPLE, s, &ev));
     if (P.sample && P.tc) {
         // group maxima over the strided sample, then the k-th best of them
         ScanArgs sc = a;
@@ -302,6 +308,7 @@ int run_chunk(const FlatPlan& P, int metric, int dtype, const void* q, int64_t n
             RDB_TRY(launch_select(ss, s));
         }
     }
+    if (ev) RDB_CUDA_TRY(cudaEventRecord(ev, s));
     {
         ScanArgs sc = a;
         sc.n = n;
@@ -314,6 +321,7 @@ int run_chunk(const FlatPlan& P, int metric, int dtype, const void* q, int64_t n
         RDB_TRY(timing_begin(TIMING_FLAT_SCAN, s, &stop_ev));
         RDB_TRY(scan(sc));
         if (stop_ev) RDB_CUDA_TRY(cudaEventRecord(stop_ev, s));
+        RDB_TRY(timing_begin(TIMING_FLAT_SELECT, s, &ev));
         SelectArgs ss = sa;
         ss.output = SEL_OUT_TOPK;
         ss.cap = P.m.cap;
@@ -324,11 +332,49 @@ int run_chunk(const FlatPlan& P, int metric, int dtype, const void* q, int64_t n
         ss.ids = ids;
         ss.id_offset = id_offset;
         ss.overflow = flag;
+        ss.mark_q = mark;
         ss.rescore_margin = metric == RDB_METRIC_L2 ? 16 : 0;
         // candidates per query: ~1.1 n k / S under a sampled threshold
         // (group maxima loosen it slightly), every row without one
         ss.expect = P.given ? P.expect : P.sample ? (int64_t)(1.1 * (double)n * (double)k / (double)(P.s.rows)) + 1 : n;
         RDB_TRY(launch_select(ss, s));
+        if (ev) RDB_CUDA_TRY(cudaEventRecord(ev, s));
+
+        // overflowed queries: exact rescan of their splits, then their select
+        RDB_TRY(timing_begin(TIMING_FLAT_REPAIR, s, &ev));
+        RepairArgs ra = {};
+        ra.metric = metric;
+        ra.cos_small = cos_small;
+        ra.dtype = dtype;
+        ra.q = q;
+        ra.nq = nq;
+        ra.ldq = ldq;
+        ra.x = x;
+        ra.n = n;
+        ra.ldx = ldx;
+        ra.d = d;
+        ra.k = k;
+        ra.qv = qv;
+        ra.xv = xv;
+        ra.flag = flag;
+        ra.mark_q = mark;
+        ra.cand = cand;
+        ra.counts = counts;
+        ra.cap = P.m.cap;
+        ra.nsplit = P.m.nsplit;
+        ra.rows_per_split = P.m.rps;
+        ra.buf_keys = repair_buffer_keys(k, P.m.cap);
+        ra.status = device_status_word();
+        ra.status_mirror = status_mirror_device();
+        RDB_TRY(launch_flat_repair(ra, s));
+        SelectArgs rs = ss;
+        rs.overflow = nullptr;
+        rs.mark_q = nullptr;
+        rs.only_q = mark;
+        rs.gate = flag;
+        rs.force_cta = 1;
+        RDB_TRY(launch_select(rs, s));
+        if (ev) RDB_CUDA_TRY(cudaEventRecord(ev, s));
     }
     return RDB_OK;
 }
@@ -344,6 +390,20 @@ size_t rdb_flat_search_workspace(int metric, int dtype, int64_t nq, int64_t n, i
                                  int flags) {
     if (nq <= 0 || n <= 0 || d <= 0 || k <= 0) return 256;
     return make_plan(metric, dtype, nq, n, d, k, flags, true).ws_bytes;
+}
+
+int rdb_flat_search_plan(int metric, int dtype, int64_t nq, int64_t n, int d, int k, int flags, int64_t* out) {
+    RDB_CHECK_ARG(out != nullptr, "out is NULL");
+    RDB_CHECK_ARG(nq >= 1 && n >= 1 && d >= 1 && k >= 1 && k <= n, "bad shape");
+    const FlatPlan P = make_plan(metric, dtype, nq, n, d, k, flags, true);
+    out[0] = P.sample ? P.s.rows : 0;
+    out[1] = P.sample && P.tc ? P.group : 0;
+    out[2] = P.m.nsplit;
+    out[3] = P.m.cap;
+    out[4] = P.m.rps;
+    out[5] = P.tc ? 1 : 0;
+    out[6] = P.nq;
+    return RDB_OK;
 }
 
 }  // extern "C"
@@ -382,11 +442,6 @@ int flat_search_impl(int metric, int dtype, const void* q, int64_t nq, int64_t l
         return set_error(RDB_ERR_WORKSPACE, "workspace too small: %zu bytes, need %zu", ws_bytes,
                          P.ws_bytes);
     unsigned char* w = static_cast<unsigned char*>(ws);
-    // the overflow word sits at offset 0 of every chunk's plan: cleared once,
-    // or-ed by every chunk's select, read back with the device status word
-    // after the last chunk (one host synchronisation per call)
-    unsigned* flag = reinterpret_cast<unsigned*>(w);
-    RDB_CUDA_TRY(cudaMemsetAsync(flag, 0, sizeof(unsigned), s));
     const size_t es = elem_size(dtype);
     for (int64_t c0 = 0; c0 < nq; c0 += chunk) {
         int64_t cn = std::min(chunk, nq - c0);
@@ -395,17 +450,16 @@ int flat_search_impl(int metric, int dtype, const void* q, int64_t nq, int64_t l
                           x, n, ldx, xv, d, k, ids, id_offset, out_d + c0 * k, out_i + c0 * k, w,
                           s, thr_given ? thr_given + c0 : nullptr));
     }
-    unsigned* host = host_words();
-    if (!host) return set_error(RDB_ERR_CUDA, "cannot allocate pinned host words");
-    host[0] = host[1] = 0;
-    RDB_CUDA_TRY(cudaMemcpyAsync(&host[0], flag, sizeof(unsigned), cudaMemcpyDeviceToHost, s));
-    unsigned* st = device_status_word();
-    if (st) RDB_CUDA_TRY(cudaMemcpyAsync(&host[1], st, sizeof(unsigned), cudaMemcpyDeviceToHost, s));
-    RDB_CUDA_TRY(cudaStreamSynchronize(s));
-    const unsigned any_overflow = host[0], hs = host[1];
-    if (hs) return set_error(RDB_ERR_TIMEOUT, "a search kernel gave up on a device wait (status 0x%x)", hs);
-    if (any_overflow)
-        return set_error(RDB_ERR_OVERFLOW, "candidate list overflow; repeat with RDB_SEARCH_EXHAUSTIVE");
+    if (flags & RDB_SEARCH_SYNC) {
+        // wait for this call and report a bounded-wait timeout of its kernels
+        unsigned* host = host_words();
+        unsigned* st = device_status_word();
+        if (!host || !st) return set_error(RDB_ERR_CUDA, "cannot allocate the status words");
+        host[1] = 0;
+        RDB_CUDA_TRY(cudaMemcpyAsync(&host[1], st, sizeof(unsigned), cudaMemcpyDeviceToHost, s));
+        RDB_CUDA_TRY(cudaStreamSynchronize(s));
+        if (host[1]) return set_error(RDB_ERR_TIMEOUT, "a search kernel gave up on a device wait (status 0x%x)", host[1]);
+    }
     return RDB_OK;
 }
 
@@ -541,10 +595,19 @@ int rdb_topk_merge(int largest, const float* in_v, const int64_t* in_i, int G, i
 int rdb_topk_merge_strided(int largest, const float* in_v, int64_t gstride_v, const int64_t* in_i,
                            int64_t gstride_i, int G, int64_t nq, int kin, int k, float* out_v, int64_t* out_i,
                            void* stream) {
+    return rdb_topk_merge_ld(largest, in_v, gstride_v, 0, in_i, gstride_i, 0, G, nq, kin, k, out_v, out_i, stream);
+}
+
+int rdb_topk_merge_ld(int largest, const float* in_v, int64_t gstride_v, int64_t ldv, const int64_t* in_i,
+                      int64_t gstride_i, int64_t ldi, int G, int64_t nq, int kin, int k, float* out_v, int64_t* out_i,
+                      void* stream) {
     RDB_CHECK_ARG(G >= 1 && kin >= 1 && k >= 1, "bad shape");
     RDB_CHECK_ARG(k <= (int64_t)G * kin, "k must be <= G * kin");
-    RDB_CHECK_ARG(gstride_v == 0 || gstride_v >= nq * kin, "list stride of the scores below nq * kin");
-    RDB_CHECK_ARG(gstride_i == 0 || gstride_i >= nq * kin, "list stride of the ids below nq * kin");
+    RDB_CHECK_ARG(ldv == 0 || ldv >= kin, "row stride of the scores below kin");
+    RDB_CHECK_ARG(ldi == 0 || ldi >= kin, "row stride of the ids below kin");
+    const int64_t lv = ldv ? ldv : kin, li = ldi ? ldi : kin;
+    RDB_CHECK_ARG(gstride_v == 0 || gstride_v >= (nq - 1) * lv + kin, "list stride of the scores too small");
+    RDB_CHECK_ARG(gstride_i == 0 || gstride_i >= (nq - 1) * li + kin, "list stride of the ids too small");
     if (nq == 0) return RDB_OK;
     SelectArgs a = {};
     a.input = SEL_MERGE;
@@ -556,6 +619,8 @@ int rdb_topk_merge_strided(int largest, const float* in_v, int64_t gstride_v, co
     a.merge_i = in_i;
     a.gstride_v = gstride_v;
     a.gstride_i = gstride_i;
+    a.ldv = ldv;
+    a.ldi = ldi;
     a.G = G;
     a.kin = kin;
     a.out_v = out_v;

@@ -80,7 +80,8 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 
 // Bounded wait for the phase of `parity`; false when it gave up (time limit or
 // another role raised the abort flag).
-__device__ __noinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag) {
+__device__ __noinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
+                                       uint64_t limit_ns = kWaitLimitNs) {
     if (mbar_try_wait(bar, parity)) return true;
     const uint64_t t0 = globaltimer_ns();
     for (;;) {
@@ -88,7 +89,7 @@ __device__ __noinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile 
         for (int i = 0; i < 32; ++i)
             if (mbar_try_wait(bar, parity)) return true;
         if (*abort_flag) return false;
-        if (globaltimer_ns() - t0 > kWaitLimitNs) return false;
+        if (globaltimer_ns() - t0 > limit_ns) return false;
     }
 }
 
@@ -831,7 +832,34 @@ int launch_shape(const ScanArgs& a, int mode, cudaStream_t s) {
     return launch_mode<SCAN_DENSE, PAIR>(mq, mx, a, idesc, grid, s);
 }
 
+// Bounded-wait probe: one thread waits on an mbarrier of its own CTA that
+// no thread ever arrives at, through the same mbar_wait as the scan roles,
+// with a caller-given limit.  Nothing else is in flight (no TMA load, no
+// MMA), so giving up leaves nothing behind; the timeout is recorded in the
+// device status word exactly as a scan role records it.
+__global__ void wait_probe_kernel(uint64_t limit_ns, unsigned* status, unsigned* out_waited_out) {
+    __shared__ __align__(8) uint64_t bar;
+    __shared__ int abort_flag;
+    if (threadIdx.x == 0) {
+        mbar_init(&bar, 1);
+        abort_flag = 0;
+        fence_barrier_init();
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        const bool ok = mbar_wait(&bar, 0, &abort_flag, limit_ns);
+        if (!ok && status) atomicOr(status, (unsigned)DEV_TIMEOUT_PROBE);
+        *out_waited_out = ok ? 0u : 1u;
+    }
+}
+
 }  // namespace
+
+int launch_wait_probe(uint64_t limit_ns, unsigned* out_waited_out, cudaStream_t s) {
+    wait_probe_kernel<<<1, 32, 0, s>>>(limit_ns, device_status_word(), out_waited_out);
+    RDB_LAUNCH_CHECK();
+    return RDB_OK;
+}
 
 bool tc_use_pair(int64_t nq) { return nq > kTcQueries; }
 

@@ -192,4 +192,18 @@ PYBIND11_MODULE(_C, m) {
         check_status(rdb_device_status(&v, clear ? 1 : 0), "device status");
         return v;
     }, py::arg("clear") = true);
+    m.def("pending_status", []() {
+        unsigned v = 0;
+        check_status(rdb_pending_status(&v), "pending status");
+        return v;
+    });
+    // (status code, message) of the bounded-wait probe on the current stream
+    m.def("probe_bounded_wait", [](unsigned long long limit_ns) {
+        int st;
+        {
+            py::gil_scoped_release nogil;
+            st = rdb_probe_bounded_wait(limit_ns, stream_ptr());
+        }
+        return std::make_tuple(st, std::string(st == RDB_OK ? "" : rdb_last_error()));
+    }, py::arg("limit_ns") = 100000ull);
 }

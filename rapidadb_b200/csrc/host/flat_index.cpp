@@ -10,6 +10,7 @@
 #include <c10/cuda/CUDAGuard.h>
 
 #include <algorithm>
+#include <cstdio>
 
 #include "host.h"
 
@@ -40,6 +41,18 @@ at::ScalarType storage_type(Precision p) {
 }
 
 void* stream_ptr() { return static_cast<void*>(at::cuda::getCurrentCUDAStream().stream()); }
+
+void check_pending_status() {
+    unsigned v = 0;
+    check_status(rdb_pending_status(&v), "device status");
+    if (v != 0) {
+        char buf[32];
+        snprintf(buf, sizeof(buf), "0x%x", v);
+        TORCH_CHECK(false, "a search kernel on this device gave up on a bounded device wait (status ", buf,
+                    "); results of searches since then are not valid. Read and clear the status with "
+                    "device_status(True)");
+    }
+}
 
 int64_t padded_ld(int dim, at::ScalarType dtype) {
     int64_t per16 = 16 / static_cast<int64_t>(c10::elementSize(dtype));
@@ -121,22 +134,23 @@ Result topk_merge(const at::Tensor& vals, const at::Tensor& ids, int64_t k, bool
     TORCH_CHECK(vals.is_cuda() && ids.is_cuda(), "merge inputs must be CUDA tensors");
     TORCH_CHECK(vals.dim() == 3 && ids.sizes() == vals.sizes(), "merge inputs must be [G, Q, k]");
     c10::cuda::CUDAGuard guard(vals.device());
-    // each list [Q, k] must be dense; the lists themselves may be strided
-    // (per-rank blocks of a gather buffer are read in place)
-    auto dense_lists = [](const at::Tensor& t) {
-        return t.stride(2) == 1 && t.stride(1) == t.size(2) && t.stride(0) >= t.size(1) * t.size(2);
+    // rows of k entries must be dense; rows and lists may be strided (the
+    // per-rank blocks of a packed exchange buffer are read in place)
+    auto readable = [](const at::Tensor& t) {
+        return t.stride(2) == 1 && t.stride(1) >= t.size(2) &&
+               t.stride(0) >= (t.size(1) > 0 ? (t.size(1) - 1) * t.stride(1) + t.size(2) : 0);
     };
-    at::Tensor v = vals.scalar_type() == at::kFloat && dense_lists(vals) ? vals : vals.to(at::kFloat).contiguous();
-    at::Tensor i = ids.scalar_type() == at::kLong && dense_lists(ids) ? ids : ids.to(at::kLong).contiguous();
+    at::Tensor v = vals.scalar_type() == at::kFloat && readable(vals) ? vals : vals.to(at::kFloat).contiguous();
+    at::Tensor i = ids.scalar_type() == at::kLong && readable(ids) ? ids : ids.to(at::kLong).contiguous();
     const int64_t G = v.size(0), Q = v.size(1), kin = v.size(2);
     TORCH_CHECK(k >= 1 && k <= G * kin, "k must be in [1, G * k_in]");
     at::Tensor ov = at::empty({Q, k}, v.options().memory_format(at::MemoryFormat::Contiguous));
     at::Tensor oi = at::empty({Q, k}, i.options().memory_format(at::MemoryFormat::Contiguous));
     if (Q == 0) return {ov, oi};
-    check_status(rdb_topk_merge_strided(largest ? 1 : 0, v.data_ptr<float>(), v.stride(0), i.data_ptr<int64_t>(),
-                                        i.stride(0), static_cast<int>(G), Q, static_cast<int>(kin),
-                                        static_cast<int>(k), ov.data_ptr<float>(), oi.data_ptr<int64_t>(),
-                                        stream_ptr()),
+    check_status(rdb_topk_merge_ld(largest ? 1 : 0, v.data_ptr<float>(), v.stride(0), v.stride(1),
+                                   i.data_ptr<int64_t>(), i.stride(0), i.stride(1), static_cast<int>(G), Q,
+                                   static_cast<int>(kin), static_cast<int>(k), ov.data_ptr<float>(),
+                                   oi.data_ptr<int64_t>(), stream_ptr()),
                  "topk merge");
     return {ov, oi};
 }
@@ -218,23 +232,18 @@ static Result search_impl(Metric metric, const at::Tensor& rows, int dim, const 
     at::Tensor out_i = at::empty({nq, k}, rows.options().dtype(at::kLong));
     if (nq == 0) return {out_d, out_i};
     const int m = static_cast<int>(metric);
+    check_pending_status();
+    // scratch from torch's stream-ordered caching allocator: a pool hit, no
+    // device allocation once warm, and safe for concurrent searches on
+    // different streams (a per-index cached buffer would not be)
     size_t ws_bytes = rdb_flat_search_workspace(m, dt, nq, n, dim, static_cast<int>(k), 0);
     at::Tensor ws = at::empty({static_cast<int64_t>(ws_bytes)}, rows.options().dtype(at::kByte));
     const int64_t* idp = ids.defined() ? ids.data_ptr<int64_t>() : nullptr;
     const float* xvp = xv.defined() ? xv.data_ptr<float>() : nullptr;
+    // no host synchronisation: overflowed candidate lists are repaired on the device
     int st = rdb_flat_search(m, dt, q.data_ptr(), nq, q.size(1), rows.data_ptr(), n, rows.size(1), xvp, dim,
                              static_cast<int>(k), idp, id_offset, 0, out_d.data_ptr<float>(),
                              out_i.data_ptr<int64_t>(), ws.data_ptr(), ws_bytes, stream_ptr());
-    if (st == RDB_ERR_OVERFLOW) {
-        // a candidate list overflowed its sampled-threshold capacity: repeat
-        // without the threshold, in query chunks that fit a bounded workspace
-        size_t need = rdb_flat_search_workspace(m, dt, nq, n, dim, static_cast<int>(k), RDB_SEARCH_EXHAUSTIVE);
-        size_t budget = std::min<size_t>(need, std::max<size_t>(ws_bytes, size_t(4) << 30));
-        ws = at::empty({static_cast<int64_t>(budget)}, rows.options().dtype(at::kByte));
-        st = rdb_flat_search(m, dt, q.data_ptr(), nq, q.size(1), rows.data_ptr(), n, rows.size(1), xvp, dim,
-                             static_cast<int>(k), idp, id_offset, RDB_SEARCH_EXHAUSTIVE, out_d.data_ptr<float>(),
-                             out_i.data_ptr<int64_t>(), ws.data_ptr(), budget, stream_ptr());
-    }
     check_status(st, "flat search");
     return {out_d, out_i};
 }
@@ -298,13 +307,13 @@ Result FlatIndex::search_threshold(const at::Tensor& queries, int64_t k, const a
     at::Tensor out_d = at::empty({nq, k}, q.options().dtype(at::kFloat));
     at::Tensor out_i = at::empty({nq, k}, q.options().dtype(at::kLong));
     if (nq == 0) return {out_d, out_i};
+    check_pending_status();
     size_t wsb = rdb_flat_search_thr_workspace(m, dt, nq, n_, dim_, static_cast<int>(k), expect);
     at::Tensor ws = at::empty({static_cast<int64_t>(wsb)}, q.options().dtype(at::kByte));
     int st = rdb_flat_search_thr(m, dt, q.data_ptr(), nq, ld_, storage_.data_ptr(), n_, ld_, xv_.data_ptr<float>(),
                                  dim_, static_cast<int>(k), ids_.data_ptr<int64_t>(), 0, thr.data_ptr<float>(), expect,
                                  out_d.data_ptr<float>(), out_i.data_ptr<int64_t>(), ws.data_ptr(), wsb,
                                  stream_ptr());
-    if (st == RDB_ERR_OVERFLOW) return search(queries, k);  // the plain search retries exhaustively if needed
     check_status(st, "flat search");
     return {out_d, out_i};
 }

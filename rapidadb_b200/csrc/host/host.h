@@ -27,6 +27,9 @@ void check_status(int status, const char* what);
 int dtype_code(at::ScalarType t);
 at::ScalarType storage_type(Precision p);
 void* stream_ptr();
+// Raises when a kernel on the current device reported a bounded-wait timeout
+// (rdb_pending_status: a non-blocking read of mapped host memory).
+void check_pending_status();
 
 // ---------------------------------------------------------------- raw ops --
 // csrc/kernels/distance.cu:471-610 (checks :475-481)

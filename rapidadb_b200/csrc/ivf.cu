@@ -530,12 +530,38 @@ void launch_ivf_flat(bool expand, dim3 grid, cudaStream_t s, int metric, int cos
                                                 ids, k, out_v, out_i);
 }
 
+bool g_ivf_flat_attr[64] = {false};
+
+// shared-memory opt-in of the list-scan kernels, once per device
+int ivf_flat_attrs() {
+    int dev = 0;
+    RDB_CUDA_TRY(cudaGetDevice(&dev));
+    if (dev >= 0 && dev < 64 && g_ivf_flat_attr[dev]) return RDB_OK;
+    const int bytes = (int)sizeof(IvfFlatSmem);
+    RDB_TRY(ivf_flat_smem_attr<float>(bytes));
+    RDB_TRY(ivf_flat_smem_attr<__half>(bytes));
+    RDB_TRY(ivf_flat_smem_attr<__nv_bfloat16>(bytes));
+    if (dev >= 0 && dev < 64) g_ivf_flat_attr[dev] = true;
+    return RDB_OK;
+}
+
 size_t pq_smem(int d, int M, int ksub) {
     return sizeof(float) * ((size_t)ksub * d + (size_t)M * ksub + ((d + 3) & ~3)) +
            sizeof(unsigned long long) * (PNW * kMaxIvfK + 1);
 }
 
 }  // namespace
+
+// Loads every kernel rdb_ivf_flat_scan can launch into the current context
+// and sets their attributes (CUDA loads kernels lazily, on first use).
+int ivf_flat_scan_preload() {
+    RDB_TRY(ivf_flat_attrs());
+    cudaFuncAttributes fa;
+    RDB_CUDA_TRY(cudaFuncGetAttributes(&fa, probe_to_labels_kernel));
+    RDB_TRY(label_sort_preload());
+    return norms_preload();
+}
+
 }  // namespace rdb
 
 using namespace rdb;
@@ -578,18 +604,7 @@ int rdb_ivf_flat_scan(int metric, int dtype, const void* q, int64_t nq, int64_t 
     const dim3 grid((unsigned)nlist, (unsigned)std::min<int64_t>(64, std::max<int64_t>(1, 4 * mean_chunks)));
     const int64_t* eperm = reinterpret_cast<const int64_t*>(base + w.off_perm);
     const int64_t* eseg = reinterpret_cast<const int64_t*>(base + w.off_seg);
-    {
-        static bool attr[64] = {false};
-        int dev = 0;
-        cudaGetDevice(&dev);
-        if (dev < 64 && !attr[dev]) {
-            const int bytes = (int)sizeof(IvfFlatSmem);
-            RDB_TRY(ivf_flat_smem_attr<float>(bytes));
-            RDB_TRY(ivf_flat_smem_attr<__half>(bytes));
-            RDB_TRY(ivf_flat_smem_attr<__nv_bfloat16>(bytes));
-            attr[dev] = true;
-        }
-    }
+    RDB_TRY(ivf_flat_attrs());
     cudaEvent_t stop_ev;
     RDB_TRY(timing_begin(TIMING_IVF_SCAN, s, &stop_ev));
     switch (dtype) {

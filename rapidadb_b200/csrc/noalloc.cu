@@ -6,23 +6,33 @@
 // a plug-in whose host runtime owns the CUDA context and forbids allocations
 // from guest code.  rdb_ivf_flat_scan needs a scratch workspace from its
 // caller; rdb_ivf_flat_scan_noalloc runs the same scan with its scratch taken
-// from a fixed array compiled into this library, so the call itself allocates
-// nothing.
+// from a fixed array compiled into this library, so after set-up
+// (rdb_noalloc_init) the call allocates nothing.
 //
 // Costs and rules:
-//   - every GPU that loads the library holds kNoAllocScratchBytes (8 MiB) of
-//     device memory for this array until the process exits;
+//   - every context that is set up (rdb_noalloc_init, or a first scan) holds
+//     kNoAllocScratchBytes (8 MiB) of device memory for this array until the
+//     context ends;
 //   - all calls on a device share the one array: calls that overlap on the
 //     GPU (on different streams, or from different host threads) race and
 //     corrupt each other's results -- serialise them;
-//   - the first call on each device looks up the array's device address with
-//     cudaGetSymbolAddress (with that device current); make that first call
-//     before any stream capture begins;
+//   - the array is device memory of this library's module, which the CUDA
+//     runtime loads into a context lazily (CUDA_MODULE_LOADING=LAZY is the
+//     default): rdb_noalloc_init() looks the array up with
+//     cudaGetSymbolAddress, which loads the module and so allocates the 8 MiB
+//     at set-up time, and loads the kernels the scan launches (each kernel is
+//     also loaded lazily, on first use).  Call it once per device and
+//     context, with that device current, before the first scan and before
+//     any stream capture.  A scan
+//     whose context has not been set up this way does the lookup itself, and
+//     that first call then allocates;
+//   - every call looks the address up again for the context current at the
+//     time (a cheap query once the module is loaded), so the address is never
+//     stale after cudaDeviceReset or in a context that the host made current
+//     itself;
 //   - the array keeps the previous call's contents, but nothing in it needs to
 //     start at zero: every scratch byte the scan reads is written earlier in
 //     the same call.
-#include <mutex>
-
 #include "common.cuh"
 
 namespace rdb {
@@ -32,22 +42,13 @@ constexpr size_t kNoAllocScratchBytes = size_t(8) << 20;
 
 static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
 
-void* g_scratch_addr[64] = {nullptr};
-std::mutex g_scratch_mu;
-
-// Device address of the scratch array on the current device (looked up once
-// per device).
+// Device address of the scratch array in the current context.  The host-side
+// name g_noalloc_scratch is only a stand-in for the symbol; the address that
+// kernels may use comes from cudaGetSymbolAddress.
 int scratch_address(void** out) {
-    int dev = 0;
-    RDB_CUDA_TRY(cudaGetDevice(&dev));
-    RDB_CHECK_ARG(dev >= 0 && dev < 64, "device ordinal %d out of range", dev);
-    std::lock_guard<std::mutex> lock(g_scratch_mu);
-    if (!g_scratch_addr[dev]) {
-        void* p = nullptr;
-        RDB_CUDA_TRY(cudaGetSymbolAddress(&p, g_noalloc_scratch));
-        g_scratch_addr[dev] = p;
-    }
-    *out = g_scratch_addr[dev];
+    void* p = nullptr;
+    RDB_CUDA_TRY(cudaGetSymbolAddress(&p, g_noalloc_scratch));
+    *out = p;
     return RDB_OK;
 }
 
@@ -59,6 +60,12 @@ using namespace rdb;
 extern "C" {
 
 size_t rdb_noalloc_scratch_bytes(void) { return kNoAllocScratchBytes; }
+
+int rdb_noalloc_init(void) {
+    void* p = nullptr;
+    RDB_TRY(scratch_address(&p));
+    return ivf_flat_scan_preload();
+}
 
 int rdb_ivf_flat_scan_noalloc(int metric, int dtype, const void* q, int64_t nq, int64_t ldq, int d,
                               const int64_t* probe, int nprobe, const void* rows, int64_t ldx, const float* xv,

@@ -50,6 +50,13 @@ __device__ __forceinline__ bool hi_eq(unsigned long long a, unsigned long long b
     return top >= 64 ? true : ((a >> top) == (b >> top));
 }
 
+// Id of element t of merge list g, query q.
+__device__ __forceinline__ int64_t merge_id(const SelectArgs& a, int g, int64_t q, int t) {
+    const int64_t ld = a.ldi ? a.ldi : a.kin;
+    const int64_t gs = a.gstride_i ? a.gstride_i : a.nq * ld;
+    return a.merge_i[(int64_t)g * gs + q * ld + t];
+}
+
 // Key of element t of segment seg of query q.
 __device__ __forceinline__ unsigned long long seg_key(const SelectArgs& a, int64_t q, int seg, int t,
                                                       float qv) {
@@ -62,8 +69,9 @@ __device__ __forceinline__ unsigned long long seg_key(const SelectArgs& a, int64
         float s = a.dense[q * a.dense_n + t];
         return ((unsigned long long)score_key(s, largest) << 32) | (uint32_t)t;
     } else {
-        const int64_t gs = a.gstride_v ? a.gstride_v : a.nq * a.kin;
-        float s = a.merge_v[(int64_t)seg * gs + q * a.kin + t];
+        const int64_t ld = a.ldv ? a.ldv : a.kin;
+        const int64_t gs = a.gstride_v ? a.gstride_v : a.nq * ld;
+        float s = a.merge_v[(int64_t)seg * gs + q * ld + t];
         return ((unsigned long long)score_key(s, largest) << 32) | (uint32_t)(seg * a.kin + t);
     }
 }
@@ -113,7 +121,9 @@ __global__ void __launch_bounds__(NT) select_kernel(SelectArgs a) {
     unsigned long long* sel = reinterpret_cast<unsigned long long*>(dsm);
     unsigned long long* cache = sel + sel_cap;
 
+    if (a.gate && *a.gate == 0) return;
     for (int64_t q = blockIdx.x; q < a.nq; q += gridDim.x) {
+        if (a.only_q && a.only_q[q] == 0) continue;  // uniform across the CTA
         // ---- segment offsets -------------------------------------------
         if (warp == 0) {
             int nseg = a.input == SEL_DENSE ? 1 : (a.input == SEL_MERGE ? a.G : a.nsplit);
@@ -136,6 +146,10 @@ __global__ void __launch_bounds__(NT) select_kernel(SelectArgs a) {
                 local += len;
             }
             if (ovf && a.overflow) atomicOr(a.overflow, 1u);
+            if (a.mark_q) {
+                const bool any_ovf = __any_sync(0xffffffffu, ovf);
+                if (lane == 0) a.mark_q[q] = any_ovf ? 1u : 0u;
+            }
             int incl = local;
             for (int o = 1; o < 32; o <<= 1) {
                 int v = __shfl_up_sync(0xffffffffu, incl, o);
@@ -322,7 +336,7 @@ __global__ void __launch_bounds__(NT) select_kernel(SelectArgs a) {
                         id = idx;
                     } else {
                         int g = idx / a.kin, t = idx % a.kin;
-                        id = a.merge_i[(int64_t)g * (a.gstride_i ? a.gstride_i : a.nq * a.kin) + q * a.kin + t];
+                        id = merge_id(a, g, q, t);
                     }
                 } else {
                     v = largest ? -INFINITY : INFINITY;
@@ -460,7 +474,9 @@ __global__ void __launch_bounds__(NT, 2) select_warp_kernel(SelectArgs a) {
     const int out_k_req = a.k + a.rescore_margin;
     const int nseg = a.input == SEL_DENSE ? 1 : (a.input == SEL_MERGE ? a.G : a.nsplit);
 
+    if (a.gate && *a.gate == 0) return;
     for (int64_t q = (int64_t)blockIdx.x * NWARP + warp; q < a.nq; q += (int64_t)gridDim.x * NWARP) {
+        if (a.only_q && a.only_q[q] == 0) continue;  // uniform across the warp
         // ---- segment offsets (two segments per lane at most)
         int len[2] = {0, 0};
         bool ovf = false;
@@ -479,7 +495,11 @@ __global__ void __launch_bounds__(NT, 2) select_warp_kernel(SelectArgs a) {
                 }
             }
         }
-        if (__any_sync(FULLM, ovf) && lane == 0 && a.overflow) atomicOr(a.overflow, 1u);
+        {
+            const bool any_ovf = __any_sync(FULLM, ovf);
+            if (any_ovf && lane == 0 && a.overflow) atomicOr(a.overflow, 1u);
+            if (a.mark_q && lane == 0) a.mark_q[q] = any_ovf ? 1u : 0u;
+        }
         int base = 0;
 #pragma unroll
         for (int h = 0; h < 2; ++h) {
@@ -638,7 +658,7 @@ __global__ void __launch_bounds__(NT, 2) select_warp_kernel(SelectArgs a) {
                     id = idx;
                 } else {
                     const int g = idx / a.kin, t = idx % a.kin;
-                    id = a.merge_i[(int64_t)g * (a.gstride_i ? a.gstride_i : a.nq * a.kin) + q * a.kin + t];
+                    id = merge_id(a, g, q, t);
                 }
                 a.out_v[q * a.k + rank] = v;
                 a.out_i[q * a.k + rank] = id;
@@ -685,7 +705,7 @@ int launch_select(const SelectArgs& a, cudaStream_t stream) {
     // fewer queries than SMs: a CTA per query spreads them over the GPU (the
     // warp kernel would occupy nq / 8 SMs)
     const bool many = a.nq >= num_sms();
-    if (out_k <= kWarpOut && nseg <= kWarpSeg && small && many) {
+    if (!a.force_cta && out_k <= kWarpOut && nseg <= kWarpSeg && small && many) {
         const int64_t blocks = (a.nq + NWARP - 1) / NWARP;
         static bool wattr[64] = {false};
         if (dev < 64 && !wattr[dev]) {
@@ -699,6 +719,7 @@ int launch_select(const SelectArgs& a, cudaStream_t stream) {
         return RDB_OK;
     }
     int64_t grid = a.nq < 65535 * 4 ? a.nq : 65535 * 4;
+    if (a.force_cta) grid = std::min<int64_t>(grid, num_sms());
     select_kernel<<<(unsigned)grid, NT, smem, stream>>>(a);
     RDB_LAUNCH_CHECK();
     return RDB_OK;

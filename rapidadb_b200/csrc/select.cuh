@@ -39,10 +39,12 @@ struct SelectArgs {
     int64_t dense_n;
 
     // SEL_MERGE
-    const float* merge_v;  // [G][nq][kin]; list g starts at merge_v + g * gstride_v
-    const int64_t* merge_i;  // same shape; list g starts at merge_i + g * gstride_i
-    int64_t gstride_v;       // 0: nq * kin
-    int64_t gstride_i;       // 0: nq * kin
+    const float* merge_v;  // [G][nq][kin]; element (g, q, t) at merge_v[g * gstride_v + q * ldv + t]
+    const int64_t* merge_i;  // same shape; element (g, q, t) at merge_i[g * gstride_i + q * ldi + t]
+    int64_t gstride_v;       // 0: nq * ldv
+    int64_t gstride_i;       // 0: nq * ldi
+    int64_t ldv;             // row (query) stride of the scores, 0: kin
+    int64_t ldi;             // row stride of the ids, 0: kin
     int G;
     int kin;
 
@@ -53,6 +55,10 @@ struct SelectArgs {
     const int64_t* ids;   // physical row -> user id (NULL: row + id_offset)
     int64_t id_offset;
     unsigned* overflow;   // set to 1 when any count exceeded cap
+    unsigned* mark_q;     // [nq] (SEL_CANDIDATES): 1 where the query's lists overflowed, else 0
+    const unsigned* only_q;  // [nq]: process only queries marked nonzero (NULL: all)
+    const unsigned* gate;    // nothing to do while *gate == 0 (NULL: always run)
+    int force_cta;           // one CTA per query (select_kernel), grid of at most one CTA per SM
     int64_t expect;       // expected elements per query (0: unknown); picks the kernel
 
     // exact L2 rescoring of the selected rows (SEL_CANDIDATES, metric L2)

@@ -517,6 +517,15 @@ int launch_typed(const ScanArgs& a, int mode, cudaStream_t s, dim3 grid) {
 
 bool simt_tma_ok(const ScanArgs& a, int mode) { return tma_scan_ok(a, mode); }
 
+int norms_preload() {
+    cudaFuncAttributes fa;
+    RDB_CUDA_TRY(cudaFuncGetAttributes(&fa, row_sqnorms_kernel<float>));
+    RDB_CUDA_TRY(cudaFuncGetAttributes(&fa, row_sqnorms_kernel<__half>));
+    RDB_CUDA_TRY(cudaFuncGetAttributes(&fa, row_sqnorms_kernel<__nv_bfloat16>));
+    RDB_CUDA_TRY(cudaFuncGetAttributes(&fa, vec_values_kernel));
+    return RDB_OK;
+}
+
 int launch_partial_finalize(const ScanArgs& a, cudaStream_t s) {
     const int64_t total = a.nq * a.n;
     if (total == 0) return RDB_OK;

@@ -141,6 +141,15 @@ SortWs sort_ws(int64_t n, int K) {
 
 size_t label_sort_workspace(int64_t n, int K) { return sort_ws(n, K).bytes; }
 
+int label_sort_preload() {
+    cudaFuncAttributes fa;
+    RDB_CUDA_TRY(cudaFuncGetAttributes(&fa, label_hist_kernel));
+    RDB_CUDA_TRY(cudaFuncGetAttributes(&fa, label_offsets_kernel));
+    RDB_CUDA_TRY(cudaFuncGetAttributes(&fa, seg_scan_kernel));
+    RDB_CUDA_TRY(cudaFuncGetAttributes(&fa, label_scatter_kernel));
+    return RDB_OK;
+}
+
 int label_sort(const int32_t* labels, int64_t n, int K, int64_t* seg_start, int64_t* perm, int64_t* counts,
                void* ws, size_t ws_bytes, cudaStream_t s) {
     RDB_CHECK_ARG(K >= 1 && K <= kMaxLabels, "label count must be in [1, %d]", kMaxLabels);

@@ -8,6 +8,8 @@ namespace rdb {
 constexpr int kMaxLabels = 16384;  // shared-memory histogram / cursor limit
 
 size_t label_sort_workspace(int64_t n, int K);
+// Loads this file's kernels into the current context (CUDA loads them lazily).
+int label_sort_preload();
 
 // perm[seg_start[c] .. seg_start[c + 1]) = the ids i with labels[i] == c, in
 // ascending i (stable); counts[c] = segment sizes (counts may be NULL).

@@ -29,49 +29,178 @@ def shard_range(n: int, rank: int, world: int) -> Tuple[int, int]:
     return lo, hi
 
 
+def pack_lists(local_d: torch.Tensor, local_i: torch.Tensor) -> torch.Tensor:
+    """[Q, k] fp32 scores and int64 ids -> one [Q, W] int32 block, W = 3k
+    rounded up to even: row q holds k score words, a pad word when k is odd
+    (keeping the ids 8-byte aligned), then the 2k words of the ids.  One
+    collective then carries both, and unpack_lists() reads them in place."""
+    Q, k = local_d.shape
+    parts = [local_d.contiguous().view(torch.int32)]
+    if k % 2:
+        parts.append(torch.zeros((Q, 1), dtype=torch.int32, device=local_d.device))
+    parts.append(local_i.contiguous().view(torch.int32))
+    return torch.cat(parts, dim=1)
+
+
+def unpack_lists(buf: torch.Tensor, k: int) -> Tuple[torch.Tensor, torch.Tensor]:
+    """[..., W] packed rows -> strided views: scores [..., k] fp32, ids [..., k] int64."""
+    off = k + (k % 2)
+    return buf[..., :k].view(torch.float32), buf[..., off:off + 2 * k].view(torch.int64)
+
+
 def gather_candidates(local_d: torch.Tensor, local_i: torch.Tensor,
                       group: Optional[dist.ProcessGroup] = None) -> Tuple[torch.Tensor, torch.Tensor]:
-    """All-gather [Q, k] fp32 scores and int64 ids from every rank with one
-    collective.  Rank r's block of the gather buffer is [Q k scores | Q k ids]
-    (32-bit words, the id block 8-byte aligned); the returned [G, Q, k] score
-    and id tensors are views of the blocks (no copies), which the merge reads
-    in place."""
+    """All-gather every rank's [Q, k] scores and ids with ONE collective of
+    packed rows (pack_lists); returns [G, Q, k] score and id views of the
+    receive buffer, which the merge reads in place."""
     world = dist.get_world_size(group)
     Q, k = local_d.shape
-    nv = Q * k + (Q * k) % 2  # score words, padded so the ids stay 8-byte aligned
-    words = nv + 2 * Q * k
-    send = torch.empty(words, dtype=torch.int32, device=local_d.device)
-    send[:Q * k].view(torch.float32).copy_(local_d.reshape(-1))
-    send[nv:].view(torch.int64).copy_(local_i.reshape(-1))
-    out = torch.empty((world, words), dtype=torch.int32, device=local_d.device)
-    dist.all_gather_into_tensor(out.view(-1), send, group=group)
-    vals = out[:, :Q * k].view(torch.float32).view(world, Q, k)
-    ids = out[:, nv:].view(torch.int64).view(world, Q, k)
-    return vals, ids
+    send = pack_lists(local_d, local_i)
+    out = torch.empty((world,) + tuple(send.shape), dtype=torch.int32, device=local_d.device)
+    dist.all_gather_into_tensor(out.view(-1), send.view(-1), group=group)
+    return unpack_lists(out, k)
 
 
 def exchange_owned(local_d: torch.Tensor, local_i: torch.Tensor,
                    group: Optional[dist.ProcessGroup] = None) -> Tuple[torch.Tensor, torch.Tensor]:
     """Owner exchange of [Q, k] lists: query slice r (shard_range(Q, r,
     world), contiguous rows) of every rank goes to rank r, which receives
-    [G, Q_r, k] scores and ids -- 1 / G of an all-gather's bytes, no packing
-    copies (one all-to-all for the scores, one for the ids)."""
+    [G, Q_r, k] scores and ids -- 1 / G of an all-gather's bytes, in ONE
+    all-to-all of packed rows (pack_lists), read in place by the merge."""
     world = dist.get_world_size(group)
     rank = dist.get_rank(group)
     Q, k = local_d.shape
-    sizes = [(b - a) * k for a, b in (shard_range(Q, r, world) for r in range(world))]
-    n_r = sizes[rank] // k if k else 0
-    vals = torch.empty(world * sizes[rank], dtype=local_d.dtype, device=local_d.device)
-    ids = torch.empty(world * sizes[rank], dtype=local_i.dtype, device=local_i.device)
-    dist.all_to_all_single(vals, local_d.contiguous().view(-1), [sizes[rank]] * world, sizes, group=group)
-    dist.all_to_all_single(ids, local_i.contiguous().view(-1), [sizes[rank]] * world, sizes, group=group)
-    return vals.view(world, n_r, k), ids.view(world, n_r, k)
+    send = pack_lists(local_d, local_i)
+    W = send.shape[1]
+    sizes = [(b - a) * W for a, b in (shard_range(Q, r, world) for r in range(world))]
+    n_r = sizes[rank] // W
+    recv = torch.empty((world, n_r, W), dtype=torch.int32, device=local_d.device)
+    dist.all_to_all_single(recv.view(-1), send.view(-1), [sizes[rank]] * world, sizes, group=group)
+    return unpack_lists(recv, k)
+
+
+class PhaseClock:
+    """CUDA events recorded on the current stream at the phase boundaries of
+    every search while ``enabled`` (CUDA queries only); ``summary()`` gives
+    the mean device time of each phase per search and clears the log."""
+
+    def __init__(self):
+        self.enabled = False
+        self._log = []
+        self._cur = None
+
+    def start(self, queries: torch.Tensor) -> None:
+        self._cur = None
+        if self.enabled and queries.is_cuda:
+            e = torch.cuda.Event(enable_timing=True)
+            e.record()
+            self._cur = [("start", e)]
+
+    def mark(self, name: str) -> None:
+        if self._cur is not None:
+            e = torch.cuda.Event(enable_timing=True)
+            e.record()
+            self._cur.append((name, e))
+
+    def end(self) -> None:
+        if self._cur is not None:
+            self._log.append(self._cur)
+        self._cur = None
+
+    def summary(self) -> dict:
+        tot, n = {}, len(self._log)
+        for marks in self._log:
+            marks[-1][1].synchronize()
+            for (_, a), (name, b) in zip(marks, marks[1:]):
+                tot[name] = tot.get(name, 0.0) + a.elapsed_time(b)
+        self._log = []
+        return {name: round(v / max(n, 1), 4) for name, v in tot.items()}
 
 
 def gpu_merge(vals: torch.Tensor, ids: torch.Tensor, k: int, largest: bool):
     from rapidadb_b200._lib import C
 
     return C().topk_merge(vals, ids, k, largest)
+
+
+def _rows_of(obj) -> Optional[int]:
+    """Stored rows of an index object (``size`` attribute or method), or None."""
+    s = getattr(obj, "size", None)
+    if s is None:
+        return None
+    return int(s() if callable(s) else s)
+
+
+def pad_results(d: torch.Tensor, i: torch.Tensor, k: int, largest: bool) -> Tuple[torch.Tensor, torch.Tensor]:
+    """[Q, k'] lists (k' <= k) padded to [Q, k] with the worst score (-inf
+    for cosine / dot, +inf for L2) and id -1, which a merge ranks last."""
+    Q, kk = d.shape
+    if kk == k:
+        return d, i
+    pd = torch.full((Q, k), -math.inf if largest else math.inf, dtype=d.dtype, device=d.device)
+    pi = torch.full((Q, k), -1, dtype=i.dtype, device=i.device)
+    pd[:, :kk] = d
+    pi[:, :kk] = i
+    return pd, pi
+
+
+class _ShardSizes:
+    """Shard sizes of every rank, gathered once (one all-gather of one int64
+    per rank, on every rank's first search) and checked against k before any
+    data collective, so a request that some shard cannot serve is answered
+    the same way on every rank instead of raising on one rank and leaving
+    the others blocked in a collective."""
+
+    def _init_sizes(self, local_size):
+        self._local_size = local_size
+        self._sizes = None
+
+    def _local_rows(self) -> Optional[int]:
+        ls = self._local_size
+        if ls is not None:
+            return int(ls() if callable(ls) else ls)
+        return _rows_of(self._size_source)
+
+    def refresh_sizes(self) -> None:
+        """Forget the cached shard sizes (call on every rank after adds or
+        resets); the next search gathers them again."""
+        self._sizes = None
+
+    def shard_sizes(self, device) -> Optional[list]:
+        """Every rank's stored rows (None when this rank's index does not
+        report a size); collective on the first call after refresh_sizes()."""
+        n_local = self._local_rows()
+        if n_local is None:
+            return None
+        if self._sizes is None:
+            world = dist.get_world_size(self.group)
+            t = torch.tensor([n_local], dtype=torch.long, device=device)
+            sizes = torch.empty(world, dtype=torch.long, device=device)
+            dist.all_gather_into_tensor(sizes, t, group=self.group)
+            self._sizes = sizes.tolist()
+        if self._sizes[dist.get_rank(self.group)] != n_local:
+            raise RuntimeError("shard size changed since the sizes were gathered: call refresh_sizes() on every rank")
+        return self._sizes
+
+    def _check_k(self, sizes, k: int) -> None:
+        if sizes is not None and not 1 <= k <= sum(sizes):
+            raise ValueError(f"k must be in [1, {sum(sizes)}] (rows stored over all shards)")
+
+    def _padded(self, search, sizes, k: int, empty_shape):
+        """search(k') on this rank's shard with k' = min(k, its rows), padded
+        to k; an empty shard returns only padding."""
+        if sizes is None:
+            return search(k)
+        n_local = sizes[dist.get_rank(self.group)]
+        if n_local >= k:
+            return search(k)
+        Q, dev = empty_shape
+        if n_local == 0:
+            d = torch.empty((Q, 0), dtype=torch.float32, device=dev)
+            i = torch.empty((Q, 0), dtype=torch.long, device=dev)
+        else:
+            d, i = search(n_local)
+        return pad_results(d, i, k, self.largest)
 
 
 def shared_sample_plan(sizes, k: int) -> Optional[Tuple[int, int, int]]:
@@ -98,7 +227,7 @@ def shared_sample_plan(sizes, k: int) -> Optional[Tuple[int, int, int]]:
     return per, g, world * per
 
 
-class ShardedSearch:
+class ShardedSearch(_ShardSizes):
     """Search one query batch against a row-sharded index.
 
     Args:
@@ -115,12 +244,21 @@ class ShardedSearch:
                       owned_range(Q) only (an all-to-all carrying 1 / G of
                       the bytes, and a merge of 1 / G of the queries), the
                       shared threshold likewise selected per slice.
+        local_size:   this rank's stored rows (int or callable); by default
+                      the index's ``size``.  With it, a shard holding fewer
+                      than k rows (or none) contributes a padded list, and k
+                      above the rows of all shards raises ValueError on every
+                      rank before any data collective.
     """
 
     def __init__(self, index, largest: bool, group: Optional[dist.ProcessGroup] = None,
-                 merge: Optional[Callable] = None, shared_threshold: bool = True, results: str = "replicated"):
+                 merge: Optional[Callable] = None, shared_threshold: bool = True, results: str = "replicated",
+                 local_size=None):
         if results not in ("replicated", "owner"):
             raise ValueError(f"results must be 'replicated' or 'owner', got {results!r}")
+        self._size_source = index
+        self._init_sizes(local_size)
+        self.clock = PhaseClock()
         self.search_fn = index if callable(index) and not hasattr(index, "search") else index.search
         self.largest = largest
         self.group = group
@@ -130,7 +268,6 @@ class ShardedSearch:
         # fp16 / bf16 rows can share one sampled threshold across the shards
         flat = getattr(index, "index", index)
         self.flat = flat if shared_threshold and hasattr(flat, "sample_maxima") and flat.tensor_core() else None
-        self._sizes = None
 
     def owned_range(self, Q: int) -> Tuple[int, int]:
         """Queries [lo, hi) of a Q-query batch whose answers this rank
@@ -139,12 +276,7 @@ class ShardedSearch:
             return 0, Q
         return shard_range(Q, dist.get_rank(self.group), dist.get_world_size(self.group))
 
-    def refresh_sizes(self) -> None:
-        """Forget the cached shard sizes (call on every rank after adds or
-        resets); the next search gathers them again."""
-        self._sizes = None
-
-    def _shared_threshold_search(self, queries: torch.Tensor, k: int):
+    def _shared_threshold_search(self, queries: torch.Tensor, k: int, sizes):
         """Shared-threshold protocol: every rank computes group maxima of a
         strided sample of its rows (1 / world of the single-GPU sample); the
         k-th best of all ranks' maxima of a query -- a lower bound on its
@@ -156,19 +288,14 @@ class ShardedSearch:
         data collective) when the shards are too small."""
         world = dist.get_world_size(self.group)
         dev = queries.device
-        if self._sizes is None:
-            # shard sizes, gathered once (refresh_sizes() after the index changes)
-            n_local = torch.tensor([self.flat.size()], dtype=torch.long, device=dev)
-            sizes = torch.empty(world, dtype=torch.long, device=dev)
-            dist.all_gather_into_tensor(sizes, n_local, group=self.group)
-            self._sizes = sizes.tolist()
-        if self._sizes[dist.get_rank(self.group)] != self.flat.size():
-            raise RuntimeError("shard size changed since the sizes were gathered: call refresh_sizes() on every rank")
-        plan = shared_sample_plan(self._sizes, k)
+        if sizes is None or min(sizes) < k:
+            return None
+        plan = shared_sample_plan(sizes, k)
         if plan is None:
             return None
         per, g, total = plan
         maxima = self.flat.sample_maxima(queries, per, g)  # [Q, per / g]
+        self.clock.mark("sample")
         Q, gl = maxima.shape
         from rapidadb_b200._lib import C
 
@@ -198,24 +325,36 @@ class ShardedSearch:
             dist.all_gather_into_tensor(allm, maxima.contiguous(), group=self.group)
             allm = allm.view(world, Q, gl).permute(1, 0, 2).reshape(Q, world * gl)
             thr = C().select_threshold(allm, k, self.largest)
+        self.clock.mark("threshold_exchange")
         expect = int(math.ceil(1.1 * self.flat.size() * k / total)) + 1
         return self.flat.search_threshold(queries, k, thr, expect)
 
     def search(self, queries: torch.Tensor, k: int) -> Tuple[torch.Tensor, torch.Tensor]:
         if not dist.is_initialized() or dist.get_world_size(self.group) == 1:
             return self.search_fn(queries, k)
+        sizes = self.shard_sizes(queries.device)
+        self._check_k(sizes, k)
+        self.clock.start(queries)
         out = None
         if self.flat is not None:
-            out = self._shared_threshold_search(queries, k)
-        local_d, local_i = out if out is not None else self.search_fn(queries, k)
+            out = self._shared_threshold_search(queries, k, sizes)
+        if out is None:
+            out = self._padded(lambda kk: self.search_fn(queries, kk), sizes, k,
+                               (queries.shape[0], queries.device))
+        local_d, local_i = out
+        self.clock.mark("scan")
         if self.results == "owner":
             vals, ids = exchange_owned(local_d, local_i, self.group)
         else:
             vals, ids = gather_candidates(local_d, local_i, self.group)
-        return self.merge(vals, ids, k, self.largest)
+        self.clock.mark("result_exchange")
+        res = self.merge(vals, ids, k, self.largest)
+        self.clock.mark("merge")
+        self.clock.end()
+        return res
 
 
-class ShardedIVFSearch:
+class ShardedIVFSearch(_ShardSizes):
     """Search a row-sharded IVF / IVF-PQ index (every rank holds the same
     trained quantizer and a slice of the rows).
 
@@ -225,12 +364,17 @@ class ShardedIVFSearch:
     Every rank then scans its rows of the probed lists for all queries
     (``index.search_probed``), and the per-rank [Q, k] lists are all-gathered
     and merged as in ShardedSearch (results="owner": each rank merges and
-    returns only its query slice, owned_range(Q), after an all-to-all)."""
+    returns only its query slice, owned_range(Q), after an all-to-all).
+    Shards with fewer than k rows contribute padded lists (``local_size`` as
+    in ShardedSearch)."""
 
     def __init__(self, index, largest: bool, group: Optional[dist.ProcessGroup] = None,
-                 merge: Optional[Callable] = None, results: str = "replicated"):
+                 merge: Optional[Callable] = None, results: str = "replicated", local_size=None):
         if results not in ("replicated", "owner"):
             raise ValueError(f"results must be 'replicated' or 'owner', got {results!r}")
+        self._size_source = index
+        self._init_sizes(local_size)
+        self.clock = PhaseClock()
         self.index = index
         self.largest = largest
         self.group = group
@@ -261,12 +405,22 @@ class ShardedIVFSearch:
         return out[:Q]
 
     def search(self, queries: torch.Tensor, k: int) -> Tuple[torch.Tensor, torch.Tensor]:
-        probe = self.probe(queries)
-        local_d, local_i = self.index.search_probed(queries, probe, k)
         if not dist.is_initialized() or dist.get_world_size(self.group) == 1:
-            return local_d, local_i
+            return self.index.search_probed(queries, self.probe(queries), k)
+        sizes = self.shard_sizes(queries.device)
+        self._check_k(sizes, k)
+        self.clock.start(queries)
+        probe = self.probe(queries)
+        self.clock.mark("probe")
+        local_d, local_i = self._padded(lambda kk: self.index.search_probed(queries, probe, kk), sizes, k,
+                                        (queries.shape[0], queries.device))
+        self.clock.mark("scan")
         if self.results == "owner":
             vals, ids = exchange_owned(local_d, local_i, self.group)
         else:
             vals, ids = gather_candidates(local_d, local_i, self.group)
-        return self.merge(vals, ids, k, self.largest)
+        self.clock.mark("result_exchange")
+        res = self.merge(vals, ids, k, self.largest)
+        self.clock.mark("merge")
+        self.clock.end()
+        return res

@@ -96,13 +96,15 @@ def test_flat_matches_reference_golden(device, case):
                       rtol=1e-5, atol=2e-5, name=name)
 
 
-def test_overflow_retry_duplicates(device):
+def test_overflow_repair_duplicates(device):
     """All rows identical: every score ties, the sampled threshold admits every
-    row, candidate lists overflow and the exhaustive retry must still return
+    row, candidate lists overflow and the on-device repair must still return
     the k lowest row ids (ties go to the lower row)."""
     import rapidadb._C as _C
 
-    N, d, k = 40000, 64, 20
+    N, d, k = 200000, 64, 20
+    cap, rps = _plan_cap("dot_product", "bf16", 3, N, d, k)
+    assert cap < rps  # every split's list overflows
     x = torch.ones(N, d, device=device, dtype=torch.bfloat16)
     idx = _C.FlatIndex(d, _C.Metric.DOT_PRODUCT, _C.Precision.BF16)
     idx.add(x)
@@ -117,5 +119,53 @@ def test_search_leaves_no_device_error(device):
     idx = _C.FlatIndex(64, _C.Metric.L2, _C.Precision.BF16)
     idx.add(torch.randn(9000, 64, device=device))
     idx.search(torch.randn(200, 64, device=device), 10)
+    torch.cuda.synchronize()
+    assert _C.device_status(True) == 0
+
+
+def _plan_cap(metric, dtype, nq, n, d, k):
+    import ctypes
+
+    lib = ctypes.CDLL(os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "rapidadb_b200",
+                                   "librdb_kernels.so"))
+    lib.rdb_flat_search_plan.argtypes = [ctypes.c_int, ctypes.c_int, ctypes.c_int64, ctypes.c_int64,
+                                         ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.POINTER(ctypes.c_int64)]
+    out = (ctypes.c_int64 * 7)()
+    code = {"fp32": 0, "fp16": 1, "bf16": 2}[dtype]
+    assert lib.rdb_flat_search_plan({"cosine": 0, "l2": 1, "dot_product": 2}[metric], code, nq, n, d, k, 0, out) == 0
+    return out[3], out[4]
+
+
+@pytest.mark.parametrize("dtype", ["fp32", "bf16"])
+@pytest.mark.parametrize("metric", ["l2", "cosine", "dot_product"])
+def test_overflow_repair_only_marked_queries(device, dtype, metric):
+    """A block of 6,000 identical rows equal to query 0: query 0's candidates
+    overflow their list capacity and are repaired on the device, while the
+    other queries (random) take the normal path in the same call.  Every
+    query must equal the exact search (the repaired one returns the lowest
+    rows of the tied block)."""
+    import rapidadb._C as _C
+
+    N, d, Q, k, lo, hi = 200000, 64, 40, 20, 70000, 76000
+    cap, rps = _plan_cap(metric, dtype, Q, N, d, k)
+    # the block covers at least one whole split, whose list overflows
+    assert cap < rps and hi - lo >= 2 * rps
+    g = np.random.default_rng(99)
+    x = g.standard_normal((N, d), dtype=np.float32)
+    v = (g.standard_normal(d).astype(np.float32) * 3.0)
+    x[lo:hi] = v
+    q = g.standard_normal((Q, d), dtype=np.float32)
+    q[0] = v
+    xt = torch.from_numpy(x).cuda().to(TORCH_DT[dtype])
+    qt = torch.from_numpy(q).cuda().to(TORCH_DT[dtype])
+    prec = {"fp32": _C.Precision.FP32, "bf16": _C.Precision.BF16}[dtype]
+    met = {"l2": _C.Metric.L2, "cosine": _C.Metric.COSINE, "dot_product": _C.Metric.DOT_PRODUCT}[metric]
+    idx = _C.FlatIndex(d, met, prec)
+    idx.add(xt)
+    dist, ind = idx.search(qt, k)
+    rd, ri = oracle.flat_search(metric, qt.float().cpu().numpy(), xt.float().cpu().numpy(), k)
+    assert_topk_match(rd, ri, dist.cpu().numpy(), ind.cpu().numpy(), rtol=RTOL[dtype], atol=1e-5,
+                      name=f"repair {metric}/{dtype}")
+    assert ind[0].cpu().tolist() == list(range(lo, lo + k))
     torch.cuda.synchronize()
     assert _C.device_status(True) == 0

@@ -145,7 +145,12 @@ class _OracleIVFShard:
         _, i = oracle.flat_search("l2", qt.numpy(), self.cent, self.nprobe)
         return torch.from_numpy(i)
 
+    def size(self):
+        return self.hi - self.lo
+
     def search_probed(self, qt, probe, k):
+        # the GPU index rejects k above its stored rows (ivf_index.cpp check_query)
+        assert 1 <= k <= self.size(), f"k={k} on a shard of {self.size()} rows"
         q = qt.numpy()
         out_d = np.full((len(q), k), np.inf, np.float32)
         out_i = np.full((len(q), k), -1, np.int64)
@@ -293,3 +298,66 @@ def test_sample_rows_deterministic_distinct():
     assert a != sample_rows(10_000, 500, 43)
     with pytest.raises(ValueError):
         sample_rows(5, 6, 0)
+
+
+# uneven shards: rank 0 holds fewer than k rows, rank 1 none, rank 2 the rest
+_UNEVEN = [(0, 6), (6, 6), (6, 3001)]
+
+
+def _uneven_flat(rank, world):
+    x, q = _data()
+    lo, hi = _UNEVEN[rank]
+
+    def local(qt, k):
+        assert 1 <= k <= hi - lo, f"k={k} on a shard of {hi - lo} rows"  # as FlatIndex::search checks
+        d, i = oracle.flat_search("l2", qt.numpy(), x[lo:hi], k, ids=np.arange(lo, hi, dtype=np.int64))
+        return torch.from_numpy(d), torch.from_numpy(i)
+
+    out = {}
+    for mode in ("replicated", "owner"):
+        s = ShardedSearch(local, largest=False, merge=_oracle_merge, results=mode, local_size=hi - lo)
+        d, i = s.search(torch.from_numpy(q), 10)
+        out[mode] = (s.owned_range(len(q)), d.numpy(), i.numpy())
+    try:
+        ShardedSearch(local, largest=False, merge=_oracle_merge, local_size=hi - lo).search(torch.from_numpy(q), 5000)
+        out["too_large"] = None
+    except ValueError as e:
+        out["too_large"] = str(e)
+    return out
+
+
+def test_short_and_empty_shards_pad_instead_of_hanging():
+    """A shard with fewer than k rows answers with a padded list, an empty
+    shard with padding only, and k above the rows of all shards raises
+    ValueError on every rank (before any data collective) -- no rank is left
+    waiting in a collective another rank never joins."""
+    out = _run(_uneven_flat, world=3)
+    x, q = _data()
+    rd, ri = oracle.flat_search("l2", q, x, 10)
+    for r in range(3):
+        for mode in ("replicated", "owner"):
+            (a, b), d, i = out[r][mode]
+            np.testing.assert_array_equal(i, ri[a:b])
+            np.testing.assert_allclose(d, rd[a:b], rtol=1e-6)
+        assert "k must be in [1, 3001]" in out[r]["too_large"]
+
+
+def _uneven_ivf(rank, world):
+    from rapidadb_b200.sharded import ShardedIVFSearch
+
+    x, q, cent, labels = _ivf_setup()
+    lo, hi = _UNEVEN[rank]
+    s = ShardedIVFSearch(_OracleIVFShard(x, labels, lo, hi, cent, 4), largest=False, merge=_oracle_merge)
+    d, i = s.search(torch.from_numpy(q), 10)
+    return d.numpy(), i.numpy()
+
+
+def test_sharded_ivf_short_and_empty_shards():
+    out = _run(_uneven_ivf, world=3)
+    x, q, cent, labels = _ivf_setup()
+    order = np.argsort(labels, kind="stable")
+    off = np.concatenate([[0], np.cumsum(np.bincount(labels, minlength=len(cent)))]).astype(np.int64)
+    rd, ri = oracle.ivf_flat_search("l2", q, cent, off, x[order], order.astype(np.int64), 4, 10)
+    for r in range(3):
+        np.testing.assert_array_equal(out[r][1], ri)
+        np.testing.assert_allclose(out[r][0], rd, rtol=1e-5)

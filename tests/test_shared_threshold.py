@@ -47,25 +47,27 @@ def test_shared_threshold_equals_single(device, metric, k, world):
 
 
 @pytest.mark.parametrize("largest", [True, False])
-def test_merge_reads_gather_blocks_in_place(device, largest):
-    """The merge reads per-rank lists straight out of a gather buffer laid out
-    like sharded.gather_candidates (scores block, then 8-byte aligned ids)."""
+@pytest.mark.parametrize("k", [13, 10])
+def test_merge_reads_packed_exchange_rows_in_place(device, largest, k):
+    """The merge reads per-rank lists straight out of a packed exchange
+    buffer (sharded.pack_lists: per row k score words, a pad word when k is
+    odd, 2k id words), through the row strides, without copies."""
     import oracle
     import rapidadb._C as _C
+    from rapidadb_b200.sharded import pack_lists, unpack_lists
 
     g = np.random.default_rng(3)
-    G, Q, k = 5, 77, 13  # odd Q * k: the id block needs the alignment pad
+    G, Q = 5, 77
     v = np.sort(g.standard_normal((G, Q, k)).astype(np.float32), axis=2)
     if largest:
         v = v[:, :, ::-1].copy()
     ids = g.permutation(G * Q * k).astype(np.int64).reshape(G, Q, k)
-    nv = Q * k + (Q * k) % 2
-    buf = torch.zeros((G, nv + 2 * Q * k), dtype=torch.int32, device="cuda")
-    buf[:, :Q * k].view(torch.float32).copy_(torch.from_numpy(v.reshape(G, -1)))
-    buf[:, nv:].view(torch.int64).copy_(torch.from_numpy(ids.reshape(G, -1)))
-    vals = buf[:, :Q * k].view(torch.float32).view(G, Q, k)
-    idv = buf[:, nv:].view(torch.int64).view(G, Q, k)
-    assert not vals.is_contiguous()
+    buf = torch.stack([pack_lists(torch.from_numpy(v[r]).cuda(), torch.from_numpy(ids[r]).cuda())
+                       for r in range(G)])
+    assert buf.shape == (G, Q, 3 * k + k % 2)
+    vals, idv = unpack_lists(buf, k)
+    assert not vals.is_contiguous() and not idv.is_contiguous()
+    assert vals.data_ptr() == buf.data_ptr()
     md, mi = _C.topk_merge(vals, idv, k, largest)
     rd, ri = oracle.topk_merge(v, ids, k, largest)
     np.testing.assert_array_equal(md.cpu().numpy(), rd)

@@ -6,8 +6,11 @@ that pool all device memory themselves, serving threads that must not block
 in an allocator, plug-ins whose host runtime forbids guest allocations): its
 scratch is a static array inside the library.  The two entry points run the
 same kernels, so their outputs must be identical; two calls in a row check
-that the second call does not see stale scratch from the first.  This file is
-named to be collected last and must pass alone or after the other tests.
+that the second call does not see stale scratch from the first.  After the
+set-up call rdb_noalloc_init() (which loads the array and the scan's kernels),
+a call changes neither the device's free memory nor torch's allocations.
+This file is named to be collected last and must pass alone or after the
+other tests.
 """
 import ctypes
 import os
@@ -28,6 +31,7 @@ def _lib():
     lib.rdb_ivf_scan_workspace.restype = ctypes.c_size_t
     lib.rdb_ivf_scan_workspace.argtypes = [_i64, ctypes.c_int, ctypes.c_int]
     lib.rdb_noalloc_scratch_bytes.restype = ctypes.c_size_t
+    lib.rdb_noalloc_init.restype = ctypes.c_int
     lib.rdb_last_error.restype = ctypes.c_char_p
     lib.rdb_ivf_flat_scan.argtypes = [ctypes.c_int, ctypes.c_int, _vp, _i64, _i64, ctypes.c_int, _vp, ctypes.c_int,
                                       _vp, _i64, _vp, _vp, _vp, ctypes.c_int, _vp, ctypes.c_int, _vp, _vp, _vp,
@@ -74,6 +78,7 @@ def _scan(lib, noalloc, q, probe, rows, list_off, ids, k, metric=1):
 
 def test_noalloc_scan_matches_workspace_scan_twice(device):
     lib = _lib()
+    assert lib.rdb_noalloc_init() == 0, lib.rdb_last_error()
     for call, (seed, metric) in enumerate([(1, 1), (2, 0)]):
         prob = _problem(seed, nq=300, nprobe=6, nlist=40, n=5000 + call * 777, d=48)
         ref_v, ref_i = _scan(lib, False, *prob, k=10, metric=metric)
@@ -95,3 +100,28 @@ def test_noalloc_rejects_oversized_requests(device):
                                        _vp(torch.cuda.current_stream().cuda_stream))
     assert rc == 4  # RDB_ERR_UNSUPPORTED, raised before any device work
     assert b"static array" in lib.rdb_last_error()
+
+
+def test_noalloc_call_allocates_nothing_after_init(device):
+    """Set up once, then the scan itself leaves the device's free memory and
+    torch's allocator untouched (inputs and outputs are allocated before)."""
+    lib = _lib()
+    assert lib.rdb_noalloc_init() == 0, lib.rdb_last_error()
+    q, probe, rows, list_off, ids = _problem(5, nq=200, nprobe=5, nlist=30, n=4000, d=32)
+    nq, d = q.shape
+    k, nprobe, nlist = 8, probe.shape[1], list_off.numel() - 1
+    out_v = torch.empty(nprobe, nq, k, device="cuda")
+    out_i = torch.empty(nprobe, nq, k, device="cuda", dtype=torch.long)
+    xv = (rows * rows).sum(1).contiguous()
+    stream = _vp(torch.cuda.current_stream().cuda_stream)
+    args = [1, 0, q.data_ptr(), nq, d, d, probe.data_ptr(), nprobe, rows.data_ptr(), d, xv.data_ptr(),
+            list_off.data_ptr(), None, nlist, ids.data_ptr(), k, out_v.data_ptr(), out_i.data_ptr(), stream]
+    torch.cuda.synchronize()
+    free0, _ = torch.cuda.mem_get_info()
+    alloc0 = torch.cuda.memory_allocated()
+    for _ in range(2):
+        assert lib.rdb_ivf_flat_scan_noalloc(*args) == 0, lib.rdb_last_error()
+    torch.cuda.synchronize()
+    free1, _ = torch.cuda.mem_get_info()
+    assert torch.cuda.memory_allocated() == alloc0
+    assert free1 == free0, f"free device memory changed by {free0 - free1} bytes"
