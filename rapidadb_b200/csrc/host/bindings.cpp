@@ -92,7 +92,42 @@ PYBIND11_MODULE(_C, m) {
         "Fused top-k search over caller-owned padded rows", py::arg("metric"), py::arg("rows"), py::arg("dim"),
         py::arg("row_values"), py::arg("queries"), py::arg("k"), py::arg("ids") = py::none(),
         py::arg("id_offset") = 0);
-    // ---- k-means primitives (rapidadb_b200.kmeans drives the Lloyd loop)
+    // ---- k-means: the Lloyd driver (kmeans_cuda, csrc/include/rapidadb/clustering/kmeans.h:9-24)
+    py::class_<KMeansResult>(m, "KMeansResult")
+        .def_readonly("centroids", &KMeansResult::centroids)
+        .def_readonly("labels", &KMeansResult::labels)
+        .def_readonly("inertia", &KMeansResult::inertia)
+        .def_readonly("iterations", &KMeansResult::iterations)
+        .def("__iter__",
+             [](const KMeansResult& r) {
+                 return py::iter(py::make_tuple(r.centroids, r.labels, r.inertia, r.iterations));
+             })
+        .def("__repr__", [](const KMeansResult& r) {
+            return "KMeansResult(k=" + std::to_string(r.centroids.size(0)) +
+                   ", iterations=" + std::to_string(r.iterations) + ")";
+        });
+    m.def(
+        "kmeans",
+        [](const at::Tensor& points, int64_t k, int64_t max_iters, double tol, int64_t seed, const py::object& init,
+           bool exact, const py::object& allreduce) {
+            Reducer red;
+            if (!allreduce.is_none()) {
+                // sharded training: the Python callback all-reduces in place
+                red = [allreduce](at::Tensor& a, at::Tensor& b) {
+                    py::gil_scoped_acquire gil;
+                    allreduce(a, b);
+                };
+            }
+            at::Tensor it = opt_tensor(init);
+            py::gil_scoped_release nogil;
+            return kmeans(points, k, max_iters, tol, seed, it, exact, red);
+        },
+        "Lloyd k-means: (centroids, labels, inertia, iterations)", py::arg("points"), py::arg("k"),
+        py::arg("max_iters") = 100, py::arg("tol") = 1e-4, py::arg("seed") = 42, py::arg("init") = py::none(),
+        py::arg("exact") = false, py::arg("allreduce") = py::none());
+    m.def("sample_rows", [](int64_t n, int64_t k, uint64_t seed) { return sample_rows(n, k, seed); },
+          "k distinct rows of [0, n) (Floyd over SplitMix64)", py::arg("n"), py::arg("k"), py::arg("seed"));
+    // ---- k-means primitives
     m.def("kmeans_assign", &kmeans_assign, "labels, squared distances", py::arg("points"), py::arg("centroids"),
           py::arg("exact") = false, py::call_guard<py::gil_scoped_release>());
     m.def("kmeans_update", &kmeans_update, "per-centroid sums and counts", py::arg("points"), py::arg("labels"),

@@ -1,6 +1,9 @@
 // Host-side k-means primitives and IVF indices (see ivf_index.cpp).
 #pragma once
 
+#include <functional>
+#include <vector>
+
 #include "host.h"
 
 namespace rdbh {
@@ -19,6 +22,22 @@ at::Tensor pq_row_terms(const at::Tensor& codes, const at::Tensor& labels, const
                         const at::Tensor& codebooks);
 at::Tensor pq_encode(const at::Tensor& x, const at::Tensor& labels, const at::Tensor& centroids,
                      const at::Tensor& codebooks);
+
+// k-means (kmeans.cpp): the shape of rapidadb::KMeansResult / kmeans_cuda,
+// csrc/include/rapidadb/clustering/kmeans.h:9-24
+struct KMeansResult {
+    at::Tensor centroids;  // [k, d] fp32
+    at::Tensor labels;     // [n] int32
+    at::Tensor inertia;    // scalar fp64: sum of squared distances (over all shards)
+    int64_t iterations;
+};
+// Applied to each iteration's (sums [k, d], counts [k]) before finalize, and
+// to ([1] inertia, [1] zero) at the end: sharded training all-reduces them.
+using Reducer = std::function<void(at::Tensor&, at::Tensor&)>;
+// k distinct indices of [0, n): Floyd's algorithm over a SplitMix64 stream
+std::vector<int64_t> sample_rows(int64_t n, int64_t k, uint64_t seed);
+KMeansResult kmeans(const at::Tensor& points, int64_t k, int64_t max_iters, double tol, int64_t seed,
+                    const at::Tensor& init, bool exact, const Reducer& reduce);
 
 class IVFBase {
   public:

@@ -14,6 +14,8 @@ in and out, as in the reference (index.py:24-140).  Differences:
   the stored arrays in stored order -- rows or PQ codes, list labels, ids,
   centroids, codebooks -- so a loaded index answers exactly like the saved
   one without retraining or re-encoding.
+* ``IndexConfig(devices=[0, 1, ...])`` row-shards the index over those GPUs
+  of this process (rapidadb_b200.multi_device).
 """
 from __future__ import annotations
 
@@ -78,6 +80,15 @@ class RapidaDB:
         self._index = self._build_index()
 
     def _build_index(self):
+        cfg = self._config
+        if cfg.devices:
+            from rapidadb_b200.multi_device import MultiDeviceIndex
+
+            return MultiDeviceIndex(lambda dev: self._build_single(), list(cfg.devices),
+                                    largest=cfg.metric != Metric.L2)
+        return self._build_single()
+
+    def _build_single(self):
         _C = C()
         cfg = self._config
         if cfg.index_type == IndexType.FLAT:
@@ -103,7 +114,7 @@ class RapidaDB:
         from rapidadb_b200.kmeans import kmeans, train_pq
         from rapidadb_b200.utils import sample_rows
 
-        x = _as_float_cuda(vectors)
+        x = self._to_device(vectors)
         if 0 < cfg.train_sample < x.shape[0]:
             idx = torch.tensor(sorted(sample_rows(x.shape[0], cfg.train_sample, cfg.seed)),
                                dtype=torch.long, device=x.device)
@@ -121,9 +132,9 @@ class RapidaDB:
         """Install trained IVF centroids [nlist, dim] (and IVF-PQ codebooks
         [pq_m, pq_k, dim / pq_m]) directly."""
         if codebooks is None:
-            self._index.set_quantizer(centroids.cuda().float())
+            self._index.set_quantizer(self._to_device(centroids).float())
         else:
-            self._index.set_quantizer(centroids.cuda().float(), codebooks.cuda().float())
+            self._index.set_quantizer(self._to_device(centroids).float(), self._to_device(codebooks).float())
 
     @property
     def is_trained(self) -> bool:
@@ -133,11 +144,9 @@ class RapidaDB:
     def add(self, vectors: torch.Tensor, ids: Optional[torch.Tensor] = None) -> None:
         """Add [n, dim] vectors (moved to CUDA if needed) with optional int64 ids
         (index.py:71-92)."""
-        vectors = _as_float_cuda(vectors)
+        vectors = self._to_device(vectors)
         if ids is not None:
-            if not ids.is_cuda:
-                ids = ids.cuda()
-            ids = ids.contiguous().long()
+            ids = ids.to(vectors.device).contiguous().long()
             self._index.add(vectors, ids)
         else:
             self._index.add(vectors)
@@ -145,8 +154,16 @@ class RapidaDB:
     def search(self, queries: torch.Tensor, k: int = 10) -> Tuple[torch.Tensor, torch.Tensor]:
         """k nearest neighbours of each query -> (distances [B, k] fp32,
         indices [B, k] int64), best first (index.py:94-112)."""
-        queries = _as_float_cuda(queries)
+        queries = self._to_device(queries)
         return self._index.search(queries, k)
+
+    def _to_device(self, t: torch.Tensor) -> torch.Tensor:
+        """Float CUDA tensor on the index's (first) device."""
+        if self._config.devices:
+            dev = torch.device("cuda", int(self._config.devices[0]))
+            if t.device != dev:
+                t = t.to(dev)
+        return _as_float_cuda(t)
 
     def reset(self) -> None:
         """Remove all vectors (index.py:114-116)."""
@@ -181,29 +198,17 @@ class RapidaDB:
     FORMAT_VERSION = 1
 
     def state_dict(self) -> dict:
-        """Configuration and stored arrays (host tensors) of this index."""
+        """Configuration and stored arrays (host tensors) of this index; a
+        multi-device index stores each shard's arrays."""
         cfg = {f.name: (getattr(self._config, f.name).value
                         if hasattr(getattr(self._config, f.name), "value") else getattr(self._config, f.name))
                for f in dataclasses.fields(self._config)}
         st = {"format": self.FORMAT, "version": self.FORMAT_VERSION, "config": cfg, "size": self.size}
-        ix = self._index
         it = self._config.index_type
-        if it == IndexType.FLAT:
-            if self.size:
-                st["vectors"] = ix.vectors().cpu()
-                st["ids"] = ix.ids().cpu()
+        if self._config.devices:
+            st["shards"] = [_index_state(s, it) for s in self._index.shards]
         else:
-            if ix.is_trained():
-                st["centroids"] = ix.centroids().cpu()
-                if it == IndexType.IVF_PQ:
-                    st["codebooks"] = ix.codebooks().cpu()
-            if self.size:
-                st["labels"] = ix.stored_labels().cpu()
-                st["ids"] = ix.stored_ids().cpu()
-                if it == IndexType.IVF:
-                    st["vectors"] = ix.stored_vectors().cpu()
-                else:
-                    st["codes"] = ix.stored_codes().cpu()
+            st.update(_index_state(self._index, it))
         return st
 
     def save(self, path) -> None:
@@ -220,22 +225,15 @@ class RapidaDB:
         c["index_type"] = IndexType(c["index_type"])
         c["precision"] = Precision(c["precision"])
         db = cls(config=IndexConfig(**c))
-        dev = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
-        ix = db._index
         it = db._config.index_type
-        with torch.cuda.device(dev):
-            if it == IndexType.FLAT:
-                if st.get("size", 0):
-                    ix.add(st["vectors"].to(dev), st["ids"].to(dev))
-            else:
-                if "centroids" in st:
-                    if it == IndexType.IVF_PQ:
-                        ix.set_quantizer(st["centroids"].to(dev), st["codebooks"].to(dev))
-                    else:
-                        ix.set_quantizer(st["centroids"].to(dev))
-                if st.get("size", 0):
-                    data = st["vectors"] if it == IndexType.IVF else st["codes"]
-                    ix.restore(data.to(dev), st["labels"].to(dev), st["ids"].to(dev))
+        if db._config.devices:
+            if len(st.get("shards", [])) != len(db._index.shards):
+                raise ValueError("shard count in the file does not match config.devices")
+            for dev, shard, sst in zip(db._index.devices, db._index.shards, st["shards"]):
+                _restore_index(shard, sst, it, dev)
+        else:
+            dev = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
+            _restore_index(db._index, st, it, dev)
         return db
 
     @classmethod
@@ -247,3 +245,42 @@ class RapidaDB:
     def __repr__(self) -> str:
         return (f"RapidaDB(dim={self.dim}, metric='{self.metric}', "
                 f"index='{self._config.index_type.value}', size={self.size})")
+
+
+def _index_state(ix, it: IndexType) -> dict:
+    """Stored arrays of one extension index, in stored (list) order."""
+    st = {}
+    if it == IndexType.FLAT:
+        if ix.size():
+            st["vectors"] = ix.vectors().cpu()
+            st["ids"] = ix.ids().cpu()
+        return st
+    if ix.is_trained():
+        st["centroids"] = ix.centroids().cpu()
+        if it == IndexType.IVF_PQ:
+            st["codebooks"] = ix.codebooks().cpu()
+    if ix.size():
+        st["labels"] = ix.stored_labels().cpu()
+        st["ids"] = ix.stored_ids().cpu()
+        if it == IndexType.IVF:
+            st["vectors"] = ix.stored_vectors().cpu()
+        else:
+            st["codes"] = ix.stored_codes().cpu()
+    return st
+
+
+def _restore_index(ix, st: dict, it: IndexType, dev: torch.device) -> None:
+    """Load arrays written by _index_state into an empty extension index on dev."""
+    with torch.cuda.device(dev):
+        if it == IndexType.FLAT:
+            if "vectors" in st:
+                ix.add(st["vectors"].to(dev), st["ids"].to(dev))
+            return
+        if "centroids" in st:
+            if it == IndexType.IVF_PQ:
+                ix.set_quantizer(st["centroids"].to(dev), st["codebooks"].to(dev))
+            else:
+                ix.set_quantizer(st["centroids"].to(dev))
+        if "ids" in st:
+            data = st["vectors"] if it == IndexType.IVF else st["codes"]
+            ix.restore(data.to(dev), st["labels"].to(dev), st["ids"].to(dev))

@@ -3,7 +3,9 @@
 The reference declares ``kmeans_cuda(points, k, max_iters=100, tol=1e-4,
 seed=42) -> KMeansResult{centroids, labels, inertia, iterations}``
 (csrc/include/rapidadb/clustering/kmeans.h:9-24) but never implements it.
-Here each iteration is
+The Lloyd driver is the C++ host layer's ``_C.kmeans`` (csrc/host/kmeans.cpp);
+``kmeans()`` here calls it, adding the process-group all-reduce of centroid
+sums and counts for sharded rows.  Each iteration is
 
     assign    labels, squared distances   (fused GEMM + argmin kernel)
     update    per-centroid sums, counts   (atomic-free segmented reduction)
@@ -96,8 +98,22 @@ def kmeans(x: torch.Tensor, k: int, max_iters: int = 100, tol: float = 1e-4, see
     """Lloyd's algorithm; ``x`` is this rank's [n, d] rows (fp32 / fp16 / bf16).
 
     fp16 / bf16 rows are assigned on the tensor cores; ``exact_assign`` uses
-    the reference's sequential-FMA distance instead (fp32)."""
-    ops = ops or GpuOps(exact_assign)
+    the reference's sequential-FMA distance instead (fp32).  Runs the C++
+    driver (_C.kmeans); ``ops`` (assign / update / finalize callables, e.g.
+    the CPU oracle in tests) runs the same loop here instead."""
+    if ops is None:
+        from rapidadb_b200._lib import C
+
+        sharded = _world(group) > 1
+        if init is None and sharded:
+            init = init_centroids(x, k, seed, group)
+
+        def allreduce(a, b):
+            _allreduce(a, group)
+            _allreduce(b, group)
+
+        r = C().kmeans(x, k, max_iters, tol, seed, init, exact_assign, allreduce if sharded else None)
+        return KMeansResult(r.centroids, r.labels, float(r.inertia.item()), int(r.iterations))
     cent = init.float().contiguous() if init is not None else init_centroids(x, k, seed, group)
     it = 0
     for it in range(1, max_iters + 1):

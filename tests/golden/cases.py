@@ -40,6 +40,10 @@ FLAT_CASES = [
 # k-means single Lloyd step from the first K rows: (case, N, d, K, seed)
 KMEANS_CASES = [("D1", 3000, 32, 16, 7), ("D2", 2000, 128, 64, 8)]
 
+# k-means, several Lloyd iterations from the first K rows, then one more
+# assignment with the final centroids: (case, N, d, K, seed, iterations)
+LLOYD_CASES = [("E1", 4000, 64, 32, 21, 5), ("E2", 3000, 128, 48, 22, 5)]
+
 
 def flat_inputs(seed: int, N: int, Q: int, d: int):
     x = randn(seed, N, d)

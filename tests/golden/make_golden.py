@@ -88,6 +88,31 @@ def main(out_dir: str) -> None:
         out[f"{name}_centroids"] = newc.cpu().numpy()
         out[f"{name}_counts"] = counts.cpu().numpy()
 
+    for name, N, d, K, seed, iters in cases.LLOYD_CASES:
+        # the reference's assign and update kernels iterated (its Lloyd
+        # driver, kmeans_cuda, is declared but never defined)
+        x, c0 = cases.kmeans_inputs(seed, N, d, K)
+        xt = torch.from_numpy(x).to(dev)
+        ct = torch.from_numpy(c0).to(dev)
+        lab = torch.empty(N, dtype=torch.int32, device=dev)
+        dist = torch.empty(N, dtype=torch.float32, device=dev)
+        counts = torch.empty(K, dtype=torch.int32, device=dev)
+        for _ in range(iters):
+            assert km.ref_kmeans_assign(ctypes.c_void_p(xt.data_ptr()), ctypes.c_void_p(ct.data_ptr()),
+                                        ctypes.c_void_p(lab.data_ptr()), ctypes.c_void_p(dist.data_ptr()),
+                                        N, K, d) == 0
+            newc = ct.clone()
+            assert km.ref_kmeans_update(ctypes.c_void_p(xt.data_ptr()), ctypes.c_void_p(lab.data_ptr()),
+                                        ctypes.c_void_p(newc.data_ptr()), ctypes.c_void_p(counts.data_ptr()),
+                                        N, K, d) == 0
+            ct = newc
+        assert km.ref_kmeans_assign(ctypes.c_void_p(xt.data_ptr()), ctypes.c_void_p(ct.data_ptr()),
+                                    ctypes.c_void_p(lab.data_ptr()), ctypes.c_void_p(dist.data_ptr()),
+                                    N, K, d) == 0
+        out[f"{name}_centroids"] = ct.cpu().numpy()
+        out[f"{name}_labels"] = lab.cpu().numpy()
+        out[f"{name}_dist"] = dist.cpu().numpy()
+
     os.makedirs(out_dir, exist_ok=True)
     path = os.path.join(out_dir, "ref_golden.npz")
     np.savez_compressed(path, **out)

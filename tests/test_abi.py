@@ -120,3 +120,15 @@ def test_ivf_argument_errors_reported():
     rc = lib.rdb_ivf_flat_scan(7, 0, None, 4, 8, 8, None, 2, None, 8, None, None, None, 16, None, 10,
                                None, None, None, 0, None)
     assert rc == 1 and b"unknown metric" in lib.rdb_last_error()
+
+
+def test_kmeans_init_rows_match_python_sampler():
+    """_C.kmeans draws its initial rows with the same Floyd / SplitMix64
+    sampler as rapidadb_b200.utils.sample_rows (host code, no GPU)."""
+    import rapidadb._C as _C
+    from rapidadb_b200.utils import sample_rows
+
+    for n, k, seed in ((10, 10, 1), (1000, 37, 42), (5, 0, 3), (100000, 4096, 7)):
+        assert list(_C.sample_rows(n, k, seed)) == sample_rows(n, k, seed)
+    with pytest.raises(RuntimeError, match="cannot sample"):
+        _C.sample_rows(3, 4, 0)

@@ -136,3 +136,48 @@ def test_kmeans_bf16_tensor_core_quality(device):
     r16 = kmeans(xt.to(torch.bfloat16), 64, 10, 0.0, seed=5)
     r32 = kmeans(xt, 64, 10, 0.0, seed=5, exact_assign=True)
     assert abs(r16.inertia - r32.inertia) <= 0.02 * r32.inertia
+
+
+@pytest.mark.parametrize("case", cases.LLOYD_CASES, ids=[c[0] for c in cases.LLOYD_CASES])
+def test_kmeans_lloyd_matches_reference_iterations(device, case):
+    """rapidadb_b200.kmeans.kmeans with the reference's assign arithmetic
+    (exact_assign) against the reference's own kernels iterated the same
+    number of times (golden): centroids within 1e-4, labels equal except at
+    near-ties, inertia within 1e-5."""
+    from lloyd import assert_lloyd_match
+    from rapidadb_b200.kmeans import kmeans
+
+    gold = np.load(GOLDEN)
+    name, N, d, K, seed, iters = case
+    x, c0 = cases.kmeans_inputs(seed, N, d, K)
+    res = kmeans(torch.from_numpy(x).cuda(), K, max_iters=iters, tol=0.0, init=torch.from_numpy(c0).cuda(),
+                 exact_assign=True)
+    assert res.iterations == iters
+    assert_lloyd_match(x, gold[f"{name}_centroids"], gold[f"{name}_labels"], res.centroids.cpu().numpy(),
+                       res.labels.cpu().numpy(), name=name)
+    ref_inertia = float((gold[f"{name}_dist"].astype(np.float64) ** 2).sum())
+    assert abs(res.inertia - ref_inertia) <= 1e-5 * ref_inertia
+
+
+def test_cpp_kmeans_driver_matches_oracle_lloyd(device):
+    """_C.kmeans (the C++ Lloyd driver, kmeans_cuda's shape): seeded initial
+    rows, exact assign, tol = 0 runs max_iters; the result unpacks as
+    (centroids, labels, inertia, iterations) and matches the oracle's Lloyd
+    from the same initial rows."""
+    from lloyd import assert_lloyd_match
+    from rapidadb_b200.utils import sample_rows
+
+    g = np.random.default_rng(4)
+    centres = g.standard_normal((24, 48)).astype(np.float32) * 3
+    x = (centres[g.integers(0, 24, 5000)] + g.standard_normal((5000, 48))).astype(np.float32)
+    r = _C().kmeans(torch.from_numpy(x).cuda(), 24, max_iters=7, tol=0.0, seed=11, exact=True)
+    cent, labels, inertia, iters = r
+    assert iters == 7 and cent.shape == (24, 48) and labels.dtype == torch.int32 and inertia.dim() == 0
+    c0 = x[sample_rows(5000, 24, 11)]
+    rc, rl, rin, rit = oracle.kmeans(x, c0, 7, 0.0)
+    assert_lloyd_match(x, rc, rl, cent.cpu().numpy(), labels.cpu().numpy(), rtol=1e-5, name="cpp kmeans")
+    assert abs(float(inertia) - rin) <= 1e-5 * rin
+    # tolerance stop: converges well before 100 iterations on separated clusters
+    r2 = _C().kmeans(torch.from_numpy(x).cuda(), 24)
+    assert 1 <= r2.iterations < 100
+    assert "KMeansResult(k=24" in repr(r2)

@@ -70,6 +70,21 @@ def test_kmeans_step_matches_reference(gold, case):
     np.testing.assert_allclose(cent, gold[f"{name}_centroids"], rtol=1e-5, atol=1e-6)
 
 
+@pytest.mark.parametrize("case", cases.LLOYD_CASES, ids=[c[0] for c in cases.LLOYD_CASES])
+def test_lloyd_iterations_match_reference(gold, case):
+    """Several Lloyd iterations of the oracle against the reference's own
+    assign + update kernels iterated the same number of times."""
+    from lloyd import assert_lloyd_match
+
+    name, N, d, K, seed, iters = case
+    x, c0 = cases.kmeans_inputs(seed, N, d, K)
+    cent, labels, inertia, it = oracle.kmeans(x, c0, iters, 0.0)
+    assert it == iters
+    assert_lloyd_match(x, gold[f"{name}_centroids"], gold[f"{name}_labels"], cent, labels, name=name)
+    ref_inertia = float((gold[f"{name}_dist"].astype(np.float64) ** 2).sum())
+    assert abs(inertia - ref_inertia) <= 1e-5 * ref_inertia
+
+
 def test_planted_oracle_mistake_is_caught(gold):
     """The golden check is sensitive: an oracle answer with one id swapped for
     a non-tied row must fail the comparison."""
