@@ -41,7 +41,7 @@ extern "C" {
 #define RDB_METRIC_L2 1
 #define RDB_METRIC_DOT 2
 
-/* ---- element types: rapidadb::Precision, types.h:9-14 (INT8 not stored) */
+/* ---- element types: rapidadb::Precision, types.h:9-14 (INT8: the SQ8 entry points below) */
 #define RDB_F32 0
 #define RDB_F16 1
 #define RDB_BF16 2
@@ -128,6 +128,28 @@ int rdb_flat_search(int metric, int dtype, const void* q, int64_t nq, int64_t ld
                     const void* x, int64_t n, int64_t ldx, const float* xv, int d, int k,
                     const int64_t* ids, int64_t id_offset, int flags, float* out_d,
                     int64_t* out_i, void* ws, size_t ws_bytes, void* stream);
+
+/* INT8 storage: per-row symmetric scalar quantisation (SQ8).  The reference
+ * names INT8 among its precisions (csrc/include/rapidadb/core/types.h:9-14,
+ * python/rapidadb/config.py:21-26) without defining it; here a row x is
+ * stored as scale = max_i |x_i| / 127 (fp32 division; 0 for a zero row) and
+ * codes c_i = rint(x_i / scale) clamped to [-127, 127] (ties to even), and
+ * stands for the dequantised row x^_i = fl(scale * c_i).
+ *   rdb_sq8_encode        x [n, d] (dtype, stride ldx) -> codes [n, ldc] int8
+ *                         (columns d .. ldc - 1 zero), scales [n]
+ *   rdb_sq8_row_values    per-row metric values of x^ (as rdb_vec_values)
+ *   rdb_flat_search_sq8   rdb_flat_search over SQ8 rows with fp32 queries: the
+ *                         exact search over x^ (reference formulas, L2 summed
+ *                         directly for the returned rows), CUDA cores, one
+ *                         byte per stored element; ldx (bytes) a multiple of 4 */
+int rdb_sq8_encode(int dtype, const void* x, int64_t n, int64_t ldx, int d, int8_t* codes, int64_t ldc, float* scales,
+                   void* stream);
+int rdb_sq8_row_values(int metric, const int8_t* codes, const float* scales, int64_t n, int64_t ldc, int d,
+                       float* out, void* stream);
+size_t rdb_flat_search_sq8_workspace(int metric, int64_t nq, int64_t n, int d, int k, int flags);
+int rdb_flat_search_sq8(int metric, const float* q, int64_t nq, int64_t ldq, const int8_t* codes, const float* scales,
+                        int64_t n, int64_t ldx, const float* xv, int d, int k, const int64_t* ids, int64_t id_offset,
+                        int flags, float* out_d, int64_t* out_i, void* ws, size_t ws_bytes, void* stream);
 
 /* Row-sharded flat search with one threshold for all shards (no reference
  * counterpart: the reference is single-GPU).  Each shard computes the group
@@ -245,6 +267,14 @@ int rdb_ivf_flat_scan(int metric, int dtype, const void* q, int64_t nq, int64_t 
                       int nprobe, const void* rows, int64_t ldx, const float* xv, const int64_t* list_off,
                       const int64_t* list_end, int nlist, const int64_t* ids, int k, float* out_v, int64_t* out_i,
                       void* ws, size_t ws_bytes, void* stream);
+
+/* rdb_ivf_flat_scan over SQ8 rows (codes [.., ldx] int8 with per-row scales,
+ * see rdb_sq8_encode) and fp32 queries: the exact scan of the dequantised
+ * rows; ldx (bytes) a multiple of 4. */
+int rdb_ivf_flat_scan_sq8(int metric, const float* q, int64_t nq, int64_t ldq, int d, const int64_t* probe,
+                          int nprobe, const int8_t* codes, int64_t ldx, const float* scales, const float* xv,
+                          const int64_t* list_off, const int64_t* list_end, int nlist, const int64_t* ids, int k,
+                          float* out_v, int64_t* out_i, void* ws, size_t ws_bytes, void* stream);
 
 /* rdb_ivf_flat_scan for callers that may not allocate GPU memory (no
  * counterpart in the reference): the same list-major scan and the same

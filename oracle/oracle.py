@@ -213,3 +213,24 @@ def ivfpq_search(q: np.ndarray, centroids: np.ndarray, list_off: np.ndarray,
                            _p(codebooks, _f32p), M, ksub, nprobe, k, _p(out_d, _f32p),
                            _p(out_i, _i64p), nthreads)
     return out_d, out_i
+
+
+def sq8_encode(x: np.ndarray) -> Tuple[np.ndarray, np.ndarray]:
+    """INT8 storage as this implementation defines it (the reference names
+    INT8 among its precisions, csrc/include/rapidadb/core/types.h:9-14 and
+    python/rapidadb/config.py:21-26, with no semantics, so parity for INT8
+    is pinned by this definition only): per row, scale = max|x| / 127 (fp32
+    division; 0 for a zero row), code = rint(x / scale) (fp32 division, ties
+    to even) clamped to [-127, 127], 0 where scale == 0.  Returns (codes
+    int8 [n, d], scales float32 [n])."""
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    scale = (np.abs(x).max(axis=1) / np.float32(127.0)).astype(np.float32)
+    with np.errstate(divide="ignore", invalid="ignore"):
+        c = np.rint(x / scale[:, None])
+    c = np.where(scale[:, None] > 0, c, 0.0)
+    return np.clip(c, -127, 127).astype(np.int8), scale
+
+
+def sq8_decode(codes: np.ndarray, scales: np.ndarray) -> np.ndarray:
+    """The dequantised rows fl(scale * code) (float32 products)."""
+    return (np.asarray(scales, np.float32)[:, None] * np.asarray(codes).astype(np.float32)).astype(np.float32)

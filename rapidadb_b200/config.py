@@ -25,7 +25,10 @@ class IndexType(str, Enum):
 
 class Precision(str, Enum):
     """Storage precision (config.py:21-26).  FP32 rows search on CUDA cores,
-    FP16 / BF16 rows on the tcgen05 tensor cores.  INT8 is not stored."""
+    FP16 / BF16 rows on the tcgen05 tensor cores.  INT8 stores each row as
+    SQ8 codes with a per-row scale (scale = max|x| / 127, code = rint(x /
+    scale)) and searches the dequantised rows exactly, on CUDA cores, with
+    fp32 queries (Flat and IVF-Flat)."""
     FP32 = "fp32"
     FP16 = "fp16"
     BF16 = "bf16"

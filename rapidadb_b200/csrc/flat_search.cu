@@ -98,7 +98,7 @@ PassPlan plan_pass(int64_t rows, int64_t row_step, int64_t nq, int qtile, int rt
 // expect_given > 0: the caller supplies the thresholds (no sample pass) and
 // expects about that many candidates per query over the n rows
 FlatPlan make_plan(int metric, int dtype, int64_t nq, int64_t n, int d, int k, int flags,
-                   bool tc_ok, int64_t expect_given = 0) {
+                   bool tc_ok, int64_t expect_given = 0, bool x_i8 = false) {
     (void)metric;
     (void)d;
     FlatPlan P = {};
@@ -110,7 +110,8 @@ FlatPlan make_plan(int metric, int dtype, int64_t nq, int64_t n, int d, int k, i
     const int sms = num_sms();
     // CTAs that run at once: TMA-fed fp32 scans hold one per SM (their ring
     // fills the shared memory), the register-staged CUDA-core scan two
-    const int64_t target = P.tc ? (pair ? sms / 2 : sms) : dtype == RDB_F32 ? sms : 2LL * sms;
+    // (SQ8 rows go through the register-staged scan)
+    const int64_t target = P.tc ? (pair ? sms / 2 : sms) : (dtype == RDB_F32 && !x_i8) ? sms : 2LL * sms;
 
     // sample size S, a power of two >= 8 k: the sample pass costs S / n of the
     // main scan, the candidates (about n k / S per query) cost the main scan's
@@ -188,7 +189,7 @@ bool tc_layout_ok(int dtype, const void* q, int64_t ldq, const void* x, int64_t 
 int run_chunk(const FlatPlan& P, int metric, int dtype, const void* q, int64_t nq, int64_t ldq,
               const void* x, int64_t n, int64_t ldx, const float* xv, int d, int k,
               const int64_t* ids, int64_t id_offset, float* out_d, int64_t* out_i,
-              unsigned char* ws, cudaStream_t s, const float* thr_given) {
+              unsigned char* ws, cudaStream_t s, const float* thr_given, const float* x_scale) {
     float* qv = reinterpret_cast<float*>(ws + P.off_qv);
     float* thr = reinterpret_cast<float*>(ws + P.off_thr);
     uint2* cand = reinterpret_cast<uint2*>(ws + P.off_cand);
@@ -216,6 +217,8 @@ int run_chunk(const FlatPlan& P, int metric, int dtype, const void* q, int64_t n
     a.d = d;
     a.qv = qv;
     a.xv = xv;
+    a.x_i8 = x_scale ? 1 : 0;
+    a.x_scale = x_scale;
     a.cand = cand;
     a.counts = counts;
 
@@ -236,6 +239,8 @@ int run_chunk(const FlatPlan& P, int metric, int dtype, const void* q, int64_t n
     sa.xdata = x;
     sa.ldx = ldx;
     sa.d = d;
+    sa.x_i8 = x_scale ? 1 : 0;
+    sa.x_scale = x_scale;
 
     auto scan = [&](const ScanArgs& sc) {
         return P.tc ? launch_scan_tc(sc, SCAN_FILTER, s) : launch_scan_simt(sc, SCAN_FILTER, s);
@@ -354,6 +359,8 @@ int run_chunk(const FlatPlan& P, int metric, int dtype, const void* q, int64_t n
         ra.ldx = ldx;
         ra.d = d;
         ra.k = k;
+        ra.x_i8 = x_scale ? 1 : 0;
+        ra.x_scale = x_scale;
         ra.qv = qv;
         ra.xv = xv;
         ra.flag = flag;
@@ -414,7 +421,7 @@ namespace {
 int flat_search_impl(int metric, int dtype, const void* q, int64_t nq, int64_t ldq, const void* x, int64_t n,
                      int64_t ldx, const float* xv, int d, int k, const int64_t* ids, int64_t id_offset, int flags,
                      const float* thr_given, int64_t expect_given, float* out_d, int64_t* out_i, void* ws,
-                     size_t ws_bytes, void* stream) {
+                     size_t ws_bytes, void* stream, const float* x_scale = nullptr) {
     RDB_CHECK_ARG(metric >= 0 && metric <= 2, "unknown metric %d", metric);
     RDB_CHECK_ARG(elem_size(dtype) != 0, "unknown dtype %d", dtype);
     RDB_CHECK_ARG(nq >= 0 && d >= 1, "bad shape");
@@ -428,15 +435,16 @@ int flat_search_impl(int metric, int dtype, const void* q, int64_t nq, int64_t l
     RDB_CHECK_ARG(metric != RDB_METRIC_COSINE || xv, "cosine needs per-row values");
     RDB_CHECK_ARG(metric != RDB_METRIC_L2 || xv, "L2 needs per-row values");
     cudaStream_t s = static_cast<cudaStream_t>(stream);
-    bool tc_ok = tc_layout_ok(dtype, q, ldq, x, ldx, d);
+    const bool x_i8 = x_scale != nullptr;
+    bool tc_ok = !x_i8 && tc_layout_ok(dtype, q, ldq, x, ldx, d);
     const int64_t eg = thr_given ? std::max<int64_t>(expect_given, 1) : 0;
 
     // largest query chunk whose plan fits the workspace
-    FlatPlan P = make_plan(metric, dtype, nq, n, d, k, flags, tc_ok, eg);
+    FlatPlan P = make_plan(metric, dtype, nq, n, d, k, flags, tc_ok, eg, x_i8);
     int64_t chunk = nq;
     while (P.ws_bytes > ws_bytes && chunk > P.qtile) {
         chunk = std::max<int64_t>(P.qtile, (chunk / 2 + P.qtile - 1) / P.qtile * P.qtile);
-        P = make_plan(metric, dtype, chunk, n, d, k, flags, tc_ok, eg);
+        P = make_plan(metric, dtype, chunk, n, d, k, flags, tc_ok, eg, x_i8);
     }
     if (P.ws_bytes > ws_bytes)
         return set_error(RDB_ERR_WORKSPACE, "workspace too small: %zu bytes, need %zu", ws_bytes,
@@ -445,10 +453,10 @@ int flat_search_impl(int metric, int dtype, const void* q, int64_t nq, int64_t l
     const size_t es = elem_size(dtype);
     for (int64_t c0 = 0; c0 < nq; c0 += chunk) {
         int64_t cn = std::min(chunk, nq - c0);
-        FlatPlan Pc = cn == chunk ? P : make_plan(metric, dtype, cn, n, d, k, flags, tc_ok, eg);
+        FlatPlan Pc = cn == chunk ? P : make_plan(metric, dtype, cn, n, d, k, flags, tc_ok, eg, x_i8);
         RDB_TRY(run_chunk(Pc, metric, dtype, static_cast<const char*>(q) + c0 * ldq * es, cn, ldq,
                           x, n, ldx, xv, d, k, ids, id_offset, out_d + c0 * k, out_i + c0 * k, w,
-                          s, thr_given ? thr_given + c0 : nullptr));
+                          s, thr_given ? thr_given + c0 : nullptr, x_scale));
     }
     if (flags & RDB_SEARCH_SYNC) {
         // wait for this call and report a bounded-wait timeout of its kernels
@@ -474,6 +482,20 @@ int rdb_flat_search(int metric, int dtype, const void* q, int64_t nq, int64_t ld
                     int64_t* out_i, void* ws, size_t ws_bytes, void* stream) {
     return flat_search_impl(metric, dtype, q, nq, ldq, x, n, ldx, xv, d, k, ids, id_offset, flags, nullptr, 0,
                             out_d, out_i, ws, ws_bytes, stream);
+}
+
+size_t rdb_flat_search_sq8_workspace(int metric, int64_t nq, int64_t n, int d, int k, int flags) {
+    if (nq <= 0 || n <= 0 || d <= 0 || k <= 0) return 256;
+    return make_plan(metric, RDB_F32, nq, n, d, k, flags, false, 0, true).ws_bytes;
+}
+
+int rdb_flat_search_sq8(int metric, const float* q, int64_t nq, int64_t ldq, const int8_t* codes, const float* scales,
+                        int64_t n, int64_t ldx, const float* xv, int d, int k, const int64_t* ids, int64_t id_offset,
+                        int flags, float* out_d, int64_t* out_i, void* ws, size_t ws_bytes, void* stream) {
+    RDB_CHECK_ARG(scales != nullptr || n == 0, "scales is NULL");
+    RDB_CHECK_ARG(ldx % 4 == 0, "SQ8 row stride must be a multiple of 4 bytes");
+    return flat_search_impl(metric, RDB_F32, q, nq, ldq, codes, n, ldx, xv, d, k, ids, id_offset, flags, nullptr, 0,
+                            out_d, out_i, ws, ws_bytes, stream, scales ? scales : nullptr);
 }
 
 size_t rdb_flat_search_thr_workspace(int metric, int dtype, int64_t nq, int64_t n, int d, int k, int64_t expect) {

@@ -77,6 +77,14 @@ PYBIND11_MODULE(_C, m) {
         .def("search_threshold", &FlatIndex::search_threshold, py::arg("queries"), py::arg("k"), py::arg("thr"),
              py::arg("expect"))
         .def("tensor_core", &FlatIndex::tensor_core)
+        .def("sq8", &FlatIndex::sq8)
+        .def("sq8_codes", &FlatIndex::sq8_codes)
+        .def("sq8_scales", &FlatIndex::sq8_scales)
+        .def("add_sq8", [](FlatIndex& self, const at::Tensor& codes, const at::Tensor& scales, const py::object& ids) {
+            at::Tensor t = opt_tensor(ids);
+            py::gil_scoped_release nogil;
+            self.add_sq8(codes, scales, t);
+        }, py::arg("codes"), py::arg("scales"), py::arg("ids") = py::none())
         .def("ids", &FlatIndex::ids)
         .def("__len__", &FlatIndex::size)
         .def("__repr__", [](const FlatIndex& self) {
@@ -172,6 +180,11 @@ PYBIND11_MODULE(_C, m) {
         .def("stored_labels", &IVFFlatIndex::stored_labels)
         .def("stored_vectors", &IVFFlatIndex::stored_vectors)
         .def("restore", &IVFFlatIndex::restore, py::arg("vectors"), py::arg("labels"), py::arg("ids"), py::call_guard<py::gil_scoped_release>())
+        .def("sq8", &IVFFlatIndex::sq8)
+        .def("stored_sq8_codes", &IVFFlatIndex::stored_sq8_codes)
+        .def("stored_sq8_scales", &IVFFlatIndex::stored_sq8_scales)
+        .def("restore_sq8", &IVFFlatIndex::restore_sq8, py::arg("codes"), py::arg("scales"), py::arg("labels"),
+             py::arg("ids"), py::call_guard<py::gil_scoped_release>())
         .def("__len__", &IVFFlatIndex::size)
         .def("__repr__", [](const IVFFlatIndex& s) {
             return "IVFFlatIndex(dim=" + std::to_string(s.dim()) + ", nlist=" + std::to_string(s.nlist()) +

@@ -35,9 +35,37 @@ at::ScalarType storage_type(Precision p) {
         case Precision::FP32: return at::kFloat;
         case Precision::FP16: return at::kHalf;
         case Precision::BF16: return at::kBFloat16;
-        default: TORCH_CHECK(false, "INT8 storage is not supported");
+        case Precision::INT8: return at::kChar;  // SQ8 codes (rdb_sq8_encode) + per-row scales
     }
     return at::kFloat;
+}
+
+void sq8_encode_into(const at::Tensor& vectors, at::Tensor codes, at::Tensor scales) {
+    const int64_t n = vectors.size(0);
+    if (n == 0) return;
+    at::Tensor v = vectors;
+    if (!(v.scalar_type() == at::kFloat || v.scalar_type() == at::kHalf || v.scalar_type() == at::kBFloat16))
+        v = v.to(at::kFloat);
+    if (v.stride(1) != 1) v = v.contiguous();
+    TORCH_CHECK(codes.is_contiguous() || codes.stride(1) == 1, "codes rows must be dense");
+    check_status(rdb_sq8_encode(dtype_code(v.scalar_type()), v.data_ptr(), n, v.stride(0), static_cast<int>(v.size(1)),
+                                codes.data_ptr<int8_t>(), codes.stride(0), scales.data_ptr<float>(), stream_ptr()),
+                 "sq8 encode");
+}
+
+at::Tensor sq8_row_values(Metric metric, const at::Tensor& codes, const at::Tensor& scales, int dim) {
+    const int64_t n = codes.size(0);
+    at::Tensor out = at::empty({n}, scales.options());
+    if (n == 0) return out;
+    check_status(rdb_sq8_row_values(static_cast<int>(metric), codes.data_ptr<int8_t>(), scales.data_ptr<float>(), n,
+                                    codes.stride(0), dim, out.data_ptr<float>(), stream_ptr()),
+                 "sq8 row values");
+    return out;
+}
+
+at::Tensor sq8_dequantize(const at::Tensor& codes, const at::Tensor& scales, int dim) {
+    // fl(scale * code), the value every SQ8 search scores against
+    return codes.narrow(1, 0, dim).to(at::kFloat) * scales.unsqueeze(1);
 }
 
 void* stream_ptr() { return static_cast<void*>(at::cuda::getCurrentCUDAStream().stream()); }
@@ -182,14 +210,17 @@ void FlatIndex::reserve(int64_t rows) {
     at::Tensor s = at::zeros({ncap, ld_}, opts.dtype(storage_type(precision_)));
     at::Tensor xv = at::empty({ncap}, s.options().dtype(at::kFloat));
     at::Tensor ids = at::empty({ncap}, s.options().dtype(at::kLong));
+    at::Tensor sc = sq8() ? at::empty({ncap}, s.options().dtype(at::kFloat)) : at::Tensor();
     if (n_ > 0) {
         s.narrow(0, 0, n_).copy_(storage_.narrow(0, 0, n_));
         xv.narrow(0, 0, n_).copy_(xv_.narrow(0, 0, n_));
         ids.narrow(0, 0, n_).copy_(ids_.narrow(0, 0, n_));
+        if (sq8()) sc.narrow(0, 0, n_).copy_(scales_.narrow(0, 0, n_));
     }
     storage_ = s;
     xv_ = xv;
     ids_ = ids;
+    scales_ = sc;
 }
 
 void FlatIndex::add(const at::Tensor& vectors, const at::Tensor& ids) {
@@ -211,12 +242,19 @@ void FlatIndex::add(const at::Tensor& vectors, const at::Tensor& ids) {
         storage_ = at::zeros({0, ld_}, vectors.options().dtype(storage_type(precision_)));
         xv_ = at::empty({0}, vectors.options().dtype(at::kFloat));
         ids_ = at::empty({0}, vectors.options().dtype(at::kLong));
+        if (sq8()) scales_ = at::empty({0}, vectors.options().dtype(at::kFloat));
     }
     if (n == 0) return;
     reserve(n_ + n);
     at::Tensor dst = storage_.narrow(0, n_, n);
-    dst.narrow(1, 0, dim_).copy_(vectors);
-    xv_.narrow(0, n_, n).copy_(row_values(metric_, dst, dim_));
+    if (sq8()) {
+        at::Tensor sc = scales_.narrow(0, n_, n);
+        sq8_encode_into(vectors, dst, sc);
+        xv_.narrow(0, n_, n).copy_(sq8_row_values(metric_, dst, sc, dim_));
+    } else {
+        dst.narrow(1, 0, dim_).copy_(vectors);
+        xv_.narrow(0, n_, n).copy_(row_values(metric_, dst, dim_));
+    }
     if (new_ids.defined())
         ids_.narrow(0, n_, n).copy_(new_ids);
     else
@@ -267,6 +305,24 @@ Result FlatIndex::search(const at::Tensor& queries, int64_t k) const {
     TORCH_CHECK(k > 0 && k <= n_, "k must be in [1, " + std::to_string(n_) + "]");
     TORCH_CHECK(is_float_type(queries.scalar_type()), "queries must be float32");
     c10::cuda::CUDAGuard guard(storage_.device());
+    if (sq8()) {
+        // SQ8 rows: fp32 queries against the dequantised rows
+        at::Tensor q = prepare_rows(queries.to(storage_.device()), at::kFloat, padded_ld(dim_, at::kFloat));
+        const int64_t nq = q.size(0);
+        at::Tensor out_d = at::empty({nq, k}, q.options().dtype(at::kFloat));
+        at::Tensor out_i = at::empty({nq, k}, q.options().dtype(at::kLong));
+        if (nq == 0) return {out_d, out_i};
+        check_pending_status();
+        const int m = static_cast<int>(metric_);
+        size_t wsb = rdb_flat_search_sq8_workspace(m, nq, n_, dim_, static_cast<int>(k), 0);
+        at::Tensor ws = at::empty({static_cast<int64_t>(wsb)}, q.options().dtype(at::kByte));
+        check_status(rdb_flat_search_sq8(m, q.data_ptr<float>(), nq, q.size(1), storage_.data_ptr<int8_t>(),
+                                         scales_.data_ptr<float>(), n_, ld_, xv_.data_ptr<float>(), dim_,
+                                         static_cast<int>(k), ids_.data_ptr<int64_t>(), 0, 0, out_d.data_ptr<float>(),
+                                         out_i.data_ptr<int64_t>(), ws.data_ptr(), wsb, stream_ptr()),
+                     "flat search");
+        return {out_d, out_i};
+    }
     at::Tensor q = prepare_rows(queries.to(storage_.device()), storage_.scalar_type(), ld_);
     return search_impl(metric_, storage_.narrow(0, 0, n_), dim_, xv_.narrow(0, 0, n_), q, k,
                        ids_.narrow(0, 0, n_), 0);
@@ -322,12 +378,53 @@ void FlatIndex::reset() {
     storage_ = at::Tensor();
     xv_ = at::Tensor();
     ids_ = at::Tensor();
+    scales_ = at::Tensor();
     n_ = 0;
 }
 
 at::Tensor FlatIndex::vectors() const {
     if (!storage_.defined()) return at::empty({0, dim_});
+    if (sq8()) return sq8_dequantize(storage_.narrow(0, 0, n_), scales_.narrow(0, 0, n_), dim_);
     return storage_.narrow(0, 0, n_).narrow(1, 0, dim_);
+}
+
+at::Tensor FlatIndex::sq8_codes() const {
+    TORCH_CHECK(sq8(), "the index does not store INT8 (SQ8) rows");
+    if (!storage_.defined()) return at::empty({0, dim_}, at::kChar);
+    return storage_.narrow(0, 0, n_).narrow(1, 0, dim_);
+}
+
+at::Tensor FlatIndex::sq8_scales() const {
+    TORCH_CHECK(sq8(), "the index does not store INT8 (SQ8) rows");
+    if (!storage_.defined()) return at::empty({0}, at::kFloat);
+    return scales_.narrow(0, 0, n_);
+}
+
+void FlatIndex::add_sq8(const at::Tensor& codes, const at::Tensor& scales, const at::Tensor& ids) {
+    TORCH_CHECK(sq8(), "the index does not store INT8 (SQ8) rows");
+    TORCH_CHECK(codes.is_cuda() && scales.is_cuda(), "codes and scales must be on CUDA");
+    TORCH_CHECK(codes.dim() == 2 && codes.size(1) == dim_ && codes.scalar_type() == at::kChar,
+                "codes must be int8 [n, " + std::to_string(dim_) + "]");
+    TORCH_CHECK(scales.dim() == 1 && scales.size(0) == codes.size(0), "scales must be [n]");
+    const int64_t n = codes.size(0);
+    c10::cuda::CUDAGuard guard(codes.device());
+    if (!storage_.defined()) {
+        storage_ = at::zeros({0, ld_}, codes.options());
+        xv_ = at::empty({0}, codes.options().dtype(at::kFloat));
+        ids_ = at::empty({0}, codes.options().dtype(at::kLong));
+        scales_ = at::empty({0}, codes.options().dtype(at::kFloat));
+    }
+    if (n == 0) return;
+    reserve(n_ + n);
+    at::Tensor dst = storage_.narrow(0, n_, n);
+    dst.narrow(1, 0, dim_).copy_(codes);
+    scales_.narrow(0, n_, n).copy_(scales.to(at::kFloat));
+    xv_.narrow(0, n_, n).copy_(sq8_row_values(metric_, dst, scales_.narrow(0, n_, n), dim_));
+    if (ids.defined() && ids.numel() > 0)
+        ids_.narrow(0, n_, n).copy_(ids.to(at::kLong));
+    else
+        ids_.narrow(0, n_, n).copy_(at::arange(n_, n_ + n, ids_.options()));
+    n_ += n;
 }
 
 at::Tensor FlatIndex::ids() const {

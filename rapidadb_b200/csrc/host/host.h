@@ -65,6 +65,12 @@ class FlatIndex {
     at::Tensor sample_maxima(const at::Tensor& queries, int64_t sample_rows, int64_t group) const;
     Result search_threshold(const at::Tensor& queries, int64_t k, const at::Tensor& thr, int64_t expect) const;
     bool tensor_core() const { return precision_ == Precision::FP16 || precision_ == Precision::BF16; }
+    // INT8 storage (SQ8, rdb_sq8_encode): codes [size, dim] int8, scales [size];
+    // vectors() returns the dequantised rows fl(scale * code)
+    bool sq8() const { return precision_ == Precision::INT8; }
+    at::Tensor sq8_codes() const;
+    at::Tensor sq8_scales() const;
+    void add_sq8(const at::Tensor& codes, const at::Tensor& scales, const at::Tensor& ids);
 
     // Search against externally owned rows (same layout rules): used by the
     // IVF coarse probe and by tests.
@@ -83,6 +89,7 @@ class FlatIndex {
     at::Tensor storage_;  // [capacity, ld_] in the storage dtype, padding zero
     at::Tensor xv_;       // [capacity] per-row metric values
     at::Tensor ids_;      // [capacity] int64
+    at::Tensor scales_;   // [capacity] fp32 SQ8 row scales (INT8 storage only)
     int64_t n_ = 0;
 };
 
@@ -91,5 +98,10 @@ class FlatIndex {
 at::Tensor prepare_rows(const at::Tensor& src, at::ScalarType dtype, int64_t ld);
 int64_t padded_ld(int dim, at::ScalarType dtype);
 at::Tensor row_values(Metric metric, const at::Tensor& rows_padded, int dim);
+// SQ8 (INT8 storage): encode rows into codes [n, ld] / scales [n] (in place),
+// per-row metric values of the dequantised rows, and the dequantised rows
+void sq8_encode_into(const at::Tensor& vectors, at::Tensor codes, at::Tensor scales);
+at::Tensor sq8_row_values(Metric metric, const at::Tensor& codes, const at::Tensor& scales, int dim);
+at::Tensor sq8_dequantize(const at::Tensor& codes, const at::Tensor& scales, int dim);
 
 }  // namespace rdbh

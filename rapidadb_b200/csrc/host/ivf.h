@@ -110,16 +110,25 @@ class IVFFlatIndex : public IVFBase {
     // scan with a given [nq, np] probe table (e.g. gathered from other ranks)
     Result search_probed(const at::Tensor& queries, const at::Tensor& probe, int64_t k) const;
     void reset() override;
-    at::Tensor stored_vectors() const { return rows_.defined() ? live_select(rows_).narrow(1, 0, dim_) : at::Tensor(); }
+    // stored rows in list order (INT8 storage: the dequantised rows)
+    at::Tensor stored_vectors() const;
     // reinstalls a saved index: vectors [n, dim], list labels [n] (non-
     // decreasing) and ids [n], all in stored order (see stored_*())
     void restore(const at::Tensor& vectors, const at::Tensor& labels, const at::Tensor& ids);
+    // INT8 storage (SQ8, rdb_sq8_encode): codes [n, dim] and scales [n] in
+    // stored order, and their exact reinstallation
+    bool sq8() const { return precision_ == Precision::INT8; }
+    at::Tensor stored_sq8_codes() const;
+    at::Tensor stored_sq8_scales() const;
+    void restore_sq8(const at::Tensor& codes, const at::Tensor& scales, const at::Tensor& labels,
+                     const at::Tensor& ids);
 
   private:
     Precision precision_;
     int64_t ld_;
-    at::Tensor rows_;  // [cap, ld] slots list by list, storage dtype (free slots zero)
-    at::Tensor xv_;    // [cap]
+    at::Tensor rows_;    // [cap, ld] slots list by list, storage dtype (free slots zero)
+    at::Tensor xv_;      // [cap]
+    at::Tensor scales_;  // [cap] SQ8 row scales (INT8 storage only)
 };
 
 class IVFPQIndex : public IVFBase {

@@ -321,15 +321,24 @@ void IVFFlatIndex::add(const at::Tensor& vectors, const at::Tensor& ids) {
     at::Tensor nid = new_ids(vectors, ids);
     // exact list assignment (reference assign arithmetic on fp32 values)
     at::Tensor lab = std::get<0>(kmeans_assign(vectors.to(at::kFloat), centroids_, true));
-    at::Tensor rows_new = prepare_rows(vectors, storage_type(precision_), ld_);
-    if (!rows_new.is_same(vectors)) rows_new = rows_new.contiguous();
-    at::Tensor xv_new = row_values(metric_, rows_new, dim_);
+    at::Tensor rows_new, xv_new, sc_new;
+    if (sq8()) {
+        rows_new = at::zeros({m, ld_}, vectors.options().dtype(at::kChar));
+        sc_new = at::empty({m}, vectors.options().dtype(at::kFloat));
+        sq8_encode_into(vectors, rows_new, sc_new);
+        xv_new = sq8_row_values(metric_, rows_new, sc_new, dim_);
+    } else {
+        rows_new = prepare_rows(vectors, storage_type(precision_), ld_);
+        if (!rows_new.is_same(vectors)) rows_new = rows_new.contiguous();
+        xv_new = row_values(metric_, rows_new, dim_);
+    }
     TORCH_CHECK(n_ + m < (int64_t(1) << 32), "at most 2^32 - 1 rows per device");
     at::Tensor dest;
     if (append_slots(lab, dest)) {
         // every list had room: rows go to free slots, nothing else moves
         rows_.index_copy_(0, dest, rows_new);
         xv_.index_copy_(0, dest, xv_new);
+        if (sq8()) scales_.index_copy_(0, dest, sc_new);
         ids_.index_copy_(0, dest, nid);
         labels_.index_copy_(0, dest, lab.to(at::kInt));
         return;
@@ -338,11 +347,13 @@ void IVFFlatIndex::add(const at::Tensor& vectors, const at::Tensor& ids) {
     const bool had = n_ > 0;
     at::Tensor old_rows = had ? live_select(rows_) : at::Tensor();
     at::Tensor old_xv = had ? live_select(xv_) : at::Tensor();
+    at::Tensor old_sc = had && sq8() ? live_select(scales_) : at::Tensor();
     at::Tensor old_ids = had ? stored_ids() : at::Tensor();
     at::Tensor old_lab = had ? stored_labels() : at::Tensor();
     new_layout(lab, dest);
     rows_ = relayout(old_rows, rows_new, dest, cap_, 0.0);
     xv_ = relayout(old_xv, xv_new, dest, cap_, 0.0);
+    if (sq8()) scales_ = relayout(old_sc, sc_new, dest, cap_, 0.0);
     ids_ = relayout(old_ids, nid, dest, cap_, -1.0);
     labels_ = relayout(old_lab, lab.to(at::kInt), dest, cap_, -1.0);
 }
@@ -355,9 +366,51 @@ void IVFFlatIndex::restore(const at::Tensor& vectors, const at::Tensor& labels, 
     reset();
     if (vectors.size(0) == 0) return;
     at::Tensor v = vectors.to(centroids_.device());
-    rows_ = prepare_rows(v, storage_type(precision_), ld_).contiguous();
-    xv_ = row_values(metric_, rows_, dim_);
+    if (sq8()) {
+        // float rows into an INT8 index: encoded like add()
+        rows_ = at::zeros({v.size(0), ld_}, v.options().dtype(at::kChar));
+        scales_ = at::empty({v.size(0)}, v.options().dtype(at::kFloat));
+        sq8_encode_into(v, rows_, scales_);
+        xv_ = sq8_row_values(metric_, rows_, scales_, dim_);
+    } else {
+        rows_ = prepare_rows(v, storage_type(precision_), ld_).contiguous();
+        xv_ = row_values(metric_, rows_, dim_);
+    }
     restore_lists(labels, ids);
+}
+
+void IVFFlatIndex::restore_sq8(const at::Tensor& codes, const at::Tensor& scales, const at::Tensor& labels,
+                               const at::Tensor& ids) {
+    TORCH_CHECK(sq8(), "the index does not store INT8 (SQ8) rows");
+    TORCH_CHECK(is_trained(), "index is not trained (call set_quantizer() first)");
+    TORCH_CHECK(codes.dim() == 2 && codes.size(1) == dim_ && codes.scalar_type() == at::kChar,
+                "codes must be int8 [n, " + std::to_string(dim_) + "]");
+    TORCH_CHECK(scales.dim() == 1 && scales.size(0) == codes.size(0) && codes.size(0) == labels.size(0),
+                "codes, scales and labels must have the same length");
+    c10::cuda::CUDAGuard guard(centroids_.device());
+    reset();
+    if (codes.size(0) == 0) return;
+    rows_ = at::zeros({codes.size(0), ld_}, centroids_.options().dtype(at::kChar));
+    rows_.narrow(1, 0, dim_).copy_(codes);
+    scales_ = scales.to(centroids_.device()).to(at::kFloat).contiguous();
+    xv_ = sq8_row_values(metric_, rows_, scales_, dim_);
+    restore_lists(labels, ids);
+}
+
+at::Tensor IVFFlatIndex::stored_vectors() const {
+    if (!rows_.defined()) return at::Tensor();
+    if (sq8()) return sq8_dequantize(live_select(rows_), live_select(scales_), dim_);
+    return live_select(rows_).narrow(1, 0, dim_);
+}
+
+at::Tensor IVFFlatIndex::stored_sq8_codes() const {
+    TORCH_CHECK(sq8(), "the index does not store INT8 (SQ8) rows");
+    return rows_.defined() ? live_select(rows_).narrow(1, 0, dim_) : at::Tensor();
+}
+
+at::Tensor IVFFlatIndex::stored_sq8_scales() const {
+    TORCH_CHECK(sq8(), "the index does not store INT8 (SQ8) rows");
+    return scales_.defined() ? live_select(scales_) : at::Tensor();
 }
 
 Result IVFFlatIndex::search(const at::Tensor& queries, int64_t k) const {
@@ -378,7 +431,8 @@ Result IVFFlatIndex::search_probed(const at::Tensor& queries, const at::Tensor& 
     at::Tensor qd = queries.to(rows_.device());
     at::Tensor probe_lists = check_probe(probe_in, qd.size(0), rows_);
     const int np = static_cast<int>(probe_lists.size(1));
-    at::Tensor q = prepare_rows(qd, rows_.scalar_type(), ld_);
+    at::Tensor q = sq8() ? prepare_rows(qd, at::kFloat, padded_ld(dim_, at::kFloat))
+                         : prepare_rows(qd, rows_.scalar_type(), ld_);
     const int64_t nq = q.size(0);
     at::Tensor cv = at::empty({np, nq, k}, q.options().dtype(at::kFloat));
     at::Tensor ci = at::empty({np, nq, k}, q.options().dtype(at::kLong));
@@ -388,6 +442,16 @@ Result IVFFlatIndex::search_probed(const at::Tensor& queries, const at::Tensor& 
     // rows on average; shorter lists are scanned with (q - x)^2 directly
     // (no row values passed)
     const bool expand = metric_ != Metric::L2 || n_ >= kIvfExpandRowsPerList * static_cast<int64_t>(nlist_);
+    if (sq8()) {
+        check_status(rdb_ivf_flat_scan_sq8(static_cast<int>(metric_), q.data_ptr<float>(), nq, q.size(1), dim_,
+                                           probe_lists.data_ptr<int64_t>(), np, rows_.data_ptr<int8_t>(), ld_,
+                                           scales_.data_ptr<float>(), expand ? xv_.data_ptr<float>() : nullptr,
+                                           list_off_.data_ptr<int64_t>(), list_end_.data_ptr<int64_t>(), nlist_,
+                                           ids_.data_ptr<int64_t>(), static_cast<int>(k), cv.data_ptr<float>(),
+                                           ci.data_ptr<int64_t>(), ws.data_ptr(), ws.numel(), stream_ptr()),
+                     "ivf scan");
+        return topk_merge(cv, ci, k, metric_ != Metric::L2);
+    }
     check_status(rdb_ivf_flat_scan(static_cast<int>(metric_), dtype_code(rows_.scalar_type()), q.data_ptr(), nq, ld_,
                                    dim_, probe_lists.data_ptr<int64_t>(), np, rows_.data_ptr(), ld_,
                                    expand ? xv_.data_ptr<float>() : nullptr, list_off_.data_ptr<int64_t>(),
@@ -402,6 +466,7 @@ void IVFFlatIndex::reset() {
     IVFBase::reset();
     rows_ = at::Tensor();
     xv_ = at::Tensor();
+    scales_ = at::Tensor();
 }
 
 // ----------------------------------------------------------------- IVF-PQ

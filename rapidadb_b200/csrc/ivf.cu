@@ -39,6 +39,8 @@ template <>
 __device__ __forceinline__ float to_f<__half>(__half v) { return __half2float(v); }
 template <>
 __device__ __forceinline__ float to_f<__nv_bfloat16>(__nv_bfloat16 v) { return __bfloat162float(v); }
+template <>
+__device__ __forceinline__ float to_f<int8_t>(int8_t v) { return static_cast<float>(v); }
 
 // a ranks before b; ties to the lower row
 __device__ __forceinline__ bool ranks_before(float a, int64_t ia, float b, int64_t ib, bool largest) {
@@ -119,7 +121,10 @@ constexpr int kL2ExpandMaxK = kMaxIvfK - kL2Margin;
 template <typename T>
 __device__ __forceinline__ float4 load4f(const T* p, bool vec, int nvalid) {
     if (vec && nvalid >= 4) {
-        if constexpr (sizeof(T) == 4) {
+        if constexpr (sizeof(T) == 1) {
+            const char4 c = __ldg(reinterpret_cast<const char4*>(p));
+            return make_float4(c.x, c.y, c.z, c.w);
+        } else if constexpr (sizeof(T) == 4) {
             return __ldg(reinterpret_cast<const float4*>(p));
         } else {
             const uint2 u = __ldg(reinterpret_cast<const uint2*>(p));
@@ -142,12 +147,25 @@ struct IvfFlatSmem {
     float s_qv[FQ];
 };
 
-// EXPAND: accumulate q.x (every metric but direct L2); false: accumulate (q - x)^2
-template <typename T, bool EXPAND>
+// four row elements as floats; SQ8 rows (TX = int8_t) dequantised with the
+// row's scale, fl(scale * code)
+template <typename TX>
+__device__ __forceinline__ float4 load_row4(const TX* p, int64_t r, const float* x_scale, bool vec, int nvalid) {
+    float4 v = load4f<TX>(p, vec, nvalid);
+    if constexpr (sizeof(TX) == 1) {
+        const float sc = __ldg(x_scale + r);
+        v = make_float4(__fmul_rn(sc, v.x), __fmul_rn(sc, v.y), __fmul_rn(sc, v.z), __fmul_rn(sc, v.w));
+    }
+    return v;
+}
+
+// EXPAND: accumulate q.x (every metric but direct L2); false: accumulate (q - x)^2.
+// T: query (and row) type; TX = int8_t: rows are SQ8 codes with x_scale.
+template <typename T, bool EXPAND, typename TX = T>
 __global__ void __launch_bounds__(FNT, 2) ivf_flat_scan_kernel(
     int metric, int cos_small, const T* __restrict__ q, int64_t Q, int64_t ldq, int d, const float* __restrict__ qv,
-    int nprobe, const int64_t* __restrict__ eperm, const int64_t* __restrict__ eseg, const T* __restrict__ rows,
-    int64_t ldx, const float* __restrict__ xv, const int64_t* __restrict__ list_off,
+    int nprobe, const int64_t* __restrict__ eperm, const int64_t* __restrict__ eseg, const TX* __restrict__ rows,
+    int64_t ldx, const float* __restrict__ x_scale, const float* __restrict__ xv, const int64_t* __restrict__ list_off,
     const int64_t* __restrict__ list_end, int nlist,
     const int64_t* __restrict__ ids, int k, float* __restrict__ out_v, int64_t* __restrict__ out_i) {
     extern __shared__ __align__(16) unsigned char ivf_smem[];
@@ -202,7 +220,7 @@ __global__ void __launch_bounds__(FNT, 2) ivf_flat_scan_kernel(
 #pragma unroll
                     for (int i = 0; i < 8; ++i) {
                         const int64_t r = t0 + sq + 32 * i;
-                        px[i] = (r < r1 && nv > 0) ? load4f<T>(rows + r * ldx + kx, vec_x, nv)
+                        px[i] = (r < r1 && nv > 0) ? load_row4<TX>(rows + r * ldx + kx, r, x_scale, vec_x, nv)
                                                    : make_float4(0.f, 0.f, 0.f, 0.f);
                     }
                 };
@@ -280,14 +298,14 @@ __global__ void __launch_bounds__(FNT, 2) ivf_flat_scan_kernel(
                     float dist = INFINITY;
                     if (has) {
                         const T* qp = q + qq * ldq;
-                        const T* xp = rows + st[j].id * ldx;
+                        const TX* xp = rows + st[j].id * ldx;
                         float a = 0.f;
                         int c = 0;
                         if (vec_q && vec_x) {
 #pragma unroll 8
                             for (; c + 4 <= d; c += 4) {
                                 const float4 u = load4f<T>(qp + c, true, 4);
-                                const float4 v = load4f<T>(xp + c, true, 4);
+                                const float4 v = load_row4<TX>(xp + c, st[j].id, x_scale, true, 4);
                                 float df = u.x - v.x;
                                 a = fmaf(df, df, a);
                                 df = u.y - v.y;
@@ -299,7 +317,9 @@ __global__ void __launch_bounds__(FNT, 2) ivf_flat_scan_kernel(
                             }
                         }
                         for (; c < d; ++c) {
-                            const float df = to_f<T>(qp[c]) - to_f<T>(xp[c]);
+                            float xe = to_f<TX>(xp[c]);
+                            if constexpr (sizeof(TX) == 1) xe = __fmul_rn(__ldg(x_scale + st[j].id), xe);
+                            const float df = to_f<T>(qp[c]) - xe;
                             a = fmaf(df, df, a);
                         }
                         dist = a;
@@ -510,22 +530,24 @@ int invert_probes(const int64_t* probe, int64_t Q, int nprobe, int nlist, const 
                       label_sort_workspace(ne, nlist), s);
 }
 
-template <typename T>
+template <typename T, typename TX = T>
 int ivf_flat_smem_attr(int bytes) {
-    RDB_CUDA_TRY(cudaFuncSetAttribute(ivf_flat_scan_kernel<T, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes));
-    RDB_CUDA_TRY(cudaFuncSetAttribute(ivf_flat_scan_kernel<T, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes));
+    RDB_CUDA_TRY(cudaFuncSetAttribute(ivf_flat_scan_kernel<T, true, TX>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      bytes));
+    RDB_CUDA_TRY(cudaFuncSetAttribute(ivf_flat_scan_kernel<T, false, TX>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      bytes));
     return RDB_OK;
 }
 
-template <typename T>
+template <typename T, typename TX = T>
 void launch_ivf_flat(bool expand, dim3 grid, cudaStream_t s, int metric, int cos_small, const void* q, int64_t nq,
                      int64_t ldq, int d, const float* qv, int nprobe, const int64_t* eperm, const int64_t* eseg,
-                     const void* rows, int64_t ldx, const float* xv, const int64_t* list_off,
+                     const void* rows, int64_t ldx, const float* x_scale, const float* xv, const int64_t* list_off,
                      const int64_t* list_end, int nlist,
                      const int64_t* ids, int k, float* out_v, int64_t* out_i) {
-    auto kern = expand ? ivf_flat_scan_kernel<T, true> : ivf_flat_scan_kernel<T, false>;
+    auto kern = expand ? ivf_flat_scan_kernel<T, true, TX> : ivf_flat_scan_kernel<T, false, TX>;
     kern<<<grid, FNT, sizeof(IvfFlatSmem), s>>>(metric, cos_small, static_cast<const T*>(q), nq, ldq, d, qv, nprobe,
-                                                eperm, eseg, static_cast<const T*>(rows), ldx, xv, list_off,
+                                                eperm, eseg, static_cast<const TX*>(rows), ldx, x_scale, xv, list_off,
                                                 list_end, nlist,
                                                 ids, k, out_v, out_i);
 }
@@ -541,6 +563,7 @@ int ivf_flat_attrs() {
     RDB_TRY(ivf_flat_smem_attr<float>(bytes));
     RDB_TRY(ivf_flat_smem_attr<__half>(bytes));
     RDB_TRY(ivf_flat_smem_attr<__nv_bfloat16>(bytes));
+    RDB_TRY((ivf_flat_smem_attr<float, int8_t>(bytes)));
     if (dev >= 0 && dev < 64) g_ivf_flat_attr[dev] = true;
     return RDB_OK;
 }
@@ -570,11 +593,17 @@ extern "C" {
 
 size_t rdb_ivf_scan_workspace(int64_t nq, int nprobe, int nlist) { return ivf_ws(nq, nprobe, nlist).bytes; }
 
-int rdb_ivf_flat_scan(int metric, int dtype, const void* q, int64_t nq, int64_t ldq, int d, const int64_t* probe,
-                      int nprobe, const void* rows, int64_t ldx, const float* xv, const int64_t* list_off,
-                      const int64_t* list_end, int nlist,
-                      const int64_t* ids, int k, float* out_v, int64_t* out_i, void* ws, size_t ws_bytes,
-                      void* stream) {
+}  // extern "C"
+
+namespace rdb {
+namespace {
+
+// x_scale != NULL: rows are SQ8 codes (int8, stride ldx bytes) with per-row
+// scales, queries fp32
+int ivf_flat_scan_impl(int metric, int dtype, const void* q, int64_t nq, int64_t ldq, int d, const int64_t* probe,
+                       int nprobe, const void* rows, int64_t ldx, const float* x_scale, const float* xv,
+                       const int64_t* list_off, const int64_t* list_end, int nlist, const int64_t* ids, int k,
+                       float* out_v, int64_t* out_i, void* ws, size_t ws_bytes, void* stream) {
     RDB_CHECK_ARG(metric >= 0 && metric <= 2, "unknown metric %d", metric);
     RDB_CHECK_ARG(elem_size(dtype) != 0, "unknown dtype %d", dtype);
     RDB_CHECK_ARG(nq >= 0 && d >= 1 && nprobe >= 1 && nlist >= 1 && nlist <= kMaxLabels, "bad shape");
@@ -607,22 +636,52 @@ int rdb_ivf_flat_scan(int metric, int dtype, const void* q, int64_t nq, int64_t 
     RDB_TRY(ivf_flat_attrs());
     cudaEvent_t stop_ev;
     RDB_TRY(timing_begin(TIMING_IVF_SCAN, s, &stop_ev));
-    switch (dtype) {
-        case RDB_F32:
-            launch_ivf_flat<float>(expand, grid, s, metric, cos_small, q, nq, ldq, d, qv, nprobe, eperm, eseg, rows,
-                                   ldx, xv, list_off, list_end, nlist, ids, k, out_v, out_i);
-            break;
-        case RDB_F16:
-            launch_ivf_flat<__half>(expand, grid, s, metric, cos_small, q, nq, ldq, d, qv, nprobe, eperm, eseg, rows,
-                                    ldx, xv, list_off, list_end, nlist, ids, k, out_v, out_i);
-            break;
-        default:
-            launch_ivf_flat<__nv_bfloat16>(expand, grid, s, metric, cos_small, q, nq, ldq, d, qv, nprobe, eperm, eseg,
-                                           rows, ldx, xv, list_off, list_end, nlist, ids, k, out_v, out_i);
+    if (x_scale) {
+        launch_ivf_flat<float, int8_t>(expand, grid, s, metric, cos_small, q, nq, ldq, d, qv, nprobe, eperm, eseg, rows,
+                                       ldx, x_scale, xv, list_off, list_end, nlist, ids, k, out_v, out_i);
+    } else {
+        switch (dtype) {
+            case RDB_F32:
+                launch_ivf_flat<float>(expand, grid, s, metric, cos_small, q, nq, ldq, d, qv, nprobe, eperm, eseg,
+                                       rows, ldx, nullptr, xv, list_off, list_end, nlist, ids, k, out_v, out_i);
+                break;
+            case RDB_F16:
+                launch_ivf_flat<__half>(expand, grid, s, metric, cos_small, q, nq, ldq, d, qv, nprobe, eperm, eseg,
+                                        rows, ldx, nullptr, xv, list_off, list_end, nlist, ids, k, out_v, out_i);
+                break;
+            default:
+                launch_ivf_flat<__nv_bfloat16>(expand, grid, s, metric, cos_small, q, nq, ldq, d, qv, nprobe, eperm,
+                                               eseg, rows, ldx, nullptr, xv, list_off, list_end, nlist, ids, k, out_v,
+                                               out_i);
+        }
     }
     RDB_LAUNCH_CHECK();
     if (stop_ev) RDB_CUDA_TRY(cudaEventRecord(stop_ev, s));
     return RDB_OK;
+}
+
+}  // namespace
+}  // namespace rdb
+
+extern "C" {
+
+int rdb_ivf_flat_scan(int metric, int dtype, const void* q, int64_t nq, int64_t ldq, int d, const int64_t* probe,
+                      int nprobe, const void* rows, int64_t ldx, const float* xv, const int64_t* list_off,
+                      const int64_t* list_end, int nlist,
+                      const int64_t* ids, int k, float* out_v, int64_t* out_i, void* ws, size_t ws_bytes,
+                      void* stream) {
+    return ivf_flat_scan_impl(metric, dtype, q, nq, ldq, d, probe, nprobe, rows, ldx, nullptr, xv, list_off, list_end,
+                              nlist, ids, k, out_v, out_i, ws, ws_bytes, stream);
+}
+
+int rdb_ivf_flat_scan_sq8(int metric, const float* q, int64_t nq, int64_t ldq, int d, const int64_t* probe,
+                          int nprobe, const int8_t* codes, int64_t ldx, const float* scales, const float* xv,
+                          const int64_t* list_off, const int64_t* list_end, int nlist, const int64_t* ids, int k,
+                          float* out_v, int64_t* out_i, void* ws, size_t ws_bytes, void* stream) {
+    RDB_CHECK_ARG(scales != nullptr, "scales is NULL");
+    RDB_CHECK_ARG(ldx % 4 == 0, "SQ8 row stride must be a multiple of 4 bytes");
+    return ivf_flat_scan_impl(metric, RDB_F32, q, nq, ldq, d, probe, nprobe, codes, ldx, scales, xv, list_off,
+                              list_end, nlist, ids, k, out_v, out_i, ws, ws_bytes, stream);
 }
 
 int rdb_pq_encode(const float* x, int64_t n, int64_t ldx, int d, const int32_t* labels, const float* centroids,

@@ -43,6 +43,12 @@ __device__ __forceinline__ float ld_f(int dtype, const void* p, int64_t i) {
     return __half2float(static_cast<const __half*>(p)[i]);
 }
 
+// Element t of stored row r (SQ8 codes dequantised with the row's scale).
+__device__ __forceinline__ float ld_row(const RepairArgs& a, int64_t r, int t) {
+    if (a.x_i8) return __fmul_rn(a.x_scale[r], static_cast<float>(static_cast<const int8_t*>(a.x)[r * a.ldx + t]));
+    return ld_f(a.dtype, a.x, r * a.ldx + t);
+}
+
 __global__ void __launch_bounds__(NT) query_prep_kernel(int metric, int cos_small, int dtype, const void* q,
                                                         int64_t nq, int64_t ldq, int d, float* qv,
                                                         unsigned* flag) {
@@ -136,12 +142,12 @@ __global__ void __launch_bounds__(NT) flat_repair_kernel(RepairArgs a) {
                 float acc = 0.f;
                 if (a.metric == RDB_METRIC_L2) {
                     for (int t = lane; t < a.d; t += 32) {
-                        const float df = ld_f(a.dtype, a.q, q * a.ldq + t) - ld_f(a.dtype, a.x, r * a.ldx + t);
+                        const float df = ld_f(a.dtype, a.q, q * a.ldq + t) - ld_row(a, r, t);
                         acc = fmaf(df, df, acc);
                     }
                 } else {
                     for (int t = lane; t < a.d; t += 32)
-                        acc = fmaf(ld_f(a.dtype, a.q, q * a.ldq + t), ld_f(a.dtype, a.x, r * a.ldx + t), acc);
+                        acc = fmaf(ld_f(a.dtype, a.q, q * a.ldq + t), ld_row(a, r, t), acc);
                 }
 #pragma unroll
                 for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);

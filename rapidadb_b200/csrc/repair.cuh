@@ -18,6 +18,8 @@ struct RepairArgs {
     int64_t ldx;
     int d;
     int k;
+    int x_i8;                 // rows are SQ8 codes: value = fl(x_scale[row] * code)
+    const float* x_scale;
     const float* qv;  // [nq] per-query values (cosine)
     const float* xv;  // [n] per-row values (cosine)
     const unsigned* flag;    // nonzero when some list of this chunk overflowed

@@ -34,6 +34,10 @@ struct ScanArgs {
 
     const float* qv;   // [nq] per-query metric value
     const float* xv;   // per physical row metric value
+    // rows stored as SQ8 codes (int8) with a per-physical-row fp32 scale:
+    // the row value is fl(x_scale[row] * code); queries stay fp32 (dtype)
+    int x_i8;
+    const float* x_scale;
     const float* thr;  // [nq] thresholds in final-score units (NULL: accept all)
 
     // SCAN_FILTER: candidate lists [nsplit][nq][cap] + counts [nsplit][nq]

@@ -46,6 +46,15 @@ __device__ __forceinline__ float load_as_float(int dtype, const void* p, int64_t
     return __half2float(static_cast<const __half*>(p)[i]);
 }
 
+// Element t of stored (physical) row prow as a float: SQ8 codes are
+// dequantised with their row's scale (a rounded product, never fused).
+__device__ __forceinline__ float load_row_elem(const SelectArgs& a, int64_t prow, int t) {
+    if (a.x_i8)
+        return __fmul_rn(__ldg(a.x_scale + prow),
+                         static_cast<float>(static_cast<const int8_t*>(a.xdata)[prow * a.ldx + t]));
+    return load_as_float(a.dtype, a.xdata, prow * a.ldx + t);
+}
+
 __device__ __forceinline__ bool hi_eq(unsigned long long a, unsigned long long b, int top) {
     return top >= 64 ? true : ((a >> top) == (b >> top));
 }
@@ -293,7 +302,7 @@ __global__ void __launch_bounds__(NT) select_kernel(SelectArgs a) {
                 float acc = 0.f;
                 for (int t = lane; t < a.d; t += 32) {
                     float df = load_as_float(a.dtype, a.qdata, q * a.ldq + t) -
-                               load_as_float(a.dtype, a.xdata, prow * a.ldx + t);
+                               load_row_elem(a, prow, t);
                     acc = fmaf(df, df, acc);
                 }
                 for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
@@ -633,7 +642,7 @@ __global__ void __launch_bounds__(NT, 2) select_warp_kernel(SelectArgs a) {
                 float acc = 0.f;
                 for (int t = lane; t < a.d; t += 32) {
                     const float df = load_as_float(a.dtype, a.qdata, q * a.ldq + t) -
-                                     load_as_float(a.dtype, a.xdata, prow * a.ldx + t);
+                                     load_row_elem(a, prow, t);
                     acc = fmaf(df, df, acc);
                 }
 #pragma unroll

@@ -69,6 +69,8 @@ struct SelectArgs {
     const void* xdata;
     int64_t ldx;
     int d;
+    int x_i8;              // rows are SQ8 codes: value = fl(x_scale[row] * code)
+    const float* x_scale;
 };
 
 // Largest k supported by the in-shared-memory final sort.

@@ -27,6 +27,8 @@ template <>
 __device__ __forceinline__ float to_f<__half>(__half v) { return __half2float(v); }
 template <>
 __device__ __forceinline__ float to_f<__nv_bfloat16>(__nv_bfloat16 v) { return __bfloat162float(v); }
+template <>
+__device__ __forceinline__ float to_f<int8_t>(int8_t v) { return static_cast<float>(v); }
 
 // ------------------------------------------------------------ row norms --
 
@@ -73,7 +75,10 @@ static_assert(BQ == 32 && BN == 256, "thread mapping assumes 32 x 256 tiles");
 template <typename T>
 __device__ __forceinline__ float4 load4(const T* p, bool vec, int nvalid) {
     if (vec && nvalid >= 4) {
-        if constexpr (sizeof(T) == 4) {
+        if constexpr (sizeof(T) == 1) {
+            const char4 c = __ldg(reinterpret_cast<const char4*>(p));
+            return make_float4(c.x, c.y, c.z, c.w);
+        } else if constexpr (sizeof(T) == 4) {
             return __ldg(reinterpret_cast<const float4*>(p));
         } else {
             const uint2 u = __ldg(reinterpret_cast<const uint2*>(p));
@@ -129,7 +134,10 @@ __device__ __forceinline__ void finish_split(const ScanArgs& a, int64_t q0, int 
     }
 }
 
-template <typename T, int MODE, bool DIRECT_L2>
+// T: query (and row) element type; TX = int8_t: rows are SQ8 codes, each
+// dequantised as fl(x_scale[row] * code) while it is staged, so the arithmetic
+// that follows is the fp32 scan over the dequantised rows
+template <typename T, int MODE, bool DIRECT_L2, typename TX = T>
 __global__ void __launch_bounds__(NT, 2) simt_scan_kernel(ScanArgs a) {
     __shared__ __align__(16) float Qs[BK][BQ];
     __shared__ float Xs[BK][XS];
@@ -138,7 +146,7 @@ __global__ void __launch_bounds__(NT, 2) simt_scan_kernel(ScanArgs a) {
     __shared__ unsigned long long sbest[BQ];
 
     const T* __restrict__ qp = static_cast<const T*>(a.q);
-    const T* __restrict__ xp = static_cast<const T*>(a.x);
+    const TX* __restrict__ xp = static_cast<const TX*>(a.x);
     const int split = blockIdx.x;
     // query blocks run along y, continuing in z past the 65535 limit of y
     const int64_t q0 = ((int64_t)blockIdx.z * gridDim.y + blockIdx.y) * BQ;
@@ -192,8 +200,13 @@ __global__ void __launch_bounds__(NT, 2) simt_scan_kernel(ScanArgs a) {
 #pragma unroll
             for (int i = 0; i < 8; ++i) {
                 const int64_t r = r0 + sq + 32 * i;
-                px[i] = (r < r_end && nv > 0) ? load4<T>(xp + r * xstride + k, vec_x, nv)
+                px[i] = (r < r_end && nv > 0) ? load4<TX>(xp + r * xstride + k, vec_x, nv)
                                              : make_float4(0.f, 0.f, 0.f, 0.f);
+                if constexpr (sizeof(TX) == 1) {
+                    const float sc = r < r_end ? __ldg(a.x_scale + r * a.row_step) : 0.f;
+                    px[i] = make_float4(__fmul_rn(sc, px[i].x), __fmul_rn(sc, px[i].y), __fmul_rn(sc, px[i].z),
+                                        __fmul_rn(sc, px[i].w));
+                }
             }
         };
         fetch(0);
@@ -470,7 +483,7 @@ __global__ void partial_finalize_kernel(int metric, int cos_small, float* __rest
 // fp32 rows and queries whose layout suits the TMA maps (16-byte aligned
 // bases and strides, coordinates within int32)
 bool tma_scan_ok(const ScanArgs& a, int mode) {
-    if (a.dtype != RDB_F32) return false;
+    if (a.dtype != RDB_F32 || a.x_i8) return false;
     if (mode != SCAN_FILTER && mode != SCAN_ARGMIN && mode != SCAN_ARGMIN_EXACT && mode != SCAN_PARTIAL) return false;
     if ((reinterpret_cast<uintptr_t>(a.q) & 15) || (reinterpret_cast<uintptr_t>(a.x) & 15)) return false;
     if (a.ldq % 4 || (a.ldx * a.row_step) % 4) return false;
@@ -555,6 +568,13 @@ int launch_scan_simt(const ScanArgs& a, int mode, cudaStream_t s) {
         return launch_tma_typed<SCAN_ARGMIN, true>(a, grid, s);
     }
     RDB_CHECK_ARG(mode != SCAN_PARTIAL, "SCAN_PARTIAL needs fp32 operands in a TMA layout");
+    if (a.x_i8) {
+        RDB_CHECK_ARG(a.dtype == RDB_F32 && a.x_scale, "SQ8 rows need fp32 queries and per-row scales");
+        RDB_CHECK_ARG(mode == SCAN_FILTER, "SQ8 rows support the filter scan only");
+        simt_scan_kernel<float, SCAN_FILTER, false, int8_t><<<grid, NT, 0, s>>>(a);
+        RDB_LAUNCH_CHECK();
+        return RDB_OK;
+    }
     switch (a.dtype) {
         case RDB_F32: return launch_typed<float>(a, mode, s, grid);
         case RDB_F16: return launch_typed<__half>(a, mode, s, grid);

@@ -248,11 +248,16 @@ class RapidaDB:
 
 
 def _index_state(ix, it: IndexType) -> dict:
-    """Stored arrays of one extension index, in stored (list) order."""
+    """Stored arrays of one extension index, in stored (list) order; INT8
+    (SQ8) rows as their codes and scales, so a reload is exact."""
     st = {}
     if it == IndexType.FLAT:
         if ix.size():
-            st["vectors"] = ix.vectors().cpu()
+            if ix.sq8():
+                st["sq8_codes"] = ix.sq8_codes().cpu()
+                st["sq8_scales"] = ix.sq8_scales().cpu()
+            else:
+                st["vectors"] = ix.vectors().cpu()
             st["ids"] = ix.ids().cpu()
         return st
     if ix.is_trained():
@@ -262,7 +267,10 @@ def _index_state(ix, it: IndexType) -> dict:
     if ix.size():
         st["labels"] = ix.stored_labels().cpu()
         st["ids"] = ix.stored_ids().cpu()
-        if it == IndexType.IVF:
+        if it == IndexType.IVF and ix.sq8():
+            st["sq8_codes"] = ix.stored_sq8_codes().cpu()
+            st["sq8_scales"] = ix.stored_sq8_scales().cpu()
+        elif it == IndexType.IVF:
             st["vectors"] = ix.stored_vectors().cpu()
         else:
             st["codes"] = ix.stored_codes().cpu()
@@ -273,7 +281,9 @@ def _restore_index(ix, st: dict, it: IndexType, dev: torch.device) -> None:
     """Load arrays written by _index_state into an empty extension index on dev."""
     with torch.cuda.device(dev):
         if it == IndexType.FLAT:
-            if "vectors" in st:
+            if "sq8_codes" in st:
+                ix.add_sq8(st["sq8_codes"].to(dev), st["sq8_scales"].to(dev), st["ids"].to(dev))
+            elif "vectors" in st:
                 ix.add(st["vectors"].to(dev), st["ids"].to(dev))
             return
         if "centroids" in st:
@@ -281,6 +291,9 @@ def _restore_index(ix, st: dict, it: IndexType, dev: torch.device) -> None:
                 ix.set_quantizer(st["centroids"].to(dev), st["codebooks"].to(dev))
             else:
                 ix.set_quantizer(st["centroids"].to(dev))
-        if "ids" in st:
+        if "sq8_codes" in st:
+            ix.restore_sq8(st["sq8_codes"].to(dev), st["sq8_scales"].to(dev), st["labels"].to(dev),
+                           st["ids"].to(dev))
+        elif "ids" in st:
             data = st["vectors"] if it == IndexType.IVF else st["codes"]
             ix.restore(data.to(dev), st["labels"].to(dev), st["ids"].to(dev))
