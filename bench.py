@@ -100,6 +100,9 @@ def parse():
     ap.add_argument("--seed", type=int, default=42)
     ap.add_argument("--rows", type=int, default=0, help="override the workload's stored rows")
     ap.add_argument("--queries", type=int, default=0, help="override the per-GPU query batch")
+    ap.add_argument("--timeline", type=int, default=0,
+                    help="after the run, record the kernel timeline of this many headline searches (CUPTI via "
+                         "torch.profiler) and print per-kernel durations and gaps to stderr")
     ap.add_argument("--results", default="owner", choices=["owner", "replicated"],
                     help="flat search on N > 1 GPUs: each rank returns the answers of its query slice "
                          "(owner) or of the whole batch (replicated)")
@@ -544,8 +547,38 @@ def run_flat(args, wl, ctx):
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         res["cpu_baseline"] = flat_cpu_baseline(x.float().cpu().numpy(), q[:256].float().cpu().numpy(), wl,
                                                 args.cpu_seconds)
+    if args.timeline > 0 and world == 1:
+        kernel_timeline(lambda: searcher.search(q, k), args.timeline)
     del x, q, db
     return res
+
+
+def kernel_timeline(fn, n):
+    """Kernels of n calls of fn as they ran back to back (CUPTI activity
+    records through torch.profiler, no replay), after a 2 s pause: per kernel
+    its duration and the idle gap before it, printed to stderr."""
+    import torch
+    from torch.profiler import ProfilerActivity, profile
+
+    fn()
+    torch.cuda.synchronize()
+    time.sleep(2.0)
+    with profile(activities=[ProfilerActivity.CUDA]) as prof:
+        for _ in range(n):
+            fn()
+        torch.cuda.synchronize()
+    ev = sorted((e for e in prof.events() if e.device_type == torch.autograd.DeviceType.CUDA),
+                key=lambda e: e.time_range.start)
+    prev = None
+    rows = []
+    for e in ev:
+        gap = None if prev is None else e.time_range.start - prev
+        rows.append({"kernel": e.name[:80], "us": round(e.time_range.elapsed_us(), 1),
+                     "gap_before_us": None if gap is None else round(gap, 1)})
+        prev = e.time_range.end
+    total = (ev[-1].time_range.end - ev[0].time_range.start) if ev else 0
+    print(json.dumps({"timeline": rows, "calls": n, "us_per_call": round(total / max(n, 1), 1)}), file=sys.stderr,
+          flush=True)
 
 
 # ------------------------------------------------------------------ IVF
