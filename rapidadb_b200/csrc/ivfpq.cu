@@ -207,27 +207,29 @@ __global__ void __launch_bounds__(SNT, (M <= 32 ? 2 : 1)) ivfpq_search_kernel(
             for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(FULL, s, o);
             if (lane == 0) t1[p] = s;
         }
-        // QT[m][j] = -2 <q_m, cb[m][j]>: one table row (group g, code j) per
-        // warp step; lane t < G computes entry g G + t, lane L stores words L
-        // and L + 32
+        // QT[m][j] = -2 <q_m, cb[m][j]>: every thread computes whole entries
+        // (entry e = j M + m, so the lanes of a warp cover the M subquantisers
+        // of consecutive codes and their table stores fall in distinct
+        // banks), the dsub codebook loads of an entry independent of each
+        // other; entry (m, j) fills its 2 NC words of table row j of group
+        // m / G (word w holds position (w / NC) mod G)
         float amax = 0.f;
-        for (int rr = warp; rr < L::NG * ksub; rr += SNW) {
-            const int g = rr / ksub, j = rr - g * ksub;
-            float val = 0.f;
-            if (lane < L::G) {
-                const int m = g * L::G + lane;
-                const float* cbp = codebooks + (static_cast<int64_t>(m) * ksub + j) * dsub;
-                const float* qp = qs + m * dsub;
-                float s = 0.f;
-                for (int u = 0; u < dsub; ++u) s = fmaf(qp[u], __ldg(cbp + u), s);
-                val = -2.f * s;
-            }
+#pragma unroll 2
+        for (int e = tid; e < M * ksub; e += SNT) {
+            const int j = e / M, m = e - j * M;
+            const float* cbp = codebooks + (static_cast<int64_t>(m) * ksub + j) * dsub;
+            const float* qp = qs + m * dsub;
+            float s = 0.f;
+            for (int u = 0; u < dsub; ++u) s = fmaf(qp[u], __ldg(cbp + u), s);
+            const float val = -2.f * s;
             amax = fmaxf(amax, fabsf(val));
+            const int g = m / L::G, t = m - g * L::G;
             uint32_t* row = lut + g * kGroupWords + j * kRowWords;
-            const float lo = __shfl_sync(FULL, val, (lane / L::NC) % L::G);
-            const float hi = __shfl_sync(FULL, val, ((lane + 32) / L::NC) % L::G);
-            row[lane] = __float_as_uint(lo);
-            row[lane + 32] = __float_as_uint(hi);
+#pragma unroll
+            for (int c = 0; c < L::NC; ++c) {
+                row[L::NC * t + c] = __float_as_uint(val);
+                row[L::NC * (t + L::G) + c] = __float_as_uint(val);
+            }
         }
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(FULL, amax, o));
