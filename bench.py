@@ -677,10 +677,13 @@ def run_ivf(args, wl, ctx, name, steps, warmup):
     probes = searcher.probe(q)
     scanned = float(sizes[probes.flatten()].sum().item())  # rows of this rank's probed list slices
     bpr = wl["M"] if pq else d * 4
+    tc = (not pq) and idx.tensor_core_search(k)
+    # the tensor-core scan reads each probed list's rows once per search
+    list_rows = float(sizes[torch.unique(probes.flatten())].sum().item())
     res = None
     if rank == 0:
         hbm, _, _, src = peaks()
-        alg_bytes = scanned * bpr
+        alg_bytes = (list_rows if tc else scanned) * bpr
         kern_ms = t["kernel_ms"]
         ach = alg_bytes / (kern_ms * 1e-3) / 1e9 if kern_ms > 0 else None
         ms = t["ms"]
@@ -705,12 +708,16 @@ def run_ivf(args, wl, ctx, name, steps, warmup):
             "roofline": {"bound": "hbm", "achieved": round(ach, 1) if ach else None, "peak": hbm, "unit": "GB/s",
                          "frac": round(ach / hbm, 4) if ach else None, "traffic": None,
                          "kernel": ("ivfpq_search_kernel<%d> (query-major)" % wl["M"] if idx.query_major()
-                                    else "ivfpq_scan_kernel") if pq else "ivf_flat_scan_kernel",
+                                    else "ivfpq_scan_kernel") if pq else (
+                                        "ivf_tc_scan_kernel (tcgen05)" if tc else "ivf_flat_scan_kernel"),
                          "kernel_ms": round(kern_ms, 4), "bytes_per_launch": alg_bytes,
                          "algorithmic_unit": (
                              "M code bytes per (query, probed row): sum over (query, probed list) of the list's "
                              "code bytes on this GPU; lists probed by queries running at the same time are "
                              "served from L2, so frac may exceed 1" if pq else
+                             "d x 4 B per stored row of every list probed by at least one query: the tensor-core "
+                             "scan reads each probed list's fp16 hi / lo planes (as many bytes as the fp32 rows) "
+                             "once per 128 probing queries of the list" if tc else
                              "d x 4 B per (query, probed row): sum over (query, probed list) of the list's row "
                              "bytes on this GPU; the list-major scan reads a list once per 32-query chunk, so "
                              "frac is far above 1 and the contraction rate bounds it"),

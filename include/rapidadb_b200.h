@@ -276,6 +276,37 @@ int rdb_ivf_flat_scan_sq8(int metric, const float* q, int64_t nq, int64_t ldq, i
                           const int64_t* list_off, const int64_t* list_end, int nlist, const int64_t* ids, int k,
                           float* out_v, int64_t* out_i, void* ws, size_t ws_bytes, void* stream);
 
+/* fp32 rows as two fp16 planes for the tensor-core IVF search: per row a
+ * power-of-two scale 2^e (largest |x_t| 2^-e in [2^13, 2^14); 1 for a zero
+ * row), hi = fp16(x 2^-e), lo = fp16(x 2^-e - hi); hi / lo [n, ldp] fp16,
+ * columns d .. ldp - 1 zero; scale [n].  *flag (may be NULL) gets bit 0 when a
+ * value is not finite (such rows must be searched with rdb_ivf_flat_scan).
+ * ldp a multiple of 8. */
+int rdb_f16_split(const float* x, int64_t n, int64_t ldx, int d, void* hi, void* lo, int64_t ldp, float* scale,
+                  unsigned* flag, void* stream);
+
+/* IVF-Flat search of fp32 rows on the tensor cores (no counterpart in the
+ * reference, whose IVF search ranks with CUDA-core distances): the list scan
+ * of rdb_ivf_flat_scan as a tcgen05 contraction of each list's probing
+ * queries with its rows (the rows' rdb_f16_split planes, three fp16 products
+ * per element into fp32), ranking the best k + 8 rows per (query, probe
+ * slot); per query the best k + 8 of those are scored again with
+ * rdb_ivf_flat_scan's arithmetic on the fp32 rows, so scores equal the
+ * CUDA-core scan's.  Output out_v / out_i [nq, k]: the merged answer (best
+ * first, ties to the lower stored row, ids[row] or -1 padding), no
+ * rdb_topk_merge step.  rows / xv / list_off / list_end / ids as
+ * rdb_ivf_flat_scan (xv required for L2 and cosine: |x|^2, resp. the norm);
+ * rows_hi / rows_lo [nrows, ldp] and row_scale [nrows] from rdb_f16_split of
+ * the same rows, ldp = d rounded up to a multiple of 64, 16-byte aligned.
+ * Supported for d <= 128 and k <= 24 (rdb_ivf_flat_search_tc_supported). */
+int rdb_ivf_flat_search_tc_supported(int d, int k);
+size_t rdb_ivf_flat_search_tc_workspace(int64_t nq, int nprobe, int nlist, int d, int k);
+int rdb_ivf_flat_search_tc(int metric, const float* q, int64_t nq, int64_t ldq, int d, const int64_t* probe,
+                           int nprobe, const float* rows, int64_t ldx, const float* xv, const void* rows_hi,
+                           const void* rows_lo, const float* row_scale, int64_t ldp, int64_t nrows,
+                           const int64_t* list_off, const int64_t* list_end, int nlist, const int64_t* ids, int k,
+                           float* out_v, int64_t* out_i, void* ws, size_t ws_bytes, void* stream);
+
 /* rdb_ivf_flat_scan for callers that may not allocate GPU memory (no
  * counterpart in the reference): the same list-major scan and the same
  * results, with its scratch taken from an 8 MiB array compiled into the

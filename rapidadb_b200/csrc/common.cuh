@@ -53,6 +53,8 @@ unsigned* host_words();
 
 int num_sms();
 size_t elem_size(int dtype);
+// |x_i|^2 over the first d columns of n rows with a stride of ld elements
+int row_sqnorms_ld(int dtype, const void* x, int64_t n, int d, int64_t ld, float* out, cudaStream_t s);
 
 // Optional CUDA-event timing of selected kernel launches (rdb_timing_*):
 // when the launch's tag is enabled, timing_begin records a start event on the

@@ -530,12 +530,7 @@ int rdb_flat_sample_maxima(int metric, int dtype, const void* q, int64_t nq, int
         return set_error(RDB_ERR_UNSUPPORTED, "sample maxima need fp16 / bf16 rows with 16-byte aligned strides");
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     float* qv = static_cast<float*>(ws);
-    if (ldq == d) {
-        RDB_TRY(rdb_row_sqnorms(dtype, q, nq, d, qv, s));
-    } else {
-        for (int64_t i = 0; i < nq; ++i)
-            RDB_TRY(rdb_row_sqnorms(dtype, static_cast<const char*>(q) + i * ldq * elem_size(dtype), 1, d, qv + i, s));
-    }
+    RDB_TRY(row_sqnorms_ld(dtype, q, nq, d, ldq, qv, s));
     RDB_TRY(rdb_vec_values(metric, d, qv, nq, qv, s));
     const bool pair = tc_use_pair(nq);
     const int qtile = pair ? 2 * kTcQueries : kTcQueries;

@@ -185,6 +185,10 @@ PYBIND11_MODULE(_C, m) {
         .def("stored_sq8_scales", &IVFFlatIndex::stored_sq8_scales)
         .def("restore_sq8", &IVFFlatIndex::restore_sq8, py::arg("codes"), py::arg("scales"), py::arg("labels"),
              py::arg("ids"), py::call_guard<py::gil_scoped_release>())
+        .def("set_tensor_cores", &IVFFlatIndex::set_tensor_cores, py::arg("on"),
+             py::call_guard<py::gil_scoped_release>())
+        .def("tensor_cores", &IVFFlatIndex::tensor_cores)
+        .def("tensor_core_search", &IVFFlatIndex::tensor_core_search, py::arg("k"))
         .def("__len__", &IVFFlatIndex::size)
         .def("__repr__", [](const IVFFlatIndex& s) {
             return "IVFFlatIndex(dim=" + std::to_string(s.dim()) + ", nlist=" + std::to_string(s.nlist()) +

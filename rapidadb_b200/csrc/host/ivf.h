@@ -122,13 +122,32 @@ class IVFFlatIndex : public IVFBase {
     at::Tensor stored_sq8_scales() const;
     void restore_sq8(const at::Tensor& codes, const at::Tensor& scales, const at::Tensor& labels,
                      const at::Tensor& ids);
+    // Tensor-core search (rdb_ivf_flat_search_tc) of FP32 rows with dim <= 128
+    // and k <= 24, on by default: the index keeps fp16 hi / lo planes of its rows
+    // (rdb_f16_split, as many bytes again as the rows).  Off frees them and
+    // searches with the CUDA-core list scan (rdb_ivf_flat_scan).
+    void set_tensor_cores(bool on);
+    bool tensor_cores() const { return tc_wanted_; }
+    // true when search(queries, k) runs on the tensor cores
+    bool tensor_core_search(int64_t k) const;
 
   private:
+    bool tc_rows() const;  // planes kept: FP32 rows, dim <= 128, switched on
+    // planes (hi, lo, scale) of fp32 rows [m, ld_]; a value that is not
+    // finite sets tc_bad_ (those rows are searched on CUDA cores)
+    std::tuple<at::Tensor, at::Tensor, at::Tensor> split_rows(const at::Tensor& rows);
+    void rebuild_planes();
+
     Precision precision_;
     int64_t ld_;
     at::Tensor rows_;    // [cap, ld] slots list by list, storage dtype (free slots zero)
     at::Tensor xv_;      // [cap]
     at::Tensor scales_;  // [cap] SQ8 row scales (INT8 storage only)
+    bool tc_wanted_ = true;
+    bool tc_bad_ = false;  // some stored value is not finite
+    int64_t dp_ = 0;       // plane stride: dim rounded up to 64
+    at::Tensor hi_, lo_;   // [cap, dp_] fp16 planes of rows_ (tensor-core search)
+    at::Tensor rscale_;    // [cap] their power-of-two row scales
 };
 
 class IVFPQIndex : public IVFBase {

@@ -309,6 +309,44 @@ constexpr int64_t kIvfExpandRowsPerList = 768;
 IVFFlatIndex::IVFFlatIndex(int dim, Metric metric, int nlist, int nprobe, Precision precision)
     : IVFBase(dim, metric, nlist, nprobe), precision_(precision) {
     ld_ = padded_ld(dim, storage_type(precision));
+    dp_ = (dim + 63) / 64 * 64;
+}
+
+bool IVFFlatIndex::tc_rows() const {
+    return tc_wanted_ && precision_ == Precision::FP32 && rdb_ivf_flat_search_tc_supported(dim_, 1);
+}
+
+bool IVFFlatIndex::tensor_core_search(int64_t k) const {
+    return tc_rows() && !tc_bad_ && hi_.defined() && k >= 1 && k <= 32 &&
+           rdb_ivf_flat_search_tc_supported(dim_, static_cast<int>(k)) != 0;
+}
+
+std::tuple<at::Tensor, at::Tensor, at::Tensor> IVFFlatIndex::split_rows(const at::Tensor& rows) {
+    const int64_t m = rows.size(0);
+    auto opt = rows.options();
+    at::Tensor hi = at::empty({m, dp_}, opt.dtype(at::kHalf));
+    at::Tensor lo = at::empty({m, dp_}, opt.dtype(at::kHalf));
+    at::Tensor sc = at::empty({m}, opt.dtype(at::kFloat));
+    at::Tensor flag = at::zeros({1}, opt.dtype(at::kInt));
+    check_status(rdb_f16_split(rows.data_ptr<float>(), m, rows.stride(0), dim_, hi.data_ptr(), lo.data_ptr(), dp_,
+                               sc.data_ptr<float>(), reinterpret_cast<unsigned*>(flag.data_ptr<int>()), stream_ptr()),
+                 "f16 split");
+    if (flag.item<int>() != 0) tc_bad_ = true;
+    return {hi, lo, sc};
+}
+
+void IVFFlatIndex::rebuild_planes() {
+    hi_ = lo_ = rscale_ = at::Tensor();
+    tc_bad_ = false;
+    if (!tc_rows() || !rows_.defined() || rows_.size(0) == 0) return;
+    std::tie(hi_, lo_, rscale_) = split_rows(rows_);
+}
+
+void IVFFlatIndex::set_tensor_cores(bool on) {
+    tc_wanted_ = on;
+    c10::cuda::OptionalCUDAGuard guard;
+    if (rows_.defined()) guard.set_device(rows_.device());
+    rebuild_planes();
 }
 
 void IVFFlatIndex::add(const at::Tensor& vectors, const at::Tensor& ids) {
@@ -333,12 +371,21 @@ void IVFFlatIndex::add(const at::Tensor& vectors, const at::Tensor& ids) {
         xv_new = row_values(metric_, rows_new, dim_);
     }
     TORCH_CHECK(n_ + m < (int64_t(1) << 32), "at most 2^32 - 1 rows per device");
+    // fp16 planes of the new rows (tensor-core search), moved like the rows
+    const bool planes = tc_rows() && (n_ == 0 || hi_.defined());
+    at::Tensor hi_new, lo_new, rs_new;
+    if (planes) std::tie(hi_new, lo_new, rs_new) = split_rows(rows_new);
     at::Tensor dest;
     if (append_slots(lab, dest)) {
         // every list had room: rows go to free slots, nothing else moves
         rows_.index_copy_(0, dest, rows_new);
         xv_.index_copy_(0, dest, xv_new);
         if (sq8()) scales_.index_copy_(0, dest, sc_new);
+        if (planes) {
+            hi_.index_copy_(0, dest, hi_new);
+            lo_.index_copy_(0, dest, lo_new);
+            rscale_.index_copy_(0, dest, rs_new);
+        }
         ids_.index_copy_(0, dest, nid);
         labels_.index_copy_(0, dest, lab.to(at::kInt));
         return;
@@ -350,10 +397,18 @@ void IVFFlatIndex::add(const at::Tensor& vectors, const at::Tensor& ids) {
     at::Tensor old_sc = had && sq8() ? live_select(scales_) : at::Tensor();
     at::Tensor old_ids = had ? stored_ids() : at::Tensor();
     at::Tensor old_lab = had ? stored_labels() : at::Tensor();
+    at::Tensor old_hi = had && planes ? live_select(hi_) : at::Tensor();
+    at::Tensor old_lo = had && planes ? live_select(lo_) : at::Tensor();
+    at::Tensor old_rs = had && planes ? live_select(rscale_) : at::Tensor();
     new_layout(lab, dest);
     rows_ = relayout(old_rows, rows_new, dest, cap_, 0.0);
     xv_ = relayout(old_xv, xv_new, dest, cap_, 0.0);
     if (sq8()) scales_ = relayout(old_sc, sc_new, dest, cap_, 0.0);
+    if (planes) {
+        hi_ = relayout(old_hi, hi_new, dest, cap_, 0.0);
+        lo_ = relayout(old_lo, lo_new, dest, cap_, 0.0);
+        rscale_ = relayout(old_rs, rs_new, dest, cap_, 1.0);
+    }
     ids_ = relayout(old_ids, nid, dest, cap_, -1.0);
     labels_ = relayout(old_lab, lab.to(at::kInt), dest, cap_, -1.0);
 }
@@ -377,6 +432,7 @@ void IVFFlatIndex::restore(const at::Tensor& vectors, const at::Tensor& labels, 
         xv_ = row_values(metric_, rows_, dim_);
     }
     restore_lists(labels, ids);
+    rebuild_planes();
 }
 
 void IVFFlatIndex::restore_sq8(const at::Tensor& codes, const at::Tensor& scales, const at::Tensor& labels,
@@ -434,6 +490,20 @@ Result IVFFlatIndex::search_probed(const at::Tensor& queries, const at::Tensor& 
     at::Tensor q = sq8() ? prepare_rows(qd, at::kFloat, padded_ld(dim_, at::kFloat))
                          : prepare_rows(qd, rows_.scalar_type(), ld_);
     const int64_t nq = q.size(0);
+    if (tensor_core_search(k)) {
+        at::Tensor ov = at::empty({nq, k}, q.options().dtype(at::kFloat));
+        at::Tensor oi = at::empty({nq, k}, q.options().dtype(at::kLong));
+        at::Tensor tws = ws_bytes(q, rdb_ivf_flat_search_tc_workspace(nq, np, nlist_, dim_, static_cast<int>(k)));
+        check_status(rdb_ivf_flat_search_tc(static_cast<int>(metric_), q.data_ptr<float>(), nq, ld_, dim_,
+                                            probe_lists.data_ptr<int64_t>(), np, rows_.data_ptr<float>(), ld_,
+                                            xv_.data_ptr<float>(), hi_.data_ptr(), lo_.data_ptr(),
+                                            rscale_.data_ptr<float>(), dp_, cap_, list_off_.data_ptr<int64_t>(),
+                                            list_end_.data_ptr<int64_t>(), nlist_, ids_.data_ptr<int64_t>(),
+                                            static_cast<int>(k), ov.data_ptr<float>(), oi.data_ptr<int64_t>(),
+                                            tws.data_ptr(), tws.numel(), stream_ptr()),
+                     "ivf tensor-core search");
+        return {ov, oi};
+    }
     at::Tensor cv = at::empty({np, nq, k}, q.options().dtype(at::kFloat));
     at::Tensor ci = at::empty({np, nq, k}, q.options().dtype(at::kLong));
     at::Tensor ws = ws_bytes(q, rdb_ivf_scan_workspace(nq, np, nlist_));
@@ -467,6 +537,8 @@ void IVFFlatIndex::reset() {
     rows_ = at::Tensor();
     xv_ = at::Tensor();
     scales_ = at::Tensor();
+    hi_ = lo_ = rscale_ = at::Tensor();
+    tc_bad_ = false;
 }
 
 // ----------------------------------------------------------------- IVF-PQ

@@ -20,6 +20,7 @@
 
 #include <algorithm>
 
+#include "ivf.cuh"
 #include "scan.cuh"
 #include "sort.cuh"
 
@@ -496,9 +497,7 @@ __global__ void __launch_bounds__(PNT) ivfpq_scan_kernel(
     }
 }
 
-struct IvfWs {
-    size_t off_lab, off_perm, off_seg, off_qv, off_sort, bytes;
-};
+}  // namespace
 
 IvfWs ivf_ws(int64_t Q, int nprobe, int nlist) {
     IvfWs w;
@@ -529,6 +528,8 @@ int invert_probes(const int64_t* probe, int64_t Q, int nprobe, int nlist, const 
                       reinterpret_cast<int64_t*>(base + w.off_perm), nullptr, base + w.off_sort,
                       label_sort_workspace(ne, nlist), s);
 }
+
+namespace {
 
 template <typename T, typename TX = T>
 int ivf_flat_smem_attr(int bytes) {
@@ -621,11 +622,7 @@ int ivf_flat_scan_impl(int metric, int dtype, const void* q, int64_t nq, int64_t
     const bool expand = metric != RDB_METRIC_L2 || (k <= kL2ExpandMaxK && xv != nullptr);
     if (metric == RDB_METRIC_COSINE || (metric == RDB_METRIC_L2 && expand)) {
         RDB_CHECK_ARG(xv, "cosine needs per-row values");
-        if (ldq == d) {
-            RDB_TRY(rdb_row_sqnorms(dtype, q, nq, d, qv, s));
-        } else {
-            RDB_TRY(rdb_row_sqnorms(dtype, q, nq, (int)ldq, qv, s));
-        }
+        RDB_TRY(row_sqnorms_ld(dtype, q, nq, d, ldq, qv, s));
         if (metric == RDB_METRIC_COSINE) RDB_TRY(rdb_vec_values(metric, d, qv, nq, qv, s));
     }
     // x: lists; y: CTAs sharing a list's query chunks, ~4x the mean chunk count

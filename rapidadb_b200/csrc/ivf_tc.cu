@@ -1,0 +1,1017 @@
+// IVF-Flat list scan on the tcgen05 tensor cores, for fp32 rows with d <= 128.
+//
+// The CUDA-core list scan (ivf.cu) is a contraction of each list's probing
+// queries with the list's rows; here the contraction runs on the tensor cores
+// with fp32-level accuracy and the ranking stays exact:
+//
+//   operands   every fp32 value v of a row (or query) is scaled by a power of
+//              two 2^-e (e per row, per query: max |v| 2^-e in [2^13, 2^14),
+//              an exact scaling) and split into two fp16 planes,
+//              hi = fp16(v 2^-e), lo = fp16(v 2^-e - hi), about 22 significant
+//              bits; rows are split once after adds (rdb_f16_split), the
+//              probing queries per search, gathered entry by entry (entries =
+//              (query, probe slot) pairs grouped by list).
+//   contraction q.x ~ 2^(eq + ex) (qh.xh + qh.xl + ql.xh): three
+//              tcgen05.mma.kind::f16 per 16-wide K step into an fp32 TMEM
+//              accumulator (relative error about 1e-6 of sum |q_i x_i|, below
+//              the rounding of an fp32 dot product of length 128).
+//   ranking    per entry the best kk = k + 8 rows of the list by that value
+//              (L2: |x|^2 - 2 q.x, cosine: the reference's final score, dot:
+//              q.x), written to the entry's (query, probe slot) list.
+//   answer     ivf_tc_finish_kernel merges a query's nprobe lists into its
+//              best kk by ranking value, scores those rows again on CUDA cores
+//              with the CUDA-core scan's arithmetic (L2 summed directly as
+//              sum (q - x)^2, dot products accumulated in dimension order) and
+//              writes the best k, ties to the lower stored row: the merged
+//              [nq, k] answer (no per-probe lists, no separate merge).
+//
+// Work is handed out in units of (list, chunk of 128 entries): a one-block
+// kernel lists them, and each CTA of the persistent scan (one per SM) takes
+// the next unit from a global counter, so long lists and lists probed by many
+// queries spread over the SMs.  Scan kernel roles:
+//   warp 0      TMA producer: takes units, publishes them to the other roles
+//               through a 4-slot shared-memory queue; loads the unit's query
+//               chunk (both planes, whole K) once into a resident buffer, then
+//               the list's rows in tiles of 256 through a two-stage ring (both
+//               planes of one 64-wide K block per stage); SWIZZLE_128B, no
+//               multicast.
+//   warp 1      allocates 512 TMEM columns (two 128 x 256 accumulators); one
+//               lane issues the MMAs and commits stage / accumulator / buffer
+//               releases.
+//   warps 2-9   epilogue, two warps per TMEM lane quadrant (32 entries): each
+//               reads half of a tile's columns, 32 at a time, into the quad's
+//               shared block (entry-major, XOR-swizzled), and after a pair
+//               barrier ranks 16 of the quad's entries over all 64 columns
+//               with lane = column: a ballot against the entry's kk-th value,
+//               and each passing column inserted into the entry's list, held
+//               across the warp (lane i: i-th best) -- one shuffle step per
+//               insertion.
+// Every mbarrier wait is bounded (mbar_wait): a role that gives up sets the
+// abort flag and a status bit, and the CTA frees its TMEM and exits.
+#include <cuda_fp16.h>
+
+#include <algorithm>
+
+#include "ivf.cuh"
+#include "sort.cuh"
+#include "tc_common.cuh"
+
+namespace rdb {
+namespace {
+
+constexpr int TQ = 128;       // entries per task (UMMA M)
+constexpr int TR = 256;       // rows per tile (UMMA N)
+constexpr int TK = 64;        // fp16 elements per K block: one 128-byte swizzle atom
+constexpr int kMaxDp = 128;   // padded dimension limit (query chunk resident in shared memory)
+constexpr int kMaxKB = kMaxDp / TK;
+constexpr int NSTAGE = 2;
+constexpr int EPIW = 8;
+constexpr int EPIT = EPIW * 32;
+constexpr int NTHR = 64 + EPIT;
+constexpr int TMEM_NCOLS = 512;
+constexpr int A_BLK = TQ * TK * 2;        // 16 KB: one plane, one K block of the query chunk
+constexpr int A_BYTES = 2 * kMaxKB * A_BLK;
+constexpr int B_PLANE = TR * TK * 2;      // 32 KB
+constexpr int STAGE_BYTES = 2 * B_PLANE;  // both planes of one K block of a row tile
+constexpr int BAR_OFF = A_BYTES + NSTAGE * STAGE_BYTES;
+constexpr int BAR_BYTES = 256;
+constexpr int UQ = 4;                        // unit hand-out slots
+constexpr int XS_OFF = BAR_OFF + BAR_BYTES;  // [2 buffers][row factor, row value][TR] per-column staging
+constexpr int GKMAX = 32;                    // group minima kept per (entry, column half)
+constexpr int MG_OFF = XS_OFF + 2 * 2 * TR * 4;  // [4 quads][32 entries][GKMAX] second half's minima
+constexpr int TH_OFF = MG_OFF + 4 * 32 * GKMAX * 4;  // [4 quads][32 entries] entry thresholds
+constexpr int SMEM_BYTES = 1024 + TH_OFF + 4 * 32 * 4;
+static_assert(SMEM_BYTES <= 232448, "shared memory over 227 KB");
+static_assert((11 + 2 * UQ) * 8 + UQ * 4 + 8 <= BAR_BYTES, "barrier region");
+constexpr int kMaxKK = 32;  // ranked rows per entry
+constexpr int kCap = 32;    // collected rows per (entry, column half)
+
+constexpr int kL2Margin = 8;
+constexpr unsigned kNoRow = 0xffffffffu;
+
+__device__ __forceinline__ void mbar_arrive_local(uint64_t* bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+__device__ __forceinline__ void epi_sync() { asm volatile("bar.sync 1, %0;" ::"n"(EPIT) : "memory"); }
+
+__device__ __forceinline__ bool epi_and(bool ok) {
+    uint32_t r;
+    asm volatile(
+        "{\n\t.reg .pred pin, pout;\n\t"
+        "setp.ne.u32 pin, %1, 0;\n\t"
+        "bar.red.and.pred pout, 1, %2, pin;\n\t"
+        "selp.u32 %0, 1, 0, pout;\n\t}"
+        : "=r"(r)
+        : "r"(ok ? 1u : 0u), "n"(EPIT)
+        : "memory");
+    return r != 0;
+}
+
+__device__ __forceinline__ void pair_sync(int quad) {
+    asm volatile("bar.sync %0, 64;" ::"r"(2 + quad) : "memory");
+}
+
+// Power-of-two scale of a vector whose largest |value| is amax: 2^e with
+// amax 2^-e in [2^13, 2^14), 1 for a zero vector.
+__device__ __forceinline__ float pow2_scale(float amax) {
+    if (!(amax > 0.f) || isinf(amax)) return 1.f;
+    int e;
+    frexpf(amax, &e);  // amax = m 2^e, m in [0.5, 1)
+    return ldexpf(1.f, e - 14 < -126 ? -126 : e - 14);  // normal, so that 1 / scale is finite
+}
+
+// One warp per vector: scale, hi / lo fp16 planes (columns d .. ldp - 1 zero).
+// flag: set when a value is not finite.
+__global__ void split_f16_kernel(const float* __restrict__ x, int64_t n, int64_t ldx, int d, __half* __restrict__ hi,
+                                 __half* __restrict__ lo, int64_t ldp, float* __restrict__ scale,
+                                 const int64_t* __restrict__ gather, int64_t gather_div, unsigned* flag) {
+    const int lane = threadIdx.x & 31;
+    const int64_t row = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    if (row >= n) return;
+    const int64_t src = gather ? gather[row] / gather_div : row;
+    const float* p = x + src * ldx;
+    float amax = 0.f;
+    bool finite = true;
+    for (int t = lane; t < d; t += 32) {
+        const float v = p[t];
+        finite &= isfinite(v);
+        amax = fmaxf(amax, fabsf(v));
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+    finite = __all_sync(0xffffffffu, finite);
+    const float s = pow2_scale(amax), inv = 1.f / s;  // exact: powers of two
+    for (int t = lane; t < (int)ldp; t += 32) {
+        const float v = t < d ? p[t] * inv : 0.f;
+        const __half h = __float2half_rn(v);
+        hi[row * ldp + t] = h;
+        lo[row * ldp + t] = __float2half_rn(v - __half2float(h));
+    }
+    if (lane == 0) {
+        scale[row] = s;
+        if (!finite && flag) atomicOr(flag, 1u);
+    }
+}
+
+struct IvfTcArgs {
+    int metric;
+    int cos_small;
+    int nkb;                  // K blocks of 64 (padded dimension / 64)
+    int kk;                   // ranked rows per entry (k + 8), <= kMaxKK
+    const int2* units;        // (list, first entry) of each unit of work
+    const int* nunits;
+    int* unit_ctr;            // next unit to hand out (zeroed by the unit-table kernel)
+    const int64_t* eseg;      // [nlist + 1] entry segments (entries sorted by list)
+    const int64_t* eperm;     // [E] entry -> query * nprobe + slot
+    int nprobe;
+    const int64_t* list_off;  // [nlist + 1]
+    const int64_t* list_end;  // [nlist] or NULL
+    const float* xv;          // per stored row: |x|^2 (L2), norm (cosine)
+    const float* row_scale;   // per stored row: 2^ex
+    const float* qv;          // per query: norm (cosine)
+    const float* ent_scale;   // per entry: 2^eq
+    float* cand_v;            // [nq * nprobe][2][kCap] ranking values, by (query, slot), column half
+    uint32_t* cand_r;         // [nq * nprobe][2][kCap] stored rows
+    int* cand_n;              // [nq * nprobe][2] rows collected (> kCap: overflow, the list is rescanned)
+};
+
+// (v, r) before (w, s): smaller value first, then the lower row
+__device__ __forceinline__ bool before(float v, uint32_t r, float w, uint32_t s) {
+    return v < w || (v == w && r < s);
+}
+
+// The units of work of one search: each list's entries in chunks of TQ, in
+// list order; one block.  Also zeroes the hand-out counter.
+__global__ void __launch_bounds__(1024) ivf_tc_units_kernel(const int64_t* __restrict__ eseg, int nlist,
+                                                            int2* __restrict__ units, int* nunits, int* ctr) {
+    __shared__ int part[1024];
+    const int tid = threadIdx.x;
+    const int per = (nlist + 1023) / 1024;
+    const int l0 = min(nlist, tid * per), l1 = min(nlist, l0 + per);
+    int s = 0;
+    for (int l = l0; l < l1; ++l) s += static_cast<int>((eseg[l + 1] - eseg[l] + TQ - 1) / TQ);
+    part[tid] = s;
+    __syncthreads();
+    for (int o = 1; o < 1024; o <<= 1) {
+        const int v = tid >= o ? part[tid - o] : 0;
+        __syncthreads();
+        part[tid] += v;
+        __syncthreads();
+    }
+    int u = part[tid] - s;
+    for (int l = l0; l < l1; ++l)
+        for (int64_t e = eseg[l]; e < eseg[l + 1]; e += TQ) units[u++] = make_int2(l, static_cast<int>(e));
+    if (tid == 1023) {
+        *nunits = part[1023];
+        *ctr = 0;
+    }
+}
+
+// Ranking value from the tensor-core dot (smaller = better): L2 |x|^2 - 2 q.x,
+// cosine minus the reference's final score, dot minus q.x.
+template <int METRIC>
+__device__ __forceinline__ float rank_key(float dot, float xv, float qv, int cos_small) {
+    if (METRIC == RDB_METRIC_L2) return fmaf(-2.f, dot, xv);
+    if (METRIC == RDB_METRIC_COSINE) return -final_score(RDB_METRIC_COSINE, cos_small, dot, qv, xv);
+    return -dot;
+}
+
+// Group of rows per minimum in the threshold pass: the largest power of two
+// <= 32 that leaves at least 4 kk groups in the list (1 for short lists), so
+// that the kk-th smallest minimum sits close to the kk-th smallest value.
+__device__ __forceinline__ int group_rows(int64_t n, int kk) {
+    int s = 32;
+    while (s > 1 && n < static_cast<int64_t>(s) * 4 * kk) s >>= 1;
+    return s;
+}
+
+// Insert v into the ascending list tv[GK] (values only), dropping the last.
+template <int GK>
+__device__ __forceinline__ void insert_sorted(float (&tv)[GK], float v) {
+    int p = 0;
+#pragma unroll
+    for (int i = 0; i < GK; ++i) p += tv[i] <= v ? 1 : 0;
+#pragma unroll
+    for (int i = GK - 1; i > 0; --i) tv[i] = i > p ? tv[i - 1] : (i == p ? v : tv[i]);
+    tv[0] = p == 0 ? v : tv[0];
+}
+
+template <int GK>
+__device__ __forceinline__ float pick_gk(const float (&tv)[GK], int i) {
+    float r = tv[0];
+#pragma unroll
+    for (int j = 1; j < GK; ++j) r = j == i ? tv[j] : r;
+    return r;
+}
+
+template <int METRIC, int GK>
+__global__ void __launch_bounds__(NTHR, 1)
+    ivf_tc_scan_kernel(const __grid_constant__ CUtensorMap mqh, const __grid_constant__ CUtensorMap mql,
+                       const __grid_constant__ CUtensorMap mxh, const __grid_constant__ CUtensorMap mxl,
+                       const IvfTcArgs a, const uint32_t idesc, unsigned* status) {
+    extern __shared__ uint8_t ivf_tc_smem[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(ivf_tc_smem) + 1023) & ~uintptr_t(1023));
+    uint8_t* abuf = smem;
+    uint8_t* ring = smem + A_BYTES;
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + BAR_OFF);
+    uint64_t* empty = full + NSTAGE;
+    uint64_t* tfull = empty + NSTAGE;
+    uint64_t* tempty = tfull + 2;
+    uint64_t* afull = tempty + 2;
+    uint64_t* aempty = afull + 1;
+    uint64_t* mma_done = aempty + 1;
+    uint64_t* ufull = mma_done + 1;
+    uint64_t* uempty = ufull + UQ;
+    volatile int* unit_slot = reinterpret_cast<volatile int*>(uempty + UQ);
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(const_cast<int*>(unit_slot) + UQ);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+    float* xs_s = reinterpret_cast<float*>(smem + XS_OFF);  // [2][2][TR]: row factor, row value
+    float* mg_s = reinterpret_cast<float*>(smem + MG_OFF);
+    float* th_s = reinterpret_cast<float*>(smem + TH_OFF);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < NSTAGE; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        for (int c = 0; c < 2; ++c) {
+            mbar_init(&tfull[c], 1);
+            mbar_init(&tempty[c], EPIW);
+        }
+        for (int s = 0; s < UQ; ++s) {
+            mbar_init(&ufull[s], 1);
+            mbar_init(&uempty[s], 1 + EPIW);
+        }
+        mbar_init(afull, 1);
+        mbar_init(aempty, 1);
+        mbar_init(mma_done, 1);
+        *abort_flag = 0;
+        fence_barrier_init();
+        tma_prefetch_desc(&mqh);
+        tma_prefetch_desc(&mql);
+        tma_prefetch_desc(&mxh);
+        tma_prefetch_desc(&mxl);
+    }
+    if (warp == 1) {
+        tmem_alloc_t<false>(tmem_slot, TMEM_NCOLS);
+        tmem_relinquish_t<false>();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+    const int nkb = a.nkb;
+    const int nunits = *a.nunits;
+
+    // the list range of unit u: rows [r0, r1), entries [ec, e1); its row tiles
+    auto unit_info = [&](int u, int64_t& r0, int64_t& r1, int64_t& ec, int64_t& e1) {
+        const int2 un = a.units[u];
+        const int l = un.x;
+        ec = un.y;
+        e1 = min(a.eseg[l + 1], ec + TQ);
+        r0 = a.list_off[l];
+        r1 = a.list_end ? a.list_end[l] : a.list_off[l + 1];
+        return r1 > r0 ? static_cast<int>((r1 - r0 + TR - 1) / TR) : 0;
+    };
+
+    if (warp == 0) {
+        if (lane == 0) {
+            // ------------------------------------------------ TMA producer
+            // each unit's row tiles twice: threshold pass, then collecting pass
+            int stage = 0;
+            uint32_t phase = 0, at = 0, ui = 0;
+            uint32_t issued_mask = 0, issued_phase = 0;
+            bool a_pending = false, ok = true;
+            for (;;) {
+                int u = atomicAdd(a.unit_ctr, 1);
+                if (u >= nunits) u = -1;
+                const int s = static_cast<int>(ui % UQ);
+                if (!mbar_wait(&uempty[s], ((ui / UQ) & 1) ^ 1, abort_flag)) {
+                    ok = false;
+                    break;
+                }
+                unit_slot[s] = u;
+                mbar_arrive_local(&ufull[s]);
+                ++ui;
+                if (u < 0) break;
+                int64_t r0, r1, ec, e1;
+                const int ntiles = unit_info(u, r0, r1, ec, e1);
+                if (ntiles == 0) continue;
+                if (!mbar_wait(aempty, (at & 1) ^ 1, abort_flag)) {
+                    ok = false;
+                    break;
+                }
+                mbar_arrive_expect_tx(afull, 2 * nkb * A_BLK);
+                for (int kb = 0; kb < nkb; ++kb) {
+                    tma_load_2d(&mqh, afull, abuf + kb * A_BLK, kb * TK, static_cast<int>(ec));
+                    tma_load_2d(&mql, afull, abuf + (kMaxKB + kb) * A_BLK, kb * TK, static_cast<int>(ec));
+                }
+                a_pending = true;
+                ++at;
+                for (int t2 = 0; t2 < 2 * ntiles && ok; ++t2) {
+                    const int t = t2 < ntiles ? t2 : t2 - ntiles;
+                    const int row0 = static_cast<int>(r0 + static_cast<int64_t>(t) * TR);
+                    for (int kb = 0; kb < nkb; ++kb) {
+                        if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag)) {
+                            ok = false;
+                            break;
+                        }
+                        uint8_t* sp = ring + stage * STAGE_BYTES;
+                        mbar_arrive_expect_tx(&full[stage], STAGE_BYTES);
+                        tma_load_2d(&mxh, &full[stage], sp, kb * TK, row0);
+                        tma_load_2d(&mxl, &full[stage], sp + B_PLANE, kb * TK, row0);
+                        issued_mask |= 1u << stage;
+                        issued_phase = (issued_phase & ~(1u << stage)) | (phase << stage);
+                        if (++stage == NSTAGE) {
+                            stage = 0;
+                            phase ^= 1;
+                        }
+                    }
+                }
+                if (!ok) break;
+            }
+            if (!ok) {
+                *abort_flag = 1;
+                if (status) atomicOr(status, DEV_TIMEOUT_PRODUCER);
+                // let the loads tracked by this CTA's barriers land before its
+                // shared memory is released
+                for (int s = 0; s < NSTAGE; ++s)
+                    if (issued_mask & (1u << s)) {
+                        const uint64_t t0 = globaltimer_ns();
+                        while (!mbar_try_wait(&full[s], (issued_phase >> s) & 1) &&
+                               globaltimer_ns() - t0 < kWaitLimitNs) {
+                        }
+                    }
+                if (a_pending) {
+                    const uint64_t t0 = globaltimer_ns();
+                    while (!mbar_try_wait(afull, (at - 1) & 1) && globaltimer_ns() - t0 < kWaitLimitNs) {
+                    }
+                }
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            // ---------------------------------------------------- MMA issuer
+            int stage = 0;
+            uint32_t phase = 0, at = 0, gt = 0, ui = 0;
+            bool ok = true, any = false;
+            for (;;) {
+                const int s = static_cast<int>(ui % UQ);
+                if (!mbar_wait(&ufull[s], (ui / UQ) & 1, abort_flag)) {
+                    ok = false;
+                    break;
+                }
+                const int u = unit_slot[s];
+                mbar_arrive_local(&uempty[s]);
+                ++ui;
+                if (u < 0) break;
+                int64_t r0, r1, ec, e1;
+                const int ntiles = unit_info(u, r0, r1, ec, e1);
+                if (ntiles == 0) continue;
+                if (!mbar_wait(afull, at & 1, abort_flag)) {
+                    ok = false;
+                    break;
+                }
+                ++at;
+                tc_fence_after();
+                for (int t2 = 0; t2 < 2 * ntiles && ok; ++t2, ++gt) {
+                    const int acc = gt & 1;
+                    if (!mbar_wait(&tempty[acc], ((gt >> 1) & 1) ^ 1, abort_flag)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * TR);
+                    for (int kb = 0; kb < nkb; ++kb) {
+                        if (!mbar_wait(&full[stage], phase, abort_flag)) {
+                            ok = false;
+                            break;
+                        }
+                        tc_fence_after();
+                        const uint64_t ah = make_sdesc(smem_u32(abuf + kb * A_BLK));
+                        const uint64_t al = make_sdesc(smem_u32(abuf + (kMaxKB + kb) * A_BLK));
+                        const uint32_t b_addr = smem_u32(ring + stage * STAGE_BYTES);
+                        const uint64_t bh = make_sdesc(b_addr);
+                        const uint64_t bl = make_sdesc(b_addr + B_PLANE);
+#pragma unroll
+                        for (int k = 0; k < TK / 16; ++k) {
+                            umma_f16(d_tmem, ah + 2 * k, bh + 2 * k, idesc, (kb > 0 || k > 0) ? 1u : 0u);
+                            umma_f16(d_tmem, ah + 2 * k, bl + 2 * k, idesc, 1u);
+                            umma_f16(d_tmem, al + 2 * k, bh + 2 * k, idesc, 1u);
+                        }
+                        any = true;
+                        umma_commit(&empty[stage]);
+                        if (++stage == NSTAGE) {
+                            stage = 0;
+                            phase ^= 1;
+                        }
+                    }
+                    if (ok) umma_commit(&tfull[acc]);
+                }
+                if (!ok) break;
+                umma_commit(aempty);  // the query chunk may be replaced
+            }
+            if (!ok) {
+                *abort_flag = 1;
+                if (status) atomicOr(status, DEV_TIMEOUT_MMA);
+            }
+            if (any) {
+                // every MMA this thread issued completes before TMEM is freed
+                umma_commit(mma_done);
+                const uint64_t t0 = globaltimer_ns();
+                while (!mbar_try_wait(mma_done, 0) && globaltimer_ns() - t0 < kWaitLimitNs) {
+                }
+            }
+        }
+    } else {
+        // -------------------------------------------------------- epilogue
+        // Warp (quad q, half h): thread = entry 32q + lane of the unit (TMEM
+        // lane), columns 128h .. 128h + 127 of each tile, 32 at a time.
+        const int ew = warp - 2;
+        const int quad = warp & 3;
+        const int half = ew >> 2;
+        const int etid = ew * 32 + lane;
+        const int kk = a.kk;
+        uint32_t gt = 0, ui = 0;
+        bool ok = true;
+        for (;;) {
+            const int s = static_cast<int>(ui % UQ);
+            if (!epi_and(mbar_wait(&ufull[s], (ui / UQ) & 1, abort_flag))) {
+                *abort_flag = 1;
+                if (status) atomicOr(status, DEV_TIMEOUT_EPILOGUE);
+                break;
+            }
+            const int u = unit_slot[s];
+            __syncwarp();
+            if (lane == 0) mbar_arrive_local(&uempty[s]);
+            ++ui;
+            if (u < 0) break;
+            int64_t r0, r1, ec, e1;
+            const int ntiles = unit_info(u, r0, r1, ec, e1);
+            const int64_t e = ec + quad * 32 + lane;
+            const bool evalid = e < e1;
+            float qs = 0.f, qv = 1.f;
+            int64_t pe = 0;
+            if (evalid) {
+                qs = a.ent_scale[e];
+                pe = a.eperm[e];
+                if (METRIC == RDB_METRIC_COSINE) qv = a.qv[pe / a.nprobe];
+            }
+            const bool quad_live = ec + quad * 32 < e1;  // same for both warps of the quad
+            const int gs = group_rows(r1 - r0, kk);
+            float tv[GK];  // smallest group minima of this half (ascending)
+#pragma unroll
+            for (int i = 0; i < GK; ++i) tv[i] = INFINITY;
+            float thr = INFINITY;  // the entry's threshold in the collecting pass
+            int cnt = 0;
+            float* cv = a.cand_v + (pe * 2 + half) * kCap;
+            uint32_t* cr = a.cand_r + (pe * 2 + half) * kCap;
+            // per-column factors of a tile: row scale x 2^eq applied per entry, row value
+            auto stage_cols = [&](int t, float& f, float& v) {
+                const int64_t r = r0 + static_cast<int64_t>(t) * TR + etid;
+                f = r < r1 ? __ldg(a.row_scale + r) : 0.f;
+                v = r < r1 && METRIC != RDB_METRIC_DOT ? __ldg(a.xv + r) : 0.f;
+            };
+            if (ntiles > 0) {
+                float f0, v0;
+                stage_cols(0, f0, v0);
+                xs_s[(gt & 1) * 2 * TR + etid] = f0;
+                xs_s[(gt & 1) * 2 * TR + TR + etid] = v0;
+            }
+            epi_sync();
+            for (int t2 = 0; t2 < 2 * ntiles; ++t2, ++gt) {
+                const bool collect = t2 >= ntiles;
+                const int t = collect ? t2 - ntiles : t2;
+                const int acc = gt & 1;
+                float fn = 0.f, vn = 0.f;
+                if (t2 + 1 < 2 * ntiles) stage_cols(t2 + 1 < ntiles ? t2 + 1 : t2 + 1 - ntiles, fn, vn);
+                if (collect && t == 0 && quad_live) {
+                    // threshold of each entry: kk-th smallest group minimum over both halves
+                    if (half == 1) {
+#pragma unroll
+                        for (int i = 0; i < GK; ++i) mg_s[(quad * 32 + lane) * GKMAX + i] = tv[i];
+                    }
+                    pair_sync(quad);
+                    if (half == 0) {
+                        // kk-th smallest of the two ascending lists
+                        const float* o = mg_s + (quad * 32 + lane) * GKMAX;
+                        int ia = 0, ib = 0;
+                        float kth = INFINITY;
+                        for (int r = 0; r < kk; ++r) {
+                            const float va = ia < GK ? pick_gk(tv, ia) : INFINITY;
+                            const float vb = ib < GK ? o[ib] : INFINITY;
+                            if (va <= vb) {
+                                kth = va;
+                                ++ia;
+                            } else {
+                                kth = vb;
+                                ++ib;
+                            }
+                        }
+                        th_s[quad * 32 + lane] = kth;
+                    }
+                    pair_sync(quad);
+                    thr = th_s[quad * 32 + lane];
+                }
+                if (!epi_and(mbar_wait(&tfull[acc], (gt >> 1) & 1, abort_flag))) {
+                    *abort_flag = 1;
+                    if (status) atomicOr(status, DEV_TIMEOUT_EPILOGUE);
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                const int64_t col0 = r0 + static_cast<int64_t>(t) * TR;
+                const float* fs = xs_s + acc * 2 * TR + half * (TR / 2);
+                const float* vs = fs + TR;
+                const uint32_t tbase = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) +
+                                       static_cast<uint32_t>(acc * TR + half * (TR / 2));
+                if (quad_live) {
+#pragma unroll 1
+                    for (int c = 0; c < TR / 2 / 32; ++c) {
+                        uint32_t rr[32];
+                        tmem_ld32_async(tbase + static_cast<uint32_t>(c * 32), rr);
+                        tmem_ld_wait(rr);
+                        if (c == TR / 2 / 32 - 1) {
+                            // the accumulator is read: the MMA may overwrite it
+                            tc_fence_before();
+                            __syncwarp();
+                            if (lane == 0) mbar_arrive_local(&tempty[acc]);
+                        }
+                        const int64_t gcol = col0 + half * (TR / 2) + c * 32;  // row of column 0 of the group
+                        const int64_t left = r1 - gcol;
+                        const int nvalid = evalid ? static_cast<int>(left < 0 ? 0 : (left > 32 ? 32 : left)) : 0;
+                        float key[32];
+#pragma unroll
+                        for (int j4 = 0; j4 < 8; ++j4) {
+                            const float4 f4 = *reinterpret_cast<const float4*>(fs + c * 32 + 4 * j4);
+                            const float4 v4 = *reinterpret_cast<const float4*>(vs + c * 32 + 4 * j4);
+                            const float ff[4] = {f4.x, f4.y, f4.z, f4.w};
+                            const float vv[4] = {v4.x, v4.y, v4.z, v4.w};
+#pragma unroll
+                            for (int q = 0; q < 4; ++q) {
+                                const int j = 4 * j4 + q;
+                                const float k0 = rank_key<METRIC>(__uint_as_float(rr[j]) * (qs * ff[q]), vv[q], qv,
+                                                                  a.cos_small);
+                                key[j] = j < nvalid ? k0 : INFINITY;
+                            }
+                        }
+                        if (!collect) {
+                            // threshold pass: minima of groups of gs rows (gs a power of two <= 32)
+#pragma unroll
+                            for (int w = 1; w < 32; w <<= 1) {
+                                if (w < gs) {
+#pragma unroll
+                                    for (int i = 0; i < 32; i += 2 * w) key[i] = fminf(key[i], key[i + w]);
+                                }
+                            }
+#pragma unroll
+                            for (int i = 0; i < 32; ++i) {
+                                if ((i & (gs - 1)) == 0 && key[i] < tv[GK - 1]) insert_sorted(tv, key[i]);
+                            }
+                        } else {
+                            // collecting pass: every row whose value reaches the entry's threshold
+                            unsigned m = 0;
+#pragma unroll
+                            for (int j = 0; j < 32; ++j) m |= (j < nvalid && key[j] <= thr ? 1u : 0u) << j;
+                            while (m) {
+                                const int j = __ffs(m) - 1;
+                                m &= m - 1;
+                                if (cnt < kCap) {
+                                    cv[cnt] = pick32(key, j);
+                                    cr[cnt] = static_cast<uint32_t>(gcol + j);
+                                }
+                                ++cnt;
+                            }
+                        }
+                    }
+                } else {
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive_local(&tempty[acc]);
+                }
+                // the next tile's column factors go to the buffer last read in tile t2 - 1
+                if (t2 + 1 < 2 * ntiles) {
+                    xs_s[((gt + 1) & 1) * 2 * TR + etid] = fn;
+                    xs_s[((gt + 1) & 1) * 2 * TR + TR + etid] = vn;
+                }
+                epi_sync();
+            }
+            if (!ok) break;
+            if (evalid) a.cand_n[pe * 2 + half] = cnt;
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc_t<false>(tmem_base, TMEM_NCOLS);
+    }
+}
+
+// One warp per query: the rows collected for its entries (or, for an entry
+// whose collection overflowed, every row of that list, with exact fp32
+// ranking values) reduced to the best KF >= kk by ranking value, those rows
+// scored again with the CUDA-core scan's arithmetic (L2 as sum (q - x)^2, dot
+// products accumulated in dimension order, cosine through final_score), and
+// the best k of them (ties to the lower stored row) written to out_v / out_i
+// [nq, k].
+template <int METRIC, int KF>
+__global__ void ivf_tc_finish_kernel(int cos_small, const float* __restrict__ q, int64_t Q, int64_t ldq, int d,
+                                     int nprobe, const int64_t* __restrict__ probe, int nlist,
+                                     const int64_t* __restrict__ list_off, const int64_t* __restrict__ list_end,
+                                     const float* __restrict__ rows, int64_t ldx, const float* __restrict__ xv,
+                                     const float* __restrict__ qv, const float* __restrict__ cand_v,
+                                     const uint32_t* __restrict__ cand_r, const int* __restrict__ cand_n,
+                                     const int64_t* __restrict__ ids, int k, float* __restrict__ out_v,
+                                     int64_t* __restrict__ out_i) {
+    static_assert(KF <= 32, "one merged row per lane");
+    const int lane = threadIdx.x & 31;
+    const int64_t qi = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    if (qi >= Q) return;
+    const float* qp = q + qi * ldq;
+    const float qvq = METRIC == RDB_METRIC_COSINE ? qv[qi] : 0.f;
+    float tv[KF];
+    uint32_t tr[KF];
+#pragma unroll
+    for (int i = 0; i < KF; ++i) {
+        tv[i] = INFINITY;
+        tr[i] = kNoRow;
+    }
+    auto offer = [&](float v, uint32_t r) {
+        if (!before(v, r, tv[KF - 1], tr[KF - 1])) return;
+        tv[KF - 1] = v;
+        tr[KF - 1] = r;
+#pragma unroll
+        for (int j = KF - 1; j > 0; --j) {
+            const bool sw = before(tv[j], tr[j], tv[j - 1], tr[j - 1]);
+            const float x0 = tv[j - 1], x1 = tv[j];
+            const uint32_t y0 = tr[j - 1], y1 = tr[j];
+            tv[j - 1] = sw ? x1 : x0;
+            tv[j] = sw ? x0 : x1;
+            tr[j - 1] = sw ? y1 : y0;
+            tr[j] = sw ? y0 : y1;
+        }
+    };
+    auto exact_dot = [&](uint32_t r) {
+        const float* xp = rows + static_cast<int64_t>(r) * ldx;
+        float acc = 0.f;
+        for (int t = 0; t < d; ++t) acc = fmaf(qp[t], xp[t], acc);
+        return acc;
+    };
+    // 1. rows collected for this query's entries (lane: probe slots lane, lane + 32, ...)
+    for (int p = lane; p < nprobe; p += 32) {
+        const int64_t pe = qi * nprobe + p;
+        const int n0 = cand_n[pe * 2], n1 = cand_n[pe * 2 + 1];
+        if (n0 > kCap || n1 > kCap) continue;  // rescanned below
+        for (int h = 0; h < 2; ++h) {
+            const int n = h ? n1 : n0;
+            const float* v = cand_v + (pe * 2 + h) * kCap;
+            const uint32_t* r = cand_r + (pe * 2 + h) * kCap;
+            for (int i = 0; i < n; ++i) offer(v[i], r[i]);
+        }
+    }
+    // 2. entries whose collection overflowed: the whole list, rows across the warp
+    for (int p0 = 0; p0 < nprobe; p0 += 32) {
+        bool over = false;
+        if (p0 + lane < nprobe) {
+            const int64_t pe = qi * nprobe + p0 + lane;
+            over = cand_n[pe * 2] > kCap || cand_n[pe * 2 + 1] > kCap;
+        }
+        unsigned ob = __ballot_sync(0xffffffffu, over);
+        while (ob) {
+            const int pl = __ffs(ob) - 1;
+            ob &= ob - 1;
+            int64_t l = probe[qi * nprobe + p0 + pl];
+            if (l < 0 || l >= nlist) l = 0;  // as the entry sort files it
+            const int64_t r0 = list_off[l], r1 = list_end ? list_end[l] : list_off[l + 1];
+            for (int64_t r = r0 + lane; r < r1; r += 32) {
+                const float dot = exact_dot(static_cast<uint32_t>(r));
+                float key;
+                if (METRIC == RDB_METRIC_L2)
+                    key = fmaf(-2.f, dot, xv[r]);
+                else if (METRIC == RDB_METRIC_COSINE)
+                    key = -final_score(RDB_METRIC_COSINE, cos_small, dot, qvq, xv[r]);
+                else
+                    key = -dot;
+                offer(key, static_cast<uint32_t>(r));
+            }
+        }
+    }
+    // 3. the warp's best KF: KF rounds of the best list head, whose lane pops it
+    uint32_t mine = kNoRow;  // merged row `lane`
+    for (int rnd = 0; rnd < KF; ++rnd) {
+        float bv = tv[0];
+        uint32_t br = tr[0];
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+            const uint32_t orr = __shfl_xor_sync(0xffffffffu, br, o);
+            if (before(ov, orr, bv, br)) {
+                bv = ov;
+                br = orr;
+            }
+        }
+        if (br == kNoRow) break;  // every list is exhausted (warp-uniform)
+        if (tr[0] == br) {
+            // a row probed twice (a repeated probe slot) leaves every list at once
+#pragma unroll
+            for (int j = 0; j < KF - 1; ++j) {
+                tv[j] = tv[j + 1];
+                tr[j] = tr[j + 1];
+            }
+            tv[KF - 1] = INFINITY;
+            tr[KF - 1] = kNoRow;
+        }
+        if (rnd == lane) mine = br;
+    }
+    // 4. exact score of this lane's merged row
+    constexpr bool largest = METRIC != RDB_METRIC_L2;
+    float sc = largest ? -INFINITY : INFINITY;
+    if (mine != kNoRow) {
+        if (METRIC == RDB_METRIC_L2) {
+            const float* xp = rows + static_cast<int64_t>(mine) * ldx;
+            float acc = 0.f;
+            for (int t = 0; t < d; ++t) {
+                const float df = qp[t] - xp[t];
+                acc = fmaf(df, df, acc);
+            }
+            sc = acc;
+        } else {
+            const float dot = exact_dot(mine);
+            sc = METRIC == RDB_METRIC_COSINE ? final_score(METRIC, cos_small, dot, qvq, xv[mine]) : dot;
+        }
+    }
+    // 5. the best k by exact score: k rounds of a warp arg-best
+    uint32_t rw = mine;
+    for (int i = 0; i < k; ++i) {
+        float bv = rw == kNoRow ? (largest ? -INFINITY : INFINITY) : sc;
+        uint32_t br = rw;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+            const uint32_t orr = __shfl_xor_sync(0xffffffffu, br, o);
+            const bool take =
+                orr != kNoRow && (br == kNoRow || (largest ? ov > bv : ov < bv) || (ov == bv && orr < br));
+            if (take) {
+                bv = ov;
+                br = orr;
+            }
+        }
+        if (rw == br) rw = kNoRow;
+        if (lane == 0) {
+            out_v[qi * k + i] = br == kNoRow ? (largest ? -INFINITY : INFINITY) : bv;
+            out_i[qi * k + i] = br == kNoRow ? -1 : (ids ? ids[br] : static_cast<int64_t>(br));
+        }
+    }
+}
+
+inline size_t au(size_t v) { return (v + 255) / 256 * 256; }
+
+struct TcWs {
+    IvfWs inv;
+    size_t off_qh, off_ql, off_qs, off_cv, off_cr, off_cn, off_units, off_n, bytes;
+    int64_t E, dp, max_units;
+    int kk;
+};
+
+// ranked rows per entry: k + 8 (the rescoring margin)
+int tc_kk(int k) { return k + kL2Margin; }
+
+TcWs tc_ws(int64_t nq, int nprobe, int nlist, int d, int k) {
+    TcWs w;
+    w.inv = ivf_ws(nq, nprobe, nlist);
+    w.E = nq * nprobe;
+    w.dp = (d + TK - 1) / TK * TK;
+    w.kk = tc_kk(k);
+    w.max_units = (w.E + TQ - 1) / TQ + nlist;
+    const int64_t Ep = std::max<int64_t>(w.E, 1);
+    size_t off = au(w.inv.bytes);
+    w.off_qh = off;
+    off = au(off + sizeof(__half) * Ep * w.dp);
+    w.off_ql = off;
+    off = au(off + sizeof(__half) * Ep * w.dp);
+    w.off_qs = off;
+    off = au(off + sizeof(float) * Ep);
+    w.off_cv = off;
+    off = au(off + sizeof(float) * Ep * 2 * kCap);
+    w.off_cr = off;
+    off = au(off + sizeof(uint32_t) * Ep * 2 * kCap);
+    w.off_cn = off;
+    off = au(off + sizeof(int) * Ep * 2);
+    w.off_units = off;
+    off = au(off + sizeof(int2) * w.max_units);
+    w.off_n = off;  // unit count, hand-out counter
+    off = au(off + 2 * sizeof(int));
+    w.bytes = off;
+    return w;
+}
+
+int map_f16(CUtensorMap* m, const void* base, int64_t rows, int64_t dp, int box_rows) {
+    return make_map(m, RDB_F16, base, rows, static_cast<int>(dp), dp * 2, TK, box_rows);
+}
+
+template <int METRIC, int GK>
+int launch_scan(const CUtensorMap& mqh, const CUtensorMap& mql, const CUtensorMap& mxh, const CUtensorMap& mxl,
+                const IvfTcArgs& a, int grid, cudaStream_t s) {
+    static bool attr[64] = {false};
+    int dev = 0;
+    RDB_CUDA_TRY(cudaGetDevice(&dev));
+    if (dev >= 0 && dev < 64 && !attr[dev]) {
+        RDB_CUDA_TRY(cudaFuncSetAttribute(ivf_tc_scan_kernel<METRIC, GK>,
+                                          cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES));
+        attr[dev] = true;
+    }
+    ivf_tc_scan_kernel<METRIC, GK><<<grid, NTHR, SMEM_BYTES, s>>>(mqh, mql, mxh, mxl, a, tc_idesc(false, TQ, TR),
+                                                                  device_status_word());
+    RDB_LAUNCH_CHECK();
+    return RDB_OK;
+}
+
+struct FinishArgs {
+    const float* q;
+    int64_t nq, ldq;
+    int d;
+    const int64_t* probe;
+    int nlist;
+    const int64_t* list_off;
+    const int64_t* list_end;
+    const float* rows;
+    int64_t ldx;
+    const int64_t* ids;
+    int k;
+    float* out_v;
+    int64_t* out_i;
+};
+
+template <int METRIC, int KF>
+int launch_finish(const IvfTcArgs& a, const FinishArgs& f, cudaStream_t s) {
+    ivf_tc_finish_kernel<METRIC, KF><<<(unsigned)((f.nq + 7) / 8), 256, 0, s>>>(
+        a.cos_small, f.q, f.nq, f.ldq, f.d, a.nprobe, f.probe, f.nlist, f.list_off, f.list_end, f.rows, f.ldx, a.xv,
+        a.qv, a.cand_v, a.cand_r, a.cand_n, f.ids, f.k, f.out_v, f.out_i);
+    RDB_LAUNCH_CHECK();
+    return RDB_OK;
+}
+
+// scan with group-minimum lists of GK >= kk, then the per-query finish
+template <int METRIC, int GK>
+int run_metric(const CUtensorMap& mqh, const CUtensorMap& mql, const CUtensorMap& mxh, const CUtensorMap& mxl,
+               const IvfTcArgs& a, int grid, const FinishArgs& f, cudaStream_t s) {
+    cudaEvent_t stop_ev;
+    RDB_TRY(timing_begin(TIMING_IVF_SCAN, s, &stop_ev));
+    RDB_TRY((launch_scan<METRIC, GK>(mqh, mql, mxh, mxl, a, grid, s)));
+    if (stop_ev) RDB_CUDA_TRY(cudaEventRecord(stop_ev, s));
+    return launch_finish<METRIC, GK>(a, f, s);
+}
+
+template <int METRIC>
+int run_kk(const CUtensorMap& mqh, const CUtensorMap& mql, const CUtensorMap& mxh, const CUtensorMap& mxl,
+           const IvfTcArgs& a, int grid, const FinishArgs& f, cudaStream_t s) {
+    if (a.kk <= 16) return run_metric<METRIC, 16>(mqh, mql, mxh, mxl, a, grid, f, s);
+    if (a.kk <= 24) return run_metric<METRIC, 24>(mqh, mql, mxh, mxl, a, grid, f, s);
+    return run_metric<METRIC, 32>(mqh, mql, mxh, mxl, a, grid, f, s);
+}
+
+}  // namespace
+}  // namespace rdb
+
+using namespace rdb;
+
+extern "C" {
+
+int rdb_f16_split(const float* x, int64_t n, int64_t ldx, int d, void* hi, void* lo, int64_t ldp, float* scale,
+                  unsigned* flag, void* stream) {
+    RDB_CHECK_ARG(n >= 0 && d >= 1 && ldx >= d && ldp >= d && ldp % 8 == 0, "bad shape");
+    if (n == 0) return RDB_OK;
+    RDB_CHECK_ARG(x && hi && lo && scale, "NULL pointer");
+    split_f16_kernel<<<(unsigned)((n + 7) / 8), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+        x, n, ldx, d, static_cast<__half*>(hi), static_cast<__half*>(lo), ldp, scale, nullptr, 1, flag);
+    RDB_LAUNCH_CHECK();
+    return RDB_OK;
+}
+
+int rdb_ivf_flat_search_tc_supported(int d, int k) {
+    return d >= 1 && d <= kMaxDp && k >= 1 && tc_kk(k) <= kMaxKK ? 1 : 0;
+}
+
+size_t rdb_ivf_flat_search_tc_workspace(int64_t nq, int nprobe, int nlist, int d, int k) {
+    if (nq <= 0 || nprobe <= 0 || nlist <= 0 || d <= 0 || k <= 0) return 256;
+    return tc_ws(nq, nprobe, nlist, d, k).bytes;
+}
+
+int rdb_ivf_flat_search_tc(int metric, const float* q, int64_t nq, int64_t ldq, int d, const int64_t* probe,
+                           int nprobe, const float* rows, int64_t ldx, const float* xv, const void* rows_hi,
+                           const void* rows_lo, const float* row_scale, int64_t ldp, int64_t nrows,
+                           const int64_t* list_off, const int64_t* list_end, int nlist, const int64_t* ids, int k,
+                           float* out_v, int64_t* out_i, void* ws, size_t ws_bytes, void* stream) {
+    RDB_CHECK_ARG(metric >= 0 && metric <= 2, "unknown metric %d", metric);
+    RDB_CHECK_ARG(nq >= 0 && nprobe >= 1 && nlist >= 1 && nlist <= kMaxLabels, "bad shape");
+    RDB_CHECK_ARG(rdb_ivf_flat_search_tc_supported(d, k), "tensor-core IVF search: d must be in [1, %d], k in [1, %d]",
+                  kMaxDp, kMaxKK - kL2Margin);
+    if (nq == 0) return RDB_OK;
+    RDB_CHECK_ARG(q && probe && rows && rows_hi && rows_lo && row_scale && list_off && out_v && out_i && ws,
+                  "NULL pointer");
+    RDB_CHECK_ARG(metric == RDB_METRIC_DOT || xv, "cosine / L2 need per-row values");
+    const TcWs w = tc_ws(nq, nprobe, nlist, d, k);
+    RDB_CHECK_ARG(ldp == w.dp, "row planes must have a stride of %lld (d padded to 64)", (long long)w.dp);
+    RDB_CHECK_ARG(w.E < (1LL << 31) - TQ && nrows < (1LL << 31) - TR, "too many entries or rows for one search");
+    RDB_CHECK_ARG((reinterpret_cast<uintptr_t>(rows_hi) & 15) == 0 && (reinterpret_cast<uintptr_t>(rows_lo) & 15) == 0,
+                  "row planes must be 16-byte aligned");
+    if (ws_bytes < w.bytes) return set_error(RDB_ERR_WORKSPACE, "workspace too small: %zu < %zu", ws_bytes, w.bytes);
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    char* base = static_cast<char*>(ws);
+    RDB_TRY(invert_probes(probe, nq, nprobe, nlist, w.inv, base, s));
+    const int64_t* eperm = reinterpret_cast<const int64_t*>(base + w.inv.off_perm);
+    const int64_t* eseg = reinterpret_cast<const int64_t*>(base + w.inv.off_seg);
+    float* qv = reinterpret_cast<float*>(base + w.inv.off_qv);
+    if (metric == RDB_METRIC_COSINE) {
+        RDB_TRY(row_sqnorms_ld(RDB_F32, q, nq, d, ldq, qv, s));
+        RDB_TRY(rdb_vec_values(metric, d, qv, nq, qv, s));
+    }
+    __half* qh = reinterpret_cast<__half*>(base + w.off_qh);
+    __half* ql = reinterpret_cast<__half*>(base + w.off_ql);
+    float* qs = reinterpret_cast<float*>(base + w.off_qs);
+    // the probing queries, entry by entry in list order, as scaled fp16 planes
+    split_f16_kernel<<<(unsigned)((w.E + 7) / 8), 256, 0, s>>>(q, w.E, ldq, d, qh, ql, w.dp, qs, eperm, nprobe,
+                                                                nullptr);
+    RDB_LAUNCH_CHECK();
+    int2* units = reinterpret_cast<int2*>(base + w.off_units);
+    int* counters = reinterpret_cast<int*>(base + w.off_n);
+    ivf_tc_units_kernel<<<1, 1024, 0, s>>>(eseg, nlist, units, counters, counters + 1);
+    RDB_LAUNCH_CHECK();
+    CUtensorMap mqh, mql, mxh, mxl;
+    RDB_TRY(map_f16(&mqh, qh, w.E, w.dp, TQ));
+    RDB_TRY(map_f16(&mql, ql, w.E, w.dp, TQ));
+    RDB_TRY(map_f16(&mxh, rows_hi, std::max<int64_t>(nrows, 1), w.dp, TR));
+    RDB_TRY(map_f16(&mxl, rows_lo, std::max<int64_t>(nrows, 1), w.dp, TR));
+    IvfTcArgs a = {};
+    a.metric = metric;
+    a.cos_small = d <= 128 ? 1 : 0;
+    a.nkb = static_cast<int>(w.dp / TK);
+    a.kk = w.kk;
+    a.units = units;
+    a.nunits = counters;
+    a.unit_ctr = counters + 1;
+    a.eseg = eseg;
+    a.eperm = eperm;
+    a.nprobe = nprobe;
+    a.list_off = list_off;
+    a.list_end = list_end;
+    a.xv = xv;
+    a.row_scale = row_scale;
+    a.qv = qv;
+    a.ent_scale = qs;
+    a.cand_v = reinterpret_cast<float*>(base + w.off_cv);
+    a.cand_r = reinterpret_cast<uint32_t*>(base + w.off_cr);
+    a.cand_n = reinterpret_cast<int*>(base + w.off_cn);
+    FinishArgs f = {q, nq, ldq, d, probe, nlist, list_off, list_end, rows, ldx, ids, k, out_v, out_i};
+    const int grid = static_cast<int>(std::min<int64_t>(w.max_units, num_sms()));
+    switch (metric) {
+        case RDB_METRIC_L2: return run_kk<RDB_METRIC_L2>(mqh, mql, mxh, mxl, a, grid, f, s);
+        case RDB_METRIC_COSINE: return run_kk<RDB_METRIC_COSINE>(mqh, mql, mxh, mxl, a, grid, f, s);
+        default: return run_kk<RDB_METRIC_DOT>(mqh, mql, mxh, mxl, a, grid, f, s);
+    }
+}
+
+}  // extern "C"

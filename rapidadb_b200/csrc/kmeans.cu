@@ -111,11 +111,7 @@ int assign_impl(int dtype, const void* x, int64_t n, int64_t ldx, int d, const v
     unsigned long long* best =
         reinterpret_cast<unsigned long long*>(static_cast<char*>(ws) + align_up(sizeof(float) * n, 256));
     // |x|^2 of each point (row stride ldx)
-    if (ldx == d) {
-        RDB_TRY(rdb_row_sqnorms(dtype, x, n, d, qv, s));
-    } else {
-        RDB_TRY(rdb_row_sqnorms(dtype, x, n, (int)ldx, qv, s));  // padding columns are zero
-    }
+    RDB_TRY(row_sqnorms_ld(dtype, x, n, d, ldx, qv, s));
     ScanArgs a = {};
     a.metric = RDB_METRIC_L2;
     a.dtype = dtype;

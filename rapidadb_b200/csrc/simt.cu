@@ -583,6 +583,23 @@ int launch_scan_simt(const ScanArgs& a, int mode, cudaStream_t s) {
     }
 }
 
+int row_sqnorms_ld(int dtype, const void* x, int64_t n, int d, int64_t ld, float* out, cudaStream_t s) {
+    RDB_CHECK_ARG(n >= 0 && d >= 1 && ld >= d, "bad shape n=%lld d=%d ld=%lld", (long long)n, d, (long long)ld);
+    if (n == 0) return RDB_OK;
+    RDB_CHECK_ARG(x && out, "NULL pointer");
+    const unsigned blocks = (unsigned)((n + 7) / 8);
+    switch (dtype) {
+        case RDB_F32: row_sqnorms_kernel<float><<<blocks, 256, 0, s>>>((const float*)x, n, d, ld, out); break;
+        case RDB_F16: row_sqnorms_kernel<__half><<<blocks, 256, 0, s>>>((const __half*)x, n, d, ld, out); break;
+        case RDB_BF16:
+            row_sqnorms_kernel<__nv_bfloat16><<<blocks, 256, 0, s>>>((const __nv_bfloat16*)x, n, d, ld, out);
+            break;
+        default: return set_error(RDB_ERR_INVALID, "unknown dtype %d", dtype);
+    }
+    RDB_LAUNCH_CHECK();
+    return RDB_OK;
+}
+
 }  // namespace rdb
 
 using namespace rdb;
@@ -590,21 +607,7 @@ using namespace rdb;
 extern "C" {
 
 int rdb_row_sqnorms(int dtype, const void* x, int64_t n, int d, float* out, void* stream) {
-    RDB_CHECK_ARG(n >= 0 && d >= 1, "bad shape n=%lld d=%d", (long long)n, d);
-    if (n == 0) return RDB_OK;
-    RDB_CHECK_ARG(x && out, "NULL pointer");
-    cudaStream_t s = static_cast<cudaStream_t>(stream);
-    unsigned blocks = (unsigned)((n + 7) / 8);
-    switch (dtype) {
-        case RDB_F32: row_sqnorms_kernel<float><<<blocks, 256, 0, s>>>((const float*)x, n, d, d, out); break;
-        case RDB_F16: row_sqnorms_kernel<__half><<<blocks, 256, 0, s>>>((const __half*)x, n, d, d, out); break;
-        case RDB_BF16:
-            row_sqnorms_kernel<__nv_bfloat16><<<blocks, 256, 0, s>>>((const __nv_bfloat16*)x, n, d, d, out);
-            break;
-        default: return set_error(RDB_ERR_INVALID, "unknown dtype %d", dtype);
-    }
-    RDB_LAUNCH_CHECK();
-    return RDB_OK;
+    return row_sqnorms_ld(dtype, x, n, d, d, out, static_cast<cudaStream_t>(stream));
 }
 
 int rdb_vec_values(int metric, int d, const float* sq, int64_t n, float* out, void* stream) {
