@@ -300,6 +300,11 @@ int rdb_f16_split(const float* x, int64_t n, int64_t ldx, int d, void* hi, void*
  * the same rows, ldp = d rounded up to a multiple of 64, 16-byte aligned.
  * Supported for d <= 128 and k <= 24 (rdb_ivf_flat_search_tc_supported). */
 int rdb_ivf_flat_search_tc_supported(int d, int k);
+/* Count of (query, probe slot) entries, on the current device since the last
+ * reset, whose collected rows overflowed the per-entry buffer so that their
+ * list was rescanned exactly (correct results, slower search; expected only
+ * for lists with many rows of equal value).  Synchronises the device. */
+int rdb_ivf_tc_overflows(unsigned long long* out_host, int reset);
 size_t rdb_ivf_flat_search_tc_workspace(int64_t nq, int nprobe, int nlist, int d, int k);
 int rdb_ivf_flat_search_tc(int metric, const float* q, int64_t nq, int64_t ldq, int d, const int64_t* probe,
                            int nprobe, const float* rows, int64_t ldx, const float* xv, const void* rows_hi,

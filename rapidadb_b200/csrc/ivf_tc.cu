@@ -208,15 +208,6 @@ __global__ void __launch_bounds__(1024) ivf_tc_units_kernel(const int64_t* __res
     }
 }
 
-// Ranking value from the tensor-core dot (smaller = better): L2 |x|^2 - 2 q.x,
-// cosine minus the reference's final score, dot minus q.x.
-template <int METRIC>
-__device__ __forceinline__ float rank_key(float dot, float xv, float qv, int cos_small) {
-    if (METRIC == RDB_METRIC_L2) return fmaf(-2.f, dot, xv);
-    if (METRIC == RDB_METRIC_COSINE) return -final_score(RDB_METRIC_COSINE, cos_small, dot, qv, xv);
-    return -dot;
-}
-
 // Group of rows per minimum in the threshold pass: the largest power of two
 // <= 32 that leaves at least 4 kk groups in the list (1 for short lists), so
 // that the kk-th smallest minimum sits close to the kk-th smallest value.
@@ -226,15 +217,15 @@ __device__ __forceinline__ int group_rows(int64_t n, int kk) {
     return s;
 }
 
-// Insert v into the ascending list tv[GK] (values only), dropping the last.
+// Insert v into the ascending list tv[GK] (values only), dropping the last:
+// element i becomes max(min(tv[i], v), tv[i - 1]) -- the old tv[i - 1] when it
+// exceeds v (shifted up), v at the insertion point, tv[i] below it; a value
+// above tv[GK - 1] leaves the list unchanged.  Branch-free, depth 2.
 template <int GK>
 __device__ __forceinline__ void insert_sorted(float (&tv)[GK], float v) {
-    int p = 0;
 #pragma unroll
-    for (int i = 0; i < GK; ++i) p += tv[i] <= v ? 1 : 0;
-#pragma unroll
-    for (int i = GK - 1; i > 0; --i) tv[i] = i > p ? tv[i - 1] : (i == p ? v : tv[i]);
-    tv[0] = p == 0 ? v : tv[0];
+    for (int i = GK - 1; i > 0; --i) tv[i] = fmaxf(fminf(tv[i], v), tv[i - 1]);
+    tv[0] = fminf(tv[0], v);
 }
 
 template <int GK>
@@ -244,6 +235,32 @@ __device__ __forceinline__ float pick_gk(const float (&tv)[GK], int i) {
     for (int j = 1; j < GK; ++j) r = j == i ? tv[j] : r;
     return r;
 }
+
+// Paired fp32 arithmetic (sm_100): two IEEE round-to-nearest operations per
+// instruction, each identical to its scalar form.
+__device__ __forceinline__ uint64_t pack2(float a, float b) {
+    uint64_t r;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
+    return r;
+}
+__device__ __forceinline__ void unpack2(uint64_t v, float& a, float& b) {
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(v));
+}
+__device__ __forceinline__ uint64_t mul_f32x2(uint64_t a, uint64_t b) {
+    uint64_t d;
+    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+__device__ __forceinline__ uint64_t fma_f32x2(uint64_t a, uint64_t b, uint64_t c) {
+    uint64_t d;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+    return d;
+}
+
+// Row tile of step t2 of a unit: the threshold pass walks tiles 0 .. n - 1,
+// the collecting pass n - 1 .. 0 (its first tiles are the last ones loaded,
+// still in L2).
+__device__ __forceinline__ int tile_of(int t2, int ntiles) { return t2 < ntiles ? t2 : 2 * ntiles - 1 - t2; }
 
 template <int METRIC, int GK>
 __global__ void __launch_bounds__(NTHR, 1)
@@ -351,7 +368,7 @@ __global__ void __launch_bounds__(NTHR, 1)
                 a_pending = true;
                 ++at;
                 for (int t2 = 0; t2 < 2 * ntiles && ok; ++t2) {
-                    const int t = t2 < ntiles ? t2 : t2 - ntiles;
+                    const int t = tile_of(t2, ntiles);
                     const int row0 = static_cast<int>(r0 + static_cast<int64_t>(t) * TR);
                     for (int kb = 0; kb < nkb; ++kb) {
                         if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag)) {
@@ -492,12 +509,12 @@ __global__ void __launch_bounds__(NTHR, 1)
             const int ntiles = unit_info(u, r0, r1, ec, e1);
             const int64_t e = ec + quad * 32 + lane;
             const bool evalid = e < e1;
-            float qs = 0.f, qv = 1.f;
+            float qf = 0.f;
             int64_t pe = 0;
             if (evalid) {
-                qs = a.ent_scale[e];
+                qf = a.ent_scale[e];
                 pe = a.eperm[e];
-                if (METRIC == RDB_METRIC_COSINE) qv = a.qv[pe / a.nprobe];
+                if (METRIC == RDB_METRIC_COSINE) qf /= a.qv[pe / a.nprobe];
             }
             const bool quad_live = ec + quad * 32 < e1;  // same for both warps of the quad
             const int gs = group_rows(r1 - r0, kk);
@@ -508,11 +525,24 @@ __global__ void __launch_bounds__(NTHR, 1)
             int cnt = 0;
             float* cv = a.cand_v + (pe * 2 + half) * kCap;
             uint32_t* cr = a.cand_r + (pe * 2 + half) * kCap;
-            // per-column factors of a tile: row scale x 2^eq applied per entry, row value
+            // per-column factors of a tile, so that value = acc * (qf * f) + v with
+            // the entry's qf: L2 f = -2 * 2^ex, v = |x|^2, qf = 2^eq; cosine
+            // f = -2^ex / xv, v = 0, qf = 2^eq / qv; dot f = -2^ex, v = 0, qf = 2^eq
             auto stage_cols = [&](int t, float& f, float& v) {
                 const int64_t r = r0 + static_cast<int64_t>(t) * TR + etid;
-                f = r < r1 ? __ldg(a.row_scale + r) : 0.f;
-                v = r < r1 && METRIC != RDB_METRIC_DOT ? __ldg(a.xv + r) : 0.f;
+                f = 0.f;
+                v = 0.f;
+                if (r < r1) {
+                    const float rs = __ldg(a.row_scale + r);
+                    if (METRIC == RDB_METRIC_L2) {
+                        f = -2.f * rs;
+                        v = __ldg(a.xv + r);
+                    } else if (METRIC == RDB_METRIC_COSINE) {
+                        f = -rs / __ldg(a.xv + r);
+                    } else {
+                        f = -rs;
+                    }
+                }
             };
             if (ntiles > 0) {
                 float f0, v0;
@@ -523,11 +553,11 @@ __global__ void __launch_bounds__(NTHR, 1)
             epi_sync();
             for (int t2 = 0; t2 < 2 * ntiles; ++t2, ++gt) {
                 const bool collect = t2 >= ntiles;
-                const int t = collect ? t2 - ntiles : t2;
+                const int t = tile_of(t2, ntiles);
                 const int acc = gt & 1;
                 float fn = 0.f, vn = 0.f;
-                if (t2 + 1 < 2 * ntiles) stage_cols(t2 + 1 < ntiles ? t2 + 1 : t2 + 1 - ntiles, fn, vn);
-                if (collect && t == 0 && quad_live) {
+                if (t2 + 1 < 2 * ntiles) stage_cols(tile_of(t2 + 1, ntiles), fn, vn);
+                if (t2 == ntiles && quad_live) {
                     // threshold of each entry: kk-th smallest group minimum over both halves
                     if (half == 1) {
 #pragma unroll
@@ -570,32 +600,47 @@ __global__ void __launch_bounds__(NTHR, 1)
                 if (quad_live) {
 #pragma unroll 1
                     for (int c = 0; c < TR / 2 / 32; ++c) {
+                        const int64_t gcol = col0 + half * (TR / 2) + c * 32;  // row of column 0 of the group
+                        const int64_t left = r1 - gcol;
+                        const int nvc = left <= 0 ? 0 : (left >= 32 ? 32 : static_cast<int>(left));  // valid columns
                         uint32_t rr[32];
-                        tmem_ld32_async(tbase + static_cast<uint32_t>(c * 32), rr);
-                        tmem_ld_wait(rr);
+                        if (nvc > 0) {
+                            tmem_ld32_async(tbase + static_cast<uint32_t>(c * 32), rr);
+                            tmem_ld_wait(rr);
+                        }
                         if (c == TR / 2 / 32 - 1) {
                             // the accumulator is read: the MMA may overwrite it
                             tc_fence_before();
                             __syncwarp();
                             if (lane == 0) mbar_arrive_local(&tempty[acc]);
                         }
-                        const int64_t gcol = col0 + half * (TR / 2) + c * 32;  // row of column 0 of the group
-                        const int64_t left = r1 - gcol;
-                        const int nvalid = evalid ? static_cast<int>(left < 0 ? 0 : (left > 32 ? 32 : left)) : 0;
+                        if (nvc == 0) continue;  // past the list's end (the rest of the tile too)
+                        // value = acc * (qf * f) + v, two columns per paired fp32 operation
                         float key[32];
+                        const uint64_t qf2 = pack2(qf, qf);
 #pragma unroll
                         for (int j4 = 0; j4 < 8; ++j4) {
                             const float4 f4 = *reinterpret_cast<const float4*>(fs + c * 32 + 4 * j4);
                             const float4 v4 = *reinterpret_cast<const float4*>(vs + c * 32 + 4 * j4);
-                            const float ff[4] = {f4.x, f4.y, f4.z, f4.w};
-                            const float vv[4] = {v4.x, v4.y, v4.z, v4.w};
-#pragma unroll
-                            for (int q = 0; q < 4; ++q) {
-                                const int j = 4 * j4 + q;
-                                const float k0 = rank_key<METRIC>(__uint_as_float(rr[j]) * (qs * ff[q]), vv[q], qv,
-                                                                  a.cos_small);
-                                key[j] = j < nvalid ? k0 : INFINITY;
+                            const int j = 4 * j4;
+                            const uint64_t a01 = pack2(__uint_as_float(rr[j]), __uint_as_float(rr[j + 1]));
+                            const uint64_t a23 = pack2(__uint_as_float(rr[j + 2]), __uint_as_float(rr[j + 3]));
+                            const uint64_t m01 = mul_f32x2(qf2, pack2(f4.x, f4.y));
+                            const uint64_t m23 = mul_f32x2(qf2, pack2(f4.z, f4.w));
+                            uint64_t k01, k23;
+                            if (METRIC == RDB_METRIC_L2) {
+                                k01 = fma_f32x2(a01, m01, pack2(v4.x, v4.y));
+                                k23 = fma_f32x2(a23, m23, pack2(v4.z, v4.w));
+                            } else {
+                                k01 = mul_f32x2(a01, m01);
+                                k23 = mul_f32x2(a23, m23);
                             }
+                            unpack2(k01, key[j], key[j + 1]);
+                            unpack2(k23, key[j + 2], key[j + 3]);
+                        }
+                        if (nvc < 32) {
+#pragma unroll
+                            for (int j = 0; j < 32; ++j) key[j] = j < nvc ? key[j] : INFINITY;
                         }
                         if (!collect) {
                             // threshold pass: minima of groups of gs rows (gs a power of two <= 32)
@@ -606,15 +651,23 @@ __global__ void __launch_bounds__(NTHR, 1)
                                     for (int i = 0; i < 32; i += 2 * w) key[i] = fminf(key[i], key[i + w]);
                                 }
                             }
+                            insert_sorted(tv, key[0]);
+                            if (gs < 32) {
 #pragma unroll
-                            for (int i = 0; i < 32; ++i) {
-                                if ((i & (gs - 1)) == 0 && key[i] < tv[GK - 1]) insert_sorted(tv, key[i]);
+                                for (int i = 1; i < 32; ++i) {
+                                    if ((i & (gs - 1)) == 0) insert_sorted(tv, key[i]);
+                                }
                             }
                         } else {
                             // collecting pass: every row whose value reaches the entry's threshold
+                            float gmin = key[0];
+#pragma unroll
+                            for (int j = 1; j < 32; ++j) gmin = fminf(gmin, key[j]);
+                            if (!evalid || !(gmin <= thr)) continue;
                             unsigned m = 0;
 #pragma unroll
-                            for (int j = 0; j < 32; ++j) m |= (j < nvalid && key[j] <= thr ? 1u : 0u) << j;
+                            for (int j = 0; j < 32; ++j) m |= key[j] <= thr ? (1u << j) : 0u;
+                            if (nvc < 32) m &= (1u << nvc) - 1;  // columns past the list's end
                             while (m) {
                                 const int j = __ffs(m) - 1;
                                 m &= m - 1;
@@ -649,6 +702,9 @@ __global__ void __launch_bounds__(NTHR, 1)
         tmem_dealloc_t<false>(tmem_base, TMEM_NCOLS);
     }
 }
+
+// Entries whose collection overflowed and were rescanned (rdb_ivf_tc_overflows).
+__device__ unsigned long long g_tc_overflows;
 
 // One warp per query: the rows collected for its entries (or, for an entry
 // whose collection overflowed, every row of that list, with exact fp32
@@ -720,6 +776,7 @@ __global__ void ivf_tc_finish_kernel(int cos_small, const float* __restrict__ q,
             over = cand_n[pe * 2] > kCap || cand_n[pe * 2 + 1] > kCap;
         }
         unsigned ob = __ballot_sync(0xffffffffu, over);
+        if (ob && lane == 0) atomicAdd(&g_tc_overflows, static_cast<unsigned long long>(__popc(ob)));
         while (ob) {
             const int pl = __ffs(ob) - 1;
             ob &= ob - 1;
@@ -928,6 +985,17 @@ int rdb_f16_split(const float* x, int64_t n, int64_t ldx, int d, void* hi, void*
     split_f16_kernel<<<(unsigned)((n + 7) / 8), 256, 0, static_cast<cudaStream_t>(stream)>>>(
         x, n, ldx, d, static_cast<__half*>(hi), static_cast<__half*>(lo), ldp, scale, nullptr, 1, flag);
     RDB_LAUNCH_CHECK();
+    return RDB_OK;
+}
+
+int rdb_ivf_tc_overflows(unsigned long long* out_host, int reset) {
+    RDB_CHECK_ARG(out_host, "NULL pointer");
+    RDB_CUDA_TRY(cudaDeviceSynchronize());
+    RDB_CUDA_TRY(cudaMemcpyFromSymbol(out_host, g_tc_overflows, sizeof(unsigned long long)));
+    if (reset) {
+        const unsigned long long zero = 0;
+        RDB_CUDA_TRY(cudaMemcpyToSymbol(g_tc_overflows, &zero, sizeof(zero)));
+    }
     return RDB_OK;
 }
 

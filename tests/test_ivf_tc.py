@@ -13,6 +13,9 @@ Shapes cover: dim not a multiple of 64 (zero-padded K), lists longer than one
 chunks), empty lists, free slots between lists (streaming adds), probed lists
 holding fewer than k rows (-1 padding), k = 1 and k = 24, every metric.
 """
+import ctypes
+import os
+
 import numpy as np
 import pytest
 import torch
@@ -21,6 +24,16 @@ import oracle
 from parity import assert_topk_match
 
 pytestmark = pytest.mark.gpu
+LIB = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "rapidadb_b200", "librdb_kernels.so")
+
+
+def overflows(reset):
+    """Entries rescanned exactly because their collected rows overflowed."""
+    lib = ctypes.CDLL(LIB)
+    lib.rdb_ivf_tc_overflows.argtypes = [ctypes.POINTER(ctypes.c_ulonglong), ctypes.c_int]
+    v = ctypes.c_ulonglong(0)
+    assert lib.rdb_ivf_tc_overflows(ctypes.byref(v), 1 if reset else 0) == 0
+    return v.value
 
 METRICS = ["l2", "cosine", "dot_product"]
 
@@ -56,10 +69,14 @@ def oracle_search(metric, idx, cent, x, q, nprobe, k):
     return oracle.ivf_flat_search(metric, q, cent.cpu().numpy(), off, x[ids], ids, nprobe, k)
 
 
-def both_paths(idx, q, k):
+def both_paths(idx, q, k, max_overflows=0):
     qt = torch.from_numpy(q).cuda()
     assert idx.tensor_core_search(k)
+    overflows(reset=True)
     d1, i1 = idx.search(qt, k)
+    n_over = overflows(reset=True)
+    if max_overflows is not None:
+        assert n_over <= max_overflows, f"{n_over} entries overflowed their candidate buffers"
     idx.set_tensor_cores(False)
     assert not idx.tensor_core_search(k)
     d2, i2 = idx.search(qt, k)
@@ -112,7 +129,7 @@ def test_tc_empty_lists_and_short_probes(device):
     sizes = idx.list_sizes().cpu().numpy()
     assert (sizes == 0).sum() >= 20
     q = np.concatenate([x[:10] + 0.01, g.standard_normal((5, d)).astype(np.float32) * 30])
-    dt, it, ds, is_ = both_paths(idx, q, 8)
+    dt, it, ds, is_ = both_paths(idx, q, 8, max_overflows=None)
     np.testing.assert_array_equal(it, is_)
     np.testing.assert_array_equal(dt, ds)
     assert (it == -1).any()
@@ -147,7 +164,7 @@ def test_tc_duplicate_rows_tie_to_lower_row(device):
     idx.set_quantizer(cent)
     idx.add(torch.from_numpy(x).cuda())
     q = x[5:6] * 3.0
-    dt, it, ds, is_ = both_paths(idx, q, 20)
+    dt, it, ds, is_ = both_paths(idx, q, 20, max_overflows=None)
     np.testing.assert_array_equal(it, is_)
     np.testing.assert_array_equal(dt, ds)
 
@@ -196,3 +213,28 @@ def test_tc_restore_rebuilds_planes(device, tmp_path):
     assert back.index.tensor_core_search(10)
     d2, i2 = back.search(torch.from_numpy(q), 10)
     assert torch.equal(i1.cpu(), i2.cpu()) and torch.equal(d1.cpu(), d2.cpu())
+
+
+@pytest.mark.parametrize("metric", METRICS)
+def test_tc_overflow_rescans_the_list_exactly(device, metric):
+    """200 copies of one row in a single list: every copy reaches the entry's
+    threshold, the collected rows overflow their buffers, and the finishing
+    kernel rescans that list exactly -- same answer as the CUDA-core scan."""
+    import rapidadb._C as _C
+
+    d = 40
+    g = np.random.default_rng(4)
+    x = g.standard_normal((3000, d)).astype(np.float32)
+    x[500:700] = x[3]
+    idx = _C.IVFFlatIndex(d, _met(_C, metric), 1, 1, _C.Precision.FP32)
+    idx.set_quantizer(torch.from_numpy(x[:1].copy()).cuda())
+    idx.add(torch.from_numpy(x).cuda())
+    q = np.concatenate([x[3:4] + 0.01, g.standard_normal((5, d)).astype(np.float32)])
+    qt = torch.from_numpy(q).cuda()
+    overflows(reset=True)
+    dt, it = idx.search(qt, 10)
+    assert overflows(reset=True) >= 1
+    idx.set_tensor_cores(False)
+    ds, is_ = idx.search(qt, 10)
+    np.testing.assert_array_equal(it.cpu().numpy(), is_.cpu().numpy())
+    np.testing.assert_array_equal(dt.cpu().numpy(), ds.cpu().numpy())
