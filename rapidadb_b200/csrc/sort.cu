@@ -124,7 +124,10 @@ struct SortWs {
 
 SortWs sort_ws(int64_t n, int K) {
     SortWs w;
-    w.nblk = (int)std::max<int64_t>(1, std::min<int64_t>((n + 65535) / 65536, 296));
+    // about two 1024-element tiles per block, as many blocks as keep the
+    // per-(block, label) histograms and offsets within 2 MB, at most 2 per SM
+    const int64_t by_mem = std::max<int64_t>(1, (int64_t(1) << 18) / std::max(K, 1));
+    w.nblk = (int)std::max<int64_t>(1, std::min<int64_t>({(n + 2047) / 2048, by_mem, 296}));
     w.per_block = (n + w.nblk - 1) / w.nblk;
     size_t off = 0;
     w.off_hist = off;
