@@ -300,10 +300,13 @@ int rdb_f16_split(const float* x, int64_t n, int64_t ldx, int d, void* hi, void*
  * the same rows, ldp = d rounded up to a multiple of 64, 16-byte aligned.
  * Supported for d <= 128 and k <= 24 (rdb_ivf_flat_search_tc_supported). */
 int rdb_ivf_flat_search_tc_supported(int d, int k);
-/* Count of (query, probe slot) entries, on the current device since the last
- * reset, whose collected rows overflowed the per-entry buffer so that their
- * list was rescanned exactly (correct results, slower search; expected only
- * for lists with many rows of equal value).  Synchronises the device. */
+/* Counts on the current device since the last reset (host out[2]): out[0]
+ * (query, probe slot) entries whose collected rows overflowed the per-entry
+ * buffer so that their list was rescanned exactly; out[1] queries of
+ * rdb_ivf_probe_tc whose collected centroids overflowed so that every
+ * centroid was scored exactly.  Both keep results correct and cost time;
+ * expected only for many rows (centroids) of equal value.  Synchronises the
+ * device. */
 int rdb_ivf_tc_overflows(unsigned long long* out_host, int reset);
 size_t rdb_ivf_flat_search_tc_workspace(int64_t nq, int nprobe, int nlist, int d, int k);
 int rdb_ivf_flat_search_tc(int metric, const float* q, int64_t nq, int64_t ldq, int d, const int64_t* probe,
@@ -311,6 +314,22 @@ int rdb_ivf_flat_search_tc(int metric, const float* q, int64_t nq, int64_t ldq, 
                            const void* rows_lo, const float* row_scale, int64_t ldp, int64_t nrows,
                            const int64_t* list_off, const int64_t* list_end, int nlist, const int64_t* ids, int k,
                            float* out_v, int64_t* out_i, void* ws, size_t ws_bytes, void* stream);
+
+/* Coarse probe on the tensor cores (replaces the CUDA-core flat search over
+ * the centroids; no reference counterpart): the nprobe nearest centroids of
+ * each query by squared L2, ascending, ties to the lower list -- probe
+ * [nq, nprobe].  Every (query, centroid) value |c|^2 - 2 q.c comes from the
+ * three-product fp16 split contraction (centroid planes from rdb_f16_split,
+ * stride ldp = d rounded up to 64), the best nprobe + 8 of each query are
+ * scored again as sum (q - c)^2 with rdb_flat_search's exact L2 arithmetic,
+ * so the lists equal those of a flat L2 search over the centroids.  cent
+ * [nlist, ldc] fp32 centroids, cent_sq [nlist] their |c|^2.  Supported for
+ * d <= 128 and min(nlist, nprobe + 8) <= 64 (rdb_ivf_probe_tc_supported). */
+int rdb_ivf_probe_tc_supported(int d, int nlist, int nprobe);
+size_t rdb_ivf_probe_tc_workspace(int64_t nq, int nlist, int d, int nprobe);
+int rdb_ivf_probe_tc(const float* q, int64_t nq, int64_t ldq, int d, const float* cent, int64_t ldc,
+                     const float* cent_sq, const void* cent_hi, const void* cent_lo, const float* cent_scale,
+                     int64_t ldp, int nlist, int nprobe, int64_t* probe, void* ws, size_t ws_bytes, void* stream);
 
 /* rdb_ivf_flat_scan for callers that may not allocate GPU memory (no
  * counterpart in the reference): the same list-major scan and the same

@@ -164,6 +164,8 @@ PYBIND11_MODULE(_C, m) {
             py::arg("vectors"), py::arg("ids") = py::none())
         .def("search", &IVFFlatIndex::search, py::arg("queries"), py::arg("k"), py::call_guard<py::gil_scoped_release>())
         .def("probe", &IVFFlatIndex::probe, py::arg("queries"), py::call_guard<py::gil_scoped_release>())
+        .def("set_probe_tensor_cores", &IVFFlatIndex::set_probe_tensor_cores, py::arg("on"))
+        .def("probe_tensor_cores", &IVFFlatIndex::probe_tensor_cores, py::arg("nprobe"))
         .def("search_probed", &IVFFlatIndex::search_probed, py::arg("queries"), py::arg("probe"), py::arg("k"), py::call_guard<py::gil_scoped_release>())
         .def("reset", &IVFFlatIndex::reset)
         .def("size", &IVFFlatIndex::size)
@@ -208,6 +210,8 @@ PYBIND11_MODULE(_C, m) {
             py::arg("vectors"), py::arg("ids") = py::none())
         .def("search", &IVFPQIndex::search, py::arg("queries"), py::arg("k"), py::call_guard<py::gil_scoped_release>())
         .def("probe", &IVFPQIndex::probe, py::arg("queries"), py::call_guard<py::gil_scoped_release>())
+        .def("set_probe_tensor_cores", &IVFPQIndex::set_probe_tensor_cores, py::arg("on"))
+        .def("probe_tensor_cores", &IVFPQIndex::probe_tensor_cores, py::arg("nprobe"))
         .def("search_probed", &IVFPQIndex::search_probed, py::arg("queries"), py::arg("probe"), py::arg("k"), py::call_guard<py::gil_scoped_release>())
         .def("reset", &IVFPQIndex::reset)
         .def("size", &IVFPQIndex::size)

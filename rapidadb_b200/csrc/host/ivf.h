@@ -61,8 +61,13 @@ class IVFBase {
     int64_t capacity() const { return cap_; }
     virtual void reset();
     // coarse probe: [nq, min(nprobe, nlist)] nearest list ids (squared L2,
-    // ties to the lower list)
+    // ties to the lower list).  With dim <= 128 and nprobe + 8 <= 64 the
+    // centroids are ranked on the tensor cores (rdb_ivf_probe_tc) and the best
+    // nprobe + 8 rescored exactly; set_probe_tensor_cores(false) uses the
+    // CUDA-core flat search throughout.
     at::Tensor probe(const at::Tensor& queries) const;
+    void set_probe_tensor_cores(bool on) { probe_tc_ = on; }
+    bool probe_tensor_cores(int64_t nprobe) const;
 
   protected:
     // reinstalls stored-order labels (non-decreasing) and ids; rebuilds the
@@ -94,6 +99,8 @@ class IVFBase {
     at::Tensor cent_rows_;  // padded copy for the coarse probe
     int64_t cent_ld_ = 0;
     at::Tensor cent_xv_;    // |c|^2
+    at::Tensor cent_hi_, cent_lo_, cent_rs_;  // fp16 planes of the centroids (tensor-core probe)
+    bool probe_tc_ = true;
     at::Tensor labels_;     // [cap] list of each slot (-1: free)
     at::Tensor ids_;        // [cap] user id of each slot (-1: free)
     at::Tensor list_off_;   // [nlist + 1] slot ranges: list l owns list_off_[l] .. list_off_[l + 1] - 1

@@ -169,12 +169,41 @@ void IVFBase::set_centroids(const at::Tensor& centroids) {
     cent_ld_ = padded_ld(dim_, at::kFloat);
     cent_rows_ = prepare_rows(centroids_, at::kFloat, cent_ld_).clone();
     cent_xv_ = row_values(Metric::L2, cent_rows_, dim_);
+    cent_hi_ = cent_lo_ = cent_rs_ = at::Tensor();
+    if (rdb_ivf_probe_tc_supported(dim_, nlist_, 1)) {
+        const int64_t dp = (dim_ + 63) / 64 * 64;
+        cent_hi_ = at::empty({nlist_, dp}, centroids_.options().dtype(at::kHalf));
+        cent_lo_ = at::empty({nlist_, dp}, centroids_.options().dtype(at::kHalf));
+        cent_rs_ = at::empty({nlist_}, centroids_.options());
+        at::Tensor flag = at::zeros({1}, centroids_.options().dtype(at::kInt));
+        check_status(rdb_f16_split(cent_rows_.data_ptr<float>(), nlist_, cent_ld_, dim_, cent_hi_.data_ptr(),
+                                   cent_lo_.data_ptr(), dp, cent_rs_.data_ptr<float>(),
+                                   reinterpret_cast<unsigned*>(flag.data_ptr<int>()), stream_ptr()),
+                     "centroid split");
+        if (flag.item<int>() != 0) cent_hi_ = cent_lo_ = cent_rs_ = at::Tensor();  // not finite: CUDA cores
+    }
+}
+
+bool IVFBase::probe_tensor_cores(int64_t nprobe) const {
+    const int np = static_cast<int>(std::min<int64_t>(nprobe, nlist_));
+    return probe_tc_ && cent_hi_.defined() && rdb_ivf_probe_tc_supported(dim_, nlist_, np) != 0;
 }
 
 at::Tensor IVFBase::probe(const at::Tensor& queries) const {
     // nprobe nearest lists by squared L2 (ties to the lower list id)
     const int np = std::min(nprobe_, nlist_);
     at::Tensor q32 = prepare_rows(queries.to(at::kFloat), at::kFloat, cent_ld_);
+    if (probe_tensor_cores(np)) {
+        const int64_t nq = q32.size(0);
+        at::Tensor out = at::empty({nq, np}, q32.options().dtype(at::kLong));
+        at::Tensor ws = ws_bytes(q32, rdb_ivf_probe_tc_workspace(nq, nlist_, dim_, np));
+        check_status(rdb_ivf_probe_tc(q32.data_ptr<float>(), nq, cent_ld_, dim_, cent_rows_.data_ptr<float>(),
+                                      cent_ld_, cent_xv_.data_ptr<float>(), cent_hi_.data_ptr(), cent_lo_.data_ptr(),
+                                      cent_rs_.data_ptr<float>(), cent_hi_.size(1), nlist_, np,
+                                      out.data_ptr<int64_t>(), ws.data_ptr(), ws.numel(), stream_ptr()),
+                     "tensor-core probe");
+        return out;
+    }
     auto res = FlatIndex::search_rows(Metric::L2, cent_rows_, dim_, cent_xv_, q32, np, at::Tensor(), 0);
     return std::get<1>(res);
 }

@@ -174,6 +174,8 @@ struct IvfTcArgs {
     float* cand_v;            // [nq * nprobe][2][kCap] ranking values, by (query, slot), column half
     uint32_t* cand_r;         // [nq * nprobe][2][kCap] stored rows
     int* cand_n;              // [nq * nprobe][2] rows collected (> kCap: overflow, the list is rescanned)
+    float* dense;             // dense mode: value of entry e, row r at dense[(e - dense_e0) * dense_ld + r]
+    int64_t dense_ld, dense_e0;
 };
 
 // (v, r) before (w, s): smaller value first, then the lower row
@@ -262,7 +264,9 @@ __device__ __forceinline__ uint64_t fma_f32x2(uint64_t a, uint64_t b, uint64_t c
 // still in L2).
 __device__ __forceinline__ int tile_of(int t2, int ntiles) { return t2 < ntiles ? t2 : 2 * ntiles - 1 - t2; }
 
-template <int METRIC, int GK>
+// DENSE: one pass that writes every (entry, row) value to a.dense (the coarse
+// probe's centroid scan); otherwise the threshold and collecting passes.
+template <int METRIC, int GK, bool DENSE>
 __global__ void __launch_bounds__(NTHR, 1)
     ivf_tc_scan_kernel(const __grid_constant__ CUtensorMap mqh, const __grid_constant__ CUtensorMap mql,
                        const __grid_constant__ CUtensorMap mxh, const __grid_constant__ CUtensorMap mxl,
@@ -321,6 +325,7 @@ __global__ void __launch_bounds__(NTHR, 1)
     const uint32_t tmem_base = *tmem_slot;
     const int nkb = a.nkb;
     const int nunits = *a.nunits;
+    constexpr int NPASS = DENSE ? 1 : 2;
 
     // the list range of unit u: rows [r0, r1), entries [ec, e1); its row tiles
     auto unit_info = [&](int u, int64_t& r0, int64_t& r1, int64_t& ec, int64_t& e1) {
@@ -367,7 +372,7 @@ __global__ void __launch_bounds__(NTHR, 1)
                 }
                 a_pending = true;
                 ++at;
-                for (int t2 = 0; t2 < 2 * ntiles && ok; ++t2) {
+                for (int t2 = 0; t2 < NPASS * ntiles && ok; ++t2) {
                     const int t = tile_of(t2, ntiles);
                     const int row0 = static_cast<int>(r0 + static_cast<int64_t>(t) * TR);
                     for (int kb = 0; kb < nkb; ++kb) {
@@ -433,7 +438,7 @@ __global__ void __launch_bounds__(NTHR, 1)
                 }
                 ++at;
                 tc_fence_after();
-                for (int t2 = 0; t2 < 2 * ntiles && ok; ++t2, ++gt) {
+                for (int t2 = 0; t2 < NPASS * ntiles && ok; ++t2, ++gt) {
                     const int acc = gt & 1;
                     if (!mbar_wait(&tempty[acc], ((gt >> 1) & 1) ^ 1, abort_flag)) {
                         ok = false;
@@ -513,7 +518,7 @@ __global__ void __launch_bounds__(NTHR, 1)
             int64_t pe = 0;
             if (evalid) {
                 qf = a.ent_scale[e];
-                pe = a.eperm[e];
+                pe = DENSE ? e : a.eperm[e];
                 if (METRIC == RDB_METRIC_COSINE) qf /= a.qv[pe / a.nprobe];
             }
             const bool quad_live = ec + quad * 32 < e1;  // same for both warps of the quad
@@ -523,8 +528,8 @@ __global__ void __launch_bounds__(NTHR, 1)
             for (int i = 0; i < GK; ++i) tv[i] = INFINITY;
             float thr = INFINITY;  // the entry's threshold in the collecting pass
             int cnt = 0;
-            float* cv = a.cand_v + (pe * 2 + half) * kCap;
-            uint32_t* cr = a.cand_r + (pe * 2 + half) * kCap;
+            float* cv = DENSE ? nullptr : a.cand_v + (pe * 2 + half) * kCap;
+            uint32_t* cr = DENSE ? nullptr : a.cand_r + (pe * 2 + half) * kCap;
             // per-column factors of a tile, so that value = acc * (qf * f) + v with
             // the entry's qf: L2 f = -2 * 2^ex, v = |x|^2, qf = 2^eq; cosine
             // f = -2^ex / xv, v = 0, qf = 2^eq / qv; dot f = -2^ex, v = 0, qf = 2^eq
@@ -551,13 +556,13 @@ __global__ void __launch_bounds__(NTHR, 1)
                 xs_s[(gt & 1) * 2 * TR + TR + etid] = v0;
             }
             epi_sync();
-            for (int t2 = 0; t2 < 2 * ntiles; ++t2, ++gt) {
+            for (int t2 = 0; t2 < NPASS * ntiles; ++t2, ++gt) {
                 const bool collect = t2 >= ntiles;
                 const int t = tile_of(t2, ntiles);
                 const int acc = gt & 1;
                 float fn = 0.f, vn = 0.f;
-                if (t2 + 1 < 2 * ntiles) stage_cols(tile_of(t2 + 1, ntiles), fn, vn);
-                if (t2 == ntiles && quad_live) {
+                if (t2 + 1 < NPASS * ntiles) stage_cols(tile_of(t2 + 1, ntiles), fn, vn);
+                if (!DENSE && t2 == ntiles && quad_live) {
                     // threshold of each entry: kk-th smallest group minimum over both halves
                     if (half == 1) {
 #pragma unroll
@@ -642,7 +647,22 @@ __global__ void __launch_bounds__(NTHR, 1)
 #pragma unroll
                             for (int j = 0; j < 32; ++j) key[j] = j < nvc ? key[j] : INFINITY;
                         }
-                        if (!collect) {
+                        if (DENSE) {
+                            if (evalid) {
+                                float* out = a.dense + (e - a.dense_e0) * a.dense_ld + (gcol - r0);
+                                const int64_t room = a.dense_ld - (gcol - r0);  // padding columns get +inf
+                                if (room >= 32 && (reinterpret_cast<uintptr_t>(out) & 15) == 0) {
+#pragma unroll
+                                    for (int j = 0; j < 32; j += 4)
+                                        *reinterpret_cast<float4*>(out + j) =
+                                            make_float4(key[j], key[j + 1], key[j + 2], key[j + 3]);
+                                } else {
+#pragma unroll
+                                    for (int j = 0; j < 32; ++j)
+                                        if (j < room) out[j] = key[j];
+                                }
+                            }
+                        } else if (!collect) {
                             // threshold pass: minima of groups of gs rows (gs a power of two <= 32)
 #pragma unroll
                             for (int w = 1; w < 32; w <<= 1) {
@@ -685,14 +705,14 @@ __global__ void __launch_bounds__(NTHR, 1)
                     if (lane == 0) mbar_arrive_local(&tempty[acc]);
                 }
                 // the next tile's column factors go to the buffer last read in tile t2 - 1
-                if (t2 + 1 < 2 * ntiles) {
+                if (t2 + 1 < NPASS * ntiles) {
                     xs_s[((gt + 1) & 1) * 2 * TR + etid] = fn;
                     xs_s[((gt + 1) & 1) * 2 * TR + TR + etid] = vn;
                 }
                 epi_sync();
             }
             if (!ok) break;
-            if (evalid) a.cand_n[pe * 2 + half] = cnt;
+            if (!DENSE && evalid) a.cand_n[pe * 2 + half] = cnt;
         }
     }
     tc_fence_before();
@@ -703,8 +723,10 @@ __global__ void __launch_bounds__(NTHR, 1)
     }
 }
 
-// Entries whose collection overflowed and were rescanned (rdb_ivf_tc_overflows).
+// Entries whose collection overflowed and were rescanned (rdb_ivf_tc_overflows),
+// and probed queries that scored every centroid exactly.
 __device__ unsigned long long g_tc_overflows;
+__device__ unsigned long long g_probe_rescans;
 
 // One warp per query: the rows collected for its entries (or, for an entry
 // whose collection overflowed, every row of that list, with exact fp32
@@ -864,7 +886,225 @@ __global__ void ivf_tc_finish_kernel(int cos_small, const float* __restrict__ q,
     }
 }
 
+// Coarse probe set-up for queries [e0, e1): one list (every centroid), its
+// entries the queries in chunks of TQ; zeroes the hand-out counter.
+__global__ void probe_units_kernel(int64_t e0, int64_t e1, int nlist, int64_t* eseg, int64_t* list_off, int2* units,
+                                   int* nunits, int* ctr) {
+    const int64_t nu = (e1 - e0 + TQ - 1) / TQ;
+    for (int64_t i = threadIdx.x; i < nu; i += blockDim.x) units[i] = make_int2(0, static_cast<int>(e0 + i * TQ));
+    if (threadIdx.x == 0) {
+        eseg[0] = e0;
+        eseg[1] = e1;
+        list_off[0] = 0;
+        list_off[1] = nlist;
+        *nunits = static_cast<int>(nu);
+        *ctr = 0;
+    }
+}
+
+constexpr int kProbeSlots = 256;  // collected centroids per query before the all-centroid rescan
+
+// float -> unsigned key with the same order (for counting below a value)
+__device__ __forceinline__ uint32_t fkey(float v) {
+    const uint32_t u = __float_as_uint(v);
+    return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+
+// Exact squared L2 of query qp and centroid cp with the flat search's
+// arithmetic: lane-strided fused multiply-add chains, then a butterfly sum
+// (every lane returns the total).
+__device__ __forceinline__ float flat_l2(const float* qp, const float* cp, int d, int lane) {
+    float acc = 0.f;
+    for (int t = lane; t < d; t += 32) {
+        const float df = qp[t] - cp[t];
+        acc = fmaf(df, df, acc);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+    return acc;
+}
+
+// One warp per query over its row of tensor-core values (|c|^2 - 2 q.c,
+// ld a multiple of 32, padding +inf): the kp-th smallest of the row's group
+// minima (8 groups per lane) bounds the kp-th smallest value; the centroids
+// at or below it (about kp) are scored again with the flat search's exact L2
+// and the best nprobe (ties to the lower list) written to probe [nq, nprobe].
+// More than kProbeSlots collected (many equal values): every centroid is
+// scored exactly instead, in chunks.
+__global__ void __launch_bounds__(256) probe_select_kernel(const float* __restrict__ dense, int64_t ld, int64_t e0,
+                                                           int64_t n, int nlist, int kp, const float* __restrict__ q,
+                                                           int64_t ldq, int d, const float* __restrict__ cent,
+                                                           int64_t ldc, int nprobe, int64_t* __restrict__ probe,
+                                                           unsigned long long* nover) {
+    __shared__ int s_idx[8][kProbeSlots];
+    __shared__ float s_val[8][kProbeSlots];
+    __shared__ int s_top_i[8][64];
+    __shared__ float s_top_v[8][64];
+    const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int64_t r = (int64_t)blockIdx.x * 8 + w;
+    if (r >= n) return;
+    const float* row = dense + r * ld;
+    const int nper = static_cast<int>(ld / 32);
+    const int gsz = nper >= 8 ? (nper + 7) / 8 : 1;
+    // group minima: lane-local runs of gsz of the lane's columns
+    float gm[8];
+#pragma unroll
+    for (int g = 0; g < 8; ++g) {
+        gm[g] = INFINITY;
+        const int i1 = min(nper, (g + 1) * gsz);
+        for (int i = g * gsz; i < i1; ++i) gm[g] = fminf(gm[g], row[i * 32 + lane]);
+    }
+    // kp-th smallest group minimum, by bisection on the ordered keys
+    uint32_t lo = 0, hi = 0xffffffffu;
+    {
+        int fin = 0;
+#pragma unroll
+        for (int g = 0; g < 8; ++g) fin += gm[g] < INFINITY ? 1 : 0;
+        if (__reduce_add_sync(0xffffffffu, fin) < kp) lo = fkey(INFINITY);
+    }
+    if (lo == 0) {
+        while (lo < hi) {
+            const uint32_t mid = lo + (hi - lo) / 2;
+            int c = 0;
+#pragma unroll
+            for (int g = 0; g < 8; ++g) c += fkey(gm[g]) <= mid ? 1 : 0;
+            if (static_cast<int>(__reduce_add_sync(0xffffffffu, c)) >= kp)
+                hi = mid;
+            else
+                lo = mid + 1;
+        }
+    }
+    const uint32_t tk = lo;
+    // collect the columns at or below it
+    int cnt = 0;
+    for (int i = 0; i < nper; ++i) {
+        const int col = i * 32 + lane;
+        const bool take = col < nlist && fkey(row[col]) <= tk;
+        const unsigned b = __ballot_sync(0xffffffffu, take);
+        const int pos = cnt + __popc(b & ((1u << lane) - 1));
+        if (take && pos < kProbeSlots) s_idx[w][pos] = col;
+        cnt += __popc(b);
+    }
+    const bool all = cnt > kProbeSlots;
+    if (all && lane == 0) atomicAdd(nover, 1ull);
+    const int total = all ? nlist : cnt;
+    const float* qp = q + (e0 + r) * ldq;
+    int ntop = 0;
+    for (int c0 = 0; c0 < total; c0 += kProbeSlots) {
+        const int nc = min(kProbeSlots, total - c0);
+        __syncwarp();
+        for (int c = 0; c < nc; ++c) {
+            const int l = all ? c0 + c : s_idx[w][c];
+            const float dist = flat_l2(qp, cent + static_cast<int64_t>(l) * ldc, d, lane);
+            if (lane == 0) {
+                s_val[w][c] = dist;
+                if (all) s_idx[w][c] = l;
+            }
+        }
+        __syncwarp();
+        // best nprobe of this chunk and the running list
+        float cv[8];
+        int ci[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            const int c = lane + 32 * j;
+            cv[j] = c < nc ? s_val[w][c] : INFINITY;
+            ci[j] = c < nc ? s_idx[w][c] : -1;
+        }
+        float tv[2];
+        int ti[2];
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+            const int c = lane + 32 * j;
+            tv[j] = c < ntop ? s_top_v[w][c] : INFINITY;
+            ti[j] = c < ntop ? s_top_i[w][c] : -1;
+        }
+        __syncwarp();
+        const int want = min(nprobe, ntop + nc);
+        for (int i = 0; i < want; ++i) {
+            float bv = INFINITY;
+            int bi = -1;
+#pragma unroll
+            for (int j = 0; j < 8; ++j)
+                if (ci[j] >= 0 && (bi < 0 || cv[j] < bv || (cv[j] == bv && ci[j] < bi))) {
+                    bv = cv[j];
+                    bi = ci[j];
+                }
+#pragma unroll
+            for (int j = 0; j < 2; ++j)
+                if (ti[j] >= 0 && (bi < 0 || tv[j] < bv || (tv[j] == bv && ti[j] < bi))) {
+                    bv = tv[j];
+                    bi = ti[j];
+                }
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) {
+                const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+                const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+                if (oi >= 0 && (bi < 0 || ov < bv || (ov == bv && oi < bi))) {
+                    bv = ov;
+                    bi = oi;
+                }
+            }
+#pragma unroll
+            for (int j = 0; j < 8; ++j)
+                if (ci[j] == bi) ci[j] = -1;
+#pragma unroll
+            for (int j = 0; j < 2; ++j)
+                if (ti[j] == bi) ti[j] = -1;
+            if (lane == 0) {
+                s_top_v[w][i] = bv;
+                s_top_i[w][i] = bi;
+            }
+        }
+        ntop = want;
+    }
+    __syncwarp();
+    for (int i = lane; i < nprobe; i += 32) probe[(e0 + r) * nprobe + i] = i < ntop ? s_top_i[w][i] : -1;
+}
+
 inline size_t au(size_t v) { return (v + 255) / 256 * 256; }
+
+// coarse probe: queries per chunk, so that the chunk's [rows, nlist] value
+// matrix stays within 2^26 floats
+int64_t probe_chunk(int64_t nq, int nlist) {
+    const int64_t ld = (nlist + 31) / 32 * 32;
+    const int64_t c = std::max<int64_t>(TQ, ((int64_t(1) << 26) / ld) / TQ * TQ);
+    return std::min<int64_t>(nq, c);
+}
+
+struct ProbeWs {
+    size_t off_qh, off_ql, off_qs, off_dense, off_eseg, off_loff, off_units, off_n, bytes;
+    int64_t dp, chunk, ld;
+    int kp;
+};
+
+ProbeWs probe_ws(int64_t nq, int nlist, int d, int nprobe) {
+    ProbeWs w;
+    w.dp = (d + TK - 1) / TK * TK;
+    w.chunk = std::max<int64_t>(1, probe_chunk(nq, nlist));
+    w.ld = (nlist + 31) / 32 * 32;
+    w.kp = std::min(nlist, nprobe + kL2Margin);
+    const int64_t nqp = std::max<int64_t>(nq, 1);
+    size_t off = 0;
+    w.off_qh = off;
+    off = au(off + sizeof(__half) * nqp * w.dp);
+    w.off_ql = off;
+    off = au(off + sizeof(__half) * nqp * w.dp);
+    w.off_qs = off;
+    off = au(off + sizeof(float) * nqp);
+    w.off_dense = off;
+    off = au(off + sizeof(float) * w.chunk * w.ld);
+    w.off_eseg = off;
+    off = au(off + 2 * sizeof(int64_t));
+    w.off_loff = off;
+    off = au(off + 2 * sizeof(int64_t));
+    w.off_units = off;
+    off = au(off + sizeof(int2) * ((w.chunk + TQ - 1) / TQ));
+    w.off_n = off;
+    off = au(off + 2 * sizeof(int));
+    w.bytes = off;
+    return w;
+}
 
 struct TcWs {
     IvfWs inv;
@@ -909,19 +1149,20 @@ int map_f16(CUtensorMap* m, const void* base, int64_t rows, int64_t dp, int box_
     return make_map(m, RDB_F16, base, rows, static_cast<int>(dp), dp * 2, TK, box_rows);
 }
 
-template <int METRIC, int GK>
+template <int METRIC, int GK, bool DENSE = false>
 int launch_scan(const CUtensorMap& mqh, const CUtensorMap& mql, const CUtensorMap& mxh, const CUtensorMap& mxl,
                 const IvfTcArgs& a, int grid, cudaStream_t s) {
     static bool attr[64] = {false};
     int dev = 0;
     RDB_CUDA_TRY(cudaGetDevice(&dev));
     if (dev >= 0 && dev < 64 && !attr[dev]) {
-        RDB_CUDA_TRY(cudaFuncSetAttribute(ivf_tc_scan_kernel<METRIC, GK>,
+        RDB_CUDA_TRY(cudaFuncSetAttribute(ivf_tc_scan_kernel<METRIC, GK, DENSE>,
                                           cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES));
         attr[dev] = true;
     }
-    ivf_tc_scan_kernel<METRIC, GK><<<grid, NTHR, SMEM_BYTES, s>>>(mqh, mql, mxh, mxl, a, tc_idesc(false, TQ, TR),
-                                                                  device_status_word());
+    ivf_tc_scan_kernel<METRIC, GK, DENSE><<<grid, NTHR, SMEM_BYTES, s>>>(mqh, mql, mxh, mxl, a,
+                                                                         tc_idesc(false, TQ, TR),
+                                                                         device_status_word());
     RDB_LAUNCH_CHECK();
     return RDB_OK;
 }
@@ -992,9 +1233,11 @@ int rdb_ivf_tc_overflows(unsigned long long* out_host, int reset) {
     RDB_CHECK_ARG(out_host, "NULL pointer");
     RDB_CUDA_TRY(cudaDeviceSynchronize());
     RDB_CUDA_TRY(cudaMemcpyFromSymbol(out_host, g_tc_overflows, sizeof(unsigned long long)));
+    RDB_CUDA_TRY(cudaMemcpyFromSymbol(out_host + 1, g_probe_rescans, sizeof(unsigned long long)));
     if (reset) {
         const unsigned long long zero = 0;
         RDB_CUDA_TRY(cudaMemcpyToSymbol(g_tc_overflows, &zero, sizeof(zero)));
+        RDB_CUDA_TRY(cudaMemcpyToSymbol(g_probe_rescans, &zero, sizeof(zero)));
     }
     return RDB_OK;
 }
@@ -1080,6 +1323,83 @@ int rdb_ivf_flat_search_tc(int metric, const float* q, int64_t nq, int64_t ldq, 
         case RDB_METRIC_COSINE: return run_kk<RDB_METRIC_COSINE>(mqh, mql, mxh, mxl, a, grid, f, s);
         default: return run_kk<RDB_METRIC_DOT>(mqh, mql, mxh, mxl, a, grid, f, s);
     }
+}
+
+int rdb_ivf_probe_tc_supported(int d, int nlist, int nprobe) {
+    return d >= 1 && d <= kMaxDp && nlist >= 1 && nprobe >= 1 && nprobe <= nlist &&
+                   std::min(nlist, nprobe + kL2Margin) <= 64
+               ? 1
+               : 0;
+}
+
+size_t rdb_ivf_probe_tc_workspace(int64_t nq, int nlist, int d, int nprobe) {
+    if (nq <= 0 || nlist <= 0 || d <= 0 || nprobe <= 0) return 256;
+    return probe_ws(nq, nlist, d, nprobe).bytes;
+}
+
+int rdb_ivf_probe_tc(const float* q, int64_t nq, int64_t ldq, int d, const float* cent, int64_t ldc,
+                     const float* cent_sq, const void* cent_hi, const void* cent_lo, const float* cent_scale,
+                     int64_t ldp, int nlist, int nprobe, int64_t* probe, void* ws, size_t ws_bytes, void* stream) {
+    RDB_CHECK_ARG(nq >= 0 && ldq >= d && ldc >= d, "bad shape");
+    RDB_CHECK_ARG(rdb_ivf_probe_tc_supported(d, nlist, nprobe),
+                  "tensor-core probe: d in [1, %d], nprobe in [1, nlist], min(nlist, nprobe + %d) <= 64", kMaxDp,
+                  kL2Margin);
+    if (nq == 0) return RDB_OK;
+    RDB_CHECK_ARG(q && cent && cent_sq && cent_hi && cent_lo && cent_scale && probe && ws, "NULL pointer");
+    const ProbeWs w = probe_ws(nq, nlist, d, nprobe);
+    RDB_CHECK_ARG(ldp == w.dp, "centroid planes must have a stride of %lld (d padded to 64)", (long long)w.dp);
+    RDB_CHECK_ARG(nq < (1LL << 31) - TQ, "too many queries for one probe");
+    RDB_CHECK_ARG((reinterpret_cast<uintptr_t>(cent_hi) & 15) == 0 && (reinterpret_cast<uintptr_t>(cent_lo) & 15) == 0,
+                  "centroid planes must be 16-byte aligned");
+    if (ws_bytes < w.bytes) return set_error(RDB_ERR_WORKSPACE, "workspace too small: %zu < %zu", ws_bytes, w.bytes);
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    char* base = static_cast<char*>(ws);
+    __half* qh = reinterpret_cast<__half*>(base + w.off_qh);
+    __half* ql = reinterpret_cast<__half*>(base + w.off_ql);
+    float* qs = reinterpret_cast<float*>(base + w.off_qs);
+    split_f16_kernel<<<(unsigned)((nq + 7) / 8), 256, 0, s>>>(q, nq, ldq, d, qh, ql, w.dp, qs, nullptr, 1, nullptr);
+    RDB_LAUNCH_CHECK();
+    CUtensorMap mqh, mql, mxh, mxl;
+    RDB_TRY(map_f16(&mqh, qh, nq, w.dp, TQ));
+    RDB_TRY(map_f16(&mql, ql, nq, w.dp, TQ));
+    RDB_TRY(map_f16(&mxh, cent_hi, nlist, w.dp, TR));
+    RDB_TRY(map_f16(&mxl, cent_lo, nlist, w.dp, TR));
+    int64_t* eseg = reinterpret_cast<int64_t*>(base + w.off_eseg);
+    int64_t* loff = reinterpret_cast<int64_t*>(base + w.off_loff);
+    int2* units = reinterpret_cast<int2*>(base + w.off_units);
+    int* counters = reinterpret_cast<int*>(base + w.off_n);
+    float* dense = reinterpret_cast<float*>(base + w.off_dense);
+    IvfTcArgs a = {};
+    a.metric = RDB_METRIC_L2;
+    a.cos_small = 1;
+    a.nkb = static_cast<int>(w.dp / TK);
+    a.kk = 1;
+    a.units = units;
+    a.nunits = counters;
+    a.unit_ctr = counters + 1;
+    a.eseg = eseg;
+    a.nprobe = 1;
+    a.list_off = loff;
+    a.list_end = nullptr;
+    a.xv = cent_sq;
+    a.row_scale = cent_scale;
+    a.ent_scale = qs;
+    a.dense = dense;
+    a.dense_ld = w.ld;
+    for (int64_t e0 = 0; e0 < nq; e0 += w.chunk) {
+        const int64_t e1 = std::min(nq, e0 + w.chunk);
+        probe_units_kernel<<<1, 256, 0, s>>>(e0, e1, nlist, eseg, loff, units, counters, counters + 1);
+        RDB_LAUNCH_CHECK();
+        a.dense_e0 = e0;
+        const int grid = static_cast<int>(std::min<int64_t>((e1 - e0 + TQ - 1) / TQ, num_sms()));
+        RDB_TRY((launch_scan<RDB_METRIC_L2, 16, true>(mqh, mql, mxh, mxl, a, grid, s)));
+        unsigned long long* nover = nullptr;
+        RDB_CUDA_TRY(cudaGetSymbolAddress(reinterpret_cast<void**>(&nover), g_probe_rescans));
+        probe_select_kernel<<<(unsigned)((e1 - e0 + 7) / 8), 256, 0, s>>>(dense, w.ld, e0, e1 - e0, nlist, w.kp, q,
+                                                                          ldq, d, cent, ldc, nprobe, probe, nover);
+        RDB_LAUNCH_CHECK();
+    }
+    return RDB_OK;
 }
 
 }  // extern "C"

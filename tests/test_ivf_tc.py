@@ -27,13 +27,18 @@ pytestmark = pytest.mark.gpu
 LIB = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "rapidadb_b200", "librdb_kernels.so")
 
 
-def overflows(reset):
-    """Entries rescanned exactly because their collected rows overflowed."""
+def overflow_counts(reset):
+    """(entries rescanned exactly because their collected rows overflowed,
+    probed queries that scored every centroid exactly)."""
     lib = ctypes.CDLL(LIB)
     lib.rdb_ivf_tc_overflows.argtypes = [ctypes.POINTER(ctypes.c_ulonglong), ctypes.c_int]
-    v = ctypes.c_ulonglong(0)
-    assert lib.rdb_ivf_tc_overflows(ctypes.byref(v), 1 if reset else 0) == 0
-    return v.value
+    v = (ctypes.c_ulonglong * 2)()
+    assert lib.rdb_ivf_tc_overflows(v, 1 if reset else 0) == 0
+    return v[0], v[1]
+
+
+def overflows(reset):
+    return overflow_counts(reset)[0]
 
 METRICS = ["l2", "cosine", "dot_product"]
 
@@ -238,3 +243,63 @@ def test_tc_overflow_rescans_the_list_exactly(device, metric):
     ds, is_ = idx.search(qt, 10)
     np.testing.assert_array_equal(it.cpu().numpy(), is_.cpu().numpy())
     np.testing.assert_array_equal(dt.cpu().numpy(), ds.cpu().numpy())
+
+
+@pytest.mark.parametrize("d,nlist,nprobe", [(128, 4096, 32), (100, 300, 56), (32, 64, 64), (16, 1000, 1),
+                                           (64, 20000 // 7, 24)])
+def test_tc_probe_equals_cuda_core_probe(device, d, nlist, nprobe):
+    """The coarse probe ranks centroids on the tensor cores and rescores the
+    best nprobe + 8 exactly: the same lists, in the same order, as the
+    CUDA-core flat search over the centroids."""
+    import rapidadb._C as _C
+
+    x, g = mixture(8, nlist, d, max(8, nlist // 20))
+    q = (x[g.integers(0, nlist, 3000)] + 0.5 * g.standard_normal((3000, d))).astype(np.float32)
+    idx = _C.IVFFlatIndex(d, _C.Metric.L2, nlist, nprobe, _C.Precision.FP32)
+    idx.set_quantizer(torch.from_numpy(x).cuda())
+    qt = torch.from_numpy(q).cuda()
+    assert idx.probe_tensor_cores(nprobe)
+    overflow_counts(reset=True)
+    p_tc = idx.probe(qt)
+    assert overflow_counts(reset=True)[1] == 0
+    idx.set_probe_tensor_cores(False)
+    assert not idx.probe_tensor_cores(nprobe)
+    p_cc = idx.probe(qt)
+    assert torch.equal(p_tc.cpu(), p_cc.cpu())
+
+
+def test_tc_probe_limits(device):
+    import rapidadb._C as _C
+
+    idx = _C.IVFFlatIndex(32, _C.Metric.L2, 200, 60, _C.Precision.FP32)
+    idx.set_quantizer(torch.randn(200, 32, device="cuda"))
+    assert idx.probe_tensor_cores(56) and not idx.probe_tensor_cores(57)  # nprobe + 8 <= 64
+    small = _C.IVFFlatIndex(32, _C.Metric.L2, 50, 50, _C.Precision.FP32)
+    small.set_quantizer(torch.randn(50, 32, device="cuda"))
+    assert small.probe_tensor_cores(50)  # every list: min(nlist, nprobe + 8) <= 64
+    wide = _C.IVFPQIndex(192, _C.Metric.L2, 16, 4, 8, 16)
+    wide.set_quantizer(torch.randn(16, 192, device="cuda"), torch.randn(8, 16, 24, device="cuda"))
+    assert not wide.probe_tensor_cores(4)  # d > 128
+
+
+def test_tc_probe_equal_centroids_rescans_exactly(device):
+    """300 copies of one centroid among 500: every copy reaches the probe's
+    threshold, more than its buffer holds, so each query scores every
+    centroid exactly -- same lists as the CUDA-core flat search (ties to the
+    lower list)."""
+    import rapidadb._C as _C
+
+    d, nlist, nprobe = 48, 500, 20
+    g = np.random.default_rng(21)
+    c = g.standard_normal((nlist, d)).astype(np.float32) * 2
+    c[100:400] = c[7]
+    q = (c[7] + 0.05 * g.standard_normal((40, d))).astype(np.float32)
+    idx = _C.IVFFlatIndex(d, _C.Metric.L2, nlist, nprobe, _C.Precision.FP32)
+    idx.set_quantizer(torch.from_numpy(c).cuda())
+    qt = torch.from_numpy(q).cuda()
+    overflow_counts(reset=True)
+    p_tc = idx.probe(qt)
+    assert overflow_counts(reset=True)[1] == 40
+    idx.set_probe_tensor_cores(False)
+    p_cc = idx.probe(qt)
+    assert torch.equal(p_tc.cpu(), p_cc.cpu())
