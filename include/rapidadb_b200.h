@@ -324,7 +324,7 @@ int rdb_ivf_flat_search_tc(int metric, const float* q, int64_t nq, int64_t ldq, 
  * scored again as sum (q - c)^2 with rdb_flat_search's exact L2 arithmetic,
  * so the lists equal those of a flat L2 search over the centroids.  cent
  * [nlist, ldc] fp32 centroids, cent_sq [nlist] their |c|^2.  Supported for
- * d <= 128 and min(nlist, nprobe + 8) <= 64 (rdb_ivf_probe_tc_supported). */
+ * d <= 128 and min(nlist, nprobe + 8) <= 128 (rdb_ivf_probe_tc_supported). */
 int rdb_ivf_probe_tc_supported(int d, int nlist, int nprobe);
 size_t rdb_ivf_probe_tc_workspace(int64_t nq, int nlist, int d, int nprobe);
 int rdb_ivf_probe_tc(const float* q, int64_t nq, int64_t ldq, int d, const float* cent, int64_t ldc,

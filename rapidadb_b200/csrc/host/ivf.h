@@ -61,7 +61,7 @@ class IVFBase {
     int64_t capacity() const { return cap_; }
     virtual void reset();
     // coarse probe: [nq, min(nprobe, nlist)] nearest list ids (squared L2,
-    // ties to the lower list).  With dim <= 128 and nprobe + 8 <= 64 the
+    // ties to the lower list).  With dim <= 128 and nprobe + 8 <= 128 the
     // centroids are ranked on the tensor cores (rdb_ivf_probe_tc) and the best
     // nprobe + 8 rescored exactly; set_probe_tensor_cores(false) uses the
     // CUDA-core flat search throughout.

@@ -175,7 +175,7 @@ struct IvfTcArgs {
     uint32_t* cand_r;         // [nq * nprobe][2][kCap] stored rows
     int* cand_n;              // [nq * nprobe][2] rows collected (> kCap: overflow, the list is rescanned)
     float* dense;             // dense mode: value of entry e, row r at dense[(e - dense_e0) * dense_ld + r]
-    int64_t dense_ld, dense_e0;
+    int64_t dense_ld, dense_e0, dense_e1;  // dense mode: entries [dense_e0, dense_e1), every unit's "list" a row block
 };
 
 // (v, r) before (w, s): smaller value first, then the lower row
@@ -332,7 +332,7 @@ __global__ void __launch_bounds__(NTHR, 1)
         const int2 un = a.units[u];
         const int l = un.x;
         ec = un.y;
-        e1 = min(a.eseg[l + 1], ec + TQ);
+        e1 = min(DENSE ? a.dense_e1 : a.eseg[l + 1], ec + TQ);
         r0 = a.list_off[l];
         r1 = a.list_end ? a.list_end[l] : a.list_off[l + 1];
         return r1 > r0 ? static_cast<int>((r1 - r0 + TR - 1) / TR) : 0;
@@ -649,8 +649,8 @@ __global__ void __launch_bounds__(NTHR, 1)
                         }
                         if (DENSE) {
                             if (evalid) {
-                                float* out = a.dense + (e - a.dense_e0) * a.dense_ld + (gcol - r0);
-                                const int64_t room = a.dense_ld - (gcol - r0);  // padding columns get +inf
+                                float* out = a.dense + (e - a.dense_e0) * a.dense_ld + gcol;
+                                const int64_t room = a.dense_ld - gcol;  // padding columns get +inf
                                 if (room >= 32 && (reinterpret_cast<uintptr_t>(out) & 15) == 0) {
 #pragma unroll
                                     for (int j = 0; j < 32; j += 4)
@@ -886,23 +886,26 @@ __global__ void ivf_tc_finish_kernel(int cos_small, const float* __restrict__ q,
     }
 }
 
-// Coarse probe set-up for queries [e0, e1): one list (every centroid), its
-// entries the queries in chunks of TQ; zeroes the hand-out counter.
-__global__ void probe_units_kernel(int64_t e0, int64_t e1, int nlist, int64_t* eseg, int64_t* list_off, int2* units,
-                                   int* nunits, int* ctr) {
-    const int64_t nu = (e1 - e0 + TQ - 1) / TQ;
-    for (int64_t i = threadIdx.x; i < nu; i += blockDim.x) units[i] = make_int2(0, static_cast<int>(e0 + i * TQ));
+constexpr int kProbeBlock = 1024;  // centroid rows per unit of the dense probe scan
+
+// Coarse probe set-up for queries [e0, e1): the centroids in blocks of
+// kProbeBlock rows (block b is "list" b), one unit per (block, TQ queries);
+// zeroes the hand-out counter.
+__global__ void probe_units_kernel(int64_t e0, int64_t e1, int nlist, int64_t* list_off, int2* units, int* nunits,
+                                   int* ctr) {
+    const int nb = (nlist + kProbeBlock - 1) / kProbeBlock;
+    const int64_t nc = (e1 - e0 + TQ - 1) / TQ;
+    for (int b = threadIdx.x; b <= nb; b += blockDim.x) list_off[b] = std::min<int64_t>(nlist, int64_t(b) * kProbeBlock);
+    for (int64_t i = threadIdx.x; i < nc * nb; i += blockDim.x)
+        units[i] = make_int2(static_cast<int>(i % nb), static_cast<int>(e0 + (i / nb) * TQ));
     if (threadIdx.x == 0) {
-        eseg[0] = e0;
-        eseg[1] = e1;
-        list_off[0] = 0;
-        list_off[1] = nlist;
-        *nunits = static_cast<int>(nu);
+        *nunits = static_cast<int>(nc * nb);
         *ctr = 0;
     }
 }
 
 constexpr int kProbeSlots = 256;  // collected centroids per query before the all-centroid rescan
+constexpr int kProbeTop = 128;    // nprobe + margin limit
 
 // float -> unsigned key with the same order (for counting below a value)
 __device__ __forceinline__ uint32_t fkey(float v) {
@@ -938,8 +941,8 @@ __global__ void __launch_bounds__(256) probe_select_kernel(const float* __restri
                                                            unsigned long long* nover) {
     __shared__ int s_idx[8][kProbeSlots];
     __shared__ float s_val[8][kProbeSlots];
-    __shared__ int s_top_i[8][64];
-    __shared__ float s_top_v[8][64];
+    __shared__ int s_top_i[8][kProbeTop];
+    __shared__ float s_top_v[8][kProbeTop];
     const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int64_t r = (int64_t)blockIdx.x * 8 + w;
     if (r >= n) return;
@@ -1011,10 +1014,10 @@ __global__ void __launch_bounds__(256) probe_select_kernel(const float* __restri
             cv[j] = c < nc ? s_val[w][c] : INFINITY;
             ci[j] = c < nc ? s_idx[w][c] : -1;
         }
-        float tv[2];
-        int ti[2];
+        float tv[kProbeTop / 32];
+        int ti[kProbeTop / 32];
 #pragma unroll
-        for (int j = 0; j < 2; ++j) {
+        for (int j = 0; j < kProbeTop / 32; ++j) {
             const int c = lane + 32 * j;
             tv[j] = c < ntop ? s_top_v[w][c] : INFINITY;
             ti[j] = c < ntop ? s_top_i[w][c] : -1;
@@ -1031,7 +1034,7 @@ __global__ void __launch_bounds__(256) probe_select_kernel(const float* __restri
                     bi = ci[j];
                 }
 #pragma unroll
-            for (int j = 0; j < 2; ++j)
+            for (int j = 0; j < kProbeTop / 32; ++j)
                 if (ti[j] >= 0 && (bi < 0 || tv[j] < bv || (tv[j] == bv && ti[j] < bi))) {
                     bv = tv[j];
                     bi = ti[j];
@@ -1049,7 +1052,7 @@ __global__ void __launch_bounds__(256) probe_select_kernel(const float* __restri
             for (int j = 0; j < 8; ++j)
                 if (ci[j] == bi) ci[j] = -1;
 #pragma unroll
-            for (int j = 0; j < 2; ++j)
+            for (int j = 0; j < kProbeTop / 32; ++j)
                 if (ti[j] == bi) ti[j] = -1;
             if (lane == 0) {
                 s_top_v[w][i] = bv;
@@ -1073,7 +1076,7 @@ int64_t probe_chunk(int64_t nq, int nlist) {
 }
 
 struct ProbeWs {
-    size_t off_qh, off_ql, off_qs, off_dense, off_eseg, off_loff, off_units, off_n, bytes;
+    size_t off_qh, off_ql, off_qs, off_dense, off_loff, off_units, off_n, bytes;
     int64_t dp, chunk, ld;
     int kp;
 };
@@ -1094,12 +1097,11 @@ ProbeWs probe_ws(int64_t nq, int nlist, int d, int nprobe) {
     off = au(off + sizeof(float) * nqp);
     w.off_dense = off;
     off = au(off + sizeof(float) * w.chunk * w.ld);
-    w.off_eseg = off;
-    off = au(off + 2 * sizeof(int64_t));
+    const int64_t nb = (nlist + kProbeBlock - 1) / kProbeBlock;
     w.off_loff = off;
-    off = au(off + 2 * sizeof(int64_t));
+    off = au(off + sizeof(int64_t) * (nb + 1));
     w.off_units = off;
-    off = au(off + sizeof(int2) * ((w.chunk + TQ - 1) / TQ));
+    off = au(off + sizeof(int2) * ((w.chunk + TQ - 1) / TQ) * nb);
     w.off_n = off;
     off = au(off + 2 * sizeof(int));
     w.bytes = off;
@@ -1327,7 +1329,7 @@ int rdb_ivf_flat_search_tc(int metric, const float* q, int64_t nq, int64_t ldq, 
 
 int rdb_ivf_probe_tc_supported(int d, int nlist, int nprobe) {
     return d >= 1 && d <= kMaxDp && nlist >= 1 && nprobe >= 1 && nprobe <= nlist &&
-                   std::min(nlist, nprobe + kL2Margin) <= 64
+                   std::min(nlist, nprobe + kL2Margin) <= kProbeTop
                ? 1
                : 0;
 }
@@ -1342,8 +1344,8 @@ int rdb_ivf_probe_tc(const float* q, int64_t nq, int64_t ldq, int d, const float
                      int64_t ldp, int nlist, int nprobe, int64_t* probe, void* ws, size_t ws_bytes, void* stream) {
     RDB_CHECK_ARG(nq >= 0 && ldq >= d && ldc >= d, "bad shape");
     RDB_CHECK_ARG(rdb_ivf_probe_tc_supported(d, nlist, nprobe),
-                  "tensor-core probe: d in [1, %d], nprobe in [1, nlist], min(nlist, nprobe + %d) <= 64", kMaxDp,
-                  kL2Margin);
+                  "tensor-core probe: d in [1, %d], nprobe in [1, nlist], min(nlist, nprobe + %d) <= %d", kMaxDp,
+                  kL2Margin, kProbeTop);
     if (nq == 0) return RDB_OK;
     RDB_CHECK_ARG(q && cent && cent_sq && cent_hi && cent_lo && cent_scale && probe && ws, "NULL pointer");
     const ProbeWs w = probe_ws(nq, nlist, d, nprobe);
@@ -1364,7 +1366,6 @@ int rdb_ivf_probe_tc(const float* q, int64_t nq, int64_t ldq, int d, const float
     RDB_TRY(map_f16(&mql, ql, nq, w.dp, TQ));
     RDB_TRY(map_f16(&mxh, cent_hi, nlist, w.dp, TR));
     RDB_TRY(map_f16(&mxl, cent_lo, nlist, w.dp, TR));
-    int64_t* eseg = reinterpret_cast<int64_t*>(base + w.off_eseg);
     int64_t* loff = reinterpret_cast<int64_t*>(base + w.off_loff);
     int2* units = reinterpret_cast<int2*>(base + w.off_units);
     int* counters = reinterpret_cast<int*>(base + w.off_n);
@@ -1377,7 +1378,6 @@ int rdb_ivf_probe_tc(const float* q, int64_t nq, int64_t ldq, int d, const float
     a.units = units;
     a.nunits = counters;
     a.unit_ctr = counters + 1;
-    a.eseg = eseg;
     a.nprobe = 1;
     a.list_off = loff;
     a.list_end = nullptr;
@@ -1388,10 +1388,12 @@ int rdb_ivf_probe_tc(const float* q, int64_t nq, int64_t ldq, int d, const float
     a.dense_ld = w.ld;
     for (int64_t e0 = 0; e0 < nq; e0 += w.chunk) {
         const int64_t e1 = std::min(nq, e0 + w.chunk);
-        probe_units_kernel<<<1, 256, 0, s>>>(e0, e1, nlist, eseg, loff, units, counters, counters + 1);
+        probe_units_kernel<<<1, 256, 0, s>>>(e0, e1, nlist, loff, units, counters, counters + 1);
         RDB_LAUNCH_CHECK();
         a.dense_e0 = e0;
-        const int grid = static_cast<int>(std::min<int64_t>((e1 - e0 + TQ - 1) / TQ, num_sms()));
+        a.dense_e1 = e1;
+        const int64_t nunits = (e1 - e0 + TQ - 1) / TQ * ((nlist + kProbeBlock - 1) / kProbeBlock);
+        const int grid = static_cast<int>(std::min<int64_t>(nunits, num_sms()));
         RDB_TRY((launch_scan<RDB_METRIC_L2, 16, true>(mqh, mql, mxh, mxl, a, grid, s)));
         unsigned long long* nover = nullptr;
         RDB_CUDA_TRY(cudaGetSymbolAddress(reinterpret_cast<void**>(&nover), g_probe_rescans));

@@ -246,7 +246,7 @@ def test_tc_overflow_rescans_the_list_exactly(device, metric):
 
 
 @pytest.mark.parametrize("d,nlist,nprobe", [(128, 4096, 32), (100, 300, 56), (32, 64, 64), (16, 1000, 1),
-                                           (64, 20000 // 7, 24)])
+                                           (64, 20000 // 7, 24), (128, 16384, 64), (96, 1500, 120)])
 def test_tc_probe_equals_cuda_core_probe(device, d, nlist, nprobe):
     """The coarse probe ranks centroids on the tensor cores and rescores the
     best nprobe + 8 exactly: the same lists, in the same order, as the
@@ -271,12 +271,12 @@ def test_tc_probe_equals_cuda_core_probe(device, d, nlist, nprobe):
 def test_tc_probe_limits(device):
     import rapidadb._C as _C
 
-    idx = _C.IVFFlatIndex(32, _C.Metric.L2, 200, 60, _C.Precision.FP32)
+    idx = _C.IVFFlatIndex(32, _C.Metric.L2, 200, 130, _C.Precision.FP32)
     idx.set_quantizer(torch.randn(200, 32, device="cuda"))
-    assert idx.probe_tensor_cores(56) and not idx.probe_tensor_cores(57)  # nprobe + 8 <= 64
-    small = _C.IVFFlatIndex(32, _C.Metric.L2, 50, 50, _C.Precision.FP32)
-    small.set_quantizer(torch.randn(50, 32, device="cuda"))
-    assert small.probe_tensor_cores(50)  # every list: min(nlist, nprobe + 8) <= 64
+    assert idx.probe_tensor_cores(120) and not idx.probe_tensor_cores(121)  # nprobe + 8 <= 128
+    small = _C.IVFFlatIndex(32, _C.Metric.L2, 100, 100, _C.Precision.FP32)
+    small.set_quantizer(torch.randn(100, 32, device="cuda"))
+    assert small.probe_tensor_cores(100)  # every list: min(nlist, nprobe + 8) <= 128
     wide = _C.IVFPQIndex(192, _C.Metric.L2, 16, 4, 8, 16)
     wide.set_quantizer(torch.randn(16, 192, device="cuda"), torch.randn(8, 16, 24, device="cuda"))
     assert not wide.probe_tensor_cores(4)  # d > 128
