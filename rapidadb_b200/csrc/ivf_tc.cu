@@ -176,6 +176,7 @@ struct IvfTcArgs {
     int* cand_n;              // [nq * nprobe][2] rows collected (> kCap: overflow, the list is rescanned)
     float* dense;             // dense mode: value of entry e, row r at dense[(e - dense_e0) * dense_ld + r]
     int64_t dense_ld, dense_e0, dense_e1;  // dense mode: entries [dense_e0, dense_e1), every unit's "list" a row block
+    float* dense_gmin;        // dense mode: minimum of each 32-row group, [entries][dense_ld / 32]
 };
 
 // (v, r) before (w, s): smaller value first, then the lower row
@@ -661,6 +662,10 @@ __global__ void __launch_bounds__(NTHR, 1)
                                     for (int j = 0; j < 32; ++j)
                                         if (j < room) out[j] = key[j];
                                 }
+                                float gmin = key[0];
+#pragma unroll
+                                for (int j = 1; j < 32; ++j) gmin = fminf(gmin, key[j]);
+                                a.dense_gmin[(e - a.dense_e0) * (a.dense_ld / 32) + gcol / 32] = gmin;
                             }
                         } else if (!collect) {
                             // threshold pass: minima of groups of gs rows (gs a power of two <= 32)
@@ -934,7 +939,8 @@ __device__ __forceinline__ float flat_l2(const float* qp, const float* cp, int d
 // and the best nprobe (ties to the lower list) written to probe [nq, nprobe].
 // More than kProbeSlots collected (many equal values): every centroid is
 // scored exactly instead, in chunks.
-__global__ void __launch_bounds__(256) probe_select_kernel(const float* __restrict__ dense, int64_t ld, int64_t e0,
+__global__ void __launch_bounds__(256) probe_select_kernel(const float* __restrict__ dense,
+                                                           const float* __restrict__ gmin, int64_t ld, int64_t e0,
                                                            int64_t n, int nlist, int kp, const float* __restrict__ q,
                                                            int64_t ldq, int d, const float* __restrict__ cent,
                                                            int64_t ldc, int nprobe, int64_t* __restrict__ probe,
@@ -948,14 +954,24 @@ __global__ void __launch_bounds__(256) probe_select_kernel(const float* __restri
     if (r >= n) return;
     const float* row = dense + r * ld;
     const int nper = static_cast<int>(ld / 32);
-    const int gsz = nper >= 8 ? (nper + 7) / 8 : 1;
-    // group minima: lane-local runs of gsz of the lane's columns
+    // With at least 2 kp groups of 32 columns, the scan's group minima bound the
+    // kp-th value and only groups at or below the bound are read again;
+    // otherwise lane-local runs of the lane's columns form the groups.
+    const bool by_groups = nper >= 2 * kp;
+    const int gsz = by_groups ? (nper + 255) / 256 : (nper >= 8 ? (nper + 7) / 8 : 1);
+    const float* grow = gmin + r * nper;
     float gm[8];
 #pragma unroll
     for (int g = 0; g < 8; ++g) {
         gm[g] = INFINITY;
-        const int i1 = min(nper, (g + 1) * gsz);
-        for (int i = g * gsz; i < i1; ++i) gm[g] = fminf(gm[g], row[i * 32 + lane]);
+        if (by_groups) {
+            // groups of gsz scan groups: lane L, slot g covers scan groups (g * 32 + L) * gsz ..
+            const int i0 = (g * 32 + lane) * gsz, i1 = min(nper, i0 + gsz);
+            for (int i = i0; i < i1; ++i) gm[g] = fminf(gm[g], grow[i]);
+        } else {
+            const int i1 = min(nper, (g + 1) * gsz);
+            for (int i = g * gsz; i < i1; ++i) gm[g] = fminf(gm[g], row[i * 32 + lane]);
+        }
     }
     // kp-th smallest group minimum, by bisection on the ordered keys
     uint32_t lo = 0, hi = 0xffffffffu;
@@ -978,15 +994,24 @@ __global__ void __launch_bounds__(256) probe_select_kernel(const float* __restri
         }
     }
     const uint32_t tk = lo;
-    // collect the columns at or below it
+    // collect the columns at or below it (by_groups: from the groups whose minimum is)
     int cnt = 0;
-    for (int i = 0; i < nper; ++i) {
-        const int col = i * 32 + lane;
-        const bool take = col < nlist && fkey(row[col]) <= tk;
-        const unsigned b = __ballot_sync(0xffffffffu, take);
-        const int pos = cnt + __popc(b & ((1u << lane) - 1));
-        if (take && pos < kProbeSlots) s_idx[w][pos] = col;
-        cnt += __popc(b);
+    for (int i0 = 0; i0 < nper; i0 += by_groups ? 32 : 1) {
+        unsigned gb = 1u;  // groups of 32 columns to read, one bit per lane's group
+        if (by_groups) {
+            const int gi = i0 + lane;
+            gb = __ballot_sync(0xffffffffu, gi < nper && fkey(grow[gi]) <= tk);
+        }
+        while (gb) {
+            const int i = by_groups ? i0 + __ffs(gb) - 1 : i0;
+            gb &= gb - 1;
+            const int col = i * 32 + lane;
+            const bool take = col < nlist && fkey(row[col]) <= tk;
+            const unsigned b = __ballot_sync(0xffffffffu, take);
+            const int pos = cnt + __popc(b & ((1u << lane) - 1));
+            if (take && pos < kProbeSlots) s_idx[w][pos] = col;
+            cnt += __popc(b);
+        }
     }
     const bool all = cnt > kProbeSlots;
     if (all && lane == 0) atomicAdd(nover, 1ull);
@@ -1076,7 +1101,7 @@ int64_t probe_chunk(int64_t nq, int nlist) {
 }
 
 struct ProbeWs {
-    size_t off_qh, off_ql, off_qs, off_dense, off_loff, off_units, off_n, bytes;
+    size_t off_qh, off_ql, off_qs, off_dense, off_gmin, off_loff, off_units, off_n, bytes;
     int64_t dp, chunk, ld;
     int kp;
 };
@@ -1097,6 +1122,8 @@ ProbeWs probe_ws(int64_t nq, int nlist, int d, int nprobe) {
     off = au(off + sizeof(float) * nqp);
     w.off_dense = off;
     off = au(off + sizeof(float) * w.chunk * w.ld);
+    w.off_gmin = off;
+    off = au(off + sizeof(float) * w.chunk * (w.ld / 32));
     const int64_t nb = (nlist + kProbeBlock - 1) / kProbeBlock;
     w.off_loff = off;
     off = au(off + sizeof(int64_t) * (nb + 1));
@@ -1370,6 +1397,7 @@ int rdb_ivf_probe_tc(const float* q, int64_t nq, int64_t ldq, int d, const float
     int2* units = reinterpret_cast<int2*>(base + w.off_units);
     int* counters = reinterpret_cast<int*>(base + w.off_n);
     float* dense = reinterpret_cast<float*>(base + w.off_dense);
+    float* gmins = reinterpret_cast<float*>(base + w.off_gmin);
     IvfTcArgs a = {};
     a.metric = RDB_METRIC_L2;
     a.cos_small = 1;
@@ -1385,6 +1413,7 @@ int rdb_ivf_probe_tc(const float* q, int64_t nq, int64_t ldq, int d, const float
     a.row_scale = cent_scale;
     a.ent_scale = qs;
     a.dense = dense;
+    a.dense_gmin = gmins;
     a.dense_ld = w.ld;
     for (int64_t e0 = 0; e0 < nq; e0 += w.chunk) {
         const int64_t e1 = std::min(nq, e0 + w.chunk);
@@ -1397,8 +1426,9 @@ int rdb_ivf_probe_tc(const float* q, int64_t nq, int64_t ldq, int d, const float
         RDB_TRY((launch_scan<RDB_METRIC_L2, 16, true>(mqh, mql, mxh, mxl, a, grid, s)));
         unsigned long long* nover = nullptr;
         RDB_CUDA_TRY(cudaGetSymbolAddress(reinterpret_cast<void**>(&nover), g_probe_rescans));
-        probe_select_kernel<<<(unsigned)((e1 - e0 + 7) / 8), 256, 0, s>>>(dense, w.ld, e0, e1 - e0, nlist, w.kp, q,
-                                                                          ldq, d, cent, ldc, nprobe, probe, nover);
+        probe_select_kernel<<<(unsigned)((e1 - e0 + 7) / 8), 256, 0, s>>>(dense, gmins, w.ld, e0, e1 - e0, nlist,
+                                                                          w.kp, q, ldq, d, cent, ldc, nprobe, probe,
+                                                                          nover);
         RDB_LAUNCH_CHECK();
     }
     return RDB_OK;
