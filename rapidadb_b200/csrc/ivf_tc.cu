@@ -76,9 +76,9 @@ constexpr int STAGE_BYTES = 2 * B_PLANE;  // both planes of one K block of a row
 constexpr int BAR_OFF = A_BYTES + NSTAGE * STAGE_BYTES;
 constexpr int BAR_BYTES = 256;
 constexpr int UQ = 4;                        // unit hand-out slots
-constexpr int XS_OFF = BAR_OFF + BAR_BYTES;  // [2 buffers][row factor, row value][TR] per-column staging
+constexpr int XS_OFF = BAR_OFF + BAR_BYTES;  // [epilogue warp][row factor, row value][TR / 2] column staging
 constexpr int GKMAX = 32;                    // group minima kept per (entry, column half)
-constexpr int MG_OFF = XS_OFF + 2 * 2 * TR * 4;  // [4 quads][32 entries][GKMAX] second half's minima
+constexpr int MG_OFF = XS_OFF + EPIW * TR * 4;  // [4 quads][32 entries][GKMAX] second half's minima
 constexpr int TH_OFF = MG_OFF + 4 * 32 * GKMAX * 4;  // [4 quads][32 entries] entry thresholds
 constexpr int SMEM_BYTES = 1024 + TH_OFF + 4 * 32 * 4;
 static_assert(SMEM_BYTES <= 232448, "shared memory over 227 KB");
@@ -92,8 +92,6 @@ constexpr unsigned kNoRow = 0xffffffffu;
 __device__ __forceinline__ void mbar_arrive_local(uint64_t* bar) {
     asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
-
-__device__ __forceinline__ void epi_sync() { asm volatile("bar.sync 1, %0;" ::"n"(EPIT) : "memory"); }
 
 __device__ __forceinline__ bool epi_and(bool ok) {
     uint32_t r;
@@ -288,7 +286,7 @@ __global__ void __launch_bounds__(NTHR, 1)
     volatile int* unit_slot = reinterpret_cast<volatile int*>(uempty + UQ);
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(const_cast<int*>(unit_slot) + UQ);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
-    float* xs_s = reinterpret_cast<float*>(smem + XS_OFF);  // [2][2][TR]: row factor, row value
+    float* xs_s = reinterpret_cast<float*>(smem + XS_OFF);  // [EPIW][2][TR / 2]: row factor, row value
     float* mg_s = reinterpret_cast<float*>(smem + MG_OFF);
     float* th_s = reinterpret_cast<float*>(smem + TH_OFF);
 
@@ -495,15 +493,18 @@ __global__ void __launch_bounds__(NTHR, 1)
         const int ew = warp - 2;
         const int quad = warp & 3;
         const int half = ew >> 2;
-        const int etid = ew * 32 + lane;
         const int kk = a.kk;
         uint32_t gt = 0, ui = 0;
-        bool ok = true;
         for (;;) {
+            // the one point where the eight epilogue warps agree: every warp
+            // leaves here, together, once any role has given up on a wait
             const int s = static_cast<int>(ui % UQ);
-            if (!epi_and(mbar_wait(&ufull[s], (ui / UQ) & 1, abort_flag))) {
-                *abort_flag = 1;
-                if (status) atomicOr(status, DEV_TIMEOUT_EPILOGUE);
+            const bool got_unit = mbar_wait(&ufull[s], (ui / UQ) & 1, abort_flag);
+            if (!epi_and(got_unit && *abort_flag == 0)) {
+                if (!got_unit) {
+                    *abort_flag = 1;
+                    if (status) atomicOr(status, DEV_TIMEOUT_EPILOGUE);
+                }
                 break;
             }
             const int u = unit_slot[s];
@@ -531,38 +532,45 @@ __global__ void __launch_bounds__(NTHR, 1)
             int cnt = 0;
             float* cv = DENSE ? nullptr : a.cand_v + (pe * 2 + half) * kCap;
             uint32_t* cr = DENSE ? nullptr : a.cand_r + (pe * 2 + half) * kCap;
-            // per-column factors of a tile, so that value = acc * (qf * f) + v with
-            // the entry's qf: L2 f = -2 * 2^ex, v = |x|^2, qf = 2^eq; cosine
-            // f = -2^ex / xv, v = 0, qf = 2^eq / qv; dot f = -2^ex, v = 0, qf = 2^eq
-            auto stage_cols = [&](int t, float& f, float& v) {
-                const int64_t r = r0 + static_cast<int64_t>(t) * TR + etid;
-                f = 0.f;
-                v = 0.f;
-                if (r < r1) {
-                    const float rs = __ldg(a.row_scale + r);
-                    if (METRIC == RDB_METRIC_L2) {
-                        f = -2.f * rs;
-                        v = __ldg(a.xv + r);
-                    } else if (METRIC == RDB_METRIC_COSINE) {
-                        f = -rs / __ldg(a.xv + r);
-                    } else {
-                        f = -rs;
+            // per-column factors of this warp's half of a tile, so that value =
+            // acc * (qf * f) + v with the entry's qf: L2 f = -2 * 2^ex, v = |x|^2,
+            // qf = 2^eq; cosine f = -2^ex / xv, v = 0, qf = 2^eq / qv; dot
+            // f = -2^ex, v = 0, qf = 2^eq.  Lane L loads columns L + 32 j; the
+            // warp stages them in its own shared buffer (no cross-warp barrier).
+            float* wst = xs_s + ew * TR;  // [f: TR / 2][v: TR / 2]
+            auto load_cols = [&](int t, float (&f)[4], float (&v)[4]) {
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    const int64_t r = r0 + static_cast<int64_t>(t) * TR + half * (TR / 2) + lane + 32 * j;
+                    f[j] = 0.f;
+                    v[j] = 0.f;
+                    if (r < r1) {
+                        const float rs = __ldg(a.row_scale + r);
+                        if (METRIC == RDB_METRIC_L2) {
+                            f[j] = -2.f * rs;
+                            v[j] = __ldg(a.xv + r);
+                        } else if (METRIC == RDB_METRIC_COSINE) {
+                            f[j] = -rs / __ldg(a.xv + r);
+                        } else {
+                            f[j] = -rs;
+                        }
                     }
                 }
             };
-            if (ntiles > 0) {
-                float f0, v0;
-                stage_cols(0, f0, v0);
-                xs_s[(gt & 1) * 2 * TR + etid] = f0;
-                xs_s[(gt & 1) * 2 * TR + TR + etid] = v0;
-            }
-            epi_sync();
+            float fn[4], vn[4];
+            if (ntiles > 0) load_cols(tile_of(0, ntiles), fn, vn);
+            bool live = true;  // false once a wait gave up: the unit is walked without work
             for (int t2 = 0; t2 < NPASS * ntiles; ++t2, ++gt) {
                 const bool collect = t2 >= ntiles;
                 const int t = tile_of(t2, ntiles);
                 const int acc = gt & 1;
-                float fn = 0.f, vn = 0.f;
-                if (t2 + 1 < NPASS * ntiles) stage_cols(tile_of(t2 + 1, ntiles), fn, vn);
+                float fc[4], vc[4];
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    fc[j] = fn[j];
+                    vc[j] = vn[j];
+                }
+                if (t2 + 1 < NPASS * ntiles) load_cols(tile_of(t2 + 1, ntiles), fn, vn);
                 if (!DENSE && t2 == ntiles && quad_live) {
                     // threshold of each entry: kk-th smallest group minimum over both halves
                     if (half == 1) {
@@ -591,19 +599,25 @@ __global__ void __launch_bounds__(NTHR, 1)
                     pair_sync(quad);
                     thr = th_s[quad * 32 + lane];
                 }
-                if (!epi_and(mbar_wait(&tfull[acc], (gt >> 1) & 1, abort_flag))) {
+                if (live && !mbar_wait(&tfull[acc], (gt >> 1) & 1, abort_flag)) {
+                    if (*abort_flag == 0 && status) atomicOr(status, DEV_TIMEOUT_EPILOGUE);
                     *abort_flag = 1;
-                    if (status) atomicOr(status, DEV_TIMEOUT_EPILOGUE);
-                    ok = false;
-                    break;
+                    live = false;
                 }
                 tc_fence_after();
+                __syncwarp();  // the previous tile's reads of the staging buffer are done
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    wst[lane + 32 * j] = fc[j];
+                    wst[TR / 2 + lane + 32 * j] = vc[j];
+                }
+                __syncwarp();
                 const int64_t col0 = r0 + static_cast<int64_t>(t) * TR;
-                const float* fs = xs_s + acc * 2 * TR + half * (TR / 2);
-                const float* vs = fs + TR;
+                const float* fs = wst;
+                const float* vs = wst + TR / 2;
                 const uint32_t tbase = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) +
                                        static_cast<uint32_t>(acc * TR + half * (TR / 2));
-                if (quad_live) {
+                if (quad_live && live) {
 #pragma unroll 1
                     for (int c = 0; c < TR / 2 / 32; ++c) {
                         const int64_t gcol = col0 + half * (TR / 2) + c * 32;  // row of column 0 of the group
@@ -709,15 +723,8 @@ __global__ void __launch_bounds__(NTHR, 1)
                     __syncwarp();
                     if (lane == 0) mbar_arrive_local(&tempty[acc]);
                 }
-                // the next tile's column factors go to the buffer last read in tile t2 - 1
-                if (t2 + 1 < NPASS * ntiles) {
-                    xs_s[((gt + 1) & 1) * 2 * TR + etid] = fn;
-                    xs_s[((gt + 1) & 1) * 2 * TR + TR + etid] = vn;
-                }
-                epi_sync();
             }
-            if (!ok) break;
-            if (!DENSE && evalid) a.cand_n[pe * 2 + half] = cnt;
+            if (!DENSE && evalid && live) a.cand_n[pe * 2 + half] = cnt;
         }
     }
     tc_fence_before();
