@@ -38,6 +38,7 @@ import argparse
 import json
 import math
 import os
+import gc
 import statistics
 import sys
 import threading
@@ -310,11 +311,22 @@ def timed(ctx, fn, steps, warmup, tag_mask, tags=None):
     e0 = torch.cuda.Event(enable_timing=True)
     e1 = torch.cuda.Event(enable_timing=True)
     n0 = lib.rdb_launch_count()
+    # no garbage-collection pause inside the timed steps (as timeit does);
+    # the slowest step's host time is reported, so a host stall that left
+    # the GPU idle is visible in the record
+    gc.collect()
+    gc_was_on = gc.isenabled()
+    gc.disable()
+    host_max = 0.0
     e0.record()
     out = None
     for _ in range(steps):
+        h0 = time.perf_counter()
         out = fn()
+        host_max = max(host_max, time.perf_counter() - h0)
     e1.record()
+    if gc_was_on:
+        gc.enable()
     launches = int(lib.rdb_launch_count() - n0)
     torch.cuda.synchronize()
     ctx.barrier()
@@ -328,7 +340,7 @@ def timed(ctx, fn, steps, warmup, tag_mask, tags=None):
     lib.rdb_timing_enable(0)
     clk = clocks.stop()
     return {"ms": ctx.max(ms), "kernel_ms": kern_ms, "phases": phases, "launches": launches,
-            "clocks": clk, "out": out}
+            "clocks": clk, "out": out, "host_ms_max_step": round(1e3 * host_max, 3)}
 
 
 def peaks():
@@ -541,6 +553,7 @@ def run_flat(args, wl, ctx):
             "gpu_launches": t["launches"],
             "roofline": roof,
             "clocks": t["clocks"],
+            "host_ms_max_step": t["host_ms_max_step"],
         }
         if exchange is not None:
             res["exchange_phases_ms"] = exchange
@@ -723,6 +736,7 @@ def run_ivf(args, wl, ctx, name, steps, warmup):
                              "frac is far above 1 and the contraction rate bounds it"),
                          "peak_source": f"{src} HBM copy"},
             "clocks": t["clocks"],
+            "host_ms_max_step": t["host_ms_max_step"],
         }
         if not pq:
             flops = 2.0 * scanned * d
@@ -838,6 +852,7 @@ def run_ivf_add(args, wl, ctx):
                          "peak_source": "nominal CUDA-core fp32 (148 SMs x 128 lanes x 2 x 1.965 GHz); "
                                         "no measured CUDA-core peak"},
             "clocks": t["clocks"],
+            "host_ms_max_step": t["host_ms_max_step"],
         }
     return res
 
@@ -914,6 +929,7 @@ def run_kmeans(args, wl, ctx, name, steps, warmup):
                                         f"runs for a quarter second under the power cap)"},
             "gpu_launches": t["launches"],
             "clocks": t["clocks"],
+            "host_ms_max_step": t["host_ms_max_step"],
         }
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         res["cpu_baseline"] = kmeans_cpu_baseline(x, state["c"], N, args.cpu_seconds)
