@@ -308,7 +308,7 @@ int rdb_ivf_flat_search_tc_supported(int d, int k);
  * expected only for many rows (centroids) of equal value.  Synchronises the
  * device. */
 int rdb_ivf_tc_overflows(unsigned long long* out_host, int reset);
-size_t rdb_ivf_flat_search_tc_workspace(int64_t nq, int nprobe, int nlist, int d, int k);
+size_t rdb_ivf_flat_search_tc_workspace(int64_t nq, int nprobe, int nlist, int d, int k, int64_t nrows);
 int rdb_ivf_flat_search_tc(int metric, const float* q, int64_t nq, int64_t ldq, int d, const int64_t* probe,
                            int nprobe, const float* rows, int64_t ldx, const float* xv, const void* rows_hi,
                            const void* rows_lo, const float* row_scale, int64_t ldp, int64_t nrows,

@@ -522,7 +522,7 @@ Result IVFFlatIndex::search_probed(const at::Tensor& queries, const at::Tensor& 
     if (tensor_core_search(k)) {
         at::Tensor ov = at::empty({nq, k}, q.options().dtype(at::kFloat));
         at::Tensor oi = at::empty({nq, k}, q.options().dtype(at::kLong));
-        at::Tensor tws = ws_bytes(q, rdb_ivf_flat_search_tc_workspace(nq, np, nlist_, dim_, static_cast<int>(k)));
+        at::Tensor tws = ws_bytes(q, rdb_ivf_flat_search_tc_workspace(nq, np, nlist_, dim_, static_cast<int>(k), cap_));
         check_status(rdb_ivf_flat_search_tc(static_cast<int>(metric_), q.data_ptr<float>(), nq, ld_, dim_,
                                             probe_lists.data_ptr<int64_t>(), np, rows_.data_ptr<float>(), ld_,
                                             xv_.data_ptr<float>(), hi_.data_ptr(), lo_.data_ptr(),

@@ -167,6 +167,7 @@ struct IvfTcArgs {
     const int64_t* list_end;  // [nlist] or NULL
     const float* xv;          // per stored row: |x|^2 (L2), norm (cosine)
     const float* row_scale;   // per stored row: 2^ex
+    const float2* colfv;      // per stored row: (f, v) with value = acc * (qf * f) + v (col_factors_kernel)
     const float* qv;          // per query: norm (cosine)
     const float* ent_scale;   // per entry: 2^eq
     float* cand_v;            // [nq * nprobe][2][kCap] ranking values, by (query, slot), column half
@@ -180,6 +181,22 @@ struct IvfTcArgs {
 // (v, r) before (w, s): smaller value first, then the lower row
 __device__ __forceinline__ bool before(float v, uint32_t r, float w, uint32_t s) {
     return v < w || (v == w && r < s);
+}
+
+// Per stored row, the column factor and value of the ranking value
+// acc * (qf * f) + v: L2 (-2 s, |x|^2), cosine (-s / xv, 0), dot (-s, 0),
+// s the row's power-of-two scale.
+__global__ void col_factors_kernel(int metric, const float* __restrict__ row_scale, const float* __restrict__ xv,
+                                   int64_t n, float2* __restrict__ out) {
+    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= n) return;
+    const float rs = row_scale[i];
+    if (metric == RDB_METRIC_L2)
+        out[i] = make_float2(-2.f * rs, xv[i]);
+    else if (metric == RDB_METRIC_COSINE)
+        out[i] = make_float2(-rs / xv[i], 0.f);
+    else
+        out[i] = make_float2(-rs, 0.f);
 }
 
 // The units of work of one search: each list's entries in chunks of TQ, in
@@ -538,39 +555,31 @@ __global__ void __launch_bounds__(NTHR, 1)
             // f = -2^ex, v = 0, qf = 2^eq.  Lane L loads columns L + 32 j; the
             // warp stages them in its own shared buffer (no cross-warp barrier).
             float* wst = xs_s + ew * TR;  // [f: TR / 2][v: TR / 2]
-            auto load_cols = [&](int t, float (&f)[4], float (&v)[4]) {
+            auto load_cols = [&](int t, float2 (&fv)[4]) {
 #pragma unroll
                 for (int j = 0; j < 4; ++j) {
                     const int64_t r = r0 + static_cast<int64_t>(t) * TR + half * (TR / 2) + lane + 32 * j;
-                    f[j] = 0.f;
-                    v[j] = 0.f;
-                    if (r < r1) {
-                        const float rs = __ldg(a.row_scale + r);
-                        if (METRIC == RDB_METRIC_L2) {
-                            f[j] = -2.f * rs;
-                            v[j] = __ldg(a.xv + r);
-                        } else if (METRIC == RDB_METRIC_COSINE) {
-                            f[j] = -rs / __ldg(a.xv + r);
-                        } else {
-                            f[j] = -rs;
-                        }
-                    }
+                    fv[j] = r < r1 ? __ldg(a.colfv + r) : make_float2(0.f, 0.f);
                 }
             };
-            float fn[4], vn[4];
-            if (ntiles > 0) load_cols(tile_of(0, ntiles), fn, vn);
+            // two tiles of column factors in flight ahead of the tile being ranked
+            const int nsteps = NPASS * ntiles;
+            float2 fv1[4], fv2[4];
+            if (nsteps > 0) load_cols(tile_of(0, ntiles), fv1);
+            if (nsteps > 1) load_cols(tile_of(1, ntiles), fv2);
             bool live = true;  // false once a wait gave up: the unit is walked without work
-            for (int t2 = 0; t2 < NPASS * ntiles; ++t2, ++gt) {
+            for (int t2 = 0; t2 < nsteps; ++t2, ++gt) {
                 const bool collect = t2 >= ntiles;
                 const int t = tile_of(t2, ntiles);
                 const int acc = gt & 1;
                 float fc[4], vc[4];
 #pragma unroll
                 for (int j = 0; j < 4; ++j) {
-                    fc[j] = fn[j];
-                    vc[j] = vn[j];
+                    fc[j] = fv1[j].x;
+                    vc[j] = fv1[j].y;
+                    fv1[j] = fv2[j];
                 }
-                if (t2 + 1 < NPASS * ntiles) load_cols(tile_of(t2 + 1, ntiles), fn, vn);
+                if (t2 + 2 < nsteps) load_cols(tile_of(t2 + 2, ntiles), fv2);
                 if (!DENSE && t2 == ntiles && quad_live) {
                     // threshold of each entry: kk-th smallest group minimum over both halves
                     if (half == 1) {
@@ -1108,7 +1117,7 @@ int64_t probe_chunk(int64_t nq, int nlist) {
 }
 
 struct ProbeWs {
-    size_t off_qh, off_ql, off_qs, off_dense, off_gmin, off_loff, off_units, off_n, bytes;
+    size_t off_qh, off_ql, off_qs, off_dense, off_gmin, off_loff, off_units, off_fv, off_n, bytes;
     int64_t dp, chunk, ld;
     int kp;
 };
@@ -1136,6 +1145,8 @@ ProbeWs probe_ws(int64_t nq, int nlist, int d, int nprobe) {
     off = au(off + sizeof(int64_t) * (nb + 1));
     w.off_units = off;
     off = au(off + sizeof(int2) * ((w.chunk + TQ - 1) / TQ) * nb);
+    w.off_fv = off;
+    off = au(off + sizeof(float2) * nlist);
     w.off_n = off;
     off = au(off + 2 * sizeof(int));
     w.bytes = off;
@@ -1144,7 +1155,7 @@ ProbeWs probe_ws(int64_t nq, int nlist, int d, int nprobe) {
 
 struct TcWs {
     IvfWs inv;
-    size_t off_qh, off_ql, off_qs, off_cv, off_cr, off_cn, off_units, off_n, bytes;
+    size_t off_qh, off_ql, off_qs, off_cv, off_cr, off_cn, off_units, off_fv, off_n, bytes;
     int64_t E, dp, max_units;
     int kk;
 };
@@ -1152,7 +1163,7 @@ struct TcWs {
 // ranked rows per entry: k + 8 (the rescoring margin)
 int tc_kk(int k) { return k + kL2Margin; }
 
-TcWs tc_ws(int64_t nq, int nprobe, int nlist, int d, int k) {
+TcWs tc_ws(int64_t nq, int nprobe, int nlist, int d, int k, int64_t nrows) {
     TcWs w;
     w.inv = ivf_ws(nq, nprobe, nlist);
     w.E = nq * nprobe;
@@ -1175,6 +1186,8 @@ TcWs tc_ws(int64_t nq, int nprobe, int nlist, int d, int k) {
     off = au(off + sizeof(int) * Ep * 2);
     w.off_units = off;
     off = au(off + sizeof(int2) * w.max_units);
+    w.off_fv = off;
+    off = au(off + sizeof(float2) * std::max<int64_t>(nrows, 1));
     w.off_n = off;  // unit count, hand-out counter
     off = au(off + 2 * sizeof(int));
     w.bytes = off;
@@ -1282,9 +1295,9 @@ int rdb_ivf_flat_search_tc_supported(int d, int k) {
     return d >= 1 && d <= kMaxDp && k >= 1 && tc_kk(k) <= kMaxKK ? 1 : 0;
 }
 
-size_t rdb_ivf_flat_search_tc_workspace(int64_t nq, int nprobe, int nlist, int d, int k) {
+size_t rdb_ivf_flat_search_tc_workspace(int64_t nq, int nprobe, int nlist, int d, int k, int64_t nrows) {
     if (nq <= 0 || nprobe <= 0 || nlist <= 0 || d <= 0 || k <= 0) return 256;
-    return tc_ws(nq, nprobe, nlist, d, k).bytes;
+    return tc_ws(nq, nprobe, nlist, d, k, nrows).bytes;
 }
 
 int rdb_ivf_flat_search_tc(int metric, const float* q, int64_t nq, int64_t ldq, int d, const int64_t* probe,
@@ -1300,7 +1313,7 @@ int rdb_ivf_flat_search_tc(int metric, const float* q, int64_t nq, int64_t ldq, 
     RDB_CHECK_ARG(q && probe && rows && rows_hi && rows_lo && row_scale && list_off && out_v && out_i && ws,
                   "NULL pointer");
     RDB_CHECK_ARG(metric == RDB_METRIC_DOT || xv, "cosine / L2 need per-row values");
-    const TcWs w = tc_ws(nq, nprobe, nlist, d, k);
+    const TcWs w = tc_ws(nq, nprobe, nlist, d, k, nrows);
     RDB_CHECK_ARG(ldp == w.dp, "row planes must have a stride of %lld (d padded to 64)", (long long)w.dp);
     RDB_CHECK_ARG(w.E < (1LL << 31) - TQ && nrows < (1LL << 31) - TR, "too many entries or rows for one search");
     RDB_CHECK_ARG((reinterpret_cast<uintptr_t>(rows_hi) & 15) == 0 && (reinterpret_cast<uintptr_t>(rows_lo) & 15) == 0,
@@ -1327,6 +1340,11 @@ int rdb_ivf_flat_search_tc(int metric, const float* q, int64_t nq, int64_t ldq, 
     int* counters = reinterpret_cast<int*>(base + w.off_n);
     ivf_tc_units_kernel<<<1, 1024, 0, s>>>(eseg, nlist, units, counters, counters + 1);
     RDB_LAUNCH_CHECK();
+    float2* colfv = reinterpret_cast<float2*>(base + w.off_fv);
+    if (nrows > 0) {
+        col_factors_kernel<<<(unsigned)((nrows + 255) / 256), 256, 0, s>>>(metric, row_scale, xv, nrows, colfv);
+        RDB_LAUNCH_CHECK();
+    }
     CUtensorMap mqh, mql, mxh, mxl;
     RDB_TRY(map_f16(&mqh, qh, w.E, w.dp, TQ));
     RDB_TRY(map_f16(&mql, ql, w.E, w.dp, TQ));
@@ -1347,6 +1365,7 @@ int rdb_ivf_flat_search_tc(int metric, const float* q, int64_t nq, int64_t ldq, 
     a.list_end = list_end;
     a.xv = xv;
     a.row_scale = row_scale;
+    a.colfv = colfv;
     a.qv = qv;
     a.ent_scale = qs;
     a.cand_v = reinterpret_cast<float*>(base + w.off_cv);
@@ -1418,6 +1437,10 @@ int rdb_ivf_probe_tc(const float* q, int64_t nq, int64_t ldq, int d, const float
     a.list_end = nullptr;
     a.xv = cent_sq;
     a.row_scale = cent_scale;
+    float2* cfv = reinterpret_cast<float2*>(base + w.off_fv);
+    col_factors_kernel<<<(unsigned)((nlist + 255) / 256), 256, 0, s>>>(RDB_METRIC_L2, cent_scale, cent_sq, nlist, cfv);
+    RDB_LAUNCH_CHECK();
+    a.colfv = cfv;
     a.ent_scale = qs;
     a.dense = dense;
     a.dense_gmin = gmins;
