@@ -317,16 +317,19 @@ def timed(ctx, fn, steps, warmup, tag_mask, tags=None):
     gc.collect()
     gc_was_on = gc.isenabled()
     gc.disable()
-    host_max = 0.0
+    allocs0 = torch.cuda.memory_stats().get("num_device_alloc", 0)
+    host_steps = []
     e0.record()
     out = None
     for _ in range(steps):
         h0 = time.perf_counter()
         out = fn()
-        host_max = max(host_max, time.perf_counter() - h0)
+        host_steps.append(time.perf_counter() - h0)
     e1.record()
+    device_allocs = torch.cuda.memory_stats().get("num_device_alloc", 0) - allocs0
     if gc_was_on:
         gc.enable()
+    host_max = max(host_steps) if host_steps else 0.0
     launches = int(lib.rdb_launch_count() - n0)
     torch.cuda.synchronize()
     ctx.barrier()
@@ -340,7 +343,8 @@ def timed(ctx, fn, steps, warmup, tag_mask, tags=None):
     lib.rdb_timing_enable(0)
     clk = clocks.stop()
     return {"ms": ctx.max(ms), "kernel_ms": kern_ms, "phases": phases, "launches": launches,
-            "clocks": clk, "out": out, "host_ms_max_step": round(1e3 * host_max, 3)}
+            "clocks": clk, "out": out, "host_ms_max_step": round(1e3 * host_max, 3),
+            "host_ms_steps": [round(1e3 * h, 3) for h in host_steps], "device_allocs": int(device_allocs)}
 
 
 def peaks():
@@ -554,6 +558,7 @@ def run_flat(args, wl, ctx):
             "roofline": roof,
             "clocks": t["clocks"],
             "host_ms_max_step": t["host_ms_max_step"],
+            "device_allocs_in_timed_steps": t["device_allocs"],
         }
         if exchange is not None:
             res["exchange_phases_ms"] = exchange
@@ -737,6 +742,7 @@ def run_ivf(args, wl, ctx, name, steps, warmup):
                          "peak_source": f"{src} HBM copy"},
             "clocks": t["clocks"],
             "host_ms_max_step": t["host_ms_max_step"],
+            "device_allocs_in_timed_steps": t["device_allocs"],
         }
         if not pq:
             flops = 2.0 * scanned * d
@@ -853,6 +859,7 @@ def run_ivf_add(args, wl, ctx):
                                         "no measured CUDA-core peak"},
             "clocks": t["clocks"],
             "host_ms_max_step": t["host_ms_max_step"],
+            "device_allocs_in_timed_steps": t["device_allocs"],
         }
     return res
 
@@ -930,6 +937,7 @@ def run_kmeans(args, wl, ctx, name, steps, warmup):
             "gpu_launches": t["launches"],
             "clocks": t["clocks"],
             "host_ms_max_step": t["host_ms_max_step"],
+            "device_allocs_in_timed_steps": t["device_allocs"],
         }
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         res["cpu_baseline"] = kmeans_cpu_baseline(x, state["c"], N, args.cpu_seconds)
