@@ -80,7 +80,8 @@ constexpr int XS_OFF = BAR_OFF + BAR_BYTES;  // [epilogue warp][row factor, row 
 constexpr int GKMAX = 32;                    // group minima kept per (entry, column half)
 constexpr int MG_OFF = XS_OFF + EPIW * TR * 4;  // [4 quads][32 entries][GKMAX] second half's minima
 constexpr int TH_OFF = MG_OFF + 4 * 32 * GKMAX * 4;  // [4 quads][32 entries] entry thresholds
-constexpr int SMEM_BYTES = 1024 + TH_OFF + 4 * 32 * 4;
+constexpr int UR_OFF = TH_OFF + 4 * 32 * 4;  // [UQ] resolved units (rows, entries, tiles)
+constexpr int SMEM_BYTES = 1024 + UR_OFF + UQ * 48;
 static_assert(SMEM_BYTES <= 232448, "shared memory over 227 KB");
 static_assert((11 + 2 * UQ) * 8 + UQ * 4 + 8 <= BAR_BYTES, "barrier region");
 constexpr int kMaxKK = 32;  // ranked rows per entry
@@ -183,6 +184,17 @@ __device__ __forceinline__ bool before(float v, uint32_t r, float w, uint32_t s)
     return v < w || (v == w && r < s);
 }
 
+// float -> unsigned key with the same order
+__device__ __forceinline__ uint32_t fkey(float v) {
+    const uint32_t u = __float_as_uint(v);
+    return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+
+// (value, row) as one 64-bit key in the order of before(); all ones = empty
+__device__ __forceinline__ uint64_t vr_key(float v, uint32_t r) {
+    return (static_cast<uint64_t>(fkey(v)) << 32) | r;
+}
+
 // Per stored row, the column factor and value of the ranking value
 // acc * (qf * f) + v: L2 (-2 s, |x|^2), cosine (-s / xv, 0), dot (-s, 0),
 // s the row's power-of-two scale.
@@ -246,14 +258,6 @@ __device__ __forceinline__ void insert_sorted(float (&tv)[GK], float v) {
     tv[0] = fminf(tv[0], v);
 }
 
-template <int GK>
-__device__ __forceinline__ float pick_gk(const float (&tv)[GK], int i) {
-    float r = tv[0];
-#pragma unroll
-    for (int j = 1; j < GK; ++j) r = j == i ? tv[j] : r;
-    return r;
-}
-
 // Paired fp32 arithmetic (sm_100): two IEEE round-to-nearest operations per
 // instruction, each identical to its scalar form.
 __device__ __forceinline__ uint64_t pack2(float a, float b) {
@@ -274,6 +278,19 @@ __device__ __forceinline__ uint64_t fma_f32x2(uint64_t a, uint64_t b, uint64_t c
     asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
     return d;
 }
+
+// A unit of work as the producer resolves it once for the other roles: list
+// rows [r0, r1), entries [ec, e1), row tiles.
+struct UnitRec {
+    int64_t r0, r1, ec, e1;
+    int ntiles, pad;
+};
+static_assert(sizeof(UnitRec) <= 48, "unit record slot");
+
+// A unit whose list fits the two TMEM accumulators (at most two row tiles) is
+// computed once: the collecting pass reads the accumulators the threshold
+// pass read (no second load and contraction of its tiles).
+__device__ __forceinline__ bool unit_reuses_tmem(int ntiles) { return ntiles <= 2; }
 
 // Row tile of step t2 of a unit: the threshold pass walks tiles 0 .. n - 1,
 // the collecting pass n - 1 .. 0 (its first tiles are the last ones loaded,
@@ -306,6 +323,7 @@ __global__ void __launch_bounds__(NTHR, 1)
     float* xs_s = reinterpret_cast<float*>(smem + XS_OFF);  // [EPIW][2][TR / 2]: row factor, row value
     float* mg_s = reinterpret_cast<float*>(smem + MG_OFF);
     float* th_s = reinterpret_cast<float*>(smem + TH_OFF);
+    volatile UnitRec* urec = reinterpret_cast<volatile UnitRec*>(smem + UR_OFF);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     if (threadIdx.x == 0) {
@@ -370,12 +388,17 @@ __global__ void __launch_bounds__(NTHR, 1)
                     ok = false;
                     break;
                 }
+                int64_t r0 = 0, r1 = 0, ec = 0, e1 = 0;
+                const int ntiles = u >= 0 ? unit_info(u, r0, r1, ec, e1) : 0;
+                urec[s].r0 = r0;
+                urec[s].r1 = r1;
+                urec[s].ec = ec;
+                urec[s].e1 = e1;
+                urec[s].ntiles = ntiles;
                 unit_slot[s] = u;
-                mbar_arrive_local(&ufull[s]);
+                mbar_arrive_local(&ufull[s]);  // release: the record is visible to the waiting roles
                 ++ui;
                 if (u < 0) break;
-                int64_t r0, r1, ec, e1;
-                const int ntiles = unit_info(u, r0, r1, ec, e1);
                 if (ntiles == 0) continue;
                 if (!mbar_wait(aempty, (at & 1) ^ 1, abort_flag)) {
                     ok = false;
@@ -388,7 +411,8 @@ __global__ void __launch_bounds__(NTHR, 1)
                 }
                 a_pending = true;
                 ++at;
-                for (int t2 = 0; t2 < NPASS * ntiles && ok; ++t2) {
+                const int mma_steps = (NPASS == 2 && unit_reuses_tmem(ntiles) ? 1 : NPASS) * ntiles;
+                for (int t2 = 0; t2 < mma_steps && ok; ++t2) {
                     const int t = tile_of(t2, ntiles);
                     const int row0 = static_cast<int>(r0 + static_cast<int64_t>(t) * TR);
                     for (int kb = 0; kb < nkb; ++kb) {
@@ -442,11 +466,10 @@ __global__ void __launch_bounds__(NTHR, 1)
                     break;
                 }
                 const int u = unit_slot[s];
+                const int ntiles = urec[s].ntiles;
                 mbar_arrive_local(&uempty[s]);
                 ++ui;
                 if (u < 0) break;
-                int64_t r0, r1, ec, e1;
-                const int ntiles = unit_info(u, r0, r1, ec, e1);
                 if (ntiles == 0) continue;
                 if (!mbar_wait(afull, at & 1, abort_flag)) {
                     ok = false;
@@ -454,7 +477,8 @@ __global__ void __launch_bounds__(NTHR, 1)
                 }
                 ++at;
                 tc_fence_after();
-                for (int t2 = 0; t2 < NPASS * ntiles && ok; ++t2, ++gt) {
+                const int mma_steps = (NPASS == 2 && unit_reuses_tmem(ntiles) ? 1 : NPASS) * ntiles;
+                for (int t2 = 0; t2 < mma_steps && ok; ++t2, ++gt) {
                     const int acc = gt & 1;
                     if (!mbar_wait(&tempty[acc], ((gt >> 1) & 1) ^ 1, abort_flag)) {
                         ok = false;
@@ -525,12 +549,12 @@ __global__ void __launch_bounds__(NTHR, 1)
                 break;
             }
             const int u = unit_slot[s];
+            const int64_t r0 = urec[s].r0, r1 = urec[s].r1, ec = urec[s].ec, e1 = urec[s].e1;
+            const int ntiles = urec[s].ntiles;
             __syncwarp();
             if (lane == 0) mbar_arrive_local(&uempty[s]);
             ++ui;
             if (u < 0) break;
-            int64_t r0, r1, ec, e1;
-            const int ntiles = unit_info(u, r0, r1, ec, e1);
             const int64_t e = ec + quad * 32 + lane;
             const bool evalid = e < e1;
             float qf = 0.f;
@@ -568,10 +592,17 @@ __global__ void __launch_bounds__(NTHR, 1)
             if (nsteps > 0) load_cols(tile_of(0, ntiles), fv1);
             if (nsteps > 1) load_cols(tile_of(1, ntiles), fv2);
             bool live = true;  // false once a wait gave up: the unit is walked without work
-            for (int t2 = 0; t2 < nsteps; ++t2, ++gt) {
+            // tile instance of step t2 in the MMA's sequence: one per step, or one
+            // per tile when the collecting pass re-reads the accumulators
+            const bool reuse = NPASS == 2 && unit_reuses_tmem(ntiles);
+            const uint32_t gt0 = gt;
+            for (int t2 = 0; t2 < nsteps; ++t2) {
                 const bool collect = t2 >= ntiles;
                 const int t = tile_of(t2, ntiles);
-                const int acc = gt & 1;
+                const uint32_t inst = gt0 + static_cast<uint32_t>(reuse ? t : t2);
+                const int acc = inst & 1;
+                const bool wait_acc = !(reuse && collect);   // the threshold pass waited for it
+                const bool free_acc = !reuse || collect;     // last read of this accumulator
                 float fc[4], vc[4];
 #pragma unroll
                 for (int j = 0; j < 4; ++j) {
@@ -588,19 +619,16 @@ __global__ void __launch_bounds__(NTHR, 1)
                     }
                     pair_sync(quad);
                     if (half == 0) {
-                        // kk-th smallest of the two ascending lists
+                        // kk-th smallest of the two ascending lists A (tv) and B (o):
+                        // min over i in [0, kk] of max(A_i, B_{kk-i}) with A_i the
+                        // i-th smallest (A_0 = -inf; A_i = +inf past the list)
                         const float* o = mg_s + (quad * 32 + lane) * GKMAX;
-                        int ia = 0, ib = 0;
-                        float kth = INFINITY;
-                        for (int r = 0; r < kk; ++r) {
-                            const float va = ia < GK ? pick_gk(tv, ia) : INFINITY;
-                            const float vb = ib < GK ? o[ib] : INFINITY;
-                            if (va <= vb) {
-                                kth = va;
-                                ++ia;
-                            } else {
-                                kth = vb;
-                                ++ib;
+                        float kth = o[kk - 1];  // i = 0
+#pragma unroll
+                        for (int i = 1; i <= GK; ++i) {
+                            if (i <= kk) {
+                                const float bi = i < kk ? o[kk - i - 1] : -INFINITY;
+                                kth = fminf(kth, fmaxf(tv[i - 1], bi));
                             }
                         }
                         th_s[quad * 32 + lane] = kth;
@@ -608,7 +636,7 @@ __global__ void __launch_bounds__(NTHR, 1)
                     pair_sync(quad);
                     thr = th_s[quad * 32 + lane];
                 }
-                if (live && !mbar_wait(&tfull[acc], (gt >> 1) & 1, abort_flag)) {
+                if (live && wait_acc && !mbar_wait(&tfull[acc], (inst >> 1) & 1, abort_flag)) {
                     if (*abort_flag == 0 && status) atomicOr(status, DEV_TIMEOUT_EPILOGUE);
                     *abort_flag = 1;
                     live = false;
@@ -637,7 +665,7 @@ __global__ void __launch_bounds__(NTHR, 1)
                             tmem_ld32_async(tbase + static_cast<uint32_t>(c * 32), rr);
                             tmem_ld_wait(rr);
                         }
-                        if (c == TR / 2 / 32 - 1) {
+                        if (c == TR / 2 / 32 - 1 && free_acc) {
                             // the accumulator is read: the MMA may overwrite it
                             tc_fence_before();
                             __syncwarp();
@@ -727,12 +755,13 @@ __global__ void __launch_bounds__(NTHR, 1)
                             }
                         }
                     }
-                } else {
+                } else if (free_acc) {
                     tc_fence_before();
                     __syncwarp();
                     if (lane == 0) mbar_arrive_local(&tempty[acc]);
                 }
             }
+            gt = gt0 + static_cast<uint32_t>(reuse ? ntiles : nsteps);
             if (!DENSE && evalid && live) a.cand_n[pe * 2 + half] = cnt;
         }
     }
@@ -771,27 +800,17 @@ __global__ void ivf_tc_finish_kernel(int cos_small, const float* __restrict__ q,
     if (qi >= Q) return;
     const float* qp = q + qi * ldq;
     const float qvq = METRIC == RDB_METRIC_COSINE ? qv[qi] : 0.f;
-    float tv[KF];
-    uint32_t tr[KF];
+    // this lane's best KF (value, row) keys, ascending; branch-free insertion
+    // (element j becomes max(min(tk[j], key), tk[j - 1]))
+    uint64_t tk[KF];
 #pragma unroll
-    for (int i = 0; i < KF; ++i) {
-        tv[i] = INFINITY;
-        tr[i] = kNoRow;
-    }
+    for (int i = 0; i < KF; ++i) tk[i] = ~0ull;
     auto offer = [&](float v, uint32_t r) {
-        if (!before(v, r, tv[KF - 1], tr[KF - 1])) return;
-        tv[KF - 1] = v;
-        tr[KF - 1] = r;
+        const uint64_t key = vr_key(v, r);
+        if (key >= tk[KF - 1]) return;
 #pragma unroll
-        for (int j = KF - 1; j > 0; --j) {
-            const bool sw = before(tv[j], tr[j], tv[j - 1], tr[j - 1]);
-            const float x0 = tv[j - 1], x1 = tv[j];
-            const uint32_t y0 = tr[j - 1], y1 = tr[j];
-            tv[j - 1] = sw ? x1 : x0;
-            tv[j] = sw ? x0 : x1;
-            tr[j - 1] = sw ? y1 : y0;
-            tr[j] = sw ? y0 : y1;
-        }
+        for (int j = KF - 1; j > 0; --j) tk[j] = max(min(tk[j], key), tk[j - 1]);
+        tk[0] = min(tk[0], key);
     };
     auto exact_dot = [&](uint32_t r) {
         const float* xp = rows + static_cast<int64_t>(r) * ldx;
@@ -842,27 +861,16 @@ __global__ void ivf_tc_finish_kernel(int cos_small, const float* __restrict__ q,
     // 3. the warp's best KF: KF rounds of the best list head, whose lane pops it
     uint32_t mine = kNoRow;  // merged row `lane`
     for (int rnd = 0; rnd < KF; ++rnd) {
-        float bv = tv[0];
-        uint32_t br = tr[0];
+        uint64_t best = tk[0];
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1) {
-            const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
-            const uint32_t orr = __shfl_xor_sync(0xffffffffu, br, o);
-            if (before(ov, orr, bv, br)) {
-                bv = ov;
-                br = orr;
-            }
-        }
-        if (br == kNoRow) break;  // every list is exhausted (warp-uniform)
-        if (tr[0] == br) {
+        for (int o = 16; o > 0; o >>= 1) best = min(best, __shfl_xor_sync(0xffffffffu, best, o));
+        if (best == ~0ull) break;  // every list is exhausted (warp-uniform)
+        const uint32_t br = static_cast<uint32_t>(best);
+        if (static_cast<uint32_t>(tk[0]) == br) {
             // a row probed twice (a repeated probe slot) leaves every list at once
 #pragma unroll
-            for (int j = 0; j < KF - 1; ++j) {
-                tv[j] = tv[j + 1];
-                tr[j] = tr[j + 1];
-            }
-            tv[KF - 1] = INFINITY;
-            tr[KF - 1] = kNoRow;
+            for (int j = 0; j < KF - 1; ++j) tk[j] = tk[j + 1];
+            tk[KF - 1] = ~0ull;
         }
         if (rnd == lane) mine = br;
     }
@@ -927,12 +935,6 @@ __global__ void probe_units_kernel(int64_t e0, int64_t e1, int nlist, int64_t* l
 
 constexpr int kProbeSlots = 256;  // collected centroids per query before the all-centroid rescan
 constexpr int kProbeTop = 128;    // nprobe + margin limit
-
-// float -> unsigned key with the same order (for counting below a value)
-__device__ __forceinline__ uint32_t fkey(float v) {
-    const uint32_t u = __float_as_uint(v);
-    return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
-}
 
 // Exact squared L2 of query qp and centroid cp with the flat search's
 // arithmetic: lane-strided fused multiply-add chains, then a butterfly sum
