@@ -299,6 +299,17 @@ int rdb_f16_split(const float* x, int64_t n, int64_t ldx, int d, void* hi, void*
  * rows_hi / rows_lo [nrows, ldp] and row_scale [nrows] from rdb_f16_split of
  * the same rows, ldp = d rounded up to a multiple of 64, 16-byte aligned.
  * Supported for d <= 128 and k <= 24 (rdb_ivf_flat_search_tc_supported). */
+/* The same search over fp16 / bf16 rows (dtype RDB_F16 / RDB_BF16) and
+ * queries of the same type, as rdb_ivf_flat_scan takes them: the MMA reads
+ * the stored rows directly (stride ldx elements, a multiple of 8; one exact
+ * fp16 / bf16 product per element into fp32), no planes; the best k + 8
+ * rows per query are rescored with rdb_ivf_flat_scan's arithmetic, so scores
+ * equal its scores.  Workspace rdb_ivf_flat_search_tc_workspace. */
+int rdb_ivf_flat_search_tc_half(int metric, int dtype, const void* q, int64_t nq, int64_t ldq, int d,
+                                const int64_t* probe, int nprobe, const void* rows, int64_t ldx, const float* xv,
+                                int64_t nrows, const int64_t* list_off, const int64_t* list_end, int nlist,
+                                const int64_t* ids, int k, float* out_v, int64_t* out_i, void* ws, size_t ws_bytes,
+                                void* stream);
 int rdb_ivf_flat_search_tc_supported(int d, int k);
 /* Counts on the current device since the last reset (host out[2]): out[0]
  * (query, probe slot) entries whose collected rows overflowed the per-entry

@@ -129,9 +129,10 @@ class IVFFlatIndex : public IVFBase {
     at::Tensor stored_sq8_scales() const;
     void restore_sq8(const at::Tensor& codes, const at::Tensor& scales, const at::Tensor& labels,
                      const at::Tensor& ids);
-    // Tensor-core search (rdb_ivf_flat_search_tc) of FP32 rows with dim <= 128
-    // and k <= 24, on by default: the index keeps fp16 hi / lo planes of its rows
-    // (rdb_f16_split, as many bytes again as the rows).  Off frees them and
+    // Tensor-core search with dim <= 128 and k <= 24, on by default: FP32 rows
+    // (rdb_ivf_flat_search_tc) through fp16 hi / lo planes the index keeps
+    // (rdb_f16_split, as many bytes again as the rows); FP16 / BF16 rows
+    // (rdb_ivf_flat_search_tc_half) as stored.  Off frees the planes and
     // searches with the CUDA-core list scan (rdb_ivf_flat_scan).
     void set_tensor_cores(bool on);
     bool tensor_cores() const { return tc_wanted_; }
@@ -140,6 +141,7 @@ class IVFFlatIndex : public IVFBase {
 
   private:
     bool tc_rows() const;  // planes kept: FP32 rows, dim <= 128, switched on
+    bool tc_half() const;  // FP16 / BF16 rows, dim <= 128, switched on: read as stored
     // planes (hi, lo, scale) of fp32 rows [m, ld_]; a value that is not
     // finite sets tc_bad_ (those rows are searched on CUDA cores)
     std::tuple<at::Tensor, at::Tensor, at::Tensor> split_rows(const at::Tensor& rows);

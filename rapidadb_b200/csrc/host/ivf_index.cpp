@@ -345,9 +345,14 @@ bool IVFFlatIndex::tc_rows() const {
     return tc_wanted_ && precision_ == Precision::FP32 && rdb_ivf_flat_search_tc_supported(dim_, 1);
 }
 
+bool IVFFlatIndex::tc_half() const {
+    return tc_wanted_ && (precision_ == Precision::FP16 || precision_ == Precision::BF16) &&
+           rdb_ivf_flat_search_tc_supported(dim_, 1);
+}
+
 bool IVFFlatIndex::tensor_core_search(int64_t k) const {
-    return tc_rows() && !tc_bad_ && hi_.defined() && k >= 1 && k <= 32 &&
-           rdb_ivf_flat_search_tc_supported(dim_, static_cast<int>(k)) != 0;
+    const bool ready = (tc_rows() && hi_.defined()) || (tc_half() && rows_.defined());
+    return ready && !tc_bad_ && k >= 1 && k <= 32 && rdb_ivf_flat_search_tc_supported(dim_, static_cast<int>(k)) != 0;
 }
 
 std::tuple<at::Tensor, at::Tensor, at::Tensor> IVFFlatIndex::split_rows(const at::Tensor& rows) {
@@ -367,7 +372,12 @@ std::tuple<at::Tensor, at::Tensor, at::Tensor> IVFFlatIndex::split_rows(const at
 void IVFFlatIndex::rebuild_planes() {
     hi_ = lo_ = rscale_ = at::Tensor();
     tc_bad_ = false;
-    if (!tc_rows() || !rows_.defined() || rows_.size(0) == 0) return;
+    if (!rows_.defined() || rows_.size(0) == 0) return;
+    if (tc_half()) {
+        tc_bad_ = !at::isfinite(rows_).all().item<bool>();
+        return;
+    }
+    if (!tc_rows()) return;
     std::tie(hi_, lo_, rscale_) = split_rows(rows_);
 }
 
@@ -400,8 +410,10 @@ void IVFFlatIndex::add(const at::Tensor& vectors, const at::Tensor& ids) {
         xv_new = row_values(metric_, rows_new, dim_);
     }
     TORCH_CHECK(n_ + m < (int64_t(1) << 32), "at most 2^32 - 1 rows per device");
-    // fp16 planes of the new rows (tensor-core search), moved like the rows
+    // fp16 planes of the new rows (tensor-core search), moved like the rows;
+    // fp16 / bf16 rows are read as stored, only checked for non-finite values
     const bool planes = tc_rows() && (n_ == 0 || hi_.defined());
+    if (tc_half() && !at::isfinite(rows_new).all().item<bool>()) tc_bad_ = true;
     at::Tensor hi_new, lo_new, rs_new;
     if (planes) std::tie(hi_new, lo_new, rs_new) = split_rows(rows_new);
     at::Tensor dest;
@@ -519,6 +531,20 @@ Result IVFFlatIndex::search_probed(const at::Tensor& queries, const at::Tensor& 
     at::Tensor q = sq8() ? prepare_rows(qd, at::kFloat, padded_ld(dim_, at::kFloat))
                          : prepare_rows(qd, rows_.scalar_type(), ld_);
     const int64_t nq = q.size(0);
+    if (tensor_core_search(k) && tc_half()) {
+        at::Tensor ov = at::empty({nq, k}, q.options().dtype(at::kFloat));
+        at::Tensor oi = at::empty({nq, k}, q.options().dtype(at::kLong));
+        at::Tensor tws = ws_bytes(q, rdb_ivf_flat_search_tc_workspace(nq, np, nlist_, dim_, static_cast<int>(k), cap_));
+        check_status(rdb_ivf_flat_search_tc_half(static_cast<int>(metric_), dtype_code(rows_.scalar_type()),
+                                                 q.data_ptr(), nq, ld_, dim_, probe_lists.data_ptr<int64_t>(), np,
+                                                 rows_.data_ptr(), ld_, xv_.data_ptr<float>(), cap_,
+                                                 list_off_.data_ptr<int64_t>(), list_end_.data_ptr<int64_t>(),
+                                                 nlist_, ids_.data_ptr<int64_t>(), static_cast<int>(k),
+                                                 ov.data_ptr<float>(), oi.data_ptr<int64_t>(), tws.data_ptr(),
+                                                 tws.numel(), stream_ptr()),
+                     "ivf tensor-core search");
+        return {ov, oi};
+    }
     if (tensor_core_search(k)) {
         at::Tensor ov = at::empty({nq, k}, q.options().dtype(at::kFloat));
         at::Tensor oi = at::empty({nq, k}, q.options().dtype(at::kLong));

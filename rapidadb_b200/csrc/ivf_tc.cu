@@ -48,6 +48,7 @@
 //               insertion.
 // Every mbarrier wait is bounded (mbar_wait): a role that gives up sets the
 // abort flag and a status bit, and the CTA frees its TMEM and exits.
+#include <cuda_bf16.h>
 #include <cuda_fp16.h>
 
 #include <algorithm>
@@ -157,6 +158,7 @@ struct IvfTcArgs {
     int metric;
     int cos_small;
     int nkb;                  // K blocks of 64 (padded dimension / 64)
+    int planes;               // 2: fp32 values as hi / lo fp16 planes; 1: fp16 / bf16 values as stored
     int kk;                   // ranked rows per entry (k + 8), <= kMaxKK
     const int2* units;        // (list, first entry) of each unit of work
     const int* nunits;
@@ -179,16 +181,15 @@ struct IvfTcArgs {
     float* dense_gmin;        // dense mode: minimum of each 32-row group, [entries][dense_ld / 32]
 };
 
-// (v, r) before (w, s): smaller value first, then the lower row
-__device__ __forceinline__ bool before(float v, uint32_t r, float w, uint32_t s) {
-    return v < w || (v == w && r < s);
-}
-
 // float -> unsigned key with the same order
 __device__ __forceinline__ uint32_t fkey(float v) {
     const uint32_t u = __float_as_uint(v);
     return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
 }
+
+__device__ __forceinline__ float tof(float v) { return v; }
+__device__ __forceinline__ float tof(__half v) { return __half2float(v); }
+__device__ __forceinline__ float tof(__nv_bfloat16 v) { return __bfloat162float(v); }
 
 // (value, row) as one 64-bit key in the order of before(); all ones = empty
 __device__ __forceinline__ uint64_t vr_key(float v, uint32_t r) {
@@ -202,7 +203,7 @@ __global__ void col_factors_kernel(int metric, const float* __restrict__ row_sca
                                    int64_t n, float2* __restrict__ out) {
     const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= n) return;
-    const float rs = row_scale[i];
+    const float rs = row_scale ? row_scale[i] : 1.f;
     if (metric == RDB_METRIC_L2)
         out[i] = make_float2(-2.f * rs, xv[i]);
     else if (metric == RDB_METRIC_COSINE)
@@ -404,10 +405,11 @@ __global__ void __launch_bounds__(NTHR, 1)
                     ok = false;
                     break;
                 }
-                mbar_arrive_expect_tx(afull, 2 * nkb * A_BLK);
+                mbar_arrive_expect_tx(afull, a.planes * nkb * A_BLK);
                 for (int kb = 0; kb < nkb; ++kb) {
                     tma_load_2d(&mqh, afull, abuf + kb * A_BLK, kb * TK, static_cast<int>(ec));
-                    tma_load_2d(&mql, afull, abuf + (kMaxKB + kb) * A_BLK, kb * TK, static_cast<int>(ec));
+                    if (a.planes == 2)
+                        tma_load_2d(&mql, afull, abuf + (kMaxKB + kb) * A_BLK, kb * TK, static_cast<int>(ec));
                 }
                 a_pending = true;
                 ++at;
@@ -421,9 +423,9 @@ __global__ void __launch_bounds__(NTHR, 1)
                             break;
                         }
                         uint8_t* sp = ring + stage * STAGE_BYTES;
-                        mbar_arrive_expect_tx(&full[stage], STAGE_BYTES);
+                        mbar_arrive_expect_tx(&full[stage], a.planes * B_PLANE);
                         tma_load_2d(&mxh, &full[stage], sp, kb * TK, row0);
-                        tma_load_2d(&mxl, &full[stage], sp + B_PLANE, kb * TK, row0);
+                        if (a.planes == 2) tma_load_2d(&mxl, &full[stage], sp + B_PLANE, kb * TK, row0);
                         issued_mask |= 1u << stage;
                         issued_phase = (issued_phase & ~(1u << stage)) | (phase << stage);
                         if (++stage == NSTAGE) {
@@ -497,11 +499,17 @@ __global__ void __launch_bounds__(NTHR, 1)
                         const uint32_t b_addr = smem_u32(ring + stage * STAGE_BYTES);
                         const uint64_t bh = make_sdesc(b_addr);
                         const uint64_t bl = make_sdesc(b_addr + B_PLANE);
+                        if (a.planes == 2) {
 #pragma unroll
-                        for (int k = 0; k < TK / 16; ++k) {
-                            umma_f16(d_tmem, ah + 2 * k, bh + 2 * k, idesc, (kb > 0 || k > 0) ? 1u : 0u);
-                            umma_f16(d_tmem, ah + 2 * k, bl + 2 * k, idesc, 1u);
-                            umma_f16(d_tmem, al + 2 * k, bh + 2 * k, idesc, 1u);
+                            for (int k = 0; k < TK / 16; ++k) {
+                                umma_f16(d_tmem, ah + 2 * k, bh + 2 * k, idesc, (kb > 0 || k > 0) ? 1u : 0u);
+                                umma_f16(d_tmem, ah + 2 * k, bl + 2 * k, idesc, 1u);
+                                umma_f16(d_tmem, al + 2 * k, bh + 2 * k, idesc, 1u);
+                            }
+                        } else {
+#pragma unroll
+                            for (int k = 0; k < TK / 16; ++k)
+                                umma_f16(d_tmem, ah + 2 * k, bh + 2 * k, idesc, (kb > 0 || k > 0) ? 1u : 0u);
                         }
                         any = true;
                         umma_commit(&empty[stage]);
@@ -785,11 +793,11 @@ __device__ unsigned long long g_probe_rescans;
 // products accumulated in dimension order, cosine through final_score), and
 // the best k of them (ties to the lower stored row) written to out_v / out_i
 // [nq, k].
-template <int METRIC, int KF>
-__global__ void ivf_tc_finish_kernel(int cos_small, const float* __restrict__ q, int64_t Q, int64_t ldq, int d,
+template <int METRIC, int KF, typename T>
+__global__ void ivf_tc_finish_kernel(int cos_small, const T* __restrict__ q, int64_t Q, int64_t ldq, int d,
                                      int nprobe, const int64_t* __restrict__ probe, int nlist,
                                      const int64_t* __restrict__ list_off, const int64_t* __restrict__ list_end,
-                                     const float* __restrict__ rows, int64_t ldx, const float* __restrict__ xv,
+                                     const T* __restrict__ rows, int64_t ldx, const float* __restrict__ xv,
                                      const float* __restrict__ qv, const float* __restrict__ cand_v,
                                      const uint32_t* __restrict__ cand_r, const int* __restrict__ cand_n,
                                      const int64_t* __restrict__ ids, int k, float* __restrict__ out_v,
@@ -798,7 +806,7 @@ __global__ void ivf_tc_finish_kernel(int cos_small, const float* __restrict__ q,
     const int lane = threadIdx.x & 31;
     const int64_t qi = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
     if (qi >= Q) return;
-    const float* qp = q + qi * ldq;
+    const T* qp = q + qi * ldq;
     const float qvq = METRIC == RDB_METRIC_COSINE ? qv[qi] : 0.f;
     // this lane's best KF (value, row) keys, ascending; branch-free insertion
     // (element j becomes max(min(tk[j], key), tk[j - 1]))
@@ -813,9 +821,9 @@ __global__ void ivf_tc_finish_kernel(int cos_small, const float* __restrict__ q,
         tk[0] = min(tk[0], key);
     };
     auto exact_dot = [&](uint32_t r) {
-        const float* xp = rows + static_cast<int64_t>(r) * ldx;
+        const T* xp = rows + static_cast<int64_t>(r) * ldx;
         float acc = 0.f;
-        for (int t = 0; t < d; ++t) acc = fmaf(qp[t], xp[t], acc);
+        for (int t = 0; t < d; ++t) acc = fmaf(tof(qp[t]), tof(xp[t]), acc);
         return acc;
     };
     // 1. rows collected for this query's entries (lane: probe slots lane, lane + 32, ...)
@@ -879,10 +887,10 @@ __global__ void ivf_tc_finish_kernel(int cos_small, const float* __restrict__ q,
     float sc = largest ? -INFINITY : INFINITY;
     if (mine != kNoRow) {
         if (METRIC == RDB_METRIC_L2) {
-            const float* xp = rows + static_cast<int64_t>(mine) * ldx;
+            const T* xp = rows + static_cast<int64_t>(mine) * ldx;
             float acc = 0.f;
             for (int t = 0; t < d; ++t) {
-                const float df = qp[t] - xp[t];
+                const float df = tof(qp[t]) - tof(xp[t]);
                 acc = fmaf(df, df, acc);
             }
             sc = acc;
@@ -1196,13 +1204,14 @@ TcWs tc_ws(int64_t nq, int nprobe, int nlist, int d, int k, int64_t nrows) {
     return w;
 }
 
-int map_f16(CUtensorMap* m, const void* base, int64_t rows, int64_t dp, int box_rows) {
-    return make_map(m, RDB_F16, base, rows, static_cast<int>(dp), dp * 2, TK, box_rows);
+int map_f16(CUtensorMap* m, const void* base, int64_t rows, int64_t dp, int box_rows, int dtype = RDB_F16,
+            int64_t ld = 0) {
+    return make_map(m, dtype, base, rows, static_cast<int>(dp), (ld ? ld : dp) * 2, TK, box_rows);
 }
 
 template <int METRIC, int GK, bool DENSE = false>
 int launch_scan(const CUtensorMap& mqh, const CUtensorMap& mql, const CUtensorMap& mxh, const CUtensorMap& mxl,
-                const IvfTcArgs& a, int grid, cudaStream_t s) {
+                const IvfTcArgs& a, int grid, cudaStream_t s, uint32_t idesc = tc_idesc(false, TQ, TR)) {
     static bool attr[64] = {false};
     int dev = 0;
     RDB_CUDA_TRY(cudaGetDevice(&dev));
@@ -1211,22 +1220,22 @@ int launch_scan(const CUtensorMap& mqh, const CUtensorMap& mql, const CUtensorMa
                                           cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES));
         attr[dev] = true;
     }
-    ivf_tc_scan_kernel<METRIC, GK, DENSE><<<grid, NTHR, SMEM_BYTES, s>>>(mqh, mql, mxh, mxl, a,
-                                                                         tc_idesc(false, TQ, TR),
+    ivf_tc_scan_kernel<METRIC, GK, DENSE><<<grid, NTHR, SMEM_BYTES, s>>>(mqh, mql, mxh, mxl, a, idesc,
                                                                          device_status_word());
     RDB_LAUNCH_CHECK();
     return RDB_OK;
 }
 
 struct FinishArgs {
-    const float* q;
+    int dtype;  // of q and rows
+    const void* q;
     int64_t nq, ldq;
     int d;
     const int64_t* probe;
     int nlist;
     const int64_t* list_off;
     const int64_t* list_end;
-    const float* rows;
+    const void* rows;
     int64_t ldx;
     const int64_t* ids;
     int k;
@@ -1234,32 +1243,144 @@ struct FinishArgs {
     int64_t* out_i;
 };
 
-template <int METRIC, int KF>
-int launch_finish(const IvfTcArgs& a, const FinishArgs& f, cudaStream_t s) {
-    ivf_tc_finish_kernel<METRIC, KF><<<(unsigned)((f.nq + 7) / 8), 256, 0, s>>>(
-        a.cos_small, f.q, f.nq, f.ldq, f.d, a.nprobe, f.probe, f.nlist, f.list_off, f.list_end, f.rows, f.ldx, a.xv,
-        a.qv, a.cand_v, a.cand_r, a.cand_n, f.ids, f.k, f.out_v, f.out_i);
+template <int METRIC, int KF, typename T>
+int launch_finish_t(const IvfTcArgs& a, const FinishArgs& f, cudaStream_t s) {
+    ivf_tc_finish_kernel<METRIC, KF, T><<<(unsigned)((f.nq + 7) / 8), 256, 0, s>>>(
+        a.cos_small, static_cast<const T*>(f.q), f.nq, f.ldq, f.d, a.nprobe, f.probe, f.nlist, f.list_off,
+        f.list_end, static_cast<const T*>(f.rows), f.ldx, a.xv, a.qv, a.cand_v, a.cand_r, a.cand_n, f.ids, f.k,
+        f.out_v, f.out_i);
     RDB_LAUNCH_CHECK();
     return RDB_OK;
+}
+
+template <int METRIC, int KF>
+int launch_finish(const IvfTcArgs& a, const FinishArgs& f, cudaStream_t s) {
+    if (f.dtype == RDB_F16) return launch_finish_t<METRIC, KF, __half>(a, f, s);
+    if (f.dtype == RDB_BF16) return launch_finish_t<METRIC, KF, __nv_bfloat16>(a, f, s);
+    return launch_finish_t<METRIC, KF, float>(a, f, s);
 }
 
 // scan with group-minimum lists of GK >= kk, then the per-query finish
 template <int METRIC, int GK>
 int run_metric(const CUtensorMap& mqh, const CUtensorMap& mql, const CUtensorMap& mxh, const CUtensorMap& mxl,
-               const IvfTcArgs& a, int grid, const FinishArgs& f, cudaStream_t s) {
+               const IvfTcArgs& a, int grid, uint32_t idesc, const FinishArgs& f, cudaStream_t s) {
     cudaEvent_t stop_ev;
     RDB_TRY(timing_begin(TIMING_IVF_SCAN, s, &stop_ev));
-    RDB_TRY((launch_scan<METRIC, GK>(mqh, mql, mxh, mxl, a, grid, s)));
+    RDB_TRY((launch_scan<METRIC, GK>(mqh, mql, mxh, mxl, a, grid, s, idesc)));
     if (stop_ev) RDB_CUDA_TRY(cudaEventRecord(stop_ev, s));
     return launch_finish<METRIC, GK>(a, f, s);
 }
 
 template <int METRIC>
 int run_kk(const CUtensorMap& mqh, const CUtensorMap& mql, const CUtensorMap& mxh, const CUtensorMap& mxl,
-           const IvfTcArgs& a, int grid, const FinishArgs& f, cudaStream_t s) {
-    if (a.kk <= 16) return run_metric<METRIC, 16>(mqh, mql, mxh, mxl, a, grid, f, s);
-    if (a.kk <= 24) return run_metric<METRIC, 24>(mqh, mql, mxh, mxl, a, grid, f, s);
-    return run_metric<METRIC, 32>(mqh, mql, mxh, mxl, a, grid, f, s);
+           const IvfTcArgs& a, int grid, uint32_t idesc, const FinishArgs& f, cudaStream_t s) {
+    if (a.kk <= 16) return run_metric<METRIC, 16>(mqh, mql, mxh, mxl, a, grid, idesc, f, s);
+    if (a.kk <= 24) return run_metric<METRIC, 24>(mqh, mql, mxh, mxl, a, grid, idesc, f, s);
+    return run_metric<METRIC, 32>(mqh, mql, mxh, mxl, a, grid, idesc, f, s);
+}
+
+// One warp per entry: the entry's query, as stored (fp16 / bf16), gathered
+// into entry order with zero columns d .. dp - 1, scale 1.
+template <typename T>
+__global__ void gather_half_kernel(const T* __restrict__ q, int64_t ldq, int d, const int64_t* __restrict__ eperm,
+                                   int nprobe, int64_t E, T* __restrict__ out, int64_t dp, float* __restrict__ scale) {
+    const int lane = threadIdx.x & 31;
+    const int64_t e = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    if (e >= E) return;
+    const T* p = q + (eperm[e] / nprobe) * ldq;
+    for (int t = lane; t < (int)dp; t += 32) out[e * dp + t] = t < d ? p[t] : T(0.f);
+    if (lane == 0) scale[e] = 1.f;
+}
+
+// The tensor-core IVF-Flat search over fp32 rows (split planes) or fp16 /
+// bf16 rows (as stored, one product per element).
+int search_tc_impl(int metric, int dtype, const void* q, int64_t nq, int64_t ldq, int d, const int64_t* probe,
+                   int nprobe, const void* rows, int64_t ldx, const float* xv, const void* rows_hi, const void* rows_lo,
+                   const float* row_scale, int64_t ldp, int64_t nrows, const int64_t* list_off,
+                   const int64_t* list_end, int nlist, const int64_t* ids, int k, float* out_v, int64_t* out_i,
+                   void* ws, size_t ws_bytes, cudaStream_t s) {
+    const bool split = dtype == RDB_F32;
+    const TcWs w = tc_ws(nq, nprobe, nlist, d, k, nrows);
+    if (split) RDB_CHECK_ARG(ldp == w.dp, "row planes must have a stride of %lld (d padded to 64)", (long long)w.dp);
+    RDB_CHECK_ARG(w.E < (1LL << 31) - TQ && nrows < (1LL << 31) - TR, "too many entries or rows for one search");
+    if (ws_bytes < w.bytes) return set_error(RDB_ERR_WORKSPACE, "workspace too small: %zu < %zu", ws_bytes, w.bytes);
+    char* base = static_cast<char*>(ws);
+    RDB_TRY(invert_probes(probe, nq, nprobe, nlist, w.inv, base, s));
+    const int64_t* eperm = reinterpret_cast<const int64_t*>(base + w.inv.off_perm);
+    const int64_t* eseg = reinterpret_cast<const int64_t*>(base + w.inv.off_seg);
+    float* qv = reinterpret_cast<float*>(base + w.inv.off_qv);
+    if (metric == RDB_METRIC_COSINE) {
+        RDB_TRY(row_sqnorms_ld(dtype, q, nq, d, ldq, qv, s));
+        RDB_TRY(rdb_vec_values(metric, d, qv, nq, qv, s));
+    }
+    __half* qh = reinterpret_cast<__half*>(base + w.off_qh);
+    __half* ql = reinterpret_cast<__half*>(base + w.off_ql);
+    float* qs = reinterpret_cast<float*>(base + w.off_qs);
+    // the probing queries, entry by entry in list order
+    const unsigned gblocks = (unsigned)((w.E + 7) / 8);
+    if (split) {
+        split_f16_kernel<<<gblocks, 256, 0, s>>>(static_cast<const float*>(q), w.E, ldq, d, qh, ql, w.dp, qs, eperm,
+                                                 nprobe, nullptr);
+    } else if (dtype == RDB_F16) {
+        gather_half_kernel<__half><<<gblocks, 256, 0, s>>>(static_cast<const __half*>(q), ldq, d, eperm, nprobe, w.E,
+                                                           qh, w.dp, qs);
+    } else {
+        gather_half_kernel<__nv_bfloat16><<<gblocks, 256, 0, s>>>(static_cast<const __nv_bfloat16*>(q), ldq, d,
+                                                                  eperm, nprobe, w.E,
+                                                                  reinterpret_cast<__nv_bfloat16*>(qh), w.dp, qs);
+    }
+    RDB_LAUNCH_CHECK();
+    int2* units = reinterpret_cast<int2*>(base + w.off_units);
+    int* counters = reinterpret_cast<int*>(base + w.off_n);
+    ivf_tc_units_kernel<<<1, 1024, 0, s>>>(eseg, nlist, units, counters, counters + 1);
+    RDB_LAUNCH_CHECK();
+    float2* colfv = reinterpret_cast<float2*>(base + w.off_fv);
+    if (nrows > 0) {
+        col_factors_kernel<<<(unsigned)((nrows + 255) / 256), 256, 0, s>>>(metric, row_scale, xv, nrows, colfv);
+        RDB_LAUNCH_CHECK();
+    }
+    const int mdt = split ? RDB_F16 : dtype;  // element type the MMA reads
+    CUtensorMap mqh, mql, mxh, mxl;
+    RDB_TRY(map_f16(&mqh, qh, w.E, w.dp, TQ, mdt));
+    RDB_TRY(map_f16(&mql, ql, w.E, w.dp, TQ, mdt));
+    if (split) {
+        RDB_TRY(map_f16(&mxh, rows_hi, std::max<int64_t>(nrows, 1), w.dp, TR));
+        RDB_TRY(map_f16(&mxl, rows_lo, std::max<int64_t>(nrows, 1), w.dp, TR));
+    } else {
+        // the stored rows themselves: ldx columns (zero past d), K blocks past them read as zero
+        RDB_TRY(map_f16(&mxh, rows, std::max<int64_t>(nrows, 1), ldx, TR, mdt, ldx));
+        mxl = mxh;
+    }
+    IvfTcArgs a = {};
+    a.metric = metric;
+    a.cos_small = d <= 128 ? 1 : 0;
+    a.nkb = static_cast<int>(w.dp / TK);
+    a.planes = split ? 2 : 1;
+    a.kk = w.kk;
+    a.units = units;
+    a.nunits = counters;
+    a.unit_ctr = counters + 1;
+    a.eseg = eseg;
+    a.eperm = eperm;
+    a.nprobe = nprobe;
+    a.list_off = list_off;
+    a.list_end = list_end;
+    a.xv = xv;
+    a.row_scale = row_scale;
+    a.colfv = colfv;
+    a.qv = qv;
+    a.ent_scale = qs;
+    a.cand_v = reinterpret_cast<float*>(base + w.off_cv);
+    a.cand_r = reinterpret_cast<uint32_t*>(base + w.off_cr);
+    a.cand_n = reinterpret_cast<int*>(base + w.off_cn);
+    FinishArgs f = {dtype, q, nq, ldq, d, probe, nlist, list_off, list_end, rows, ldx, ids, k, out_v, out_i};
+    const int grid = static_cast<int>(std::min<int64_t>(w.max_units, num_sms()));
+    const uint32_t idesc = tc_idesc(mdt == RDB_BF16, TQ, TR);
+    switch (metric) {
+        case RDB_METRIC_L2: return run_kk<RDB_METRIC_L2>(mqh, mql, mxh, mxl, a, grid, idesc, f, s);
+        case RDB_METRIC_COSINE: return run_kk<RDB_METRIC_COSINE>(mqh, mql, mxh, mxl, a, grid, idesc, f, s);
+        default: return run_kk<RDB_METRIC_DOT>(mqh, mql, mxh, mxl, a, grid, idesc, f, s);
+    }
 }
 
 }  // namespace
@@ -1315,71 +1436,31 @@ int rdb_ivf_flat_search_tc(int metric, const float* q, int64_t nq, int64_t ldq, 
     RDB_CHECK_ARG(q && probe && rows && rows_hi && rows_lo && row_scale && list_off && out_v && out_i && ws,
                   "NULL pointer");
     RDB_CHECK_ARG(metric == RDB_METRIC_DOT || xv, "cosine / L2 need per-row values");
-    const TcWs w = tc_ws(nq, nprobe, nlist, d, k, nrows);
-    RDB_CHECK_ARG(ldp == w.dp, "row planes must have a stride of %lld (d padded to 64)", (long long)w.dp);
-    RDB_CHECK_ARG(w.E < (1LL << 31) - TQ && nrows < (1LL << 31) - TR, "too many entries or rows for one search");
     RDB_CHECK_ARG((reinterpret_cast<uintptr_t>(rows_hi) & 15) == 0 && (reinterpret_cast<uintptr_t>(rows_lo) & 15) == 0,
                   "row planes must be 16-byte aligned");
-    if (ws_bytes < w.bytes) return set_error(RDB_ERR_WORKSPACE, "workspace too small: %zu < %zu", ws_bytes, w.bytes);
-    cudaStream_t s = static_cast<cudaStream_t>(stream);
-    char* base = static_cast<char*>(ws);
-    RDB_TRY(invert_probes(probe, nq, nprobe, nlist, w.inv, base, s));
-    const int64_t* eperm = reinterpret_cast<const int64_t*>(base + w.inv.off_perm);
-    const int64_t* eseg = reinterpret_cast<const int64_t*>(base + w.inv.off_seg);
-    float* qv = reinterpret_cast<float*>(base + w.inv.off_qv);
-    if (metric == RDB_METRIC_COSINE) {
-        RDB_TRY(row_sqnorms_ld(RDB_F32, q, nq, d, ldq, qv, s));
-        RDB_TRY(rdb_vec_values(metric, d, qv, nq, qv, s));
-    }
-    __half* qh = reinterpret_cast<__half*>(base + w.off_qh);
-    __half* ql = reinterpret_cast<__half*>(base + w.off_ql);
-    float* qs = reinterpret_cast<float*>(base + w.off_qs);
-    // the probing queries, entry by entry in list order, as scaled fp16 planes
-    split_f16_kernel<<<(unsigned)((w.E + 7) / 8), 256, 0, s>>>(q, w.E, ldq, d, qh, ql, w.dp, qs, eperm, nprobe,
-                                                                nullptr);
-    RDB_LAUNCH_CHECK();
-    int2* units = reinterpret_cast<int2*>(base + w.off_units);
-    int* counters = reinterpret_cast<int*>(base + w.off_n);
-    ivf_tc_units_kernel<<<1, 1024, 0, s>>>(eseg, nlist, units, counters, counters + 1);
-    RDB_LAUNCH_CHECK();
-    float2* colfv = reinterpret_cast<float2*>(base + w.off_fv);
-    if (nrows > 0) {
-        col_factors_kernel<<<(unsigned)((nrows + 255) / 256), 256, 0, s>>>(metric, row_scale, xv, nrows, colfv);
-        RDB_LAUNCH_CHECK();
-    }
-    CUtensorMap mqh, mql, mxh, mxl;
-    RDB_TRY(map_f16(&mqh, qh, w.E, w.dp, TQ));
-    RDB_TRY(map_f16(&mql, ql, w.E, w.dp, TQ));
-    RDB_TRY(map_f16(&mxh, rows_hi, std::max<int64_t>(nrows, 1), w.dp, TR));
-    RDB_TRY(map_f16(&mxl, rows_lo, std::max<int64_t>(nrows, 1), w.dp, TR));
-    IvfTcArgs a = {};
-    a.metric = metric;
-    a.cos_small = d <= 128 ? 1 : 0;
-    a.nkb = static_cast<int>(w.dp / TK);
-    a.kk = w.kk;
-    a.units = units;
-    a.nunits = counters;
-    a.unit_ctr = counters + 1;
-    a.eseg = eseg;
-    a.eperm = eperm;
-    a.nprobe = nprobe;
-    a.list_off = list_off;
-    a.list_end = list_end;
-    a.xv = xv;
-    a.row_scale = row_scale;
-    a.colfv = colfv;
-    a.qv = qv;
-    a.ent_scale = qs;
-    a.cand_v = reinterpret_cast<float*>(base + w.off_cv);
-    a.cand_r = reinterpret_cast<uint32_t*>(base + w.off_cr);
-    a.cand_n = reinterpret_cast<int*>(base + w.off_cn);
-    FinishArgs f = {q, nq, ldq, d, probe, nlist, list_off, list_end, rows, ldx, ids, k, out_v, out_i};
-    const int grid = static_cast<int>(std::min<int64_t>(w.max_units, num_sms()));
-    switch (metric) {
-        case RDB_METRIC_L2: return run_kk<RDB_METRIC_L2>(mqh, mql, mxh, mxl, a, grid, f, s);
-        case RDB_METRIC_COSINE: return run_kk<RDB_METRIC_COSINE>(mqh, mql, mxh, mxl, a, grid, f, s);
-        default: return run_kk<RDB_METRIC_DOT>(mqh, mql, mxh, mxl, a, grid, f, s);
-    }
+    return search_tc_impl(metric, RDB_F32, q, nq, ldq, d, probe, nprobe, rows, ldx, xv, rows_hi, rows_lo, row_scale,
+                          ldp, nrows, list_off, list_end, nlist, ids, k, out_v, out_i, ws, ws_bytes,
+                          static_cast<cudaStream_t>(stream));
+}
+
+int rdb_ivf_flat_search_tc_half(int metric, int dtype, const void* q, int64_t nq, int64_t ldq, int d,
+                                const int64_t* probe, int nprobe, const void* rows, int64_t ldx, const float* xv,
+                                int64_t nrows, const int64_t* list_off, const int64_t* list_end, int nlist,
+                                const int64_t* ids, int k, float* out_v, int64_t* out_i, void* ws, size_t ws_bytes,
+                                void* stream) {
+    RDB_CHECK_ARG(metric >= 0 && metric <= 2, "unknown metric %d", metric);
+    RDB_CHECK_ARG(dtype == RDB_F16 || dtype == RDB_BF16, "rows must be fp16 or bf16");
+    RDB_CHECK_ARG(nq >= 0 && nprobe >= 1 && nlist >= 1 && nlist <= kMaxLabels, "bad shape");
+    RDB_CHECK_ARG(rdb_ivf_flat_search_tc_supported(d, k), "tensor-core IVF search: d must be in [1, %d], k in [1, %d]",
+                  kMaxDp, kMaxKK - kL2Margin);
+    RDB_CHECK_ARG(ldx >= d && ldx % 8 == 0, "row stride must be a multiple of 8 elements (16 bytes)");
+    if (nq == 0) return RDB_OK;
+    RDB_CHECK_ARG(q && probe && rows && list_off && out_v && out_i && ws, "NULL pointer");
+    RDB_CHECK_ARG(metric == RDB_METRIC_DOT || xv, "cosine / L2 need per-row values");
+    RDB_CHECK_ARG((reinterpret_cast<uintptr_t>(rows) & 15) == 0, "rows must be 16-byte aligned");
+    return search_tc_impl(metric, dtype, q, nq, ldq, d, probe, nprobe, rows, ldx, xv, nullptr, nullptr, nullptr, 0,
+                          nrows, list_off, list_end, nlist, ids, k, out_v, out_i, ws, ws_bytes,
+                          static_cast<cudaStream_t>(stream));
 }
 
 int rdb_ivf_probe_tc_supported(int d, int nlist, int nprobe) {
@@ -1430,6 +1511,7 @@ int rdb_ivf_probe_tc(const float* q, int64_t nq, int64_t ldq, int d, const float
     a.metric = RDB_METRIC_L2;
     a.cos_small = 1;
     a.nkb = static_cast<int>(w.dp / TK);
+    a.planes = 2;
     a.kk = 1;
     a.units = units;
     a.nunits = counters;

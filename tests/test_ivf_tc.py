@@ -197,7 +197,35 @@ def test_tc_off_for_non_finite_rows_and_unsupported_shapes(device):
     half = _C.IVFFlatIndex(16, _C.Metric.L2, 1, 1, _C.Precision.FP16)
     half.set_quantizer(cent)
     half.add(x)
-    assert not half.tensor_core_search(10)  # fp16 storage: CUDA-core scan
+    assert half.tensor_core_search(10)  # fp16 storage: the stored rows feed the MMA
+    half.add(bad)
+    assert not half.tensor_core_search(10)
+    sq8 = _C.IVFFlatIndex(16, _C.Metric.L2, 1, 1, _C.Precision.INT8)
+    sq8.set_quantizer(cent)
+    sq8.add(x)
+    assert not sq8.tensor_core_search(10)  # INT8 (SQ8) storage: CUDA-core scan
+
+
+@pytest.mark.parametrize("precision", ["FP16", "BF16"])
+@pytest.mark.parametrize("metric", METRICS)
+@pytest.mark.parametrize("d", [128, 100, 32])
+def test_tc_half_storage_equals_cuda_core_scan(device, precision, metric, d):
+    """fp16 / bf16 rows: the MMA reads the stored rows (one exact product per
+    element, K past d read as zero) and the kept rows are rescored with the
+    CUDA-core scan's half-precision arithmetic: scores equal bit for bit."""
+    import rapidadb._C as _C
+    from rapidadb_b200.kmeans import kmeans
+
+    x, g = mixture(12, 20000, d, 40)
+    q = (x[g.integers(0, len(x), 300)] + 0.4 * g.standard_normal((300, d))).astype(np.float32)
+    xt = torch.from_numpy(x).cuda()
+    cent = kmeans(xt, 40, 5, 0.0, seed=3).centroids
+    idx = _C.IVFFlatIndex(d, _met(_C, metric), 40, 5, getattr(_C.Precision, precision))
+    idx.set_quantizer(cent)
+    idx.add(xt[:7000])
+    idx.add(xt[7000:])
+    dt, it, ds, is_ = both_paths(idx, q, 10)
+    assert_topk_match(ds, is_, dt, it, rtol=0.0, atol=0.0, name=f"{precision} {metric} d={d}")
 
 
 def test_tc_restore_rebuilds_planes(device, tmp_path):
