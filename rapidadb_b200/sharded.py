@@ -29,7 +29,30 @@ def shard_range(n: int, rank: int, world: int) -> Tuple[int, int]:
     return lo, hi
 
 
-def pack_lists(local_d: torch.Tensor, local_i: torch.Tensor) -> torch.Tensor:
+class BufferPool:
+    """Device buffers kept across searches, one per (name, shape, dtype,
+    device).  The tensors a search hands to NCCL are reused instead of
+    allocated every search: the caching allocator cannot hand out a block that
+    a collective still holds, so a host running several searches ahead of the
+    GPU would otherwise grow the pool with new device allocations.  Reuse is in
+    stream order: every collective here is issued blocking (the current stream
+    waits for it), so a later search's writes follow the earlier reads.  One
+    buffer is kept per distinct shape; nothing returned to a caller aliases
+    them."""
+
+    def __init__(self):
+        self._bufs = {}
+
+    def get(self, name: str, shape, dtype, device) -> torch.Tensor:
+        key = (name, tuple(int(v) for v in shape), dtype, str(device))
+        t = self._bufs.get(key)
+        if t is None:
+            t = torch.empty(key[1], dtype=dtype, device=device)
+            self._bufs[key] = t
+        return t
+
+
+def pack_lists(local_d: torch.Tensor, local_i: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
     """[Q, k] fp32 scores and int64 ids -> one [Q, W] int32 block, W = 3k
     rounded up to even: row q holds k score words, a pad word when k is odd
     (keeping the ids 8-byte aligned), then the 2k words of the ids.  One
@@ -39,7 +62,9 @@ def pack_lists(local_d: torch.Tensor, local_i: torch.Tensor) -> torch.Tensor:
     if k % 2:
         parts.append(torch.zeros((Q, 1), dtype=torch.int32, device=local_d.device))
     parts.append(local_i.contiguous().view(torch.int32))
-    return torch.cat(parts, dim=1)
+    if out is None:
+        return torch.cat(parts, dim=1)
+    return torch.cat(parts, dim=1, out=out)
 
 
 def unpack_lists(buf: torch.Tensor, k: int) -> Tuple[torch.Tensor, torch.Tensor]:
@@ -48,21 +73,30 @@ def unpack_lists(buf: torch.Tensor, k: int) -> Tuple[torch.Tensor, torch.Tensor]
     return buf[..., :k].view(torch.float32), buf[..., off:off + 2 * k].view(torch.int64)
 
 
+def _packed_width(k: int) -> int:
+    return 3 * k + (k % 2)
+
+
 def gather_candidates(local_d: torch.Tensor, local_i: torch.Tensor,
-                      group: Optional[dist.ProcessGroup] = None) -> Tuple[torch.Tensor, torch.Tensor]:
+                      group: Optional[dist.ProcessGroup] = None,
+                      pool: Optional[BufferPool] = None) -> Tuple[torch.Tensor, torch.Tensor]:
     """All-gather every rank's [Q, k] scores and ids with ONE collective of
     packed rows (pack_lists); returns [G, Q, k] score and id views of the
     receive buffer, which the merge reads in place."""
     world = dist.get_world_size(group)
     Q, k = local_d.shape
-    send = pack_lists(local_d, local_i)
-    out = torch.empty((world,) + tuple(send.shape), dtype=torch.int32, device=local_d.device)
+    dev = local_d.device
+    W = _packed_width(k)
+    send = pack_lists(local_d, local_i, pool.get("send", (Q, W), torch.int32, dev) if pool else None)
+    out = (pool.get("gather", (world, Q, W), torch.int32, dev) if pool
+           else torch.empty((world, Q, W), dtype=torch.int32, device=dev))
     dist.all_gather_into_tensor(out.view(-1), send.view(-1), group=group)
     return unpack_lists(out, k)
 
 
 def exchange_owned(local_d: torch.Tensor, local_i: torch.Tensor,
-                   group: Optional[dist.ProcessGroup] = None) -> Tuple[torch.Tensor, torch.Tensor]:
+                   group: Optional[dist.ProcessGroup] = None,
+                   pool: Optional[BufferPool] = None) -> Tuple[torch.Tensor, torch.Tensor]:
     """Owner exchange of [Q, k] lists: query slice r (shard_range(Q, r,
     world), contiguous rows) of every rank goes to rank r, which receives
     [G, Q_r, k] scores and ids -- 1 / G of an all-gather's bytes, in ONE
@@ -70,11 +104,13 @@ def exchange_owned(local_d: torch.Tensor, local_i: torch.Tensor,
     world = dist.get_world_size(group)
     rank = dist.get_rank(group)
     Q, k = local_d.shape
-    send = pack_lists(local_d, local_i)
-    W = send.shape[1]
+    dev = local_d.device
+    W = _packed_width(k)
+    send = pack_lists(local_d, local_i, pool.get("send", (Q, W), torch.int32, dev) if pool else None)
     sizes = [(b - a) * W for a, b in (shard_range(Q, r, world) for r in range(world))]
     n_r = sizes[rank] // W
-    recv = torch.empty((world, n_r, W), dtype=torch.int32, device=local_d.device)
+    recv = (pool.get("owned", (world, n_r, W), torch.int32, dev) if pool
+            else torch.empty((world, n_r, W), dtype=torch.int32, device=dev))
     dist.all_to_all_single(recv.view(-1), send.view(-1), [sizes[rank]] * world, sizes, group=group)
     return unpack_lists(recv, k)
 
@@ -264,6 +300,7 @@ class ShardedSearch(_ShardSizes):
         self.group = group
         self.merge = merge or gpu_merge
         self.results = results
+        self.pool = BufferPool()
         # the extension FlatIndex (directly or inside a RapidaDB facade) with
         # fp16 / bf16 rows can share one sampled threshold across the shards
         flat = getattr(index, "index", index)
@@ -304,15 +341,15 @@ class ShardedSearch(_ShardSizes):
             # rank's maxima, then the thresholds are all-gathered
             lo, hi = self.owned_range(Q)
             sizes = [(b - a) * gl for a, b in (shard_range(Q, r, world) for r in range(world))]
-            recv = torch.empty(world * (hi - lo) * gl, dtype=maxima.dtype, device=dev)
+            recv = self.pool.get("maxima", (world * (hi - lo) * gl,), maxima.dtype, dev)
             dist.all_to_all_single(recv, maxima.contiguous().view(-1), [(hi - lo) * gl] * world, sizes,
                                    group=self.group)
             mine = recv.view(world, hi - lo, gl).permute(1, 0, 2).reshape(hi - lo, world * gl)
             cap = -(-Q // world)  # slices differ by at most one query: pad to the largest
-            thr_mine = torch.zeros(cap, dtype=maxima.dtype, device=dev)
+            thr_mine = self.pool.get("thr_mine", (cap,), maxima.dtype, dev)  # rows past hi - lo: padding
             if hi > lo:
                 thr_mine[: hi - lo] = C().select_threshold(mine, k, self.largest)
-            allt = torch.empty(world * cap, dtype=maxima.dtype, device=dev)
+            allt = self.pool.get("thr_all", (world * cap,), maxima.dtype, dev)
             dist.all_gather_into_tensor(allt, thr_mine, group=self.group)
             if Q % world == 0:
                 thr = allt
@@ -321,7 +358,7 @@ class ShardedSearch(_ShardSizes):
                 thr = torch.cat([allt[r, : b - a] for r, (a, b) in enumerate(shard_range(Q, r, world)
                                                                               for r in range(world))])
         else:
-            allm = torch.empty((world * Q, gl), dtype=maxima.dtype, device=dev)
+            allm = self.pool.get("maxima_all", (world * Q, gl), maxima.dtype, dev)
             dist.all_gather_into_tensor(allm, maxima.contiguous(), group=self.group)
             allm = allm.view(world, Q, gl).permute(1, 0, 2).reshape(Q, world * gl)
             thr = C().select_threshold(allm, k, self.largest)
@@ -344,9 +381,9 @@ class ShardedSearch(_ShardSizes):
         local_d, local_i = out
         self.clock.mark("scan")
         if self.results == "owner":
-            vals, ids = exchange_owned(local_d, local_i, self.group)
+            vals, ids = exchange_owned(local_d, local_i, self.group, self.pool)
         else:
-            vals, ids = gather_candidates(local_d, local_i, self.group)
+            vals, ids = gather_candidates(local_d, local_i, self.group, self.pool)
         self.clock.mark("result_exchange")
         res = self.merge(vals, ids, k, self.largest)
         self.clock.mark("merge")
@@ -380,6 +417,7 @@ class ShardedIVFSearch(_ShardSizes):
         self.group = group
         self.merge = merge or gpu_merge
         self.results = results
+        self.pool = BufferPool()
 
     def owned_range(self, Q: int) -> Tuple[int, int]:
         """Queries [lo, hi) of a Q-query batch whose answers this rank returns."""
@@ -397,12 +435,12 @@ class ShardedIVFSearch(_ShardSizes):
         lo, hi = min(rank * chunk, Q), min((rank + 1) * chunk, Q)
         local = self.index.probe(queries[lo:hi]) if hi > lo else None
         np_ = local.shape[1] if local is not None else self.index.probe(queries[:1]).shape[1]
-        buf = torch.zeros((chunk, np_), dtype=torch.long, device=queries.device)
+        buf = self.pool.get("probe_mine", (chunk, np_), torch.long, queries.device)  # rows past hi - lo: padding
         if local is not None:
             buf[: hi - lo] = local
-        out = torch.empty((world * chunk, np_), dtype=torch.long, device=queries.device)
+        out = self.pool.get("probe_all", (world * chunk, np_), torch.long, queries.device)
         dist.all_gather_into_tensor(out, buf, group=self.group)
-        return out[:Q]
+        return out[:Q].clone()  # the caller may keep it; the pooled buffer is reused by the next probe
 
     def search(self, queries: torch.Tensor, k: int) -> Tuple[torch.Tensor, torch.Tensor]:
         if not dist.is_initialized() or dist.get_world_size(self.group) == 1:
@@ -416,9 +454,9 @@ class ShardedIVFSearch(_ShardSizes):
                                         (queries.shape[0], queries.device))
         self.clock.mark("scan")
         if self.results == "owner":
-            vals, ids = exchange_owned(local_d, local_i, self.group)
+            vals, ids = exchange_owned(local_d, local_i, self.group, self.pool)
         else:
-            vals, ids = gather_candidates(local_d, local_i, self.group)
+            vals, ids = gather_candidates(local_d, local_i, self.group, self.pool)
         self.clock.mark("result_exchange")
         res = self.merge(vals, ids, k, self.largest)
         self.clock.mark("merge")
