@@ -6,8 +6,10 @@ Headline workload (default ``flat_cosine_bf16``): exact cosine search over
 then rounded), queries of the same distribution, k = 100.  With N GPUs
 (torchrun, one process per GPU) the rows are split across the ranks and the
 query batch is 1,024 x N (per-GPU work fixed: "scaling": "weak"); a step is
-local fused search -> one NCCL all-to-all of the packed [Q, k] lists by query
-slice -> merge kernel on the rank owning the slice.
+sample maxima -> threshold exchange -> local fused search -> exchange of the
+packed [Q, k] lists by query slice -> merge kernel on the rank owning the
+slice, each exchange one kernel reading the other ranks' memory over NVLink
+(``--transport collective``: NCCL all-to-all / all-gather instead).
 
 * ``value``   queries/s with queries resident in HBM, CUDA events between
               barriers, max over ranks.  The stored rows (1.5 GB) exceed L2
@@ -107,6 +109,9 @@ def parse():
     ap.add_argument("--results", default="owner", choices=["owner", "replicated"],
                     help="flat search on N > 1 GPUs: each rank returns the answers of its query slice "
                          "(owner) or of the whole batch (replicated)")
+    ap.add_argument("--transport", default="auto", choices=["auto", "peer", "collective"],
+                    help="flat search on N > 1 GPUs: exchanges through the peer exchange kernel over NVLink "
+                         "(peer; auto picks it on one node) or NCCL collectives")
     return ap.parse_args()
 
 
@@ -296,8 +301,12 @@ def timed(ctx, fn, steps, warmup, tag_mask, tags=None):
     timed region), clocks, out (fn's last result)."""
     import torch
 
+    # the warm-up keeps each result alive until the next call returns, as the
+    # timed loop does, so the caching allocator already holds both result
+    # blocks (otherwise the second timed step makes a device allocation)
+    out = None
     for _ in range(warmup):
-        fn()
+        out = fn()
     torch.cuda.synchronize()
     ctx.barrier()
     lib = kernel_lib()
@@ -320,7 +329,6 @@ def timed(ctx, fn, steps, warmup, tag_mask, tags=None):
     allocs0 = torch.cuda.memory_stats().get("num_device_alloc", 0)
     host_steps = []
     e0.record()
-    out = None
     for _ in range(steps):
         h0 = time.perf_counter()
         out = fn()
@@ -415,7 +423,8 @@ def run_flat(args, wl, ctx):
     cfg = IndexConfig(dim=d, metric=Metric(wl["metric"]), precision=Precision(wl["precision"]))
     db = RapidaDB(config=cfg)
     db.add(x, torch.arange(lo, hi, device=dev, dtype=torch.long))
-    searcher = ShardedSearch(db, wl["metric"] != "l2", results=args.results if world > 1 else "replicated")
+    searcher = ShardedSearch(db, wl["metric"] != "l2", results=args.results if world > 1 else "replicated",
+                             transport=args.transport)
     own_lo, own_hi = searcher.owned_range(Q)
 
     # ---- device-resident timing: the main-scan launches carry CUDA events
@@ -541,9 +550,12 @@ def run_flat(args, wl, ctx):
             "config": flat_config(args, wl, world),
             "parallelism": f"row-shard x{world}" if world > 1 else "single GPU",
             "rows_per_gpu": n_local,
-            "results_mode": ("owner: rank r merges and returns the answers of its 1/%d slice of the query batch "
-                             "(one all-to-all of packed per-rank lists)" % world if args.results == "owner"
-                             else "replicated: every rank merges the whole batch (one all-gather)")
+            "results_mode": ("owner: rank r merges and returns the answers of its 1/%d slice of the query batch"
+                             % world if args.results == "owner" else "replicated: every rank merges the whole batch")
+            if world > 1 else None,
+            "transport": (("peer: one exchange kernel per exchange (sample maxima, thresholds, lists) reading "
+                           "the other ranks' arenas over NVLink (CUDA IPC, plain peer loads)")
+                          if searcher.peer is not None else "collective: NCCL all-to-all / all-gather")
             if world > 1 else None,
             "l2_flush": "not needed: stored rows (%.2f GB per GPU) exceed L2 (126 MB)" % (
                 n_local * d * (2 if half else 4) / 1e9),
@@ -567,6 +579,15 @@ def run_flat(args, wl, ctx):
                                                 args.cpu_seconds)
     if args.timeline > 0 and world == 1:
         kernel_timeline(lambda: searcher.search(q, k), args.timeline)
+    searcher.close()  # collective: every rank frees its exchange arena
+    from rapidadb_b200._lib import C
+
+    status = C().device_status(True)  # bounded device waits that ran out, any rank
+    status = int(ctx.max(float(status)))
+    if rank == 0:
+        res["device_status"] = status
+    if status:
+        raise RuntimeError(f"a bounded device wait ran out during the flat workload (status {status:#x})")
     del x, q, db
     return res
 

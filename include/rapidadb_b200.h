@@ -57,7 +57,7 @@ int rdb_version(void);
 /* Reads (and with clear != 0 resets) the current device's status word, where
  * kernels record bounded waits that ran out (tensor-core scan: bit 0 producer,
  * 1 MMA issuer, 2 epilogue; bit 4 the TMA-fed CUDA-core scan; bit 5
- * rdb_probe_bounded_wait).  Synchronises the device. */
+ * rdb_probe_bounded_wait; bit 6 rdb_peer_gather).  Synchronises the device. */
 int rdb_device_status(unsigned* out_host, int clear);
 /* The status word as last forwarded by a completed rdb_flat_search on the
  * current device, read from mapped host memory without synchronising (0: no
@@ -201,6 +201,50 @@ int rdb_topk_merge_strided(int largest, const float* in_v, int64_t gstride_v, co
 int rdb_topk_merge_ld(int largest, const float* in_v, int64_t gstride_v, int64_t ldv, const int64_t* in_i,
                       int64_t gstride_i, int64_t ldi, int G, int64_t nq, int kin, int k, float* out_v, int64_t* out_i,
                       void* stream);
+
+/* ---- peer exchange over NVLink (no reference counterpart: the reference is
+ * single-GPU, README.md:14) --------------------------------------------- */
+
+#define RDB_PEER_MAX_RANKS 8
+#define RDB_PEER_SLOTS 8
+#define RDB_PEER_FLAG_BYTES 512 /* the flags at the start of every arena */
+#define RDB_PEER_HANDLE_BYTES 64
+
+/* One exchange arena per rank: `bytes` of device memory on the current
+ * device, zeroed, and its 64-byte CUDA IPC handle for the other processes of
+ * the node.  Bytes [0, RDB_PEER_FLAG_BYTES) hold the exchange flags (64 bytes
+ * per slot, word p written by rank p); the data sections follow. */
+int rdb_peer_arena_alloc(size_t bytes, void** ptr, unsigned char* handle);
+int rdb_peer_arena_free(void* ptr);
+/* Maps another process's arena into this one (peer access enabled). */
+int rdb_peer_arena_open(const unsigned char* handle, void** ptr);
+int rdb_peer_arena_close(void* ptr);
+
+/* One exchange step.  Rank p's source rows are rows row0[p] ..
+ * row0[p] + nrows[p] - 1 of the array at byte src_off of rank p's arena
+ * (rows src_row_stride bytes apart, row_bytes bytes each); they land at
+ * dst + dst_off[p] + i * dst_row_stride in this rank's memory. */
+typedef struct RdbPeerGather {
+    int world, rank;          /* ranks of the exchange (<= RDB_PEER_MAX_RANKS), this rank */
+    int slot, pad;            /* flag slot, < RDB_PEER_SLOTS */
+    unsigned long long epoch; /* above every earlier epoch of the slot; the same on every rank */
+    void* base[RDB_PEER_MAX_RANKS]; /* every rank's arena as mapped here (own included) */
+    long long arena_bytes;          /* size of every arena: every source row lies inside it */
+    long long src_off, src_row_stride, row_bytes;
+    long long row0[RDB_PEER_MAX_RANKS], nrows[RDB_PEER_MAX_RANKS];
+    void* dst;
+    long long dst_off[RDB_PEER_MAX_RANKS], dst_row_stride;
+} RdbPeerGather;
+
+/* Launches one kernel on `stream` that (1) signals slot `slot` at `epoch` in
+ * every rank's arena: this rank's source rows, written by earlier work on
+ * the stream, are ready; (2) waits until every rank has signalled the slot
+ * at `epoch` or later, for at most limit_ns (1 us .. 10 s); (3) copies the
+ * rows with peer loads.  A wait that runs out sets bit 6 (64) of the device
+ * status word (rdb_device_status, rdb_pending_status) and copies nothing.
+ * Multicast is not used.  All sizes, offsets and strides are multiples of 4
+ * bytes; 16-byte alignment throughout selects 16-byte copies. */
+int rdb_peer_gather(const RdbPeerGather* args, unsigned long long limit_ns, void* stream);
 
 /* ---- k-means --------------------------------------------------------- */
 

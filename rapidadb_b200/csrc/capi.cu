@@ -175,6 +175,16 @@ int rdb_timing_enable(int mask) {
     std::lock_guard<std::mutex> lock(rdb::g_timing.mu);
     rdb::g_timing.mask = mask;
     rdb::g_timing.used = 0;
+    // the event pairs are created here, before the launches that record them,
+    // so that no event creation (a driver call that can stall behind other
+    // driver work) falls between the timed launches; more are created on demand
+    constexpr size_t kReserve = 1024;
+    while (mask && rdb::g_timing.ev.size() < kReserve) {
+        cudaEvent_t a, b;
+        RDB_CUDA_TRY(cudaEventCreate(&a));
+        RDB_CUDA_TRY(cudaEventCreate(&b));
+        rdb::g_timing.ev.push_back({a, b, 0});
+    }
     return RDB_OK;
 }
 

@@ -83,6 +83,7 @@ enum DeviceStatus : unsigned {
     DEV_OVERFLOW = 1u << 3,
     DEV_TIMEOUT_SIMT = 1u << 4,  // TMA-fed CUDA-core scan
     DEV_TIMEOUT_PROBE = 1u << 5,  // rdb_probe_bounded_wait
+    DEV_TIMEOUT_PEER = 1u << 6,   // rdb_peer_gather: another rank did not signal in time
 };
 unsigned* device_status_word();  // per-device, zero-initialised
 // Per-device word in mapped pinned host memory (device address) that the

@@ -1,7 +1,11 @@
 // Python module rapidadb_b200._C: the names of the reference's rapidadb._C
 // (csrc/bindings/torch_extension.cpp:16-90) plus the IVF / PQ / k-means
 // additions.  Thin: argument conversion only; logic lives in host/*.cpp.
+#include <c10/cuda/CUDAGuard.h>
 #include <torch/extension.h>
+
+#include <algorithm>
+#include <vector>
 
 #include "host.h"
 #include "ivf.h"
@@ -73,7 +77,7 @@ PYBIND11_MODULE(_C, m) {
         .def("capacity", &FlatIndex::capacity)
         .def("vectors", &FlatIndex::vectors)
         .def("sample_maxima", &FlatIndex::sample_maxima, py::arg("queries"), py::arg("sample_rows"),
-             py::arg("group"))
+             py::arg("group"), py::arg("out") = py::none())
         .def("search_threshold", &FlatIndex::search_threshold, py::arg("queries"), py::arg("k"), py::arg("thr"),
              py::arg("expect"))
         .def("tensor_core", &FlatIndex::tensor_core)
@@ -144,7 +148,7 @@ PYBIND11_MODULE(_C, m) {
           py::arg("sums"), py::arg("counts"), py::arg("centroids"), py::call_guard<py::gil_scoped_release>());
     m.def("label_sort", &label_sort, "stable counting sort by label", py::arg("labels"), py::arg("k"), py::call_guard<py::gil_scoped_release>());
     m.def("select_threshold", &select_threshold, "k-th best score of each row", py::arg("scores"), py::arg("k"),
-          py::arg("largest"), py::call_guard<py::gil_scoped_release>());
+          py::arg("largest"), py::arg("out") = py::none(), py::call_guard<py::gil_scoped_release>());
     m.def("pq_row_terms", &pq_row_terms, "per-row constant of the IVF-PQ distance", py::arg("codes"),
           py::arg("labels"), py::arg("centroids"), py::arg("codebooks"), py::call_guard<py::gil_scoped_release>());
     m.def("pq_encode", &pq_encode, "residual PQ codes", py::arg("points"), py::arg("labels"),
@@ -238,6 +242,71 @@ PYBIND11_MODULE(_C, m) {
             return "IVFPQIndex(dim=" + std::to_string(s.dim()) + ", nlist=" + std::to_string(s.nlist()) +
                    ", m=" + std::to_string(s.pq_m()) + ", size=" + std::to_string(s.size()) + ")";
         });
+
+    // ---- peer exchange arenas (CUDA IPC) and the exchange kernel of the
+    // row-sharded search; pointers travel as integers
+    m.def("peer_arena_alloc", [](int device, int64_t nbytes) {
+        c10::cuda::CUDAGuard guard(static_cast<c10::DeviceIndex>(device));
+        void* p = nullptr;
+        unsigned char h[RDB_PEER_HANDLE_BYTES];
+        check_status(rdb_peer_arena_alloc(static_cast<size_t>(nbytes), &p, h), "peer arena");
+        return std::make_tuple(reinterpret_cast<uintptr_t>(p), py::bytes(reinterpret_cast<const char*>(h), sizeof h));
+    }, py::arg("device"), py::arg("nbytes"));
+    m.def("peer_arena_open", [](int device, const py::bytes& handle) {
+        c10::cuda::CUDAGuard guard(static_cast<c10::DeviceIndex>(device));
+        const std::string h = handle;
+        TORCH_CHECK(h.size() == RDB_PEER_HANDLE_BYTES, "a peer arena handle has ", RDB_PEER_HANDLE_BYTES, " bytes");
+        void* p = nullptr;
+        check_status(rdb_peer_arena_open(reinterpret_cast<const unsigned char*>(h.data()), &p), "peer arena open");
+        return reinterpret_cast<uintptr_t>(p);
+    }, py::arg("device"), py::arg("handle"));
+    m.def("peer_arena_close", [](int device, uintptr_t p) {
+        c10::cuda::CUDAGuard guard(static_cast<c10::DeviceIndex>(device));
+        check_status(rdb_peer_arena_close(reinterpret_cast<void*>(p)), "peer arena close");
+    }, py::arg("device"), py::arg("ptr"));
+    m.def("peer_arena_free", [](int device, uintptr_t p) {
+        c10::cuda::CUDAGuard guard(static_cast<c10::DeviceIndex>(device));
+        check_status(rdb_peer_arena_free(reinterpret_cast<void*>(p)), "peer arena free");
+    }, py::arg("device"), py::arg("ptr"));
+    m.def(
+        "peer_gather",
+        [](int rank, int slot, uint64_t epoch, const std::vector<uintptr_t>& base, int64_t arena_bytes, int64_t src_off,
+           int64_t src_row_stride, int64_t row_bytes, const std::vector<int64_t>& row0,
+           const std::vector<int64_t>& nrows, const at::Tensor& dst, const std::vector<int64_t>& dst_off,
+           int64_t dst_row_stride, uint64_t limit_ns) {
+            const size_t world = base.size();
+            TORCH_CHECK(world >= 1 && world <= RDB_PEER_MAX_RANKS && row0.size() == world && nrows.size() == world &&
+                            dst_off.size() == world,
+                        "peer_gather: one base, row0, nrows and dst_off per rank (at most ", RDB_PEER_MAX_RANKS, ")");
+            TORCH_CHECK(dst.is_cuda() && dst.is_contiguous(), "peer_gather: dst must be a contiguous CUDA tensor");
+            int64_t end = 0;
+            for (size_t p = 0; p < world; ++p)
+                if (nrows[p] > 0) end = std::max(end, dst_off[p] + (nrows[p] - 1) * dst_row_stride + row_bytes);
+            TORCH_CHECK(end <= static_cast<int64_t>(dst.numel() * dst.element_size()),
+                        "peer_gather: the rows do not fit in dst");
+            RdbPeerGather a{};
+            a.world = static_cast<int>(world);
+            a.rank = rank;
+            a.slot = slot;
+            a.epoch = epoch;
+            a.arena_bytes = arena_bytes;
+            a.src_off = src_off;
+            a.src_row_stride = src_row_stride;
+            a.row_bytes = row_bytes;
+            a.dst = dst.data_ptr();
+            a.dst_row_stride = dst_row_stride;
+            for (size_t p = 0; p < world; ++p) {
+                a.base[p] = reinterpret_cast<void*>(base[p]);
+                a.row0[p] = row0[p];
+                a.nrows[p] = nrows[p];
+                a.dst_off[p] = dst_off[p];
+            }
+            c10::cuda::CUDAGuard guard(dst.device());
+            check_status(rdb_peer_gather(&a, limit_ns, stream_ptr()), "peer gather");
+        },
+        py::arg("rank"), py::arg("slot"), py::arg("epoch"), py::arg("base"), py::arg("arena_bytes"), py::arg("src_off"),
+        py::arg("src_row_stride"), py::arg("row_bytes"), py::arg("row0"), py::arg("nrows"), py::arg("dst"),
+        py::arg("dst_off"), py::arg("dst_row_stride"), py::arg("limit_ns") = 2000000000ull);
 
     m.def("padded_ld", [](int dim, at::ScalarType t) { return padded_ld(dim, t); });
     m.def("prepare_rows", &prepare_rows, py::arg("src"), py::arg("dtype"), py::arg("ld"));

@@ -183,11 +183,22 @@ Result topk_merge(const at::Tensor& vals, const at::Tensor& ids, int64_t k, bool
     return {ov, oi};
 }
 
-at::Tensor select_threshold(const at::Tensor& scores, int64_t k, bool largest) {
+// `out` (optional): a contiguous fp32 [nq] CUDA tensor to write into
+static void check_out(const c10::optional<at::Tensor>& out, const at::Tensor& like, at::IntArrayRef shape,
+                      const char* what) {
+    if (!out.has_value()) return;
+    const at::Tensor& o = *out;
+    TORCH_CHECK(o.is_cuda() && o.device() == like.device() && o.scalar_type() == at::kFloat && o.is_contiguous() &&
+                    o.sizes() == shape,
+                what, ": out must be a contiguous float32 tensor of shape ", shape, " on ", like.device());
+}
+
+at::Tensor select_threshold(const at::Tensor& scores, int64_t k, bool largest, const c10::optional<at::Tensor>& out_opt) {
     TORCH_CHECK(scores.is_cuda() && scores.dim() == 2, "scores must be a [nq, G] CUDA tensor");
     c10::cuda::CUDAGuard guard(scores.device());
     at::Tensor sc = scores.to(at::kFloat).contiguous();
-    at::Tensor out = at::empty({sc.size(0)}, sc.options());
+    check_out(out_opt, sc, {sc.size(0)}, "select_threshold");
+    at::Tensor out = out_opt.has_value() ? *out_opt : at::empty({sc.size(0)}, sc.options());
     check_status(rdb_select_threshold(largest ? 1 : 0, sc.data_ptr<float>(), sc.size(0), sc.size(1),
                                       static_cast<int>(k), out.data_ptr<float>(), stream_ptr()),
                  "select threshold");
@@ -328,7 +339,8 @@ Result FlatIndex::search(const at::Tensor& queries, int64_t k) const {
                        ids_.narrow(0, 0, n_), 0);
 }
 
-at::Tensor FlatIndex::sample_maxima(const at::Tensor& queries, int64_t sample_rows, int64_t group) const {
+at::Tensor FlatIndex::sample_maxima(const at::Tensor& queries, int64_t sample_rows, int64_t group,
+                                    const c10::optional<at::Tensor>& out_opt) const {
     TORCH_CHECK(queries.is_cuda(), "queries must be on CUDA");
     TORCH_CHECK(queries.dim() == 2 && queries.size(1) == dim_,
                 "queries must be [batch, " + std::to_string(dim_) + "]");
@@ -337,7 +349,8 @@ at::Tensor FlatIndex::sample_maxima(const at::Tensor& queries, int64_t sample_ro
     c10::cuda::CUDAGuard guard(storage_.device());
     at::Tensor q = prepare_rows(queries.to(storage_.device()), storage_.scalar_type(), ld_);
     const int64_t nq = q.size(0);
-    at::Tensor out = at::empty({nq, sample_rows / group}, q.options().dtype(at::kFloat));
+    check_out(out_opt, q, {nq, sample_rows / group}, "sample_maxima");
+    at::Tensor out = out_opt.has_value() ? *out_opt : at::empty({nq, sample_rows / group}, q.options().dtype(at::kFloat));
     at::Tensor ws = at::empty({static_cast<int64_t>(rdb_flat_sample_workspace(nq))}, q.options().dtype(at::kByte));
     check_status(rdb_flat_sample_maxima(static_cast<int>(metric_), dtype_code(storage_.scalar_type()), q.data_ptr(),
                                         nq, ld_, storage_.data_ptr(), n_, ld_, xv_.data_ptr<float>(), dim_,

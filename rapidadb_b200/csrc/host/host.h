@@ -39,7 +39,8 @@ Result topk(const at::Tensor& distances, int64_t k, bool largest);
 // merge of per-shard [G, Q, kin] lists into [Q, k]
 Result topk_merge(const at::Tensor& vals, const at::Tensor& ids, int64_t k, bool largest);
 // k-th best of each row of scores [nq, G] (L2 smallest, else largest)
-at::Tensor select_threshold(const at::Tensor& scores, int64_t k, bool largest);
+at::Tensor select_threshold(const at::Tensor& scores, int64_t k, bool largest,
+                            const c10::optional<at::Tensor>& out = c10::nullopt);
 
 // -------------------------------------------------------------- FlatIndex --
 // csrc/include/rapidadb/index/flat_index.h:12-53, csrc/index/flat_index.cpp
@@ -62,7 +63,8 @@ class FlatIndex {
     // rdb_flat_search_thr): group maxima [nq, sample_rows / group] of a
     // strided sample of the stored rows, and a search keeping only rows that
     // reach thr [nq] (expect: candidates per query expected over the rows).
-    at::Tensor sample_maxima(const at::Tensor& queries, int64_t sample_rows, int64_t group) const;
+    at::Tensor sample_maxima(const at::Tensor& queries, int64_t sample_rows, int64_t group,
+                             const c10::optional<at::Tensor>& out = c10::nullopt) const;
     Result search_threshold(const at::Tensor& queries, int64_t k, const at::Tensor& thr, int64_t expect) const;
     bool tensor_core() const { return precision_ == Precision::FP16 || precision_ == Precision::BF16; }
     // INT8 storage (SQ8, rdb_sq8_encode): codes [size, dim] int8, scales [size];

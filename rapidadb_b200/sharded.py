@@ -3,10 +3,11 @@
 The reference is single-GPU (its README.md:14 only claims multi-GPU).  Here
 the database is split by rows across the ranks of a process group: every rank
 holds a contiguous slice with global ids, answers the same query batch with its
-local fused search, the per-rank [Q, k] candidate lists are exchanged with ONE
-all-gather (NCCL over NVLink on GPUs, gloo on CPU in tests), and a final merge
-kernel keeps the best k per query.  k-means centroid sums are reduced with an
-all-reduce (see rapidadb_b200.kmeans).
+local fused search, the per-rank [Q, k] candidate lists are exchanged (GPU
+ranks of one node: one exchange kernel reading the other ranks' memory over
+NVLink, PeerExchange; otherwise one all-gather or all-to-all, NCCL or gloo),
+and a final merge kernel keeps the best k per query.  k-means centroid sums
+are reduced with an all-reduce (see rapidadb_b200.kmeans).
 
 ``local_search`` and ``merge`` are injectable so the exchange logic can be
 exercised on CPU ranks with the oracle standing in for the GPU parts.
@@ -113,6 +114,144 @@ def exchange_owned(local_d: torch.Tensor, local_i: torch.Tensor,
             else torch.empty((world, n_r, W), dtype=torch.int32, device=dev))
     dist.all_to_all_single(recv.view(-1), send.view(-1), [sizes[rank]] * world, sizes, group=group)
     return unpack_lists(recv, k)
+
+
+class PeerUnavailable(RuntimeError):
+    """The ranks cannot map each other's memory (not one node, no peer access)."""
+
+
+class _DeviceSpan:
+    """Raw device memory handed to torch.as_tensor (zero copy)."""
+
+    def __init__(self, ptr: int, nbytes: int):
+        self.__cuda_array_interface__ = {"shape": (nbytes,), "typestr": "|u1", "data": (ptr, False),
+                                         "version": 3, "strides": None}
+
+
+class PeerExchange:
+    """NVLink transport of ShardedSearch for ranks on one node: every rank
+    owns one exchange arena (device memory shared with the other processes as
+    a CUDA IPC handle and mapped into each of them), and every exchange is ONE
+    kernel (rdb_peer_gather) that signals this rank's rows ready, waits for
+    the other ranks (bounded: a wait that runs out sets a device status bit
+    and copies nothing) and reads the rows it needs straight out of their
+    arenas with peer loads.  No collective library runs on the data path.
+
+    Every search is one epoch; the flags hold epochs, so nothing is reset
+    between searches.  Setup, growth and close() are collective (every rank
+    calls them in the same order); if any rank cannot map the others'
+    arenas, every rank raises PeerUnavailable."""
+
+    FLAG_BYTES = 512  # RDB_PEER_FLAG_BYTES
+    MAX_RANKS = 8     # RDB_PEER_MAX_RANKS
+    SLOT_MAXIMA, SLOT_THRESHOLD, SLOT_LISTS = 0, 1, 2
+
+    def __init__(self, group: Optional[dist.ProcessGroup], device, limit_ns: int = 2_000_000_000):
+        self.group = group
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        self.device = torch.device(device)
+        if self.device.index is None:
+            self.device = torch.device("cuda", torch.cuda.current_device())
+        if self.world > self.MAX_RANKS:
+            raise PeerUnavailable(f"at most {self.MAX_RANKS} ranks")
+        self.limit_ns = int(limit_ns)
+        self.nbytes = 0
+        self.ptr = None
+        self.bases = []
+        self.buf = None
+        self.epoch = 0
+        self._off = {}
+
+    def _all_ok(self, ok: bool) -> bool:
+        t = torch.tensor([1 if ok else 0], dtype=torch.int32, device=self.device)
+        dist.all_reduce(t, op=dist.ReduceOp.MIN, group=self.group)
+        return bool(t.item())
+
+    def reserve(self, sections: dict) -> None:
+        """Lays out the named sections ({name: bytes}, the same on every rank)
+        after the flags, 256-byte aligned; a layout that does not fit the
+        arena grows it first (collective)."""
+        off, layout = self.FLAG_BYTES, {}
+        for name, n in sections.items():
+            layout[name] = off
+            off += (int(n) + 255) // 256 * 256
+        if off > self.nbytes:
+            self._map(max(off, 2 * self.nbytes))
+        self._off = layout
+
+    def _map(self, nbytes: int) -> None:
+        from rapidadb_b200._lib import C
+
+        dev = self.device.index
+        if self.ptr is not None:
+            self._release()
+        ok, ptr, handle = True, None, bytes(64)
+        try:
+            ptr, handle = C().peer_arena_alloc(dev, nbytes)
+        except RuntimeError:
+            ok = False
+        h = torch.tensor(list(handle), dtype=torch.uint8, device=self.device)
+        allh = torch.empty((self.world, 64), dtype=torch.uint8, device=self.device)
+        dist.all_gather_into_tensor(allh, h, group=self.group)
+        allh = allh.cpu()
+        bases = []
+        if ok:
+            try:
+                for p in range(self.world):
+                    bases.append(ptr if p == self.rank else C().peer_arena_open(dev, bytes(allh[p].tolist())))
+            except RuntimeError:
+                ok = False
+        if not self._all_ok(ok):
+            for p, b in enumerate(bases):
+                if p != self.rank:
+                    C().peer_arena_close(dev, b)
+            if ptr is not None:
+                C().peer_arena_free(dev, ptr)
+            raise PeerUnavailable("the ranks cannot map each other's exchange arenas")
+        self.ptr, self.bases, self.nbytes = ptr, bases, nbytes
+        self.buf = torch.as_tensor(_DeviceSpan(ptr, nbytes), device=self.device)
+
+    def _release(self) -> None:
+        from rapidadb_b200._lib import C
+
+        dev = self.device.index
+        # no rank may still read an arena: finish local work, then agree
+        torch.cuda.synchronize(self.device)
+        self._all_ok(True)
+        for p, b in enumerate(self.bases):
+            if p != self.rank:
+                C().peer_arena_close(dev, b)
+        torch.cuda.synchronize(self.device)
+        self._all_ok(True)
+        C().peer_arena_free(dev, self.ptr)
+        self.ptr, self.bases, self.buf, self.nbytes, self._off = None, [], None, 0, {}
+
+    def close(self) -> None:
+        """Unmaps and frees the arenas (collective)."""
+        if self.ptr is not None:
+            self._release()
+
+    def next_epoch(self) -> int:
+        self.epoch += 1
+        return self.epoch
+
+    def view(self, section: str, shape, dtype) -> torch.Tensor:
+        """This rank's section as a tensor of `shape` (contiguous)."""
+        n = math.prod(shape) * dtype.itemsize
+        off = self._off[section]
+        return self.buf[off: off + n].view(dtype).view(tuple(shape))
+
+    def gather(self, slot: int, section: str, epoch: int, *, row0, nrows, row_bytes: int, src_row_stride: int,
+               dst: torch.Tensor, dst_off, dst_row_stride: int) -> None:
+        """Rows row0[p] .. row0[p] + nrows[p] - 1 of `section` of every rank
+        p's arena -> dst (bytes dst_off[p] + i * dst_row_stride), one kernel
+        on the current stream after this rank's own section is written."""
+        from rapidadb_b200._lib import C
+
+        C().peer_gather(self.rank, slot, epoch, self.bases, self.nbytes, self._off[section], src_row_stride, row_bytes,
+                        [int(v) for v in row0], [int(v) for v in nrows], dst, [int(v) for v in dst_off],
+                        dst_row_stride, self.limit_ns)
 
 
 class PhaseClock:
@@ -285,13 +424,25 @@ class ShardedSearch(_ShardSizes):
                       than k rows (or none) contributes a padded list, and k
                       above the rows of all shards raises ValueError on every
                       rank before any data collective.
+        transport:    "auto" -- the peer transport (PeerExchange: one
+                      exchange kernel over NVLink per exchange, no
+                      collective library on the data path) when the ranks
+                      are CUDA ranks of one node under the NCCL backend,
+                      else collectives; "collective" -- torch.distributed
+                      collectives (NCCL / gloo); "peer" -- the peer
+                      transport or an error.
     """
 
     def __init__(self, index, largest: bool, group: Optional[dist.ProcessGroup] = None,
                  merge: Optional[Callable] = None, shared_threshold: bool = True, results: str = "replicated",
-                 local_size=None):
+                 local_size=None, transport: str = "auto"):
         if results not in ("replicated", "owner"):
             raise ValueError(f"results must be 'replicated' or 'owner', got {results!r}")
+        if transport not in ("auto", "collective", "peer"):
+            raise ValueError(f"transport must be 'auto', 'collective' or 'peer', got {transport!r}")
+        self.transport = transport
+        self.peer: Optional[PeerExchange] = None
+        self._peer_off = transport == "collective"
         self._size_source = index
         self._init_sizes(local_size)
         self.clock = PhaseClock()
@@ -313,30 +464,72 @@ class ShardedSearch(_ShardSizes):
             return 0, Q
         return shard_range(Q, dist.get_rank(self.group), dist.get_world_size(self.group))
 
-    def _shared_threshold_search(self, queries: torch.Tensor, k: int, sizes):
+    def _peer_exchange(self, device) -> Optional[PeerExchange]:
+        """The peer transport (set up on the first search, collectively), or
+        None for collectives."""
+        if self._peer_off:
+            return None
+        if self.peer is None:
+            usable = (device.type == "cuda" and "nccl" in str(dist.get_backend(self.group))
+                      and dist.get_world_size(self.group) <= PeerExchange.MAX_RANKS)
+            try:
+                if not usable:
+                    raise PeerUnavailable("the peer transport needs CUDA ranks under the NCCL backend, "
+                                          f"at most {PeerExchange.MAX_RANKS}")
+                ex = PeerExchange(self.group, device)
+                ex.reserve({})
+                self.peer = ex
+            except PeerUnavailable:
+                if self.transport == "peer":
+                    raise
+                self._peer_off = True
+                return None
+        return self.peer
+
+    def close(self) -> None:
+        """Frees the peer transport's arenas (collective: every rank calls it)."""
+        if self.peer is not None:
+            self.peer.close()
+            self.peer = None
+
+    def _shared_threshold_search(self, queries: torch.Tensor, k: int, sizes, plan, ex=None, epoch=0):
         """Shared-threshold protocol: every rank computes group maxima of a
         strided sample of its rows (1 / world of the single-GPU sample); the
         k-th best of all ranks' maxima of a query -- a lower bound on its
         global k-th best score -- filters every shard.  results="replicated"
-        all-gathers the maxima and every rank selects every query's threshold;
-        results="owner" sends each rank the maxima of its query slice
-        (all-to-all), selects those thresholds there and all-gathers them.
-        The shard sizes are gathered on the first search.  None (before any
-        data collective) when the shards are too small."""
+        brings every rank every rank's maxima and every rank selects every
+        query's threshold; results="owner" brings each rank the maxima of its
+        query slice, selects those thresholds there and shares them.  With
+        the peer transport (ex) the maxima and thresholds move through the
+        exchange arenas (one exchange kernel each), else through an
+        all-to-all / all-gather."""
         world = dist.get_world_size(self.group)
+        rank = dist.get_rank(self.group)
         dev = queries.device
-        if sizes is None or min(sizes) < k:
-            return None
-        plan = shared_sample_plan(sizes, k)
-        if plan is None:
-            return None
         per, g, total = plan
-        maxima = self.flat.sample_maxima(queries, per, g)  # [Q, per / g]
+        Q, gl = queries.shape[0], per // g
+        # [Q, gl] group maxima, written straight into the exchange arena
+        maxima = self.flat.sample_maxima(queries, per, g, **(
+            {"out": ex.view("maxima", (Q, gl), torch.float32)} if ex is not None else {}))
         self.clock.mark("sample")
-        Q, gl = maxima.shape
         from rapidadb_b200._lib import C
 
-        if self.results == "owner":
+        if ex is not None:
+            lo, hi = self.owned_range(Q)
+            mine = self.pool.get("peer_maxima", (hi - lo, world * gl), maxima.dtype, dev)
+            ex.gather(PeerExchange.SLOT_MAXIMA, "maxima", epoch, row0=[lo] * world, nrows=[hi - lo] * world,
+                      row_bytes=4 * gl, src_row_stride=4 * gl, dst=mine,
+                      dst_off=[4 * gl * p for p in range(world)], dst_row_stride=4 * gl * world)
+            thr = ex.view("thr", (Q,), maxima.dtype)
+            if hi > lo:
+                C().select_threshold(mine, k, self.largest, out=thr[lo:hi])
+            if self.results == "owner":
+                # every rank's slice of thresholds into this rank's array (its own already in place)
+                sl = [shard_range(Q, p, world) for p in range(world)]
+                ex.gather(PeerExchange.SLOT_THRESHOLD, "thr", epoch, row0=[a for a, _ in sl],
+                          nrows=[0 if p == rank else b - a for p, (a, b) in enumerate(sl)], row_bytes=4,
+                          src_row_stride=4, dst=thr, dst_off=[4 * a for a, _ in sl], dst_row_stride=4)
+        elif self.results == "owner":
             # each rank selects the thresholds of its query slice from every
             # rank's maxima, then the thresholds are all-gathered
             lo, hi = self.owned_range(Q)
@@ -366,24 +559,55 @@ class ShardedSearch(_ShardSizes):
         expect = int(math.ceil(1.1 * self.flat.size() * k / total)) + 1
         return self.flat.search_threshold(queries, k, thr, expect)
 
+    def _exchange_lists(self, local_d, local_i, ex=None, epoch=0):
+        """This rank's [Q, k] lists -> [G, Q_r, k] score and id views of the
+        lists it merges (its query slice under results="owner", else all
+        queries)."""
+        if ex is None:
+            if self.results == "owner":
+                return exchange_owned(local_d, local_i, self.group, self.pool)
+            return gather_candidates(local_d, local_i, self.group, self.pool)
+        world = dist.get_world_size(self.group)
+        Q, k = local_d.shape
+        W = _packed_width(k)
+        # two list sections by epoch parity: with no threshold exchange
+        # between two searches, a rank may pack the next lists while another
+        # still reads these
+        name = "lists%d" % (epoch & 1)
+        pack_lists(local_d, local_i, ex.view(name, (Q, W), torch.int32))
+        lo, hi = self.owned_range(Q)
+        recv = self.pool.get("peer_lists", (world, hi - lo, W), torch.int32, local_d.device)
+        ex.gather(PeerExchange.SLOT_LISTS, name, epoch, row0=[lo] * world, nrows=[hi - lo] * world,
+                  row_bytes=4 * W, src_row_stride=4 * W, dst=recv,
+                  dst_off=[4 * W * (hi - lo) * p for p in range(world)], dst_row_stride=4 * W)
+        return unpack_lists(recv, k)
+
     def search(self, queries: torch.Tensor, k: int) -> Tuple[torch.Tensor, torch.Tensor]:
         if not dist.is_initialized() or dist.get_world_size(self.group) == 1:
             return self.search_fn(queries, k)
         sizes = self.shard_sizes(queries.device)
         self._check_k(sizes, k)
+        Q = queries.shape[0]
+        plan = None
+        if self.flat is not None and sizes is not None and min(sizes) >= k:
+            plan = shared_sample_plan(sizes, k)
+        ex = self._peer_exchange(queries.device)
+        epoch = 0
+        if ex is not None:
+            gl = plan[0] // plan[1] if plan is not None else 0
+            W4 = 4 * Q * _packed_width(k)
+            ex.reserve({"maxima": 4 * Q * gl, "thr": 4 * Q, "lists0": W4, "lists1": W4})
+            epoch = ex.next_epoch()
         self.clock.start(queries)
         out = None
-        if self.flat is not None:
-            out = self._shared_threshold_search(queries, k, sizes)
+        if plan is not None:
+            out = self._shared_threshold_search(queries, k, sizes, plan, ex, epoch)
         if out is None:
             out = self._padded(lambda kk: self.search_fn(queries, kk), sizes, k,
                                (queries.shape[0], queries.device))
         local_d, local_i = out
         self.clock.mark("scan")
-        if self.results == "owner":
-            vals, ids = exchange_owned(local_d, local_i, self.group, self.pool)
-        else:
-            vals, ids = gather_candidates(local_d, local_i, self.group, self.pool)
+        vals, ids = self._exchange_lists(local_d, local_i, ex, epoch)
         self.clock.mark("result_exchange")
         res = self.merge(vals, ids, k, self.largest)
         self.clock.mark("merge")

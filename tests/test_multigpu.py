@@ -64,6 +64,18 @@ def _worker(rank, port, out_q):
         so = ShardedSearch(flat, largest=True, results="owner")
         d, i = so.search(qt, 20)
         res["flat_owner"] = (so.owned_range(len(q)), d.cpu().numpy(), i.cpu().numpy())
+        # both transports explicitly: the peer exchange kernel (three searches:
+        # the epochs advance, the list sections alternate) and NCCL collectives
+        for mode in ("owner", "replicated"):
+            for transport in ("peer", "collective"):
+                for thr in (True, False):
+                    s = ShardedSearch(flat, largest=True, results=mode, transport=transport, shared_threshold=thr)
+                    for _ in range(3):
+                        d, i = s.search(qt, 20)
+                    res[f"flat_{mode}_{transport}_{thr}"] = (s.owned_range(len(q)), d.cpu().numpy(), i.cpu().numpy())
+                    assert (s.peer is not None) == (transport == "peer")
+                    s.close()
+        assert _C.device_status(True) == 0
         # k-means over the shards (sums / counts all-reduced)
         km = kmeans(xt, 32, max_iters=5, tol=0.0, seed=3, group=dist.group.WORLD, exact_assign=True)
         res["kmeans"] = (km.centroids.cpu().numpy(), km.inertia)
@@ -127,6 +139,10 @@ def test_sharded_equals_single_gpu():
         assert (a, b) == shard_range(len(q), r, WORLD)
         assert_topk_match(d[a:b].cpu().numpy(), i[a:b].cpu().numpy(), do, io, rtol=1e-4, atol=1e-5)
         covered += b - a
+        for key, ((a, b), do, io) in ((kk, v) for kk, v in out[r].items() if kk.startswith("flat_") and
+                                      kk != "flat_owner"):
+            assert (a, b) == (shard_range(len(q), r, WORLD) if "_owner_" in key else (0, len(q))), key
+            assert_topk_match(d[a:b].cpu().numpy(), i[a:b].cpu().numpy(), do, io, rtol=1e-4, atol=1e-5)
     assert covered == len(q)
     for r in range(WORLD):
         np.testing.assert_allclose(out[r]["kmeans"][0], km.centroids.cpu().numpy(), rtol=1e-5, atol=1e-5)

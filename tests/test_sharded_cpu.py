@@ -280,6 +280,42 @@ def test_results_mode_is_checked():
         ShardedSearch(lambda q, k: (q, q), largest=False, results="everyone")
     with pytest.raises(ValueError, match="results"):
         ShardedIVFSearch(object(), largest=False, results="")
+    with pytest.raises(ValueError, match="transport"):
+        ShardedSearch(lambda q, k: (q, q), largest=False, transport="nvlink")
+
+
+def _transport_on_gloo(rank, world):
+    """CPU ranks have no peer transport: "auto" falls back to collectives,
+    "peer" raises on every rank before any data moves."""
+    from rapidadb_b200.sharded import PeerUnavailable
+
+    x, q = _data()
+    lo, hi = shard_range(len(x), rank, world)
+
+    def local(qt, k):
+        d, i = oracle.flat_search("l2", qt.numpy(), x[lo:hi], k, ids=np.arange(lo, hi, dtype=np.int64))
+        return torch.from_numpy(d), torch.from_numpy(i)
+
+    s = ShardedSearch(local, largest=False, merge=_oracle_merge, results="owner")
+    d, i = s.search(torch.from_numpy(q), 10)
+    out = {"auto": (s.owned_range(len(q)), d.numpy(), i.numpy(), s.peer is None)}
+    try:
+        ShardedSearch(local, largest=False, merge=_oracle_merge, transport="peer").search(torch.from_numpy(q), 10)
+        out["peer"] = None
+    except PeerUnavailable as e:
+        out["peer"] = str(e)
+    return out
+
+
+def test_peer_transport_needs_gpu_ranks():
+    out = _run(_transport_on_gloo, world=2)
+    x, q = _data()
+    rd, ri = oracle.flat_search("l2", q, x, 10)
+    for r in range(2):
+        (a, b), d, i, no_peer = out[r]["auto"]
+        assert no_peer
+        np.testing.assert_array_equal(i, ri[a:b])
+        assert "NCCL" in out[r]["peer"]
 
 
 def test_shard_range_partitions():
