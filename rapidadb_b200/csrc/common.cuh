@@ -197,6 +197,32 @@ __host__ __device__ inline float key_score(uint32_t k, bool largest) {
     return asc_key_float(largest ? ~k : k);
 }
 
+// ------------------------------------------------- paired fp32 (sm_100) --
+//
+// Two fp32 lanes in one 64-bit register: one fma.rn.f32x2 / mul.rn.f32x2
+// instruction does two independent, individually rounded operations, so the
+// results equal two scalar fmaf / multiplications.
+
+__device__ __forceinline__ uint64_t pack2(float a, float b) {
+    uint64_t r;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
+    return r;
+}
+__device__ __forceinline__ void unpack2(uint64_t v, float& a, float& b) {
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(v));
+}
+__device__ __forceinline__ uint64_t mul_f32x2(uint64_t a, uint64_t b) {
+    uint64_t d;
+    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+__device__ __forceinline__ uint64_t fma_f32x2(uint64_t a, uint64_t b, uint64_t c) {
+    uint64_t d;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+    return d;
+}
+
+
 // --------------------------------------------------------- spin waits --
 
 __device__ __forceinline__ uint64_t globaltimer_ns() {

@@ -261,25 +261,6 @@ __device__ __forceinline__ void insert_sorted(float (&tv)[GK], float v) {
 
 // Paired fp32 arithmetic (sm_100): two IEEE round-to-nearest operations per
 // instruction, each identical to its scalar form.
-__device__ __forceinline__ uint64_t pack2(float a, float b) {
-    uint64_t r;
-    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
-    return r;
-}
-__device__ __forceinline__ void unpack2(uint64_t v, float& a, float& b) {
-    asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(v));
-}
-__device__ __forceinline__ uint64_t mul_f32x2(uint64_t a, uint64_t b) {
-    uint64_t d;
-    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
-    return d;
-}
-__device__ __forceinline__ uint64_t fma_f32x2(uint64_t a, uint64_t b, uint64_t c) {
-    uint64_t d;
-    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
-    return d;
-}
-
 // A unit of work as the producer resolves it once for the other roles: list
 // rows [r0, r1), entries [ec, e1), row tiles.
 struct UnitRec {
