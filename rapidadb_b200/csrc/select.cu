@@ -175,7 +175,7 @@ __global__ void __launch_bounds__(NT) select_kernel(SelectArgs a) {
         const int T = S.total;
         const float qv = (a.input == SEL_CANDIDATES && a.qv) ? a.qv[q] : 0.f;
         const int want = min(out_k_req, T);  // elements to select
-        const bool cached = T <= kCacheKeys;
+        const bool cached = T <= a.cache_keys;
 
         // ---- pass 0: keys (cached) and min / max ---------------------------
         unsigned long long kmin = ~0ull, kmax = 0ull;
@@ -693,7 +693,15 @@ int launch_select(const SelectArgs& a, cudaStream_t stream) {
         RDB_CHECK_ARG(a.G >= 1 && a.G <= kMaxSeg, "G %d out of range", a.G);
     int P = 1;
     while (P < out_k) P <<= 1;
-    size_t smem = sizeof(unsigned long long) * ((size_t)P + kCacheKeys);
+    // the CTA kernel caches up to kCacheKeys keys per query in shared memory;
+    // with an expected count it holds that many plus an eighth and 256 (the
+    // count's spread is about its square root), so more CTAs fit on an SM;
+    // a query with more elements reads them again from global memory / L2
+    SelectArgs ac = a;
+    ac.cache_keys = kCacheKeys;
+    if (a.expect > 0)
+        ac.cache_keys = (int)std::min<int64_t>(kCacheKeys, (a.expect + a.expect / 8 + 256 + 63) / 64 * 64);
+    size_t smem = sizeof(unsigned long long) * ((size_t)P + ac.cache_keys);
     static bool attr_set[64] = {false};
     int dev = 0;
     cudaGetDevice(&dev);
@@ -729,7 +737,7 @@ int launch_select(const SelectArgs& a, cudaStream_t stream) {
     }
     int64_t grid = a.nq < 65535 * 4 ? a.nq : 65535 * 4;
     if (a.force_cta) grid = std::min<int64_t>(grid, num_sms());
-    select_kernel<<<(unsigned)grid, NT, smem, stream>>>(a);
+    select_kernel<<<(unsigned)grid, NT, smem, stream>>>(ac);
     RDB_LAUNCH_CHECK();
     return RDB_OK;
 }

@@ -60,6 +60,7 @@ struct SelectArgs {
     const unsigned* gate;    // nothing to do while *gate == 0 (NULL: always run)
     int force_cta;           // one CTA per query (select_kernel), grid of at most one CTA per SM
     int64_t expect;       // expected elements per query (0: unknown); picks the kernel
+    int cache_keys;       // set by launch_select: keys per query the CTA kernel holds in shared memory
 
     // exact L2 rescoring of the selected rows (SEL_CANDIDATES, metric L2)
     int rescore_margin;  // extra rows selected before rescoring (0 = off)
