@@ -120,7 +120,9 @@ __device__ __forceinline__ int next_pow2(int v) {
     return p;
 }
 
-__global__ void __launch_bounds__(NT) select_kernel(SelectArgs a) {
+// seven CTAs per SM (32 registers, a few bytes spilled): with the key cache
+// sized from the expected count, 148 x 7 = 1,036 queries run in one wave
+__global__ void __launch_bounds__(NT, 7) select_kernel(SelectArgs a) {
     extern __shared__ __align__(16) unsigned char dsm[];
     __shared__ SelShared S;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
