@@ -925,18 +925,31 @@ __global__ void probe_units_kernel(int64_t e0, int64_t e1, int nlist, int64_t* l
 constexpr int kProbeSlots = 256;  // collected centroids per query before the all-centroid rescan
 constexpr int kProbeTop = 128;    // nprobe + margin limit
 
-// Exact squared L2 of query qp and centroid cp with the flat search's
-// arithmetic: lane-strided fused multiply-add chains, then a butterfly sum
-// (every lane returns the total).
-__device__ __forceinline__ float flat_l2(const float* qp, const float* cp, int d, int lane) {
-    float acc = 0.f;
+// Exact squared L2 of query qp and U centroids cp[u] with the flat search's
+// arithmetic: per centroid, lane-strided fused multiply-add chains, then a
+// butterfly sum (every lane gets the total).  The U chains and butterflies
+// are interleaved so that their latencies overlap; each centroid's value is
+// the one a single chain would give.
+template <int U>
+__device__ __forceinline__ void flat_l2_multi(const float* qp, const float* const (&cp)[U], int d, int lane,
+                                              float (&out)[U]) {
+    float acc[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u) acc[u] = 0.f;
     for (int t = lane; t < d; t += 32) {
-        const float df = qp[t] - cp[t];
-        acc = fmaf(df, df, acc);
+        const float qv = qp[t];
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+            const float df = qv - cp[u][t];
+            acc[u] = fmaf(df, df, acc[u]);
+        }
     }
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
-    return acc;
+    for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+        for (int u = 0; u < U; ++u) acc[u] += __shfl_xor_sync(0xffffffffu, acc[u], o);
+#pragma unroll
+    for (int u = 0; u < U; ++u) out[u] = acc[u];
 }
 
 // One warp per query over its row of tensor-core values (|c|^2 - 2 q.c,
@@ -1010,14 +1023,32 @@ __global__ void __launch_bounds__(256) probe_select_kernel(const float* __restri
             gb = __ballot_sync(0xffffffffu, gi < nper && fkey(grow[gi]) <= tk);
         }
         while (gb) {
-            const int i = by_groups ? i0 + __ffs(gb) - 1 : i0;
-            gb &= gb - 1;
-            const int col = i * 32 + lane;
-            const bool take = col < nlist && fkey(row[col]) <= tk;
-            const unsigned b = __ballot_sync(0xffffffffu, take);
-            const int pos = cnt + __popc(b & ((1u << lane) - 1));
-            if (take && pos < kProbeSlots) s_idx[w][pos] = col;
-            cnt += __popc(b);
+            // up to four groups at a time: their loads in flight together
+            int gi4[4];
+            float v4[4];
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                gi4[u] = -1;
+                if (gb) {
+                    gi4[u] = i0 + __ffs(gb) - 1;
+                    gb &= gb - 1;
+                }
+            }
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                const int col = gi4[u] * 32 + lane;
+                v4[u] = (gi4[u] >= 0 && col < nlist) ? row[col] : INFINITY;
+            }
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                if (gi4[u] < 0) break;  // warp-uniform
+                const int col = gi4[u] * 32 + lane;
+                const bool take = col < nlist && fkey(v4[u]) <= tk;
+                const unsigned b = __ballot_sync(0xffffffffu, take);
+                const int pos = cnt + __popc(b & ((1u << lane) - 1));
+                if (take && pos < kProbeSlots) s_idx[w][pos] = col;
+                cnt += __popc(b);
+            }
         }
     }
     const bool all = cnt > kProbeSlots;
@@ -1028,12 +1059,25 @@ __global__ void __launch_bounds__(256) probe_select_kernel(const float* __restri
     for (int c0 = 0; c0 < total; c0 += kProbeSlots) {
         const int nc = min(kProbeSlots, total - c0);
         __syncwarp();
-        for (int c = 0; c < nc; ++c) {
-            const int l = all ? c0 + c : s_idx[w][c];
-            const float dist = flat_l2(qp, cent + static_cast<int64_t>(l) * ldc, d, lane);
+        for (int c = 0; c < nc; c += 4) {
+            // four centroids at a time (the last ones repeat centroid nc - 1, unused)
+            int l4[4];
+            const float* cp4[4];
+            float dist4[4];
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                const int cc = min(c + u, nc - 1);
+                l4[u] = all ? c0 + cc : s_idx[w][cc];
+                cp4[u] = cent + static_cast<int64_t>(l4[u]) * ldc;
+            }
+            flat_l2_multi<4>(qp, cp4, d, lane, dist4);
             if (lane == 0) {
-                s_val[w][c] = dist;
-                if (all) s_idx[w][c] = l;
+#pragma unroll
+                for (int u = 0; u < 4; ++u)
+                    if (c + u < nc) {
+                        s_val[w][c + u] = dist4[u];
+                        if (all) s_idx[w][c + u] = l4[u];
+                    }
             }
         }
         __syncwarp();
