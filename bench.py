@@ -110,8 +110,8 @@ def parse():
                     help="flat search on N > 1 GPUs: each rank returns the answers of its query slice "
                          "(owner) or of the whole batch (replicated)")
     ap.add_argument("--transport", default="auto", choices=["auto", "peer", "collective"],
-                    help="flat search on N > 1 GPUs: exchanges through the peer exchange kernel over NVLink "
-                         "(peer; auto picks it on one node) or NCCL collectives")
+                    help="sharded searches on N > 1 GPUs: exchanges through the peer exchange kernel over "
+                         "NVLink (peer; auto picks it on one node) or NCCL collectives")
     return ap.parse_args()
 
 
@@ -630,8 +630,10 @@ def ivf_rows(wl, world):
 def run_ivf(args, wl, ctx, name, steps, warmup):
     """IVF-Flat / IVF-PQ search QPS.  Rows are split over the ranks (every
     rank trains the same quantizer from the same seeded sample); the coarse
-    probe is split across ranks and the list table all-gathered; each rank
-    scans its rows of the probed lists; one all-to-all + merge."""
+    probe is split across ranks and the list table shared; each rank scans
+    its rows of the probed lists; the lists of each query slice go to its
+    owner, which merges them (exchanges: the peer exchange kernel, or NCCL
+    with --transport collective)."""
     import numpy as np
     import torch
     import torch.distributed as dist
@@ -668,7 +670,8 @@ def run_ivf(args, wl, ctx, name, steps, warmup):
     torch.cuda.synchronize()
     t_setup = time.perf_counter() - t_setup
     q = gen_mixture(0, Q, d, wl, args.seed, torch.float32, dev, salt=1)
-    searcher = ShardedIVFSearch(idx, largest=False, results="owner" if world > 1 else "replicated")
+    searcher = ShardedIVFSearch(idx, largest=False, results="owner" if world > 1 else "replicated",
+                                transport=args.transport)
     own_lo, own_hi = searcher.owned_range(Q)
     tag = 4 if pq else 2
     t = timed(ctx, lambda: searcher.search(q, k), steps, warmup, tag)
@@ -689,6 +692,7 @@ def run_ivf(args, wl, ctx, name, steps, warmup):
         rd, ri = searcher.search(qbuf, k)
         rd.cpu(), ri.cpu()
     e2e_s = ctx.max(time.perf_counter() - t0)
+    searcher.close()  # collective: every rank frees its exchange arena
 
     # recall@k against exact search over the same rows (the first 100 queries, owned by rank 0)
     nrec = min(100, own_hi - own_lo)

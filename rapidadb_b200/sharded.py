@@ -144,7 +144,7 @@ class PeerExchange:
 
     FLAG_BYTES = 512  # RDB_PEER_FLAG_BYTES
     MAX_RANKS = 8     # RDB_PEER_MAX_RANKS
-    SLOT_MAXIMA, SLOT_THRESHOLD, SLOT_LISTS = 0, 1, 2
+    SLOT_MAXIMA, SLOT_THRESHOLD, SLOT_LISTS, SLOT_PROBE = 0, 1, 2, 3
 
     def __init__(self, group: Optional[dist.ProcessGroup], device, limit_ns: int = 2_000_000_000):
         self.group = group
@@ -378,6 +378,69 @@ class _ShardSizes:
         return pad_results(d, i, k, self.largest)
 
 
+class _PeerTransport:
+    """Transport of the sharded searches' exchanges: the peer exchange
+    kernel over NVLink (PeerExchange) or torch.distributed collectives."""
+
+    def _init_transport(self, transport: str) -> None:
+        if transport not in ("auto", "collective", "peer"):
+            raise ValueError(f"transport must be 'auto', 'collective' or 'peer', got {transport!r}")
+        self.transport = transport
+        self.peer: Optional[PeerExchange] = None
+        self._peer_off = transport == "collective"
+
+    def _peer_exchange(self, device) -> Optional[PeerExchange]:
+        """The peer transport (set up on the first search, collectively), or
+        None for collectives."""
+        if self._peer_off:
+            return None
+        if self.peer is None:
+            usable = (device.type == "cuda" and "nccl" in str(dist.get_backend(self.group))
+                      and dist.get_world_size(self.group) <= PeerExchange.MAX_RANKS)
+            try:
+                if not usable:
+                    raise PeerUnavailable("the peer transport needs CUDA ranks under the NCCL backend, "
+                                          f"at most {PeerExchange.MAX_RANKS}")
+                ex = PeerExchange(self.group, device)
+                ex.reserve({})
+                self.peer = ex
+            except PeerUnavailable:
+                if self.transport == "peer":
+                    raise
+                self._peer_off = True
+                return None
+        return self.peer
+
+    def close(self) -> None:
+        """Frees the peer transport's arenas (collective: every rank calls it)."""
+        if self.peer is not None:
+            self.peer.close()
+            self.peer = None
+
+    def _exchange_lists(self, local_d, local_i, ex=None, epoch=0):
+        """This rank's [Q, k] lists -> [G, Q_r, k] score and id views of the
+        lists it merges (its query slice under results="owner", else all
+        queries)."""
+        if ex is None:
+            if self.results == "owner":
+                return exchange_owned(local_d, local_i, self.group, self.pool)
+            return gather_candidates(local_d, local_i, self.group, self.pool)
+        world = dist.get_world_size(self.group)
+        Q, k = local_d.shape
+        W = _packed_width(k)
+        # two list sections by epoch parity: with no threshold exchange
+        # between two searches, a rank may pack the next lists while another
+        # still reads these
+        name = "lists%d" % (epoch & 1)
+        pack_lists(local_d, local_i, ex.view(name, (Q, W), torch.int32))
+        lo, hi = self.owned_range(Q)
+        recv = self.pool.get("peer_lists", (world, hi - lo, W), torch.int32, local_d.device)
+        ex.gather(PeerExchange.SLOT_LISTS, name, epoch, row0=[lo] * world, nrows=[hi - lo] * world,
+                  row_bytes=4 * W, src_row_stride=4 * W, dst=recv,
+                  dst_off=[4 * W * (hi - lo) * p for p in range(world)], dst_row_stride=4 * W)
+        return unpack_lists(recv, k)
+
+
 def shared_sample_plan(sizes, k: int) -> Optional[Tuple[int, int, int]]:
     """Sample plan of the shared-threshold protocol for shard sizes `sizes`:
     (rows sampled per rank, rows per group maximum, total sampled rows), or
@@ -402,7 +465,7 @@ def shared_sample_plan(sizes, k: int) -> Optional[Tuple[int, int, int]]:
     return per, g, world * per
 
 
-class ShardedSearch(_ShardSizes):
+class ShardedSearch(_ShardSizes, _PeerTransport):
     """Search one query batch against a row-sharded index.
 
     Args:
@@ -438,11 +501,7 @@ class ShardedSearch(_ShardSizes):
                  local_size=None, transport: str = "auto"):
         if results not in ("replicated", "owner"):
             raise ValueError(f"results must be 'replicated' or 'owner', got {results!r}")
-        if transport not in ("auto", "collective", "peer"):
-            raise ValueError(f"transport must be 'auto', 'collective' or 'peer', got {transport!r}")
-        self.transport = transport
-        self.peer: Optional[PeerExchange] = None
-        self._peer_off = transport == "collective"
+        self._init_transport(transport)
         self._size_source = index
         self._init_sizes(local_size)
         self.clock = PhaseClock()
@@ -463,34 +522,6 @@ class ShardedSearch(_ShardSizes):
         if self.results != "owner" or not dist.is_initialized() or dist.get_world_size(self.group) == 1:
             return 0, Q
         return shard_range(Q, dist.get_rank(self.group), dist.get_world_size(self.group))
-
-    def _peer_exchange(self, device) -> Optional[PeerExchange]:
-        """The peer transport (set up on the first search, collectively), or
-        None for collectives."""
-        if self._peer_off:
-            return None
-        if self.peer is None:
-            usable = (device.type == "cuda" and "nccl" in str(dist.get_backend(self.group))
-                      and dist.get_world_size(self.group) <= PeerExchange.MAX_RANKS)
-            try:
-                if not usable:
-                    raise PeerUnavailable("the peer transport needs CUDA ranks under the NCCL backend, "
-                                          f"at most {PeerExchange.MAX_RANKS}")
-                ex = PeerExchange(self.group, device)
-                ex.reserve({})
-                self.peer = ex
-            except PeerUnavailable:
-                if self.transport == "peer":
-                    raise
-                self._peer_off = True
-                return None
-        return self.peer
-
-    def close(self) -> None:
-        """Frees the peer transport's arenas (collective: every rank calls it)."""
-        if self.peer is not None:
-            self.peer.close()
-            self.peer = None
 
     def _shared_threshold_search(self, queries: torch.Tensor, k: int, sizes, plan, ex=None, epoch=0):
         """Shared-threshold protocol: every rank computes group maxima of a
@@ -559,29 +590,6 @@ class ShardedSearch(_ShardSizes):
         expect = int(math.ceil(1.1 * self.flat.size() * k / total)) + 1
         return self.flat.search_threshold(queries, k, thr, expect)
 
-    def _exchange_lists(self, local_d, local_i, ex=None, epoch=0):
-        """This rank's [Q, k] lists -> [G, Q_r, k] score and id views of the
-        lists it merges (its query slice under results="owner", else all
-        queries)."""
-        if ex is None:
-            if self.results == "owner":
-                return exchange_owned(local_d, local_i, self.group, self.pool)
-            return gather_candidates(local_d, local_i, self.group, self.pool)
-        world = dist.get_world_size(self.group)
-        Q, k = local_d.shape
-        W = _packed_width(k)
-        # two list sections by epoch parity: with no threshold exchange
-        # between two searches, a rank may pack the next lists while another
-        # still reads these
-        name = "lists%d" % (epoch & 1)
-        pack_lists(local_d, local_i, ex.view(name, (Q, W), torch.int32))
-        lo, hi = self.owned_range(Q)
-        recv = self.pool.get("peer_lists", (world, hi - lo, W), torch.int32, local_d.device)
-        ex.gather(PeerExchange.SLOT_LISTS, name, epoch, row0=[lo] * world, nrows=[hi - lo] * world,
-                  row_bytes=4 * W, src_row_stride=4 * W, dst=recv,
-                  dst_off=[4 * W * (hi - lo) * p for p in range(world)], dst_row_stride=4 * W)
-        return unpack_lists(recv, k)
-
     def search(self, queries: torch.Tensor, k: int) -> Tuple[torch.Tensor, torch.Tensor]:
         if not dist.is_initialized() or dist.get_world_size(self.group) == 1:
             return self.search_fn(queries, k)
@@ -615,24 +623,27 @@ class ShardedSearch(_ShardSizes):
         return res
 
 
-class ShardedIVFSearch(_ShardSizes):
+class ShardedIVFSearch(_ShardSizes, _PeerTransport):
     """Search a row-sharded IVF / IVF-PQ index (every rank holds the same
     trained quantizer and a slice of the rows).
 
     The coarse probe is split across ranks -- rank r probes its contiguous
-    slice of the query batch -- and the [Q, nprobe] list table is
-    all-gathered, so the replicated probe costs each GPU 1/G of the batch.
-    Every rank then scans its rows of the probed lists for all queries
-    (``index.search_probed``), and the per-rank [Q, k] lists are all-gathered
+    slice of the query batch -- and the [Q, nprobe] list table is shared,
+    so the replicated probe costs each GPU 1/G of the batch.  Every rank
+    then scans its rows of the probed lists for all queries
+    (``index.search_probed``), and the per-rank [Q, k] lists are exchanged
     and merged as in ShardedSearch (results="owner": each rank merges and
-    returns only its query slice, owned_range(Q), after an all-to-all).
-    Shards with fewer than k rows contribute padded lists (``local_size`` as
-    in ShardedSearch)."""
+    returns only its query slice, owned_range(Q)).  Both exchanges go
+    through the peer exchange kernel or collectives (``transport`` as in
+    ShardedSearch).  Shards with fewer than k rows contribute padded lists
+    (``local_size`` as in ShardedSearch)."""
 
     def __init__(self, index, largest: bool, group: Optional[dist.ProcessGroup] = None,
-                 merge: Optional[Callable] = None, results: str = "replicated", local_size=None):
+                 merge: Optional[Callable] = None, results: str = "replicated", local_size=None,
+                 transport: str = "auto"):
         if results not in ("replicated", "owner"):
             raise ValueError(f"results must be 'replicated' or 'owner', got {results!r}")
+        self._init_transport(transport)
         self._size_source = index
         self._init_sizes(local_size)
         self.clock = PhaseClock()
@@ -649,38 +660,72 @@ class ShardedIVFSearch(_ShardSizes):
             return 0, Q
         return shard_range(Q, dist.get_rank(self.group), dist.get_world_size(self.group))
 
-    def probe(self, queries: torch.Tensor) -> torch.Tensor:
-        if not dist.is_initialized() or dist.get_world_size(self.group) == 1:
-            return self.index.probe(queries)
+    def _probe_slice(self, queries: torch.Tensor):
+        """This rank's slice of the coarse probe: (slices of every rank,
+        its [hi - lo, nprobe] lists or None, nprobe)."""
         world = dist.get_world_size(self.group)
         rank = dist.get_rank(self.group)
         Q = queries.shape[0]
         chunk = (Q + world - 1) // world
-        lo, hi = min(rank * chunk, Q), min((rank + 1) * chunk, Q)
+        sl = [(min(p * chunk, Q), min((p + 1) * chunk, Q)) for p in range(world)]
+        lo, hi = sl[rank]
         local = self.index.probe(queries[lo:hi]) if hi > lo else None
         np_ = local.shape[1] if local is not None else self.index.probe(queries[:1]).shape[1]
+        return sl, local, np_
+
+    def probe(self, queries: torch.Tensor) -> torch.Tensor:
+        """The [Q, nprobe] list table of the batch (collective over the
+        ranks; each probes its slice), as a new tensor."""
+        if not dist.is_initialized() or dist.get_world_size(self.group) == 1:
+            return self.index.probe(queries)
+        world = dist.get_world_size(self.group)
+        Q = queries.shape[0]
+        sl, local, np_ = self._probe_slice(queries)
+        chunk = (Q + world - 1) // world
         buf = self.pool.get("probe_mine", (chunk, np_), torch.long, queries.device)  # rows past hi - lo: padding
         if local is not None:
-            buf[: hi - lo] = local
+            buf[: local.shape[0]] = local
         out = self.pool.get("probe_all", (world * chunk, np_), torch.long, queries.device)
         dist.all_gather_into_tensor(out, buf, group=self.group)
         return out[:Q].clone()  # the caller may keep it; the pooled buffer is reused by the next probe
+
+    def _probe_peer(self, queries: torch.Tensor, k: int, ex: PeerExchange) -> Tuple[torch.Tensor, int]:
+        """The list table through the exchange arenas: this rank's slice in
+        place, every other rank's slice read from its arena by one exchange
+        kernel.  Returns the table (a view of this rank's arena, valid until
+        the next search) and the search's epoch."""
+        rank = dist.get_rank(self.group)
+        Q = queries.shape[0]
+        sl, local, np_ = self._probe_slice(queries)
+        W4 = 4 * Q * _packed_width(k)
+        ex.reserve({"probe": 8 * Q * np_, "lists0": W4, "lists1": W4})
+        epoch = ex.next_epoch()
+        table = ex.view("probe", (Q, np_), torch.long)
+        lo, hi = sl[rank]
+        if local is not None:
+            table[lo:hi] = local
+        ex.gather(PeerExchange.SLOT_PROBE, "probe", epoch, row0=[a for a, _ in sl],
+                  nrows=[0 if p == rank else b - a for p, (a, b) in enumerate(sl)], row_bytes=8 * np_,
+                  src_row_stride=8 * np_, dst=table, dst_off=[8 * np_ * a for a, _ in sl], dst_row_stride=8 * np_)
+        return table, epoch
 
     def search(self, queries: torch.Tensor, k: int) -> Tuple[torch.Tensor, torch.Tensor]:
         if not dist.is_initialized() or dist.get_world_size(self.group) == 1:
             return self.index.search_probed(queries, self.probe(queries), k)
         sizes = self.shard_sizes(queries.device)
         self._check_k(sizes, k)
+        ex = self._peer_exchange(queries.device)
         self.clock.start(queries)
-        probe = self.probe(queries)
+        epoch = 0
+        if ex is not None:
+            probe, epoch = self._probe_peer(queries, k, ex)
+        else:
+            probe = self.probe(queries)
         self.clock.mark("probe")
         local_d, local_i = self._padded(lambda kk: self.index.search_probed(queries, probe, kk), sizes, k,
                                         (queries.shape[0], queries.device))
         self.clock.mark("scan")
-        if self.results == "owner":
-            vals, ids = exchange_owned(local_d, local_i, self.group, self.pool)
-        else:
-            vals, ids = gather_candidates(local_d, local_i, self.group, self.pool)
+        vals, ids = self._exchange_lists(local_d, local_i, ex, epoch)
         self.clock.mark("result_exchange")
         res = self.merge(vals, ids, k, self.largest)
         self.clock.mark("merge")

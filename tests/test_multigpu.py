@@ -85,6 +85,15 @@ def _worker(rank, port, out_q):
         ivf.add(xt, torch.arange(lo, hi, device=dev))
         d, i = ShardedIVFSearch(ivf, largest=False).search(qt, 10)
         res["ivf"] = (d.cpu().numpy(), i.cpu().numpy())
+        # both transports and result modes, three searches each
+        for mode in ("owner", "replicated"):
+            for transport in ("peer", "collective"):
+                s = ShardedIVFSearch(ivf, largest=False, results=mode, transport=transport)
+                for _ in range(3):
+                    d, i = s.search(qt, 10)
+                res[f"ivf_{mode}_{transport}"] = (s.owned_range(len(q)), d.cpu().numpy(), i.cpu().numpy())
+                assert (s.peer is not None) == (transport == "peer")
+                s.close()
         # IVF-PQ (query-major search) with the same quantizer, shared codebooks
         pq = _C.IVFPQIndex(64, _C.Metric.L2, 32, 6, 16, 64)
         pq.set_quantizer(km.centroids, _books(dev))
@@ -148,4 +157,7 @@ def test_sharded_equals_single_gpu():
         np.testing.assert_allclose(out[r]["kmeans"][0], km.centroids.cpu().numpy(), rtol=1e-5, atol=1e-5)
         assert abs(out[r]["kmeans"][1] - km.inertia) <= 1e-5 * km.inertia
         assert_topk_match(di.cpu().numpy(), ii.cpu().numpy(), *out[r]["ivf"], rtol=1e-5, atol=1e-4)
+        for key, ((a, b), do, io) in ((kk, v) for kk, v in out[r].items() if kk.startswith("ivf_")):
+            assert (a, b) == (shard_range(len(q), r, WORLD) if "_owner_" in key else (0, len(q))), key
+            assert_topk_match(di[a:b].cpu().numpy(), ii[a:b].cpu().numpy(), do, io, rtol=1e-5, atol=1e-4)
         assert_topk_match(dp.cpu().numpy(), ip.cpu().numpy(), *out[r]["ivfpq"], rtol=1e-5, atol=1e-3)
