@@ -303,11 +303,16 @@ __device__ __forceinline__ void tc_scan_body(uint8_t* smem_raw, const CUtensorMa
         float best = -INFINITY;
         uint32_t best_r = 0;
         float gb = -INFINITY;  // running group maximum (groups of 64 / 128 rows)
+        float gw = 0.f;        // and the group's largest 1 / xv (cosine)
         const float* __restrict__ xvp = a.xv;
         const int64_t step = a.row_step;
+        // cosine group maxima rank by t = dot / xv: the tile holds 1 / xv
+        // (0 for a zero row, whose dot is 0), one division per row and tile
+        const bool cos_recip = MODE == SCAN_GROUPMAX && a.metric == RDB_METRIC_COSINE;
         auto load_xv = [&](int t) -> float {
             const int64_t r = r_begin + static_cast<int64_t>(t) * BN + etid;
-            return (xvp && r < r_end) ? __ldg(xvp + r * step) : 0.f;
+            const float x = (xvp && r < r_end) ? __ldg(xvp + r * step) : 0.f;
+            return cos_recip ? (x > 0.f ? 1.f / x : 0.f) : x;
         };
         float xv_next = 0.f;
         if (ntiles > 0) xv_s[etid] = load_xv(0);
@@ -378,9 +383,12 @@ __device__ __forceinline__ void tc_scan_body(uint8_t* smem_raw, const CUtensorMa
                         }
                     }
                 } else if (MODE == SCAN_GROUPMAX) {
-                    // approximate final scores (fast reciprocal: a few ulps; the
-                    // threshold's 2^-16 slack absorbs it), larger = better; L2 is
-                    // ranked in the order-reversed space dot - xv / 2
+                    // ranking values, larger = better: L2 in the order-reversed
+                    // space dot - xv / 2; cosine t = dot / xv (the tile holds
+                    // 1 / xv), turned into a score bound per group below; dot
+                    // as is.  w = 1 / xv of the rows, for the cosine bound.
+                    const bool cos_eps = a.metric == RDB_METRIC_COSINE && !a.cos_small;
+                    float w[32];
 #pragma unroll
                     for (int j4 = 0; j4 < 8; ++j4) {
                         const float4 x4 = xs4[j4];
@@ -389,50 +397,79 @@ __device__ __forceinline__ void tc_scan_body(uint8_t* smem_raw, const CUtensorMa
                         for (int u = 0; u < 4; ++u) {
                             const int j = 4 * j4 + u;
                             float sc;
-                            if (a.metric == RDB_METRIC_L2) {
+                            if (a.metric == RDB_METRIC_L2)
                                 sc = fmaf(-0.5f, xx[u], v[j]);
-                            } else if (a.metric == RDB_METRIC_COSINE) {
-                                const float den = a.cos_small ? qv * xx[u] : fmaf(qv, xx[u], 1e-8f);
-                                sc = __fdividef(v[j], den);
-                            } else {
+                            else if (a.metric == RDB_METRIC_COSINE)
+                                sc = v[j] * xx[u];
+                            else
                                 sc = v[j];
-                            }
-                            v[j] = ((valid >> j) & 1u) ? sc : -INFINITY;
+                            const bool ok = (valid >> j) & 1u;
+                            v[j] = ok ? sc : -INFINITY;
+                            w[j] = ok ? xx[u] : 0.f;
                         }
                     }
                     const int g = a.group;
-                    auto emit = [&](float* p, float mx) {
-                        *p = a.metric == RDB_METRIC_L2 ? fmaxf(qv - 2.f * mx, 0.f) : mx;
+                    // group maximum -> the value written: for cosine a lower
+                    // bound on the score of the row with the largest t, which
+                    // is dot / (qv xv + 1e-8) = t / (qv + 1e-8 / xv) (d > 128;
+                    // t / qv for d <= 128, whose values carry the epsilon under
+                    // the square roots): t / (qv + 1e-8 wmax) for t > 0 with
+                    // wmax the group's largest 1 / xv, t / qv otherwise, so the
+                    // k-th best of the group bounds is still at most the k-th
+                    // best score (rounding: a few ulps, within the threshold's
+                    // 2^-16 slack)
+                    auto emit = [&](float* p, float mx, float wmax) {
+                        float out = mx;
+                        if (a.metric == RDB_METRIC_L2)
+                            out = fmaxf(qv - 2.f * mx, 0.f);
+                        else if (a.metric == RDB_METRIC_COSINE)
+                            out = mx > 0.f ? mx / (cos_eps ? fmaf(1e-8f, wmax, qv) : qv)
+                                           : (mx < 0.f ? mx / qv : mx);
+                        *p = out;
                     };
                     if (qvalid) {
                         float* gout = a.group_out + q * a.ngroups;
                         if (g > 32) {
                             // groups of 64 / 128 span two / four chunks of this warp
-                            float m0 = v[0];
+                            float m0 = v[0], m1 = v[1], w0 = w[0], w1 = w[1];
 #pragma unroll
-                            for (int j = 1; j < 32; ++j) m0 = fmaxf(m0, v[j]);
-                            gb = fmaxf(gb, m0);
+                            for (int j = 2; j < 32; j += 2) {
+                                m0 = fmaxf(m0, v[j]);
+                                m1 = fmaxf(m1, v[j + 1]);
+                                if (cos_eps) {
+                                    w0 = fmaxf(w0, w[j]);
+                                    w1 = fmaxf(w1, w[j + 1]);
+                                }
+                            }
+                            gb = fmaxf(gb, fmaxf(m0, m1));
+                            gw = fmaxf(gw, fmaxf(w0, w1));
                             if (((c + 1) * 32) % g == 0) {
                                 const int64_t gs = (col0 + 32) - g;  // first row of the group
-                                if (gs < r_end) emit(gout + gs / g, gb);
+                                if (gs < r_end) emit(gout + gs / g, gb, gw);
                                 gb = -INFINITY;
+                                gw = 0.f;
                             }
                         } else if (g == 16) {
 #pragma unroll
                             for (int h = 0; h < 2; ++h) {
-                                float m0 = v[16 * h];
+                                float m0 = v[16 * h], w0 = w[16 * h];
 #pragma unroll
-                                for (int j = 1; j < 16; ++j) m0 = fmaxf(m0, v[16 * h + j]);
-                                if ((valid >> (16 * h)) & 1u) emit(gout + col0 / 16 + h, m0);
+                                for (int j = 1; j < 16; ++j) {
+                                    m0 = fmaxf(m0, v[16 * h + j]);
+                                    w0 = fmaxf(w0, w[16 * h + j]);
+                                }
+                                if ((valid >> (16 * h)) & 1u) emit(gout + col0 / 16 + h, m0, w0);
                             }
                         } else {
-                            float gm = -INFINITY;
+                            float gm = -INFINITY, gwm = 0.f;
 #pragma unroll
                             for (int j = 0; j < 32; ++j) {
                                 gm = fmaxf(gm, v[j]);
+                                gwm = fmaxf(gwm, w[j]);
                                 if (((j + 1) & (g - 1)) == 0) {
-                                    if ((valid >> (j + 1 - g)) & 1u) emit(gout + (col0 + j) / g, gm);
+                                    if ((valid >> (j + 1 - g)) & 1u) emit(gout + (col0 + j) / g, gm, gwm);
                                     gm = -INFINITY;
+                                    gwm = 0.f;
                                 }
                             }
                         }
