@@ -1081,6 +1081,25 @@ __global__ void __launch_bounds__(256) probe_select_kernel(const float* __restri
             }
         }
         __syncwarp();
+        if (!all) {
+            // every candidate in this one chunk: each goes straight to the
+            // position of its rank in (distance, list) order -- the order of
+            // the selection below (a NaN distance counts as +inf)
+            for (int c = lane; c < nc; c += 32) {
+                const float v0 = s_val[w][c];
+                const float v = v0 != v0 ? INFINITY : v0;
+                const int id = s_idx[w][c];
+                int rank = 0;
+                for (int j = 0; j < nc; ++j) {
+                    const float u0 = s_val[w][j];
+                    const float u = u0 != u0 ? INFINITY : u0;
+                    rank += (u < v || (u == v && s_idx[w][j] < id)) ? 1 : 0;
+                }
+                if (rank < nprobe) probe[(e0 + r) * nprobe + rank] = id;
+            }
+            for (int i = nc + lane; i < nprobe; i += 32) probe[(e0 + r) * nprobe + i] = -1;
+            return;
+        }
         // best nprobe of this chunk and the running list
         float cv[8];
         int ci[8];
