@@ -42,7 +42,9 @@ constexpr int EPI_THREADS = EPI_WARPS * 32;
 constexpr int NUM_THREADS = 64 + EPI_THREADS;
 constexpr int BAR_BYTES = 256;
 constexpr int XV_BYTES = 2 * BN * 4;
-constexpr int EPI_SHARED_BYTES = 2 * BM * 4;  // per-query candidate counters / arg-best hand-over
+// per-query candidate counters / arg-best hand-over, then per 32-row block the
+// largest 1 / xv of the row values' two buffers (cosine group maxima)
+constexpr int EPI_SHARED_BYTES = 2 * BM * 4 + 2 * (BN / 32) * 4;
 static_assert(EPI_THREADS == BN, "one epilogue thread per row of a tile (row values)");
 
 static_assert(NUM_ACC * BN <= TMEM_COLS, "accumulators exceed TMEM allocation");
@@ -112,6 +114,7 @@ __device__ __forceinline__ void tc_scan_body(uint8_t* smem_raw, const CUtensorMa
     float* xv_s = reinterpret_cast<float*>(smem + NST * Cfg::STAGE_B + BAR_BYTES);
     uint32_t* cnt_s = reinterpret_cast<uint32_t*>(xv_s + 2 * BN);  // [BM]
     float* best_s = reinterpret_cast<float*>(cnt_s + BM);            // [BM]
+    float* rxm_s = best_s + BM;                                      // [2][BN / 32]
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const uint32_t rank = PAIR ? cluster_rank() : 0u;
@@ -303,7 +306,6 @@ __device__ __forceinline__ void tc_scan_body(uint8_t* smem_raw, const CUtensorMa
         float best = -INFINITY;
         uint32_t best_r = 0;
         float gb = -INFINITY;  // running group maximum (groups of 64 / 128 rows)
-        float gw = 0.f;        // and the group's largest 1 / xv (cosine)
         const float* __restrict__ xvp = a.xv;
         const int64_t step = a.row_step;
         // cosine group maxima rank by t = dot / xv: the tile holds 1 / xv
@@ -315,7 +317,16 @@ __device__ __forceinline__ void tc_scan_body(uint8_t* smem_raw, const CUtensorMa
             return cos_recip ? (x > 0.f ? 1.f / x : 0.f) : x;
         };
         float xv_next = 0.f;
-        if (ntiles > 0) xv_s[etid] = load_xv(0);
+        // the row values of a tile into buffer b; cosine group maxima also
+        // keep each 32-row block's largest 1 / xv (a warp holds 32 rows)
+        auto put_xv = [&](int b, float x) {
+            xv_s[b * BN + etid] = x;
+            if (cos_recip) {
+                const unsigned m = __reduce_max_sync(0xffffffffu, __float_as_uint(x));  // x >= 0
+                if (lane == 0) rxm_s[b * (BN / 32) + etid / 32] = __uint_as_float(m);
+            }
+        };
+        if (ntiles > 0) put_xv(0, load_xv(0));
         epi_bar_sync();
         for (int t = 0; t < ntiles; ++t) {
             const int acc = t & 1;
@@ -386,9 +397,8 @@ __device__ __forceinline__ void tc_scan_body(uint8_t* smem_raw, const CUtensorMa
                     // ranking values, larger = better: L2 in the order-reversed
                     // space dot - xv / 2; cosine t = dot / xv (the tile holds
                     // 1 / xv), turned into a score bound per group below; dot
-                    // as is.  w = 1 / xv of the rows, for the cosine bound.
+                    // as is
                     const bool cos_eps = a.metric == RDB_METRIC_COSINE && !a.cos_small;
-                    float w[32];
 #pragma unroll
                     for (int j4 = 0; j4 < 8; ++j4) {
                         const float4 x4 = xs4[j4];
@@ -403,73 +413,66 @@ __device__ __forceinline__ void tc_scan_body(uint8_t* smem_raw, const CUtensorMa
                                 sc = v[j] * xx[u];
                             else
                                 sc = v[j];
-                            const bool ok = (valid >> j) & 1u;
-                            v[j] = ok ? sc : -INFINITY;
-                            w[j] = ok ? xx[u] : 0.f;
+                            v[j] = ((valid >> j) & 1u) ? sc : -INFINITY;
                         }
                     }
                     const int g = a.group;
+                    const float* rxm = rxm_s + acc * (BN / 32);  // this tile's 32-row block maxima of 1 / xv
                     // group maximum -> the value written: for cosine a lower
                     // bound on the score of the row with the largest t, which
                     // is dot / (qv xv + 1e-8) = t / (qv + 1e-8 / xv) (d > 128;
                     // t / qv for d <= 128, whose values carry the epsilon under
                     // the square roots): t / (qv + 1e-8 wmax) for t > 0 with
-                    // wmax the group's largest 1 / xv, t / qv otherwise, so the
-                    // k-th best of the group bounds is still at most the k-th
-                    // best score (rounding: a few ulps, within the threshold's
-                    // 2^-16 slack)
-                    auto emit = [&](float* p, float mx, float wmax) {
+                    // wmax at least the group's largest 1 / xv (the maximum
+                    // over the 32-row blocks it lies in), t / qv otherwise, so
+                    // the k-th best of the group bounds is still at most the
+                    // k-th best score (rounding: a few ulps, within the
+                    // threshold's 2^-16 slack).  Blocks [b0, b1] of the tile.
+                    auto emit = [&](float* p, float mx, int b0, int b1) {
                         float out = mx;
-                        if (a.metric == RDB_METRIC_L2)
+                        if (a.metric == RDB_METRIC_L2) {
                             out = fmaxf(qv - 2.f * mx, 0.f);
-                        else if (a.metric == RDB_METRIC_COSINE)
+                        } else if (a.metric == RDB_METRIC_COSINE) {
+                            float wmax = 0.f;
+                            if (cos_eps)
+                                for (int b = b0; b <= b1; ++b) wmax = fmaxf(wmax, rxm[b]);
                             out = mx > 0.f ? mx / (cos_eps ? fmaf(1e-8f, wmax, qv) : qv)
                                            : (mx < 0.f ? mx / qv : mx);
+                        }
                         *p = out;
                     };
                     if (qvalid) {
                         float* gout = a.group_out + q * a.ngroups;
                         if (g > 32) {
                             // groups of 64 / 128 span two / four chunks of this warp
-                            float m0 = v[0], m1 = v[1], w0 = w[0], w1 = w[1];
+                            float m0 = v[0], m1 = v[1];
 #pragma unroll
                             for (int j = 2; j < 32; j += 2) {
                                 m0 = fmaxf(m0, v[j]);
                                 m1 = fmaxf(m1, v[j + 1]);
-                                if (cos_eps) {
-                                    w0 = fmaxf(w0, w[j]);
-                                    w1 = fmaxf(w1, w[j + 1]);
-                                }
                             }
                             gb = fmaxf(gb, fmaxf(m0, m1));
-                            gw = fmaxf(gw, fmaxf(w0, w1));
                             if (((c + 1) * 32) % g == 0) {
                                 const int64_t gs = (col0 + 32) - g;  // first row of the group
-                                if (gs < r_end) emit(gout + gs / g, gb, gw);
+                                if (gs < r_end) emit(gout + gs / g, gb, c + 1 - g / 32, c);
                                 gb = -INFINITY;
-                                gw = 0.f;
                             }
                         } else if (g == 16) {
 #pragma unroll
                             for (int h = 0; h < 2; ++h) {
-                                float m0 = v[16 * h], w0 = w[16 * h];
+                                float m0 = v[16 * h];
 #pragma unroll
-                                for (int j = 1; j < 16; ++j) {
-                                    m0 = fmaxf(m0, v[16 * h + j]);
-                                    w0 = fmaxf(w0, w[16 * h + j]);
-                                }
-                                if ((valid >> (16 * h)) & 1u) emit(gout + col0 / 16 + h, m0, w0);
+                                for (int j = 1; j < 16; ++j) m0 = fmaxf(m0, v[16 * h + j]);
+                                if ((valid >> (16 * h)) & 1u) emit(gout + col0 / 16 + h, m0, c, c);
                             }
                         } else {
-                            float gm = -INFINITY, gwm = 0.f;
+                            float gm = -INFINITY;
 #pragma unroll
                             for (int j = 0; j < 32; ++j) {
                                 gm = fmaxf(gm, v[j]);
-                                gwm = fmaxf(gwm, w[j]);
                                 if (((j + 1) & (g - 1)) == 0) {
-                                    if ((valid >> (j + 1 - g)) & 1u) emit(gout + (col0 + j) / g, gm, gwm);
+                                    if ((valid >> (j + 1 - g)) & 1u) emit(gout + (col0 + j) / g, gm, c, c);
                                     gm = -INFINITY;
-                                    gwm = 0.f;
                                 }
                             }
                         }
@@ -513,7 +516,7 @@ __device__ __forceinline__ void tc_scan_body(uint8_t* smem_raw, const CUtensorMa
             if (lane == 0) mbar_arrive_cluster_relaxed(tempty_lead[acc]);
             // publish the next tile's row values (its buffer was last read in
             // tile t - 1, which every epilogue thread has finished)
-            if (t + 1 < ntiles) xv_s[((t + 1) & 1) * BN + etid] = xv_next;
+            if (t + 1 < ntiles) put_xv((t + 1) & 1, xv_next);
             epi_bar_sync();
         }
         // the second warp of each quadrant hands its arg-best to the first
