@@ -258,6 +258,16 @@ class Ctx:
         if self.world > 1:
             dist.barrier()
 
+    def device_barrier(self):
+        """A one-element all-reduce on the current stream, not waited for on
+        the host: work queued after it starts on every rank's GPU once all
+        ranks' GPUs have reached it."""
+        import torch
+        import torch.distributed as dist
+
+        if self.world > 1:
+            dist.all_reduce(torch.zeros(1, device=self.dev))
+
     def max(self, v):
         """Max over ranks of a host float."""
         import torch
@@ -319,6 +329,10 @@ def timed(ctx, fn, steps, warmup, tag_mask, tags=None):
     torch.cuda.synchronize()
     e0 = torch.cuda.Event(enable_timing=True)
     e1 = torch.cuda.Event(enable_timing=True)
+    # the ranks' timed regions start together on the devices (a rank whose
+    # host left the barrier later would otherwise add that delay to the
+    # others' first exchange and so to the max over ranks)
+    ctx.device_barrier()
     n0 = lib.rdb_launch_count()
     # no garbage-collection pause inside the timed steps (as timeit does);
     # the slowest step's host time is reported, so a host stall that left

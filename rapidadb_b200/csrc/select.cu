@@ -719,8 +719,12 @@ int launch_select(const SelectArgs& a, cudaStream_t stream) {
                               : a.input == SEL_MERGE ? (int64_t)a.G * a.kin
                                                      : a.cap * a.nsplit;
     // a warp re-reads elements beyond its on-chip cache on every pass: larger
-    // expected inputs go to the CTA kernel
-    const bool small = a.expect > 0 ? a.expect <= kWarpCache : max_elems <= 32768;
+    // expected inputs go to the CTA kernel, and so do expected counts above
+    // kWarpExpect, where the CTA kernel (seven per SM, keys sized to the
+    // count) selects faster (B200: 1,024 queries x ~1,680 candidates in
+    // 36 us against 2,048 x ~840 in 72 us for the warp kernel)
+    constexpr int64_t kWarpExpect = 512;
+    const bool small = a.expect > 0 ? a.expect <= kWarpExpect : max_elems <= 32768;
     // fewer queries than SMs: a CTA per query spreads them over the GPU (the
     // warp kernel would occupy nq / 8 SMs)
     const bool many = a.nq >= num_sms();
