@@ -397,3 +397,34 @@ def test_sharded_ivf_short_and_empty_shards():
     for r in range(3):
         np.testing.assert_array_equal(out[r][1], ri)
         np.testing.assert_allclose(out[r][0], rd, rtol=1e-5)
+
+
+def test_peer_arena_layout_on_host():
+    """PeerExchange's section layout without a GPU: sections start past the
+    flags, 256-byte aligned, in the order given; views have the requested
+    shape and dtype; the arena is mapped again only when a layout outgrows
+    it (to at least twice its size), and never for a layout that fits."""
+    from rapidadb_b200.sharded import PeerExchange
+
+    ex = PeerExchange.__new__(PeerExchange)
+    ex.nbytes, ex.ptr, ex.bases, ex.buf, ex._off, ex.epoch = 0, None, [], None, {}, 0
+    maps = []
+
+    def fake_map(nbytes):
+        maps.append(nbytes)
+        ex.nbytes = nbytes
+        ex.buf = torch.zeros(nbytes, dtype=torch.uint8)
+
+    ex._map = fake_map
+    ex.reserve({"maxima": 4 * 10 * 3, "thr": 4 * 10, "lists0": 100, "lists1": 100})
+    assert ex._off == {"maxima": 512, "thr": 768, "lists0": 1024, "lists1": 1280}
+    assert maps == [1536]
+    m = ex.view("maxima", (10, 3), torch.float32)
+    assert m.shape == (10, 3) and m.dtype == torch.float32 and m.data_ptr() == ex.buf.data_ptr() + 512
+    m.fill_(1.5)
+    assert ex.view("thr", (10,), torch.float32).sum().item() == 0.0  # sections do not overlap
+    ex.reserve({"maxima": 120})  # fits: no new mapping
+    assert maps == [1536]
+    ex.reserve({"probe": 8 * 1000})
+    assert maps == [1536, 8704] and ex._off == {"probe": 512}
+    assert [ex.next_epoch() for _ in range(3)] == [1, 2, 3]
