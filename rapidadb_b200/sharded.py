@@ -145,6 +145,7 @@ class PeerExchange:
     FLAG_BYTES = 512  # RDB_PEER_FLAG_BYTES
     MAX_RANKS = 8     # RDB_PEER_MAX_RANKS
     SLOT_MAXIMA, SLOT_THRESHOLD, SLOT_LISTS, SLOT_PROBE = 0, 1, 2, 3
+    STATUS_TIMEOUT = 1 << 6  # device status bit of a wait that ran out
 
     def __init__(self, group: Optional[dist.ProcessGroup], device, limit_ns: int = 2_000_000_000):
         self.group = group
@@ -391,9 +392,19 @@ class _PeerTransport:
 
     def _peer_exchange(self, device) -> Optional[PeerExchange]:
         """The peer transport (set up on the first search, collectively), or
-        None for collectives."""
+        None for collectives.  Raises when an exchange wait on this device
+        has run out since the status was last cleared (another rank fell
+        behind by more than the limit or left): the results of the searches
+        since then are not valid."""
         if self._peer_off:
             return None
+        if self.peer is not None:
+            from rapidadb_b200._lib import C
+
+            if C().pending_status() & PeerExchange.STATUS_TIMEOUT:
+                raise RuntimeError("a peer exchange wait on this device ran out (another rank fell behind or "
+                                   "left); results since then are not valid. Read and clear the status with "
+                                   "device_status(True) on every rank")
         if self.peer is None:
             usable = (device.type == "cuda" and "nccl" in str(dist.get_backend(self.group))
                       and dist.get_world_size(self.group) <= PeerExchange.MAX_RANKS)

@@ -89,7 +89,9 @@ def test_missing_signal_times_out_and_copies_nothing(device):
     C.device_status(True)
     C.peer_gather(0, 1, 4, [p0, p1], 4096, FLAGS, 64, 64, [0, 0], [0, 1], dst, [0, 0], 64, limit_ns=100_000)
     torch.cuda.synchronize()
+    assert C.pending_status() & PEER_BIT  # mirrored to host memory: the next search raises
     assert C.device_status(True) & PEER_BIT
+    assert C.pending_status() == 0
     assert C.device_status(False) == 0
     assert not dst.any()
     C.peer_arena_free(dev.index, p0)
