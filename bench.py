@@ -483,6 +483,7 @@ def run_flat(args, wl, ctx):
         d2h = hd.numel() * hd.element_size() + hi_.numel() * hi_.element_size()
     e2e_seq_s = ctx.max(time.perf_counter() - t0)
     e2e_s, e2e_mode = e2e_seq_s, "sequential: each step copies its batch in, searches, reads the results back"
+    e2e_pipe_s = None
     if world == 1:
         # the public pipelined API (rapidadb_b200.pipeline.AsyncBatchSearcher):
         # the same host batches, staged in pinned memory, copied in, searched
@@ -498,9 +499,12 @@ def run_flat(args, wl, ctx):
         torch.cuda.synchronize()
         t0 = time.perf_counter()
         pipe.search_host(src, k, batch_size=Q)
-        e2e_s = time.perf_counter() - t0
+        e2e_pipe_s = time.perf_counter() - t0
         pipe.close()
-        e2e_mode = "pipelined: AsyncBatchSearcher, 2 worker streams, one batch per step"
+        # both are the public API with the same host batches: the faster of
+        # the two is the end-to-end figure, and the record names it
+        if e2e_pipe_s < e2e_s:
+            e2e_s, e2e_mode = e2e_pipe_s, "pipelined: AsyncBatchSearcher, 2 worker streams, one batch per step"
 
     # ---- recall against exact fp32 search over the same stored values
     nrec = min(64, own_hi - own_lo)  # rank 0 owns the first queries in every results mode
@@ -579,7 +583,8 @@ def run_flat(args, wl, ctx):
                               source="separate %d-step pass with CUDA events around every phase" % min(args.steps, 10)),
             "e2e": {"value": round(Q * args.steps / e2e_s, 1), "unit": "queries/s",
                     "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h), "mode": e2e_mode,
-                    "sequential_value": round(Q * args.steps / e2e_seq_s, 1)},
+                    "sequential_value": round(Q * args.steps / e2e_seq_s, 1),
+                    "pipelined_value": round(Q * args.steps / e2e_pipe_s, 1) if world == 1 else None},
             "gpu_launches": t["launches"],
             "roofline": roof,
             "clocks": t["clocks"],
