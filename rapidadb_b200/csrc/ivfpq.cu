@@ -213,22 +213,44 @@ __global__ void __launch_bounds__(SNT, (M <= 32 ? 2 : 1)) ivfpq_search_kernel(
         // banks), the dsub codebook loads of an entry independent of each
         // other; entry (m, j) fills its 2 NC words of table row j of group
         // m / G (word w holds position (w / NC) mod G)
+        // M <= 32: a thread's entries (at most M / 2 with ksub <= 256) stay in
+        // registers until the scale is known and are written once, in fixed
+        // point; wider codes store fp32 entries and convert them in a second
+        // pass over the table
+        constexpr int KREG = M <= 32 ? (M * 256 + SNT - 1) / SNT : 1;
+        float vreg[KREG];
         float amax = 0.f;
-#pragma unroll 2
-        for (int e = tid; e < M * ksub; e += SNT) {
+        auto entry = [&](int e) -> float {
             const int j = e / M, m = e - j * M;
             const float* cbp = codebooks + (static_cast<int64_t>(m) * ksub + j) * dsub;
             const float* qp = qs + m * dsub;
             float s = 0.f;
             for (int u = 0; u < dsub; ++u) s = fmaf(qp[u], __ldg(cbp + u), s);
-            const float val = -2.f * s;
-            amax = fmaxf(amax, fabsf(val));
+            return -2.f * s;
+        };
+        auto store = [&](int e, uint32_t word) {
+            const int j = e / M, m = e - j * M;
             const int g = m / L::G, t = m - g * L::G;
             uint32_t* row = lut + g * kGroupWords + j * kRowWords;
 #pragma unroll
             for (int c = 0; c < L::NC; ++c) {
-                row[L::NC * t + c] = __float_as_uint(val);
-                row[L::NC * (t + L::G) + c] = __float_as_uint(val);
+                row[L::NC * t + c] = word;
+                row[L::NC * (t + L::G) + c] = word;
+            }
+        };
+        if constexpr (M <= 32) {
+#pragma unroll
+            for (int i = 0; i < KREG; ++i) {
+                const int e = tid + i * SNT;
+                vreg[i] = e < M * ksub ? entry(e) : 0.f;
+                amax = fmaxf(amax, fabsf(vreg[i]));
+            }
+        } else {
+#pragma unroll 2
+            for (int e = tid; e < M * ksub; e += SNT) {
+                const float val = entry(e);
+                amax = fmaxf(amax, fabsf(val));
+                store(e, __float_as_uint(val));
             }
         }
 #pragma unroll
@@ -244,11 +266,19 @@ __global__ void __launch_bounds__(SNT, (M <= 32 ? 2 : 1)) ivfpq_search_kernel(
         if (bound > 0.f) frexpf(bound, &ex);  // bound < 2^ex
         ex = max(ex, -90);                    // keep 2^(30 - ex) finite
         const float scale = ldexpf(1.f, 30 - ex), inv_scale = ldexpf(1.f, ex - 30);
-        for (int rr = warp; rr < L::NG * ksub; rr += SNW) {
-            const int g = rr / ksub, j = rr - g * ksub;
-            uint32_t* row = lut + g * kGroupWords + j * kRowWords;
-            row[lane] = static_cast<uint32_t>(__float2int_rn(__uint_as_float(row[lane]) * scale));
-            row[lane + 32] = static_cast<uint32_t>(__float2int_rn(__uint_as_float(row[lane + 32]) * scale));
+        if constexpr (M <= 32) {
+#pragma unroll
+            for (int i = 0; i < KREG; ++i) {
+                const int e = tid + i * SNT;
+                if (e < M * ksub) store(e, static_cast<uint32_t>(__float2int_rn(vreg[i] * scale)));
+            }
+        } else {
+            for (int rr = warp; rr < L::NG * ksub; rr += SNW) {
+                const int g = rr / ksub, j = rr - g * ksub;
+                uint32_t* row = lut + g * kGroupWords + j * kRowWords;
+                row[lane] = static_cast<uint32_t>(__float2int_rn(__uint_as_float(row[lane]) * scale));
+                row[lane + 32] = static_cast<uint32_t>(__float2int_rn(__uint_as_float(row[lane + 32]) * scale));
+            }
         }
         __syncthreads();
 
