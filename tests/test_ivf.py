@@ -96,10 +96,12 @@ def test_ivf_flat_bf16_storage(device):
     assert recall(i.cpu().numpy(), ri) >= 0.99
 
 
-@pytest.mark.parametrize("M,nlist,nprobe,query_major", [(8, 32, 6, True), (16, 64, 40, True), (2, 32, 6, False)])
+@pytest.mark.parametrize("M,nlist,nprobe,query_major", [(4, 32, 6, True), (8, 32, 6, True), (16, 64, 40, True),
+                                                          (32, 64, 40, True), (2, 32, 6, False)])
 def test_ivfpq_codes_and_search_match_oracle(device, M, nlist, nprobe, query_major):
-    """M = 8 / 16 run the query-major kernel (rotated code layout, per-row
-    terms), M = 2 the list-major scan + merge; both against the oracle's ADC."""
+    """M = 4 / 8 / 16 / 32 run the query-major kernel (rotated code layout,
+    per-row terms, the table built in registers), M = 2 the list-major scan
+    + merge; both against the oracle's ADC."""
     import rapidadb._C as _C
     from rapidadb_b200.kmeans import kmeans, train_pq
 
