@@ -35,6 +35,7 @@ SHAPES = [  # (N, Q, d, k)
     (20000, 300, 64, 10),  # at least one query per SM: the warp-per-query selects
     (40000, 7, 64, 10),    # one query block: the fp32 sample pass split over K (2 chunks)
     (36000, 20, 300, 30),  # the same over 10 K chunks, the last one partial
+    (80000, 150, 64, 100),  # sample groups of 16 rows with d <= 128; ~540 candidates per query (CTA select)
 ]
 
 
