@@ -375,14 +375,16 @@ __global__ void __launch_bounds__(NT, 7) select_kernel(SelectArgs a) {
 constexpr int kWarpSeg = 64;
 constexpr int kWarpOut = 128;
 
-constexpr int kWarpCache = 1024;  // elements per query kept on chip
+constexpr int kWarpCache = 1024;       // elements per query kept on chip (registers for a dense row)
+constexpr int kWarpCacheSmall = 512;   // the small instance: shared memory only, four CTAs per SM
 
-struct WarpSel {
+template <int CACHE>
+struct WarpSelT {
     int seg_off[kWarpSeg + 1];
     int hist[256];
     int nsel;
     unsigned long long sel[kWarpOut];
-    unsigned long long cache[kWarpCache];  // candidate / merge keys when T <= kWarpCache
+    unsigned long long cache[CACHE];  // element keys when T <= CACHE
 };
 
 // One histogram pass + bucket search.  Elements are offered through `each`
@@ -390,7 +392,7 @@ struct WarpSel {
 // pred(key), digit ((field(key) >> shift) & 255) is counted; returns the bucket
 // holding the remaining-th smallest field value and updates remaining / the
 // count of that bucket.
-template <class Each, class Pred, class Field>
+template <class WarpSel, class Each, class Pred, class Field>
 __device__ __forceinline__ uint32_t warp_radix_pass(WarpSel& W, int lane, Each&& each, Pred&& pred, Field&& field,
                                                     int shift, uint32_t match_mask, uint32_t match_val,
                                                     int& remaining, int& cnt_b) {
@@ -444,7 +446,7 @@ __device__ __forceinline__ uint32_t warp_radix_pass(WarpSel& W, int lane, Each&&
 // most the number of such elements); fmin / fmax bound the field values.
 // Returns the value; remaining = how many elements equal to it are needed,
 // cnt_eq = how many there are.
-template <class Each, class Pred, class Field>
+template <class WarpSel, class Each, class Pred, class Field>
 __device__ __forceinline__ uint32_t warp_select32(WarpSel& W, int lane, Each&& each, Pred&& pred, Field&& field,
                                                   uint32_t fmin, uint32_t fmax, int want, int& remaining,
                                                   int& cnt_eq) {
@@ -476,7 +478,14 @@ __device__ __forceinline__ uint32_t warp_select32(WarpSel& W, int lane, Each&& e
     return val;
 }
 
-__global__ void __launch_bounds__(NT, 2) select_warp_kernel(SelectArgs a) {
+// CACHE = kWarpCache: up to 1024 elements on chip (a dense row in
+// registers), two CTAs per SM; CACHE = kWarpCacheSmall: up to 512, all in
+// shared memory (about 6.5 KB per warp), four CTAs per SM, for the small
+// candidate lists of row-sharded searches.
+template <int CACHE>
+__global__ void __launch_bounds__(NT, (CACHE <= kWarpCacheSmall ? 4 : 2)) select_warp_kernel(SelectArgs a) {
+    using WarpSel = WarpSelT<CACHE>;
+    constexpr bool kRegDense = CACHE == kWarpCache;
     extern __shared__ __align__(16) unsigned char wsm[];
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     WarpSel& W = reinterpret_cast<WarpSel*>(wsm)[warp];
@@ -533,12 +542,12 @@ __global__ void __launch_bounds__(NT, 2) select_warp_kernel(SelectArgs a) {
         const int want = min(out_k_req, T);
 
         // element keys: a dense row of <= kWarpCache scores in registers
-        // (element lane + 32 i: score key kh[i]), other inputs of
-        // <= kWarpCache elements copied once into W.cache, larger ones
-        // re-read from global memory / L2 on every pass
-        const int mode = T > kWarpCache ? 0 : (a.input == SEL_DENSE ? 1 : 2);
-        uint32_t kh[kWarpCache / 32];
-        if (mode == 1) {
+        // (element lane + 32 i: score key kh[i]; CACHE = kWarpCache only),
+        // other inputs of <= CACHE elements copied once into W.cache, larger
+        // ones re-read from global memory / L2 on every pass
+        const int mode = T > CACHE ? 0 : ((kRegDense && a.input == SEL_DENSE) ? 1 : 2);
+        uint32_t kh[kRegDense ? kWarpCache / 32 : 1];
+        if (kRegDense && mode == 1) {
 #pragma unroll
             for (int i = 0; i < kWarpCache / 32; ++i) {
                 const int e = lane + 32 * i;
@@ -552,7 +561,7 @@ __global__ void __launch_bounds__(NT, 2) select_warp_kernel(SelectArgs a) {
             __syncwarp();
         }
         auto each = [&](auto&& fn) {
-            if (mode == 1) {
+            if (kRegDense && mode == 1) {
 #pragma unroll
                 for (int i = 0; i < kWarpCache / 32; ++i) {
                     const int e = lane + 32 * i;
@@ -724,20 +733,35 @@ int launch_select(const SelectArgs& a, cudaStream_t stream) {
     // count) selects faster (B200: 1,024 queries x ~1,680 candidates in
     // 36 us against 2,048 x ~840 in 72 us for the warp kernel)
     constexpr int64_t kWarpExpect = 512;
+    constexpr int64_t kWarpSmallExpect = 384;  // counts rarely above 512 (spread ~ sqrt(expect))
     const bool small = a.expect > 0 ? a.expect <= kWarpExpect : max_elems <= 32768;
     // fewer queries than SMs: a CTA per query spreads them over the GPU (the
     // warp kernel would occupy nq / 8 SMs)
     const bool many = a.nq >= num_sms();
     if (!a.force_cta && out_k <= kWarpOut && nseg <= kWarpSeg && small && many) {
         const int64_t blocks = (a.nq + NWARP - 1) / NWARP;
-        static bool wattr[64] = {false};
-        if (dev < 64 && !wattr[dev]) {
-            RDB_CUDA_TRY(cudaFuncSetAttribute(select_warp_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                              (int)(sizeof(WarpSel) * NWARP)));
-            wattr[dev] = true;
+        const unsigned nb = (unsigned)std::min<int64_t>(blocks, 65535LL * 16);
+        // expected counts well under 512 (the per-rank lists of row-sharded
+        // searches): the small instance, twice the warps per SM
+        if (a.expect > 0 && a.expect <= kWarpSmallExpect) {
+            static bool wattr_small[64] = {false};
+            if (dev < 64 && !wattr_small[dev]) {
+                RDB_CUDA_TRY(cudaFuncSetAttribute(select_warp_kernel<kWarpCacheSmall>,
+                                                  cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                  (int)(sizeof(WarpSelT<kWarpCacheSmall>) * NWARP)));
+                wattr_small[dev] = true;
+            }
+            select_warp_kernel<kWarpCacheSmall><<<nb, NT, sizeof(WarpSelT<kWarpCacheSmall>) * NWARP, stream>>>(a);
+        } else {
+            static bool wattr[64] = {false};
+            if (dev < 64 && !wattr[dev]) {
+                RDB_CUDA_TRY(cudaFuncSetAttribute(select_warp_kernel<kWarpCache>,
+                                                  cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                  (int)(sizeof(WarpSelT<kWarpCache>) * NWARP)));
+                wattr[dev] = true;
+            }
+            select_warp_kernel<kWarpCache><<<nb, NT, sizeof(WarpSelT<kWarpCache>) * NWARP, stream>>>(a);
         }
-        select_warp_kernel<<<(unsigned)std::min<int64_t>(blocks, 65535LL * 16), NT, sizeof(WarpSel) * NWARP,
-                             stream>>>(a);
         RDB_LAUNCH_CHECK();
         return RDB_OK;
     }
