@@ -132,3 +132,40 @@ def test_kmeans_init_rows_match_python_sampler():
         assert list(_C.sample_rows(n, k, seed)) == sample_rows(n, k, seed)
     with pytest.raises(RuntimeError, match="cannot sample"):
         _C.sample_rows(3, 4, 0)
+
+
+class RdbPeerGather(ctypes.Structure):
+    """include/rapidadb_b200.h: RdbPeerGather (RDB_PEER_MAX_RANKS = 8)."""
+    _fields_ = [("world", ctypes.c_int), ("rank", ctypes.c_int), ("slot", ctypes.c_int), ("pad", ctypes.c_int),
+                ("epoch", ctypes.c_ulonglong), ("base", ctypes.c_void_p * 8), ("arena_bytes", ctypes.c_longlong),
+                ("src_off", ctypes.c_longlong), ("src_row_stride", ctypes.c_longlong),
+                ("row_bytes", ctypes.c_longlong), ("row0", ctypes.c_longlong * 8), ("nrows", ctypes.c_longlong * 8),
+                ("dst", ctypes.c_void_p), ("dst_off", ctypes.c_longlong * 8), ("dst_row_stride", ctypes.c_longlong)]
+
+
+def test_peer_gather_argument_errors_without_gpu():
+    """Every bad argument of the peer exchange is rejected before any device
+    work (no GPU here), with a message naming it."""
+    lib = ctypes.CDLL(LIB)
+    lib.rdb_last_error.restype = ctypes.c_char_p
+    f = lib.rdb_peer_gather
+    f.argtypes = [ctypes.POINTER(RdbPeerGather), ctypes.c_ulonglong, ctypes.c_void_p]
+
+    def args(**kw):
+        a = RdbPeerGather(world=2, rank=0, slot=2, epoch=1, arena_bytes=4096, src_off=512, src_row_stride=64,
+                          row_bytes=64, dst=1 << 20, dst_row_stride=64)
+        a.base[0], a.base[1] = 1 << 24, 1 << 25
+        a.nrows[0] = a.nrows[1] = 1
+        for k, v in kw.items():
+            setattr(a, k, v)
+        return a
+
+    cases = [(dict(world=9), b"world"), (dict(rank=2), b"rank"), (dict(slot=8), b"slot"), (dict(epoch=0), b"epoch"),
+             (dict(row_bytes=6), b"row_bytes"), (dict(src_off=16), b"src_off"), (dict(dst=None), b"dst"),
+             (dict(arena_bytes=560), b"past the end")]
+    for kw, msg in cases:
+        a = args(**kw)
+        assert f(ctypes.byref(a), 2_000_000_000, None) == 1, kw  # RDB_ERR_INVALID
+        assert msg in lib.rdb_last_error(), (kw, lib.rdb_last_error())
+    a = args()
+    assert f(ctypes.byref(a), 10, None) == 1 and b"limit_ns" in lib.rdb_last_error()
